@@ -1,0 +1,203 @@
+"""ctypes binding of the CPU oracle (oracle.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline and reference arms, as the checker of the CUDA path.
+The product package never imports this module.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
+
+TRACE_FN = ctypes.CFUNCTYPE(None, ctypes.c_char_p, ctypes.POINTER(ctypes.c_float), ctypes.c_int64, ctypes.c_void_p)
+
+
+class OrInfo(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in
+                ("hidden", "layers", "heads", "ff", "per_layer", "out_dim", "dense_head", "vocab",
+                 "sliding_window", "max_tokens")] + [
+        ("eps", ctypes.c_float),
+        ("kv_heads", ctypes.c_int32 * 64), ("head_dim", ctypes.c_int32 * 64), ("sliding", ctypes.c_int32 * 64),
+        ("rope_base", ctypes.c_float * 64)]
+
+
+def build() -> str:
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(os.path.join(HERE, "oracle.c")):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        P = ctypes.POINTER
+        f32p, i32p, i64p = P(ctypes.c_float), P(ctypes.c_int32), P(ctypes.c_int64)
+        L.or_open.argtypes = [ctypes.c_char_p, P(ctypes.c_void_p), ctypes.c_char_p, ctypes.c_int]
+        L.or_close.argtypes = [ctypes.c_void_p]
+        L.or_get_info.argtypes = [ctypes.c_void_p, P(OrInfo)]
+        L.or_forward.argtypes = [ctypes.c_void_p, i32p, ctypes.c_int32, f32p, TRACE_FN, ctypes.c_void_p]
+        L.or_dequantize_row.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int64, f32p, ctypes.c_int64]
+        L.or_matmul.argtypes = [f32p, ctypes.c_int64, ctypes.c_int64, f32p, ctypes.c_int64, f32p]
+        L.or_rmsnorm.argtypes = [f32p, ctypes.c_int64, ctypes.c_int64, f32p, ctypes.c_float, f32p]
+        L.or_gelu_tanh.argtypes = [ctypes.c_float]
+        L.or_gelu_tanh.restype = ctypes.c_float
+        L.or_rope_table.argtypes = [ctypes.c_int32, ctypes.c_float, ctypes.c_int32, f32p]
+        L.or_attention.argtypes = [f32p, f32p, f32p] + [ctypes.c_int32] * 4 + [ctypes.c_float, ctypes.c_int32, f32p]
+        L.or_batches.argtypes = [i64p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, i64p, i32p]
+        L.or_batches.restype = ctypes.c_int32
+        L.or_finish.argtypes = [f32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, f32p]
+        L.or_seeded_next.argtypes = [P(ctypes.c_uint64)]
+        L.or_seeded_next.restype = ctypes.c_uint64
+        L.or_set_threads.argtypes = [ctypes.c_int]
+        L.or_threads.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def _f32(a):
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    return a, a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+
+
+class OracleError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[{code}] {message}")
+        self.code = code
+        self.message = message
+
+
+class OracleModel:
+    """CPUReference over a GGUF file: one sequence per `forward` call."""
+
+    def __init__(self, path: str):
+        L = lib()
+        h = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(512)
+        rc = L.or_open(path.encode(), ctypes.byref(h), err, 512)
+        if rc:
+            raise OracleError(rc, err.value.decode())
+        self._h = h
+        info = OrInfo()
+        L.or_get_info(h, ctypes.byref(info))
+        self.info = info
+
+    def close(self):
+        if self._h:
+            lib().or_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def out_dim(self) -> int:
+        return self.info.out_dim
+
+    def forward(self, tokens, trace: dict | None = None, trace_names=None) -> np.ndarray:
+        """Pooled, unnormalised vector of one sequence; fills `trace[name]` when given."""
+        toks = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.zeros(self.info.out_dim, dtype=np.float32)
+        cb = TRACE_FN(0)
+        if trace is not None:
+            def _cb(name, data, n, user):
+                key = name.decode()
+                if trace_names is None or key in trace_names:
+                    trace[key] = np.ctypeslib.as_array(data, shape=(n,)).copy()
+            cb = TRACE_FN(_cb)
+        rc = lib().or_forward(self._h, toks.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), len(toks),
+                              out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), cb, None)
+        if rc:
+            raise OracleError(rc, "forward rejected its input")
+        return out
+
+    def dequantize_row(self, tensor: str, row: int, width: int) -> np.ndarray:
+        out = np.zeros(width, dtype=np.float32)
+        rc = lib().or_dequantize_row(self._h, tensor.encode(), row, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), width)
+        if rc:
+            raise OracleError(rc, f"cannot dequantize {tensor}[{row}]")
+        return out
+
+
+def matmul(x, w):
+    x, xp = _f32(x)
+    w, wp = _f32(w)
+    y = np.zeros((x.shape[0], w.shape[0]), dtype=np.float32)
+    lib().or_matmul(xp, x.shape[0], x.shape[1], wp, w.shape[0], y.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    return y
+
+
+def rmsnorm(x, weight, eps=1e-6):
+    x, xp = _f32(x)
+    out = np.zeros_like(x)
+    wp = None
+    if weight is not None:
+        weight, wp = _f32(weight)
+    lib().or_rmsnorm(xp, x.shape[0], x.shape[1], wp, eps, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    return out
+
+
+def gelu_tanh(x: float) -> float:
+    return lib().or_gelu_tanh(x)
+
+
+def rope_table(head_dim: int, base: float, positions: int) -> np.ndarray:
+    out = np.zeros(positions * head_dim, dtype=np.float32)
+    lib().or_rope_table(head_dim, base, positions, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    return out.reshape(positions, head_dim // 2, 2)
+
+
+def attention(q, k, v, tokens, heads, kv_heads, hd, window=0, scale=1.0):
+    q, qp = _f32(q)
+    k, kp = _f32(k)
+    v, vp = _f32(v)
+    out = np.zeros(tokens * heads * hd, dtype=np.float32)
+    lib().or_attention(qp, kp, vp, tokens, heads, kv_heads, hd, scale, window,
+                       out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    return out
+
+
+def batches(costs, batch_size, budgets):
+    """EmbeddingModel.batches: a list of (start, end) ranges."""
+    n = len(costs)
+    ncost = len(budgets)
+    c = np.ascontiguousarray(np.array(costs, dtype=np.int64).reshape(n, ncost) if n else np.zeros((0, ncost), np.int64))
+    b = np.ascontiguousarray(np.array(budgets, dtype=np.int64))
+    out = np.zeros(max(2 * n, 2), dtype=np.int32)
+    cnt = lib().or_batches(c.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), n, ncost,
+                           0 if batch_size is None else batch_size, b.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
+                           out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)))
+    return [(int(out[2 * i]), int(out[2 * i + 1])) for i in range(cnt)]
+
+
+def finish(v, dims, normalise):
+    v, vp = _f32(v)
+    out = np.zeros(min(dims, len(v)), dtype=np.float32)
+    lib().or_finish(vp, len(v), dims, 1 if normalise else 0, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    return out
+
+
+def seeded_draws(seed: int, n: int) -> list:
+    state = ctypes.c_uint64((seed + 0x9E3779B97F4A7C15) & 0xFFFFFFFFFFFFFFFF)
+    return [lib().or_seeded_next(ctypes.byref(state)) for _ in range(n)]
+
+
+def set_threads(n: int) -> None:
+    lib().or_set_threads(n)
+
+
+def threads() -> int:
+    return lib().or_threads()

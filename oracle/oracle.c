@@ -1,0 +1,891 @@
+/*
+ * oracle.c -- CPU restatement of the reference's fp32 forward pass.
+ *
+ * TEST INFRASTRUCTURE ONLY (see oracle.h): the checker for the CUDA path,
+ * never part of the product.  Each function cites the reference lines it
+ * restates.  All arithmetic is fp32 like the reference's CPUReference; only
+ * the RoPE table is computed in double, as RopeTable.swift does.
+ */
+#define _GNU_SOURCE
+#include "oracle.h"
+
+#include <errno.h>
+#include <fcntl.h>
+#include <math.h>
+#include <omp.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#define MAX_LAYERS 64
+
+/* ------------------------------------------------------------------ GGUF */
+/* GGUFValue.swift:83-114: ggml type ids, block sizes and block bytes. */
+enum { T_F32 = 0, T_F16 = 1, T_Q8_0 = 8, T_BF16 = 30 };
+
+typedef struct {
+    char* name;
+    int ndim;
+    int64_t shape[4];
+    uint32_t type;
+    uint64_t offset;
+    const uint8_t* data;
+    float* dequant; /* cached fp32 copy, CPUReference.matrix (CPUReference.swift:31-38) */
+} tensor_t;
+
+typedef struct {
+    char* key;
+    uint32_t type;
+    const uint8_t* raw; /* position of the value in the mapping */
+    uint64_t count;     /* array element count */
+    uint32_t elem;      /* array element type */
+} kv_t;
+
+struct or_model {
+    uint8_t* base;
+    size_t size;
+    size_t mapped;
+    kv_t* kvs;
+    int64_t nkv;
+    tensor_t* tensors;
+    int64_t ntensors;
+    or_info info;
+    char arch[64];
+    int has_ple, has_output, has_dense;
+    float embedding_scale, per_layer_scale;
+    float* rope[MAX_LAYERS]; /* per layer (shared by head dim and base) */
+    int rope_owner[MAX_LAYERS];
+    float out_scale[MAX_LAYERS];
+};
+
+static int set_err(char* err, int errlen, int code, const char* fmt, ...) {
+    if (err && errlen > 0) {
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(err, (size_t)errlen, fmt, ap);
+        va_end(ap);
+    }
+    return code;
+}
+
+static int64_t type_block(uint32_t t) { return t == T_Q8_0 ? 32 : 1; }
+static int64_t type_bytes(uint32_t t) {
+    switch (t) {
+    case T_F32: return 4;
+    case T_F16: case T_BF16: return 2;
+    case T_Q8_0: return 34;
+    default: return -1;
+    }
+}
+static int64_t tensor_elems(const tensor_t* t) {
+    int64_t n = 1;
+    for (int i = 0; i < t->ndim; i++) n *= t->shape[i];
+    return n;
+}
+static int64_t tensor_bytes(const tensor_t* t) { return tensor_elems(t) / type_block(t->type) * type_bytes(t->type); }
+
+typedef struct {
+    const uint8_t* base;
+    size_t size, pos;
+} cursor_t;
+
+static int need(cursor_t* c, size_t n) { return c->pos + n <= c->size; }
+
+/* Skips one metadata value of `type` (GGUFFile.swift:124-176). Returns 0 on success. */
+static int skip_value(cursor_t* c, uint32_t type, int depth) {
+    static const int64_t fixed[] = {1, 1, 2, 2, 4, 4, 4, 1, -1, -1, 8, 8, 8};
+    if (type > 12 || depth > 4) return -1;
+    if (type == 8) {
+        if (!need(c, 8)) return -1;
+        uint64_t n;
+        memcpy(&n, c->base + c->pos, 8);
+        c->pos += 8;
+        if (!need(c, n)) return -1;
+        c->pos += n;
+        return 0;
+    }
+    if (type == 9) {
+        if (!need(c, 12)) return -1;
+        uint32_t et;
+        uint64_t n;
+        memcpy(&et, c->base + c->pos, 4);
+        memcpy(&n, c->base + c->pos + 4, 8);
+        c->pos += 12;
+        for (uint64_t i = 0; i < n; i++)
+            if (skip_value(c, et, depth + 1)) return -1;
+        return 0;
+    }
+    if (!need(c, (size_t)fixed[type])) return -1;
+    c->pos += (size_t)fixed[type];
+    return 0;
+}
+
+static const kv_t* find_kv(const or_model* m, const char* key) {
+    for (int64_t i = 0; i < m->nkv; i++)
+        if (strcmp(m->kvs[i].key, key) == 0) return &m->kvs[i];
+    return NULL;
+}
+
+/* GGUFValue.intValue / floatValue (GGUFValue.swift:26-46). */
+static int kv_int(const kv_t* kv, int64_t* out) {
+    const uint8_t* p = kv->raw;
+    switch (kv->type) {
+    case 0: *out = *(const uint8_t*)p; return 1;
+    case 1: *out = *(const int8_t*)p; return 1;
+    case 2: { uint16_t v; memcpy(&v, p, 2); *out = v; return 1; }
+    case 3: { int16_t v; memcpy(&v, p, 2); *out = v; return 1; }
+    case 4: { uint32_t v; memcpy(&v, p, 4); *out = v; return 1; }
+    case 5: { int32_t v; memcpy(&v, p, 4); *out = v; return 1; }
+    case 10: { uint64_t v; memcpy(&v, p, 8); *out = (int64_t)v; return 1; }
+    case 11: { int64_t v; memcpy(&v, p, 8); *out = v; return 1; }
+    default: return 0;
+    }
+}
+static int kv_float(const kv_t* kv, float* out) {
+    if (kv->type == 6) { memcpy(out, kv->raw, 4); return 1; }
+    if (kv->type == 12) { double d; memcpy(&d, kv->raw, 8); *out = (float)d; return 1; }
+    int64_t i;
+    if (kv_int(kv, &i)) { *out = (float)i; return 1; }
+    return 0;
+}
+
+static tensor_t* find_tensor(or_model* m, const char* name) {
+    for (int64_t i = 0; i < m->ntensors; i++)
+        if (strcmp(m->tensors[i].name, name) == 0) return &m->tensors[i];
+    return NULL;
+}
+
+static char* read_string(cursor_t* c) {
+    if (!need(c, 8)) return NULL;
+    uint64_t n;
+    memcpy(&n, c->base + c->pos, 8);
+    c->pos += 8;
+    if (!need(c, n)) return NULL;
+    char* s = (char*)malloc(n + 1);
+    memcpy(s, c->base + c->pos, n);
+    s[n] = 0;
+    c->pos += n;
+    return s;
+}
+
+/* GGUFFile.init (GGUFFile.swift:21-67) over a MAP_SHARED mapping (MappedFile.swift:17-39). */
+static int parse_gguf(or_model* m, const char* path, char* err, int errlen) {
+    int fd = open(path, O_RDONLY);
+    if (fd < 0) return set_err(err, errlen, OR_ERR_FILE_NOT_READABLE, "cannot read %s: %s", path, strerror(errno));
+    struct stat st;
+    if (fstat(fd, &st) != 0) {
+        close(fd);
+        return set_err(err, errlen, OR_ERR_FILE_NOT_READABLE, "cannot read %s: %s", path, strerror(errno));
+    }
+    if (st.st_size <= 0) {
+        close(fd);
+        return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: file is empty");
+    }
+    m->size = (size_t)st.st_size;
+    long page = sysconf(_SC_PAGESIZE);
+    m->mapped = (m->size + (size_t)page - 1) / (size_t)page * (size_t)page;
+    void* p = mmap(NULL, m->mapped, PROT_READ, MAP_SHARED, fd, 0);
+    close(fd);
+    if (p == MAP_FAILED) return set_err(err, errlen, OR_ERR_FILE_NOT_READABLE, "cannot read %s: mmap failed", path);
+    m->base = (uint8_t*)p;
+    cursor_t c = {m->base, m->size, 0};
+    uint32_t magic, version;
+    uint64_t ntensors, nkv;
+    if (!need(&c, 4)) return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: truncated header at byte 0");
+    memcpy(&magic, c.base, 4);
+    c.pos = 4;
+    if (magic != 0x46554747u) return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: bad magic 0x%x", magic);
+    if (!need(&c, 20)) return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: truncated header at byte %zu", c.pos);
+    memcpy(&version, c.base + 4, 4);
+    if (version != 2 && version != 3)
+        return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: unsupported version %u", version);
+    memcpy(&ntensors, c.base + 8, 8);
+    memcpy(&nkv, c.base + 16, 8);
+    c.pos = 24;
+    if (nkv > (1u << 20) || ntensors > (1u << 20))
+        return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: truncated header at byte %zu", c.pos);
+    m->kvs = (kv_t*)calloc(nkv ? nkv : 1, sizeof(kv_t));
+    for (uint64_t i = 0; i < nkv; i++) {
+        char* key = read_string(&c);
+        if (!key || !need(&c, 4))
+            return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: truncated header at byte %zu", c.pos);
+        m->kvs[i].key = key;
+        m->nkv = (int64_t)i + 1;
+        memcpy(&m->kvs[i].type, c.base + c.pos, 4);
+        c.pos += 4;
+        uint32_t t = m->kvs[i].type;
+        if (t > 12) return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: unknown metadata value type %u", t);
+        if (t == 9) {
+            if (!need(&c, 12))
+                return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: truncated header at byte %zu", c.pos);
+            memcpy(&m->kvs[i].elem, c.base + c.pos, 4);
+            memcpy(&m->kvs[i].count, c.base + c.pos + 4, 8);
+            m->kvs[i].raw = c.base + c.pos + 12;
+        } else {
+            m->kvs[i].raw = c.base + c.pos;
+        }
+        if (skip_value(&c, t, 0))
+            return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: truncated header at byte %zu", c.pos);
+    }
+    m->tensors = (tensor_t*)calloc(ntensors ? ntensors : 1, sizeof(tensor_t));
+    for (uint64_t i = 0; i < ntensors; i++) {
+        tensor_t* t = &m->tensors[i];
+        t->name = read_string(&c);
+        m->ntensors = (int64_t)i + 1;
+        if (!t->name || !need(&c, 4))
+            return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: truncated header at byte %zu", c.pos);
+        uint32_t nd;
+        memcpy(&nd, c.base + c.pos, 4);
+        c.pos += 4;
+        if (nd > 4) return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: tensor %s has %u dimensions", t->name, nd);
+        t->ndim = (int)nd;
+        for (uint32_t d = 0; d < nd; d++) {
+            if (!need(&c, 8))
+                return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: truncated header at byte %zu", c.pos);
+            uint64_t s;
+            memcpy(&s, c.base + c.pos, 8);
+            c.pos += 8;
+            t->shape[d] = (int64_t)s;
+        }
+        if (!need(&c, 12))
+            return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: truncated header at byte %zu", c.pos);
+        memcpy(&t->type, c.base + c.pos, 4);
+        memcpy(&t->offset, c.base + c.pos + 4, 8);
+        c.pos += 12;
+        if (type_bytes(t->type) < 0)
+            return set_err(err, errlen, OR_ERR_UNSUPPORTED_TENSOR_TYPE, "tensor %s uses unsupported storage type %u", t->name, t->type);
+    }
+    int64_t alignment = 32;
+    const kv_t* a = find_kv(m, "general.alignment");
+    if (a) {
+        int64_t v;
+        if (kv_int(a, &v) && v > 0) alignment = v;
+    }
+    size_t data = (c.pos + (size_t)alignment - 1) / (size_t)alignment * (size_t)alignment;
+    for (int64_t i = 0; i < m->ntensors; i++) {
+        tensor_t* t = &m->tensors[i];
+        if (data + t->offset + (uint64_t)tensor_bytes(t) > m->size)
+            return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: tensor %s extends past the end of the file", t->name);
+        t->data = m->base + data + t->offset;
+    }
+    return OR_OK;
+}
+
+/* ------------------------------------------------------------------ weights */
+static float f16_to_f32(uint16_t h) {
+    uint32_t s = (uint32_t)(h >> 15) << 31, e = (h >> 10) & 0x1f, f = h & 0x3ff, bits;
+    if (e == 0) {
+        if (f == 0) bits = s;
+        else { /* subnormal */
+            float v = ldexpf((float)f, -24);
+            return (h >> 15) ? -v : v;
+        }
+    } else if (e == 31) bits = s | 0x7f800000u | (f << 13);
+    else bits = s | ((e + 112) << 23) | (f << 13);
+    float r;
+    memcpy(&r, &bits, 4);
+    return r;
+}
+
+static int64_t tensor_cols(const tensor_t* t) { return t->shape[0]; }
+static int64_t tensor_rows(const tensor_t* t) { return tensor_elems(t) / t->shape[0]; }
+static int64_t row_bytes(const tensor_t* t) { return tensor_cols(t) / type_block(t->type) * type_bytes(t->type); }
+
+/* WeightTensor.dequantizeRow (Weights.swift:19-43). */
+static void dequant_row(const tensor_t* t, int64_t row, float* out) {
+    const uint8_t* p = t->data + row * row_bytes(t);
+    int64_t n = tensor_cols(t);
+    switch (t->type) {
+    case T_F32: memcpy(out, p, (size_t)n * 4); break;
+    case T_F16:
+        for (int64_t i = 0; i < n; i++) { uint16_t h; memcpy(&h, p + 2 * i, 2); out[i] = f16_to_f32(h); }
+        break;
+    case T_BF16:
+        for (int64_t i = 0; i < n; i++) {
+            uint16_t h;
+            memcpy(&h, p + 2 * i, 2);
+            uint32_t b = (uint32_t)h << 16;
+            memcpy(&out[i], &b, 4);
+        }
+        break;
+    case T_Q8_0:
+        for (int64_t b = 0; b < n / 32; b++) {
+            const uint8_t* bp = p + b * 34;
+            uint16_t h;
+            memcpy(&h, bp, 2);
+            float scale = f16_to_f32(h);
+            for (int j = 0; j < 32; j++) out[b * 32 + j] = scale * (float)(int8_t)bp[2 + j];
+        }
+        break;
+    }
+}
+
+static const float* matrix(or_model* m, tensor_t* t) {
+    if (!t->dequant) {
+        int64_t rows = tensor_rows(t), cols = tensor_cols(t);
+        float* d = (float*)malloc((size_t)(rows * cols) * 4);
+#pragma omp parallel for schedule(static)
+        for (int64_t r = 0; r < rows; r++) dequant_row(t, r, d + r * cols);
+        t->dequant = d;
+    }
+    (void)m;
+    return t->dequant;
+}
+
+int or_dequantize_row(or_model* m, const char* name, int64_t row, float* out, int64_t n) {
+    tensor_t* t = find_tensor(m, name);
+    if (!t) return OR_ERR_MISSING_TENSOR;
+    if (row < 0 || row >= tensor_rows(t) || n < tensor_cols(t)) return OR_ERR_INVALID_OPTIONS;
+    dequant_row(t, row, out);
+    return OR_OK;
+}
+
+/* ModelWeights.init's tensor(name, shape, types) check (Weights.swift:93-98). */
+static int check_tensor(or_model* m, const char* name, int64_t s0, int64_t s1, int f32_only, char* err, int errlen,
+                        tensor_t** out) {
+    tensor_t* t = find_tensor(m, name);
+    if (!t) return set_err(err, errlen, OR_ERR_MISSING_TENSOR, "weight file lacks tensor %s", name);
+    int want_nd = s1 < 0 ? 1 : 2;
+    if (t->ndim != want_nd || t->shape[0] != s0 || (want_nd == 2 && t->shape[1] != s1)) {
+        if (want_nd == 1)
+            return set_err(err, errlen, OR_ERR_SHAPE_MISMATCH, "tensor %s has shape [%lld], expected [%lld]", name,
+                           (long long)t->shape[0], (long long)s0);
+        return set_err(err, errlen, OR_ERR_SHAPE_MISMATCH, "tensor %s has shape [%lld, %lld], expected [%lld, %lld]",
+                       name, (long long)t->shape[0], (long long)(t->ndim > 1 ? t->shape[1] : 1), (long long)s0,
+                       (long long)s1);
+    }
+    if (f32_only && t->type != T_F32)
+        return set_err(err, errlen, OR_ERR_UNSUPPORTED_TENSOR_TYPE, "tensor %s uses unsupported storage type %u", name, t->type);
+    if (out) *out = t;
+    return OR_OK;
+}
+
+/* ModelConfig.init (ModelConfig.swift:54-112), accepting the reference's
+ * gemma-embedding2 and the measured gemma-embedding shape. */
+static int read_config(or_model* m, char* err, int errlen) {
+    const kv_t* a = find_kv(m, "general.architecture");
+    if (!a || a->type != 8) return set_err(err, errlen, OR_ERR_UNSUPPORTED_ARCHITECTURE, "unsupported architecture ''");
+    uint64_t n;
+    memcpy(&n, a->raw, 8);
+    if (n >= sizeof(m->arch)) n = sizeof(m->arch) - 1;
+    memcpy(m->arch, a->raw + 8, n);
+    m->arch[n] = 0;
+    if (strcmp(m->arch, "gemma-embedding2") != 0 && strcmp(m->arch, "gemma-embedding") != 0)
+        return set_err(err, errlen, OR_ERR_UNSUPPORTED_ARCHITECTURE, "unsupported architecture '%s'", m->arch);
+    char key[256];
+#define INT_KEY(dst, k)                                                                                 \
+    do {                                                                                                \
+        snprintf(key, sizeof key, "%s.%s", m->arch, k);                                                 \
+        const kv_t* kv_ = find_kv(m, key);                                                              \
+        int64_t v_;                                                                                     \
+        if (!kv_ || !kv_int(kv_, &v_)) return set_err(err, errlen, OR_ERR_MISSING_METADATA, "weight file lacks metadata key %s", key); \
+        dst = (int32_t)v_;                                                                              \
+    } while (0)
+#define FLOAT_KEY(dst, k)                                                                               \
+    do {                                                                                                \
+        snprintf(key, sizeof key, "%s.%s", m->arch, k);                                                 \
+        const kv_t* kv_ = find_kv(m, key);                                                              \
+        if (!kv_ || !kv_float(kv_, &dst)) return set_err(err, errlen, OR_ERR_MISSING_METADATA, "weight file lacks metadata key %s", key); \
+    } while (0)
+    or_info* I = &m->info;
+    INT_KEY(I->layers, "block_count");
+    INT_KEY(I->hidden, "embedding_length");
+    INT_KEY(I->heads, "attention.head_count");
+    if (I->layers <= 0 || I->layers > MAX_LAYERS)
+        return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: %d layers", I->layers);
+    snprintf(key, sizeof key, "%s.attention.head_count_kv", m->arch);
+    const kv_t* kvh = find_kv(m, key);
+    if (!kvh || kvh->type != 9 || (int64_t)kvh->count != I->layers || (kvh->elem != 5 && kvh->elem != 4))
+        return set_err(err, errlen, OR_ERR_MISSING_METADATA, "weight file lacks metadata key %s", key);
+    snprintf(key, sizeof key, "%s.attention.sliding_window_pattern", m->arch);
+    const kv_t* pat = find_kv(m, key);
+    if (!pat || pat->type != 9 || pat->elem != 7 || (int64_t)pat->count != I->layers)
+        return set_err(err, errlen, OR_ERR_MISSING_METADATA, "weight file lacks metadata key %s", key);
+    int32_t hdg, hds, vg, vs;
+    INT_KEY(hdg, "attention.key_length");
+    INT_KEY(hds, "attention.key_length_swa");
+    INT_KEY(vg, "attention.value_length");
+    INT_KEY(vs, "attention.value_length_swa");
+    if (vg != hdg || vs != hds) return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: key and value head sizes differ");
+    float rope_g, rope_s;
+    FLOAT_KEY(rope_g, "rope.freq_base");
+    snprintf(key, sizeof key, "%s.rope.freq_base_swa", m->arch);
+    const kv_t* rs = find_kv(m, key);
+    if (!rs || !kv_float(rs, &rope_s)) rope_s = rope_g;
+    const kv_t* toks = find_kv(m, "tokenizer.ggml.tokens");
+    if (!toks || toks->type != 9 || toks->elem != 8)
+        return set_err(err, errlen, OR_ERR_MISSING_METADATA, "weight file lacks metadata key tokenizer.ggml.tokens");
+    I->vocab = (int32_t)toks->count;
+    INT_KEY(I->out_dim, "embedding_length_out");
+    INT_KEY(I->ff, "feed_forward_length");
+    INT_KEY(I->per_layer, "embedding_length_per_layer_input");
+    INT_KEY(I->sliding_window, "attention.sliding_window");
+    FLOAT_KEY(I->eps, "attention.layer_norm_rms_epsilon");
+    I->max_tokens = 8192; /* ModelConfig.supportedMaxTokens (ModelConfig.swift:52) */
+    for (int i = 0; i < I->layers; i++) {
+        int32_t kvn;
+        memcpy(&kvn, kvh->raw + 4 * i, 4);
+        I->sliding[i] = pat->raw[i] != 0;
+        I->kv_heads[i] = kvn;
+        I->head_dim[i] = I->sliding[i] ? hds : hdg;
+        I->rope_base[i] = I->sliding[i] ? rope_s : rope_g;
+    }
+    m->embedding_scale = sqrtf((float)I->hidden);
+    m->per_layer_scale = 1.0f / sqrtf((float)I->hidden);
+    return OR_OK;
+#undef INT_KEY
+#undef FLOAT_KEY
+}
+
+static int check_weights(or_model* m, char* err, int errlen) {
+    or_info* I = &m->info;
+    int d = I->hidden, ff = I->ff, pl = I->per_layer, rc;
+    char name[128];
+    if ((rc = check_tensor(m, "token_embd.weight", d, I->vocab, 0, err, errlen, NULL))) return rc;
+    m->has_ple = pl > 0;
+    if (m->has_ple) {
+        if ((rc = check_tensor(m, "per_layer_model_proj.weight", d, (int64_t)pl * I->layers, 0, err, errlen, NULL))) return rc;
+        if ((rc = check_tensor(m, "per_layer_proj_norm.weight", pl, -1, 1, err, errlen, NULL))) return rc;
+    }
+    if ((rc = check_tensor(m, "output_norm.weight", d, -1, 1, err, errlen, NULL))) return rc;
+    m->has_output = strcmp(m->arch, "gemma-embedding2") == 0;
+    if (m->has_output) {
+        if ((rc = check_tensor(m, "output.weight", d, I->out_dim, 0, err, errlen, NULL))) return rc;
+        I->dense_head = 0;
+    } else {
+        tensor_t* t = find_tensor(m, "dense_2.weight");
+        if (!t) return set_err(err, errlen, OR_ERR_MISSING_TENSOR, "weight file lacks tensor dense_2.weight");
+        I->dense_head = t->ndim == 2 ? (int32_t)t->shape[1] : 0;
+        if ((rc = check_tensor(m, "dense_2.weight", d, I->dense_head, 0, err, errlen, NULL))) return rc;
+        if ((rc = check_tensor(m, "dense_3.weight", I->dense_head, I->out_dim, 0, err, errlen, NULL))) return rc;
+        m->has_dense = 1;
+    }
+    for (int i = 0; i < I->layers; i++) {
+        int hd = I->head_dim[i], qd = I->heads * hd, kvd = I->kv_heads[i] * hd;
+#define CHK(suffix, a, b, f32)                                                        \
+    snprintf(name, sizeof name, "blk.%d.%s", i, suffix);                              \
+    if ((rc = check_tensor(m, name, a, b, f32, err, errlen, NULL))) return rc;
+        CHK("attn_norm.weight", d, -1, 1);
+        CHK("attn_q.weight", d, qd, 0);
+        CHK("attn_k.weight", d, kvd, 0);
+        CHK("attn_v.weight", d, kvd, 0);
+        CHK("attn_output.weight", qd, d, 0);
+        CHK("attn_q_norm.weight", hd, -1, 1);
+        CHK("attn_k_norm.weight", hd, -1, 1);
+        CHK("post_attention_norm.weight", d, -1, 1);
+        CHK("ffn_norm.weight", d, -1, 1);
+        CHK("ffn_gate.weight", d, ff, 0);
+        CHK("ffn_up.weight", d, ff, 0);
+        CHK("ffn_down.weight", ff, d, 0);
+        CHK("post_ffw_norm.weight", d, -1, 1);
+        m->out_scale[i] = 1.0f;
+        if (m->has_ple) {
+            CHK("inp_gate.weight", d, pl, 0);
+            CHK("proj.weight", pl, d, 0);
+            CHK("post_norm.weight", d, -1, 1);
+            tensor_t* s;
+            snprintf(name, sizeof name, "blk.%d.layer_output_scale.weight", i);
+            if ((rc = check_tensor(m, name, 1, -1, 1, err, errlen, &s))) return rc;
+            memcpy(&m->out_scale[i], s->data, 4);
+        }
+#undef CHK
+    }
+    return OR_OK;
+}
+
+void or_close(or_model* m) {
+    if (!m) return;
+    for (int64_t i = 0; i < m->ntensors; i++) {
+        free(m->tensors[i].name);
+        free(m->tensors[i].dequant);
+    }
+    for (int64_t i = 0; i < m->nkv; i++) free(m->kvs[i].key);
+    free(m->tensors);
+    free(m->kvs);
+    for (int i = 0; i < MAX_LAYERS; i++)
+        if (m->rope_owner[i]) free(m->rope[i]);
+    if (m->base) munmap(m->base, m->mapped);
+    free(m);
+}
+
+int or_open(const char* path, or_model** out, char* err, int errlen) {
+    *out = NULL;
+    or_model* m = (or_model*)calloc(1, sizeof(or_model));
+    int rc = parse_gguf(m, path, err, errlen);
+    if (!rc) rc = read_config(m, err, errlen);
+    if (!rc) rc = check_weights(m, err, errlen);
+    if (rc) {
+        or_close(m);
+        return rc;
+    }
+    /* One table per (head dim, base), as CPUReference.ropeTable caches them (CPUReference.swift:21-28). */
+    for (int i = 0; i < m->info.layers; i++) {
+        for (int j = 0; j < i; j++)
+            if (m->info.head_dim[j] == m->info.head_dim[i] && m->info.rope_base[j] == m->info.rope_base[i]) {
+                m->rope[i] = m->rope[j];
+                break;
+            }
+        if (!m->rope[i]) {
+            int pairs = m->info.head_dim[i] / 2;
+            m->rope[i] = (float*)malloc((size_t)m->info.max_tokens * pairs * 2 * 4);
+            or_rope_table(m->info.head_dim[i], m->info.rope_base[i], m->info.max_tokens, m->rope[i]);
+            m->rope_owner[i] = 1;
+        }
+    }
+    *out = m;
+    return OR_OK;
+}
+
+int or_get_info(const or_model* m, or_info* info) {
+    *info = m->info;
+    return OR_OK;
+}
+
+void or_set_threads(int n) {
+    if (n > 0) omp_set_num_threads(n);
+}
+int or_threads(void) { return omp_get_max_threads(); }
+
+/* ------------------------------------------------------------------ math */
+/* RopeTable.init (RopeTable.swift:16-31): invFreq = base^(-2i/hd) in double, cos/sin rounded to float. */
+void or_rope_table(int32_t head_dim, float base, int32_t positions, float* values) {
+    int pairs = head_dim / 2;
+    for (int i = 0; i < pairs; i++) {
+        double inv = pow((double)base, -2.0 * (double)i / (double)head_dim);
+        for (int pos = 0; pos < positions; pos++) {
+            double theta = (double)pos * inv;
+            values[((size_t)pos * pairs + i) * 2] = (float)cos(theta);
+            values[((size_t)pos * pairs + i) * 2 + 1] = (float)sin(theta);
+        }
+    }
+}
+
+typedef float v8 __attribute__((vector_size(32)));
+
+static inline float hsum8(v8 s) { return ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7])); }
+
+static inline float dot_tail(const float* a, const float* b, int64_t k0, int64_t k, float s) {
+    for (int64_t i = k0; i < k; i++) s += a[i] * b[i];
+    return s;
+}
+
+/* CPUReference.matmul (CPUReference.swift:63-74): y[M,N] = x[M,K] * w[N,K]^T in fp32.
+ * Blocked 4 rows x 2 weight rows; each output is one fixed-order fp32 sum. */
+void or_matmul(const float* x, int64_t m, int64_t k, const float* w, int64_t n, float* y) {
+    int64_t k8 = k / 8 * 8;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t mb = 0; mb < (m + 3) / 4; mb++) {
+        int64_t r0 = mb * 4, rn = m - r0 < 4 ? m - r0 : 4;
+        for (int64_t j = 0; j < n; j += 2) {
+            int64_t jn = n - j < 2 ? n - j : 2;
+            v8 acc[4][2];
+            memset(acc, 0, sizeof acc);
+            for (int64_t i = 0; i < k8; i += 8) {
+                v8 wv[2];
+                for (int c = 0; c < jn; c++) memcpy(&wv[c], w + (j + c) * k + i, 32);
+                for (int r = 0; r < rn; r++) {
+                    v8 xv;
+                    memcpy(&xv, x + (r0 + r) * k + i, 32);
+                    for (int c = 0; c < jn; c++) acc[r][c] += xv * wv[c];
+                }
+            }
+            for (int r = 0; r < rn; r++)
+                for (int c = 0; c < jn; c++)
+                    y[(r0 + r) * n + j + c] = dot_tail(x + (r0 + r) * k, w + (j + c) * k, k8, k, hsum8(acc[r][c]));
+        }
+    }
+}
+
+/* CPUReference.rmsNorm (CPUReference.swift:77-90). weight may be NULL. */
+void or_rmsnorm(const float* x, int64_t rows, int64_t width, const float* weight, float eps, float* out) {
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++) {
+        float ss = 0;
+        for (int64_t i = 0; i < width; i++) {
+            float v = x[r * width + i];
+            ss += v * v;
+        }
+        float inv = 1.0f / sqrtf(ss / (float)width + eps);
+        for (int64_t i = 0; i < width; i++) out[r * width + i] = x[r * width + i] * inv * (weight ? weight[i] : 1.0f);
+    }
+}
+
+/* CPUReference.geluTanh (CPUReference.swift:92-95). */
+float or_gelu_tanh(float x) {
+    const float c = 0.79788456080286535587989211986876f;
+    return 0.5f * x * (1.0f + tanhf(c * x * (1.0f + 0.044715f * x * x)));
+}
+
+/* CPUReference.rope (CPUReference.swift:98-113), positions 0..T-1. */
+static void rope(float* x, int64_t tokens, int64_t heads, int64_t hd, const float* table) {
+    int64_t half = hd / 2;
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < tokens; t++)
+        for (int64_t h = 0; h < heads; h++) {
+            float* o = x + (t * heads + h) * hd;
+            for (int64_t i = 0; i < half; i++) {
+                float c = table[(t * half + i) * 2], s = table[(t * half + i) * 2 + 1];
+                float a = o[i], b = o[i + half];
+                o[i] = a * c - b * s;
+                o[i + half] = a * s + b * c;
+            }
+        }
+}
+
+/* CPUReference.attention (CPUReference.swift:117-174): bidirectional, GQA, keys with
+ * |i - j| > window / 2 masked when window > 0, softmax with expf in fp32.
+ * Computed one query row at a time; each row's arithmetic is the reference's. */
+void or_attention(const float* q, const float* k, const float* v, int32_t tokens, int32_t heads, int32_t kv_heads,
+                  int32_t hd, float scale, int32_t window, float* out) {
+    int group = heads / kv_heads;
+#pragma omp parallel
+    {
+        float* s = (float*)malloc((size_t)tokens * 4);
+        float* acc = (float*)malloc((size_t)hd * 4);
+#pragma omp for schedule(dynamic, 4) collapse(2)
+        for (int h = 0; h < heads; h++)
+            for (int i = 0; i < tokens; i++) {
+                int kh = h / group;
+                const float* qi = q + ((int64_t)i * heads + h) * hd;
+                float mx = -INFINITY;
+                for (int j = 0; j < tokens; j++) {
+                    if (window > 0 && abs(i - j) > window / 2) {
+                        s[j] = -INFINITY;
+                        continue;
+                    }
+                    const float* kj = k + ((int64_t)j * kv_heads + kh) * hd;
+                    v8 a8 = {0};
+                    int d = 0;
+                    for (; d + 8 <= hd; d += 8) {
+                        v8 qa, ka;
+                        memcpy(&qa, qi + d, 32);
+                        memcpy(&ka, kj + d, 32);
+                        a8 += qa * ka;
+                    }
+                    float dot = dot_tail(qi, kj, d, hd, hsum8(a8));
+                    s[j] = dot * scale;
+                    if (s[j] > mx) mx = s[j];
+                }
+                float sum = 0;
+                for (int j = 0; j < tokens; j++) {
+                    float e = s[j] == -INFINITY ? 0.0f : expf(s[j] - mx);
+                    s[j] = e;
+                    sum += e;
+                }
+                float inv = 1.0f / sum;
+                for (int d = 0; d < hd; d++) acc[d] = 0;
+                for (int j = 0; j < tokens; j++) {
+                    float p = s[j] * inv;
+                    if (p == 0.0f) continue;
+                    const float* vj = v + ((int64_t)j * kv_heads + kh) * hd;
+                    for (int d = 0; d < hd; d++) acc[d] += p * vj[d];
+                }
+                memcpy(out + ((int64_t)i * heads + h) * hd, acc, (size_t)hd * 4);
+            }
+        free(s);
+        free(acc);
+    }
+}
+
+/* ------------------------------------------------------------------ forward */
+static void trace(or_trace_fn fn, void* user, const char* name, const float* data, int64_t n) {
+    if (fn) fn(name, data, n, user);
+}
+
+static tensor_t* layer_tensor(or_model* m, int l, const char* suffix) {
+    char name[128];
+    snprintf(name, sizeof name, "blk.%d.%s", l, suffix);
+    return find_tensor(m, name);
+}
+
+/* CPUReference.forward(rows:trace:) (CPUReference.swift:183-283) over token rows. For the
+ * gemma-embedding shape (no per-layer inputs, no output projection) the layer loop is the
+ * same without lines 206-210 and 259-270, and the pooled mean of rmsnorm(x, output_norm)
+ * goes through dense_2 then dense_3. */
+int or_forward(or_model* m, const int32_t* tokens, int32_t T, float* pooled, or_trace_fn tr, void* user) {
+    const or_info* I = &m->info;
+    const int64_t d = I->hidden, ff = I->ff, pl = I->per_layer, L = I->layers;
+    const float eps = I->eps;
+    if (T <= 0 || T > I->max_tokens) return OR_ERR_INVALID_OPTIONS;
+    for (int t = 0; t < T; t++)
+        if (tokens[t] < 0 || tokens[t] >= I->vocab) return OR_ERR_INVALID_OPTIONS;
+    char name[64];
+    float* x = (float*)malloc((size_t)(T * d) * 4);
+    tensor_t* emb = find_tensor(m, "token_embd.weight");
+    for (int64_t t = 0; t < T; t++) {
+        dequant_row(emb, tokens[t], x + t * d);
+        for (int64_t i = 0; i < d; i++) x[t * d + i] *= m->embedding_scale;
+    }
+    trace(tr, user, "inp_scaled", x, T * d);
+
+    float* perLayer = NULL;
+    if (m->has_ple) {
+        const float* w = matrix(m, find_tensor(m, "per_layer_model_proj.weight"));
+        perLayer = (float*)malloc((size_t)(T * pl * L) * 4);
+        or_matmul(x, T, d, w, pl * L, perLayer);
+        for (int64_t i = 0; i < T * pl * L; i++) perLayer[i] *= m->per_layer_scale;
+        or_rmsnorm(perLayer, T * L, pl, matrix(m, find_tensor(m, "per_layer_proj_norm.weight")), eps, perLayer);
+        trace(tr, user, "inp_per_layer", perLayer, T * pl * L);
+    }
+
+    int64_t maxq = 0, maxkv = 0;
+    for (int l = 0; l < L; l++) {
+        if (I->heads * I->head_dim[l] > maxq) maxq = I->heads * I->head_dim[l];
+        if (I->kv_heads[l] * I->head_dim[l] > maxkv) maxkv = I->kv_heads[l] * I->head_dim[l];
+    }
+    float* h = (float*)malloc((size_t)(T * d) * 4);
+    float* q = (float*)malloc((size_t)(T * maxq) * 4);
+    float* k = (float*)malloc((size_t)(T * maxkv) * 4);
+    float* v = (float*)malloc((size_t)(T * maxkv) * 4);
+    float* attn = (float*)malloc((size_t)(T * maxq) * 4);
+    float* o = (float*)malloc((size_t)(T * d) * 4);
+    float* gate = (float*)malloc((size_t)(T * ff) * 4);
+    float* up = (float*)malloc((size_t)(T * ff) * 4);
+    float* g = pl ? (float*)malloc((size_t)(T * pl) * 4) : NULL;
+
+    for (int l = 0; l < L; l++) {
+        const int64_t heads = I->heads, kvh = I->kv_heads[l], hd = I->head_dim[l];
+        or_rmsnorm(x, T, d, matrix(m, layer_tensor(m, l, "attn_norm.weight")), eps, h);
+        snprintf(name, sizeof name, "attn_norm-%d", l); trace(tr, user, name, h, T * d);
+        or_matmul(h, T, d, matrix(m, layer_tensor(m, l, "attn_q.weight")), heads * hd, q);
+        or_matmul(h, T, d, matrix(m, layer_tensor(m, l, "attn_k.weight")), kvh * hd, k);
+        or_matmul(h, T, d, matrix(m, layer_tensor(m, l, "attn_v.weight")), kvh * hd, v);
+        snprintf(name, sizeof name, "Qcur-%d", l); trace(tr, user, name, q, T * heads * hd);
+        snprintf(name, sizeof name, "Kcur-%d", l); trace(tr, user, name, k, T * kvh * hd);
+        snprintf(name, sizeof name, "Vcur-%d", l); trace(tr, user, name, v, T * kvh * hd);
+        or_rmsnorm(q, T * heads, hd, matrix(m, layer_tensor(m, l, "attn_q_norm.weight")), eps, q);
+        or_rmsnorm(k, T * kvh, hd, matrix(m, layer_tensor(m, l, "attn_k_norm.weight")), eps, k);
+        or_rmsnorm(v, T * kvh, hd, NULL, eps, v);
+        snprintf(name, sizeof name, "Qcur_normed-%d", l); trace(tr, user, name, q, T * heads * hd);
+        snprintf(name, sizeof name, "Kcur_normed-%d", l); trace(tr, user, name, k, T * kvh * hd);
+        snprintf(name, sizeof name, "Vcur_normed-%d", l); trace(tr, user, name, v, T * kvh * hd);
+        rope(q, T, heads, hd, m->rope[l]);
+        rope(k, T, kvh, hd, m->rope[l]);
+        snprintf(name, sizeof name, "Qcur_pos-%d", l); trace(tr, user, name, q, T * heads * hd);
+        snprintf(name, sizeof name, "Kcur_pos-%d", l); trace(tr, user, name, k, T * kvh * hd);
+        or_attention(q, k, v, T, (int32_t)heads, (int32_t)kvh, (int32_t)hd, 1.0f,
+                     I->sliding[l] ? I->sliding_window : 0, attn);
+        snprintf(name, sizeof name, "kqv_out-%d", l); trace(tr, user, name, attn, T * heads * hd);
+        or_matmul(attn, T, heads * hd, matrix(m, layer_tensor(m, l, "attn_output.weight")), d, o);
+        or_rmsnorm(o, T, d, matrix(m, layer_tensor(m, l, "post_attention_norm.weight")), eps, o);
+        snprintf(name, sizeof name, "attn_post_norm-%d", l); trace(tr, user, name, o, T * d);
+        for (int64_t i = 0; i < T * d; i++) x[i] += o[i];
+        snprintf(name, sizeof name, "attn_out-%d", l); trace(tr, user, name, x, T * d);
+
+        or_rmsnorm(x, T, d, matrix(m, layer_tensor(m, l, "ffn_norm.weight")), eps, h);
+        snprintf(name, sizeof name, "ffn_norm-%d", l); trace(tr, user, name, h, T * d);
+        or_matmul(h, T, d, matrix(m, layer_tensor(m, l, "ffn_gate.weight")), ff, gate);
+        or_matmul(h, T, d, matrix(m, layer_tensor(m, l, "ffn_up.weight")), ff, up);
+        for (int64_t i = 0; i < T * ff; i++) gate[i] = or_gelu_tanh(gate[i]) * up[i];
+        snprintf(name, sizeof name, "ffn_geglu-%d", l); trace(tr, user, name, gate, T * ff);
+        or_matmul(gate, T, ff, matrix(m, layer_tensor(m, l, "ffn_down.weight")), d, o);
+        snprintf(name, sizeof name, "ffn_out-%d", l); trace(tr, user, name, o, T * d);
+        or_rmsnorm(o, T, d, matrix(m, layer_tensor(m, l, "post_ffw_norm.weight")), eps, o);
+        snprintf(name, sizeof name, "ffn_post_norm-%d", l); trace(tr, user, name, o, T * d);
+        for (int64_t i = 0; i < T * d; i++) x[i] += o[i];
+        snprintf(name, sizeof name, "pe_in-%d", l); trace(tr, user, name, x, T * d);
+
+        if (m->has_ple) {
+            or_matmul(x, T, d, matrix(m, layer_tensor(m, l, "inp_gate.weight")), pl, g);
+            for (int64_t t = 0; t < T; t++)
+                for (int64_t i = 0; i < pl; i++) {
+                    int64_t idx = t * pl + i;
+                    g[idx] = or_gelu_tanh(g[idx]) * perLayer[(t * L + l) * pl + i];
+                }
+            or_matmul(g, T, pl, matrix(m, layer_tensor(m, l, "proj.weight")), d, o);
+            or_rmsnorm(o, T, d, matrix(m, layer_tensor(m, l, "post_norm.weight")), eps, o);
+            snprintf(name, sizeof name, "per_layer_embd_out-%d", l); trace(tr, user, name, o, T * d);
+            for (int64_t i = 0; i < T * d; i++) x[i] = (x[i] + o[i]) * m->out_scale[l];
+        }
+        snprintf(name, sizeof name, "l_out-%d", l); trace(tr, user, name, x, T * d);
+    }
+
+    or_rmsnorm(x, T, d, matrix(m, find_tensor(m, "output_norm.weight")), eps, h);
+    trace(tr, user, "result_norm", h, T * d);
+    const int64_t od = I->out_dim;
+    if (m->has_output) {
+        float* proj = (float*)malloc((size_t)(T * od) * 4);
+        or_matmul(h, T, d, matrix(m, find_tensor(m, "output.weight")), od, proj);
+        trace(tr, user, "result_embd", proj, T * od);
+        for (int64_t i = 0; i < od; i++) pooled[i] = 0;
+        for (int64_t t = 0; t < T; t++)
+            for (int64_t i = 0; i < od; i++) pooled[i] += proj[t * od + i];
+        for (int64_t i = 0; i < od; i++) pooled[i] /= (float)T;
+        free(proj);
+    } else {
+        float* mean = (float*)calloc((size_t)d, 4);
+        for (int64_t t = 0; t < T; t++)
+            for (int64_t i = 0; i < d; i++) mean[i] += h[t * d + i];
+        for (int64_t i = 0; i < d; i++) mean[i] /= (float)T;
+        trace(tr, user, "result_pooled", mean, d);
+        float* mid = (float*)malloc((size_t)I->dense_head * 4);
+        or_matmul(mean, 1, d, matrix(m, find_tensor(m, "dense_2.weight")), I->dense_head, mid);
+        trace(tr, user, "result_dense_2", mid, I->dense_head);
+        or_matmul(mid, 1, I->dense_head, matrix(m, find_tensor(m, "dense_3.weight")), od, pooled);
+        trace(tr, user, "result_embd", pooled, od);
+        free(mean);
+        free(mid);
+    }
+    free(x); free(h); free(q); free(k); free(v); free(attn); free(o); free(gate); free(up); free(g); free(perLayer);
+    return OR_OK;
+}
+
+/* ------------------------------------------------------------------ host logic */
+/* EmbeddingModel.batches (EmbeddingModel.swift:200-215). batch_size <= 0 means nil.
+ * costs is [n][ncost]; ranges receives (start, end) pairs; returns the range count. */
+int32_t or_batches(const int64_t* costs, int32_t n, int32_t ncost, int32_t batch_size, const int64_t* budgets,
+                   int32_t* ranges) {
+    int32_t count = 0, start = 0;
+    int64_t totals[16] = {0};
+    if (ncost > 16) return -1;
+    for (int32_t i = 0; i < n; i++) {
+        int full;
+        if (batch_size > 0) full = i - start >= batch_size;
+        else {
+            full = 0;
+            for (int c = 0; c < ncost; c++)
+                if (totals[c] + costs[(int64_t)i * ncost + c] > budgets[c]) full = 1;
+        }
+        if (i > start && full) {
+            ranges[2 * count] = start;
+            ranges[2 * count + 1] = i;
+            count++;
+            start = i;
+            for (int c = 0; c < ncost; c++) totals[c] = 0;
+        }
+        for (int c = 0; c < ncost; c++) totals[c] += costs[(int64_t)i * ncost + c];
+    }
+    if (start < n) {
+        ranges[2 * count] = start;
+        ranges[2 * count + 1] = n;
+        count++;
+    }
+    return count;
+}
+
+/* EmbeddingModel.finish (EmbeddingModel.swift:260-267). */
+void or_finish(const float* v, int32_t n, int32_t dims, int32_t normalise, float* out) {
+    int32_t k = dims < n ? dims : n;
+    for (int32_t i = 0; i < k; i++) out[i] = v[i];
+    if (normalise) {
+        float s = 0;
+        for (int32_t i = 0; i < k; i++) s += out[i] * out[i];
+        float norm = sqrtf(s);
+        if (norm > 0)
+            for (int32_t i = 0; i < k; i++) out[i] /= norm;
+    }
+}
+
+/* SeededRandom.next (Tests/GemmaEmbedTests/KernelTests.swift:14-20). *state holds
+ * the generator state (seed + 0x9E3779B97F4A7C15 after init). */
+uint64_t or_seeded_next(uint64_t* state) {
+    *state += 0x9E3779B97F4A7C15ull;
+    uint64_t z = *state;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}

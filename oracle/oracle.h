@@ -1,0 +1,86 @@
+/*
+ * oracle.h -- CPU restatement of the reference's fp32 forward pass.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the checker for the CUDA path:
+ * only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference
+ * arm may load it.  The product library never links or calls it.
+ *
+ * It restates, in plain C with fp32 arithmetic:
+ *   - GGUF parsing        Sources/GemmaEmbed/GGUF/GGUFFile.swift:21-67, GGUFValue.swift:83-131
+ *   - model config        Sources/GemmaEmbed/Model/ModelConfig.swift:54-112
+ *   - weight views        Sources/GemmaEmbed/Model/Weights.swift:19-43, 92-132
+ *   - RoPE table          Sources/GemmaEmbed/Model/RopeTable.swift:16-31
+ *   - forward             Sources/GemmaEmbed/Model/CPUReference.swift:63-283
+ *   - batch planning      Sources/GemmaEmbed/EmbeddingModel.swift:200-215
+ *   - finish              Sources/GemmaEmbed/EmbeddingModel.swift:260-267
+ *
+ * Parity pins: the batch planner is pinned by the reference's known answers
+ * (Tests/GemmaEmbedTests/EmbeddingModelTests.swift:101-109, committed as
+ * tests/golden/batches.json); the Q8_0 block layout by the tensor offsets in
+ * Tests/GemmaEmbedTests/Fixtures/model.json.  The forward's numerics are
+ * "parity unpinned": the reference's golden embeddings need the real
+ * embeddinggemma GGUF, which is not available, and the reference itself
+ * (Swift + Accelerate) cannot be built on Linux.  The forward is a
+ * line-by-line restatement checked by internal consistency tests.
+ */
+#ifndef GE_ORACLE_H
+#define GE_ORACLE_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes: the same numbering as include/gemma_embed.h. */
+enum {
+    OR_OK = 0,
+    OR_ERR_FILE_NOT_READABLE = 1,
+    OR_ERR_INVALID_GGUF = 2,
+    OR_ERR_UNSUPPORTED_TENSOR_TYPE = 3,
+    OR_ERR_UNSUPPORTED_ARCHITECTURE = 4,
+    OR_ERR_MISSING_TENSOR = 5,
+    OR_ERR_MISSING_METADATA = 6,
+    OR_ERR_SHAPE_MISMATCH = 7,
+    OR_ERR_INVALID_OPTIONS = 9,
+};
+
+typedef struct or_model or_model;
+
+typedef struct {
+    int32_t hidden, layers, heads, ff, per_layer, out_dim, dense_head, vocab, sliding_window, max_tokens;
+    float eps;
+    int32_t kv_heads[64], head_dim[64], sliding[64];
+    float rope_base[64];
+} or_info;
+
+typedef void (*or_trace_fn)(const char* name, const float* data, int64_t count, void* user);
+
+int or_open(const char* path, or_model** out, char* err, int errlen);
+void or_close(or_model* m);
+int or_get_info(const or_model* m, or_info* info);
+/* Threads used by the OpenMP regions (0 = all available). */
+void or_set_threads(int n);
+int or_threads(void);
+
+/* CPUReference.forward(tokens:trace:): the pooled, unnormalised vector of one sequence. */
+int or_forward(or_model* m, const int32_t* tokens, int32_t T, float* pooled, or_trace_fn trace, void* user);
+
+/* WeightTensor.dequantizeRow for any tensor by name. */
+int or_dequantize_row(or_model* m, const char* tensor, int64_t row, float* out, int64_t n);
+
+/* Static pieces, exposed for unit tests. */
+void or_matmul(const float* x, int64_t m, int64_t k, const float* w, int64_t n, float* y);
+void or_rmsnorm(const float* x, int64_t rows, int64_t width, const float* weight, float eps, float* out);
+float or_gelu_tanh(float x);
+void or_rope_table(int32_t head_dim, float base, int32_t positions, float* values);
+void or_attention(const float* q, const float* k, const float* v, int32_t tokens, int32_t heads, int32_t kv_heads,
+                  int32_t hd, float scale, int32_t window, float* out);
+int32_t or_batches(const int64_t* costs, int32_t n, int32_t ncost, int32_t batch_size, const int64_t* budgets,
+                   int32_t* ranges);
+void or_finish(const float* v, int32_t n, int32_t dims, int32_t normalise, float* out);
+uint64_t or_seeded_next(uint64_t* state);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
