@@ -1,0 +1,290 @@
+"""B200 EmbeddingGemma text encoder behind the reference's EmbeddingModel API.
+
+Python mirror of `Sources/GemmaEmbed/EmbeddingModel.swift` and `EmbedOptions.swift` over the
+C ABI of libgemma_embed_cuda.so (include/gemma_embed.h).  Texts are passed pre-tokenised
+(lists of token ids): the tokenizer (`Tokenizer/Tokenizer.swift`) is outside this package.
+
+    model = EmbeddingModel.load(path)
+    docs = model.embed([[2, 651, 1], [2, 9, 10, 1]])            # list[Embedding]
+    raw = model.embed_tokens([[2, 651, 1]])                    # pooled, unnormalised [n][768]
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from typing import Callable, Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+
+__all__ = ["EmbeddingModel", "EmbedOptions", "LoadOptions", "Embedding", "EmbeddingProgress", "ModelInfo",
+           "GemmaEmbedError", "TaskPrefix", "ALLOWED_DIMENSIONS"]
+
+ALLOWED_DIMENSIONS = (768, 512, 256, 128)
+
+# ge_status codes (include/gemma_embed.h) by GemmaEmbedError case (Errors.swift:6-23).
+STATUS = {
+    0: "ok", 1: "fileNotReadable", 2: "invalidGGUF", 3: "unsupportedTensorType", 4: "unsupportedArchitecture",
+    5: "missingTensor", 6: "missingMetadata", 7: "tensorShapeMismatch", 8: "noDevice", 9: "invalidOptions",
+    10: "gpuFailure", 11: "outOfMemory", 12: "timeout", 13: "cancelled",
+}
+LOAD_NO_GRAPHS = 1
+LOAD_Q8_ONLY = 2
+
+
+class GemmaEmbedError(RuntimeError):
+    """A failed call: `.case` names the GemmaEmbedError case, `.code` the ge_status value."""
+
+    def __init__(self, code: int, message: str):
+        self.code = code
+        self.case = STATUS.get(code, "unknown")
+        self.message = message
+        super().__init__(f"{self.case}: {message}")
+
+
+class TaskPrefix:
+    """The instruction prefixes of EmbedOptions.swift:6-31, for callers that tokenise."""
+
+    @staticmethod
+    def document(title: Optional[str] = None) -> str:
+        return f"title: {title or 'none'} | text: "
+
+    @staticmethod
+    def query(task: Optional[str] = None) -> str:
+        return f"task: {task or 'search result'} | query: "
+
+    clustering = "task: clustering | query: "
+    classification = "task: classification | query: "
+    similarity = "task: sentence similarity | query: "
+    none = ""
+
+
+@dataclass
+class EmbedOptions:
+    """EmbedOptions (EmbedOptions.swift:34-56) without the task prefix, which tokenisation applies."""
+    max_tokens: int = 2048
+    dimensions: int = 768
+    normalise: bool = True
+    batch_size: Optional[int] = None
+
+
+@dataclass
+class LoadOptions:
+    """LoadOptions (EmbedOptions.swift:171-203): the fields a text forward uses, plus devices."""
+    batch_token_budget: int = 8192
+    devices: Sequence[int] = (0,)
+    use_graphs: bool = True
+    q8_only: bool = False
+
+
+@dataclass
+class Embedding:
+    vector: np.ndarray
+    token_count: int
+    truncated: bool
+
+
+@dataclass
+class EmbeddingProgress:
+    completed_texts: int
+    total_texts: int
+    completed_tokens: int
+
+
+@dataclass
+class ModelInfo:
+    architecture: str
+    name: str
+    layer_count: int
+    hidden_size: int
+    output_dimensions: int
+    feed_forward_size: int
+    per_layer_input_size: int
+    head_count: int
+    vocabulary_size: int
+    sliding_window: int
+    max_tokens: int
+    norm_epsilon: float
+    quantization: str
+    file_size: int
+    device_count: int
+    device_name: str
+    eos_id: int
+    bos_id: int
+
+
+def _check(rc: int, handle=None):
+    if rc != 0:
+        msg = _lib.lib().ge_last_error(handle)
+        raise GemmaEmbedError(rc, msg.decode() if msg else "")
+
+
+def _i32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
+
+
+def _ptr(a: np.ndarray, t):
+    return a.ctypes.data_as(ctypes.POINTER(t))
+
+
+def pack(sequences) -> tuple:
+    """PackedBatch.append over `sequences` (MetalForward.swift:17-21): ids, positions, ranges."""
+    seqs = [_i32(s) for s in sequences]
+    lens = [len(s) for s in seqs]
+    tokens = np.concatenate(seqs) if seqs else np.zeros(0, np.int32)
+    positions = np.concatenate([np.arange(n, dtype=np.int32) for n in lens]) if seqs else np.zeros(0, np.int32)
+    starts = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64) if seqs else np.zeros(0, np.int64)
+    return tokens, positions, [(int(s), int(n)) for s, n in zip(starts, lens)]
+
+
+class EmbeddingModel:
+    """EmbeddingModel (EmbeddingModel.swift:24-290) on one or more B200 GPUs."""
+
+    def __init__(self, handle, options: LoadOptions):
+        self._h = handle
+        self.options = options
+        info = _lib.GeInfo()
+        _check(_lib.lib().ge_info_get(handle, ctypes.byref(info)), handle)
+        self.info = ModelInfo(
+            architecture=info.architecture.decode(), name=info.name.decode(), layer_count=info.layer_count,
+            hidden_size=info.hidden_size, output_dimensions=info.output_dimensions,
+            feed_forward_size=info.feed_forward_size, per_layer_input_size=info.per_layer_input_size,
+            head_count=info.head_count, vocabulary_size=info.vocabulary_size, sliding_window=info.sliding_window,
+            max_tokens=info.max_tokens, norm_epsilon=info.norm_epsilon, quantization=info.quantization.decode(),
+            file_size=info.file_size, device_count=info.device_count, device_name=info.device_name.decode(),
+            eos_id=info.eos_id, bos_id=info.bos_id)
+
+    @classmethod
+    def load(cls, path: str, options: Optional[LoadOptions] = None) -> "EmbeddingModel":
+        """EmbeddingModel.load(from:options:) (EmbeddingModel.swift:40-122)."""
+        options = options or LoadOptions()
+        L = _lib.lib()
+        o = _lib.GeLoadOpts()
+        L.ge_load_opts_default(ctypes.byref(o))
+        mask = 0
+        for d in options.devices:
+            mask |= 1 << int(d)
+        o.device_mask = mask
+        o.batch_token_budget = int(options.batch_token_budget)
+        o.flags = (0 if options.use_graphs else LOAD_NO_GRAPHS) | (LOAD_Q8_ONLY if options.q8_only else 0)
+        h = ctypes.c_void_p()
+        _check(L.ge_load(str(path).encode(), ctypes.byref(o), ctypes.byref(h)), None)
+        return cls(h, options)
+
+    def close(self):
+        if self._h:
+            _lib.lib().ge_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # -------------------------------------------------------------- forward entry points
+    def forward_packed(self, tokens, positions, seqs) -> np.ndarray:
+        """MetalForward.run over one PackedBatch: pooled, unnormalised [nseq][output_dimensions]."""
+        tokens = _i32(tokens)
+        pos = None if positions is None else _i32(positions)
+        arr = (_lib.GeSeq * max(len(seqs), 1))(*[_lib.GeSeq(int(s), int(n)) for s, n in seqs])
+        out = np.zeros((len(seqs), self.info.output_dimensions), dtype=np.float32)
+        _check(_lib.lib().ge_forward_packed(self._h, _ptr(tokens, ctypes.c_int32),
+                                           None if pos is None else _ptr(pos, ctypes.c_int32), len(tokens), arr,
+                                           len(seqs), _ptr(out, ctypes.c_float)), self._h)
+        return out
+
+    def embed_tokens(self, sequences) -> np.ndarray:
+        """embedTokens (EmbeddingModel.swift:285-289): pooled, unnormalised vectors."""
+        tokens, positions, seqs = pack(sequences)
+        return self.forward_packed(tokens, positions, seqs)
+
+    def forward_device(self, d_tokens, seqs, d_out, stream=None, device: int = 0) -> None:
+        """The forward over device-resident ids: torch int32 / float32 CUDA tensors or raw pointers."""
+        tp = d_tokens.data_ptr() if hasattr(d_tokens, "data_ptr") else int(d_tokens)
+        op = d_out.data_ptr() if hasattr(d_out, "data_ptr") else int(d_out)
+        ntok = int(sum(n for _, n in seqs))
+        sp = stream.cuda_stream if hasattr(stream, "cuda_stream") else (stream or 0)
+        arr = (_lib.GeSeq * max(len(seqs), 1))(*[_lib.GeSeq(int(s), int(n)) for s, n in seqs])
+        _check(_lib.lib().ge_forward_device(self._h, device, ctypes.c_void_p(tp), ntok, arr, len(seqs),
+                                           ctypes.c_void_p(op), ctypes.c_void_p(sp)), self._h)
+
+    def trace(self, tokens, layer: int) -> np.ndarray:
+        """The residual stream after `layer` ("l_out-<layer>"), or result_norm for layer -1: [ntok][hidden]."""
+        tokens = _i32(tokens)
+        out = np.zeros((len(tokens), self.info.hidden_size), dtype=np.float32)
+        _check(_lib.lib().ge_forward_trace(self._h, _ptr(tokens, ctypes.c_int32), len(tokens), layer,
+                                          _ptr(out, ctypes.c_float)), self._h)
+        return out
+
+    # -------------------------------------------------------------- EmbeddingModel API
+    def embed(self, texts, options: Optional[EmbedOptions] = None,
+              progress: Optional[Callable[[EmbeddingProgress], Optional[bool]]] = None) -> list:
+        """embed(_ texts:options:progress:) (EmbeddingModel.swift:145-175) over token-id lists.
+
+        A single list of ints embeds one text and returns one Embedding.  `progress` runs after
+        every batch; returning True cancels the call between batches (GemmaEmbedError
+        'cancelled')."""
+        options = options or EmbedOptions()
+        single = len(texts) > 0 and np.isscalar(texts[0])
+        seqs = [_i32(texts)] if single else [_i32(t) for t in texts]
+        n = len(seqs)
+        if n == 0:
+            o = _lib.GeEmbedOpts(options.max_tokens, options.dimensions, int(options.normalise),
+                                 options.batch_size or 0)
+            _check(_lib.lib().ge_embed_tokens(self._h, None, None, 0, ctypes.byref(o), None, None, None,
+                                             _lib.PROGRESS_FN(0), None), self._h)
+            return []
+        ptrs = (_lib.i32p * n)(*[_ptr(s, ctypes.c_int32) for s in seqs])
+        lens = np.array([len(s) for s in seqs], dtype=np.int32)
+        dims = options.dimensions
+        out = np.zeros((n, dims if dims > 0 else 1), dtype=np.float32)
+        counts = np.zeros(n, dtype=np.int32)
+        trunc = np.zeros(n, dtype=np.int32)
+        if options.batch_size is not None and options.batch_size < 1:
+            raise GemmaEmbedError(9, "invalid options: batchSize must be at least 1")
+        o = _lib.GeEmbedOpts(options.max_tokens, dims, int(options.normalise), options.batch_size or 0)
+        cb = _lib.PROGRESS_FN(0)
+        if progress is not None:
+            def _cb(done, total, tokens, user):
+                return 1 if progress(EmbeddingProgress(done, total, tokens)) else 0
+            cb = _lib.PROGRESS_FN(_cb)
+        _check(_lib.lib().ge_embed_tokens(self._h, ptrs, _ptr(lens, ctypes.c_int32), n, ctypes.byref(o),
+                                         _ptr(out, ctypes.c_float), _ptr(counts, ctypes.c_int32),
+                                         _ptr(trunc, ctypes.c_int32), cb, None), self._h)
+        res = [Embedding(out[i].copy(), int(counts[i]), bool(trunc[i])) for i in range(n)]
+        return res[0] if single else res
+
+    @staticmethod
+    def similarity(a: Embedding, b: Embedding) -> float:
+        """Dot product of the common prefix (EmbeddingModel.swift:178-182)."""
+        k = min(len(a.vector), len(b.vector))
+        return float(np.dot(a.vector[:k].astype(np.float32), b.vector[:k].astype(np.float32)))
+
+    @staticmethod
+    def batches(costs, batch_size: Optional[int], budgets) -> list:
+        """EmbeddingModel.batches (EmbeddingModel.swift:200-215) as a list of ranges."""
+        n, k = len(costs), len(budgets)
+        c = np.ascontiguousarray(np.array(costs, dtype=np.int64).reshape(n, k)) if n else np.zeros((0, k), np.int64)
+        b = np.ascontiguousarray(np.array(budgets, dtype=np.int64))
+        out = np.zeros(max(2 * n, 2), dtype=np.int32)
+        cnt = ctypes.c_int32(0)
+        _check(_lib.lib().ge_batches(_ptr(c, ctypes.c_int64), n, k, batch_size or 0, _ptr(b, ctypes.c_int64),
+                                    _ptr(out, ctypes.c_int32), ctypes.byref(cnt)))
+        return [range(int(out[2 * i]), int(out[2 * i + 1])) for i in range(cnt.value)]
+
+    @staticmethod
+    def finish(vector, dimensions: int, normalise: bool) -> np.ndarray:
+        """EmbeddingModel.finish (EmbeddingModel.swift:260-267)."""
+        v = np.ascontiguousarray(np.asarray(vector, dtype=np.float32))
+        out = np.zeros(min(dimensions, len(v)), dtype=np.float32)
+        _check(_lib.lib().ge_finish(_ptr(v, ctypes.c_float), len(v), dimensions, int(normalise),
+                                   _ptr(out, ctypes.c_float)))
+        return out

@@ -1,0 +1,84 @@
+"""ctypes binding of libgemma_embed_cuda.so (the C ABI in include/gemma_embed.h).
+
+The library is required: importing the package without it raises, and there is no
+CPU fallback for any entry point.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libgemma_embed_cuda.so")
+
+P = ctypes.POINTER
+i32p, i64p, f32p, u16p, i8p = P(ctypes.c_int32), P(ctypes.c_int64), P(ctypes.c_float), P(ctypes.c_uint16), P(ctypes.c_int8)
+
+
+class GeSeq(ctypes.Structure):
+    _fields_ = [("start", ctypes.c_uint32), ("length", ctypes.c_uint32)]
+
+
+class GeLoadOpts(ctypes.Structure):
+    _fields_ = [("device_mask", ctypes.c_uint32), ("batch_token_budget", ctypes.c_int32), ("flags", ctypes.c_uint32)]
+
+
+class GeEmbedOpts(ctypes.Structure):
+    _fields_ = [("max_tokens", ctypes.c_int32), ("dimensions", ctypes.c_int32), ("normalise", ctypes.c_int32),
+                ("batch_size", ctypes.c_int32)]
+
+
+class GeInfo(ctypes.Structure):
+    _fields_ = [("architecture", ctypes.c_char * 64), ("name", ctypes.c_char * 128)] + [
+        (n, ctypes.c_int32) for n in ("layer_count", "hidden_size", "output_dimensions", "feed_forward_size",
+                                      "per_layer_input_size", "head_count", "vocabulary_size", "sliding_window",
+                                      "max_tokens")] + [
+        ("norm_epsilon", ctypes.c_float), ("quantization", ctypes.c_char * 16), ("file_size", ctypes.c_int64),
+        ("device_count", ctypes.c_int32), ("eos_id", ctypes.c_int32), ("bos_id", ctypes.c_int32),
+        ("device_name", ctypes.c_char * 128)]
+
+
+PROGRESS_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p)
+
+# Every entry point of include/gemma_embed.h with its argument and result types.
+SIGNATURES = {
+    "ge_load_opts_default": ([P(GeLoadOpts)], None),
+    "ge_embed_opts_default": ([P(GeEmbedOpts)], None),
+    "ge_load": ([ctypes.c_char_p, P(GeLoadOpts), P(ctypes.c_void_p)], ctypes.c_int),
+    "ge_free": ([ctypes.c_void_p], None),
+    "ge_last_error": ([ctypes.c_void_p], ctypes.c_char_p),
+    "ge_info_get": ([ctypes.c_void_p, P(GeInfo)], ctypes.c_int),
+    "ge_forward_packed": ([ctypes.c_void_p, i32p, i32p, ctypes.c_int32, P(GeSeq), ctypes.c_int32, f32p], ctypes.c_int),
+    "ge_forward_device": ([ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int32, P(GeSeq), ctypes.c_int32,
+                           ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "ge_forward_trace": ([ctypes.c_void_p, i32p, ctypes.c_int32, ctypes.c_int32, f32p], ctypes.c_int),
+    "ge_embed_tokens": ([ctypes.c_void_p, P(i32p), i32p, ctypes.c_int32, P(GeEmbedOpts), f32p, i32p, i32p,
+                         PROGRESS_FN, ctypes.c_void_p], ctypes.c_int),
+    "ge_batches": ([i64p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, i64p, i32p, i32p], ctypes.c_int),
+    "ge_finish": ([f32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, f32p], ctypes.c_int),
+}
+
+# Kernel-level entry points of include/gemma_embed_testing.h.
+TEST_SIGNATURES = {
+    "ge_test_gemm": ([u16p, ctypes.c_int32, ctypes.c_int32, P(ctypes.c_uint8), ctypes.c_int32, ctypes.c_int32,
+                      ctypes.c_int32, f32p, f32p], ctypes.c_int),
+    "ge_test_attention": ([u16p, u16p, u16p, ctypes.c_int32, P(GeSeq), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                           ctypes.c_int32, ctypes.c_int32, u16p], ctypes.c_int),
+    "ge_test_last_error": ([], ctypes.c_char_p),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python gemma-embed-swift_b200/build.py`")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (args, res) in {**SIGNATURES, **TEST_SIGNATURES}.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+    return _lib

@@ -1,0 +1,400 @@
+// api.cpp -- the C ABI (include/gemma_embed.h): argument checks, the multi-GPU dispatcher and
+// the host-side pieces of EmbeddingModel (Sources/GemmaEmbed/EmbeddingModel.swift):
+// truncation, batch planning, packing and finish.
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+#include <numeric>
+#include <thread>
+
+#include "gemma_embed.h"
+#include "model.hpp"
+
+namespace ge {
+int load_model(ge_model* m, const char* path, const ge_load_opts* opts);
+void free_model(ge_model* m);
+}  // namespace ge
+
+namespace {
+
+thread_local std::string t_last_error;
+
+// Checks that `seqs` tile [0, ntok) in order with lengths 1..max_tokens, that every id is a
+// token of the vocabulary (negative ids are the reference's vector rows, which only the image
+// and audio towers produce) and that positions index the RoPE table.
+int check_batch(ge_model* m, const int32_t* tokens, const int32_t* positions, int32_t ntok, const ge_seq* seqs,
+                int32_t nseq) {
+    const ge::Config& c = m->cfg;
+    if (ntok < 0 || nseq < 0) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: negative size");
+    if ((ntok > 0 && !tokens) || (nseq > 0 && !seqs))
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: NULL input array");
+    uint64_t next = 0;
+    for (int32_t s = 0; s < nseq; s++) {
+        if (seqs[s].start != next)
+            return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: sequence " + std::to_string(s) +
+                                                                 " does not start where the previous one ends");
+        if (seqs[s].length == 0 || seqs[s].length > uint32_t(c.max_tokens))
+            return ge::set_error(m, GE_ERR_INVALID_OPTIONS,
+                                 "invalid options: sequence " + std::to_string(s) + " has " +
+                                     std::to_string(seqs[s].length) + " tokens; allowed 1.." + std::to_string(c.max_tokens));
+        next += seqs[s].length;
+    }
+    if (next != uint64_t(ntok))
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: sequence lengths sum to " +
+                                                            std::to_string(next) + ", not " + std::to_string(ntok));
+    for (int32_t t = 0; t < ntok; t++) {
+        if (tokens[t] < 0)
+            return ge::set_error(m, GE_ERR_INVALID_OPTIONS,
+                                 "invalid options: vector rows (negative ids) need an image or audio encoder");
+        if (tokens[t] >= c.vocab)
+            return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: token id " + std::to_string(tokens[t]) +
+                                                                " is outside the vocabulary of " + std::to_string(c.vocab));
+        if (positions && (positions[t] < 0 || positions[t] >= c.max_tokens))
+            return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: position " +
+                                                                std::to_string(positions[t]) + " is out of range");
+    }
+    return GE_OK;
+}
+
+// Sequences per device: longest first onto the least-loaded device, with a cost that counts
+// attention's quadratic term, keeping each device's sequences in their original order.
+std::vector<std::vector<int>> shard(const ge_seq* seqs, int nseq, int ndev) {
+    std::vector<int> order(nseq);
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return seqs[a].length > seqs[b].length; });
+    std::vector<double> load(ndev, 0.0);
+    std::vector<std::vector<int>> parts(ndev);
+    for (int i : order) {
+        const int dv = int(std::min_element(load.begin(), load.end()) - load.begin());
+        const double n = seqs[i].length;
+        load[dv] += n + n * n / 2048.0;
+        parts[dv].push_back(i);
+    }
+    for (auto& p : parts) std::sort(p.begin(), p.end());
+    return parts;
+}
+
+int forward_packed_locked(ge_model* m, const int32_t* tokens, const int32_t* positions, int32_t ntok, const ge_seq* seqs,
+                          int32_t nseq, float* out) {
+    const int ndev = int(m->devs.size());
+    const int od = m->cfg.out_dim;
+    if (ndev == 1 || nseq <= 1) {
+        ge::ForwardArgs a;
+        a.tokens = tokens;
+        a.positions = positions;
+        a.ntok = ntok;
+        a.seqs = seqs;
+        a.nseq = nseq;
+        a.out = out;
+        return ge::run_forward(m, m->devs[0], a);
+    }
+    // Multi-GPU: each device packs its own share of the sequences, runs it on its own host
+    // thread and stream, and its pooled rows go back to their original positions.
+    auto parts = shard(seqs, nseq, ndev);
+    std::vector<int> rc(ndev, GE_OK);
+    std::vector<std::string> msgs(ndev);
+    std::vector<std::thread> th;
+    for (int dv = 0; dv < ndev; dv++) {
+        if (parts[dv].empty()) continue;
+        th.emplace_back([&, dv]() {
+            const auto& idx = parts[dv];
+            std::vector<int32_t> tk, ps;
+            std::vector<ge_seq> sq;
+            for (int i : idx) {
+                sq.push_back({uint32_t(tk.size()), seqs[i].length});
+                tk.insert(tk.end(), tokens + seqs[i].start, tokens + seqs[i].start + seqs[i].length);
+                if (positions) ps.insert(ps.end(), positions + seqs[i].start, positions + seqs[i].start + seqs[i].length);
+            }
+            std::vector<float> o(idx.size() * size_t(od));
+            ge::ForwardArgs a;
+            a.tokens = tk.data();
+            a.positions = positions ? ps.data() : nullptr;
+            a.ntok = int(tk.size());
+            a.seqs = sq.data();
+            a.nseq = int(sq.size());
+            a.out = o.data();
+            a.error = &msgs[dv];  // each device thread reports into its own string
+            rc[dv] = ge::run_forward(m, m->devs[dv], a);
+            if (rc[dv] == GE_OK)
+                for (size_t j = 0; j < idx.size(); j++) memcpy(out + size_t(idx[j]) * od, o.data() + j * od, od * 4);
+        });
+    }
+    for (auto& t : th) t.join();
+    for (int dv = 0; dv < ndev; dv++)
+        if (rc[dv] != GE_OK) return ge::set_error(m, rc[dv], msgs[dv]);
+    return GE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+void ge_load_opts_default(ge_load_opts* o) {
+    if (!o) return;
+    o->device_mask = 1;
+    o->batch_token_budget = 8192;
+    o->flags = 0;
+}
+
+void ge_embed_opts_default(ge_embed_opts* o) {
+    if (!o) return;
+    o->max_tokens = 2048;
+    o->dimensions = 768;
+    o->normalise = 1;
+    o->batch_size = 0;
+}
+
+int ge_load(const char* path, const ge_load_opts* opts, ge_model** out) {
+    if (!out) {
+        t_last_error = "invalid options: output handle is NULL";
+        return GE_ERR_INVALID_OPTIONS;
+    }
+    *out = nullptr;
+    ge_model* m = new ge_model();
+    ge_load_opts o;
+    ge_load_opts_default(&o);
+    if (opts) o = *opts;
+    m->budget = std::max(64, o.batch_token_budget);
+    m->flags = o.flags;
+    int rc = ge::load_model(m, path, &o);
+    if (rc == GE_OK) {
+        // One forward over a short sequence initialises every kernel before the first request
+        // (EmbeddingModel.swift:111-114).
+        const int32_t warm[4] = {m->cfg.bos_id, 3, 4, m->cfg.eos_id};
+        bool ids_ok = true;
+        for (int32_t t : warm) ids_ok = ids_ok && t >= 0 && t < m->cfg.vocab;
+        if (ids_ok) {
+            ge_seq s{0, 4};
+            std::vector<float> v(size_t(m->cfg.out_dim));
+            for (auto& d : m->devs) {
+                ge::ForwardArgs a;
+                a.tokens = warm;
+                a.ntok = 4;
+                a.seqs = &s;
+                a.nseq = 1;
+                a.out = v.data();
+                rc = ge::run_forward(m, d, a);
+                if (rc) break;
+            }
+        }
+    }
+    if (rc != GE_OK) {
+        t_last_error = m->last_error;
+        ge::free_model(m);
+        delete m;
+        return rc;
+    }
+    *out = m;
+    return GE_OK;
+}
+
+void ge_free(ge_model* m) {
+    if (!m) return;
+    {
+        std::lock_guard<std::mutex> g(m->mu);
+        ge::free_model(m);
+    }
+    delete m;
+}
+
+const char* ge_last_error(const ge_model* m) { return m ? m->last_error.c_str() : t_last_error.c_str(); }
+
+int ge_info_get(const ge_model* m, ge_info* info) {
+    if (!m || !info) return GE_ERR_INVALID_OPTIONS;
+    const ge::Config& c = m->cfg;
+    memset(info, 0, sizeof *info);
+    snprintf(info->architecture, sizeof info->architecture, "%s", c.arch.c_str());
+    snprintf(info->name, sizeof info->name, "%s", c.name.c_str());
+    info->layer_count = c.layers;
+    info->hidden_size = c.hidden;
+    info->output_dimensions = c.out_dim;
+    info->feed_forward_size = c.ff;
+    info->per_layer_input_size = c.per_layer;
+    info->head_count = c.heads;
+    info->vocabulary_size = c.vocab;
+    info->sliding_window = c.sliding_window;
+    info->max_tokens = c.max_tokens;
+    info->norm_epsilon = c.eps;
+    snprintf(info->quantization, sizeof info->quantization, "%s", c.quant.c_str());
+    info->file_size = m->file_size;
+    info->device_count = int32_t(m->devs.size());
+    info->eos_id = c.eos_id;
+    info->bos_id = c.bos_id;
+    if (!m->devs.empty()) snprintf(info->device_name, sizeof info->device_name, "%s", m->devs[0].name.c_str());
+    return GE_OK;
+}
+
+int ge_forward_packed(ge_model* m, const int32_t* tokens, const int32_t* positions, int32_t ntok, const ge_seq* seqs,
+                      int32_t nseq, float* pooled_out) {
+    if (!m) return GE_ERR_INVALID_OPTIONS;
+    std::lock_guard<std::mutex> g(m->mu);
+    int rc = check_batch(m, tokens, positions, ntok, seqs, nseq);
+    if (rc) return rc;
+    if (nseq == 0) return GE_OK;
+    if (!pooled_out) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: output array is NULL");
+    return forward_packed_locked(m, tokens, positions, ntok, seqs, nseq, pooled_out);
+}
+
+int ge_forward_device(ge_model* m, int32_t device_ordinal, const int32_t* d_tokens, int32_t ntok, const ge_seq* seqs,
+                      int32_t nseq, float* d_pooled, void* stream) {
+    if (!m) return GE_ERR_INVALID_OPTIONS;
+    std::lock_guard<std::mutex> g(m->mu);
+    ge::Device* dev = nullptr;
+    for (auto& d : m->devs)
+        if (d.ordinal == device_ordinal) dev = &d;
+    if (!dev) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: the model is not loaded on that device");
+    if (ntok < 0 || nseq < 0 || (nseq > 0 && (!seqs || !d_tokens || !d_pooled)))
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: bad sizes or NULL arrays");
+    uint64_t next = 0;
+    for (int32_t s = 0; s < nseq; s++) {
+        if (seqs[s].start != next || seqs[s].length == 0 || seqs[s].length > uint32_t(m->cfg.max_tokens))
+            return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: sequences must tile the batch in order");
+        next += seqs[s].length;
+    }
+    if (next != uint64_t(ntok)) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: lengths do not sum to ntok");
+    if (nseq == 0) return GE_OK;
+    ge::ForwardArgs a;
+    a.tokens = d_tokens;
+    a.tokens_on_device = true;
+    a.ntok = ntok;
+    a.seqs = seqs;
+    a.nseq = nseq;
+    a.out = d_pooled;
+    a.out_on_device = true;
+    a.stream = static_cast<cudaStream_t>(stream);
+    return ge::run_forward(m, *dev, a);
+}
+
+int ge_forward_trace(ge_model* m, const int32_t* tokens, int32_t ntok, int32_t layer, float* hidden_out) {
+    if (!m) return GE_ERR_INVALID_OPTIONS;
+    std::lock_guard<std::mutex> g(m->mu);
+    if (layer < -1 || layer >= m->cfg.layers || !hidden_out)
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: layer out of range or NULL output");
+    ge_seq s{0, uint32_t(ntok)};
+    int rc = check_batch(m, tokens, nullptr, ntok, &s, 1);
+    if (rc) return rc;
+    ge::ForwardArgs a;
+    a.tokens = tokens;
+    a.ntok = ntok;
+    a.seqs = &s;
+    a.nseq = 1;
+    a.trace_layer = layer;
+    a.trace_out = hidden_out;
+    return ge::run_forward(m, m->devs[0], a);
+}
+
+int ge_batches(const int64_t* costs, int32_t n, int32_t ncost, int32_t batch_size, const int64_t* budgets,
+               int32_t* ranges_out, int32_t* count_out) {
+    if (n < 0 || ncost < 1 || (n > 0 && (!costs || !ranges_out)) || !budgets || !count_out) return GE_ERR_INVALID_OPTIONS;
+    // EmbeddingModel.batches (EmbeddingModel.swift:200-215).
+    std::vector<int64_t> totals(size_t(ncost), 0);
+    int32_t count = 0, start = 0;
+    for (int32_t i = 0; i < n; i++) {
+        bool full = false;
+        if (batch_size > 0) {
+            full = i - start >= batch_size;
+        } else {
+            for (int32_t c = 0; c < ncost; c++) full = full || totals[c] + costs[int64_t(i) * ncost + c] > budgets[c];
+        }
+        if (i > start && full) {
+            ranges_out[2 * count] = start;
+            ranges_out[2 * count + 1] = i;
+            count++;
+            start = i;
+            std::fill(totals.begin(), totals.end(), 0);
+        }
+        for (int32_t c = 0; c < ncost; c++) totals[c] += costs[int64_t(i) * ncost + c];
+    }
+    if (start < n) {
+        ranges_out[2 * count] = start;
+        ranges_out[2 * count + 1] = n;
+        count++;
+    }
+    *count_out = count;
+    return GE_OK;
+}
+
+int ge_finish(const float* v, int32_t n, int32_t dims, int32_t normalise, float* out) {
+    if (!v || !out || n < 0 || dims < 0) return GE_ERR_INVALID_OPTIONS;
+    // EmbeddingModel.finish (EmbeddingModel.swift:260-267).
+    const int32_t k = std::min(dims, n);
+    for (int32_t i = 0; i < k; i++) out[i] = v[i];
+    if (normalise) {
+        float s = 0.f;
+        for (int32_t i = 0; i < k; i++) s += out[i] * out[i];
+        const float norm = sqrtf(s);
+        if (norm > 0.f)
+            for (int32_t i = 0; i < k; i++) out[i] /= norm;
+    }
+    return GE_OK;
+}
+
+int ge_embed_tokens(ge_model* m, const int32_t* const* texts, const int32_t* lengths, int32_t count,
+                    const ge_embed_opts* opts, float* out, int32_t* token_counts, int32_t* truncated,
+                    ge_progress_fn progress, void* user) {
+    if (!m) return GE_ERR_INVALID_OPTIONS;
+    ge_embed_opts o;
+    ge_embed_opts_default(&o);
+    if (opts) o = *opts;
+    const ge::Config& c = m->cfg;
+    // Option checks of EmbeddingModel.embed (EmbeddingModel.swift:147-153).
+    if (!(o.dimensions == 768 || o.dimensions == 512 || o.dimensions == 256 || o.dimensions == 128) ||
+        o.dimensions > c.out_dim)
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: dimensions must be one of [768, 512, 256, 128]");
+    if (o.max_tokens < 2 || o.max_tokens > c.max_tokens)
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS,
+                             "invalid options: maxTokens must be between 2 and " + std::to_string(c.max_tokens));
+    if (o.batch_size < 0) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: batchSize must be at least 1");
+    if (count < 0) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: negative text count");
+    if (count == 0) return GE_OK;
+    if (!texts || !lengths || !out) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: NULL array");
+    // prepare: truncation keeps EOS (EmbeddingModel.swift:189-196).
+    std::vector<std::vector<int32_t>> prepared(count);
+    for (int32_t i = 0; i < count; i++) {
+        if (lengths[i] <= 0 || !texts[i])
+            return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: text " + std::to_string(i) + " has no tokens");
+        std::vector<int32_t>& ids = prepared[i];
+        if (lengths[i] > o.max_tokens) {
+            ids.assign(texts[i], texts[i] + (o.max_tokens - 1));
+            ids.push_back(c.eos_id);
+        } else {
+            ids.assign(texts[i], texts[i] + lengths[i]);
+        }
+        if (token_counts) token_counts[i] = int32_t(ids.size());
+        if (truncated) truncated[i] = lengths[i] > o.max_tokens ? 1 : 0;
+    }
+    std::vector<int64_t> costs(count);
+    for (int32_t i = 0; i < count; i++) costs[i] = int64_t(prepared[i].size());
+    const int64_t budget = m->budget;
+    std::vector<int32_t> ranges(2 * size_t(count));
+    int32_t nr = 0;
+    ge_batches(costs.data(), count, 1, o.batch_size, &budget, ranges.data(), &nr);
+    int32_t done_texts = 0;
+    int64_t done_tokens = 0;
+    std::vector<float> pooled;
+    for (int32_t r = 0; r < nr; r++) {
+        const int32_t b = ranges[2 * r], e = ranges[2 * r + 1];
+        std::vector<int32_t> toks;
+        std::vector<ge_seq> seqs;
+        for (int32_t i = b; i < e; i++) {
+            seqs.push_back({uint32_t(toks.size()), uint32_t(prepared[i].size())});
+            toks.insert(toks.end(), prepared[i].begin(), prepared[i].end());
+        }
+        pooled.resize(size_t(e - b) * c.out_dim);
+        int rc = ge_forward_packed(m, toks.data(), nullptr, int32_t(toks.size()), seqs.data(), int32_t(seqs.size()),
+                                   pooled.data());
+        if (rc) return rc;
+        for (int32_t i = b; i < e; i++)
+            ge_finish(pooled.data() + size_t(i - b) * c.out_dim, c.out_dim, o.dimensions, o.normalise,
+                      out + size_t(i) * o.dimensions);
+        done_texts += e - b;
+        done_tokens += int64_t(toks.size());
+        if (progress && progress(done_texts, count, done_tokens, user) != 0 && r + 1 < nr)
+            return ge::set_error(m, GE_ERR_CANCELLED, "embedding was cancelled");
+    }
+    return GE_OK;
+}
+
+}  // extern "C"

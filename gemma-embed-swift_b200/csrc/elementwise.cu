@@ -1,0 +1,282 @@
+// elementwise.cu -- row kernels of the forward pass: one warp per row, fp32 arithmetic in
+// the reference's operation order, fp16 stores for every value that feeds a GEMM.
+//
+// Reference kernels replaced (Sources/GemmaEmbed/Shaders/Elementwise.metal):
+//   embed_q8 (8-35) + rmsnorm_rows (38-75)          -> k_embed
+//   rmsnorm_rope_{256,512} (97-136) + v norm        -> k_qkv_norm_rope
+//   rmsnorm_residual(_norm) (260-354)               -> k_residual_norm
+//   rmsnorm_rows with preScale (per-layer inputs)   -> k_rmsnorm_rows
+//   mean_pool (243-256)                             -> k_mean_pool
+// and the pooled dense head / output projection, which have no Metal kernel (the
+// reference projects per token with its GEMM, MetalForward.swift:421).
+#include "kernels.hpp"
+#include "ptx.cuh"
+
+namespace ge {
+
+constexpr int kRowsPerBlock = 8;  // warps per 256-thread block
+
+// x = dequant(table row) * scale, h = rmsnorm(x) * w.  Embedding.swift semantics:
+// CPUReference.swift:190-203 (token rows) and Elementwise.metal:8-35 (padding rows zeroed).
+__global__ void k_embed(const int32_t* __restrict__ tokens, int ntok, int rows, const int8_t* __restrict__ tq,
+                        const __half* __restrict__ ts, int width, float scale, float* __restrict__ x,
+                        __half* __restrict__ x16, const float* __restrict__ w, float eps, __half* __restrict__ h) {
+    const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    float* xr = x + long(row) * width;
+    __half* hr = h + long(row) * width;
+    if (row >= ntok) {
+        for (int i = lane; i < width; i += 32) {
+            xr[i] = 0.f;
+            hr[i] = __float2half_rn(0.f);
+            if (x16) x16[long(row) * width + i] = __float2half_rn(0.f);
+        }
+        return;
+    }
+    const long id = tokens[row];
+    const int8_t* q = tq + id * width;
+    const __half* s = ts + id * (width / 32);
+    float ss = 0.f;
+    for (int i = lane; i < width; i += 32) {
+        const float v = (__half2float(s[i >> 5]) * float(q[i])) * scale;
+        xr[i] = v;
+        ss += v * v;
+        if (x16) x16[long(row) * width + i] = __float2half_rn(v);
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / float(width) + eps);
+    for (int i = lane; i < width; i += 32) hr[i] = __float2half_rn(xr[i] * inv * w[i]);
+}
+
+cudaError_t launch_embed(const int32_t* tokens, int ntok, int rows, const int8_t* table_q, const __half* table_s,
+                         int width, float scale, float* x, __half* x16, const float* norm_w, float eps, __half* h,
+                         cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    k_embed<<<(rows + kRowsPerBlock - 1) / kRowsPerBlock, 256, 0, stream>>>(tokens, ntok, rows, table_q, table_s, width,
+                                                                             scale, x, x16, norm_w, eps, h);
+    return cudaGetLastError();
+}
+
+// One warp per (token, head slot): slots [0, H) are query heads, [H, H+KV) key heads,
+// [H+KV, H+2KV) value heads of the fused projection row.  CPUReference.swift:225-235.
+template <int HD>
+__global__ void k_qkv_norm_rope(const float* __restrict__ qkv, int ntok, int rows, int heads, int kvh,
+                                const float* __restrict__ qw, const float* __restrict__ kw,
+                                const int32_t* __restrict__ pos, const float* __restrict__ rope, float eps,
+                                __half* __restrict__ q, __half* __restrict__ k, __half* __restrict__ v) {
+    constexpr int PER = HD / 32;
+    const int slots = heads + 2 * kvh;
+    const long gw = long(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (gw >= long(rows) * slots) return;
+    const int row = int(gw / slots), slot = int(gw % slots);
+    __half* dst;
+    const float* w = nullptr;
+    if (slot < heads) {
+        dst = q + long(row) * heads * HD + slot * HD;
+        w = qw;
+    } else if (slot < heads + kvh) {
+        dst = k + long(row) * kvh * HD + (slot - heads) * HD;
+        w = kw;
+    } else {
+        dst = v + long(row) * kvh * HD + (slot - heads - kvh) * HD;
+    }
+    if (row >= ntok) {
+#pragma unroll
+        for (int j = 0; j < PER; j++) dst[lane + 32 * j] = __float2half_rn(0.f);
+        return;
+    }
+    const float* src = qkv + long(row) * slots * HD + slot * HD;
+    float e[PER];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        e[j] = src[lane + 32 * j];
+        ss += e[j] * e[j];
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / float(HD) + eps);
+#pragma unroll
+    for (int j = 0; j < PER; j++) e[j] = e[j] * inv * (w ? w[lane + 32 * j] : 1.0f);
+    if (w) {
+        // NeoX rotation of pairs (i, i + HD/2): element lane + 32j pairs with lane + 32(j + PER/2).
+        const float* cs = rope + long(pos[row]) * HD;  // [pairs][2] per position
+#pragma unroll
+        for (int j = 0; j < PER / 2; j++) {
+            const int i = lane + 32 * j;
+            const float c = cs[2 * i], s = cs[2 * i + 1];
+            const float a = e[j], b = e[j + PER / 2];
+            e[j] = a * c - b * s;
+            e[j + PER / 2] = a * s + b * c;
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < PER; j++) dst[lane + 32 * j] = __float2half_rn(e[j]);
+}
+
+cudaError_t launch_qkv_norm_rope(const float* qkv, int ntok, int rows, int heads, int kv_heads, int hd,
+                                      const float* q_w, const float* k_w, const int32_t* positions, const float* rope,
+                                      float eps, __half* q, __half* k, __half* v, cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    const long warps = long(rows) * (heads + 2 * kv_heads);
+    const int blocks = int((warps + kRowsPerBlock - 1) / kRowsPerBlock);
+    if (hd == 256)
+        k_qkv_norm_rope<256><<<blocks, 256, 0, stream>>>(qkv, ntok, rows, heads, kv_heads, q_w, k_w, positions, rope,
+                                                         eps, q, k, v);
+    else if (hd == 512)
+        k_qkv_norm_rope<512><<<blocks, 256, 0, stream>>>(qkv, ntok, rows, heads, kv_heads, q_w, k_w, positions, rope,
+                                                         eps, q, k, v);
+    else
+        return cudaErrorInvalidValue;
+    return cudaGetLastError();
+}
+
+// x = (x + rmsnorm(t) * w_post) * scale, then optionally the next norm of x.
+// CPUReference.swift:239-243, 252-256, 266-269 and Elementwise.metal:260-354.
+__global__ void k_residual_norm(float* __restrict__ x, const float* __restrict__ t, int rows, int width,
+                                const float* __restrict__ wp, float scale, const float* __restrict__ wn, float eps,
+                                __half* __restrict__ h16, float* __restrict__ y32, __half* __restrict__ x16) {
+    const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    float* xr = x + long(row) * width;
+    const float* tr = t + long(row) * width;
+    float ss = 0.f;
+    for (int i = lane; i < width; i += 32) ss += tr[i] * tr[i];
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / float(width) + eps);
+    float ss2 = 0.f;
+    for (int i = lane; i < width; i += 32) {
+        float v = xr[i] + tr[i] * inv * wp[i];
+        if (scale != 1.0f) v *= scale;
+        xr[i] = v;
+        ss2 += v * v;
+        if (x16) x16[long(row) * width + i] = __float2half_rn(v);
+    }
+    if (!wn) return;
+    ss2 = warp_sum(ss2);
+    const float inv2 = 1.0f / sqrtf(ss2 / float(width) + eps);
+    for (int i = lane; i < width; i += 32) {
+        const float y = xr[i] * inv2 * wn[i];
+        if (h16) h16[long(row) * width + i] = __float2half_rn(y);
+        if (y32) y32[long(row) * width + i] = y;
+    }
+}
+
+cudaError_t launch_residual_norm(float* x, const float* t, int rows, int width, const float* w_post, float scale,
+                                 const float* w_next, float eps, __half* h16, float* y32, __half* x16,
+                                 cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    k_residual_norm<<<(rows + kRowsPerBlock - 1) / kRowsPerBlock, 256, 0, stream>>>(x, t, rows, width, w_post, scale,
+                                                                                     w_next, eps, h16, y32, x16);
+    return cudaGetLastError();
+}
+
+// out = rmsnorm(x * pre) * w over `width`-wide rows (the per-layer-input norm,
+// CPUReference.swift:206-209 and Elementwise.metal:38-75 with preScale).
+__global__ void k_rmsnorm_rows(const float* __restrict__ x, long rows, int width, float pre,
+                               const float* __restrict__ w, float eps, float* __restrict__ out) {
+    const long row = long(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* xr = x + row * width;
+    float* o = out + row * width;
+    float ss = 0.f;
+    for (int i = lane; i < width; i += 32) {
+        const float v = xr[i] * pre;
+        ss += v * v;
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / float(width) + eps);
+    for (int i = lane; i < width; i += 32) o[i] = (xr[i] * pre) * inv * w[i];
+}
+
+cudaError_t launch_rmsnorm_rows(const float* x, int rows, int width, float pre, const float* w, float eps, float* out,
+                                cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    k_rmsnorm_rows<<<(rows + kRowsPerBlock - 1) / kRowsPerBlock, 256, 0, stream>>>(x, rows, width, pre, w, eps, out);
+    return cudaGetLastError();
+}
+
+// pooled[s][c] = sum over the sequence's rows / length (Elementwise.metal:243-256).
+__global__ void k_mean_pool(const float* __restrict__ y, int width, const uint32_t* __restrict__ seqs,
+                            float* __restrict__ pooled) {
+    const uint32_t start = seqs[2 * blockIdx.x], len = seqs[2 * blockIdx.x + 1];
+    for (int c = threadIdx.x; c < width; c += blockDim.x) {
+        float acc = 0.f;
+        for (uint32_t r = 0; r < len; r++) acc += y[long(start + r) * width + c];
+        pooled[long(blockIdx.x) * width + c] = acc / float(len);
+    }
+}
+
+cudaError_t launch_mean_pool(const float* y, int width, const uint32_t* seqs, int nseq, float* pooled,
+                             cudaStream_t stream) {
+    if (nseq <= 0) return cudaSuccess;
+    k_mean_pool<<<nseq, 256, 0, stream>>>(y, width, seqs, pooled);
+    return cudaGetLastError();
+}
+
+// out[s][n] = sum_k in[s][k] * (scale * q)[n][k], fp32: one warp per output column n.
+__global__ void k_dense_rows(const float* __restrict__ in, int nrows, const int8_t* __restrict__ q,
+                             const __half* __restrict__ st, int N, int K, float* __restrict__ out) {
+    const int n = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (n >= N) return;
+    const int8_t* qr = q + long(n) * K;
+    for (int s = 0; s < nrows; s++) {
+        const float* xr = in + long(s) * K;
+        float acc = 0.f;
+        for (int k = lane; k < K; k += 32) acc += xr[k] * (__half2float(st[long(k >> 5) * N + n]) * float(qr[k]));
+        acc = warp_sum(acc);
+        if (lane == 0) out[long(s) * N + n] = acc;
+    }
+}
+
+cudaError_t launch_dense_rows(const float* in, int nrows, const DevWeight& w, float* out, cudaStream_t stream) {
+    if (nrows <= 0) return cudaSuccess;
+    k_dense_rows<<<(w.N + kRowsPerBlock - 1) / kRowsPerBlock, 256, 0, stream>>>(in, nrows, w.q8, w.scales_t, w.N, w.K,
+                                                                                 out);
+    return cudaGetLastError();
+}
+
+}  // namespace ge
+
+namespace ge {
+
+// positions[start + i] = i for every sequence (PackedBatch.append, MetalForward.swift:17-21).
+__global__ void k_positions(const uint32_t* __restrict__ seqs, int32_t* __restrict__ positions) {
+    const uint32_t start = seqs[2 * blockIdx.x], len = seqs[2 * blockIdx.x + 1];
+    for (uint32_t i = threadIdx.x; i < len; i += blockDim.x) positions[start + i] = int32_t(i);
+}
+
+cudaError_t launch_positions(const uint32_t* seqs, int nseq, int32_t* positions, cudaStream_t stream) {
+    if (nseq <= 0) return cudaSuccess;
+    k_positions<<<nseq, 256, 0, stream>>>(seqs, positions);
+    return cudaGetLastError();
+}
+
+// out[s][n] = sum_k in[s][k] * w[n][k] in fp32 with an fp32 weight matrix: one warp per n.
+__global__ void k_dense_f32(const float* __restrict__ in, int nrows, const float* __restrict__ w, int N, int K,
+                            float* __restrict__ out) {
+    const int n = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (n >= N) return;
+    const float* wr = w + long(n) * K;
+    for (int s = 0; s < nrows; s++) {
+        const float* xr = in + long(s) * K;
+        float acc = 0.f;
+        for (int k = lane; k < K; k += 32) acc += xr[k] * wr[k];
+        acc = warp_sum(acc);
+        if (lane == 0) out[long(s) * N + n] = acc;
+    }
+}
+
+cudaError_t launch_dense_f32(const float* in, int nrows, const float* w, int N, int K, float* out,
+                             cudaStream_t stream) {
+    if (nrows <= 0) return cudaSuccess;
+    k_dense_f32<<<(N + kRowsPerBlock - 1) / kRowsPerBlock, 256, 0, stream>>>(in, nrows, w, N, K, out);
+    return cudaGetLastError();
+}
+
+}  // namespace ge

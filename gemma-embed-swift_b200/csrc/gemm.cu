@@ -1,0 +1,389 @@
+// gemm.cu -- Y[M,N] = X[M,K] * W[N,K]^T on the sm_100a tensor cores (tcgen05, kind::f16).
+//
+// Replaces the reference's Q8_0 GEMM family (Sources/GemmaEmbed/Shaders/GEMM.metal:72-165,
+// 219-412; dispatch in Metal/MetalForward.swift:513-612).  X is an fp16 activation, W a
+// Q8_0 weight; both multiply as fp16 and accumulate in fp32 in tensor memory.
+//
+// Persistent, warp-specialised kernel, one CTA per SM, tiles of 128 x BN, K steps of 64:
+//   warp 4      TMA producer (one elected thread): X tile, and either the fp16 W tile or
+//               the Q8 W tile (int8 values + fp16 block scales)
+//   warps 6-9   (Q8 only) dequantise the int8 tile into the 128-byte-swizzled fp16 operand:
+//               q * scale rounded once to fp16, the same value the fp16-resident weights hold
+//   warp 5      tcgen05.mma issuer (one elected thread) and tensor-memory owner
+//   warps 0-3   epilogue: tensor memory -> registers -> global, with fused activations
+// Two accumulators of BN columns let the epilogue of one tile overlap the next tile's MMAs.
+// Every wait is bounded: on timeout the kernel records GE_ERR_TIMEOUT and returns.
+#include <cudaTypedefs.h>
+
+#include "kernels.hpp"
+#include "ptx.cuh"
+
+namespace ge {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kBN = 256;
+
+template <int BN, bool Q8>
+struct GemmLayout {
+    static constexpr int kStages = Q8 ? 3 : 4;
+    static constexpr int kA = BM * BK * 2;
+    static constexpr int kB = BN * BK * 2;
+    static constexpr int kB8 = Q8 ? BN * BK : 0;
+    static constexpr int kSc = Q8 ? 2 * BN * 2 : 0;
+    static constexpr int kStage = (kA + kB + kB8 + kSc + 1023) / 1024 * 1024;
+    static constexpr int kBarOff = kStages * kStage;
+    static constexpr int kBytes = kBarOff + 256 + 1024;  // barriers, TMEM slot, alignment slack
+    static constexpr int kThreads = Q8 ? 320 : 192;
+};
+
+struct GemmParams {
+    int M, N, K;
+    void* out;
+    int ldo;
+    const float* aux;
+    int ldaux;
+    int* err;
+};
+
+// Waits without giving up on another role's error (used to drain in-flight TMA loads).
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer();
+    while (!mbar_test(bar, parity) && globaltimer() - t0 < kWaitLimitNs) {
+    }
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Dequantises 16 int8 values with one fp16 scale into 8 half2 words (exact q, one rounding).
+__device__ __forceinline__ void dequant16(uint4 raw, __half2 s2, uint32_t (&o)[8]) {
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+    const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152 = 1024 + 128
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const uint32_t u = w[i] ^ 0x80808080u;  // int8 -> uint8 biased by 128
+        uint32_t lo = __byte_perm(u, 0x64646464u, 0x4140);  // halves 1024 + b0, 1024 + b1
+        uint32_t hi = __byte_perm(u, 0x64646464u, 0x4342);  // halves 1024 + b2, 1024 + b3
+        __half2 hl = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&lo), bias), s2);
+        __half2 hh = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&hi), bias), s2);
+        o[2 * i] = *reinterpret_cast<uint32_t*>(&hl);
+        o[2 * i + 1] = *reinterpret_cast<uint32_t*>(&hh);
+    }
+}
+
+template <int BN, int EPI, bool Q8>
+__global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
+    k_gemm(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+           const __grid_constant__ CUtensorMap mapS, GemmParams p) {
+    using L = GemmLayout<BN, Q8>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full_tma = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+    uint64_t* full_b = full_tma + L::kStages;
+    uint64_t* empty = full_b + L::kStages;
+    uint64_t* tfull = empty + L::kStages;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_tiles = p.N / BN;
+    const int tiles = n_tiles * (p.M / BM);
+    const int kb_count = p.K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < L::kStages; s++) {
+            mbar_init(&full_tma[s], 1);
+            mbar_init(&full_b[s], 128);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 128);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 4 && lane == 0) {
+        tma_prefetch(&mapA);
+        tma_prefetch(&mapB);
+        if (Q8) tma_prefetch(&mapS);
+    }
+    if (warp == 5) {
+        tmem_alloc(tmem_slot, 2 * BN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        // ---------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            long issued = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                const int m0 = (t / n_tiles) * BM, n0 = (t % n_tiles) * BN;
+                for (int kb = 0; kb < kb_count; kb++) {
+                    if (!mbar_wait(&empty[s], ph ^ 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = smem + s * L::kStage;
+                    mbar_expect_tx(&full_tma[s], L::kA + (Q8 ? L::kB8 + L::kSc : L::kB));
+                    tma_load_2d(st, &mapA, &full_tma[s], kb * BK, m0);
+                    if (Q8) {
+                        tma_load_2d(st + L::kA + L::kB, &mapB, &full_tma[s], kb * BK, n0);
+                        tma_load_2d(st + L::kA + L::kB + L::kB8, &mapS, &full_tma[s], n0, kb * 2);
+                    } else {
+                        tma_load_2d(st + L::kA, &mapB, &full_tma[s], kb * BK, n0);
+                    }
+                    issued++;
+                    if (++s == L::kStages) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+            // Every issued load must land before the CTA exits, also after an error.
+            for (int j = 0; j < L::kStages; j++) {
+                const long c = issued / L::kStages + (j < issued % L::kStages ? 1 : 0);
+                if (c > 0) drain_wait(&full_tma[j], uint32_t((c - 1) & 1));
+            }
+        }
+    } else if (warp == 5) {
+        // ---------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = idesc_f16(BM, BN);
+            int s = 0, acc = 0;
+            uint32_t ph = 0, acc_ph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+                if (!mbar_wait(&tempty[acc], acc_ph ^ 1, p.err)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + uint32_t(acc * BN);
+                for (int kb = 0; kb < kb_count; kb++) {
+                    if (!mbar_wait(&full_tma[s], ph, p.err) || (Q8 && !mbar_wait(&full_b[s], ph, p.err))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    uint8_t* st = smem + s * L::kStage;
+                    const uint64_t ad = sw128_desc(smem_u32(st), 16, 1024);
+                    const uint64_t bd = sw128_desc(smem_u32(st + L::kA), 16, 1024);
+#pragma unroll
+                    for (int kk = 0; kk < BK / 16; kk++)
+                        umma_f16(d, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), idesc, (kb | kk) != 0);
+                    umma_commit(&empty[s]);
+                    if (++s == L::kStages) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(&tfull[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_ph ^= 1;
+                }
+            }
+        }
+    } else if (warp < 4) {
+        // ---------------------------------------------------------- epilogue
+        int acc = 0;
+        uint32_t acc_ph = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+            if (!mbar_wait(&tfull[acc], acc_ph, p.err)) break;
+            tc_fence_after();
+            const int m0 = (t / n_tiles) * BM, n0 = (t % n_tiles) * BN;
+            const long row = m0 + warp * 32 + lane;
+            const uint32_t taddr = tmem + (uint32_t(warp * 32) << 16) + uint32_t(acc * BN);
+            uint32_t r[32];
+            if (EPI == EPI_GEGLU) {
+                uint32_t u[32];
+                __half* out = reinterpret_cast<__half*>(p.out) + row * p.ldo + n0 / 2;
+#pragma unroll 1
+                for (int c = 0; c < BN / 64; c++) {
+                    tmem_ld32(taddr + uint32_t(c * 32), r);
+                    tmem_ld32(taddr + uint32_t(BN / 2 + c * 32), u);
+                    tmem_wait_ld();
+                    uint32_t packed[16];
+#pragma unroll
+                    for (int i = 0; i < 16; i++)
+                        packed[i] = pack_half2(gelu_tanh(__uint_as_float(r[2 * i])) * __uint_as_float(u[2 * i]),
+                                               gelu_tanh(__uint_as_float(r[2 * i + 1])) * __uint_as_float(u[2 * i + 1]));
+                    uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 4; i++)
+                        dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; c++) {
+                    tmem_ld32(taddr + uint32_t(c * 32), r);
+                    tmem_wait_ld();
+                    const int col = n0 + c * 32;
+                    if (EPI == EPI_F32) {
+                        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + row * p.ldo + col);
+#pragma unroll
+                        for (int i = 0; i < 8; i++)
+                            dst[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                                 __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+                    } else {
+                        uint32_t packed[16];
+                        if (EPI == EPI_GELU_MUL) {
+                            const float4* ax = reinterpret_cast<const float4*>(p.aux + row * p.ldaux + col);
+#pragma unroll
+                            for (int i = 0; i < 8; i++) {
+                                const float4 a = ax[i];
+                                packed[2 * i] = pack_half2(gelu_tanh(__uint_as_float(r[4 * i])) * a.x,
+                                                           gelu_tanh(__uint_as_float(r[4 * i + 1])) * a.y);
+                                packed[2 * i + 1] = pack_half2(gelu_tanh(__uint_as_float(r[4 * i + 2])) * a.z,
+                                                               gelu_tanh(__uint_as_float(r[4 * i + 3])) * a.w);
+                            }
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 16; i++)
+                                packed[i] = pack_half2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+                        }
+                        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.out) + row * p.ldo + col);
+#pragma unroll
+                        for (int i = 0; i < 4; i++)
+                            dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+            if (++acc == 2) {
+                acc = 0;
+                acc_ph ^= 1;
+            }
+        }
+    } else if (Q8) {
+        // ---------------------------------------------------------- Q8 -> fp16 converters
+        const int tid = threadIdx.x - 192;
+        int s = 0;
+        uint32_t ph = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            for (int kb = 0; kb < kb_count; kb++) {
+                if (!mbar_wait(&full_tma[s], ph, p.err)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* st = smem + s * L::kStage;
+                uint8_t* b16 = st + L::kA;
+                const uint8_t* b8 = b16 + L::kB;
+                const __half* sc = reinterpret_cast<const __half*>(b8 + L::kB8);
+#pragma unroll 2
+                for (int i = 0; i < BN * 4 / 128; i++) {
+                    const int idx = i * 128 + tid;
+                    const int r = idx >> 2, c = idx & 3;
+                    const uint4 raw = *reinterpret_cast<const uint4*>(b8 + r * BK + c * 16);
+                    const __half2 s2 = __half2half2(sc[(c >> 1) * BN + r]);
+                    uint32_t o[8];
+                    dequant16(raw, s2, o);
+                    uint8_t* rowp = b16 + r * 128;
+                    const int j0 = (2 * c) ^ (r & 7), j1 = (2 * c + 1) ^ (r & 7);
+                    *reinterpret_cast<uint4*>(rowp + j0 * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+                    *reinterpret_cast<uint4*>(rowp + j1 * 16) = make_uint4(o[4], o[5], o[6], o[7]);
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(&full_b[s]);
+                if (++s == L::kStages) {
+                    s = 0;
+                    ph ^= 1;
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2 * BN);
+    }
+}
+
+// ---------------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }
+    return fn;
+}
+
+static bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes, void* ptr, uint64_t inner,
+                      uint64_t outer, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {inner * uint64_t(elem_bytes)};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, type, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool encode_weight_maps(DevWeight& w, int bn) {
+    bool ok = encode_2d(&w.map_q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.q8, w.K, w.N, BK, bn,
+                        CU_TENSOR_MAP_SWIZZLE_NONE) &&
+              encode_2d(&w.map_scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.scales_t, w.N, w.K / 32, bn, 2,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (ok && w.f16)
+        ok = encode_2d(&w.map_f16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.f16, w.K, w.N, BK, bn,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+    return ok;
+}
+
+bool encode_activation_map(DevActivation& a) {
+    return encode_2d(&a.map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.ptr, a.cols, a.rows, BK, BM,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <int EPI, bool Q8>
+static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
+    using L = GemmLayout<kBN, Q8>;
+    auto kern = k_gemm<kBN, EPI, Q8>;
+    static unsigned configured = 0;  // one bit per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(configured & (1u << dev))) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+        if (e != cudaSuccess) return e;
+        configured |= 1u << dev;
+    }
+    GemmParams p{g.m_rows, g.w->N, g.w->K, g.out, g.ldo, g.aux, g.ldaux, g.err};
+    const int tiles = (g.m_rows / BM) * (g.w->N / kBN);
+    const int grid = tiles < g.num_sms ? tiles : g.num_sms;
+    const CUtensorMap& mb = Q8 ? g.w->map_q8 : g.w->map_f16;
+    kern<<<grid, L::kThreads, L::kBytes, stream>>>(g.a->map, mb, g.w->map_scales, p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream) {
+    if (g.m_rows <= 0) return cudaSuccess;
+    if (g.m_rows % BM || g.w->N % kBN || g.w->K % BK || g.a->cols != g.w->K || g.a->rows < g.m_rows)
+        return cudaErrorInvalidValue;
+    const bool q8 = g.use_q8 || !g.w->f16;
+    switch (g.epilogue) {
+    case EPI_F32: return q8 ? launch_t<EPI_F32, true>(g, stream) : launch_t<EPI_F32, false>(g, stream);
+    case EPI_F16: return q8 ? launch_t<EPI_F16, true>(g, stream) : launch_t<EPI_F16, false>(g, stream);
+    case EPI_GEGLU: return q8 ? launch_t<EPI_GEGLU, true>(g, stream) : launch_t<EPI_GEGLU, false>(g, stream);
+    case EPI_GELU_MUL: return q8 ? launch_t<EPI_GELU_MUL, true>(g, stream) : launch_t<EPI_GELU_MUL, false>(g, stream);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace ge

@@ -1,0 +1,113 @@
+// kernels.hpp -- host-side launchers of the sm_100a kernels used by the forward pass.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ge {
+
+// Rows of every activation buffer are padded to this multiple: one tcgen05 M tile.
+constexpr int kRowTile = 128;
+
+// ------------------------------------------------------------------ GEMM
+enum GemmEpilogue : int {
+    EPI_F32 = 0,    // out[m][n] = acc (fp32)
+    EPI_F16 = 1,    // out[m][n] = acc (fp16)
+    EPI_GEGLU = 2,  // weight rows interleave gate and up in blocks of BN/2: out = gelu(gate) * up (fp16)
+    EPI_GELU_MUL = 3,  // out = gelu(acc) * aux[m][n] (fp16), aux fp32 with row stride ldaux
+};
+
+// One GEMM weight as the device keeps it: the Q8_0 planes (int8 values [N][K] and the fp16
+// block scales transposed to [K/32][N]) and, unless disabled, the exact fp16 dequantisation
+// [N][K] (each element round-to-nearest of scale * q, the value the Q8 path produces in
+// shared memory).
+struct DevWeight {
+    int N = 0, K = 0;
+    int8_t* q8 = nullptr;
+    __half* scales_t = nullptr;
+    __half* f16 = nullptr;
+    CUtensorMap map_q8, map_scales, map_f16;
+};
+
+// A row-major fp16 activation matrix that feeds GEMMs as the A operand.
+struct DevActivation {
+    __half* ptr = nullptr;
+    int rows = 0, cols = 0;
+    CUtensorMap map;
+};
+
+bool encode_weight_maps(DevWeight& w, int bn);
+bool encode_activation_map(DevActivation& a);
+
+struct GemmLaunch {
+    const DevActivation* a;
+    const DevWeight* w;
+    int m_rows;       // rows to compute, a multiple of kRowTile
+    void* out;
+    int ldo;          // output row stride in elements
+    int epilogue;
+    const float* aux = nullptr;
+    int ldaux = 0;
+    bool use_q8 = false;  // dequantise Q8 tiles in shared memory instead of reading fp16 weights
+    int* err;
+    int num_sms;
+};
+cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream);
+
+// ------------------------------------------------------------------ elementwise
+// x[t] = q8row(table[id]) * scale for t < ntok, 0 for padded rows; h = rmsnorm(x) * w (fp16).
+// Optionally also x16 = fp16(x) (the per-layer-input GEMM's operand).
+cudaError_t launch_embed(const int32_t* tokens, int ntok, int rows, const int8_t* table_q, const __half* table_s,
+                         int width, float scale, float* x, __half* x16, const float* norm_w, float eps, __half* h,
+                         cudaStream_t stream);
+
+// Per (token, head): q, k = rope(rmsnorm(head) * w); v = rmsnorm(head). Reads the fused
+// projection output qkv (fp32, [rows][(H + 2 KV) * hd]) and writes fp16 q, k, v; rows at or
+// past ntok are written as zeros.
+cudaError_t launch_qkv_norm_rope(const float* qkv, int ntok, int rows, int heads, int kv_heads, int hd,
+                                 const float* q_w, const float* k_w, const int32_t* positions, const float* rope,
+                                 float eps, __half* q, __half* k, __half* v, cudaStream_t stream);
+
+// x = (x + rmsnorm(t) * w_post) * scale; then, when w_next is set,
+// h16 = fp16(rmsnorm(x) * w_next) or y32 = rmsnorm(x) * w_next, and x16 = fp16(x) if set.
+cudaError_t launch_residual_norm(float* x, const float* t, int rows, int width, const float* w_post, float scale,
+                                 const float* w_next, float eps, __half* h16, float* y32, __half* x16,
+                                 cudaStream_t stream);
+
+// Per-row RMSNorm of `width`-wide chunks with a pre-scale: out = fp16(rmsnorm(x * pre) * w).
+cudaError_t launch_rmsnorm_rows(const float* x, int rows, int width, float pre, const float* w, float eps, float* out,
+                                cudaStream_t stream);
+
+// pooled[s] = mean over the sequence's rows of y (fp32).
+cudaError_t launch_mean_pool(const float* y, int width, const uint32_t* seqs, int nseq, float* pooled,
+                             cudaStream_t stream);
+
+// out[s][n] = sum_k in[s][k] * W[n][k] with W dequantised from Q8 planes on the fly, fp32.
+cudaError_t launch_dense_rows(const float* in, int nrows, const DevWeight& w, float* out, cudaStream_t stream);
+
+// out[s][n] = sum_k in[s][k] * w[n][k], fp32 weights [N][K].
+cudaError_t launch_dense_f32(const float* in, int nrows, const float* w, int N, int K, float* out,
+                             cudaStream_t stream);
+
+// positions[start + i] = i over the sequences (start, length) pairs.
+cudaError_t launch_positions(const uint32_t* seqs, int nseq, int32_t* positions, cudaStream_t stream);
+
+// ------------------------------------------------------------------ attention
+struct AttnLaunch {
+    const __half* q;  // [rows][heads * hd]
+    const __half* k;  // [rows][kv_heads * hd]
+    const __half* v;
+    __half* out;      // [rows][heads * hd]
+    const uint32_t* work;  // (seq_start, seq_len, q0) triples
+    int work_items;
+    int heads, kv_heads, hd;
+    int half_window;  // 0: global attention
+    int queries_per_item;
+    int* err;
+};
+cudaError_t launch_attention(const AttnLaunch& a, cudaStream_t stream);
+int attention_queries_per_item(int hd);
+
+}  // namespace ge

@@ -1,0 +1,843 @@
+// model.cpp -- loading (GGUF -> validated config -> repacked device weights) and the forward
+// pass on one device.  Mirrors the reference's EmbeddingModel.init (EmbeddingModel.swift:46-122),
+// ModelConfig / ModelWeights (Model/ModelConfig.swift:54-112, Model/Weights.swift:92-132) and
+// MetalForward.execute / encode (Metal/MetalForward.swift:310-423).
+#include "model.hpp"
+
+#include <math.h>
+#include <string.h>
+
+#include <algorithm>
+#include <thread>
+
+namespace ge {
+
+cudaError_t launch_qkv_norm_rope(const float* qkv, int ntok, int rows, int heads, int kv_heads, int hd,
+                                 const float* q_w, const float* k_w, const int32_t* positions, const float* rope,
+                                 float eps, __half* q, __half* k, __half* v, cudaStream_t stream);
+
+int Config::max_q() const {
+    int m = 0;
+    for (auto& l : layer) m = std::max(m, heads * l.hd);
+    return m;
+}
+int Config::max_kv() const {
+    int m = 0;
+    for (auto& l : layer) m = std::max(m, l.kv * l.hd);
+    return m;
+}
+
+int set_error(ge_model* m, int code, const std::string& msg) {
+    if (m) m->last_error = msg;
+    return code;
+}
+
+namespace {
+
+constexpr int kQ8GemmMaxRows = 256;  // batches at or below this many rows read Q8 weights directly
+constexpr int kBN = 256;
+
+int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+float half_bits_to_float(uint16_t h) {
+    __half_raw r;
+    r.x = h;
+    return __half2float(__half(r));
+}
+uint16_t float_to_half_bits(float f) {
+    __half h = __float2half_rn(f);
+    return __half_raw(h).x;
+}
+
+// ------------------------------------------------------------------ config
+struct LoadError {
+    int code;
+    std::string msg;
+};
+
+bool read_config(const GgufFile& f, Config& c, LoadError& e) {
+    if (!f.get_string("general.architecture", c.arch)) c.arch.clear();
+    if (c.arch != "gemma-embedding2" && c.arch != "gemma-embedding") {
+        e = {GE_ERR_UNSUPPORTED_ARCHITECTURE,
+             "unsupported architecture '" + c.arch + "'; supported: gemma-embedding2, gemma-embedding"};
+        return false;
+    }
+    const std::string a = c.arch + ".";
+    auto need_int = [&](const std::string& k, int& out) {
+        int64_t v;
+        if (!f.get_int(a + k, v)) {
+            e = {GE_ERR_MISSING_METADATA, "weight file lacks metadata key " + a + k};
+            return false;
+        }
+        out = int(v);
+        return true;
+    };
+    auto need_float = [&](const std::string& k, float& out) {
+        if (!f.get_float(a + k, out)) {
+            e = {GE_ERR_MISSING_METADATA, "weight file lacks metadata key " + a + k};
+            return false;
+        }
+        return true;
+    };
+    if (!need_int("block_count", c.layers) || !need_int("embedding_length", c.hidden) ||
+        !need_int("attention.head_count", c.heads))
+        return false;
+    std::vector<int32_t> kvs;
+    std::vector<bool> pattern;
+    if (!f.get_int_array(a + "attention.head_count_kv", kvs) || int(kvs.size()) != c.layers) {
+        e = {GE_ERR_MISSING_METADATA, "weight file lacks metadata key " + a + "attention.head_count_kv"};
+        return false;
+    }
+    if (!f.get_bool_array(a + "attention.sliding_window_pattern", pattern) || int(pattern.size()) != c.layers) {
+        e = {GE_ERR_MISSING_METADATA, "weight file lacks metadata key " + a + "attention.sliding_window_pattern"};
+        return false;
+    }
+    int hdg, hds, vg, vs;
+    if (!need_int("attention.key_length", hdg) || !need_int("attention.key_length_swa", hds) ||
+        !need_int("attention.value_length", vg) || !need_int("attention.value_length_swa", vs))
+        return false;
+    if (vg != hdg || vs != hds) {
+        e = {GE_ERR_INVALID_GGUF, "invalid GGUF file: key and value head sizes differ"};
+        return false;
+    }
+    float rope_g, rope_s;
+    if (!need_float("rope.freq_base", rope_g)) return false;
+    if (!f.get_float(a + "rope.freq_base_swa", rope_s)) rope_s = rope_g;
+    int64_t vocab;
+    if (!f.get_string_array_count("tokenizer.ggml.tokens", vocab)) {
+        e = {GE_ERR_MISSING_METADATA, "weight file lacks metadata key tokenizer.ggml.tokens"};
+        return false;
+    }
+    c.vocab = int(vocab);
+    if (!need_int("embedding_length_out", c.out_dim) || !need_int("feed_forward_length", c.ff) ||
+        !need_int("embedding_length_per_layer_input", c.per_layer) ||
+        !need_int("attention.sliding_window", c.sliding_window) ||
+        !need_float("attention.layer_norm_rms_epsilon", c.eps))
+        return false;
+    if (!f.get_string("general.name", c.name)) c.name = c.arch;
+    int64_t v;
+    if (f.get_int("tokenizer.ggml.bos_token_id", v)) c.bos_id = int(v);
+    if (f.get_int("tokenizer.ggml.eos_token_id", v)) c.eos_id = int(v);
+    c.layer.resize(c.layers);
+    for (int i = 0; i < c.layers; i++) {
+        LayerCfg& l = c.layer[i];
+        l.sliding = pattern[i];
+        l.kv = kvs[i];
+        l.hd = l.sliding ? hds : hdg;
+        l.rope_base = l.sliding ? rope_s : rope_g;
+        l.rope_index = -1;
+        for (size_t r = 0; r < c.ropes.size(); r++)
+            if (c.ropes[r].first == l.hd && c.ropes[r].second == l.rope_base) l.rope_index = int(r);
+        if (l.rope_index < 0) {
+            l.rope_index = int(c.ropes.size());
+            c.ropes.push_back({l.hd, l.rope_base});
+        }
+    }
+    c.emb_scale = sqrtf(float(c.hidden));
+    c.pl_scale = 1.0f / sqrtf(float(c.hidden));
+    c.has_ple = c.per_layer > 0;
+    c.has_output = c.arch == "gemma-embedding2";
+    c.has_dense = !c.has_output;
+    const GgufTensor* q = f.tensor("blk.0.attn_q.weight");
+    c.quant = !q ? "unknown" : q->type == GGML_Q8_0 ? "Q8_0" : q->type == GGML_F16 ? "F16" : q->type == GGML_BF16 ? "BF16" : "F32";
+    return true;
+}
+
+// ModelWeights' shape and type checks (Weights.swift:93-98).
+const GgufTensor* need_tensor(const GgufFile& f, const std::string& name, std::vector<int64_t> shape, bool f32_only,
+                              LoadError& e) {
+    const GgufTensor* t = f.tensor(name);
+    auto fmt = [](const std::vector<int64_t>& s) {
+        std::string r = "[";
+        for (size_t i = 0; i < s.size(); i++) r += (i ? ", " : "") + std::to_string(s[i]);
+        return r + "]";
+    };
+    if (!t) {
+        e = {GE_ERR_MISSING_TENSOR, "weight file lacks tensor " + name};
+        return nullptr;
+    }
+    if (t->shape != shape) {
+        e = {GE_ERR_SHAPE_MISMATCH, "tensor " + name + " has shape " + fmt(t->shape) + ", expected " + fmt(shape)};
+        return nullptr;
+    }
+    if (f32_only && t->type != GGML_F32) {
+        e = {GE_ERR_UNSUPPORTED_TENSOR_TYPE, "tensor " + name + " uses unsupported storage type " + std::to_string(t->type)};
+        return nullptr;
+    }
+    return t;
+}
+
+// Dequantised fp32 row of a tensor (WeightTensor.dequantizeRow, Weights.swift:19-43).
+void dequant_row(const GgufTensor& t, int64_t row, float* out) {
+    const int64_t n = t.cols();
+    const uint8_t* p = t.data + row * (n / ggml_block_elems(t.type) * ggml_block_bytes(t.type));
+    switch (t.type) {
+    case GGML_F32: memcpy(out, p, size_t(n) * 4); break;
+    case GGML_F16:
+        for (int64_t i = 0; i < n; i++) {
+            uint16_t h;
+            memcpy(&h, p + 2 * i, 2);
+            out[i] = half_bits_to_float(h);
+        }
+        break;
+    case GGML_BF16:
+        for (int64_t i = 0; i < n; i++) {
+            uint16_t h;
+            memcpy(&h, p + 2 * i, 2);
+            uint32_t b = uint32_t(h) << 16;
+            memcpy(&out[i], &b, 4);
+        }
+        break;
+    case GGML_Q8_0:
+        for (int64_t b = 0; b < n / 32; b++) {
+            uint16_t h;
+            memcpy(&h, p + b * 34, 2);
+            const float s = half_bits_to_float(h);
+            for (int j = 0; j < 32; j++) out[b * 32 + j] = s * float(int8_t(p[b * 34 + 2 + j]));
+        }
+        break;
+    }
+}
+
+template <class F>
+void parallel_rows(int64_t rows, F fn) {
+    const int nt = std::max(1, std::min<int>(16, int(std::thread::hardware_concurrency())));
+    std::vector<std::thread> th;
+    for (int t = 0; t < nt; t++)
+        th.emplace_back([=]() {
+            for (int64_t r = t; r < rows; r += nt) fn(r);
+        });
+    for (auto& x : th) x.join();
+}
+
+// A GEMM weight assembled on the host from one or more GGUF tensors stacked along N.
+// `rows_of(dst_row)` names the (tensor, source row) each destination row comes from.
+struct HostWeight {
+    int N = 0, K = 0;
+    bool q8 = true;
+    std::vector<int8_t> q;
+    std::vector<uint16_t> scales_t;  // [K/32][N]
+    std::vector<uint16_t> f16;       // [N][K]
+};
+
+template <class RowFn>
+HostWeight build_weight(int N, int K, bool want_f16, RowFn src) {
+    HostWeight w;
+    w.N = N;
+    w.K = K;
+    const GgufTensor* t0 = src(0).first;
+    w.q8 = t0->type == GGML_Q8_0;
+    for (int r = 1; r < N && w.q8; r++) w.q8 = src(r).first->type == GGML_Q8_0;
+    if (w.q8) {
+        w.q.resize(size_t(N) * K);
+        w.scales_t.resize(size_t(N) * (K / 32));
+    }
+    if (want_f16 || !w.q8) w.f16.resize(size_t(N) * K);
+    parallel_rows(N, [&](int64_t r) {
+        auto s = src(int(r));
+        const GgufTensor& t = *s.first;
+        if (w.q8) {
+            const uint8_t* p = t.data + int64_t(s.second) * (K / 32) * 34;
+            for (int b = 0; b < K / 32; b++) {
+                uint16_t h;
+                memcpy(&h, p + b * 34, 2);
+                w.scales_t[size_t(b) * N + r] = h;
+                const float sc = half_bits_to_float(h);
+                for (int j = 0; j < 32; j++) {
+                    const int8_t qv = int8_t(p[b * 34 + 2 + j]);
+                    w.q[size_t(r) * K + b * 32 + j] = qv;
+                    // scale * q is exact in fp32; one round to nearest gives the fp16 operand.
+                    if (!w.f16.empty()) w.f16[size_t(r) * K + b * 32 + j] = float_to_half_bits(sc * float(qv));
+                }
+            }
+        } else {
+            std::vector<float> row(K);
+            dequant_row(t, s.second, row.data());
+            for (int k = 0; k < K; k++) w.f16[size_t(r) * K + k] = float_to_half_bits(row[k]);
+        }
+    });
+    return w;
+}
+
+std::vector<float> dequant_matrix(const GgufTensor& t) {
+    std::vector<float> out(size_t(t.elements()));
+    parallel_rows(t.rows(), [&](int64_t r) { dequant_row(t, r, out.data() + r * t.cols()); });
+    return out;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ device memory helpers
+template <class T>
+static cudaError_t dev_alloc(Device& d, T** p, size_t count) {
+    void* q = nullptr;
+    cudaError_t e = cudaMalloc(&q, std::max<size_t>(count, 1) * sizeof(T));
+    if (e != cudaSuccess) return e;
+    d.allocations.push_back(q);
+    *p = static_cast<T*>(q);
+    return cudaSuccess;
+}
+
+template <class T>
+static cudaError_t dev_upload(Device& d, T** p, const T* src, size_t count) {
+    cudaError_t e = dev_alloc(d, p, count);
+    if (e == cudaSuccess && count) e = cudaMemcpy(*p, src, count * sizeof(T), cudaMemcpyHostToDevice);
+    return e;
+}
+
+static cudaError_t upload_weight(Device& d, DevWeight& w, const HostWeight& h) {
+    w.N = h.N;
+    w.K = h.K;
+    cudaError_t e = cudaSuccess;
+    if (h.q8) {
+        e = dev_upload(d, &w.q8, h.q.data(), h.q.size());
+        if (e == cudaSuccess) e = dev_upload(d, reinterpret_cast<uint16_t**>(&w.scales_t), h.scales_t.data(), h.scales_t.size());
+    }
+    if (e == cudaSuccess && !h.f16.empty())
+        e = dev_upload(d, reinterpret_cast<uint16_t**>(&w.f16), h.f16.data(), h.f16.size());
+    if (e == cudaSuccess && !encode_weight_maps(w, kBN)) e = cudaErrorInvalidValue;
+    return e;
+}
+
+static void free_workspace(Workspace& ws) {
+    for (void* p : {(void*)ws.tokens, (void*)ws.positions, (void*)ws.seqs, (void*)ws.work, (void*)ws.x, (void*)ws.qkv,
+                    (void*)ws.o, (void*)ws.y, (void*)ws.ple, (void*)ws.pooled, (void*)ws.mid, (void*)ws.out,
+                    (void*)ws.h, (void*)ws.x16, (void*)ws.q, (void*)ws.k, (void*)ws.v, (void*)ws.attn, (void*)ws.act,
+                    (void*)ws.g})
+        if (p) cudaFree(p);
+    for (void* p : {(void*)ws.h_tokens, (void*)ws.h_positions, (void*)ws.h_seqs, (void*)ws.h_work, (void*)ws.h_out,
+                    (void*)ws.h_err})
+        if (p) cudaFreeHost(p);
+    ws = Workspace();
+}
+
+// Grows the workspace to at least (rows, seqs, work items) (MetalForward.workspace(forRows:),
+// MetalForward.swift:173-178).  Capacities grow geometrically so repeated calls settle.
+static cudaError_t ensure_workspace(const Config& c, Device& d, int rows, int seqs, int work) {
+    Workspace& ws = d.ws;
+    if (ws.cap_rows >= rows && ws.cap_seqs >= seqs && ws.cap_work >= work) return cudaSuccess;
+    cudaError_t e = cudaStreamSynchronize(d.stream);
+    if (e != cudaSuccess) return e;
+    const int R = std::max(rows, ws.cap_rows + ws.cap_rows / 2 > rows ? round_up(ws.cap_rows + ws.cap_rows / 2, kRowTile) : rows);
+    const int S = std::max({seqs, ws.cap_seqs * 2, 16});
+    const int W = std::max({work, ws.cap_work * 2, 64});
+    free_workspace(ws);
+    const size_t d_ = size_t(c.hidden), qd = size_t(c.max_q()), kvd = size_t(c.max_kv());
+    const size_t qkvd = qd + 2 * kvd;
+    auto A = [&](auto** p, size_t n) -> cudaError_t {
+        using T = std::remove_pointer_t<std::remove_reference_t<decltype(*p)>>;
+        void* q = nullptr;
+        cudaError_t r = cudaMalloc(&q, std::max<size_t>(n, 1) * sizeof(T));
+        *p = static_cast<T*>(q);
+        return r;
+    };
+    auto H = [&](auto** p, size_t n) -> cudaError_t {
+        using T = std::remove_pointer_t<std::remove_reference_t<decltype(*p)>>;
+        void* q = nullptr;
+        cudaError_t r = cudaMallocHost(&q, std::max<size_t>(n, 1) * sizeof(T));
+        *p = static_cast<T*>(q);
+        return r;
+    };
+    const size_t r = size_t(R);
+    cudaError_t err = cudaSuccess;
+    auto chk = [&](cudaError_t x) {
+        if (err == cudaSuccess) err = x;
+    };
+    chk(A(&ws.tokens, r));
+    chk(A(&ws.positions, r));
+    chk(A(&ws.seqs, 2 * size_t(S)));
+    chk(A(&ws.work, 3 * size_t(W)));
+    chk(A(&ws.x, r * d_));
+    chk(A(&ws.qkv, r * qkvd));
+    chk(A(&ws.o, r * d_));
+    chk(A(&ws.y, r * d_));
+    chk(A(&ws.h, r * d_));
+    chk(A(&ws.q, r * qd));
+    chk(A(&ws.k, r * kvd));
+    chk(A(&ws.v, r * kvd));
+    chk(A(&ws.attn, r * qd));
+    chk(A(&ws.act, r * size_t(c.ff)));
+    if (c.has_ple) {
+        chk(A(&ws.x16, r * d_));
+        chk(A(&ws.ple, r * size_t(c.layers) * c.per_layer));
+        chk(A(&ws.g, r * size_t(c.per_layer)));
+    }
+    chk(A(&ws.pooled, size_t(S) * d_));
+    chk(A(&ws.mid, size_t(S) * std::max(c.dense_head, 1)));
+    chk(A(&ws.out, size_t(S) * c.out_dim));
+    chk(H(&ws.h_tokens, r));
+    chk(H(&ws.h_positions, r));
+    chk(H(&ws.h_seqs, 2 * size_t(S)));
+    chk(H(&ws.h_work, 3 * size_t(W)));
+    chk(H(&ws.h_out, size_t(S) * std::max(c.out_dim, c.hidden)));
+    chk(H(&ws.h_err, 1));
+    if (err != cudaSuccess) {
+        free_workspace(ws);
+        return err;
+    }
+    ws.cap_rows = R;
+    ws.cap_seqs = S;
+    ws.cap_work = W;
+    auto act = [&](DevActivation& a, __half* p, int cols) {
+        a.ptr = p;
+        a.rows = R;
+        a.cols = cols;
+        return encode_activation_map(a);
+    };
+    bool ok = act(ws.a_h, ws.h, c.hidden) && act(ws.a_act, ws.act, c.ff);
+    if (c.has_ple) ok = ok && act(ws.a_x16, ws.x16, c.hidden) && act(ws.a_g, ws.g, c.per_layer);
+    ws.a_attn.clear();
+    for (auto& l : c.layer) {
+        const int cols = c.heads * l.hd;
+        bool have = false;
+        for (auto& a : ws.a_attn) have = have || a.cols == cols;
+        if (!have) {
+            DevActivation a;
+            ok = ok && act(a, ws.attn, cols);
+            ws.a_attn.push_back(a);
+        }
+    }
+    return ok ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// ------------------------------------------------------------------ load
+static int load_device(ge_model* m, Device& d, const std::vector<HostWeight>& hw, const std::vector<std::vector<float>>& norms,
+                       const std::vector<std::vector<float>>& ropes, const std::vector<float>& dense2,
+                       const std::vector<float>& dense3, const std::vector<float>& output, const HostWeight& emb,
+                       const HostWeight* plp) {
+    const Config& c = m->cfg;
+    cudaError_t e = cudaSetDevice(d.ordinal);
+    cudaDeviceProp prop;
+    if (e == cudaSuccess) e = cudaGetDeviceProperties(&prop, d.ordinal);
+    if (e != cudaSuccess) return set_error(m, GE_ERR_NO_DEVICE, std::string("cannot use CUDA device: ") + cudaGetErrorString(e));
+    if (prop.major != 10)
+        return set_error(m, GE_ERR_NO_DEVICE, std::string("device ") + prop.name + " is not an sm_100 (B200-class) GPU");
+    d.num_sms = prop.multiProcessorCount;
+    d.name = prop.name;
+    e = cudaStreamCreateWithFlags(&d.stream, cudaStreamNonBlocking);
+    auto fail = [&](cudaError_t x) {
+        return set_error(m, x == cudaErrorMemoryAllocation ? GE_ERR_OUT_OF_MEMORY : GE_ERR_GPU_FAILURE,
+                         std::string("device upload failed: ") + cudaGetErrorString(x));
+    };
+    if (e != cudaSuccess) return fail(e);
+    if ((e = dev_alloc(d, &d.err, 1)) != cudaSuccess || (e = cudaMemset(d.err, 0, sizeof(int))) != cudaSuccess) return fail(e);
+    // Token embedding table: int8 plane [V][d] and fp16 scales [V][d/32].
+    if ((e = dev_upload(d, &d.emb_q, emb.q.data(), emb.q.size())) != cudaSuccess) return fail(e);
+    if ((e = dev_upload(d, reinterpret_cast<uint16_t**>(&d.emb_s), emb.scales_t.data(), emb.scales_t.size())) != cudaSuccess)
+        return fail(e);
+    size_t ni = 0, wi = 0;
+    cudaError_t norm_err = cudaSuccess;
+    auto norm = [&](float** p) {
+        cudaError_t x = dev_upload(d, p, norms[ni].data(), norms[ni].size());
+        if (norm_err == cudaSuccess) norm_err = x;
+        ni++;
+    };
+    d.layers.resize(c.layers);
+    for (int l = 0; l < c.layers; l++) {
+        LayerDev& L = d.layers[l];
+        for (DevWeight* w : {&L.qkv, &L.o, &L.gu, &L.down})
+            if ((e = upload_weight(d, *w, hw[wi++])) != cudaSuccess) return fail(e);
+        if (c.has_ple)
+            for (DevWeight* w : {&L.inp_gate, &L.proj})
+                if ((e = upload_weight(d, *w, hw[wi++])) != cudaSuccess) return fail(e);
+        norm(&L.attn_norm);
+        norm(&L.q_norm);
+        norm(&L.k_norm);
+        norm(&L.post_attn);
+        norm(&L.ffn_norm);
+        norm(&L.post_ffw);
+        if (c.has_ple) {
+            norm(&L.post_norm);
+            L.out_scale = norms[ni++][0];
+        }
+    }
+    norm(&d.out_norm);
+    if (c.has_ple) {
+        norm(&d.pl_norm);
+        if ((e = upload_weight(d, d.plp, *plp)) != cudaSuccess) return fail(e);
+    }
+    if (norm_err != cudaSuccess) return fail(norm_err);
+    for (auto& r : ropes) {
+        float* p = nullptr;
+        if ((e = dev_upload(d, &p, r.data(), r.size())) != cudaSuccess) return fail(e);
+        d.rope.push_back(p);
+    }
+    if (c.has_dense) {
+        if ((e = dev_upload(d, &d.dense2, dense2.data(), dense2.size())) != cudaSuccess) return fail(e);
+        if ((e = dev_upload(d, &d.dense3, dense3.data(), dense3.size())) != cudaSuccess) return fail(e);
+    }
+    if (c.has_output && (e = dev_upload(d, &d.output, output.data(), output.size())) != cudaSuccess) return fail(e);
+    return GE_OK;
+}
+
+static void free_device(Device& d) {
+    if (d.stream) {
+        cudaSetDevice(d.ordinal);
+        cudaStreamSynchronize(d.stream);
+    }
+    free_workspace(d.ws);
+    for (void* p : d.allocations) cudaFree(p);
+    d.allocations.clear();
+    if (d.stream) cudaStreamDestroy(d.stream);
+    d.stream = nullptr;
+}
+
+int load_model(ge_model* m, const char* path, const ge_load_opts* opts) {
+    GgufError ge_err;
+    if (!path) return set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: weight path is NULL");
+    int rc = m->file.open(path, ge_err);
+    if (rc) return set_error(m, ge_err.code, ge_err.message);
+    m->file_size = int64_t(m->file.size);
+    LoadError le{0, ""};
+    Config& c = m->cfg;
+    if (!read_config(m->file, c, le)) return set_error(m, le.code, le.msg);
+    if (c.layers <= 0 || c.hidden % 128 || c.ff % 128 || c.heads <= 0)
+        return set_error(m, GE_ERR_INVALID_GGUF, "invalid GGUF file: unsupported dimensions");
+    for (auto& l : c.layer)
+        if ((l.hd != 256 && l.hd != 512) || l.kv <= 0 || c.heads % l.kv)
+            return set_error(m, GE_ERR_INVALID_GGUF, "invalid GGUF file: unsupported head layout");
+    const GgufFile& f = m->file;
+    const int d = c.hidden, ff = c.ff, pl = c.per_layer;
+    // ---- shape checks (ModelWeights.init, Weights.swift:100-131)
+    const GgufTensor* emb = need_tensor(f, "token_embd.weight", {d, c.vocab}, false, le);
+    if (!emb) return set_error(m, le.code, le.msg);
+    if (emb->type != GGML_Q8_0)
+        return set_error(m, GE_ERR_UNSUPPORTED_TENSOR_TYPE, "tensor token_embd.weight must be Q8_0");
+    const GgufTensor *plp = nullptr, *pln = nullptr, *outn, *outw = nullptr, *d2 = nullptr, *d3 = nullptr;
+    if (c.has_ple) {
+        if (!(plp = need_tensor(f, "per_layer_model_proj.weight", {d, int64_t(pl) * c.layers}, false, le)) ||
+            !(pln = need_tensor(f, "per_layer_proj_norm.weight", {pl}, true, le)))
+            return set_error(m, le.code, le.msg);
+    }
+    if (!(outn = need_tensor(f, "output_norm.weight", {d}, true, le))) return set_error(m, le.code, le.msg);
+    if (c.has_output) {
+        if (!(outw = need_tensor(f, "output.weight", {d, c.out_dim}, false, le))) return set_error(m, le.code, le.msg);
+    } else {
+        const GgufTensor* t = f.tensor("dense_2.weight");
+        if (!t || t->shape.size() != 2) return set_error(m, GE_ERR_MISSING_TENSOR, "weight file lacks tensor dense_2.weight");
+        c.dense_head = int(t->shape[1]);
+        if (!(d2 = need_tensor(f, "dense_2.weight", {d, c.dense_head}, false, le)) ||
+            !(d3 = need_tensor(f, "dense_3.weight", {c.dense_head, c.out_dim}, false, le)))
+            return set_error(m, le.code, le.msg);
+    }
+    struct LT {
+        const GgufTensor *attn_norm, *q, *k, *v, *o, *qn, *kn, *pan, *fn, *gate, *up, *down, *pfn, *ig, *proj, *pn, *os;
+    };
+    std::vector<LT> lt(c.layers);
+    for (int i = 0; i < c.layers; i++) {
+        const int hd = c.layer[i].hd, qd = c.heads * hd, kvd = c.layer[i].kv * hd;
+        const std::string p = "blk." + std::to_string(i) + ".";
+        LT& t = lt[i];
+        if (!(t.attn_norm = need_tensor(f, p + "attn_norm.weight", {d}, true, le)) ||
+            !(t.q = need_tensor(f, p + "attn_q.weight", {d, qd}, false, le)) ||
+            !(t.k = need_tensor(f, p + "attn_k.weight", {d, kvd}, false, le)) ||
+            !(t.v = need_tensor(f, p + "attn_v.weight", {d, kvd}, false, le)) ||
+            !(t.o = need_tensor(f, p + "attn_output.weight", {qd, d}, false, le)) ||
+            !(t.qn = need_tensor(f, p + "attn_q_norm.weight", {hd}, true, le)) ||
+            !(t.kn = need_tensor(f, p + "attn_k_norm.weight", {hd}, true, le)) ||
+            !(t.pan = need_tensor(f, p + "post_attention_norm.weight", {d}, true, le)) ||
+            !(t.fn = need_tensor(f, p + "ffn_norm.weight", {d}, true, le)) ||
+            !(t.gate = need_tensor(f, p + "ffn_gate.weight", {d, ff}, false, le)) ||
+            !(t.up = need_tensor(f, p + "ffn_up.weight", {d, ff}, false, le)) ||
+            !(t.down = need_tensor(f, p + "ffn_down.weight", {ff, d}, false, le)) ||
+            !(t.pfn = need_tensor(f, p + "post_ffw_norm.weight", {d}, true, le)))
+            return set_error(m, le.code, le.msg);
+        if (c.has_ple) {
+            if (!(t.ig = need_tensor(f, p + "inp_gate.weight", {d, pl}, false, le)) ||
+                !(t.proj = need_tensor(f, p + "proj.weight", {pl, d}, false, le)) ||
+                !(t.pn = need_tensor(f, p + "post_norm.weight", {d}, true, le)) ||
+                !(t.os = need_tensor(f, p + "layer_output_scale.weight", {1}, true, le)))
+                return set_error(m, le.code, le.msg);
+        }
+    }
+    // ---- host-side repack
+    const bool want_f16 = !(m->flags & GE_LOAD_Q8_ONLY);
+    std::vector<HostWeight> hw;
+    for (int i = 0; i < c.layers; i++) {
+        const LT& t = lt[i];
+        const int hd = c.layer[i].hd, qd = c.heads * hd, kvd = c.layer[i].kv * hd;
+        if ((qd + 2 * kvd) % kBN || d % kBN || (2 * ff) % kBN || (pl && pl % kBN))
+            return set_error(m, GE_ERR_INVALID_GGUF, "invalid GGUF file: projection widths must be multiples of 256");
+        // Fused q, k, v projection: rows [Wq; Wk; Wv].
+        hw.push_back(build_weight(qd + 2 * kvd, d, want_f16, [&](int r) -> std::pair<const GgufTensor*, int> {
+            if (r < qd) return {t.q, r};
+            if (r < qd + kvd) return {t.k, r - qd};
+            return {t.v, r - qd - kvd};
+        }));
+        hw.push_back(build_weight(d, qd, want_f16, [&](int r) -> std::pair<const GgufTensor*, int> { return {t.o, r}; }));
+        // Gate and up interleaved in blocks of kBN/2 rows, so one output tile holds both halves.
+        hw.push_back(build_weight(2 * ff, d, want_f16, [&](int r) -> std::pair<const GgufTensor*, int> {
+            const int blk = r / (kBN / 2), off = r % (kBN / 2);
+            return {(blk & 1) ? t.up : t.gate, (blk >> 1) * (kBN / 2) + off};
+        }));
+        hw.push_back(build_weight(d, ff, want_f16, [&](int r) -> std::pair<const GgufTensor*, int> { return {t.down, r}; }));
+        if (c.has_ple) {
+            hw.push_back(build_weight(pl, d, want_f16, [&](int r) -> std::pair<const GgufTensor*, int> { return {t.ig, r}; }));
+            hw.push_back(build_weight(d, pl, want_f16, [&](int r) -> std::pair<const GgufTensor*, int> { return {t.proj, r}; }));
+        }
+    }
+    std::vector<std::vector<float>> norms;
+    for (int i = 0; i < c.layers; i++) {
+        const LT& t = lt[i];
+        for (const GgufTensor* n : {t.attn_norm, t.qn, t.kn, t.pan, t.fn, t.pfn}) norms.push_back(dequant_matrix(*n));
+        if (c.has_ple) {
+            norms.push_back(dequant_matrix(*t.pn));
+            norms.push_back(dequant_matrix(*t.os));
+        }
+    }
+    norms.push_back(dequant_matrix(*outn));
+    if (c.has_ple) norms.push_back(dequant_matrix(*pln));
+    // RoPE tables (RopeTable.swift:16-31): invFreq in double, cos/sin rounded to float.
+    std::vector<std::vector<float>> ropes;
+    for (auto& rp : c.ropes) {
+        const int hd = rp.first, pairs = hd / 2;
+        std::vector<float> tab(size_t(c.max_tokens) * pairs * 2);
+        for (int i = 0; i < pairs; i++) {
+            const double inv = pow(double(rp.second), -2.0 * double(i) / double(hd));
+            for (int pos = 0; pos < c.max_tokens; pos++) {
+                const double th = double(pos) * inv;
+                tab[(size_t(pos) * pairs + i) * 2] = float(cos(th));
+                tab[(size_t(pos) * pairs + i) * 2 + 1] = float(sin(th));
+            }
+        }
+        ropes.push_back(std::move(tab));
+    }
+    std::vector<float> dense2, dense3, output;
+    if (c.has_dense) {
+        dense2 = dequant_matrix(*d2);
+        dense3 = dequant_matrix(*d3);
+    }
+    if (c.has_output) output = dequant_matrix(*outw);
+    // Embedding table planes: int8 [V][d] and scales [V][d/32] (row-major, not transposed).
+    HostWeight embw;
+    embw.N = c.vocab;
+    embw.K = d;
+    embw.q.resize(size_t(c.vocab) * d);
+    embw.scales_t.resize(size_t(c.vocab) * (d / 32));
+    parallel_rows(c.vocab, [&](int64_t r) {
+        const uint8_t* p = emb->data + r * (d / 32) * 34;
+        for (int b = 0; b < d / 32; b++) {
+            memcpy(&embw.scales_t[size_t(r) * (d / 32) + b], p + b * 34, 2);
+            memcpy(&embw.q[size_t(r) * d + b * 32], p + b * 34 + 2, 32);
+        }
+    });
+    HostWeight plpw;
+    if (c.has_ple)
+        plpw = build_weight(pl * c.layers, d, true, [&](int r) -> std::pair<const GgufTensor*, int> { return {plp, r}; });
+
+    // ---- devices
+    uint32_t mask = opts ? opts->device_mask : 0;
+    if (!mask) mask = 1;
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0)
+        return set_error(m, GE_ERR_NO_DEVICE, "no CUDA device is available");
+    for (int i = 0; i < 32; i++)
+        if (mask & (1u << i)) {
+            if (i >= count) return set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: device " + std::to_string(i) + " does not exist");
+            Device dv;
+            dv.ordinal = i;
+            m->devs.push_back(dv);
+        }
+    for (auto& dv : m->devs) {
+        rc = load_device(m, dv, hw, norms, ropes, dense2, dense3, output, embw, c.has_ple ? &plpw : nullptr);
+        if (rc) return rc;
+    }
+    return GE_OK;
+}
+
+void free_model(ge_model* m) {
+    for (auto& d : m->devs) free_device(d);
+    m->devs.clear();
+}
+
+// ------------------------------------------------------------------ forward
+// Work items, one per block of `qpi` queries of every sequence (AttentionWork.items,
+// MetalForward.swift:45-58).
+static int build_work(const ge_seq* seqs, int nseq, int qpi, uint32_t* out) {
+    int n = 0;
+    for (int s = 0; s < nseq; s++)
+        for (uint32_t q0 = 0; q0 < seqs[s].length; q0 += uint32_t(qpi)) {
+            if (out) {
+                out[3 * n] = seqs[s].start;
+                out[3 * n + 1] = seqs[s].length;
+                out[3 * n + 2] = q0;
+            }
+            n++;
+        }
+    return n;
+}
+
+int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
+    const Config& c = m->cfg;
+    cudaError_t e = cudaSetDevice(d.ordinal);
+    cudaStream_t st = a.stream ? a.stream : d.stream;
+    auto report = [&](int code, const std::string& msg) {
+        if (a.error) *a.error = msg;
+        else m->last_error = msg;
+        return code;
+    };
+    auto gpu_fail = [&](cudaError_t x, const char* what) {
+        return report(x == cudaErrorMemoryAllocation ? GE_ERR_OUT_OF_MEMORY : GE_ERR_GPU_FAILURE,
+                      std::string("GPU execution failed: ") + what + ": " + cudaGetErrorString(x));
+    };
+    if (e != cudaSuccess) return gpu_fail(e, "cudaSetDevice");
+    const int ntok = a.ntok, nseq = a.nseq;
+    const int rows = std::max(kRowTile, round_up(ntok, kRowTile));
+    const int qpi = attention_queries_per_item(256);
+    const int nwork = build_work(a.seqs, nseq, qpi, nullptr);
+    if ((e = ensure_workspace(c, d, rows, nseq, nwork)) != cudaSuccess) return gpu_fail(e, "workspace");
+    Workspace& ws = d.ws;
+    // ---- inputs
+    for (int s = 0; s < nseq; s++) {
+        ws.h_seqs[2 * s] = a.seqs[s].start;
+        ws.h_seqs[2 * s + 1] = a.seqs[s].length;
+    }
+    build_work(a.seqs, nseq, qpi, ws.h_work);
+    const int32_t* tokens = ws.tokens;
+    if (a.tokens_on_device) {
+        tokens = a.tokens;
+    } else {
+        memcpy(ws.h_tokens, a.tokens, size_t(ntok) * 4);
+        if ((e = cudaMemcpyAsync(ws.tokens, ws.h_tokens, size_t(ntok) * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+            return gpu_fail(e, "token upload");
+    }
+    if ((e = cudaMemcpyAsync(ws.seqs, ws.h_seqs, size_t(nseq) * 8, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(ws.work, ws.h_work, size_t(nwork) * 12, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+        return gpu_fail(e, "batch upload");
+    if (a.positions) {
+        memcpy(ws.h_positions, a.positions, size_t(ntok) * 4);
+        e = cudaMemcpyAsync(ws.positions, ws.h_positions, size_t(ntok) * 4, cudaMemcpyHostToDevice, st);
+    } else {
+        e = launch_positions(ws.seqs, nseq, ws.positions, st);
+    }
+    if (e != cudaSuccess) return gpu_fail(e, "positions");
+
+    // ---- layers (MetalForward.encode, MetalForward.swift:364-423)
+    const int D = c.hidden;
+    const bool q8 = rows <= kQ8GemmMaxRows || (m->flags & GE_LOAD_Q8_ONLY);
+    auto gemm = [&](const DevActivation& A, const DevWeight& W, void* out, int ldo, int epi, const float* aux = nullptr,
+                    int ldaux = 0) {
+        GemmLaunch g;
+        g.a = &A;
+        g.w = &W;
+        g.m_rows = rows;
+        g.out = out;
+        g.ldo = ldo;
+        g.epilogue = epi;
+        g.aux = aux;
+        g.ldaux = ldaux;
+        g.use_q8 = q8;
+        g.err = d.err;
+        g.num_sms = d.num_sms;
+        return launch_gemm(g, st);
+    };
+#define CK(expr, what)                                  \
+    do {                                                \
+        cudaError_t e_ = (expr);                        \
+        if (e_ != cudaSuccess) return gpu_fail(e_, what); \
+    } while (0)
+
+    CK(launch_embed(tokens, ntok, rows, d.emb_q, d.emb_s, D, c.emb_scale, ws.x, c.has_ple ? ws.x16 : nullptr,
+                    d.layers[0].attn_norm, c.eps, ws.h, st),
+       "embed");
+    if (c.has_ple) {
+        // ple = rmsnorm_pl(x0 * Wplp^T / sqrt(d)) for every layer at once (CPUReference.swift:206-210).
+        const int plw = c.per_layer * c.layers;
+        CK(gemm(ws.a_x16, d.plp, ws.ple, plw, EPI_F32), "per-layer projection");
+        CK(launch_rmsnorm_rows(ws.ple, rows * c.layers, c.per_layer, c.pl_scale, d.pl_norm, c.eps, ws.ple, st),
+           "per-layer norm");
+    }
+    for (int l = 0; l < c.layers; l++) {
+        const LayerCfg& lc = c.layer[l];
+        const LayerDev& L = d.layers[l];
+        const int qd = c.heads * lc.hd;
+        CK(gemm(ws.a_h, L.qkv, ws.qkv, L.qkv.N, EPI_F32), "qkv projection");
+        CK(launch_qkv_norm_rope(ws.qkv, ntok, rows, c.heads, lc.kv, lc.hd, L.q_norm, L.k_norm, ws.positions,
+                                d.rope[lc.rope_index], c.eps, ws.q, ws.k, ws.v, st),
+           "q/k/v norm and rope");
+        AttnLaunch al;
+        al.q = ws.q;
+        al.k = ws.k;
+        al.v = ws.v;
+        al.out = ws.attn;
+        al.work = ws.work;
+        al.work_items = nwork;
+        al.heads = c.heads;
+        al.kv_heads = lc.kv;
+        al.hd = lc.hd;
+        al.half_window = lc.sliding ? c.sliding_window / 2 : 0;
+        al.queries_per_item = qpi;
+        al.err = d.err;
+        CK(launch_attention(al, st), "attention");
+        const DevActivation* aa = nullptr;
+        for (auto& x : ws.a_attn)
+            if (x.cols == qd) aa = &x;
+        CK(gemm(*aa, L.o, ws.o, D, EPI_F32), "attention output");
+        CK(launch_residual_norm(ws.x, ws.o, rows, D, L.post_attn, 1.0f, L.ffn_norm, c.eps, ws.h, nullptr, nullptr, st),
+           "post-attention residual");
+        CK(gemm(ws.a_h, L.gu, ws.act, c.ff, EPI_GEGLU), "gate/up projection");
+        CK(gemm(ws.a_act, L.down, ws.o, D, EPI_F32), "down projection");
+        const bool last = l + 1 == c.layers;
+        const float* next = last ? d.out_norm : d.layers[l + 1].attn_norm;
+        if (c.has_ple) {
+            CK(launch_residual_norm(ws.x, ws.o, rows, D, L.post_ffw, 1.0f, nullptr, c.eps, nullptr, nullptr, ws.x16, st),
+               "post-ffn residual");
+            CK(gemm(ws.a_x16, L.inp_gate, ws.g, c.per_layer, EPI_GELU_MUL, ws.ple + size_t(l) * c.per_layer,
+                    c.per_layer * c.layers),
+               "per-layer gate");
+            CK(gemm(ws.a_g, L.proj, ws.o, D, EPI_F32), "per-layer projection");
+            CK(launch_residual_norm(ws.x, ws.o, rows, D, L.post_norm, L.out_scale, next, c.eps, last ? nullptr : ws.h,
+                                    last ? ws.y : nullptr, nullptr, st),
+               "per-layer residual");
+        } else {
+            CK(launch_residual_norm(ws.x, ws.o, rows, D, L.post_ffw, 1.0f, next, c.eps, last ? nullptr : ws.h,
+                                    last ? ws.y : nullptr, nullptr, st),
+               "post-ffn residual");
+        }
+        if (a.trace_layer == l) break;
+    }
+    // ---- pooling and head
+    const float* result = nullptr;
+    int width = c.out_dim;
+    if (a.trace_layer >= 0) {
+        result = ws.x;
+        width = D;
+    } else if (a.trace_layer == -1) {
+        result = ws.y;
+        width = D;
+    } else {
+        CK(launch_mean_pool(ws.y, D, ws.seqs, nseq, ws.pooled, st), "mean pool");
+        if (c.has_dense) {
+            CK(launch_dense_f32(ws.pooled, nseq, d.dense2, c.dense_head, D, ws.mid, st), "dense head");
+            CK(launch_dense_f32(ws.mid, nseq, d.dense3, c.out_dim, c.dense_head, ws.out, st), "dense head");
+        } else {
+            CK(launch_dense_f32(ws.pooled, nseq, d.output, c.out_dim, D, ws.out, st), "output projection");
+        }
+        result = ws.out;
+    }
+    const size_t out_elems = a.trace_layer >= -1 ? size_t(ntok) * D : size_t(nseq) * width;
+    float* host_out = a.trace_layer >= -1 ? a.trace_out : a.out;
+    if (a.out_on_device && a.trace_layer < -1) {
+        CK(cudaMemcpyAsync(a.out, result, out_elems * 4, cudaMemcpyDeviceToDevice, st), "result copy");
+        return GE_OK;
+    }
+    CK(cudaMemcpyAsync(ws.h_err, d.err, sizeof(int), cudaMemcpyDeviceToHost, st), "error readback");
+    if (a.trace_layer >= -1) {
+        // The trace spans ntok rows of D, which may exceed the pooled staging buffer.
+        CK(cudaMemcpyAsync(host_out, result, out_elems * 4, cudaMemcpyDeviceToHost, st), "trace readback");
+        CK(cudaStreamSynchronize(st), "synchronize");
+    } else {
+        CK(cudaMemcpyAsync(ws.h_out, result, out_elems * 4, cudaMemcpyDeviceToHost, st), "result readback");
+        CK(cudaStreamSynchronize(st), "synchronize");
+        memcpy(host_out, ws.h_out, out_elems * 4);
+    }
+#undef CK
+    if (*ws.h_err) {
+        const int code = *ws.h_err;
+        cudaMemset(d.err, 0, sizeof(int));
+        return report(code, "GPU execution failed: a device-side wait timed out");
+    }
+    return GE_OK;
+}
+
+}  // namespace ge

@@ -1,0 +1,112 @@
+// model.hpp -- the loaded model: configuration, per-device weights and workspaces, and the
+// forward pass that replaces MetalForward (Sources/GemmaEmbed/Metal/MetalForward.swift).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "gemma_embed.h"
+#include "gguf.hpp"
+#include "kernels.hpp"
+
+namespace ge {
+
+// LayerConfig (Sources/GemmaEmbed/Model/ModelConfig.swift:31-37).
+struct LayerCfg {
+    bool sliding = false;
+    int kv = 0, hd = 0;
+    float rope_base = 0.f;
+    int rope_index = 0;  // which RoPE table (one per distinct head dim and base)
+};
+
+// ModelConfig (ModelConfig.swift:40-112) for the two supported architectures.
+struct Config {
+    std::string arch, name, quant;
+    int hidden = 0, layers = 0, heads = 0, ff = 0, per_layer = 0, out_dim = 0, dense_head = 0, vocab = 0;
+    int sliding_window = 0, max_tokens = 8192;
+    float eps = 1e-6f, emb_scale = 1.f, pl_scale = 1.f;
+    int bos_id = 2, eos_id = 1;
+    bool has_ple = false, has_output = false, has_dense = false;
+    std::vector<LayerCfg> layer;
+    std::vector<std::pair<int, float>> ropes;  // (head dim, base) per RoPE table
+    int max_q() const;
+    int max_kv() const;
+};
+
+struct LayerDev {
+    DevWeight qkv, o, gu, down, inp_gate, proj;
+    float *attn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *post_attn = nullptr, *ffn_norm = nullptr,
+          *post_ffw = nullptr, *post_norm = nullptr;
+    float out_scale = 1.f;
+};
+
+struct Workspace {
+    int cap_rows = 0, cap_seqs = 0, cap_work = 0;
+    int32_t *tokens = nullptr, *positions = nullptr;
+    uint32_t *seqs = nullptr, *work = nullptr;
+    float *x = nullptr, *qkv = nullptr, *o = nullptr, *y = nullptr, *ple = nullptr;
+    float *pooled = nullptr, *mid = nullptr, *out = nullptr;
+    __half *h = nullptr, *x16 = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *act = nullptr,
+           *g = nullptr;
+    // GEMM A-operand views (buffer, column count) with their TMA descriptors.
+    DevActivation a_h, a_x16, a_act, a_g;
+    std::vector<DevActivation> a_attn;  // one per distinct query width
+    // Pinned host staging.
+    int32_t *h_tokens = nullptr, *h_positions = nullptr;
+    uint32_t *h_seqs = nullptr, *h_work = nullptr;
+    float* h_out = nullptr;
+    int* h_err = nullptr;
+};
+
+struct Device {
+    int ordinal = 0, num_sms = 148;
+    std::string name;
+    cudaStream_t stream = nullptr;
+    int8_t* emb_q = nullptr;
+    __half* emb_s = nullptr;
+    std::vector<LayerDev> layers;
+    DevWeight plp;  // per_layer_model_proj (fp16 only)
+    float *pl_norm = nullptr, *out_norm = nullptr;
+    float *dense2 = nullptr, *dense3 = nullptr, *output = nullptr;  // fp32 [N][K]
+    std::vector<float*> rope;
+    int* err = nullptr;
+    Workspace ws;
+    std::vector<void*> allocations;
+};
+
+}  // namespace ge
+
+struct ge_model {
+    ge::Config cfg;
+    ge::GgufFile file;
+    std::vector<ge::Device> devs;
+    std::mutex mu;
+    std::string last_error;
+    int budget = 8192;
+    uint32_t flags = 0;
+    int64_t file_size = 0;
+};
+
+namespace ge {
+// One forward over a packed batch on one device (the body of MetalForward.execute/encode).
+// tokens/positions/out are host pointers unless the *_dev flags say otherwise.
+struct ForwardArgs {
+    const int32_t* tokens = nullptr;
+    bool tokens_on_device = false;
+    const int32_t* positions = nullptr;  // host; nullptr derives 0..len-1 per sequence
+    int ntok = 0;
+    const ge_seq* seqs = nullptr;  // host
+    int nseq = 0;
+    float* out = nullptr;
+    bool out_on_device = false;
+    cudaStream_t stream = nullptr;  // stream for device-resident calls; nullptr uses the device's own
+    int trace_layer = -2;           // >= -1: copy that layer's hidden state into trace_out instead
+    float* trace_out = nullptr;
+    std::string* error = nullptr;   // where failures are reported; nullptr: the model's last_error
+};
+int run_forward(ge_model* m, Device& d, const ForwardArgs& a);
+int set_error(ge_model* m, int code, const std::string& msg);
+}  // namespace ge

@@ -1,0 +1,191 @@
+// testing.cpp -- kernel-level entry points for parity tests (include/gemma_embed_testing.h).
+#include <string.h>
+
+#include <string>
+#include <vector>
+
+#include "gemma_embed_testing.h"
+#include "kernels.hpp"
+
+namespace {
+
+thread_local std::string t_err;
+
+struct DevBuf {
+    void* p = nullptr;
+    ~DevBuf() {
+        if (p) cudaFree(p);
+    }
+    cudaError_t alloc(size_t bytes) { return cudaMalloc(&p, bytes ? bytes : 1); }
+};
+
+int fail(int code, const std::string& msg) {
+    t_err = msg;
+    return code;
+}
+
+#define TRY(expr)                                                                                    \
+    do {                                                                                             \
+        cudaError_t e_ = (expr);                                                                     \
+        if (e_ != cudaSuccess) return fail(GE_ERR_GPU_FAILURE, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+uint16_t f2h(float f) {
+    __half h = __float2half_rn(f);
+    return __half_raw(h).x;
+}
+float h2f(uint16_t b) {
+    __half_raw r;
+    r.x = b;
+    return __half2float(__half(r));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ge_test_last_error(void) { return t_err.c_str(); }
+
+int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int32_t n, int32_t epilogue, int32_t use_q8,
+                 const float* aux, float* out) {
+    if (m <= 0 || k <= 0 || n <= 0 || k % 64 || n % 256 || !a || !w || !out || epilogue < 0 || epilogue > 3 ||
+        (epilogue == 3 && !aux))
+        return fail(GE_ERR_INVALID_OPTIONS, "invalid options: shapes must be k % 64 == 0 and n % 256 == 0");
+    const int rows = (m + ge::kRowTile - 1) / ge::kRowTile * ge::kRowTile;
+    // Host repack of the Q8_0 rows into the device planes the loader builds.
+    std::vector<int8_t> q(size_t(n) * k);
+    std::vector<uint16_t> st(size_t(n) * (k / 32)), f16(size_t(n) * k);
+    for (int r = 0; r < n; r++)
+        for (int b = 0; b < k / 32; b++) {
+            const uint8_t* blk = w + (size_t(r) * (k / 32) + b) * 34;
+            uint16_t s;
+            memcpy(&s, blk, 2);
+            st[size_t(b) * n + r] = s;
+            for (int j = 0; j < 32; j++) {
+                const int8_t v = int8_t(blk[2 + j]);
+                q[size_t(r) * k + b * 32 + j] = v;
+                f16[size_t(r) * k + b * 32 + j] = f2h(h2f(s) * float(v));
+            }
+        }
+    int dev = 0, sms = 0;
+    TRY(cudaGetDevice(&dev));
+    TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    DevBuf da, dq, ds, dh, dout, daux, derr;
+    const int out_cols = epilogue == 2 ? n / 2 : n;
+    const size_t out_elem = epilogue == 0 ? 4 : 2;
+    TRY(da.alloc(size_t(rows) * k * 2));
+    TRY(cudaMemset(da.p, 0, size_t(rows) * k * 2));
+    TRY(cudaMemcpy(da.p, a, size_t(m) * k * 2, cudaMemcpyHostToDevice));
+    TRY(dq.alloc(q.size()));
+    TRY(cudaMemcpy(dq.p, q.data(), q.size(), cudaMemcpyHostToDevice));
+    TRY(ds.alloc(st.size() * 2));
+    TRY(cudaMemcpy(ds.p, st.data(), st.size() * 2, cudaMemcpyHostToDevice));
+    TRY(dh.alloc(f16.size() * 2));
+    TRY(cudaMemcpy(dh.p, f16.data(), f16.size() * 2, cudaMemcpyHostToDevice));
+    TRY(dout.alloc(size_t(rows) * out_cols * out_elem));
+    TRY(derr.alloc(sizeof(int)));
+    TRY(cudaMemset(derr.p, 0, sizeof(int)));
+    if (epilogue == 3) {
+        TRY(daux.alloc(size_t(rows) * n * 4));
+        TRY(cudaMemset(daux.p, 0, size_t(rows) * n * 4));
+        TRY(cudaMemcpy(daux.p, aux, size_t(m) * n * 4, cudaMemcpyHostToDevice));
+    }
+    ge::DevWeight W;
+    W.N = n;
+    W.K = k;
+    W.q8 = static_cast<int8_t*>(dq.p);
+    W.scales_t = static_cast<__half*>(ds.p);
+    W.f16 = static_cast<__half*>(dh.p);
+    ge::DevActivation A;
+    A.ptr = static_cast<__half*>(da.p);
+    A.rows = rows;
+    A.cols = k;
+    if (!ge::encode_weight_maps(W, 256) || !ge::encode_activation_map(A))
+        return fail(GE_ERR_GPU_FAILURE, "tensor map encoding failed");
+    ge::GemmLaunch g;
+    g.a = &A;
+    g.w = &W;
+    g.m_rows = rows;
+    g.out = dout.p;
+    g.ldo = out_cols;
+    g.epilogue = epilogue;
+    g.aux = static_cast<const float*>(daux.p);
+    g.ldaux = n;
+    g.use_q8 = use_q8 != 0;
+    g.err = static_cast<int*>(derr.p);
+    g.num_sms = sms;
+    TRY(ge::launch_gemm(g, nullptr));
+    TRY(cudaDeviceSynchronize());
+    int herr = 0;
+    TRY(cudaMemcpy(&herr, derr.p, sizeof(int), cudaMemcpyDeviceToHost));
+    if (herr) return fail(herr, "GPU execution failed: a device-side wait timed out");
+    if (out_elem == 4) {
+        TRY(cudaMemcpy(out, dout.p, size_t(m) * out_cols * 4, cudaMemcpyDeviceToHost));
+    } else {
+        std::vector<uint16_t> h(size_t(m) * out_cols);
+        TRY(cudaMemcpy(h.data(), dout.p, h.size() * 2, cudaMemcpyDeviceToHost));
+        for (size_t i = 0; i < h.size(); i++) out[i] = h2f(h[i]);
+    }
+    return GE_OK;
+}
+
+int ge_test_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, int32_t ntok, const ge_seq* seqs,
+                      int32_t nseq, int32_t heads, int32_t kvh, int32_t hd, int32_t half_window, uint16_t* out) {
+    if (ntok <= 0 || nseq <= 0 || !q || !k || !v || !seqs || !out || heads <= 0 || kvh <= 0 || heads % kvh ||
+        (hd != 256 && hd != 512) || half_window < 0)
+        return fail(GE_ERR_INVALID_OPTIONS, "invalid options");
+    uint64_t next = 0;
+    for (int s = 0; s < nseq; s++) {
+        if (seqs[s].start != next || seqs[s].length == 0) return fail(GE_ERR_INVALID_OPTIONS, "sequences must tile the batch");
+        next += seqs[s].length;
+    }
+    if (next != uint64_t(ntok)) return fail(GE_ERR_INVALID_OPTIONS, "lengths do not sum to ntok");
+    const int rows = (ntok + ge::kRowTile - 1) / ge::kRowTile * ge::kRowTile;
+    const int qpi = ge::attention_queries_per_item(hd);
+    std::vector<uint32_t> work;
+    for (int s = 0; s < nseq; s++)
+        for (uint32_t q0 = 0; q0 < seqs[s].length; q0 += uint32_t(qpi)) {
+            work.push_back(seqs[s].start);
+            work.push_back(seqs[s].length);
+            work.push_back(q0);
+        }
+    DevBuf dq, dk, dv, dout, dwork, derr;
+    const size_t qn = size_t(rows) * heads * hd, kn = size_t(rows) * kvh * hd;
+    TRY(dq.alloc(qn * 2));
+    TRY(dk.alloc(kn * 2));
+    TRY(dv.alloc(kn * 2));
+    TRY(dout.alloc(qn * 2));
+    TRY(cudaMemset(dq.p, 0, qn * 2));
+    TRY(cudaMemset(dk.p, 0, kn * 2));
+    TRY(cudaMemset(dv.p, 0, kn * 2));
+    TRY(cudaMemset(dout.p, 0xFF, qn * 2));  // NaN fill: every row of every sequence must be written
+    TRY(cudaMemcpy(dq.p, q, size_t(ntok) * heads * hd * 2, cudaMemcpyHostToDevice));
+    TRY(cudaMemcpy(dk.p, k, size_t(ntok) * kvh * hd * 2, cudaMemcpyHostToDevice));
+    TRY(cudaMemcpy(dv.p, v, size_t(ntok) * kvh * hd * 2, cudaMemcpyHostToDevice));
+    TRY(dwork.alloc(work.size() * 4));
+    TRY(cudaMemcpy(dwork.p, work.data(), work.size() * 4, cudaMemcpyHostToDevice));
+    TRY(derr.alloc(sizeof(int)));
+    TRY(cudaMemset(derr.p, 0, sizeof(int)));
+    ge::AttnLaunch al;
+    al.q = static_cast<const __half*>(dq.p);
+    al.k = static_cast<const __half*>(dk.p);
+    al.v = static_cast<const __half*>(dv.p);
+    al.out = static_cast<__half*>(dout.p);
+    al.work = static_cast<const uint32_t*>(dwork.p);
+    al.work_items = int(work.size() / 3);
+    al.heads = heads;
+    al.kv_heads = kvh;
+    al.hd = hd;
+    al.half_window = half_window;
+    al.queries_per_item = qpi;
+    al.err = static_cast<int*>(derr.p);
+    TRY(ge::launch_attention(al, nullptr));
+    TRY(cudaDeviceSynchronize());
+    int herr = 0;
+    TRY(cudaMemcpy(&herr, derr.p, sizeof(int), cudaMemcpyDeviceToHost));
+    if (herr) return fail(herr, "GPU execution failed: a device-side wait timed out");
+    TRY(cudaMemcpy(out, dout.p, size_t(ntok) * heads * hd * 2, cudaMemcpyDeviceToHost));
+    return GE_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,160 @@
+/*
+ * gemma_embed.h -- C ABI of the B200 EmbeddingGemma text-encoder forward.
+ *
+ * This library replaces the reference's Metal forward (`MetalForward.run`,
+ * Sources/GemmaEmbed/Metal/MetalForward.swift:199-204) behind its
+ * `EmbeddingModel.load / embed / EmbedOptions` API
+ * (Sources/GemmaEmbed/EmbeddingModel.swift:40-289, EmbedOptions.swift:34-56,
+ * 171-203).  Every entry point takes plain pointers and sizes; the caller
+ * owns every host array and nothing is retained after a call returns.  Calls
+ * on one model handle are serialised internally (the reference's single GPU
+ * queue, EmbeddingModel.swift:37, 269-281).  Every call returns a status code
+ * (0 = success) and never aborts; `ge_last_error` gives the message.
+ */
+#ifndef GEMMA_EMBED_H
+#define GEMMA_EMBED_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GE_API __attribute__((visibility("default")))
+
+/* Status codes, one per GemmaEmbedError case that a text forward can raise
+ * (Sources/GemmaEmbed/Errors.swift:6-23). */
+typedef enum ge_status {
+    GE_OK = 0,
+    GE_ERR_FILE_NOT_READABLE = 1,      /* .fileNotReadable */
+    GE_ERR_INVALID_GGUF = 2,           /* .invalidGGUF */
+    GE_ERR_UNSUPPORTED_TENSOR_TYPE = 3,/* .unsupportedTensorType */
+    GE_ERR_UNSUPPORTED_ARCHITECTURE = 4,/* .unsupportedArchitecture */
+    GE_ERR_MISSING_TENSOR = 5,         /* .missingTensor */
+    GE_ERR_MISSING_METADATA = 6,       /* .missingMetadata */
+    GE_ERR_SHAPE_MISMATCH = 7,         /* .tensorShapeMismatch */
+    GE_ERR_NO_DEVICE = 8,              /* .noMetalDevice: no usable sm_100 device */
+    GE_ERR_INVALID_OPTIONS = 9,        /* .invalidOptions (also bad ids, sizes, positions) */
+    GE_ERR_GPU_FAILURE = 10,           /* .gpuFailure */
+    GE_ERR_OUT_OF_MEMORY = 11,         /* workspace growth failed (a .gpuFailure in the reference) */
+    GE_ERR_TIMEOUT = 12,               /* a bounded device-side wait gave up (a .gpuFailure in the reference) */
+    GE_ERR_CANCELLED = 13              /* .cancelled */
+} ge_status;
+
+typedef struct ge_model ge_model;
+
+/* SequenceRange (MetalForward.swift:8-21): rows [start, start + length) of a packed batch. */
+typedef struct ge_seq {
+    uint32_t start;
+    uint32_t length;
+} ge_seq;
+
+/* LoadOptions (EmbedOptions.swift:171-203), the fields a text forward uses. */
+typedef struct ge_load_opts {
+    uint32_t device_mask;       /* bit i selects CUDA device i; 0 selects device 0 */
+    int32_t batch_token_budget; /* LoadOptions.batchTokenBudget; default 8192, at least 64 */
+    uint32_t flags;             /* GE_LOAD_* bits */
+} ge_load_opts;
+
+#define GE_LOAD_NO_GRAPHS 1u      /* launch kernels directly instead of replaying captured CUDA graphs */
+#define GE_LOAD_Q8_ONLY 2u        /* keep only the Q8_0 planes resident; every GEMM dequantises in shared memory */
+
+/* EmbedOptions (EmbedOptions.swift:34-56) minus the task prefix, which the tokenizer applies. */
+typedef struct ge_embed_opts {
+    int32_t max_tokens; /* default 2048; 2 .. ge_info.max_tokens */
+    int32_t dimensions; /* 768, 512, 256 or 128 (Matryoshka prefix) */
+    int32_t normalise;  /* L2-normalise the prefix */
+    int32_t batch_size; /* texts per batch; 0 packs by the token budget */
+} ge_embed_opts;
+
+/* ModelInfo (ModelConfig.swift:5-27) plus the devices in use. */
+typedef struct ge_info {
+    char architecture[64];
+    char name[128];
+    int32_t layer_count;
+    int32_t hidden_size;
+    int32_t output_dimensions;
+    int32_t feed_forward_size;
+    int32_t per_layer_input_size;
+    int32_t head_count;
+    int32_t vocabulary_size;
+    int32_t sliding_window;
+    int32_t max_tokens;
+    float norm_epsilon;
+    char quantization[16];
+    int64_t file_size;
+    int32_t device_count;
+    int32_t eos_id;
+    int32_t bos_id;
+    char device_name[128];
+} ge_info;
+
+/* Progress after every batch (EmbeddingProgress, EmbedOptions.swift:155-160). Returning
+ * nonzero cancels the call between batches, which then returns GE_ERR_CANCELLED
+ * (the reference's Task.checkCancellation, EmbeddingModel.swift:162). */
+typedef int (*ge_progress_fn)(int32_t completed_texts, int32_t total_texts, int64_t completed_tokens, void* user);
+
+GE_API void ge_load_opts_default(ge_load_opts* opts);
+GE_API void ge_embed_opts_default(ge_embed_opts* opts);
+
+/* EmbeddingModel.load(from:options:) (EmbeddingModel.swift:40-122): parse and validate the
+ * GGUF, repack its Q8_0 weights into the device layout and upload them to every selected
+ * GPU, then run one warm-up forward.  On failure *out is NULL and ge_last_error(NULL) holds
+ * the message. */
+GE_API int ge_load(const char* gguf_path, const ge_load_opts* opts, ge_model** out);
+
+/* Releases every device and host resource of the model. NULL is ignored. */
+GE_API void ge_free(ge_model* model);
+
+/* Message of the last failed call on `model`, or of the calling thread's last failed
+ * ge_load when `model` is NULL.  Valid until the next call on the same handle. */
+GE_API const char* ge_last_error(const ge_model* model);
+
+GE_API int ge_info_get(const ge_model* model, ge_info* info);
+
+/* MetalForward.run(_:) (MetalForward.swift:199-204) over one PackedBatch: `ntok` token ids
+ * packed back to back, their positions, and `nseq` sequence ranges that tile [0, ntok) in
+ * order.  Writes the pooled, unnormalised vectors, `nseq` rows of output_dimensions floats,
+ * row i for sequence i.  With several devices the sequences are sharded across them and
+ * gathered into `pooled_out` at their original rows. */
+GE_API int ge_forward_packed(ge_model* model, const int32_t* tokens, const int32_t* positions, int32_t ntok,
+                             const ge_seq* seqs, int32_t nseq, float* pooled_out);
+
+/* The same forward over device-resident token ids on one device of the model: `d_tokens`
+ * (ntok int32) and `d_pooled` (nseq * output_dimensions float) are device pointers on
+ * device `device_ordinal`; `seqs` is a host array; positions are 0..length-1 per sequence.
+ * Work is enqueued on `stream` (a cudaStream_t, NULL for the default stream) and the call
+ * returns without synchronising. */
+GE_API int ge_forward_device(ge_model* model, int32_t device_ordinal, const int32_t* d_tokens, int32_t ntok,
+                             const ge_seq* seqs, int32_t nseq, float* d_pooled, void* stream);
+
+/* Per-layer hidden state for parity checks (the `trace` names of CPUReference.forward,
+ * CPUReference.swift:204-276): runs one sequence of `ntok` tokens and copies the fp32
+ * residual stream after layer `layer` ("l_out-<layer>") into `hidden_out` (ntok * hidden
+ * floats).  layer == -1 copies rmsnorm(x, output_norm) ("result_norm"). */
+GE_API int ge_forward_trace(ge_model* model, const int32_t* tokens, int32_t ntok, int32_t layer, float* hidden_out);
+
+/* EmbeddingModel.embed over pre-tokenised texts (EmbeddingModel.swift:145-175 without the
+ * tokenizer): truncation to max_tokens keeping EOS (189-196), batching by count or token
+ * budget (200-215), one forward per batch, then the Matryoshka prefix and L2 (260-267).
+ * `out` receives count * dimensions floats; `token_counts` and `truncated` (count entries
+ * each, may be NULL) receive Embedding.tokenCount and Embedding.truncated. */
+GE_API int ge_embed_tokens(ge_model* model, const int32_t* const* texts, const int32_t* lengths, int32_t count,
+                           const ge_embed_opts* opts, float* out, int32_t* token_counts, int32_t* truncated,
+                           ge_progress_fn progress, void* user);
+
+/* EmbeddingModel.batches (EmbeddingModel.swift:200-215): splits `n` items with `ncost` costs
+ * each (row-major costs[n][ncost]) into consecutive ranges, by count when batch_size > 0,
+ * otherwise before the item that would take any summed cost past its budget.  Writes
+ * (start, end) pairs to ranges_out (room for 2 * n) and the range count to *count_out. */
+GE_API int ge_batches(const int64_t* costs, int32_t n, int32_t ncost, int32_t batch_size, const int64_t* budgets,
+                      int32_t* ranges_out, int32_t* count_out);
+
+/* EmbeddingModel.finish (EmbeddingModel.swift:260-267): the first `dims` values of `v`,
+ * L2-normalised when `normalise` is nonzero and the norm is positive. */
+GE_API int ge_finish(const float* v, int32_t n, int32_t dims, int32_t normalise, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,41 @@
+/*
+ * gemma_embed_testing.h -- kernel-level entry points of libgemma_embed_cuda.so for parity
+ * tests, mirroring how the reference's KernelTests drive single kernels through its
+ * `Kernels` encoders (Tests/GemmaEmbedTests/KernelTests.swift:89-104).  Each call allocates
+ * its own device buffers, runs one kernel on the current CUDA device and copies the result
+ * back; they are not for production use.
+ */
+#ifndef GEMMA_EMBED_TESTING_H
+#define GEMMA_EMBED_TESTING_H
+
+#include <stdint.h>
+
+#include "gemma_embed.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Kernels.gemm (Metal/MetalForward.swift:513-557): out = a * W^T for a fp16 `a` [m][k]
+ * (bit patterns) and a Q8_0 weight given as GGUF rows `w_q8_0` [n][k/32 * 34 bytes].
+ * epilogue: 0 fp32 store, 1 fp16 store, 2 GeGLU over rows interleaved as the loader does
+ * (out has n/2 columns), 3 gelu(acc) * aux (aux fp32 [m][n]).  use_q8 selects the
+ * in-shared-memory dequantisation path instead of the fp16-resident weights.  Results are
+ * returned as fp32 [m][n] (or [m][n/2]). */
+GE_API int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w_q8_0, int32_t n, int32_t epilogue,
+                        int32_t use_q8, const float* aux, float* out);
+
+/* Kernels.attention (Metal/MetalForward.swift:669-694): q [ntok][heads][hd], k and v
+ * [ntok][kv_heads][hd] as fp16 bit patterns, sequences tiling [0, ntok); out receives fp16
+ * bit patterns [ntok][heads][hd].  half_window 0 is global attention. */
+GE_API int ge_test_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, int32_t ntok, const ge_seq* seqs,
+                             int32_t nseq, int32_t heads, int32_t kv_heads, int32_t hd, int32_t half_window,
+                             uint16_t* out);
+
+/* Message of the calling thread's last failed ge_test_* call. */
+GE_API const char* ge_test_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

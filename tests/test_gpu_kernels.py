@@ -1,0 +1,150 @@
+"""Kernel parity on the GPU through the C ABI (include/gemma_embed_testing.h), mirroring the
+reference's KernelTests (Tests/GemmaEmbedTests/KernelTests.swift): every model GEMM shape, the
+fused epilogues, Q8-in-shared-memory vs fp16-resident weights bit for bit, and attention over
+packed sequences with no cross-sequence leakage."""
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+# Kernel tolerance: max |got - want| / max |want| (TestSupport.maxRelDiff). The reference
+# asserts 1e-4 for fp32 GEMM outputs (KernelTests.swift:105-110); fp32 outputs here meet the
+# same bound; fp16 outputs add one fp16 rounding (2^-11 relative).
+TOL_F32 = 1e-4
+TOL_F16 = 2e-3
+
+
+def max_rel(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    assert not np.isnan(got).any()
+    return float(np.abs(got - want).max() / max(np.abs(want).max(), 1e-30))
+
+
+def gemm(ge, a16, wq, n, epi, use_q8, aux=None):
+    from importlib import import_module
+    L = import_module("gemma-embed-swift_b200._lib").lib()
+    m, k = a16.shape
+    cols = n // 2 if epi == 2 else n
+    out = np.zeros((m, cols), np.float32)
+    a = np.ascontiguousarray(a16.view(np.uint16))
+    w = np.ascontiguousarray(wq)
+    auxp = None
+    if aux is not None:
+        aux = np.ascontiguousarray(aux, np.float32)
+        auxp = aux.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    rc = L.ge_test_gemm(a.ctypes.data_as(ctypes.POINTER(ctypes.c_uint16)), m, k,
+                        w.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), n, epi, int(use_q8), auxp,
+                        out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    assert rc == 0, L.ge_test_last_error()
+    return out
+
+
+def make_case(synth, m, k, n, seed):
+    rng = np.random.default_rng(seed)
+    a = rng.uniform(-1, 1, size=(m, k)).astype(np.float16)
+    w = synth.floats(seed, n * k, (3.0 / k) ** 0.5).reshape(n, k)
+    wq = synth.quantize_q8_0(w)
+    wd = synth.dequantize_q8_0(wq, k).astype(np.float16).astype(np.float64)  # the fp16 operand
+    return a, wq, wd
+
+
+SHAPES = [(768, 1280), (768, 768), (768, 2304), (1152, 768),      # gemma-embedding: qkv, o, gate|up, down
+          (512, 2048), (512, 3072), (1024, 512), (512, 4096), (2048, 512), (512, 512)]  # gemma-embedding2
+
+
+@pytest.mark.parametrize("k,n", SHAPES)
+@pytest.mark.parametrize("m", [128, 200, 1000])
+def test_gemm_shapes_fp32(ge, synth, cuda_device, m, k, n):
+    a, wq, wd = make_case(synth, m, k, n, seed=k + n + m)
+    want = a.astype(np.float64) @ wd.T
+    got16 = gemm(ge, a, wq, n, 0, use_q8=False)
+    got8 = gemm(ge, a, wq, n, 0, use_q8=True)
+    assert max_rel(got16, want) < TOL_F32
+    # The Q8 path dequantises in shared memory to the very same fp16 operand: identical bits.
+    assert got8.tobytes() == got16.tobytes()
+
+
+@pytest.mark.parametrize("use_q8", [False, True])
+def test_gemm_epilogues(ge, synth, oracle, cuda_device, use_q8):
+    m, k, ff = 300, 768, 1152
+    a, wq_gate, wd_gate = make_case(synth, m, k, ff, seed=11)
+    _, wq_up, wd_up = make_case(synth, m, k, ff, seed=12)
+    a64 = a.astype(np.float64)
+    # fp16 store
+    n = 1280
+    _, wq, wd = make_case(synth, m, k, n, seed=13)
+    got = gemm(ge, a, wq, n, 1, use_q8)
+    assert max_rel(got, a64 @ wd.T) < TOL_F16
+    # GeGLU over rows interleaved in blocks of 128 (gate block j, up block j, ...)
+    rows = []
+    for j in range(ff // 128):
+        rows.append(wq_gate[j * 128:(j + 1) * 128])
+        rows.append(wq_up[j * 128:(j + 1) * 128])
+    wq_gu = np.concatenate(rows)
+    gate = a64 @ wd_gate.T
+    up = a64 @ wd_up.T
+    gelu = np.vectorize(oracle.gelu_tanh)
+    want = gelu(gate.astype(np.float32)).astype(np.float64) * up
+    got = gemm(ge, a, wq_gu, 2 * ff, 2, use_q8)
+    assert got.shape == (m, ff)
+    assert max_rel(got, want) < TOL_F16
+    # gelu(acc) * aux
+    aux = np.random.default_rng(5).normal(size=(m, ff)).astype(np.float32)
+    got = gemm(ge, a, wq_gate[:1024], 1024, 3, use_q8, aux=aux[:, :1024])
+    want = gelu(gate[:, :1024].astype(np.float32)).astype(np.float64) * aux[:, :1024]
+    assert max_rel(got, want) < TOL_F16
+
+
+def test_gemm_rows_are_independent_of_the_batch(ge, synth, cuda_device):
+    """A row's result does not depend on the other rows of the batch or the tile it lands in
+    (KernelTests.swift:323-339, MetalForwardTests.swift:75-97)."""
+    k, n = 768, 2304
+    a, wq, _ = make_case(synth, 700, k, n, seed=21)
+    full = gemm(ge, a, wq, n, 0, use_q8=False)
+    for lo, hi in [(0, 1), (5, 133), (128, 256), (699, 700)]:
+        part = gemm(ge, np.ascontiguousarray(a[lo:hi]), wq, n, 0, use_q8=(hi - lo) < 64)
+        assert part.tobytes() == full[lo:hi].tobytes()
+
+
+def attention(ge, q, k, v, lens, heads, kvh, hd, hw):
+    from importlib import import_module
+    lib_mod = import_module("gemma-embed-swift_b200._lib")
+    L = lib_mod.lib()
+    ntok = sum(lens)
+    starts = np.concatenate([[0], np.cumsum(lens)[:-1]])
+    seqs = (lib_mod.GeSeq * len(lens))(*[lib_mod.GeSeq(int(s), int(n)) for s, n in zip(starts, lens)])
+    out = np.zeros((ntok, heads, hd), np.float16)
+    args = [np.ascontiguousarray(x).view(np.uint16) for x in (q, k, v)]
+    rc = L.ge_test_attention(*[x.ctypes.data_as(ctypes.POINTER(ctypes.c_uint16)) for x in args], ntok, seqs,
+                             len(lens), heads, kvh, hd, hw, out.view(np.uint16).ctypes.data_as(ctypes.POINTER(ctypes.c_uint16)))
+    assert rc == 0, L.ge_test_last_error()
+    return out.astype(np.float32)
+
+
+CONFIGS = [(3, 1, 256, 512), (3, 1, 256, 0), (4, 2, 256, 512), (4, 1, 512, 0), (4, 1, 512, 512)]
+LENGTHS = [[1, 7, 64], [1024, 5], [2048], [2048, 3, 1024, 7]]
+
+
+@pytest.mark.parametrize("heads,kvh,hd,hw", CONFIGS)
+@pytest.mark.parametrize("lens", LENGTHS)
+def test_attention_packed_sequences(ge, oracle, cuda_device, heads, kvh, hd, hw, lens):
+    """Packed attention equals per-sequence CPU attention, with no leakage across sequence
+    boundaries, for global and sliding-window layers (KernelTests.swift:552-656)."""
+    rng = np.random.default_rng(hd + hw + len(lens))
+    ntok = sum(lens)
+    scale = 1 / np.sqrt(hd)
+    q = rng.uniform(-2 * scale, 2 * scale, size=(ntok, heads, hd)).astype(np.float16)
+    k = rng.uniform(-2 * scale, 2 * scale, size=(ntok, kvh, hd)).astype(np.float16)
+    v = rng.uniform(-1, 1, size=(ntok, kvh, hd)).astype(np.float16)
+    got = attention(ge, q, k, v, lens, heads, kvh, hd, hw)
+    s = 0
+    for n in lens:
+        want = oracle.attention(q[s:s + n].astype(np.float32), k[s:s + n].astype(np.float32),
+                                v[s:s + n].astype(np.float32), n, heads, kvh, hd, window=2 * hw).reshape(n, heads, hd)
+        g = got[s:s + n]
+        assert not np.isnan(g).any()
+        assert max_rel(g, want) < TOL_F16, (n, heads, kvh, hd, hw)
+        s += n
