@@ -1,0 +1,306 @@
+"""Benchmark of the EmbeddingGemma text-encoder forward on B200 GPUs.
+
+Metric: embedded tokens/s at BASELINE config 2 -- 64 texts with lengths
+uniform in 32..512 packed by token count (about 17.4k tokens), random-init seed-0 Q8_0
+weights of the 24-layer hidden-768 encoder -- on N GPUs, one process per GPU.  Each rank
+embeds its own seeded 64-text batch per step (weak scaling: the sequences of a batch are
+independent, so the data-parallel shard has no collective).  A token is an input token
+including BOS/EOS (Embedding.tokenCount).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`value` times K device-resident forwards (ids already in HBM) with CUDA events, max over
+ranks.  `e2e` times the same K steps through the public C ABI call with host buffers
+(ge_forward_packed: host->device ids and positions, device->host pooled vectors inside the
+timed region).  `--impl reference` times the CPU oracle (the restated CPUReference.forward,
+the only runnable form of the reference's path here) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import importlib
+import io
+import json
+import os
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+PKG = "gemma-embed-swift_b200"
+
+
+def args_():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=30)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--config", type=int, default=2)
+    p.add_argument("--arch", default="gemma-embedding")
+    p.add_argument("--profile-reps", type=int, default=5)
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="bound of the CPU-baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            m = json.load(f)
+        return {"hbm_gbs": m["hbm_gbs"], "bf16_tflops": m["bf16_tflops"],
+                "bf16_tflops_sustained": m["bf16_tflops_sustained"], "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    FIELDS = ["index", "clocks.sm", "clocks.max.sm", "power.draw", "clocks_event_reasons.active",
+              "clocks_event_reasons.hw_slowdown", "clocks_event_reasons.hw_thermal_slowdown",
+              "clocks_event_reasons.sw_thermal_slowdown", "clocks_event_reasons.sw_power_cap"]
+
+    def __init__(self, gpu_index: int):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(gpu_index), "--query-gpu=" + ",".join(self.FIELDS), "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        rows = [r for r in csv.reader(io.StringIO(out)) if len(r) == len(self.FIELDS)]
+        sm = sorted(float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit())
+        mx = max((float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()), default=None)
+        reasons = set()
+        for r in rows:
+            for name, val in zip(["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"], r[5:9]):
+                if val.strip() == "Active":
+                    reasons.add(name)
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(rows)}
+
+
+def cpu_baseline(path, seqs, seconds):
+    """The CPU oracle on a bounded prefix of the same batch, all host threads."""
+    from oracle import binding
+    m = binding.OracleModel(path)
+    m.forward(seqs[0][:8])  # dequantises and caches every weight matrix outside the timing
+    tokens = 0
+    done = 0
+    t0 = time.perf_counter()
+    for s in seqs:
+        m.forward(s)
+        tokens += len(s)
+        done += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    dt = time.perf_counter() - t0
+    cores = binding.threads()
+    m.close()
+    return {"value": tokens / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"first {done} of {len(seqs)} texts of the same batch ({tokens} tokens), one pass, {dt:.1f} s"}
+
+
+def run_reference(a, rank, world):
+    """--impl reference: the reference's CPU path (its restated CPUReference) on the host cores."""
+    if rank != 0:
+        return 0
+    synth = importlib.import_module(PKG + ".synthetic")
+    from oracle import binding
+    path = synth.model_path(a.arch, seed=0)
+    seqs = synth.config_sequences(a.config, seed=0)
+    m = binding.OracleModel(path)
+    m.forward(seqs[0][:8])
+    # One step = one text of the batch, in order, cycling: a bounded sample of the workload.
+    order = list(range(len(seqs)))
+    for i in range(a.warmup):
+        m.forward(seqs[order[i % len(order)]])
+    tokens = 0
+    t0 = time.perf_counter()
+    for i in range(a.steps):
+        s = seqs[order[(a.warmup + i) % len(order)]]
+        m.forward(s)
+        tokens += len(s)
+    dt = time.perf_counter() - t0
+    value = tokens / dt
+    cores = binding.threads()
+    line = {"impl": "reference", "metric": "embedded tokens/sec (config 2: 64 texts x 32..512 tokens)", "value": value,
+            "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": dt * 1000 / a.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"config {a.config}", "arch": a.arch, "step": "one text of the seeded batch"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": f"{a.steps} texts of the config-{a.config} batch ({tokens} tokens)"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    m.close()
+    return 0
+
+
+def main():
+    a = args_()
+    rank, world, local = dist_env()
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group(backend="nccl" if a.impl == "ours" else "gloo",
+                                timeout=datetime.timedelta(seconds=300))
+    if a.impl == "reference":
+        rc = run_reference(a, rank, world)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return rc
+
+    import numpy as np
+    import torch
+
+    ge = importlib.import_module(PKG)
+    synth = importlib.import_module(PKG + ".synthetic")
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    # Rank 0 writes the synthetic GGUF first; the others then read the cached file.
+    if rank == 0:
+        path = synth.model_path(a.arch, seed=0)
+    barrier()
+    if rank != 0:
+        path = synth.model_path(a.arch, seed=0)
+    model = ge.EmbeddingModel.load(path, ge.LoadOptions(devices=(local,)))
+    seqs = synth.config_sequences(a.config, seed=rank)
+    tokens, positions, ranges = ge.pack(seqs)
+    ntok, nseq = len(tokens), len(ranges)
+    od = model.info.output_dimensions
+
+    d_tokens = torch.from_numpy(tokens).cuda()
+    d_out = torch.empty((nseq, od), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step_device():
+        model.forward_device(d_tokens, ranges, d_out, stream=stream, device=local)
+
+    for _ in range(max(a.warmup, 3)):
+        step_device()
+    torch.cuda.synchronize()
+
+    # ---- device-resident throughput
+    clocks = ClockSampler(local)
+    time.sleep(0.3)
+    launches0 = model_launches(model)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(a.steps):
+        step_device()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clock_info = clocks.stop()
+    launches = model_launches(model) - launches0
+    ms_total = e0.elapsed_time(e1)
+    ms_max, tok_sum = reduce_max_sum(dist, ms_total, ntok * a.steps)
+    value = tok_sum / (ms_max / 1000.0)
+
+    # ---- end to end through the public API with host buffers
+    for _ in range(2):
+        model.forward_packed(tokens, positions, ranges)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        out = model.forward_packed(tokens, positions, ranges)
+    t1 = time.perf_counter()
+    barrier()
+    e2e_ms, _ = reduce_max_sum(dist, (t1 - t0) * 1000.0, 0)
+    e2e = tok_sum / (e2e_ms / 1000.0)
+    nwork = sum((n + 31) // 32 for _, n in ranges)
+    h2d = ntok * 4 * 2 + nseq * 8 + nwork * 12
+    d2h = nseq * od * 4 + 4
+
+    # ---- per-kernel roofline (rank 0): the kernel class with the largest share of a forward
+    pk = peaks()
+    roofline = None
+    prof = []
+    if rank == 0:
+        prof = model.profile(tokens, ranges, reps=a.profile_reps)
+        fwd_ms = sum(p["ms_per_launch"] * p["launches_per_forward"] for p in prof)
+        top = max(prof, key=lambda p: p["ms_per_launch"] * p["launches_per_forward"])
+        tensor = top["flops_per_launch"] > 0
+        if tensor:
+            ach = top["flops_per_launch"] / (top["ms_per_launch"] / 1000.0) / 1e12
+            peak, unit = pk["bf16_tflops"], "TFLOP/s"
+        else:
+            ach = top["bytes_per_launch"] / (top["ms_per_launch"] / 1000.0) / 1e9
+            peak, unit = pk["hbm_gbs"], "GB/s"
+        roofline = {"kernel": top["name"], "bound": "tensor" if tensor else "hbm", "achieved": ach, "peak": peak,
+                    "unit": unit, "frac": ach / peak, "traffic": None, "peak_source": pk["source"],
+                    "share_of_forward": top["ms_per_launch"] * top["launches_per_forward"] / fwd_ms,
+                    "launches_per_forward": top["launches_per_forward"]}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cpu = cpu_baseline(path, seqs, a.cpu_seconds)
+
+    if rank == 0:
+        line = {"metric": "embedded tokens/sec (config 2: 64 texts x 32..512 tokens)", "value": value,
+                "unit": "tokens/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+                "ms_per_step": ms_max / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f16", "data": "synthetic",
+                "config": {"workload": f"config {a.config}", "arch": a.arch, "tokens_per_rank": ntok,
+                           "texts_per_rank": nseq, "global_batch_tokens": tok_sum // a.steps,
+                           "parallelism": f"dp{world}",
+                           "l2": "working set larger than L2 (fp16 weights 203 MB + ~0.5 GB of activations per step)"},
+                "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                        "api": "ge_forward_packed"},
+                "gpu_launches": int(launches), "clocks": clock_info, "roofline": roofline, "cpu_baseline": cpu,
+                "latency_ms_p50": ms_max / a.steps,
+                "kernels": [{k: (round(v, 5) if isinstance(v, float) else v) for k, v in p.items()} for p in prof]}
+        print(json.dumps(line), flush=True)
+    model.close()
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+def model_launches(model) -> int:
+    ctypes = importlib.import_module("ctypes")
+    lib_mod = importlib.import_module(PKG + "._lib")
+    info = lib_mod.GeInfo()
+    lib_mod.lib().ge_info_get(model._h, ctypes.byref(info))
+    return int(info.kernel_launches)
+
+
+def reduce_max_sum(dist, ms, tokens):
+    if dist is None:
+        return ms, tokens
+    import torch
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    n = torch.tensor([tokens], dtype=torch.float64, device="cuda")
+    dist.all_reduce(n, op=dist.ReduceOp.SUM)
+    return float(t.item()), int(n.item())
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -216,6 +216,20 @@ class EmbeddingModel:
         _check(_lib.lib().ge_forward_device(self._h, device, ctypes.c_void_p(tp), ntok, arr, len(seqs),
                                            ctypes.c_void_p(op), ctypes.c_void_p(sp)), self._h)
 
+    def profile(self, tokens, seqs, reps: int = 10) -> list:
+        """Profiler.profile (Metal/Profiler.swift:16-88): per kernel class, mean ms per launch over
+        `reps` back-to-back launches, algorithmic FLOPs and bytes per launch, launches per forward."""
+        tokens = _i32(tokens)
+        arr = (_lib.GeSeq * max(len(seqs), 1))(*[_lib.GeSeq(int(s), int(n)) for s, n in seqs])
+        cap = 64
+        out = (_lib.GeKernelTime * cap)()
+        cnt = ctypes.c_int32(0)
+        _check(_lib.lib().ge_profile(self._h, _ptr(tokens, ctypes.c_int32), len(tokens), arr, len(seqs), reps, out, cap,
+                                    ctypes.byref(cnt)), self._h)
+        return [{"name": out[i].name.decode(), "ms_per_launch": out[i].ms_per_launch,
+                 "flops_per_launch": out[i].flops_per_launch, "bytes_per_launch": out[i].bytes_per_launch,
+                 "launches_per_forward": out[i].launches_per_forward} for i in range(cnt.value)]
+
     def trace(self, tokens, layer: int) -> np.ndarray:
         """The residual stream after `layer` ("l_out-<layer>"), or result_norm for layer -1: [ntok][hidden]."""
         tokens = _i32(tokens)

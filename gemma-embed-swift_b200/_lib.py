@@ -35,7 +35,12 @@ class GeInfo(ctypes.Structure):
                                       "max_tokens")] + [
         ("norm_epsilon", ctypes.c_float), ("quantization", ctypes.c_char * 16), ("file_size", ctypes.c_int64),
         ("device_count", ctypes.c_int32), ("eos_id", ctypes.c_int32), ("bos_id", ctypes.c_int32),
-        ("device_name", ctypes.c_char * 128)]
+        ("device_name", ctypes.c_char * 128), ("kernel_launches", ctypes.c_int64)]
+
+
+class GeKernelTime(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 32), ("ms_per_launch", ctypes.c_double), ("flops_per_launch", ctypes.c_double),
+                ("bytes_per_launch", ctypes.c_double), ("launches_per_forward", ctypes.c_int32)]
 
 
 PROGRESS_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p)
@@ -54,6 +59,8 @@ SIGNATURES = {
     "ge_forward_trace": ([ctypes.c_void_p, i32p, ctypes.c_int32, ctypes.c_int32, f32p], ctypes.c_int),
     "ge_embed_tokens": ([ctypes.c_void_p, P(i32p), i32p, ctypes.c_int32, P(GeEmbedOpts), f32p, i32p, i32p,
                          PROGRESS_FN, ctypes.c_void_p], ctypes.c_int),
+    "ge_profile": ([ctypes.c_void_p, i32p, ctypes.c_int32, P(GeSeq), ctypes.c_int32, ctypes.c_int32, P(GeKernelTime),
+                    ctypes.c_int32, i32p], ctypes.c_int),
     "ge_batches": ([i64p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, i64p, i32p, i32p], ctypes.c_int),
     "ge_finish": ([f32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, f32p], ctypes.c_int),
 }

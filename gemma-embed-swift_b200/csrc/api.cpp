@@ -223,6 +223,48 @@ int ge_info_get(const ge_model* m, ge_info* info) {
     info->eos_id = c.eos_id;
     info->bos_id = c.bos_id;
     if (!m->devs.empty()) snprintf(info->device_name, sizeof info->device_name, "%s", m->devs[0].name.c_str());
+    info->kernel_launches = m->launches.load();
+    return GE_OK;
+}
+
+int ge_profile(ge_model* m, const int32_t* tokens, int32_t ntok, const ge_seq* seqs, int32_t nseq, int32_t reps,
+               ge_kernel_time* out, int32_t cap, int32_t* count) {
+    if (!m) return GE_ERR_INVALID_OPTIONS;
+    std::lock_guard<std::mutex> g(m->mu);
+    if (reps < 1 || cap < 0 || (cap > 0 && !out) || !count)
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: reps must be at least 1");
+    int rc = check_batch(m, tokens, nullptr, ntok, seqs, nseq);
+    if (rc) return rc;
+    if (nseq == 0) {
+        *count = 0;
+        return GE_OK;
+    }
+    ge::ProfileSink sink;
+    sink.reps = reps;
+    std::vector<float> pooled(size_t(nseq) * m->cfg.out_dim);
+    ge::ForwardArgs a;
+    a.tokens = tokens;
+    a.ntok = ntok;
+    a.seqs = seqs;
+    a.nseq = nseq;
+    a.out = pooled.data();
+    a.profile = &sink;
+    rc = ge::run_forward(m, m->devs[0], a);
+    if (rc) return rc;
+    int32_t n = 0;
+    for (auto& e : sink.entries) {
+        if (n < cap) {
+            ge_kernel_time& k = out[n];
+            memset(&k, 0, sizeof k);
+            snprintf(k.name, sizeof k.name, "%s", e.name.c_str());
+            k.ms_per_launch = e.ms;
+            k.flops_per_launch = e.flops;
+            k.bytes_per_launch = e.bytes;
+            k.launches_per_forward = e.occurrences;
+        }
+        n++;
+    }
+    *count = n < cap ? n : cap;
     return GE_OK;
 }
 

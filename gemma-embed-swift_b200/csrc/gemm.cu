@@ -337,10 +337,13 @@ static bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes
 }
 
 bool encode_weight_maps(DevWeight& w, int bn) {
-    bool ok = encode_2d(&w.map_q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.q8, w.K, w.N, BK, bn,
-                        CU_TENSOR_MAP_SWIZZLE_NONE) &&
-              encode_2d(&w.map_scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.scales_t, w.N, w.K / 32, bn, 2,
-                        CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (!w.q8 && !w.f16) return false;
+    bool ok = true;
+    if (w.q8)  // weights stored as F16/BF16/F32 in the GGUF have no Q8 planes
+        ok = encode_2d(&w.map_q8, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.q8, w.K, w.N, BK, bn,
+                       CU_TENSOR_MAP_SWIZZLE_NONE) &&
+             encode_2d(&w.map_scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.scales_t, w.N, w.K / 32, bn, 2,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
     if (ok && w.f16)
         ok = encode_2d(&w.map_f16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.f16, w.K, w.N, BK, bn,
                        CU_TENSOR_MAP_SWIZZLE_128B);
@@ -376,7 +379,9 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream) {
     if (g.m_rows <= 0) return cudaSuccess;
     if (g.m_rows % BM || g.w->N % kBN || g.w->K % BK || g.a->cols != g.w->K || g.a->rows < g.m_rows)
         return cudaErrorInvalidValue;
-    const bool q8 = g.use_q8 || !g.w->f16;
+    // The Q8 path needs the Q8 planes; weights without them always take the fp16 path.
+    if (!g.w->f16 && !g.w->q8) return cudaErrorInvalidValue;
+    const bool q8 = g.w->q8 && (g.use_q8 || !g.w->f16);
     switch (g.epilogue) {
     case EPI_F32: return q8 ? launch_t<EPI_F32, true>(g, stream) : launch_t<EPI_F32, false>(g, stream);
     case EPI_F16: return q8 ? launch_t<EPI_F16, true>(g, stream) : launch_t<EPI_F16, false>(g, stream);

@@ -687,6 +687,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     const int nwork = build_work(a.seqs, nseq, qpi, nullptr);
     if ((e = ensure_workspace(c, d, rows, nseq, nwork)) != cudaSuccess) return gpu_fail(e, "workspace");
     Workspace& ws = d.ws;
+    int64_t launches = 0;
     // ---- inputs
     for (int s = 0; s < nseq; s++) {
         ws.h_seqs[2 * s] = a.seqs[s].start;
@@ -701,6 +702,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         if ((e = cudaMemcpyAsync(ws.tokens, ws.h_tokens, size_t(ntok) * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess)
             return gpu_fail(e, "token upload");
     }
+    if (a.positions == nullptr) launches++;  // the positions kernel below
     if ((e = cudaMemcpyAsync(ws.seqs, ws.h_seqs, size_t(nseq) * 8, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
         (e = cudaMemcpyAsync(ws.work, ws.h_work, size_t(nwork) * 12, cudaMemcpyHostToDevice, st)) != cudaSuccess)
         return gpu_fail(e, "batch upload");
@@ -736,24 +738,86 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         cudaError_t e_ = (expr);                        \
         if (e_ != cudaSuccess) return gpu_fail(e_, what); \
     } while (0)
+    // Every kernel launch goes through K: it counts launches and, when profiling, times the
+    // first launch of each kernel class over `reps` back-to-back repetitions (the reference's
+    // Profiler, Metal/Profiler.swift:16-88).
+    auto K = [&](const char* name, double flops, double bytes, auto&& fn) -> cudaError_t {
+        if (a.profile) {
+            ProfileEntry* pe = a.profile->find(name);
+            if (pe) {
+                pe->occurrences++;
+            } else {
+                cudaEvent_t e0, e1;
+                cudaEventCreate(&e0);
+                cudaEventCreate(&e1);
+                cudaEventRecord(e0, st);
+                for (int r = 0; r < a.profile->reps; r++) {
+                    cudaError_t x = fn();
+                    if (x != cudaSuccess) return x;
+                    launches++;
+                }
+                cudaEventRecord(e1, st);
+                cudaError_t x = cudaEventSynchronize(e1);
+                float ms = 0.f;
+                cudaEventElapsedTime(&ms, e0, e1);
+                cudaEventDestroy(e0);
+                cudaEventDestroy(e1);
+                if (x != cudaSuccess) return x;
+                a.profile->add(name, double(ms) / a.profile->reps, flops, bytes);
+                return cudaSuccess;
+            }
+        }
+        launches++;
+        return fn();
+    };
+    // Algorithmic work of a GEMM launch: the rows that hold tokens, not the padding.
+    auto gemm_flops = [&](const DevWeight& W) { return 2.0 * ntok * W.N * double(W.K); };
+    auto gemm_bytes = [&](const DevWeight& W, double out_elem_bytes) {
+        return double(ntok) * W.K * 2 + double(W.N) * W.K * (q8 ? 34.0 / 32.0 : 2.0) + double(ntok) * W.N * out_elem_bytes;
+    };
+    // Keys each query sees, summed over the batch, for the attention FLOP count.
+    auto visible_keys = [&](int hw) {
+        double sum = 0;
+        for (int s = 0; s < nseq; s++) {
+            const int64_t n = a.seqs[s].length;
+            if (hw <= 0) {
+                sum += double(n) * n;
+                continue;
+            }
+            for (int64_t i = 0; i < n; i++) sum += double(std::min<int64_t>(n - 1, i + hw) - std::max<int64_t>(0, i - hw) + 1);
+        }
+        return sum;
+    };
+    const double vk_sliding = a.profile ? visible_keys(c.sliding_window / 2) : 0, vk_global = a.profile ? visible_keys(0) : 0;
 
-    CK(launch_embed(tokens, ntok, rows, d.emb_q, d.emb_s, D, c.emb_scale, ws.x, c.has_ple ? ws.x16 : nullptr,
-                    d.layers[0].attn_norm, c.eps, ws.h, st),
+    CK(K("embed", 0, double(ntok) * D * (1 + 2.0 / 32 + 4 + 2),
+         [&] {
+             return launch_embed(tokens, ntok, rows, d.emb_q, d.emb_s, D, c.emb_scale, ws.x, c.has_ple ? ws.x16 : nullptr,
+                                 d.layers[0].attn_norm, c.eps, ws.h, st);
+         }),
        "embed");
     if (c.has_ple) {
         // ple = rmsnorm_pl(x0 * Wplp^T / sqrt(d)) for every layer at once (CPUReference.swift:206-210).
         const int plw = c.per_layer * c.layers;
-        CK(gemm(ws.a_x16, d.plp, ws.ple, plw, EPI_F32), "per-layer projection");
-        CK(launch_rmsnorm_rows(ws.ple, rows * c.layers, c.per_layer, c.pl_scale, d.pl_norm, c.eps, ws.ple, st),
+        CK(K("gemm_per_layer_inputs", gemm_flops(d.plp), gemm_bytes(d.plp, 4),
+             [&] { return gemm(ws.a_x16, d.plp, ws.ple, plw, EPI_F32); }),
+           "per-layer projection");
+        CK(K("per_layer_norm", 0, double(ntok) * plw * 8,
+             [&] { return launch_rmsnorm_rows(ws.ple, rows * c.layers, c.per_layer, c.pl_scale, d.pl_norm, c.eps, ws.ple, st); }),
            "per-layer norm");
     }
     for (int l = 0; l < c.layers; l++) {
         const LayerCfg& lc = c.layer[l];
         const LayerDev& L = d.layers[l];
         const int qd = c.heads * lc.hd;
-        CK(gemm(ws.a_h, L.qkv, ws.qkv, L.qkv.N, EPI_F32), "qkv projection");
-        CK(launch_qkv_norm_rope(ws.qkv, ntok, rows, c.heads, lc.kv, lc.hd, L.q_norm, L.k_norm, ws.positions,
-                                d.rope[lc.rope_index], c.eps, ws.q, ws.k, ws.v, st),
+        CK(K("gemm_qkv", gemm_flops(L.qkv), gemm_bytes(L.qkv, 4),
+             [&] { return gemm(ws.a_h, L.qkv, ws.qkv, L.qkv.N, EPI_F32); }),
+           "qkv projection");
+        CK(K("qkv_norm_rope", 0, double(ntok) * L.qkv.N * 6,
+             [&] {
+                 return launch_qkv_norm_rope(ws.qkv, ntok, rows, c.heads, lc.kv, lc.hd, L.q_norm, L.k_norm, ws.positions,
+                                             d.rope[lc.rope_index], c.eps, ws.q, ws.k, ws.v, st);
+             }),
            "q/k/v norm and rope");
         AttnLaunch al;
         al.q = ws.q;
@@ -768,30 +832,55 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         al.half_window = lc.sliding ? c.sliding_window / 2 : 0;
         al.queries_per_item = qpi;
         al.err = d.err;
-        CK(launch_attention(al, st), "attention");
+        CK(K(lc.sliding ? "attention_sliding" : "attention_global",
+             4.0 * c.heads * lc.hd * (lc.sliding ? vk_sliding : vk_global),
+             double(ntok) * (2.0 * qd + 2.0 * lc.kv * lc.hd) * 2, [&] { return launch_attention(al, st); }),
+           "attention");
         const DevActivation* aa = nullptr;
         for (auto& x : ws.a_attn)
             if (x.cols == qd) aa = &x;
-        CK(gemm(*aa, L.o, ws.o, D, EPI_F32), "attention output");
-        CK(launch_residual_norm(ws.x, ws.o, rows, D, L.post_attn, 1.0f, L.ffn_norm, c.eps, ws.h, nullptr, nullptr, st),
+        CK(K("gemm_o", gemm_flops(L.o), gemm_bytes(L.o, 4), [&] { return gemm(*aa, L.o, ws.o, D, EPI_F32); }),
+           "attention output");
+        CK(K("residual_norm", 0, double(ntok) * D * 14,
+             [&] {
+                 return launch_residual_norm(ws.x, ws.o, rows, D, L.post_attn, 1.0f, L.ffn_norm, c.eps, ws.h, nullptr,
+                                             nullptr, st);
+             }),
            "post-attention residual");
-        CK(gemm(ws.a_h, L.gu, ws.act, c.ff, EPI_GEGLU), "gate/up projection");
-        CK(gemm(ws.a_act, L.down, ws.o, D, EPI_F32), "down projection");
+        CK(K("gemm_gate_up", gemm_flops(L.gu), gemm_bytes(L.gu, 1), [&] { return gemm(ws.a_h, L.gu, ws.act, c.ff, EPI_GEGLU); }),
+           "gate/up projection");
+        CK(K("gemm_down", gemm_flops(L.down), gemm_bytes(L.down, 4),
+             [&] { return gemm(ws.a_act, L.down, ws.o, D, EPI_F32); }),
+           "down projection");
         const bool last = l + 1 == c.layers;
         const float* next = last ? d.out_norm : d.layers[l + 1].attn_norm;
         if (c.has_ple) {
-            CK(launch_residual_norm(ws.x, ws.o, rows, D, L.post_ffw, 1.0f, nullptr, c.eps, nullptr, nullptr, ws.x16, st),
+            CK(K("residual_norm", 0, double(ntok) * D * 14,
+                 [&] {
+                     return launch_residual_norm(ws.x, ws.o, rows, D, L.post_ffw, 1.0f, nullptr, c.eps, nullptr, nullptr,
+                                                 ws.x16, st);
+                 }),
                "post-ffn residual");
-            CK(gemm(ws.a_x16, L.inp_gate, ws.g, c.per_layer, EPI_GELU_MUL, ws.ple + size_t(l) * c.per_layer,
-                    c.per_layer * c.layers),
+            CK(K("gemm_inp_gate", gemm_flops(L.inp_gate), gemm_bytes(L.inp_gate, 2),
+                 [&] {
+                     return gemm(ws.a_x16, L.inp_gate, ws.g, c.per_layer, EPI_GELU_MUL, ws.ple + size_t(l) * c.per_layer,
+                                 c.per_layer * c.layers);
+                 }),
                "per-layer gate");
-            CK(gemm(ws.a_g, L.proj, ws.o, D, EPI_F32), "per-layer projection");
-            CK(launch_residual_norm(ws.x, ws.o, rows, D, L.post_norm, L.out_scale, next, c.eps, last ? nullptr : ws.h,
-                                    last ? ws.y : nullptr, nullptr, st),
+            CK(K("gemm_proj", gemm_flops(L.proj), gemm_bytes(L.proj, 4), [&] { return gemm(ws.a_g, L.proj, ws.o, D, EPI_F32); }),
+               "per-layer projection");
+            CK(K("residual_norm", 0, double(ntok) * D * 14,
+                 [&] {
+                     return launch_residual_norm(ws.x, ws.o, rows, D, L.post_norm, L.out_scale, next, c.eps,
+                                                 last ? nullptr : ws.h, last ? ws.y : nullptr, nullptr, st);
+                 }),
                "per-layer residual");
         } else {
-            CK(launch_residual_norm(ws.x, ws.o, rows, D, L.post_ffw, 1.0f, next, c.eps, last ? nullptr : ws.h,
-                                    last ? ws.y : nullptr, nullptr, st),
+            CK(K("residual_norm", 0, double(ntok) * D * 14,
+                 [&] {
+                     return launch_residual_norm(ws.x, ws.o, rows, D, L.post_ffw, 1.0f, next, c.eps, last ? nullptr : ws.h,
+                                                 last ? ws.y : nullptr, nullptr, st);
+                 }),
                "post-ffn residual");
         }
         if (a.trace_layer == l) break;
@@ -806,17 +895,25 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         result = ws.y;
         width = D;
     } else {
-        CK(launch_mean_pool(ws.y, D, ws.seqs, nseq, ws.pooled, st), "mean pool");
+        CK(K("mean_pool", 0, double(ntok) * D * 4, [&] { return launch_mean_pool(ws.y, D, ws.seqs, nseq, ws.pooled, st); }),
+           "mean pool");
         if (c.has_dense) {
-            CK(launch_dense_f32(ws.pooled, nseq, d.dense2, c.dense_head, D, ws.mid, st), "dense head");
-            CK(launch_dense_f32(ws.mid, nseq, d.dense3, c.out_dim, c.dense_head, ws.out, st), "dense head");
+            CK(K("dense_head", 2.0 * nseq * D * c.dense_head, double(D) * c.dense_head * 4,
+                 [&] { return launch_dense_f32(ws.pooled, nseq, d.dense2, c.dense_head, D, ws.mid, st); }),
+               "dense head");
+            CK(K("dense_head", 2.0 * nseq * D * c.dense_head, double(D) * c.dense_head * 4,
+                 [&] { return launch_dense_f32(ws.mid, nseq, d.dense3, c.out_dim, c.dense_head, ws.out, st); }),
+               "dense head");
         } else {
-            CK(launch_dense_f32(ws.pooled, nseq, d.output, c.out_dim, D, ws.out, st), "output projection");
+            CK(K("output_projection", 2.0 * nseq * D * c.out_dim, double(D) * c.out_dim * 4,
+                 [&] { return launch_dense_f32(ws.pooled, nseq, d.output, c.out_dim, D, ws.out, st); }),
+               "output projection");
         }
         result = ws.out;
     }
     const size_t out_elems = a.trace_layer >= -1 ? size_t(ntok) * D : size_t(nseq) * width;
     float* host_out = a.trace_layer >= -1 ? a.trace_out : a.out;
+    m->launches += launches;
     if (a.out_on_device && a.trace_layer < -1) {
         CK(cudaMemcpyAsync(a.out, result, out_elems * 4, cudaMemcpyDeviceToDevice, st), "result copy");
         return GE_OK;

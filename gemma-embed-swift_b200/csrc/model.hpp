@@ -4,6 +4,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -88,9 +89,33 @@ struct ge_model {
     int budget = 8192;
     uint32_t flags = 0;
     int64_t file_size = 0;
+    std::atomic<int64_t> launches{0};  // kernel launches issued by this model so far
 };
 
 namespace ge {
+struct ProfileEntry {
+    std::string name;
+    double ms = 0, flops = 0, bytes = 0;
+    int occurrences = 1;
+};
+// Per-kernel-class timings collected by a profiling forward (ge_profile).
+struct ProfileSink {
+    int reps = 10;
+    std::vector<ProfileEntry> entries;
+    ProfileEntry* find(const std::string& n) {
+        for (auto& e : entries)
+            if (e.name == n) return &e;
+        return nullptr;
+    }
+    void add(const std::string& n, double ms, double flops, double bytes) {
+        ProfileEntry e;
+        e.name = n;
+        e.ms = ms;
+        e.flops = flops;
+        e.bytes = bytes;
+        entries.push_back(e);
+    }
+};
 // One forward over a packed batch on one device (the body of MetalForward.execute/encode).
 // tokens/positions/out are host pointers unless the *_dev flags say otherwise.
 struct ForwardArgs {
@@ -106,6 +131,7 @@ struct ForwardArgs {
     int trace_layer = -2;           // >= -1: copy that layer's hidden state into trace_out instead
     float* trace_out = nullptr;
     std::string* error = nullptr;   // where failures are reported; nullptr: the model's last_error
+    ProfileSink* profile = nullptr;  // time each kernel class instead of only running it
 };
 int run_forward(ge_model* m, Device& d, const ForwardArgs& a);
 int set_error(ge_model* m, int code, const std::string& msg);

@@ -87,7 +87,17 @@ typedef struct ge_info {
     int32_t eos_id;
     int32_t bos_id;
     char device_name[128];
+    int64_t kernel_launches; /* CUDA kernels this model has launched so far, on all devices */
 } ge_info;
+
+/* One kernel class of a profiling forward (ge_profile). */
+typedef struct ge_kernel_time {
+    char name[32];
+    double ms_per_launch;     /* mean over `reps` back-to-back launches, CUDA events on the launch stream */
+    double flops_per_launch;  /* algorithmic FLOPs of one launch (token rows only) */
+    double bytes_per_launch;  /* algorithmic HBM bytes of one launch */
+    int32_t launches_per_forward;
+} ge_kernel_time;
 
 /* Progress after every batch (EmbeddingProgress, EmbedOptions.swift:155-160). Returning
  * nonzero cancels the call between batches, which then returns GE_ERR_CANCELLED
@@ -133,6 +143,13 @@ GE_API int ge_forward_device(ge_model* model, int32_t device_ordinal, const int3
  * residual stream after layer `layer` ("l_out-<layer>") into `hidden_out` (ntok * hidden
  * floats).  layer == -1 copies rmsnorm(x, output_norm) ("result_norm"). */
 GE_API int ge_forward_trace(ge_model* model, const int32_t* tokens, int32_t ntok, int32_t layer, float* hidden_out);
+
+/* Profiler.profile(model:texts:reps:) (Sources/GemmaEmbed/Metal/Profiler.swift:16-88): runs one forward over
+ * the packed batch on the first device, timing the first launch of every kernel class over
+ * `reps` back-to-back repetitions.  Fills up to `cap` entries and sets *count.  The forward's
+ * output is discarded (repeated in-place kernels change it). */
+GE_API int ge_profile(ge_model* model, const int32_t* tokens, int32_t ntok, const ge_seq* seqs, int32_t nseq,
+                      int32_t reps, ge_kernel_time* out, int32_t cap, int32_t* count);
 
 /* EmbeddingModel.embed over pre-tokenised texts (EmbeddingModel.swift:145-175 without the
  * tokenizer): truncation to max_tokens keeping EOS (189-196), batching by count or token
