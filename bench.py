@@ -194,7 +194,8 @@ def main():
 
     d_tokens = torch.from_numpy(tokens).cuda()
     d_out = torch.empty((nseq, od), dtype=torch.float32, device="cuda")
-    stream = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()  # every kernel of the timed steps runs on this stream
 
     def step_device():
         model.forward_device(d_tokens, ranges, d_out, stream=stream, device=local)

@@ -211,6 +211,7 @@ class EmbeddingModel:
         tp = d_tokens.data_ptr() if hasattr(d_tokens, "data_ptr") else int(d_tokens)
         op = d_out.data_ptr() if hasattr(d_out, "data_ptr") else int(d_out)
         ntok = int(sum(n for _, n in seqs))
+        # A torch stream, a raw cudaStream_t, or None for the legacy default stream.
         sp = stream.cuda_stream if hasattr(stream, "cuda_stream") else (stream or 0)
         arr = (_lib.GeSeq * max(len(seqs), 1))(*[_lib.GeSeq(int(s), int(n)) for s, n in seqs])
         _check(_lib.lib().ge_forward_device(self._h, device, ctypes.c_void_p(tp), ntok, arr, len(seqs),

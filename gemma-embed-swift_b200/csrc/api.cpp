@@ -305,7 +305,8 @@ int ge_forward_device(ge_model* m, int32_t device_ordinal, const int32_t* d_toke
     a.nseq = nseq;
     a.out = d_pooled;
     a.out_on_device = true;
-    a.stream = static_cast<cudaStream_t>(stream);
+    // NULL is the caller's legacy default stream, never the library's internal stream.
+    a.stream = stream ? static_cast<cudaStream_t>(stream) : cudaStreamLegacy;
     return ge::run_forward(m, *dev, a);
 }
 
