@@ -231,6 +231,17 @@ class EmbeddingModel:
                  "flops_per_launch": out[i].flops_per_launch, "bytes_per_launch": out[i].bytes_per_launch,
                  "launches_per_forward": out[i].launches_per_forward} for i in range(cnt.value)]
 
+    def pool_head_noalloc(self, d_hidden, ntok: int, d_seqs, nseq: int, d_out, stream=None, device: int = 0) -> None:
+        """Mean-pool and head over caller-owned device buffers without allocating (ge_pool_head_noalloc),
+        for callers that cannot allocate device memory.  Arguments are torch CUDA tensors or raw
+        device pointers: d_hidden [ntok][hidden] fp32, d_seqs [nseq][2] uint32/int32 (start, length),
+        d_out [nseq][output_dimensions] fp32.  At most 128 sequences per call."""
+        ptr = lambda t: t.data_ptr() if hasattr(t, "data_ptr") else int(t)
+        sp = stream.cuda_stream if hasattr(stream, "cuda_stream") else (stream or 0)
+        _check(_lib.lib().ge_pool_head_noalloc(self._h, device, ctypes.c_void_p(ptr(d_hidden)), ntok,
+                                              ctypes.c_void_p(ptr(d_seqs)), nseq, ctypes.c_void_p(ptr(d_out)),
+                                              ctypes.c_void_p(sp)), self._h)
+
     def trace(self, tokens, layer: int) -> np.ndarray:
         """The residual stream after `layer` ("l_out-<layer>"), or result_norm for layer -1: [ntok][hidden]."""
         tokens = _i32(tokens)

@@ -61,6 +61,8 @@ SIGNATURES = {
                          PROGRESS_FN, ctypes.c_void_p], ctypes.c_int),
     "ge_profile": ([ctypes.c_void_p, i32p, ctypes.c_int32, P(GeSeq), ctypes.c_int32, ctypes.c_int32, P(GeKernelTime),
                     ctypes.c_int32, i32p], ctypes.c_int),
+    "ge_pool_head_noalloc": ([ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p,
+                              ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "ge_batches": ([i64p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, i64p, i32p, i32p], ctypes.c_int),
     "ge_finish": ([f32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, f32p], ctypes.c_int),
 }

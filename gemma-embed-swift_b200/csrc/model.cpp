@@ -27,6 +27,8 @@ int Config::max_kv() const {
     return m;
 }
 
+cudaError_t noalloc_setup(int device);
+
 int set_error(ge_model* m, int code, const std::string& msg) {
     if (m) m->last_error = msg;
     return code;
@@ -467,6 +469,7 @@ static int load_device(ge_model* m, Device& d, const std::vector<HostWeight>& hw
         if ((e = dev_upload(d, &d.dense3, dense3.data(), dense3.size())) != cudaSuccess) return fail(e);
     }
     if (c.has_output && (e = dev_upload(d, &d.output, output.data(), output.size())) != cudaSuccess) return fail(e);
+    if ((e = noalloc_setup(d.ordinal)) != cudaSuccess) return fail(e);
     return GE_OK;
 }
 

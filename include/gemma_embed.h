@@ -160,6 +160,26 @@ GE_API int ge_embed_tokens(ge_model* model, const int32_t* const* texts, const i
                            const ge_embed_opts* opts, float* out, int32_t* token_counts, int32_t* truncated,
                            ge_progress_fn progress, void* user);
 
+/* No counterpart in the reference.  The last stage of the forward -- mean-pool over each
+ * sequence, then the dense head (or the output projection) -- for callers that cannot allocate
+ * device memory: a plugin inside a host runtime that owns all device memory through its own
+ * allocator, or a serving loop where an allocation could implicitly synchronise the device.
+ * It calls no cudaMalloc, cudaFree or allocating library routine: its intermediates live in one
+ * file-scope __device__ array of GE_NOALLOC_MAX_SEQS rows (2.5 MiB, held by every GPU that
+ * loads the library until the process exits).
+ *   d_hidden: device [ntok][hidden_size] fp32, the final-normed hidden states (the values
+ *             ge_forward_trace returns for layer -1); d_seqs: device (start, length) uint32 pairs
+ *             that tile [0, ntok); d_out: device [nseq][output_dimensions] fp32.
+ * Work is enqueued on `stream` (a cudaStream_t; NULL is the legacy default stream) without
+ * synchronising.  nseq above GE_NOALLOC_MAX_SEQS returns GE_ERR_INVALID_OPTIONS.  ge_load
+ * looks up the array's device address (cudaGetSymbolAddress) once on each of its devices; if
+ * that lookup has not succeeded, the first call on the device repeats it, so make the first
+ * call before any stream capture.  All calls share the one array and each overwrites what it
+ * reads: calls whose work overlaps on the GPU (other streams, other host threads) race on it. */
+#define GE_NOALLOC_MAX_SEQS 128
+GE_API int ge_pool_head_noalloc(ge_model* model, int32_t device_ordinal, const float* d_hidden, int32_t ntok,
+                                const uint32_t* d_seqs, int32_t nseq, float* d_out, void* stream);
+
 /* EmbeddingModel.batches (EmbeddingModel.swift:200-215): splits `n` items with `ncost` costs
  * each (row-major costs[n][ncost]) into consecutive ranges, by count when batch_size > 0,
  * otherwise before the item that would take any summed cost past its budget.  Writes
