@@ -116,9 +116,315 @@ __global__ void __launch_bounds__(256) k_attention_simt(const __half* __restrict
     }
 }
 
-int attention_queries_per_item(int hd) {
-    (void)hd;
-    return kSimtQueries;
+// ---------------------------------------------------------------------------------------
+// Tensor-core kernel (head dim 256): one CTA per (work item of 128 queries, query head).
+//   warp 0      TMA producer: the Q tile once, then K and V tiles of 64 keys into 2-slot rings
+//   warp 1      tcgen05.mma issuer and tensor-memory owner: S_j = Q K_j^T (128 x 64, fp32 in
+//               TMEM, two buffers) and O += P_j V_j (128 x 256, fp32 in TMEM)
+//   warps 2-5   softmax, one thread per query row: masks S_j, keeps the running maximum and
+//               sum, writes P_j (fp16, 128-byte swizzled) to shared memory, and rescales O in
+//               tensor memory only when the row maximum grows by more than kRescale; until then
+//               every term of the row uses the same stale maximum, so the result is exact
+// Tensor memory: O in columns [0, 256), the S buffers in [256, 320) and [320, 384).
+constexpr int kTcQ = 128;
+constexpr int kTcKeys = 64;
+constexpr int kTcHd = 256;
+constexpr float kRescale = 8.0f;
+constexpr int kQBytes = kTcQ * kTcHd * 2;     // 64 KB: 4 chunks of [128 rows][64 dims]
+constexpr int kKVBytes = kTcKeys * kTcHd * 2; // 32 KB per stage: 4 chunks of [64 keys][64 dims]
+constexpr int kPBytes = kTcQ * kTcKeys * 2;   // 16 KB per buffer: [128 rows][64 keys]
+constexpr int kOffK = kQBytes;
+constexpr int kOffV = kOffK + 2 * kKVBytes;
+constexpr int kOffP = kOffV + 2 * kKVBytes;
+constexpr int kOffBar = kOffP + 2 * kPBytes;
+constexpr int kTcSmem = kOffBar + 256 + 1024;
+constexpr uint32_t kTmemO = 0, kTmemS = 256;
+
+struct TcAttnParams {
+    const uint32_t* work;
+    __half* out;
+    int heads, kvh, hw;
+    int* err;
+};
+
+__device__ __forceinline__ void drain(uint64_t* bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer();
+    while (!mbar_test(bar, parity) && globaltimer() - t0 < kWaitLimitNs) {
+    }
+}
+
+__global__ void __launch_bounds__(192, 1) k_attention_tc(const __grid_constant__ CUtensorMap mapQ,
+                                                          const __grid_constant__ CUtensorMap mapK,
+                                                          const __grid_constant__ CUtensorMap mapV, TcAttnParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+    uint64_t* q_full = bars;
+    uint64_t* k_full = bars + 1;
+    uint64_t* k_empty = bars + 3;
+    uint64_t* v_full = bars + 5;
+    uint64_t* v_empty = bars + 7;
+    uint64_t* s_full = bars + 9;
+    uint64_t* p_full = bars + 11;
+    uint64_t* pv_done = bars + 13;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+
+    const uint32_t seq_start = p.work[3 * blockIdx.x], len = p.work[3 * blockIdx.x + 1], q0 = p.work[3 * blockIdx.x + 2];
+    const int h = blockIdx.y;
+    const int kh = h / (p.heads / p.kvh);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    // Key blocks: the whole sequence, or the window of the whole query block
+    // (Attention.metal:66-74), starting on a multiple of kTcKeys from the sequence start.
+    int k_start = 0, k_end = int(len);
+    if (p.hw > 0) {
+        k_start = max(int(q0) - p.hw, 0);
+        k_end = min(int(q0) + kTcQ - 1 + p.hw + 1, int(len));
+    }
+    k_start = k_start / kTcKeys * kTcKeys;
+    const int nblk = (k_end - k_start + kTcKeys - 1) / kTcKeys;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&v_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&p_full[i], 128);
+            mbar_init(&pv_done[i], 1);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch(&mapQ);
+        tma_prefetch(&mapK);
+        tma_prefetch(&mapV);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            bool ok = true;
+            int issued_k = 0, issued_v = 0;
+            mbar_expect_tx(q_full, kQBytes);
+            for (int c = 0; c < 4; c++)
+                tma_load_2d(smem + c * (kQBytes / 4), &mapQ, q_full, h * kTcHd + c * 64, int(seq_start + q0));
+            for (int j = 0; j < nblk && ok; j++) {
+                const int b = j & 1;
+                const uint32_t ph = uint32_t((j >> 1) & 1);
+                const int row = int(seq_start) + k_start + j * kTcKeys;
+                if (!mbar_wait(&k_empty[b], ph ^ 1, p.err)) break;
+                mbar_expect_tx(&k_full[b], kKVBytes);
+                for (int c = 0; c < 4; c++)
+                    tma_load_2d(smem + kOffK + b * kKVBytes + c * (kKVBytes / 4), &mapK, &k_full[b], kh * kTcHd + c * 64, row);
+                issued_k++;
+                if (!mbar_wait(&v_empty[b], ph ^ 1, p.err)) break;
+                mbar_expect_tx(&v_full[b], kKVBytes);
+                for (int c = 0; c < 4; c++)
+                    tma_load_2d(smem + kOffV + b * kKVBytes + c * (kKVBytes / 4), &mapV, &v_full[b], kh * kTcHd + c * 64, row);
+                issued_v++;
+            }
+            // Every issued load lands before the CTA exits, also after an error.
+            drain(q_full, 0);
+            for (int b = 0; b < 2; b++) {
+                const int ck = issued_k / 2 + (b < issued_k % 2 ? 1 : 0);
+                const int cv = issued_v / 2 + (b < issued_v % 2 ? 1 : 0);
+                if (ck > 0) drain(&k_full[b], uint32_t((ck - 1) & 1));
+                if (cv > 0) drain(&v_full[b], uint32_t((cv - 1) & 1));
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t id_s = idesc_f16(kTcQ, kTcKeys);            // K-major Q and K
+            const uint32_t id_o = idesc_f16(kTcQ, kTcHd, 0, 1);        // K-major P, MN-major V
+            const uint32_t q_addr = smem_u32(smem);
+            bool ok = mbar_wait(q_full, 0, p.err);
+            auto issue_pv = [&](int j) -> bool {
+                const int b = j & 1;
+                const uint32_t ph = uint32_t((j >> 1) & 1);
+                if (!mbar_wait(&p_full[b], ph, p.err) || !mbar_wait(&v_full[b], ph, p.err)) return false;
+                tc_fence_after();
+                const uint32_t pa = smem_u32(smem + kOffP + b * kPBytes);
+                const uint32_t va = smem_u32(smem + kOffV + b * kKVBytes);
+#pragma unroll
+                for (int kk = 0; kk < kTcKeys / 16; kk++) {
+                    const uint64_t ad = sw128_desc(pa + kk * 32, 16, 1024);
+                    // V chunk of 64 dims = one [64 keys][128 B] box; 16 keys advance 2048 B.
+                    const uint64_t bd = sw128_desc(va + kk * 2048, kKVBytes / 4, 1024);
+                    umma_f16(tmem + kTmemO, ad, bd, id_o, (j | kk) != 0);
+                }
+                umma_commit(&v_empty[b]);
+                umma_commit(&pv_done[b]);
+                return true;
+            };
+            for (int j = 0; j < nblk && ok; j++) {
+                const int b = j & 1;
+                const uint32_t ph = uint32_t((j >> 1) & 1);
+                if (!mbar_wait(&k_full[b], ph, p.err)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t ka = smem_u32(smem + kOffK + b * kKVBytes);
+#pragma unroll
+                for (int kk = 0; kk < kTcHd / 16; kk++) {
+                    const int c = kk >> 2, w = kk & 3;  // 64-dim chunk, 16-dim step inside it
+                    const uint64_t ad = sw128_desc(q_addr + c * (kQBytes / 4) + w * 32, 16, 1024);
+                    const uint64_t bd = sw128_desc(ka + c * (kKVBytes / 4) + w * 32, 16, 1024);
+                    umma_f16(tmem + kTmemS + b * kTcKeys, ad, bd, id_s, kk != 0);
+                }
+                umma_commit(&k_empty[b]);
+                umma_commit(&s_full[b]);
+                if (j > 0 && !issue_pv(j - 1)) ok = false;
+            }
+            if (ok && nblk > 0) issue_pv(nblk - 1);
+        }
+    } else {
+        // ---------------------------------------------------------- softmax (one thread per row)
+        const int quad = warp & 3;  // TMEM lane group this warp may access
+        const int r = quad * 32 + lane;
+        const int qi = int(q0) + r;
+        const uint32_t lane_base = tmem + (uint32_t(quad * 32) << 16);
+        float m_used = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nblk; j++) {
+            const int b = j & 1;
+            const uint32_t ph = uint32_t((j >> 1) & 1);
+            if (!mbar_wait(&s_full[b], ph, p.err)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            uint32_t sr[64];
+            tmem_ld32(lane_base + kTmemS + b * kTcKeys, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+            tmem_ld32(lane_base + kTmemS + b * kTcKeys + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+            tmem_wait_ld();
+            const int kb = k_start + j * kTcKeys;
+            float mb = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < 64; i++) {
+                const int kj = kb + i;
+                bool valid = kj < int(len);
+                if (p.hw > 0) valid = valid && abs(qi - kj) <= p.hw;
+                const float s = valid ? __uint_as_float(sr[i]) : -INFINITY;
+                sr[i] = __float_as_uint(s);
+                mb = fmaxf(mb, s);
+            }
+            // Rescale O when this row's maximum grew past the threshold (warp-uniform decision:
+            // tensor-memory loads and stores are warp-collective).
+            const bool grow = mb > m_used + kRescale && m_used != -INFINITY;
+            if (__any_sync(0xffffffffu, grow)) {
+                const float alpha = grow ? expf(m_used - mb) : 1.0f;
+                if (j > 0 && !mbar_wait(&pv_done[(j - 1) & 1], uint32_t(((j - 1) >> 1) & 1), p.err)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll 1
+                for (int c = 0; c < kTcHd / 32; c++) {
+                    uint32_t o[32];
+                    tmem_ld32(lane_base + kTmemO + c * 32, o);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                    tmem_st32(lane_base + kTmemO + c * 32, o);
+                }
+                tmem_wait_st();
+                if (grow) {
+                    l *= alpha;
+                    m_used = mb;
+                }
+            }
+            if (m_used == -INFINITY) m_used = mb;  // first block with a visible key (O and l are still 0)
+            // P_j goes to buffer b once PV_{j-2}, which read that buffer, has completed.
+            if (j >= 2 && !mbar_wait(&pv_done[b], uint32_t(((j - 2) >> 1) & 1), p.err)) {
+                ok = false;
+                break;
+            }
+            uint8_t* prow = smem + kOffP + b * kPBytes + r * 128;
+            float sum = 0.f;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {  // 8 chunks of 8 keys = 16 bytes each
+                uint32_t w[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const float s0 = __uint_as_float(sr[c * 8 + 2 * e]), s1 = __uint_as_float(sr[c * 8 + 2 * e + 1]);
+                    const float p0 = s0 == -INFINITY ? 0.f : expf(s0 - m_used);
+                    const float p1 = s1 == -INFINITY ? 0.f : expf(s1 - m_used);
+                    sum += p0 + p1;
+                    __half2 hp = __floats2half2_rn(p0, p1);
+                    w[e] = *reinterpret_cast<uint32_t*>(&hp);
+                }
+                *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            l += sum;
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(&p_full[b]);
+        }
+        // ---- epilogue: O / l for the rows of this sequence
+        if (ok && nblk > 0) {
+            const int jl = nblk - 1;
+            if (mbar_wait(&pv_done[jl & 1], uint32_t((jl >> 1) & 1), p.err)) {
+                tc_fence_after();
+                const float inv = l > 0.f ? 1.0f / l : 0.f;
+                __half* orow = p.out + (long(seq_start) + qi) * long(p.heads) * kTcHd + h * kTcHd;
+                const bool store = qi < int(len);
+#pragma unroll 1
+                for (int c = 0; c < kTcHd / 32; c++) {
+                    uint32_t o[32];
+                    tmem_ld32(lane_base + kTmemO + c * 32, o);
+                    tmem_wait_ld();
+                    if (store) {
+                        uint32_t pk[16];
+#pragma unroll
+                        for (int i = 0; i < 16; i++) {
+                            __half2 hv = __floats2half2_rn(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
+                            pk[i] = *reinterpret_cast<uint32_t*>(&hv);
+                        }
+                        uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+                        for (int i = 0; i < 4; i++) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+int attention_queries_per_item(int hd) { return hd == kTcHd ? kTcQ : kSimtQueries; }
+
+static cudaError_t launch_tc(const AttnLaunch& a, cudaStream_t stream) {
+    static unsigned configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(configured & (1u << dev))) {
+        cudaError_t e = cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+        if (e != cudaSuccess) return e;
+        configured |= 1u << dev;
+    }
+    TcAttnParams p{a.work, a.out, a.heads, a.kv_heads, a.half_window, a.err};
+    dim3 grid(a.work_items, a.heads);
+    k_attention_tc<<<grid, 192, kTcSmem, stream>>>(a.maps->q, a.maps->k, a.maps->v, p);
+    return cudaGetLastError();
 }
 
 template <int HD>
@@ -138,10 +444,17 @@ static cudaError_t launch_simt(const AttnLaunch& a, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
+bool encode_attention_maps(AttnMaps& m, const __half* q, const __half* k, const __half* v, int rows, int heads, int kvh,
+                           int hd) {
+    return encode_fp16_map(&m.q, q, uint64_t(heads) * hd, rows, 64, kTcQ) &&
+           encode_fp16_map(&m.k, k, uint64_t(kvh) * hd, rows, 64, kTcKeys) &&
+           encode_fp16_map(&m.v, v, uint64_t(kvh) * hd, rows, 64, kTcKeys);
+}
+
 cudaError_t launch_attention(const AttnLaunch& a, cudaStream_t stream) {
     if (a.work_items <= 0) return cudaSuccess;
-    if (a.queries_per_item != kSimtQueries || a.heads % a.kv_heads) return cudaErrorInvalidValue;
-    if (a.hd == 256) return launch_simt<256>(a, stream);
+    if (a.heads % a.kv_heads || a.queries_per_item != attention_queries_per_item(a.hd)) return cudaErrorInvalidValue;
+    if (a.hd == kTcHd) return a.maps ? launch_tc(a, stream) : cudaErrorInvalidValue;
     if (a.hd == 512) return launch_simt<512>(a, stream);
     return cudaErrorInvalidValue;
 }

@@ -350,6 +350,12 @@ bool encode_weight_maps(DevWeight& w, int bn) {
     return ok;
 }
 
+bool encode_fp16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                     uint32_t box_outer) {
+    return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), inner, outer, box_inner, box_outer,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 bool encode_activation_map(DevActivation& a) {
     return encode_2d(&a.map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.ptr, a.cols, a.rows, BK, BM,
                      CU_TENSOR_MAP_SWIZZLE_128B);

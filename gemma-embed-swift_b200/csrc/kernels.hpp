@@ -95,6 +95,16 @@ cudaError_t launch_dense_f32(const float* in, int nrows, const float* w, int N, 
 cudaError_t launch_positions(const uint32_t* seqs, int nseq, int32_t* positions, cudaStream_t stream);
 
 // ------------------------------------------------------------------ attention
+// TMA descriptors of the q, k and v buffers for the tensor-core attention kernel.
+struct AttnMaps {
+    CUtensorMap q, k, v;
+};
+bool encode_attention_maps(AttnMaps& m, const __half* q, const __half* k, const __half* v, int rows, int heads, int kvh,
+                           int hd);
+// A 2-D fp16 tensor map with 128-byte swizzle over a row-major [outer][inner] matrix.
+bool encode_fp16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                     uint32_t box_outer);
+
 struct AttnLaunch {
     const __half* q;  // [rows][heads * hd]
     const __half* k;  // [rows][kv_heads * hd]
@@ -106,6 +116,7 @@ struct AttnLaunch {
     int half_window;  // 0: global attention
     int queries_per_item;
     int* err;
+    const AttnMaps* maps = nullptr;  // required for head dim 256 (tensor-core kernel)
 };
 cudaError_t launch_attention(const AttnLaunch& a, cudaStream_t stream);
 int attention_queries_per_item(int hd);

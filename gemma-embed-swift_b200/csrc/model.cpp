@@ -388,6 +388,17 @@ static cudaError_t ensure_workspace(const Config& c, Device& d, int rows, int se
     };
     bool ok = act(ws.a_h, ws.h, c.hidden) && act(ws.a_act, ws.act, c.ff);
     if (c.has_ple) ok = ok && act(ws.a_x16, ws.x16, c.hidden) && act(ws.a_g, ws.g, c.per_layer);
+    ws.attn_maps.clear();
+    for (auto& l : c.layer) {
+        if (l.hd != 256) continue;
+        bool have = false;
+        for (auto& x : ws.attn_maps) have = have || x.first == l.kv;
+        if (!have) {
+            AttnMaps am;
+            ok = ok && encode_attention_maps(am, ws.q, ws.k, ws.v, R, c.heads, l.kv, l.hd);
+            ws.attn_maps.push_back({l.kv, am});
+        }
+    }
     ws.a_attn.clear();
     for (auto& l : c.layer) {
         const int cols = c.heads * l.hd;
@@ -686,9 +697,14 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     if (e != cudaSuccess) return gpu_fail(e, "cudaSetDevice");
     const int ntok = a.ntok, nseq = a.nseq;
     const int rows = std::max(kRowTile, round_up(ntok, kRowTile));
-    const int qpi = attention_queries_per_item(256);
+    // Two work lists: blocks of the tensor-core kernel's query count, and of the CUDA-core
+    // kernel's for head-dim-512 layers, stored back to back.
+    bool any512 = false;
+    for (auto& l : c.layer) any512 = any512 || l.hd == 512;
+    const int qpi = attention_queries_per_item(256), qpi512 = attention_queries_per_item(512);
     const int nwork = build_work(a.seqs, nseq, qpi, nullptr);
-    if ((e = ensure_workspace(c, d, rows, nseq, nwork)) != cudaSuccess) return gpu_fail(e, "workspace");
+    const int nwork512 = any512 ? build_work(a.seqs, nseq, qpi512, nullptr) : 0;
+    if ((e = ensure_workspace(c, d, rows, nseq, nwork + nwork512)) != cudaSuccess) return gpu_fail(e, "workspace");
     Workspace& ws = d.ws;
     int64_t launches = 0;
     // ---- inputs
@@ -697,6 +713,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         ws.h_seqs[2 * s + 1] = a.seqs[s].length;
     }
     build_work(a.seqs, nseq, qpi, ws.h_work);
+    if (any512) build_work(a.seqs, nseq, qpi512, ws.h_work + 3 * size_t(nwork));
     const int32_t* tokens = ws.tokens;
     if (a.tokens_on_device) {
         tokens = a.tokens;
@@ -707,7 +724,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     }
     if (a.positions == nullptr) launches++;  // the positions kernel below
     if ((e = cudaMemcpyAsync(ws.seqs, ws.h_seqs, size_t(nseq) * 8, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
-        (e = cudaMemcpyAsync(ws.work, ws.h_work, size_t(nwork) * 12, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+        (e = cudaMemcpyAsync(ws.work, ws.h_work, size_t(nwork + nwork512) * 12, cudaMemcpyHostToDevice, st)) != cudaSuccess)
         return gpu_fail(e, "batch upload");
     if (a.positions) {
         memcpy(ws.h_positions, a.positions, size_t(ntok) * 4);
@@ -827,14 +844,17 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         al.k = ws.k;
         al.v = ws.v;
         al.out = ws.attn;
-        al.work = ws.work;
-        al.work_items = nwork;
+        const bool tc = lc.hd == 256;
+        al.work = tc ? ws.work : ws.work + 3 * size_t(nwork);
+        al.work_items = tc ? nwork : nwork512;
         al.heads = c.heads;
         al.kv_heads = lc.kv;
         al.hd = lc.hd;
         al.half_window = lc.sliding ? c.sliding_window / 2 : 0;
-        al.queries_per_item = qpi;
+        al.queries_per_item = tc ? qpi : qpi512;
         al.err = d.err;
+        for (auto& x : ws.attn_maps)
+            if (tc && x.first == lc.kv) al.maps = &x.second;
         CK(K(lc.sliding ? "attention_sliding" : "attention_global",
              4.0 * c.heads * lc.hd * (lc.sliding ? vk_sliding : vk_global),
              double(ntok) * (2.0 * qd + 2.0 * lc.kv * lc.hd) * 2, [&] { return launch_attention(al, st); }),

@@ -55,6 +55,7 @@ struct Workspace {
     // GEMM A-operand views (buffer, column count) with their TMA descriptors.
     DevActivation a_h, a_x16, a_act, a_g;
     std::vector<DevActivation> a_attn;  // one per distinct query width
+    std::vector<std::pair<int, AttnMaps>> attn_maps;  // per KV head count, head-dim-256 layers
     // Pinned host staging.
     int32_t *h_tokens = nullptr, *h_positions = nullptr;
     uint32_t *h_seqs = nullptr, *h_work = nullptr;

@@ -179,6 +179,12 @@ int ge_test_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
     al.half_window = half_window;
     al.queries_per_item = qpi;
     al.err = static_cast<int*>(derr.p);
+    ge::AttnMaps maps;
+    if (hd == 256) {
+        if (!ge::encode_attention_maps(maps, al.q, al.k, al.v, rows, heads, kvh, hd))
+            return fail(GE_ERR_GPU_FAILURE, "tensor map encoding failed");
+        al.maps = &maps;
+    }
     TRY(ge::launch_attention(al, nullptr));
     TRY(cudaDeviceSynchronize());
     int herr = 0;
