@@ -129,7 +129,8 @@ __global__ void __launch_bounds__(256) k_attention_simt(const __half* __restrict
 constexpr int kTcQ = 128;
 constexpr int kTcKeys = 64;
 constexpr int kTcHd = 256;
-constexpr float kRescale = 8.0f;
+constexpr float kRescale = 8.0f;  // log2 units: a stale maximum may leave P up to 2^8
+constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kQBytes = kTcQ * kTcHd * 2;     // 64 KB: 4 chunks of [128 rows][64 dims]
 constexpr int kKVBytes = kTcKeys * kTcHd * 2; // 32 KB per stage: 4 chunks of [64 keys][64 dims]
 constexpr int kPBytes = kTcQ * kTcKeys * 2;   // 16 KB per buffer: [128 rows][64 keys]
@@ -296,7 +297,10 @@ __global__ void __launch_bounds__(192, 1) k_attention_tc(const __grid_constant__
         const int r = quad * 32 + lane;
         const int qi = int(q0) + r;
         const uint32_t lane_base = tmem + (uint32_t(quad * 32) << 16);
-        float m_used = -INFINITY, l = 0.f;
+        // Keys this row sees: [row_lo, row_hi) of its sequence.
+        const int row_lo = p.hw > 0 ? max(qi - p.hw, 0) : 0;
+        const int row_hi = p.hw > 0 ? min(qi + p.hw + 1, int(len)) : int(len);
+        float m_used = -INFINITY, l = 0.f;  // running maximum (log2 units) and sum
         bool ok = true;
         for (int j = 0; j < nblk; j++) {
             const int b = j & 1;
@@ -311,21 +315,29 @@ __global__ void __launch_bounds__(192, 1) k_attention_tc(const __grid_constant__
             tmem_ld32(lane_base + kTmemS + b * kTcKeys + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
             tmem_wait_ld();
             const int kb = k_start + j * kTcKeys;
+            // Scores in log2 units: p = 2^(s log2e - m), one FFMA and one ex2 per key.
             float mb = -INFINITY;
+            if (kb >= row_lo && kb + kTcKeys <= row_hi) {  // every key of the block is visible
 #pragma unroll
-            for (int i = 0; i < 64; i++) {
-                const int kj = kb + i;
-                bool valid = kj < int(len);
-                if (p.hw > 0) valid = valid && abs(qi - kj) <= p.hw;
-                const float s = valid ? __uint_as_float(sr[i]) : -INFINITY;
-                sr[i] = __float_as_uint(s);
-                mb = fmaxf(mb, s);
+                for (int i = 0; i < 64; i++) {
+                    const float t = __uint_as_float(sr[i]) * kLog2e;
+                    sr[i] = __float_as_uint(t);
+                    mb = fmaxf(mb, t);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 64; i++) {
+                    const int kj = kb + i;
+                    const float t = (kj >= row_lo && kj < row_hi) ? __uint_as_float(sr[i]) * kLog2e : -INFINITY;
+                    sr[i] = __float_as_uint(t);
+                    mb = fmaxf(mb, t);
+                }
             }
             // Rescale O when this row's maximum grew past the threshold (warp-uniform decision:
             // tensor-memory loads and stores are warp-collective).
             const bool grow = mb > m_used + kRescale && m_used != -INFINITY;
             if (__any_sync(0xffffffffu, grow)) {
-                const float alpha = grow ? expf(m_used - mb) : 1.0f;
+                const float alpha = grow ? ex2_approx(m_used - mb) : 1.0f;
                 if (j > 0 && !mbar_wait(&pv_done[(j - 1) & 1], uint32_t(((j - 1) >> 1) & 1), p.err)) {
                     ok = false;
                     break;
@@ -354,14 +366,14 @@ __global__ void __launch_bounds__(192, 1) k_attention_tc(const __grid_constant__
             }
             uint8_t* prow = smem + kOffP + b * kPBytes + r * 128;
             float sum = 0.f;
+            const float mu = m_used == -INFINITY ? 0.f : m_used;
 #pragma unroll
             for (int c = 0; c < 8; c++) {  // 8 chunks of 8 keys = 16 bytes each
                 uint32_t w[4];
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
-                    const float s0 = __uint_as_float(sr[c * 8 + 2 * e]), s1 = __uint_as_float(sr[c * 8 + 2 * e + 1]);
-                    const float p0 = s0 == -INFINITY ? 0.f : expf(s0 - m_used);
-                    const float p1 = s1 == -INFINITY ? 0.f : expf(s1 - m_used);
+                    const float p0 = ex2_approx(__uint_as_float(sr[c * 8 + 2 * e]) - mu);   // 2^-inf = 0
+                    const float p1 = ex2_approx(__uint_as_float(sr[c * 8 + 2 * e + 1]) - mu);
                     sum += p0 + p1;
                     __half2 hp = __floats2half2_rn(p0, p1);
                     w[e] = *reinterpret_cast<uint32_t*>(&hp);

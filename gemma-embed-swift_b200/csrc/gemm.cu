@@ -32,7 +32,11 @@ struct GemmLayout {
     static constexpr int kB8 = Q8 ? BN * BK : 0;
     static constexpr int kSc = Q8 ? 2 * BN * 2 : 0;
     static constexpr int kStage = (kA + kB + kB8 + kSc + 1023) / 1024 * 1024;
-    static constexpr int kBarOff = kStages * kStage;
+    // Epilogue staging: per epilogue warp, kStgBufs tiles of 32 rows x 128 bytes that TMA
+    // stores to global memory (one buffer on the Q8 path, whose stages are larger).
+    static constexpr int kStgBufs = Q8 ? 1 : 2;
+    static constexpr int kStgOff = kStages * kStage;
+    static constexpr int kBarOff = kStgOff + 4 * kStgBufs * 4096;
     static constexpr int kBytes = kBarOff + 256 + 1024;  // barriers, TMEM slot, alignment slack
     static constexpr int kThreads = Q8 ? 320 : 192;
 };
@@ -77,7 +81,7 @@ __device__ __forceinline__ void dequant16(uint4 raw, __half2 s2, uint32_t (&o)[8
 template <int BN, int EPI, bool Q8>
 __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-           const __grid_constant__ CUtensorMap mapS, GemmParams p) {
+           const __grid_constant__ CUtensorMap mapS, const __grid_constant__ CUtensorMap mapC, GemmParams p) {
     using L = GemmLayout<BN, Q8>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -109,6 +113,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
         tma_prefetch(&mapA);
         tma_prefetch(&mapB);
         if (Q8) tma_prefetch(&mapS);
+        tma_prefetch(&mapC);
     }
     if (warp == 5) {
         tmem_alloc(tmem_slot, 2 * BN);
@@ -194,67 +199,85 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
         }
     } else if (warp < 4) {
         // ---------------------------------------------------------- epilogue
+        // Each warp owns 32 accumulator rows (its TMEM lane quarter).  Per 128-byte column group
+        // a thread packs its row's values, writes them 128-byte-swizzled into the warp's staging
+        // buffer, and lane 0 TMA-stores the 32 x 128-byte box: full-line writes to global memory.
+        uint8_t* stg = smem + L::kStgOff + warp * L::kStgBufs * 4096;
+        int sbuf = 0;
+        auto emit = [&](const uint32_t (&v)[32], int x, int y) {
+            if (lane == 0) bulk_wait_read<L::kStgBufs - 1>();
+            __syncwarp();
+            uint8_t* buf = stg + sbuf * 4096 + lane * 128;
+#pragma unroll
+            for (int j = 0; j < 8; j++)
+                *reinterpret_cast<uint4*>(buf + ((j ^ (lane & 7)) * 16)) =
+                    make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(&mapC, stg + sbuf * 4096, x, y);
+                bulk_commit();
+            }
+            sbuf = (sbuf + 1 == L::kStgBufs) ? 0 : sbuf + 1;
+        };
         int acc = 0;
         uint32_t acc_ph = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
             if (!mbar_wait(&tfull[acc], acc_ph, p.err)) break;
             tc_fence_after();
             const int m0 = (t / n_tiles) * BM, n0 = (t % n_tiles) * BN;
-            const long row = m0 + warp * 32 + lane;
+            const int y = m0 + warp * 32;
+            const long row = y + lane;
             const uint32_t taddr = tmem + (uint32_t(warp * 32) << 16) + uint32_t(acc * BN);
-            uint32_t r[32];
-            if (EPI == EPI_GEGLU) {
-                uint32_t u[32];
-                __half* out = reinterpret_cast<__half*>(p.out) + row * p.ldo + n0 / 2;
-#pragma unroll 1
-                for (int c = 0; c < BN / 64; c++) {
-                    tmem_ld32(taddr + uint32_t(c * 32), r);
-                    tmem_ld32(taddr + uint32_t(BN / 2 + c * 32), u);
-                    tmem_wait_ld();
-                    uint32_t packed[16];
-#pragma unroll
-                    for (int i = 0; i < 16; i++)
-                        packed[i] = pack_half2(gelu_tanh(__uint_as_float(r[2 * i])) * __uint_as_float(u[2 * i]),
-                                               gelu_tanh(__uint_as_float(r[2 * i + 1])) * __uint_as_float(u[2 * i + 1]));
-                    uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
-#pragma unroll
-                    for (int i = 0; i < 4; i++)
-                        dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
-                }
-            } else {
+            uint32_t r[32], u[32], packed[32];
+            if (EPI == EPI_F32) {
 #pragma unroll 1
                 for (int c = 0; c < BN / 32; c++) {
                     tmem_ld32(taddr + uint32_t(c * 32), r);
                     tmem_wait_ld();
-                    const int col = n0 + c * 32;
-                    if (EPI == EPI_F32) {
-                        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + row * p.ldo + col);
+                    emit(r, n0 + c * 32, y);
+                }
+            } else if (EPI == EPI_GEGLU) {
+                // Columns [0, BN/2) of the tile are gate rows, [BN/2, BN) the matching up rows.
+#pragma unroll 1
+                for (int c = 0; c < BN / 128; c++) {
 #pragma unroll
-                        for (int i = 0; i < 8; i++)
-                            dst[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
-                                                 __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
-                    } else {
-                        uint32_t packed[16];
+                    for (int half = 0; half < 2; half++) {
+                        tmem_ld32(taddr + uint32_t(c * 64 + half * 32), r);
+                        tmem_ld32(taddr + uint32_t(BN / 2 + c * 64 + half * 32), u);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 16; i++)
+                            packed[half * 16 + i] =
+                                pack_half2(gelu_tanh(__uint_as_float(r[2 * i])) * __uint_as_float(u[2 * i]),
+                                           gelu_tanh(__uint_as_float(r[2 * i + 1])) * __uint_as_float(u[2 * i + 1]));
+                    }
+                    emit(packed, n0 / 2 + c * 64, y);
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < BN / 64; c++) {
+#pragma unroll
+                    for (int half = 0; half < 2; half++) {
+                        tmem_ld32(taddr + uint32_t(c * 64 + half * 32), r);
+                        tmem_wait_ld();
                         if (EPI == EPI_GELU_MUL) {
-                            const float4* ax = reinterpret_cast<const float4*>(p.aux + row * p.ldaux + col);
+                            const float4* ax = reinterpret_cast<const float4*>(p.aux + row * p.ldaux + n0 + c * 64 + half * 32);
 #pragma unroll
                             for (int i = 0; i < 8; i++) {
                                 const float4 a = ax[i];
-                                packed[2 * i] = pack_half2(gelu_tanh(__uint_as_float(r[4 * i])) * a.x,
-                                                           gelu_tanh(__uint_as_float(r[4 * i + 1])) * a.y);
-                                packed[2 * i + 1] = pack_half2(gelu_tanh(__uint_as_float(r[4 * i + 2])) * a.z,
-                                                               gelu_tanh(__uint_as_float(r[4 * i + 3])) * a.w);
+                                packed[half * 16 + 2 * i] = pack_half2(gelu_tanh(__uint_as_float(r[4 * i])) * a.x,
+                                                                       gelu_tanh(__uint_as_float(r[4 * i + 1])) * a.y);
+                                packed[half * 16 + 2 * i + 1] = pack_half2(gelu_tanh(__uint_as_float(r[4 * i + 2])) * a.z,
+                                                                           gelu_tanh(__uint_as_float(r[4 * i + 3])) * a.w);
                             }
                         } else {
 #pragma unroll
                             for (int i = 0; i < 16; i++)
-                                packed[i] = pack_half2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+                                packed[half * 16 + i] = pack_half2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
                         }
-                        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__half*>(p.out) + row * p.ldo + col);
-#pragma unroll
-                        for (int i = 0; i < 4; i++)
-                            dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
                     }
+                    emit(packed, n0 + c * 64, y);
                 }
             }
             tc_fence_before();
@@ -264,6 +287,9 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
                 acc_ph ^= 1;
             }
         }
+        // Every store has left shared memory and reached global memory before the CTA exits.
+        if (lane == 0) bulk_wait_all();
+        __syncwarp();
     } else if (Q8) {
         // ---------------------------------------------------------- Q8 -> fp16 converters
         const int tid = threadIdx.x - 192;
@@ -377,7 +403,15 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
     const int tiles = (g.m_rows / BM) * (g.w->N / kBN);
     const int grid = tiles < g.num_sms ? tiles : g.num_sms;
     const CUtensorMap& mb = Q8 ? g.w->map_q8 : g.w->map_f16;
-    kern<<<grid, L::kThreads, L::kBytes, stream>>>(g.a->map, mb, g.w->map_scales, p);
+    // Output map: boxes of 32 rows x 128 bytes (32 fp32 or 64 fp16 columns), 128-byte swizzle.
+    const bool f32 = EPI == EPI_F32;
+    const int out_cols = EPI == EPI_GEGLU ? g.w->N / 2 : g.w->N;
+    if (g.ldo < out_cols) return cudaErrorInvalidValue;
+    CUtensorMap mc;
+    if (!encode_2d(&mc, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, f32 ? 4 : 2, g.out,
+                   uint64_t(g.ldo), uint64_t(g.m_rows), f32 ? 32 : 64, 32, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
+    kern<<<grid, L::kThreads, L::kBytes, stream>>>(g.a->map, mb, g.w->map_scales, mc, p);
     return cudaGetLastError();
 }
 
