@@ -48,6 +48,16 @@ struct GemmParams {
     const float* aux;
     int ldaux;
     int* err;
+    // EPI_QKV
+    int heads, kvh, ntok;
+    float eps;
+    const float *q_norm, *k_norm, *rope;
+    const int32_t* positions;
+};
+
+// Output tensor maps of the epilogue: c0 only, or q, k, v for EPI_QKV.
+struct OutMaps {
+    CUtensorMap c0, c1, c2;
 };
 
 // Waits without giving up on another role's error (used to drain in-flight TMA loads).
@@ -81,7 +91,7 @@ __device__ __forceinline__ void dequant16(uint4 raw, __half2 s2, uint32_t (&o)[8
 template <int BN, int EPI, bool Q8>
 __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-           const __grid_constant__ CUtensorMap mapS, const __grid_constant__ CUtensorMap mapC, GemmParams p) {
+           const __grid_constant__ CUtensorMap mapS, const __grid_constant__ OutMaps outs, GemmParams p) {
     using L = GemmLayout<BN, Q8>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -113,7 +123,11 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
         tma_prefetch(&mapA);
         tma_prefetch(&mapB);
         if (Q8) tma_prefetch(&mapS);
-        tma_prefetch(&mapC);
+        tma_prefetch(&outs.c0);
+        if (EPI == EPI_QKV) {
+            tma_prefetch(&outs.c1);
+            tma_prefetch(&outs.c2);
+        }
     }
     if (warp == 5) {
         tmem_alloc(tmem_slot, 2 * BN);
@@ -204,7 +218,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
         // buffer, and lane 0 TMA-stores the 32 x 128-byte box: full-line writes to global memory.
         uint8_t* stg = smem + L::kStgOff + warp * L::kStgBufs * 4096;
         int sbuf = 0;
-        auto emit = [&](const uint32_t (&v)[32], int x, int y) {
+        auto emit = [&](const uint32_t (&v)[32], int x, int y, const CUtensorMap* map) {
             if (lane == 0) bulk_wait_read<L::kStgBufs - 1>();
             __syncwarp();
             uint8_t* buf = stg + sbuf * 4096 + lane * 128;
@@ -215,7 +229,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-                tma_store_2d(&mapC, stg + sbuf * 4096, x, y);
+                tma_store_2d(map, stg + sbuf * 4096, x, y);
                 bulk_commit();
             }
             sbuf = (sbuf + 1 == L::kStgBufs) ? 0 : sbuf + 1;
@@ -235,7 +249,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
                 for (int c = 0; c < BN / 32; c++) {
                     tmem_ld32(taddr + uint32_t(c * 32), r);
                     tmem_wait_ld();
-                    emit(r, n0 + c * 32, y);
+                    emit(r, n0 + c * 32, y, &outs.c0);
                 }
             } else if (EPI == EPI_GEGLU) {
                 // Columns [0, BN/2) of the tile are gate rows, [BN/2, BN) the matching up rows.
@@ -252,9 +266,9 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
                                 pack_half2(gelu_tanh(__uint_as_float(r[2 * i])) * __uint_as_float(u[2 * i]),
                                            gelu_tanh(__uint_as_float(r[2 * i + 1])) * __uint_as_float(u[2 * i + 1]));
                     }
-                    emit(packed, n0 / 2 + c * 64, y);
+                    emit(packed, n0 / 2 + c * 64, y, &outs.c0);
                 }
-            } else {
+            } else if (EPI == EPI_F16 || EPI == EPI_GELU_MUL) {
 #pragma unroll 1
                 for (int c = 0; c < BN / 64; c++) {
 #pragma unroll
@@ -277,7 +291,69 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
                                 packed[half * 16 + i] = pack_half2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
                         }
                     }
-                    emit(packed, n0 + c * 64, y);
+                    emit(packed, n0 + c * 64, y, &outs.c0);
+                }
+            } else if (EPI == EPI_QKV) {
+                // One head per tile: slot < heads is a query head, then key heads, then value heads.
+                const int slot = n0 / BN;
+                const CUtensorMap* dst = &outs.c2;
+                const float* w = nullptr;
+                int xbase = (slot - p.heads - p.kvh) * BN;
+                if (slot < p.heads) {
+                    dst = &outs.c0;
+                    w = p.q_norm;
+                    xbase = slot * BN;
+                } else if (slot < p.heads + p.kvh) {
+                    dst = &outs.c1;
+                    w = p.k_norm;
+                    xbase = (slot - p.heads) * BN;
+                }
+                float ss = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; c++) {
+                    tmem_ld32(taddr + uint32_t(c * 32), r);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 32; i++) ss += __uint_as_float(r[i]) * __uint_as_float(r[i]);
+                }
+                const float inv = 1.0f / sqrtf(ss / float(BN) + p.eps);
+                const int pos = row < p.ntok ? p.positions[row] : 0;
+                const float* cs = p.rope + long(pos) * BN;  // [pair][cos, sin]
+                // Output column groups [64cc, 64cc + 64) and their rotation partners 128 apart.
+#pragma unroll 1
+                for (int cc = 0; cc < BN / 128; cc++) {
+                    uint32_t hi[32];
+#pragma unroll
+                    for (int half = 0; half < 2; half++) {
+                        const int c = 2 * cc + half;
+                        tmem_ld32(taddr + uint32_t(c * 32), r);
+                        tmem_ld32(taddr + uint32_t(BN / 2 + c * 32), u);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; i += 2) {
+                            float o[4];
+#pragma unroll
+                            for (int e = 0; e < 2; e++) {
+                                const int col = c * 32 + i + e;
+                                float a = __uint_as_float(r[i + e]) * inv;
+                                float b = __uint_as_float(u[i + e]) * inv;
+                                if (w) {
+                                    a = a * w[col];
+                                    b = b * w[col + BN / 2];
+                                    const float cv = cs[2 * col], sv = cs[2 * col + 1];
+                                    o[e] = a * cv - b * sv;
+                                    o[2 + e] = a * sv + b * cv;
+                                } else {
+                                    o[e] = a;
+                                    o[2 + e] = b;
+                                }
+                            }
+                            packed[half * 16 + i / 2] = pack_half2(o[0], o[1]);
+                            hi[half * 16 + i / 2] = pack_half2(o[2], o[3]);
+                        }
+                    }
+                    emit(packed, xbase + cc * 64, y, dst);
+                    emit(hi, xbase + BN / 2 + cc * 64, y, dst);
                 }
             }
             tc_fence_before();
@@ -399,18 +475,46 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
         if (e != cudaSuccess) return e;
         configured |= 1u << dev;
     }
-    GemmParams p{g.m_rows, g.w->N, g.w->K, g.out, g.ldo, g.aux, g.ldaux, g.err};
+    GemmParams p{};
+    p.M = g.m_rows;
+    p.N = g.w->N;
+    p.K = g.w->K;
+    p.out = g.out;
+    p.ldo = g.ldo;
+    p.aux = g.aux;
+    p.ldaux = g.ldaux;
+    p.err = g.err;
     const int tiles = (g.m_rows / BM) * (g.w->N / kBN);
     const int grid = tiles < g.num_sms ? tiles : g.num_sms;
     const CUtensorMap& mb = Q8 ? g.w->map_q8 : g.w->map_f16;
-    // Output map: boxes of 32 rows x 128 bytes (32 fp32 or 64 fp16 columns), 128-byte swizzle.
-    const bool f32 = EPI == EPI_F32;
-    const int out_cols = EPI == EPI_GEGLU ? g.w->N / 2 : g.w->N;
-    if (g.ldo < out_cols) return cudaErrorInvalidValue;
-    CUtensorMap mc;
-    if (!encode_2d(&mc, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, f32 ? 4 : 2, g.out,
-                   uint64_t(g.ldo), uint64_t(g.m_rows), f32 ? 32 : 64, 32, CU_TENSOR_MAP_SWIZZLE_128B))
-        return cudaErrorInvalidValue;
+    // Output maps: boxes of 32 rows x 128 bytes (32 fp32 or 64 fp16 columns), 128-byte swizzle.
+    OutMaps mc;
+    if (EPI == EPI_QKV) {
+        const QkvEpilogue& q = *g.qkv;
+        if (g.w->N != (q.heads + 2 * q.kv_heads) * kBN) return cudaErrorInvalidValue;
+        if (!encode_2d(&mc.c0, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q.q, uint64_t(q.heads) * kBN, uint64_t(g.m_rows), 64, 32,
+                       CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !encode_2d(&mc.c1, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q.k, uint64_t(q.kv_heads) * kBN, uint64_t(g.m_rows), 64,
+                       32, CU_TENSOR_MAP_SWIZZLE_128B) ||
+            !encode_2d(&mc.c2, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q.v, uint64_t(q.kv_heads) * kBN, uint64_t(g.m_rows), 64,
+                       32, CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorInvalidValue;
+        p.heads = q.heads;
+        p.kvh = q.kv_heads;
+        p.ntok = q.ntok;
+        p.eps = q.eps;
+        p.q_norm = q.q_norm;
+        p.k_norm = q.k_norm;
+        p.rope = q.rope;
+        p.positions = q.positions;
+    } else {
+        const bool f32 = EPI == EPI_F32;
+        const int out_cols = EPI == EPI_GEGLU ? g.w->N / 2 : g.w->N;
+        if (g.ldo < out_cols) return cudaErrorInvalidValue;
+        if (!encode_2d(&mc.c0, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, f32 ? 4 : 2, g.out,
+                       uint64_t(g.ldo), uint64_t(g.m_rows), f32 ? 32 : 64, 32, CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorInvalidValue;
+    }
     kern<<<grid, L::kThreads, L::kBytes, stream>>>(g.a->map, mb, g.w->map_scales, mc, p);
     return cudaGetLastError();
 }
@@ -427,6 +531,9 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream) {
     case EPI_F16: return q8 ? launch_t<EPI_F16, true>(g, stream) : launch_t<EPI_F16, false>(g, stream);
     case EPI_GEGLU: return q8 ? launch_t<EPI_GEGLU, true>(g, stream) : launch_t<EPI_GEGLU, false>(g, stream);
     case EPI_GELU_MUL: return q8 ? launch_t<EPI_GELU_MUL, true>(g, stream) : launch_t<EPI_GELU_MUL, false>(g, stream);
+    case EPI_QKV:
+        if (!g.qkv) return cudaErrorInvalidValue;
+        return q8 ? launch_t<EPI_QKV, true>(g, stream) : launch_t<EPI_QKV, false>(g, stream);
     default: return cudaErrorInvalidValue;
     }
 }

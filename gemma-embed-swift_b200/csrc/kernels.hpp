@@ -17,6 +17,19 @@ enum GemmEpilogue : int {
     EPI_F16 = 1,    // out[m][n] = acc (fp16)
     EPI_GEGLU = 2,  // weight rows interleave gate and up in blocks of BN/2: out = gelu(gate) * up (fp16)
     EPI_GELU_MUL = 3,  // out = gelu(acc) * aux[m][n] (fp16), aux fp32 with row stride ldaux
+    EPI_QKV = 4,       // 256-wide head tiles of [q heads | k heads | v heads]: per-head RMSNorm,
+                       // weighted and NeoX-rotated for q and k, unweighted for v -> fp16 q, k, v
+};
+
+// Outputs and constants of the fused q/k/v epilogue (CPUReference.swift:225-235).
+struct QkvEpilogue {
+    __half *q = nullptr, *k = nullptr, *v = nullptr;  // [rows][heads * 256], [rows][kv * 256] x 2
+    int heads = 0, kv_heads = 0;
+    const float *q_norm = nullptr, *k_norm = nullptr;
+    const int32_t* positions = nullptr;  // RoPE position of each token row
+    const float* rope = nullptr;         // [positions][128][cos, sin]
+    int ntok = 0;                        // rows at or past ntok are padding (position 0)
+    float eps = 1e-6f;
 };
 
 // One GEMM weight as the device keeps it: the Q8_0 planes (int8 values [N][K] and the fp16
@@ -53,6 +66,7 @@ struct GemmLaunch {
     bool use_q8 = false;  // dequantise Q8 tiles in shared memory instead of reading fp16 weights
     int* err;
     int num_sms;
+    const QkvEpilogue* qkv = nullptr;  // EPI_QKV only
 };
 cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream);
 

@@ -738,7 +738,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     const int D = c.hidden;
     const bool q8 = rows <= kQ8GemmMaxRows || (m->flags & GE_LOAD_Q8_ONLY);
     auto gemm = [&](const DevActivation& A, const DevWeight& W, void* out, int ldo, int epi, const float* aux = nullptr,
-                    int ldaux = 0) {
+                    int ldaux = 0, const QkvEpilogue* qkv = nullptr) {
         GemmLaunch g;
         g.a = &A;
         g.w = &W;
@@ -751,6 +751,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         g.use_q8 = q8;
         g.err = d.err;
         g.num_sms = d.num_sms;
+        g.qkv = qkv;
         return launch_gemm(g, st);
     };
 #define CK(expr, what)                                  \
@@ -830,15 +831,34 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         const LayerCfg& lc = c.layer[l];
         const LayerDev& L = d.layers[l];
         const int qd = c.heads * lc.hd;
-        CK(K("gemm_qkv", gemm_flops(L.qkv), gemm_bytes(L.qkv, 4),
-             [&] { return gemm(ws.a_h, L.qkv, ws.qkv, L.qkv.N, EPI_F32); }),
-           "qkv projection");
-        CK(K("qkv_norm_rope", 0, double(ntok) * L.qkv.N * 6,
-             [&] {
-                 return launch_qkv_norm_rope(ws.qkv, ntok, rows, c.heads, lc.kv, lc.hd, L.q_norm, L.k_norm, ws.positions,
-                                             d.rope[lc.rope_index], c.eps, ws.q, ws.k, ws.v, st);
-             }),
-           "q/k/v norm and rope");
+        if (lc.hd == 256) {
+            // Projection, per-head norms and RoPE in one kernel: the epilogue writes fp16 q, k, v.
+            QkvEpilogue qe;
+            qe.q = ws.q;
+            qe.k = ws.k;
+            qe.v = ws.v;
+            qe.heads = c.heads;
+            qe.kv_heads = lc.kv;
+            qe.q_norm = L.q_norm;
+            qe.k_norm = L.k_norm;
+            qe.positions = ws.positions;
+            qe.rope = d.rope[lc.rope_index];
+            qe.ntok = ntok;
+            qe.eps = c.eps;
+            CK(K("gemm_qkv_norm_rope", gemm_flops(L.qkv), gemm_bytes(L.qkv, 2),
+                 [&] { return gemm(ws.a_h, L.qkv, nullptr, 0, EPI_QKV, nullptr, 0, &qe); }),
+               "qkv projection");
+        } else {
+            CK(K("gemm_qkv", gemm_flops(L.qkv), gemm_bytes(L.qkv, 4),
+                 [&] { return gemm(ws.a_h, L.qkv, ws.qkv, L.qkv.N, EPI_F32); }),
+               "qkv projection");
+            CK(K("qkv_norm_rope", 0, double(ntok) * L.qkv.N * 6,
+                 [&] {
+                     return launch_qkv_norm_rope(ws.qkv, ntok, rows, c.heads, lc.kv, lc.hd, L.q_norm, L.k_norm,
+                                                 ws.positions, d.rope[lc.rope_index], c.eps, ws.q, ws.k, ws.v, st);
+                 }),
+               "q/k/v norm and rope");
+        }
         AttnLaunch al;
         al.q = ws.q;
         al.k = ws.k;
