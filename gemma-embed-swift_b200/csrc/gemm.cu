@@ -53,6 +53,7 @@ struct GemmParams {
     float eps;
     const float *q_norm, *k_norm, *rope;
     const int32_t* positions;
+    int rope_positions;
 };
 
 // Output tensor maps of the epilogue: c0 only, or q, k, v for EPI_QKV.
@@ -234,6 +235,26 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
             }
             sbuf = (sbuf + 1 == L::kStgBufs) ? 0 : sbuf + 1;
         };
+        // Piecewise staging: open the next buffer, put 16-byte chunks of this thread's row,
+        // then store the 32 x 128-byte box.
+        uint8_t* open_buf = nullptr;
+        auto stg_begin = [&]() {
+            if (lane == 0) bulk_wait_read<L::kStgBufs - 1>();
+            __syncwarp();
+            open_buf = stg + sbuf * 4096;
+        };
+        auto stg_put = [&](int j, uint4 v) {
+            *reinterpret_cast<uint4*>(open_buf + lane * 128 + ((j ^ (lane & 7)) * 16)) = v;
+        };
+        auto stg_end = [&](int x, int y, const CUtensorMap* map) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(map, open_buf, x, y);
+                bulk_commit();
+            }
+            sbuf = (sbuf + 1 == L::kStgBufs) ? 0 : sbuf + 1;
+        };
         int acc = 0;
         uint32_t acc_ph = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
@@ -318,42 +339,46 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
                 }
                 const float inv = 1.0f / sqrtf(ss / float(BN) + p.eps);
                 const int pos = row < p.ntok ? p.positions[row] : 0;
-                const float* cs = p.rope + long(pos) * BN;  // [pair][cos, sin]
-                // Output column groups [64cc, 64cc + 64) and their rotation partners 128 apart.
+                // Pair-major table [pair][position][cos, sin]: the 32 rows of a warp are mostly
+                // consecutive positions, so each pair's load is one contiguous line per warp.
+                const float2* cs = reinterpret_cast<const float2*>(p.rope) + pos;
+                // Output boxes of 64 columns: the low half [64cc, 64cc + 64) of the head and its
+                // rotation partners 128 columns up.  Each is written 16 columns at a time.
 #pragma unroll 1
-                for (int cc = 0; cc < BN / 128; cc++) {
-                    uint32_t hi[32];
-#pragma unroll
-                    for (int half = 0; half < 2; half++) {
-                        const int c = 2 * cc + half;
-                        tmem_ld32(taddr + uint32_t(c * 32), r);
-                        tmem_ld32(taddr + uint32_t(BN / 2 + c * 32), u);
+                for (int box = 0; box < BN / 64; box++) {
+                    const int cc = box >> 1, side = box & 1;
+                    stg_begin();
+#pragma unroll 1
+                    for (int qd = 0; qd < 4; qd++) {
+                        const int col0 = cc * 64 + qd * 16;
+                        uint32_t ra[16], rb[16];
+                        tmem_ld16(taddr + uint32_t(col0), ra);
+                        tmem_ld16(taddr + uint32_t(BN / 2 + col0), rb);
                         tmem_wait_ld();
+                        uint32_t pk[8];
 #pragma unroll
-                        for (int i = 0; i < 32; i += 2) {
-                            float o[4];
+                        for (int i = 0; i < 16; i += 2) {
+                            float o[2];
 #pragma unroll
                             for (int e = 0; e < 2; e++) {
-                                const int col = c * 32 + i + e;
-                                float a = __uint_as_float(r[i + e]) * inv;
-                                float b = __uint_as_float(u[i + e]) * inv;
+                                const int col = col0 + i + e;
+                                float a = __uint_as_float(ra[i + e]) * inv;
+                                float b = __uint_as_float(rb[i + e]) * inv;
                                 if (w) {
                                     a = a * w[col];
                                     b = b * w[col + BN / 2];
-                                    const float cv = cs[2 * col], sv = cs[2 * col + 1];
-                                    o[e] = a * cv - b * sv;
-                                    o[2 + e] = a * sv + b * cv;
+                                    const float2 tcs = cs[long(col) * p.rope_positions];
+                                    o[e] = side == 0 ? a * tcs.x - b * tcs.y : a * tcs.y + b * tcs.x;
                                 } else {
-                                    o[e] = a;
-                                    o[2 + e] = b;
+                                    o[e] = side == 0 ? a : b;
                                 }
                             }
-                            packed[half * 16 + i / 2] = pack_half2(o[0], o[1]);
-                            hi[half * 16 + i / 2] = pack_half2(o[2], o[3]);
+                            pk[i / 2] = pack_half2(o[0], o[1]);
                         }
+                        stg_put(2 * qd, make_uint4(pk[0], pk[1], pk[2], pk[3]));
+                        stg_put(2 * qd + 1, make_uint4(pk[4], pk[5], pk[6], pk[7]));
                     }
-                    emit(packed, xbase + cc * 64, y, dst);
-                    emit(hi, xbase + BN / 2 + cc * 64, y, dst);
+                    stg_end(xbase + side * (BN / 2) + cc * 64, y, dst);
                 }
             }
             tc_fence_before();
@@ -505,7 +530,8 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
         p.eps = q.eps;
         p.q_norm = q.q_norm;
         p.k_norm = q.k_norm;
-        p.rope = q.rope;
+        p.rope = q.rope_t;
+        p.rope_positions = q.rope_positions;
         p.positions = q.positions;
     } else {
         const bool f32 = EPI == EPI_F32;

@@ -27,7 +27,8 @@ struct QkvEpilogue {
     int heads = 0, kv_heads = 0;
     const float *q_norm = nullptr, *k_norm = nullptr;
     const int32_t* positions = nullptr;  // RoPE position of each token row
-    const float* rope = nullptr;         // [positions][128][cos, sin]
+    const float* rope_t = nullptr;       // [128 pairs][rope_positions][cos, sin]
+    int rope_positions = 0;
     int ntok = 0;                        // rows at or past ntok are padding (position 0)
     float eps = 1e-6f;
 };

@@ -470,10 +470,20 @@ static int load_device(ge_model* m, Device& d, const std::vector<HostWeight>& hw
         if ((e = upload_weight(d, d.plp, *plp)) != cudaSuccess) return fail(e);
     }
     if (norm_err != cudaSuccess) return fail(norm_err);
-    for (auto& r : ropes) {
+    for (size_t ri = 0; ri < ropes.size(); ri++) {
+        const std::vector<float>& r = ropes[ri];
         float* p = nullptr;
         if ((e = dev_upload(d, &p, r.data(), r.size())) != cudaSuccess) return fail(e);
         d.rope.push_back(p);
+        const int pairs = c.ropes[ri].first / 2;
+        std::vector<float> t(r.size());
+        for (int pos = 0; pos < c.max_tokens; pos++)
+            for (int i = 0; i < pairs; i++) {
+                t[(size_t(i) * c.max_tokens + pos) * 2] = r[(size_t(pos) * pairs + i) * 2];
+                t[(size_t(i) * c.max_tokens + pos) * 2 + 1] = r[(size_t(pos) * pairs + i) * 2 + 1];
+            }
+        if ((e = dev_upload(d, &p, t.data(), t.size())) != cudaSuccess) return fail(e);
+        d.rope_t.push_back(p);
     }
     if (c.has_dense) {
         if ((e = dev_upload(d, &d.dense2, dense2.data(), dense2.size())) != cudaSuccess) return fail(e);
@@ -842,7 +852,8 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
             qe.q_norm = L.q_norm;
             qe.k_norm = L.k_norm;
             qe.positions = ws.positions;
-            qe.rope = d.rope[lc.rope_index];
+            qe.rope_t = d.rope_t[lc.rope_index];
+            qe.rope_positions = c.max_tokens;
             qe.ntok = ntok;
             qe.eps = c.eps;
             CK(K("gemm_qkv_norm_rope", gemm_flops(L.qkv), gemm_bytes(L.qkv, 2),

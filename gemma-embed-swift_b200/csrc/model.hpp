@@ -73,7 +73,8 @@ struct Device {
     DevWeight plp;  // per_layer_model_proj (fp16 only)
     float *pl_norm = nullptr, *out_norm = nullptr;
     float *dense2 = nullptr, *dense3 = nullptr, *output = nullptr;  // fp32 [N][K]
-    std::vector<float*> rope;
+    std::vector<float*> rope;    // per table: [position][pair][cos, sin]
+    std::vector<float*> rope_t;  // per table: [pair][position][cos, sin]
     int* err = nullptr;
     Workspace ws;
     std::vector<void*> allocations;

@@ -56,12 +56,14 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
     if (mbar_test(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
-    while (true) {
+    for (uint32_t spin = 1;; spin++) {
         if (mbar_test(bar, parity)) return true;
-        if (*reinterpret_cast<volatile int*>(err) != 0) return false;
-        if (globaltimer() - t0 > kWaitLimitNs) {
-            atomicCAS(err, 0, kErrTimeout);
-            return false;
+        if ((spin & 63) == 0) {  // the error word and the clock are checked every 64 tries
+            if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+            if (globaltimer() - t0 > kWaitLimitNs) {
+                atomicCAS(err, 0, kErrTimeout);
+                return false;
+            }
         }
     }
 }
@@ -165,6 +167,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
           "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
           "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
           "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr)
         : "memory");
 }
