@@ -61,7 +61,7 @@ cudaError_t launch_embed(const int32_t* tokens, int ntok, int rows, const int8_t
 // One warp per (token, head slot): slots [0, H) are query heads, [H, H+KV) key heads,
 // [H+KV, H+2KV) value heads of the fused projection row.  CPUReference.swift:225-235.
 template <int HD>
-__global__ void k_qkv_norm_rope(const float* __restrict__ qkv, int ntok, int rows, int heads, int kvh,
+__global__ void k_qkv_norm_rope(const __half* __restrict__ qkv, int ntok, int rows, int heads, int kvh,
                                 const float* __restrict__ qw, const float* __restrict__ kw,
                                 const int32_t* __restrict__ pos, const float* __restrict__ rope, float eps,
                                 __half* __restrict__ q, __half* __restrict__ k, __half* __restrict__ v) {
@@ -87,12 +87,12 @@ __global__ void k_qkv_norm_rope(const float* __restrict__ qkv, int ntok, int row
         for (int j = 0; j < PER; j++) dst[lane + 32 * j] = __float2half_rn(0.f);
         return;
     }
-    const float* src = qkv + long(row) * slots * HD + slot * HD;
+    const __half* src = qkv + long(row) * slots * HD + slot * HD;
     float e[PER];
     float ss = 0.f;
 #pragma unroll
     for (int j = 0; j < PER; j++) {
-        e[j] = src[lane + 32 * j];
+        e[j] = __half2float(src[lane + 32 * j]);
         ss += e[j] * e[j];
     }
     ss = warp_sum(ss);
@@ -115,7 +115,7 @@ __global__ void k_qkv_norm_rope(const float* __restrict__ qkv, int ntok, int row
     for (int j = 0; j < PER; j++) dst[lane + 32 * j] = __float2half_rn(e[j]);
 }
 
-cudaError_t launch_qkv_norm_rope(const float* qkv, int ntok, int rows, int heads, int kv_heads, int hd,
+cudaError_t launch_qkv_norm_rope(const __half* qkv, int ntok, int rows, int heads, int kv_heads, int hd,
                                       const float* q_w, const float* k_w, const int32_t* positions, const float* rope,
                                       float eps, __half* q, __half* k, __half* v, cudaStream_t stream) {
     if (rows <= 0) return cudaSuccess;
@@ -133,43 +133,100 @@ cudaError_t launch_qkv_norm_rope(const float* qkv, int ntok, int rows, int heads
 }
 
 // x = (x + rmsnorm(t) * w_post) * scale, then optionally the next norm of x.
-// CPUReference.swift:239-243, 252-256, 266-269 and Elementwise.metal:260-354.
-__global__ void k_residual_norm(float* __restrict__ x, const float* __restrict__ t, int rows, int width,
+// CPUReference.swift:239-243, 252-256, 266-269 and Elementwise.metal:260-354.  One warp per
+// row; lane l holds the 8-element groups l, l + 32, ... (W / 256 groups) in registers.
+template <int W>
+__global__ void k_residual_norm(float* __restrict__ x, const __half* __restrict__ t, int rows,
                                 const float* __restrict__ wp, float scale, const float* __restrict__ wn, float eps,
                                 __half* __restrict__ h16, float* __restrict__ y32, __half* __restrict__ x16) {
+    constexpr int G = W / 256;  // groups of 8 per lane
     const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
-    float* xr = x + long(row) * width;
-    const float* tr = t + long(row) * width;
+    float* xr = x + long(row) * W;
+    const __half* tr = t + long(row) * W;
+    float tv[G][8], xv[G][8];
     float ss = 0.f;
-    for (int i = lane; i < width; i += 32) ss += tr[i] * tr[i];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        const int c = (lane + 32 * g) * 8;
+        const uint4 raw = *reinterpret_cast<const uint4*>(tr + c);
+        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float2 f = __half22float2(h2[i]);
+            tv[g][2 * i] = f.x;
+            tv[g][2 * i + 1] = f.y;
+            ss += f.x * f.x + f.y * f.y;
+        }
+        const float4 a = *reinterpret_cast<const float4*>(xr + c);
+        const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
+        xv[g][0] = a.x; xv[g][1] = a.y; xv[g][2] = a.z; xv[g][3] = a.w;
+        xv[g][4] = b.x; xv[g][5] = b.y; xv[g][6] = b.z; xv[g][7] = b.w;
+    }
     ss = warp_sum(ss);
-    const float inv = 1.0f / sqrtf(ss / float(width) + eps);
+    const float inv = 1.0f / sqrtf(ss / float(W) + eps);
     float ss2 = 0.f;
-    for (int i = lane; i < width; i += 32) {
-        float v = xr[i] + tr[i] * inv * wp[i];
-        if (scale != 1.0f) v *= scale;
-        xr[i] = v;
-        ss2 += v * v;
-        if (x16) x16[long(row) * width + i] = __float2half_rn(v);
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        const int c = (lane + 32 * g) * 8;
+        const float4 w0 = *reinterpret_cast<const float4*>(wp + c);
+        const float4 w1 = *reinterpret_cast<const float4*>(wp + c + 4);
+        const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            float v = xv[g][i] + tv[g][i] * inv * ww[i];
+            if (scale != 1.0f) v *= scale;
+            xv[g][i] = v;
+            ss2 += v * v;
+        }
+        *reinterpret_cast<float4*>(xr + c) = make_float4(xv[g][0], xv[g][1], xv[g][2], xv[g][3]);
+        *reinterpret_cast<float4*>(xr + c + 4) = make_float4(xv[g][4], xv[g][5], xv[g][6], xv[g][7]);
+        if (x16) {
+            uint4 o;
+            __half2* o2 = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+            for (int i = 0; i < 4; i++) o2[i] = __floats2half2_rn(xv[g][2 * i], xv[g][2 * i + 1]);
+            *reinterpret_cast<uint4*>(x16 + long(row) * W + c) = o;
+        }
     }
     if (!wn) return;
     ss2 = warp_sum(ss2);
-    const float inv2 = 1.0f / sqrtf(ss2 / float(width) + eps);
-    for (int i = lane; i < width; i += 32) {
-        const float y = xr[i] * inv2 * wn[i];
-        if (h16) h16[long(row) * width + i] = __float2half_rn(y);
-        if (y32) y32[long(row) * width + i] = y;
+    const float inv2 = 1.0f / sqrtf(ss2 / float(W) + eps);
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        const int c = (lane + 32 * g) * 8;
+        const float4 w0 = *reinterpret_cast<const float4*>(wn + c);
+        const float4 w1 = *reinterpret_cast<const float4*>(wn + c + 4);
+        const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        float y[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) y[i] = xv[g][i] * inv2 * ww[i];
+        if (h16) {
+            uint4 o;
+            __half2* o2 = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+            for (int i = 0; i < 4; i++) o2[i] = __floats2half2_rn(y[2 * i], y[2 * i + 1]);
+            *reinterpret_cast<uint4*>(h16 + long(row) * W + c) = o;
+        }
+        if (y32) {
+            *reinterpret_cast<float4*>(y32 + long(row) * W + c) = make_float4(y[0], y[1], y[2], y[3]);
+            *reinterpret_cast<float4*>(y32 + long(row) * W + c + 4) = make_float4(y[4], y[5], y[6], y[7]);
+        }
     }
 }
 
-cudaError_t launch_residual_norm(float* x, const float* t, int rows, int width, const float* w_post, float scale,
+cudaError_t launch_residual_norm(float* x, const __half* t, int rows, int width, const float* w_post, float scale,
                                  const float* w_next, float eps, __half* h16, float* y32, __half* x16,
                                  cudaStream_t stream) {
     if (rows <= 0) return cudaSuccess;
-    k_residual_norm<<<(rows + kRowsPerBlock - 1) / kRowsPerBlock, 256, 0, stream>>>(x, t, rows, width, w_post, scale,
-                                                                                     w_next, eps, h16, y32, x16);
+    const int blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
+    if (width == 768)
+        k_residual_norm<768><<<blocks, 256, 0, stream>>>(x, t, rows, w_post, scale, w_next, eps, h16, y32, x16);
+    else if (width == 512)
+        k_residual_norm<512><<<blocks, 256, 0, stream>>>(x, t, rows, w_post, scale, w_next, eps, h16, y32, x16);
+    else
+        return cudaErrorInvalidValue;
     return cudaGetLastError();
 }
 
@@ -199,13 +256,29 @@ cudaError_t launch_rmsnorm_rows(const float* x, int rows, int width, float pre, 
     return cudaGetLastError();
 }
 
-// pooled[s][c] = sum over the sequence's rows / length (Elementwise.metal:243-256).
+// pooled[s][c] = sum over the sequence's rows / length (Elementwise.metal:243-256).  One
+// block per sequence: warp w sums rows w, w + 8, ... of every column, then the 8 partial sums
+// of a column are added in warp order, so a sequence's mean depends only on its own rows.
 __global__ void k_mean_pool(const float* __restrict__ y, int width, const uint32_t* __restrict__ seqs,
                             float* __restrict__ pooled) {
+    extern __shared__ float part[];  // [8][width]
     const uint32_t start = seqs[2 * blockIdx.x], len = seqs[2 * blockIdx.x + 1];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int c0 = lane * 4; c0 < width; c0 += 128) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (uint32_t r = warp; r < len; r += 8) {
+            const float4 v = *reinterpret_cast<const float4*>(y + long(start + r) * width + c0);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        *reinterpret_cast<float4*>(part + warp * width + c0) = acc;
+    }
+    __syncthreads();
     for (int c = threadIdx.x; c < width; c += blockDim.x) {
         float acc = 0.f;
-        for (uint32_t r = 0; r < len; r++) acc += y[long(start + r) * width + c];
+        for (int w = 0; w < 8; w++) acc += part[w * width + c];
         pooled[long(blockIdx.x) * width + c] = acc / float(len);
     }
 }
@@ -213,7 +286,8 @@ __global__ void k_mean_pool(const float* __restrict__ y, int width, const uint32
 cudaError_t launch_mean_pool(const float* y, int width, const uint32_t* seqs, int nseq, float* pooled,
                              cudaStream_t stream) {
     if (nseq <= 0) return cudaSuccess;
-    k_mean_pool<<<nseq, 256, 0, stream>>>(y, width, seqs, pooled);
+    if (width % 128) return cudaErrorInvalidValue;
+    k_mean_pool<<<nseq, 256, 8 * width * sizeof(float), stream>>>(y, width, seqs, pooled);
     return cudaGetLastError();
 }
 
@@ -256,25 +330,39 @@ cudaError_t launch_positions(const uint32_t* seqs, int nseq, int32_t* positions,
     return cudaGetLastError();
 }
 
-// out[s][n] = sum_k in[s][k] * w[n][k] in fp32 with an fp32 weight matrix: one warp per n.
+// out[s][n] = sum_k in[s][k] * w[n][k] in fp32 with an fp32 weight matrix: one warp per n,
+// four input rows per pass so each weight load feeds four independent sums.
 __global__ void k_dense_f32(const float* __restrict__ in, int nrows, const float* __restrict__ w, int N, int K,
                             float* __restrict__ out) {
     const int n = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (n >= N) return;
     const float* wr = w + long(n) * K;
-    for (int s = 0; s < nrows; s++) {
-        const float* xr = in + long(s) * K;
-        float acc = 0.f;
-        for (int k = lane; k < K; k += 32) acc += xr[k] * wr[k];
-        acc = warp_sum(acc);
-        if (lane == 0) out[long(s) * N + n] = acc;
+    for (int s0 = 0; s0 < nrows; s0 += 4) {
+        const int ns = min(4, nrows - s0);
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int k = lane * 4; k < K; k += 128) {
+            const float4 wv = *reinterpret_cast<const float4*>(wr + k);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                if (j < ns) {
+                    const float4 xv = *reinterpret_cast<const float4*>(in + long(s0 + j) * K + k);
+                    acc[j] += xv.x * wv.x + xv.y * wv.y + xv.z * wv.z + xv.w * wv.w;
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const float v = warp_sum(acc[j]);
+            if (lane == 0 && j < ns) out[long(s0 + j) * N + n] = v;
+        }
     }
 }
 
 cudaError_t launch_dense_f32(const float* in, int nrows, const float* w, int N, int K, float* out,
                              cudaStream_t stream) {
     if (nrows <= 0) return cudaSuccess;
+    if (K % 128) return cudaErrorInvalidValue;
     k_dense_f32<<<(N + kRowsPerBlock - 1) / kRowsPerBlock, 256, 0, stream>>>(in, nrows, w, N, K, out);
     return cudaGetLastError();
 }

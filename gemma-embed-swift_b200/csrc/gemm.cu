@@ -48,17 +48,6 @@ struct GemmParams {
     const float* aux;
     int ldaux;
     int* err;
-    // EPI_QKV
-    int heads, kvh, ntok;
-    float eps;
-    const float *q_norm, *k_norm, *rope;
-    const int32_t* positions;
-    int rope_positions;
-};
-
-// Output tensor maps of the epilogue: c0 only, or q, k, v for EPI_QKV.
-struct OutMaps {
-    CUtensorMap c0, c1, c2;
 };
 
 // Waits without giving up on another role's error (used to drain in-flight TMA loads).
@@ -92,7 +81,7 @@ __device__ __forceinline__ void dequant16(uint4 raw, __half2 s2, uint32_t (&o)[8
 template <int BN, int EPI, bool Q8>
 __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-           const __grid_constant__ CUtensorMap mapS, const __grid_constant__ OutMaps outs, GemmParams p) {
+           const __grid_constant__ CUtensorMap mapS, const __grid_constant__ CUtensorMap mapC, GemmParams p) {
     using L = GemmLayout<BN, Q8>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -124,11 +113,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
         tma_prefetch(&mapA);
         tma_prefetch(&mapB);
         if (Q8) tma_prefetch(&mapS);
-        tma_prefetch(&outs.c0);
-        if (EPI == EPI_QKV) {
-            tma_prefetch(&outs.c1);
-            tma_prefetch(&outs.c2);
-        }
+        tma_prefetch(&mapC);
     }
     if (warp == 5) {
         tmem_alloc(tmem_slot, 2 * BN);
@@ -235,26 +220,6 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
             }
             sbuf = (sbuf + 1 == L::kStgBufs) ? 0 : sbuf + 1;
         };
-        // Piecewise staging: open the next buffer, put 16-byte chunks of this thread's row,
-        // then store the 32 x 128-byte box.
-        uint8_t* open_buf = nullptr;
-        auto stg_begin = [&]() {
-            if (lane == 0) bulk_wait_read<L::kStgBufs - 1>();
-            __syncwarp();
-            open_buf = stg + sbuf * 4096;
-        };
-        auto stg_put = [&](int j, uint4 v) {
-            *reinterpret_cast<uint4*>(open_buf + lane * 128 + ((j ^ (lane & 7)) * 16)) = v;
-        };
-        auto stg_end = [&](int x, int y, const CUtensorMap* map) {
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                tma_store_2d(map, open_buf, x, y);
-                bulk_commit();
-            }
-            sbuf = (sbuf + 1 == L::kStgBufs) ? 0 : sbuf + 1;
-        };
         int acc = 0;
         uint32_t acc_ph = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
@@ -270,7 +235,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
                 for (int c = 0; c < BN / 32; c++) {
                     tmem_ld32(taddr + uint32_t(c * 32), r);
                     tmem_wait_ld();
-                    emit(r, n0 + c * 32, y, &outs.c0);
+                    emit(r, n0 + c * 32, y, &mapC);
                 }
             } else if (EPI == EPI_GEGLU) {
                 // Columns [0, BN/2) of the tile are gate rows, [BN/2, BN) the matching up rows.
@@ -287,7 +252,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
                                 pack_half2(gelu_tanh(__uint_as_float(r[2 * i])) * __uint_as_float(u[2 * i]),
                                            gelu_tanh(__uint_as_float(r[2 * i + 1])) * __uint_as_float(u[2 * i + 1]));
                     }
-                    emit(packed, n0 / 2 + c * 64, y, &outs.c0);
+                    emit(packed, n0 / 2 + c * 64, y, &mapC);
                 }
             } else if (EPI == EPI_F16 || EPI == EPI_GELU_MUL) {
 #pragma unroll 1
@@ -312,73 +277,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
                                 packed[half * 16 + i] = pack_half2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
                         }
                     }
-                    emit(packed, n0 + c * 64, y, &outs.c0);
-                }
-            } else if (EPI == EPI_QKV) {
-                // One head per tile: slot < heads is a query head, then key heads, then value heads.
-                const int slot = n0 / BN;
-                const CUtensorMap* dst = &outs.c2;
-                const float* w = nullptr;
-                int xbase = (slot - p.heads - p.kvh) * BN;
-                if (slot < p.heads) {
-                    dst = &outs.c0;
-                    w = p.q_norm;
-                    xbase = slot * BN;
-                } else if (slot < p.heads + p.kvh) {
-                    dst = &outs.c1;
-                    w = p.k_norm;
-                    xbase = (slot - p.heads) * BN;
-                }
-                float ss = 0.f;
-#pragma unroll 1
-                for (int c = 0; c < BN / 32; c++) {
-                    tmem_ld32(taddr + uint32_t(c * 32), r);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int i = 0; i < 32; i++) ss += __uint_as_float(r[i]) * __uint_as_float(r[i]);
-                }
-                const float inv = 1.0f / sqrtf(ss / float(BN) + p.eps);
-                const int pos = row < p.ntok ? p.positions[row] : 0;
-                // Pair-major table [pair][position][cos, sin]: the 32 rows of a warp are mostly
-                // consecutive positions, so each pair's load is one contiguous line per warp.
-                const float2* cs = reinterpret_cast<const float2*>(p.rope) + pos;
-                // Output boxes of 64 columns: the low half [64cc, 64cc + 64) of the head and its
-                // rotation partners 128 columns up.  Each is written 16 columns at a time.
-#pragma unroll 1
-                for (int box = 0; box < BN / 64; box++) {
-                    const int cc = box >> 1, side = box & 1;
-                    stg_begin();
-#pragma unroll 1
-                    for (int qd = 0; qd < 4; qd++) {
-                        const int col0 = cc * 64 + qd * 16;
-                        uint32_t ra[16], rb[16];
-                        tmem_ld16(taddr + uint32_t(col0), ra);
-                        tmem_ld16(taddr + uint32_t(BN / 2 + col0), rb);
-                        tmem_wait_ld();
-                        uint32_t pk[8];
-#pragma unroll
-                        for (int i = 0; i < 16; i += 2) {
-                            float o[2];
-#pragma unroll
-                            for (int e = 0; e < 2; e++) {
-                                const int col = col0 + i + e;
-                                float a = __uint_as_float(ra[i + e]) * inv;
-                                float b = __uint_as_float(rb[i + e]) * inv;
-                                if (w) {
-                                    a = a * w[col];
-                                    b = b * w[col + BN / 2];
-                                    const float2 tcs = cs[long(col) * p.rope_positions];
-                                    o[e] = side == 0 ? a * tcs.x - b * tcs.y : a * tcs.y + b * tcs.x;
-                                } else {
-                                    o[e] = side == 0 ? a : b;
-                                }
-                            }
-                            pk[i / 2] = pack_half2(o[0], o[1]);
-                        }
-                        stg_put(2 * qd, make_uint4(pk[0], pk[1], pk[2], pk[3]));
-                        stg_put(2 * qd + 1, make_uint4(pk[4], pk[5], pk[6], pk[7]));
-                    }
-                    stg_end(xbase + side * (BN / 2) + cc * 64, y, dst);
+                    emit(packed, n0 + c * 64, y, &mapC);
                 }
             }
             tc_fence_before();
@@ -512,35 +411,14 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
     const int tiles = (g.m_rows / BM) * (g.w->N / kBN);
     const int grid = tiles < g.num_sms ? tiles : g.num_sms;
     const CUtensorMap& mb = Q8 ? g.w->map_q8 : g.w->map_f16;
-    // Output maps: boxes of 32 rows x 128 bytes (32 fp32 or 64 fp16 columns), 128-byte swizzle.
-    OutMaps mc;
-    if (EPI == EPI_QKV) {
-        const QkvEpilogue& q = *g.qkv;
-        if (g.w->N != (q.heads + 2 * q.kv_heads) * kBN) return cudaErrorInvalidValue;
-        if (!encode_2d(&mc.c0, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q.q, uint64_t(q.heads) * kBN, uint64_t(g.m_rows), 64, 32,
-                       CU_TENSOR_MAP_SWIZZLE_128B) ||
-            !encode_2d(&mc.c1, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q.k, uint64_t(q.kv_heads) * kBN, uint64_t(g.m_rows), 64,
-                       32, CU_TENSOR_MAP_SWIZZLE_128B) ||
-            !encode_2d(&mc.c2, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, q.v, uint64_t(q.kv_heads) * kBN, uint64_t(g.m_rows), 64,
-                       32, CU_TENSOR_MAP_SWIZZLE_128B))
-            return cudaErrorInvalidValue;
-        p.heads = q.heads;
-        p.kvh = q.kv_heads;
-        p.ntok = q.ntok;
-        p.eps = q.eps;
-        p.q_norm = q.q_norm;
-        p.k_norm = q.k_norm;
-        p.rope = q.rope_t;
-        p.rope_positions = q.rope_positions;
-        p.positions = q.positions;
-    } else {
-        const bool f32 = EPI == EPI_F32;
-        const int out_cols = EPI == EPI_GEGLU ? g.w->N / 2 : g.w->N;
-        if (g.ldo < out_cols) return cudaErrorInvalidValue;
-        if (!encode_2d(&mc.c0, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, f32 ? 4 : 2, g.out,
-                       uint64_t(g.ldo), uint64_t(g.m_rows), f32 ? 32 : 64, 32, CU_TENSOR_MAP_SWIZZLE_128B))
-            return cudaErrorInvalidValue;
-    }
+    // Output map: boxes of 32 rows x 128 bytes (32 fp32 or 64 fp16 columns), 128-byte swizzle.
+    const bool f32 = EPI == EPI_F32;
+    const int out_cols = EPI == EPI_GEGLU ? g.w->N / 2 : g.w->N;
+    if (g.ldo < out_cols) return cudaErrorInvalidValue;
+    CUtensorMap mc;
+    if (!encode_2d(&mc, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, f32 ? 4 : 2, g.out,
+                   uint64_t(g.ldo), uint64_t(g.m_rows), f32 ? 32 : 64, 32, CU_TENSOR_MAP_SWIZZLE_128B))
+        return cudaErrorInvalidValue;
     kern<<<grid, L::kThreads, L::kBytes, stream>>>(g.a->map, mb, g.w->map_scales, mc, p);
     return cudaGetLastError();
 }
@@ -557,9 +435,6 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream) {
     case EPI_F16: return q8 ? launch_t<EPI_F16, true>(g, stream) : launch_t<EPI_F16, false>(g, stream);
     case EPI_GEGLU: return q8 ? launch_t<EPI_GEGLU, true>(g, stream) : launch_t<EPI_GEGLU, false>(g, stream);
     case EPI_GELU_MUL: return q8 ? launch_t<EPI_GELU_MUL, true>(g, stream) : launch_t<EPI_GELU_MUL, false>(g, stream);
-    case EPI_QKV:
-        if (!g.qkv) return cudaErrorInvalidValue;
-        return q8 ? launch_t<EPI_QKV, true>(g, stream) : launch_t<EPI_QKV, false>(g, stream);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -17,21 +17,8 @@ enum GemmEpilogue : int {
     EPI_F16 = 1,    // out[m][n] = acc (fp16)
     EPI_GEGLU = 2,  // weight rows interleave gate and up in blocks of BN/2: out = gelu(gate) * up (fp16)
     EPI_GELU_MUL = 3,  // out = gelu(acc) * aux[m][n] (fp16), aux fp32 with row stride ldaux
-    EPI_QKV = 4,       // 256-wide head tiles of [q heads | k heads | v heads]: per-head RMSNorm,
-                       // weighted and NeoX-rotated for q and k, unweighted for v -> fp16 q, k, v
 };
 
-// Outputs and constants of the fused q/k/v epilogue (CPUReference.swift:225-235).
-struct QkvEpilogue {
-    __half *q = nullptr, *k = nullptr, *v = nullptr;  // [rows][heads * 256], [rows][kv * 256] x 2
-    int heads = 0, kv_heads = 0;
-    const float *q_norm = nullptr, *k_norm = nullptr;
-    const int32_t* positions = nullptr;  // RoPE position of each token row
-    const float* rope_t = nullptr;       // [128 pairs][rope_positions][cos, sin]
-    int rope_positions = 0;
-    int ntok = 0;                        // rows at or past ntok are padding (position 0)
-    float eps = 1e-6f;
-};
 
 // One GEMM weight as the device keeps it: the Q8_0 planes (int8 values [N][K] and the fp16
 // block scales transposed to [K/32][N]) and, unless disabled, the exact fp16 dequantisation
@@ -67,7 +54,6 @@ struct GemmLaunch {
     bool use_q8 = false;  // dequantise Q8 tiles in shared memory instead of reading fp16 weights
     int* err;
     int num_sms;
-    const QkvEpilogue* qkv = nullptr;  // EPI_QKV only
 };
 cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream);
 
@@ -79,15 +65,16 @@ cudaError_t launch_embed(const int32_t* tokens, int ntok, int rows, const int8_t
                          cudaStream_t stream);
 
 // Per (token, head): q, k = rope(rmsnorm(head) * w); v = rmsnorm(head). Reads the fused
-// projection output qkv (fp32, [rows][(H + 2 KV) * hd]) and writes fp16 q, k, v; rows at or
+// projection output qkv (fp16, [rows][(H + 2 KV) * hd]) and writes fp16 q, k, v; rows at or
 // past ntok are written as zeros.
-cudaError_t launch_qkv_norm_rope(const float* qkv, int ntok, int rows, int heads, int kv_heads, int hd,
+cudaError_t launch_qkv_norm_rope(const __half* qkv, int ntok, int rows, int heads, int kv_heads, int hd,
                                  const float* q_w, const float* k_w, const int32_t* positions, const float* rope,
                                  float eps, __half* q, __half* k, __half* v, cudaStream_t stream);
 
 // x = (x + rmsnorm(t) * w_post) * scale; then, when w_next is set,
 // h16 = fp16(rmsnorm(x) * w_next) or y32 = rmsnorm(x) * w_next, and x16 = fp16(x) if set.
-cudaError_t launch_residual_norm(float* x, const float* t, int rows, int width, const float* w_post, float scale,
+// t is the fp16 output of the projection; width 512 or 768.
+cudaError_t launch_residual_norm(float* x, const __half* t, int rows, int width, const float* w_post, float scale,
                                  const float* w_next, float eps, __half* h16, float* y32, __half* x16,
                                  cudaStream_t stream);
 

@@ -12,9 +12,6 @@
 
 namespace ge {
 
-cudaError_t launch_qkv_norm_rope(const float* qkv, int ntok, int rows, int heads, int kv_heads, int hd,
-                                 const float* q_w, const float* k_w, const int32_t* positions, const float* rope,
-                                 float eps, __half* q, __half* k, __half* v, cudaStream_t stream);
 
 int Config::max_q() const {
     int m = 0;
@@ -302,8 +299,8 @@ static cudaError_t upload_weight(Device& d, DevWeight& w, const HostWeight& h) {
 }
 
 static void free_workspace(Workspace& ws) {
-    for (void* p : {(void*)ws.tokens, (void*)ws.positions, (void*)ws.seqs, (void*)ws.work, (void*)ws.x, (void*)ws.qkv,
-                    (void*)ws.o, (void*)ws.y, (void*)ws.ple, (void*)ws.pooled, (void*)ws.mid, (void*)ws.out,
+    for (void* p : {(void*)ws.tokens, (void*)ws.positions, (void*)ws.seqs, (void*)ws.work, (void*)ws.x, (void*)ws.qkv16,
+                    (void*)ws.o16, (void*)ws.y, (void*)ws.ple, (void*)ws.pooled, (void*)ws.mid, (void*)ws.out,
                     (void*)ws.h, (void*)ws.x16, (void*)ws.q, (void*)ws.k, (void*)ws.v, (void*)ws.attn, (void*)ws.act,
                     (void*)ws.g})
         if (p) cudaFree(p);
@@ -350,8 +347,8 @@ static cudaError_t ensure_workspace(const Config& c, Device& d, int rows, int se
     chk(A(&ws.seqs, 2 * size_t(S)));
     chk(A(&ws.work, 3 * size_t(W)));
     chk(A(&ws.x, r * d_));
-    chk(A(&ws.qkv, r * qkvd));
-    chk(A(&ws.o, r * d_));
+    chk(A(&ws.qkv16, r * qkvd));
+    chk(A(&ws.o16, r * d_));
     chk(A(&ws.y, r * d_));
     chk(A(&ws.h, r * d_));
     chk(A(&ws.q, r * qd));
@@ -470,20 +467,10 @@ static int load_device(ge_model* m, Device& d, const std::vector<HostWeight>& hw
         if ((e = upload_weight(d, d.plp, *plp)) != cudaSuccess) return fail(e);
     }
     if (norm_err != cudaSuccess) return fail(norm_err);
-    for (size_t ri = 0; ri < ropes.size(); ri++) {
-        const std::vector<float>& r = ropes[ri];
+    for (const std::vector<float>& r : ropes) {
         float* p = nullptr;
         if ((e = dev_upload(d, &p, r.data(), r.size())) != cudaSuccess) return fail(e);
         d.rope.push_back(p);
-        const int pairs = c.ropes[ri].first / 2;
-        std::vector<float> t(r.size());
-        for (int pos = 0; pos < c.max_tokens; pos++)
-            for (int i = 0; i < pairs; i++) {
-                t[(size_t(i) * c.max_tokens + pos) * 2] = r[(size_t(pos) * pairs + i) * 2];
-                t[(size_t(i) * c.max_tokens + pos) * 2 + 1] = r[(size_t(pos) * pairs + i) * 2 + 1];
-            }
-        if ((e = dev_upload(d, &p, t.data(), t.size())) != cudaSuccess) return fail(e);
-        d.rope_t.push_back(p);
     }
     if (c.has_dense) {
         if ((e = dev_upload(d, &d.dense2, dense2.data(), dense2.size())) != cudaSuccess) return fail(e);
@@ -515,7 +502,7 @@ int load_model(ge_model* m, const char* path, const ge_load_opts* opts) {
     LoadError le{0, ""};
     Config& c = m->cfg;
     if (!read_config(m->file, c, le)) return set_error(m, le.code, le.msg);
-    if (c.layers <= 0 || c.hidden % 128 || c.ff % 128 || c.heads <= 0)
+    if (c.layers <= 0 || (c.hidden != 512 && c.hidden != 768) || c.ff % 128 || c.heads <= 0)
         return set_error(m, GE_ERR_INVALID_GGUF, "invalid GGUF file: unsupported dimensions");
     for (auto& l : c.layer)
         if ((l.hd != 256 && l.hd != 512) || l.kv <= 0 || c.heads % l.kv)
@@ -748,7 +735,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     const int D = c.hidden;
     const bool q8 = rows <= kQ8GemmMaxRows || (m->flags & GE_LOAD_Q8_ONLY);
     auto gemm = [&](const DevActivation& A, const DevWeight& W, void* out, int ldo, int epi, const float* aux = nullptr,
-                    int ldaux = 0, const QkvEpilogue* qkv = nullptr) {
+                    int ldaux = 0) {
         GemmLaunch g;
         g.a = &A;
         g.w = &W;
@@ -761,7 +748,6 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         g.use_q8 = q8;
         g.err = d.err;
         g.num_sms = d.num_sms;
-        g.qkv = qkv;
         return launch_gemm(g, st);
     };
 #define CK(expr, what)                                  \
@@ -841,35 +827,16 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         const LayerCfg& lc = c.layer[l];
         const LayerDev& L = d.layers[l];
         const int qd = c.heads * lc.hd;
-        if (lc.hd == 256) {
-            // Projection, per-head norms and RoPE in one kernel: the epilogue writes fp16 q, k, v.
-            QkvEpilogue qe;
-            qe.q = ws.q;
-            qe.k = ws.k;
-            qe.v = ws.v;
-            qe.heads = c.heads;
-            qe.kv_heads = lc.kv;
-            qe.q_norm = L.q_norm;
-            qe.k_norm = L.k_norm;
-            qe.positions = ws.positions;
-            qe.rope_t = d.rope_t[lc.rope_index];
-            qe.rope_positions = c.max_tokens;
-            qe.ntok = ntok;
-            qe.eps = c.eps;
-            CK(K("gemm_qkv_norm_rope", gemm_flops(L.qkv), gemm_bytes(L.qkv, 2),
-                 [&] { return gemm(ws.a_h, L.qkv, nullptr, 0, EPI_QKV, nullptr, 0, &qe); }),
-               "qkv projection");
-        } else {
-            CK(K("gemm_qkv", gemm_flops(L.qkv), gemm_bytes(L.qkv, 4),
-                 [&] { return gemm(ws.a_h, L.qkv, ws.qkv, L.qkv.N, EPI_F32); }),
-               "qkv projection");
-            CK(K("qkv_norm_rope", 0, double(ntok) * L.qkv.N * 6,
-                 [&] {
-                     return launch_qkv_norm_rope(ws.qkv, ntok, rows, c.heads, lc.kv, lc.hd, L.q_norm, L.k_norm,
-                                                 ws.positions, d.rope[lc.rope_index], c.eps, ws.q, ws.k, ws.v, st);
-                 }),
-               "q/k/v norm and rope");
-        }
+        // The projection stores fp16; the per-head norms and RoPE read it back warp per row.
+        CK(K("gemm_qkv", gemm_flops(L.qkv), gemm_bytes(L.qkv, 2),
+             [&] { return gemm(ws.a_h, L.qkv, ws.qkv16, L.qkv.N, EPI_F16); }),
+           "qkv projection");
+        CK(K("qkv_norm_rope", 0, double(ntok) * L.qkv.N * 4,
+             [&] {
+                 return launch_qkv_norm_rope(ws.qkv16, ntok, rows, c.heads, lc.kv, lc.hd, L.q_norm, L.k_norm, ws.positions,
+                                             d.rope[lc.rope_index], c.eps, ws.q, ws.k, ws.v, st);
+             }),
+           "q/k/v norm and rope");
         AttnLaunch al;
         al.q = ws.q;
         al.k = ws.k;
@@ -893,25 +860,25 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         const DevActivation* aa = nullptr;
         for (auto& x : ws.a_attn)
             if (x.cols == qd) aa = &x;
-        CK(K("gemm_o", gemm_flops(L.o), gemm_bytes(L.o, 4), [&] { return gemm(*aa, L.o, ws.o, D, EPI_F32); }),
+        CK(K("gemm_o", gemm_flops(L.o), gemm_bytes(L.o, 2), [&] { return gemm(*aa, L.o, ws.o16, D, EPI_F16); }),
            "attention output");
-        CK(K("residual_norm", 0, double(ntok) * D * 14,
+        CK(K("residual_norm", 0, double(ntok) * D * 12,
              [&] {
-                 return launch_residual_norm(ws.x, ws.o, rows, D, L.post_attn, 1.0f, L.ffn_norm, c.eps, ws.h, nullptr,
+                 return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_attn, 1.0f, L.ffn_norm, c.eps, ws.h, nullptr,
                                              nullptr, st);
              }),
            "post-attention residual");
         CK(K("gemm_gate_up", gemm_flops(L.gu), gemm_bytes(L.gu, 1), [&] { return gemm(ws.a_h, L.gu, ws.act, c.ff, EPI_GEGLU); }),
            "gate/up projection");
-        CK(K("gemm_down", gemm_flops(L.down), gemm_bytes(L.down, 4),
-             [&] { return gemm(ws.a_act, L.down, ws.o, D, EPI_F32); }),
+        CK(K("gemm_down", gemm_flops(L.down), gemm_bytes(L.down, 2),
+             [&] { return gemm(ws.a_act, L.down, ws.o16, D, EPI_F16); }),
            "down projection");
         const bool last = l + 1 == c.layers;
         const float* next = last ? d.out_norm : d.layers[l + 1].attn_norm;
         if (c.has_ple) {
-            CK(K("residual_norm", 0, double(ntok) * D * 14,
+            CK(K("residual_norm", 0, double(ntok) * D * 12,
                  [&] {
-                     return launch_residual_norm(ws.x, ws.o, rows, D, L.post_ffw, 1.0f, nullptr, c.eps, nullptr, nullptr,
+                     return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_ffw, 1.0f, nullptr, c.eps, nullptr, nullptr,
                                                  ws.x16, st);
                  }),
                "post-ffn residual");
@@ -921,18 +888,18 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
                                  c.per_layer * c.layers);
                  }),
                "per-layer gate");
-            CK(K("gemm_proj", gemm_flops(L.proj), gemm_bytes(L.proj, 4), [&] { return gemm(ws.a_g, L.proj, ws.o, D, EPI_F32); }),
+            CK(K("gemm_proj", gemm_flops(L.proj), gemm_bytes(L.proj, 2), [&] { return gemm(ws.a_g, L.proj, ws.o16, D, EPI_F16); }),
                "per-layer projection");
-            CK(K("residual_norm", 0, double(ntok) * D * 14,
+            CK(K("residual_norm", 0, double(ntok) * D * 12,
                  [&] {
-                     return launch_residual_norm(ws.x, ws.o, rows, D, L.post_norm, L.out_scale, next, c.eps,
+                     return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_norm, L.out_scale, next, c.eps,
                                                  last ? nullptr : ws.h, last ? ws.y : nullptr, nullptr, st);
                  }),
                "per-layer residual");
         } else {
-            CK(K("residual_norm", 0, double(ntok) * D * 14,
+            CK(K("residual_norm", 0, double(ntok) * D * 12,
                  [&] {
-                     return launch_residual_norm(ws.x, ws.o, rows, D, L.post_ffw, 1.0f, next, c.eps, last ? nullptr : ws.h,
+                     return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_ffw, 1.0f, next, c.eps, last ? nullptr : ws.h,
                                                  last ? ws.y : nullptr, nullptr, st);
                  }),
                "post-ffn residual");

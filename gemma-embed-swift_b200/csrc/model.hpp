@@ -48,8 +48,10 @@ struct Workspace {
     int cap_rows = 0, cap_seqs = 0, cap_work = 0;
     int32_t *tokens = nullptr, *positions = nullptr;
     uint32_t *seqs = nullptr, *work = nullptr;
-    float *x = nullptr, *qkv = nullptr, *o = nullptr, *y = nullptr, *ple = nullptr;
+    float *x = nullptr, *y = nullptr, *ple = nullptr;
+    __half* o16 = nullptr;  // fp16 output of the o, down and per-layer projections
     float *pooled = nullptr, *mid = nullptr, *out = nullptr;
+    __half *qkv16 = nullptr;  // fused q|k|v projection output
     __half *h = nullptr, *x16 = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *act = nullptr,
            *g = nullptr;
     // GEMM A-operand views (buffer, column count) with their TMA descriptors.
@@ -73,8 +75,7 @@ struct Device {
     DevWeight plp;  // per_layer_model_proj (fp16 only)
     float *pl_norm = nullptr, *out_norm = nullptr;
     float *dense2 = nullptr, *dense3 = nullptr, *output = nullptr;  // fp32 [N][K]
-    std::vector<float*> rope;    // per table: [position][pair][cos, sin]
-    std::vector<float*> rope_t;  // per table: [pair][position][cos, sin]
+    std::vector<float*> rope;  // per table: [position][pair][cos, sin]
     int* err = nullptr;
     Workspace ws;
     std::vector<void*> allocations;
