@@ -95,9 +95,18 @@ class ClockSampler:
                 "samples": len(rows)}
 
 
+def host_threads() -> int:
+    """Every core this process may run on (torchrun sets OMP_NUM_THREADS=1; the CPU arms use all)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_baseline(path, seqs, seconds):
     """The CPU oracle on a bounded prefix of the same batch, all host threads."""
     from oracle import binding
+    binding.set_threads(host_threads())
     m = binding.OracleModel(path)
     m.forward(seqs[0][:8])  # dequantises and caches every weight matrix outside the timing
     tokens = 0
@@ -124,6 +133,7 @@ def run_reference(a, rank, world):
     from oracle import binding
     path = synth.model_path(a.arch, seed=0)
     seqs = synth.config_sequences(a.config, seed=0)
+    binding.set_threads(host_threads())
     m = binding.OracleModel(path)
     m.forward(seqs[0][:8])
     # One step = one text of the batch, in order, cycling: a bounded sample of the workload.

@@ -424,15 +424,21 @@ __global__ void __launch_bounds__(192, 1) k_attention_tc(const __grid_constant__
 
 int attention_queries_per_item(int hd) { return hd == kTcHd ? kTcQ : kSimtQueries; }
 
+template <int HD>
+static int simt_smem() {
+    return (kSimtQueries * HD + kSimtKeys * (HD + 1) + kSimtKeys * HD) * 4;
+}
+
+// Sets the shared-memory limits of the attention kernels on the current device; runs at
+// load, before any stream capture.
+cudaError_t configure_attention_kernels() {
+    cudaError_t e = cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(k_attention_simt<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, simt_smem<512>());
+    return e;
+}
+
 static cudaError_t launch_tc(const AttnLaunch& a, cudaStream_t stream) {
-    static unsigned configured = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!(configured & (1u << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
-        if (e != cudaSuccess) return e;
-        configured |= 1u << dev;
-    }
     TcAttnParams p{a.work, a.out, a.heads, a.kv_heads, a.half_window, a.err};
     dim3 grid(a.work_items, a.heads);
     k_attention_tc<<<grid, 192, kTcSmem, stream>>>(a.maps->q, a.maps->k, a.maps->v, p);
@@ -441,15 +447,7 @@ static cudaError_t launch_tc(const AttnLaunch& a, cudaStream_t stream) {
 
 template <int HD>
 static cudaError_t launch_simt(const AttnLaunch& a, cudaStream_t stream) {
-    const int smem = (kSimtQueries * HD + kSimtKeys * (HD + 1) + kSimtKeys * HD) * 4;
-    static unsigned configured = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!(configured & (1u << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(k_attention_simt<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
-        configured |= 1u << dev;
-    }
+    const int smem = simt_smem<HD>();
     dim3 grid(a.work_items, a.heads);
     k_attention_simt<HD><<<grid, 256, smem, stream>>>(a.q, a.k, a.v, a.out, a.work, a.heads, a.kv_heads, a.half_window,
                                                       1.0f);

@@ -60,12 +60,15 @@ cudaError_t launch_embed(const int32_t* tokens, int ntok, int rows, const int8_t
 
 // One warp per (token, head slot): slots [0, H) are query heads, [H, H+KV) key heads,
 // [H+KV, H+2KV) value heads of the fused projection row.  CPUReference.swift:225-235.
+// Lane l holds elements [Q*l, Q*l + Q) of each half of the head (Q = HD / 64), so every
+// element and its rotation partner HD/2 away sit in the same lane, loaded as 8-byte vectors.
 template <int HD>
 __global__ void k_qkv_norm_rope(const __half* __restrict__ qkv, int ntok, int rows, int heads, int kvh,
                                 const float* __restrict__ qw, const float* __restrict__ kw,
                                 const int32_t* __restrict__ pos, const float* __restrict__ rope, float eps,
                                 __half* __restrict__ q, __half* __restrict__ k, __half* __restrict__ v) {
-    constexpr int PER = HD / 32;
+    constexpr int Q = HD / 64;  // elements per lane per half: 4 (hd 256) or 8 (hd 512)
+    constexpr int HALF = HD / 2;
     const int slots = heads + 2 * kvh;
     const long gw = long(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -82,37 +85,59 @@ __global__ void k_qkv_norm_rope(const __half* __restrict__ qkv, int ntok, int ro
     } else {
         dst = v + long(row) * kvh * HD + (slot - heads - kvh) * HD;
     }
-    if (row >= ntok) {
+    const int c = lane * Q;
+    float a[Q], b[Q];
+    if (row < ntok) {
+        const __half* src = qkv + long(row) * slots * HD + slot * HD;
 #pragma unroll
-        for (int j = 0; j < PER; j++) dst[lane + 32 * j] = __float2half_rn(0.f);
-        return;
+        for (int i = 0; i < Q; i += 4) {
+            const uint2 ra = *reinterpret_cast<const uint2*>(src + c + i);
+            const uint2 rb = *reinterpret_cast<const uint2*>(src + HALF + c + i);
+            const float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(&ra.x));
+            const float2 a1 = __half22float2(*reinterpret_cast<const __half2*>(&ra.y));
+            const float2 b0 = __half22float2(*reinterpret_cast<const __half2*>(&rb.x));
+            const float2 b1 = __half22float2(*reinterpret_cast<const __half2*>(&rb.y));
+            a[i] = a0.x; a[i + 1] = a0.y; a[i + 2] = a1.x; a[i + 3] = a1.y;
+            b[i] = b0.x; b[i + 1] = b0.y; b[i + 2] = b1.x; b[i + 3] = b1.y;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < Q; i++) a[i] = b[i] = 0.f;
     }
-    const __half* src = qkv + long(row) * slots * HD + slot * HD;
-    float e[PER];
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < PER; j++) {
-        e[j] = __half2float(src[lane + 32 * j]);
-        ss += e[j] * e[j];
-    }
+    for (int i = 0; i < Q; i++) ss += a[i] * a[i] + b[i] * b[i];
     ss = warp_sum(ss);
     const float inv = 1.0f / sqrtf(ss / float(HD) + eps);
 #pragma unroll
-    for (int j = 0; j < PER; j++) e[j] = e[j] * inv * (w ? w[lane + 32 * j] : 1.0f);
-    if (w) {
-        // NeoX rotation of pairs (i, i + HD/2): element lane + 32j pairs with lane + 32(j + PER/2).
-        const float* cs = rope + long(pos[row]) * HD;  // [pairs][2] per position
+    for (int i = 0; i < Q; i++) {
+        a[i] = a[i] * inv * (w ? w[c + i] : 1.0f);
+        b[i] = b[i] * inv * (w ? w[HALF + c + i] : 1.0f);
+    }
+    if (w && row < ntok) {
+        // NeoX rotation of the pairs (c + i, HALF + c + i), table [position][pair][cos, sin].
+        const float* cs = rope + long(pos[row]) * HD + 2 * c;
 #pragma unroll
-        for (int j = 0; j < PER / 2; j++) {
-            const int i = lane + 32 * j;
-            const float c = cs[2 * i], s = cs[2 * i + 1];
-            const float a = e[j], b = e[j + PER / 2];
-            e[j] = a * c - b * s;
-            e[j + PER / 2] = a * s + b * c;
+        for (int i = 0; i < Q; i += 2) {
+            const float4 t = *reinterpret_cast<const float4*>(cs + 2 * i);
+            const float c0 = t.x, s0 = t.y, c1 = t.z, s1 = t.w;
+            const float a0 = a[i], b0 = b[i], a1 = a[i + 1], b1 = b[i + 1];
+            a[i] = a0 * c0 - b0 * s0;
+            b[i] = a0 * s0 + b0 * c0;
+            a[i + 1] = a1 * c1 - b1 * s1;
+            b[i + 1] = a1 * s1 + b1 * c1;
         }
     }
 #pragma unroll
-    for (int j = 0; j < PER; j++) dst[lane + 32 * j] = __float2half_rn(e[j]);
+    for (int i = 0; i < Q; i += 4) {
+        uint2 oa, ob;
+        *reinterpret_cast<__half2*>(&oa.x) = __floats2half2_rn(a[i], a[i + 1]);
+        *reinterpret_cast<__half2*>(&oa.y) = __floats2half2_rn(a[i + 2], a[i + 3]);
+        *reinterpret_cast<__half2*>(&ob.x) = __floats2half2_rn(b[i], b[i + 1]);
+        *reinterpret_cast<__half2*>(&ob.y) = __floats2half2_rn(b[i + 2], b[i + 3]);
+        *reinterpret_cast<uint2*>(dst + c + i) = oa;
+        *reinterpret_cast<uint2*>(dst + HALF + c + i) = ob;
+    }
 }
 
 cudaError_t launch_qkv_norm_rope(const __half* qkv, int ntok, int rows, int heads, int kv_heads, int hd,

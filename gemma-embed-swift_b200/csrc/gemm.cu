@@ -388,17 +388,26 @@ bool encode_activation_map(DevActivation& a) {
 }
 
 template <int EPI, bool Q8>
+static cudaError_t configure_t() {
+    using L = GemmLayout<kBN, Q8>;
+    return cudaFuncSetAttribute(k_gemm<kBN, EPI, Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+}
+
+// Sets the shared-memory limit of every GEMM variant on the current device; runs at load,
+// before any stream capture.
+cudaError_t configure_gemm_kernels() {
+    cudaError_t e = cudaSuccess;
+    for (cudaError_t x : {configure_t<EPI_F32, false>(), configure_t<EPI_F32, true>(), configure_t<EPI_F16, false>(),
+                          configure_t<EPI_F16, true>(), configure_t<EPI_GEGLU, false>(), configure_t<EPI_GEGLU, true>(),
+                          configure_t<EPI_GELU_MUL, false>(), configure_t<EPI_GELU_MUL, true>()})
+        if (e == cudaSuccess) e = x;
+    return e;
+}
+
+template <int EPI, bool Q8>
 static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
     using L = GemmLayout<kBN, Q8>;
     auto kern = k_gemm<kBN, EPI, Q8>;
-    static unsigned configured = 0;  // one bit per device
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!(configured & (1u << dev))) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
-        if (e != cudaSuccess) return e;
-        configured |= 1u << dev;
-    }
     GemmParams p{};
     p.M = g.m_rows;
     p.N = g.w->N;

@@ -56,6 +56,10 @@ struct GemmLaunch {
     int num_sms;
 };
 cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream);
+// Kernel attributes (dynamic shared-memory limits) for the current device; call once per
+// device before the first launch or stream capture.
+cudaError_t configure_gemm_kernels();
+cudaError_t configure_attention_kernels();
 
 // ------------------------------------------------------------------ elementwise
 // x[t] = q8row(table[id]) * scale for t < ntok, 0 for padded rows; h = rmsnorm(x) * w (fp16).

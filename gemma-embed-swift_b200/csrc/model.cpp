@@ -317,6 +317,7 @@ static cudaError_t ensure_workspace(const Config& c, Device& d, int rows, int se
     if (ws.cap_rows >= rows && ws.cap_seqs >= seqs && ws.cap_work >= work) return cudaSuccess;
     cudaError_t e = cudaStreamSynchronize(d.stream);
     if (e != cudaSuccess) return e;
+    clear_graphs(d);  // captured graphs point into the old buffers
     const int R = std::max(rows, ws.cap_rows + ws.cap_rows / 2 > rows ? round_up(ws.cap_rows + ws.cap_rows / 2, kRowTile) : rows);
     const int S = std::max({seqs, ws.cap_seqs * 2, 16});
     const int W = std::max({work, ws.cap_work * 2, 64});
@@ -478,6 +479,8 @@ static int load_device(ge_model* m, Device& d, const std::vector<HostWeight>& hw
     }
     if (c.has_output && (e = dev_upload(d, &d.output, output.data(), output.size())) != cudaSuccess) return fail(e);
     if ((e = noalloc_setup(d.ordinal)) != cudaSuccess) return fail(e);
+    if ((e = configure_gemm_kernels()) != cudaSuccess || (e = configure_attention_kernels()) != cudaSuccess)
+        return fail(e);
     return GE_OK;
 }
 
@@ -486,6 +489,7 @@ static void free_device(Device& d) {
         cudaSetDevice(d.ordinal);
         cudaStreamSynchronize(d.stream);
     }
+    clear_graphs(d);
     free_workspace(d.ws);
     for (void* p : d.allocations) cudaFree(p);
     d.allocations.clear();
@@ -661,6 +665,38 @@ void free_model(ge_model* m) {
     m->devs.clear();
 }
 
+// ------------------------------------------------------------------ graphs
+constexpr size_t kMaxGraphs = 16;
+
+GraphEntry* find_graph(Device& d, const GraphKey& k) {
+    for (auto& g : d.graphs)
+        if (g.key == k) {
+            g.last_use = ++d.graph_clock;
+            return &g;
+        }
+    return nullptr;
+}
+
+void store_graph(Device& d, const GraphKey& k, cudaGraphExec_t exec, int64_t launches) {
+    if (d.graphs.size() >= kMaxGraphs) {
+        auto lru = std::min_element(d.graphs.begin(), d.graphs.end(),
+                                    [](const GraphEntry& a, const GraphEntry& b) { return a.last_use < b.last_use; });
+        cudaGraphExecDestroy(lru->exec);
+        d.graphs.erase(lru);
+    }
+    GraphEntry g;
+    g.key = k;
+    g.exec = exec;
+    g.launches = launches;
+    g.last_use = ++d.graph_clock;
+    d.graphs.push_back(g);
+}
+
+void clear_graphs(Device& d) {
+    for (auto& g : d.graphs) cudaGraphExecDestroy(g.exec);
+    d.graphs.clear();
+}
+
 // ------------------------------------------------------------------ forward
 // Work items, one per block of `qpi` queries of every sequence (AttentionWork.items,
 // MetalForward.swift:45-58).
@@ -731,6 +767,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     }
     if (e != cudaSuccess) return gpu_fail(e, "positions");
 
+    cudaStream_t ks = st;  // the stream kernels are launched on (the capture stream while capturing)
     // ---- layers (MetalForward.encode, MetalForward.swift:364-423)
     const int D = c.hidden;
     const bool q8 = rows <= kQ8GemmMaxRows || (m->flags & GE_LOAD_Q8_ONLY);
@@ -748,7 +785,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         g.use_q8 = q8;
         g.err = d.err;
         g.num_sms = d.num_sms;
-        return launch_gemm(g, st);
+        return launch_gemm(g, ks);
     };
 #define CK(expr, what)                                  \
     do {                                                \
@@ -767,13 +804,13 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
                 cudaEvent_t e0, e1;
                 cudaEventCreate(&e0);
                 cudaEventCreate(&e1);
-                cudaEventRecord(e0, st);
+                cudaEventRecord(e0, ks);
                 for (int r = 0; r < a.profile->reps; r++) {
                     cudaError_t x = fn();
                     if (x != cudaSuccess) return x;
                     launches++;
                 }
-                cudaEventRecord(e1, st);
+                cudaEventRecord(e1, ks);
                 cudaError_t x = cudaEventSynchronize(e1);
                 float ms = 0.f;
                 cudaEventElapsedTime(&ms, e0, e1);
@@ -807,131 +844,158 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     };
     const double vk_sliding = a.profile ? visible_keys(c.sliding_window / 2) : 0, vk_global = a.profile ? visible_keys(0) : 0;
 
-    CK(K("embed", 0, double(ntok) * D * (1 + 2.0 / 32 + 4 + 2),
-         [&] {
-             return launch_embed(tokens, ntok, rows, d.emb_q, d.emb_s, D, c.emb_scale, ws.x, c.has_ple ? ws.x16 : nullptr,
-                                 d.layers[0].attn_norm, c.eps, ws.h, st);
-         }),
-       "embed");
-    if (c.has_ple) {
-        // ple = rmsnorm_pl(x0 * Wplp^T / sqrt(d)) for every layer at once (CPUReference.swift:206-210).
-        const int plw = c.per_layer * c.layers;
-        CK(K("gemm_per_layer_inputs", gemm_flops(d.plp), gemm_bytes(d.plp, 4),
-             [&] { return gemm(ws.a_x16, d.plp, ws.ple, plw, EPI_F32); }),
-           "per-layer projection");
-        CK(K("per_layer_norm", 0, double(ntok) * plw * 8,
-             [&] { return launch_rmsnorm_rows(ws.ple, rows * c.layers, c.per_layer, c.pl_scale, d.pl_norm, c.eps, ws.ple, st); }),
-           "per-layer norm");
-    }
-    for (int l = 0; l < c.layers; l++) {
-        const LayerCfg& lc = c.layer[l];
-        const LayerDev& L = d.layers[l];
-        const int qd = c.heads * lc.hd;
-        // The projection stores fp16; the per-head norms and RoPE read it back warp per row.
-        CK(K("gemm_qkv", gemm_flops(L.qkv), gemm_bytes(L.qkv, 2),
-             [&] { return gemm(ws.a_h, L.qkv, ws.qkv16, L.qkv.N, EPI_F16); }),
-           "qkv projection");
-        CK(K("qkv_norm_rope", 0, double(ntok) * L.qkv.N * 4,
+    auto launch_all = [&]() -> int {
+        CK(K("embed", 0, double(ntok) * D * (1 + 2.0 / 32 + 4 + 2),
              [&] {
-                 return launch_qkv_norm_rope(ws.qkv16, ntok, rows, c.heads, lc.kv, lc.hd, L.q_norm, L.k_norm, ws.positions,
-                                             d.rope[lc.rope_index], c.eps, ws.q, ws.k, ws.v, st);
+                 return launch_embed(tokens, ntok, rows, d.emb_q, d.emb_s, D, c.emb_scale, ws.x, c.has_ple ? ws.x16 : nullptr,
+                                     d.layers[0].attn_norm, c.eps, ws.h, ks);
              }),
-           "q/k/v norm and rope");
-        AttnLaunch al;
-        al.q = ws.q;
-        al.k = ws.k;
-        al.v = ws.v;
-        al.out = ws.attn;
-        const bool tc = lc.hd == 256;
-        al.work = tc ? ws.work : ws.work + 3 * size_t(nwork);
-        al.work_items = tc ? nwork : nwork512;
-        al.heads = c.heads;
-        al.kv_heads = lc.kv;
-        al.hd = lc.hd;
-        al.half_window = lc.sliding ? c.sliding_window / 2 : 0;
-        al.queries_per_item = tc ? qpi : qpi512;
-        al.err = d.err;
-        for (auto& x : ws.attn_maps)
-            if (tc && x.first == lc.kv) al.maps = &x.second;
-        CK(K(lc.sliding ? "attention_sliding" : "attention_global",
-             4.0 * c.heads * lc.hd * (lc.sliding ? vk_sliding : vk_global),
-             double(ntok) * (2.0 * qd + 2.0 * lc.kv * lc.hd) * 2, [&] { return launch_attention(al, st); }),
-           "attention");
-        const DevActivation* aa = nullptr;
-        for (auto& x : ws.a_attn)
-            if (x.cols == qd) aa = &x;
-        CK(K("gemm_o", gemm_flops(L.o), gemm_bytes(L.o, 2), [&] { return gemm(*aa, L.o, ws.o16, D, EPI_F16); }),
-           "attention output");
-        CK(K("residual_norm", 0, double(ntok) * D * 12,
-             [&] {
-                 return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_attn, 1.0f, L.ffn_norm, c.eps, ws.h, nullptr,
-                                             nullptr, st);
-             }),
-           "post-attention residual");
-        CK(K("gemm_gate_up", gemm_flops(L.gu), gemm_bytes(L.gu, 1), [&] { return gemm(ws.a_h, L.gu, ws.act, c.ff, EPI_GEGLU); }),
-           "gate/up projection");
-        CK(K("gemm_down", gemm_flops(L.down), gemm_bytes(L.down, 2),
-             [&] { return gemm(ws.a_act, L.down, ws.o16, D, EPI_F16); }),
-           "down projection");
-        const bool last = l + 1 == c.layers;
-        const float* next = last ? d.out_norm : d.layers[l + 1].attn_norm;
+           "embed");
         if (c.has_ple) {
-            CK(K("residual_norm", 0, double(ntok) * D * 12,
-                 [&] {
-                     return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_ffw, 1.0f, nullptr, c.eps, nullptr, nullptr,
-                                                 ws.x16, st);
-                 }),
-               "post-ffn residual");
-            CK(K("gemm_inp_gate", gemm_flops(L.inp_gate), gemm_bytes(L.inp_gate, 2),
-                 [&] {
-                     return gemm(ws.a_x16, L.inp_gate, ws.g, c.per_layer, EPI_GELU_MUL, ws.ple + size_t(l) * c.per_layer,
-                                 c.per_layer * c.layers);
-                 }),
-               "per-layer gate");
-            CK(K("gemm_proj", gemm_flops(L.proj), gemm_bytes(L.proj, 2), [&] { return gemm(ws.a_g, L.proj, ws.o16, D, EPI_F16); }),
+            // ple = rmsnorm_pl(x0 * Wplp^T / sqrt(d)) for every layer at once (CPUReference.swift:206-210).
+            const int plw = c.per_layer * c.layers;
+            CK(K("gemm_per_layer_inputs", gemm_flops(d.plp), gemm_bytes(d.plp, 4),
+                 [&] { return gemm(ws.a_x16, d.plp, ws.ple, plw, EPI_F32); }),
                "per-layer projection");
-            CK(K("residual_norm", 0, double(ntok) * D * 12,
-                 [&] {
-                     return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_norm, L.out_scale, next, c.eps,
-                                                 last ? nullptr : ws.h, last ? ws.y : nullptr, nullptr, st);
-                 }),
-               "per-layer residual");
-        } else {
-            CK(K("residual_norm", 0, double(ntok) * D * 12,
-                 [&] {
-                     return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_ffw, 1.0f, next, c.eps, last ? nullptr : ws.h,
-                                                 last ? ws.y : nullptr, nullptr, st);
-                 }),
-               "post-ffn residual");
+            CK(K("per_layer_norm", 0, double(ntok) * plw * 8,
+                 [&] { return launch_rmsnorm_rows(ws.ple, rows * c.layers, c.per_layer, c.pl_scale, d.pl_norm, c.eps, ws.ple, ks); }),
+               "per-layer norm");
         }
-        if (a.trace_layer == l) break;
-    }
-    // ---- pooling and head
-    const float* result = nullptr;
-    int width = c.out_dim;
-    if (a.trace_layer >= 0) {
-        result = ws.x;
-        width = D;
-    } else if (a.trace_layer == -1) {
-        result = ws.y;
-        width = D;
+        for (int l = 0; l < c.layers; l++) {
+            const LayerCfg& lc = c.layer[l];
+            const LayerDev& L = d.layers[l];
+            const int qd = c.heads * lc.hd;
+            // The projection stores fp16; the per-head norms and RoPE read it back warp per row.
+            CK(K("gemm_qkv", gemm_flops(L.qkv), gemm_bytes(L.qkv, 2),
+                 [&] { return gemm(ws.a_h, L.qkv, ws.qkv16, L.qkv.N, EPI_F16); }),
+               "qkv projection");
+            CK(K("qkv_norm_rope", 0, double(ntok) * L.qkv.N * 4,
+                 [&] {
+                     return launch_qkv_norm_rope(ws.qkv16, ntok, rows, c.heads, lc.kv, lc.hd, L.q_norm, L.k_norm, ws.positions,
+                                                 d.rope[lc.rope_index], c.eps, ws.q, ws.k, ws.v, ks);
+                 }),
+               "q/k/v norm and rope");
+            AttnLaunch al;
+            al.q = ws.q;
+            al.k = ws.k;
+            al.v = ws.v;
+            al.out = ws.attn;
+            const bool tc = lc.hd == 256;
+            al.work = tc ? ws.work : ws.work + 3 * size_t(nwork);
+            al.work_items = tc ? nwork : nwork512;
+            al.heads = c.heads;
+            al.kv_heads = lc.kv;
+            al.hd = lc.hd;
+            al.half_window = lc.sliding ? c.sliding_window / 2 : 0;
+            al.queries_per_item = tc ? qpi : qpi512;
+            al.err = d.err;
+            for (auto& x : ws.attn_maps)
+                if (tc && x.first == lc.kv) al.maps = &x.second;
+            CK(K(lc.sliding ? "attention_sliding" : "attention_global",
+                 4.0 * c.heads * lc.hd * (lc.sliding ? vk_sliding : vk_global),
+                 double(ntok) * (2.0 * qd + 2.0 * lc.kv * lc.hd) * 2, [&] { return launch_attention(al, ks); }),
+               "attention");
+            const DevActivation* aa = nullptr;
+            for (auto& x : ws.a_attn)
+                if (x.cols == qd) aa = &x;
+            CK(K("gemm_o", gemm_flops(L.o), gemm_bytes(L.o, 2), [&] { return gemm(*aa, L.o, ws.o16, D, EPI_F16); }),
+               "attention output");
+            CK(K("residual_norm", 0, double(ntok) * D * 12,
+                 [&] {
+                     return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_attn, 1.0f, L.ffn_norm, c.eps, ws.h, nullptr,
+                                                 nullptr, ks);
+                 }),
+               "post-attention residual");
+            CK(K("gemm_gate_up", gemm_flops(L.gu), gemm_bytes(L.gu, 1), [&] { return gemm(ws.a_h, L.gu, ws.act, c.ff, EPI_GEGLU); }),
+               "gate/up projection");
+            CK(K("gemm_down", gemm_flops(L.down), gemm_bytes(L.down, 2),
+                 [&] { return gemm(ws.a_act, L.down, ws.o16, D, EPI_F16); }),
+               "down projection");
+            const bool last = l + 1 == c.layers;
+            const float* next = last ? d.out_norm : d.layers[l + 1].attn_norm;
+            if (c.has_ple) {
+                CK(K("residual_norm", 0, double(ntok) * D * 12,
+                     [&] {
+                         return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_ffw, 1.0f, nullptr, c.eps, nullptr, nullptr,
+                                                     ws.x16, ks);
+                     }),
+                   "post-ffn residual");
+                CK(K("gemm_inp_gate", gemm_flops(L.inp_gate), gemm_bytes(L.inp_gate, 2),
+                     [&] {
+                         return gemm(ws.a_x16, L.inp_gate, ws.g, c.per_layer, EPI_GELU_MUL, ws.ple + size_t(l) * c.per_layer,
+                                     c.per_layer * c.layers);
+                     }),
+                   "per-layer gate");
+                CK(K("gemm_proj", gemm_flops(L.proj), gemm_bytes(L.proj, 2), [&] { return gemm(ws.a_g, L.proj, ws.o16, D, EPI_F16); }),
+                   "per-layer projection");
+                CK(K("residual_norm", 0, double(ntok) * D * 12,
+                     [&] {
+                         return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_norm, L.out_scale, next, c.eps,
+                                                     last ? nullptr : ws.h, last ? ws.y : nullptr, nullptr, ks);
+                     }),
+                   "per-layer residual");
+            } else {
+                CK(K("residual_norm", 0, double(ntok) * D * 12,
+                     [&] {
+                         return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_ffw, 1.0f, next, c.eps, last ? nullptr : ws.h,
+                                                     last ? ws.y : nullptr, nullptr, ks);
+                     }),
+                   "post-ffn residual");
+            }
+            if (a.trace_layer == l) break;
+        }
+        // ---- pooling and head
+        if (a.trace_layer < -1) {
+            CK(K("mean_pool", 0, double(ntok) * D * 4, [&] { return launch_mean_pool(ws.y, D, ws.seqs, nseq, ws.pooled, ks); }),
+               "mean pool");
+            if (c.has_dense) {
+                CK(K("dense_head", 2.0 * nseq * D * c.dense_head, double(D) * c.dense_head * 4,
+                     [&] { return launch_dense_f32(ws.pooled, nseq, d.dense2, c.dense_head, D, ws.mid, ks); }),
+                   "dense head");
+                CK(K("dense_head", 2.0 * nseq * D * c.dense_head, double(D) * c.dense_head * 4,
+                     [&] { return launch_dense_f32(ws.mid, nseq, d.dense3, c.out_dim, c.dense_head, ws.out, ks); }),
+                   "dense head");
+            } else {
+                CK(K("output_projection", 2.0 * nseq * D * c.out_dim, double(D) * c.out_dim * 4,
+                     [&] { return launch_dense_f32(ws.pooled, nseq, d.output, c.out_dim, D, ws.out, ks); }),
+                   "output projection");
+            }
+        }
+        return GE_OK;
+    };
+    // Captured CUDA graphs replay the whole launch sequence of a batch shape with one call
+    // (kernel arguments, tensor maps included, are fixed per workspace and shape).
+    const bool use_graph = !(m->flags & GE_LOAD_NO_GRAPHS) && !a.profile && a.trace_layer < -1;
+    GraphKey gk{rows, ntok, nseq, nwork, nwork512, reinterpret_cast<uintptr_t>(tokens)};
+    GraphEntry* ge_ = use_graph ? find_graph(d, gk) : nullptr;
+    if (ge_) {
+        if ((e = cudaGraphLaunch(ge_->exec, st)) != cudaSuccess) return gpu_fail(e, "graph launch");
+        launches += ge_->launches;
+    } else if (use_graph) {
+        ks = d.stream;
+        const int64_t before = launches;
+        if ((e = cudaStreamBeginCapture(ks, cudaStreamCaptureModeThreadLocal)) != cudaSuccess)
+            return gpu_fail(e, "graph capture");
+        const int rc = launch_all();
+        cudaGraph_t graph = nullptr;
+        e = cudaStreamEndCapture(ks, &graph);
+        if (rc != GE_OK) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        if (e != cudaSuccess) return gpu_fail(e, "graph capture");
+        cudaGraphExec_t exec = nullptr;
+        e = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) return gpu_fail(e, "graph instantiation");
+        store_graph(d, gk, exec, launches - before);
+        if ((e = cudaGraphLaunch(exec, st)) != cudaSuccess) return gpu_fail(e, "graph launch");
     } else {
-        CK(K("mean_pool", 0, double(ntok) * D * 4, [&] { return launch_mean_pool(ws.y, D, ws.seqs, nseq, ws.pooled, st); }),
-           "mean pool");
-        if (c.has_dense) {
-            CK(K("dense_head", 2.0 * nseq * D * c.dense_head, double(D) * c.dense_head * 4,
-                 [&] { return launch_dense_f32(ws.pooled, nseq, d.dense2, c.dense_head, D, ws.mid, st); }),
-               "dense head");
-            CK(K("dense_head", 2.0 * nseq * D * c.dense_head, double(D) * c.dense_head * 4,
-                 [&] { return launch_dense_f32(ws.mid, nseq, d.dense3, c.out_dim, c.dense_head, ws.out, st); }),
-               "dense head");
-        } else {
-            CK(K("output_projection", 2.0 * nseq * D * c.out_dim, double(D) * c.out_dim * 4,
-                 [&] { return launch_dense_f32(ws.pooled, nseq, d.output, c.out_dim, D, ws.out, st); }),
-               "output projection");
-        }
-        result = ws.out;
+        const int rc = launch_all();
+        if (rc != GE_OK) return rc;
     }
+    const float* result = a.trace_layer >= 0 ? ws.x : a.trace_layer == -1 ? ws.y : ws.out;
+    const int width = a.trace_layer >= -1 ? D : c.out_dim;
     const size_t out_elems = a.trace_layer >= -1 ? size_t(ntok) * D : size_t(nseq) * width;
     float* host_out = a.trace_layer >= -1 ? a.trace_out : a.out;
     m->launches += launches;

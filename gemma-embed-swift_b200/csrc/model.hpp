@@ -65,6 +65,22 @@ struct Workspace {
     int* h_err = nullptr;
 };
 
+// A captured forward for one batch shape on one workspace.
+struct GraphKey {
+    int rows = 0, ntok = 0, nseq = 0, nwork = 0, nwork512 = 0;
+    uintptr_t tokens = 0;  // the token buffer the embedding kernel reads
+    bool operator==(const GraphKey& o) const {
+        return rows == o.rows && ntok == o.ntok && nseq == o.nseq && nwork == o.nwork && nwork512 == o.nwork512 &&
+               tokens == o.tokens;
+    }
+};
+struct GraphEntry {
+    GraphKey key;
+    cudaGraphExec_t exec = nullptr;
+    int64_t launches = 0;
+    uint64_t last_use = 0;
+};
+
 struct Device {
     int ordinal = 0, num_sms = 148;
     std::string name;
@@ -78,6 +94,8 @@ struct Device {
     std::vector<float*> rope;  // per table: [position][pair][cos, sin]
     int* err = nullptr;
     Workspace ws;
+    std::vector<GraphEntry> graphs;  // at most kMaxGraphs, least recently used evicted
+    uint64_t graph_clock = 0;
     std::vector<void*> allocations;
 };
 
@@ -137,5 +155,8 @@ struct ForwardArgs {
     ProfileSink* profile = nullptr;  // time each kernel class instead of only running it
 };
 int run_forward(ge_model* m, Device& d, const ForwardArgs& a);
+GraphEntry* find_graph(Device& d, const GraphKey& k);
+void store_graph(Device& d, const GraphKey& k, cudaGraphExec_t exec, int64_t launches);
+void clear_graphs(Device& d);
 int set_error(ge_model* m, int code, const std::string& msg);
 }  // namespace ge

@@ -102,6 +102,7 @@ int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int3
     A.cols = k;
     if (!ge::encode_weight_maps(W, 256) || !ge::encode_activation_map(A))
         return fail(GE_ERR_GPU_FAILURE, "tensor map encoding failed");
+    TRY(ge::configure_gemm_kernels());
     ge::GemmLaunch g;
     g.a = &A;
     g.w = &W;
@@ -166,6 +167,7 @@ int ge_test_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
     TRY(cudaMemcpy(dwork.p, work.data(), work.size() * 4, cudaMemcpyHostToDevice));
     TRY(derr.alloc(sizeof(int)));
     TRY(cudaMemset(derr.p, 0, sizeof(int)));
+    TRY(ge::configure_attention_kernels());
     ge::AttnLaunch al;
     al.q = static_cast<const __half*>(dq.p);
     al.k = static_cast<const __half*>(dk.p);
