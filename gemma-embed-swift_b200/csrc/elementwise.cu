@@ -58,10 +58,11 @@ cudaError_t launch_embed(const int32_t* tokens, int ntok, int rows, const int8_t
     return cudaGetLastError();
 }
 
-// One warp per (token, head slot): slots [0, H) are query heads, [H, H+KV) key heads,
-// [H+KV, H+2KV) value heads of the fused projection row.  CPUReference.swift:225-235.
-// Lane l holds elements [Q*l, Q*l + Q) of each half of the head (Q = HD / 64), so every
-// element and its rotation partner HD/2 away sit in the same lane, loaded as 8-byte vectors.
+// One warp per token, over the head slots of its fused projection row: slots [0, H) are query
+// heads, [H, H+KV) key heads, [H+KV, H+2KV) value heads.  CPUReference.swift:225-235.
+// Lane l holds elements [Q*l, Q*l + Q) of each half of a head (Q = HD / 64), so every element
+// and its rotation partner HD/2 away sit in the same lane; the token's cos/sin pairs are read
+// once and reused for every query and key head.
 template <int HD>
 __global__ void k_qkv_norm_rope(const __half* __restrict__ qkv, int ntok, int rows, int heads, int kvh,
                                 const float* __restrict__ qw, const float* __restrict__ kw,
@@ -70,73 +71,82 @@ __global__ void k_qkv_norm_rope(const __half* __restrict__ qkv, int ntok, int ro
     constexpr int Q = HD / 64;  // elements per lane per half: 4 (hd 256) or 8 (hd 512)
     constexpr int HALF = HD / 2;
     const int slots = heads + 2 * kvh;
-    const long gw = long(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
+    const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
-    if (gw >= long(rows) * slots) return;
-    const int row = int(gw / slots), slot = int(gw % slots);
-    __half* dst;
-    const float* w = nullptr;
-    if (slot < heads) {
-        dst = q + long(row) * heads * HD + slot * HD;
-        w = qw;
-    } else if (slot < heads + kvh) {
-        dst = k + long(row) * kvh * HD + (slot - heads) * HD;
-        w = kw;
-    } else {
-        dst = v + long(row) * kvh * HD + (slot - heads - kvh) * HD;
-    }
+    if (row >= rows) return;
     const int c = lane * Q;
-    float a[Q], b[Q];
-    if (row < ntok) {
-        const __half* src = qkv + long(row) * slots * HD + slot * HD;
-#pragma unroll
-        for (int i = 0; i < Q; i += 4) {
-            const uint2 ra = *reinterpret_cast<const uint2*>(src + c + i);
-            const uint2 rb = *reinterpret_cast<const uint2*>(src + HALF + c + i);
-            const float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(&ra.x));
-            const float2 a1 = __half22float2(*reinterpret_cast<const __half2*>(&ra.y));
-            const float2 b0 = __half22float2(*reinterpret_cast<const __half2*>(&rb.x));
-            const float2 b1 = __half22float2(*reinterpret_cast<const __half2*>(&rb.y));
-            a[i] = a0.x; a[i + 1] = a0.y; a[i + 2] = a1.x; a[i + 3] = a1.y;
-            b[i] = b0.x; b[i + 1] = b0.y; b[i + 2] = b1.x; b[i + 3] = b1.y;
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < Q; i++) a[i] = b[i] = 0.f;
-    }
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < Q; i++) ss += a[i] * a[i] + b[i] * b[i];
-    ss = warp_sum(ss);
-    const float inv = 1.0f / sqrtf(ss / float(HD) + eps);
-#pragma unroll
-    for (int i = 0; i < Q; i++) {
-        a[i] = a[i] * inv * (w ? w[c + i] : 1.0f);
-        b[i] = b[i] * inv * (w ? w[HALF + c + i] : 1.0f);
-    }
-    if (w && row < ntok) {
-        // NeoX rotation of the pairs (c + i, HALF + c + i), table [position][pair][cos, sin].
-        const float* cs = rope + long(pos[row]) * HD + 2 * c;
+    const bool live = row < ntok;
+    float cs_c[Q], cs_s[Q];
+    if (live) {
+        const float* cs = rope + long(pos[row]) * HD + 2 * c;  // [position][pair][cos, sin]
 #pragma unroll
         for (int i = 0; i < Q; i += 2) {
             const float4 t = *reinterpret_cast<const float4*>(cs + 2 * i);
-            const float c0 = t.x, s0 = t.y, c1 = t.z, s1 = t.w;
-            const float a0 = a[i], b0 = b[i], a1 = a[i + 1], b1 = b[i + 1];
-            a[i] = a0 * c0 - b0 * s0;
-            b[i] = a0 * s0 + b0 * c0;
-            a[i + 1] = a1 * c1 - b1 * s1;
-            b[i + 1] = a1 * s1 + b1 * c1;
+            cs_c[i] = t.x;
+            cs_s[i] = t.y;
+            cs_c[i + 1] = t.z;
+            cs_s[i + 1] = t.w;
         }
     }
+    const __half* src_row = qkv + long(row) * slots * HD;
+    for (int slot = 0; slot < slots; slot++) {
+        __half* dst;
+        const float* w = nullptr;
+        if (slot < heads) {
+            dst = q + long(row) * heads * HD + slot * HD;
+            w = qw;
+        } else if (slot < heads + kvh) {
+            dst = k + long(row) * kvh * HD + (slot - heads) * HD;
+            w = kw;
+        } else {
+            dst = v + long(row) * kvh * HD + (slot - heads - kvh) * HD;
+        }
+        float a[Q], b[Q];
+        if (live) {
+            const __half* src = src_row + slot * HD;
 #pragma unroll
-    for (int i = 0; i < Q; i += 4) {
-        uint2 oa, ob;
-        *reinterpret_cast<__half2*>(&oa.x) = __floats2half2_rn(a[i], a[i + 1]);
-        *reinterpret_cast<__half2*>(&oa.y) = __floats2half2_rn(a[i + 2], a[i + 3]);
-        *reinterpret_cast<__half2*>(&ob.x) = __floats2half2_rn(b[i], b[i + 1]);
-        *reinterpret_cast<__half2*>(&ob.y) = __floats2half2_rn(b[i + 2], b[i + 3]);
-        *reinterpret_cast<uint2*>(dst + c + i) = oa;
-        *reinterpret_cast<uint2*>(dst + HALF + c + i) = ob;
+            for (int i = 0; i < Q; i += 4) {
+                const uint2 ra = *reinterpret_cast<const uint2*>(src + c + i);
+                const uint2 rb = *reinterpret_cast<const uint2*>(src + HALF + c + i);
+                const float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(&ra.x));
+                const float2 a1 = __half22float2(*reinterpret_cast<const __half2*>(&ra.y));
+                const float2 b0 = __half22float2(*reinterpret_cast<const __half2*>(&rb.x));
+                const float2 b1 = __half22float2(*reinterpret_cast<const __half2*>(&rb.y));
+                a[i] = a0.x; a[i + 1] = a0.y; a[i + 2] = a1.x; a[i + 3] = a1.y;
+                b[i] = b0.x; b[i + 1] = b0.y; b[i + 2] = b1.x; b[i + 3] = b1.y;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < Q; i++) a[i] = b[i] = 0.f;
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < Q; i++) ss += a[i] * a[i] + b[i] * b[i];
+        ss = warp_sum(ss);
+        const float inv = 1.0f / sqrtf(ss / float(HD) + eps);
+#pragma unroll
+        for (int i = 0; i < Q; i++) {
+            a[i] = a[i] * inv * (w ? w[c + i] : 1.0f);
+            b[i] = b[i] * inv * (w ? w[HALF + c + i] : 1.0f);
+        }
+        if (w && live) {  // NeoX rotation of the pairs (c + i, HALF + c + i)
+#pragma unroll
+            for (int i = 0; i < Q; i++) {
+                const float a0 = a[i], b0 = b[i];
+                a[i] = a0 * cs_c[i] - b0 * cs_s[i];
+                b[i] = a0 * cs_s[i] + b0 * cs_c[i];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < Q; i += 4) {
+            uint2 oa, ob;
+            *reinterpret_cast<__half2*>(&oa.x) = __floats2half2_rn(a[i], a[i + 1]);
+            *reinterpret_cast<__half2*>(&oa.y) = __floats2half2_rn(a[i + 2], a[i + 3]);
+            *reinterpret_cast<__half2*>(&ob.x) = __floats2half2_rn(b[i], b[i + 1]);
+            *reinterpret_cast<__half2*>(&ob.y) = __floats2half2_rn(b[i + 2], b[i + 3]);
+            *reinterpret_cast<uint2*>(dst + c + i) = oa;
+            *reinterpret_cast<uint2*>(dst + HALF + c + i) = ob;
+        }
     }
 }
 
@@ -144,8 +154,7 @@ cudaError_t launch_qkv_norm_rope(const __half* qkv, int ntok, int rows, int head
                                       const float* q_w, const float* k_w, const int32_t* positions, const float* rope,
                                       float eps, __half* q, __half* k, __half* v, cudaStream_t stream) {
     if (rows <= 0) return cudaSuccess;
-    const long warps = long(rows) * (heads + 2 * kv_heads);
-    const int blocks = int((warps + kRowsPerBlock - 1) / kRowsPerBlock);
+    const int blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
     if (hd == 256)
         k_qkv_norm_rope<256><<<blocks, 256, 0, stream>>>(qkv, ntok, rows, heads, kv_heads, q_w, k_w, positions, rope,
                                                          eps, q, k, v);

@@ -24,11 +24,13 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kBN = 256;
 
-template <int BN, bool Q8>
+// PAIR: a 2-CTA cluster computes 256 x BN tiles with tcgen05.mma.cta_group::2; each CTA
+// holds 128 rows of A and BN/2 rows of B per stage, so shared-memory traffic per MMA halves.
+template <int BN, bool Q8, bool PAIR = false>
 struct GemmLayout {
-    static constexpr int kStages = Q8 ? 3 : 4;
+    static constexpr int kStages = Q8 ? 3 : (PAIR ? 6 : 4);
     static constexpr int kA = BM * BK * 2;
-    static constexpr int kB = BN * BK * 2;
+    static constexpr int kB = (PAIR ? BN / 2 : BN) * BK * 2;
     static constexpr int kB8 = Q8 ? BN * BK : 0;
     static constexpr int kSc = Q8 ? 2 * BN * 2 : 0;
     static constexpr int kStage = (kA + kB + kB8 + kSc + 1023) / 1024 * 1024;
@@ -78,11 +80,12 @@ __device__ __forceinline__ void dequant16(uint4 raw, __half2 s2, uint32_t (&o)[8
     }
 }
 
-template <int BN, int EPI, bool Q8>
-__global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
+template <int BN, int EPI, bool Q8, bool PAIR>
+__global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR>::kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
            const __grid_constant__ CUtensorMap mapS, const __grid_constant__ CUtensorMap mapC, GemmParams p) {
-    using L = GemmLayout<BN, Q8>;
+    static_assert(!(PAIR && Q8), "the pair kernel reads fp16 weights");
+    using L = GemmLayout<BN, Q8, PAIR>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full_tma = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
@@ -94,8 +97,17 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tiles = p.N / BN;
-    const int tiles = n_tiles * (p.M / BM);
     const int kb_count = p.K / BK;
+    // Tiles in a fixed order: n fastest, so the CTAs working at one time share A rows in L2.
+    // A pair's tile covers 256 rows: the pair leader (rank 0) the first 128, rank 1 the rest.
+    const uint32_t crank = PAIR ? cluster_ctarank() : 0;
+    const int tiles = n_tiles * (PAIR ? (p.M + 2 * BM - 1) / (2 * BM) : p.M / BM);
+    const int first = PAIR ? int(blockIdx.x >> 1) : int(blockIdx.x);
+    const int step = PAIR ? int(gridDim.x >> 1) : int(gridDim.x);
+    auto tile_origin = [&](int t, int& m0, int& n0) {
+        m0 = (t / n_tiles) * (PAIR ? 2 * BM : BM) + int(crank) * BM;
+        n0 = (t % n_tiles) * BN;
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < L::kStages; s++) {
@@ -105,7 +117,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 128);
+            mbar_init(&tempty[a], PAIR ? 8 : 128);  // PAIR: one arrival per epilogue warp of both CTAs
         }
         fence_mbar_init();
     }
@@ -116,11 +128,17 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
         tma_prefetch(&mapC);
     }
     if (warp == 5) {
-        tmem_alloc(tmem_slot, 2 * BN);
-        tmem_relinquish();
+        if (PAIR) {
+            tmem_alloc_pair(tmem_slot, 2 * BN);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, 2 * BN);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync();  // the peer's barriers are initialised before any remote use
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -131,17 +149,27 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
             uint32_t ph = 0;
             long issued = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-                const int m0 = (t / n_tiles) * BM, n0 = (t % n_tiles) * BN;
+            for (int t = first; t < tiles && ok; t += step) {
+                int m0, n0;
+                tile_origin(t, m0, n0);
                 for (int kb = 0; kb < kb_count; kb++) {
                     if (!mbar_wait(&empty[s], ph ^ 1, p.err)) {
                         ok = false;
                         break;
                     }
                     uint8_t* st = smem + s * L::kStage;
-                    mbar_expect_tx(&full_tma[s], L::kA + (Q8 ? L::kB8 + L::kSc : L::kB));
-                    tma_load_2d(st, &mapA, &full_tma[s], kb * BK, m0);
-                    if (Q8) {
+                    if (PAIR) {
+                        // Both CTAs' loads complete on the leader's barrier, which expects them all.
+                        const uint32_t bar = mapa_shared(&full_tma[s], 0);
+                        if (crank == 0) mbar_expect_tx(&full_tma[s], 2 * (L::kA + L::kB));
+                        tma_load_2d_pair(st, &mapA, bar, kb * BK, m0);
+                        tma_load_2d_pair(st + L::kA, &mapB, bar, kb * BK, n0 + int(crank) * (BN / 2));
+                    } else {
+                        mbar_expect_tx(&full_tma[s], L::kA + (Q8 ? L::kB8 + L::kSc : L::kB));
+                        tma_load_2d(st, &mapA, &full_tma[s], kb * BK, m0);
+                    }
+                    if (PAIR) {
+                    } else if (Q8) {
                         tma_load_2d(st + L::kA + L::kB, &mapB, &full_tma[s], kb * BK, n0);
                         tma_load_2d(st + L::kA + L::kB + L::kB8, &mapS, &full_tma[s], n0, kb * 2);
                     } else {
@@ -154,20 +182,22 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
                     }
                 }
             }
-            // Every issued load must land before the CTA exits, also after an error.
-            for (int j = 0; j < L::kStages; j++) {
-                const long c = issued / L::kStages + (j < issued % L::kStages ? 1 : 0);
-                if (c > 0) drain_wait(&full_tma[j], uint32_t((c - 1) & 1));
-            }
+            // Every issued load must land before the CTA exits, also after an error.  A pair's
+            // loads complete on the leader's barriers, so the leader drains for both CTAs.
+            if (crank == 0)
+                for (int j = 0; j < L::kStages; j++) {
+                    const long c = issued / L::kStages + (j < issued % L::kStages ? 1 : 0);
+                    if (c > 0) drain_wait(&full_tma[j], uint32_t((c - 1) & 1));
+                }
         }
     } else if (warp == 5) {
         // ---------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            const uint32_t idesc = idesc_f16(BM, BN);
+        if (lane == 0 && crank == 0) {  // a pair's MMAs are issued by its leader alone
+            const uint32_t idesc = idesc_f16(PAIR ? 2 * BM : BM, BN);
             int s = 0, acc = 0;
             uint32_t ph = 0, acc_ph = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+            for (int t = first; t < tiles && ok; t += step) {
                 if (!mbar_wait(&tempty[acc], acc_ph ^ 1, p.err)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + uint32_t(acc * BN);
@@ -180,17 +210,30 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
                     uint8_t* st = smem + s * L::kStage;
                     const uint64_t ad = sw128_desc(smem_u32(st), 16, 1024);
                     const uint64_t bd = sw128_desc(smem_u32(st + L::kA), 16, 1024);
+                    if (PAIR) {
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; kk++)
-                        umma_f16(d, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), idesc, (kb | kk) != 0);
-                    umma_commit(&empty[s]);
+                        for (int kk = 0; kk < BK / 16; kk++)
+                            umma_f16_pair(d, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), idesc, (kb | kk) != 0);
+                        umma_commit_pair(mapa_shared(&empty[s], 0));
+                        umma_commit_pair(mapa_shared(&empty[s], 1));
+                    } else {
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; kk++)
+                            umma_f16(d, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), idesc, (kb | kk) != 0);
+                        umma_commit(&empty[s]);
+                    }
                     if (++s == L::kStages) {
                         s = 0;
                         ph ^= 1;
                     }
                 }
                 if (!ok) break;
-                umma_commit(&tfull[acc]);
+                if (PAIR) {
+                    umma_commit_pair(mapa_shared(&tfull[acc], 0));
+                    umma_commit_pair(mapa_shared(&tfull[acc], 1));
+                } else {
+                    umma_commit(&tfull[acc]);
+                }
                 if (++acc == 2) {
                     acc = 0;
                     acc_ph ^= 1;
@@ -222,10 +265,11 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
         };
         int acc = 0;
         uint32_t acc_ph = 0;
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        for (int t = first; t < tiles; t += step) {
             if (!mbar_wait(&tfull[acc], acc_ph, p.err)) break;
             tc_fence_after();
-            const int m0 = (t / n_tiles) * BM, n0 = (t % n_tiles) * BN;
+            int m0, n0;
+            tile_origin(t, m0, n0);
             const int y = m0 + warp * 32;
             const long row = y + lane;
             const uint32_t taddr = tmem + (uint32_t(warp * 32) << 16) + uint32_t(acc * BN);
@@ -281,7 +325,12 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
                 }
             }
             tc_fence_before();
-            mbar_arrive(&tempty[acc]);
+            if (PAIR) {  // the accumulator is released to the leader, which issues the MMAs
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(&tempty[acc], 0));
+            } else {
+                mbar_arrive(&tempty[acc]);
+            }
             if (++acc == 2) {
                 acc = 0;
                 acc_ph ^= 1;
@@ -296,7 +345,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
         int s = 0;
         uint32_t ph = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        for (int t = first; t < tiles && ok; t += step) {
             for (int kb = 0; kb < kb_count; kb++) {
                 if (!mbar_wait(&full_tma[s], ph, p.err)) {
                     ok = false;
@@ -331,9 +380,13 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8>::kThreads, 1)
 
     tc_fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync();  // neither CTA leaves while the other may still signal it
     if (warp == 5) {
         tc_fence_after();
-        tmem_dealloc(tmem, 2 * BN);
+        if (PAIR)
+            tmem_dealloc_pair(tmem, 2 * BN);
+        else
+            tmem_dealloc(tmem, 2 * BN);
     }
 }
 
@@ -372,6 +425,8 @@ bool encode_weight_maps(DevWeight& w, int bn) {
                        CU_TENSOR_MAP_SWIZZLE_NONE);
     if (ok && w.f16)
         ok = encode_2d(&w.map_f16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.f16, w.K, w.N, BK, bn,
+                       CU_TENSOR_MAP_SWIZZLE_128B) &&
+             encode_2d(&w.map_f16_half, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.f16, w.K, w.N, BK, bn / 2,
                        CU_TENSOR_MAP_SWIZZLE_128B);
     return ok;
 }
@@ -387,27 +442,34 @@ bool encode_activation_map(DevActivation& a) {
                      CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int EPI, bool Q8>
+template <int EPI, bool Q8, bool PAIR>
 static cudaError_t configure_t() {
-    using L = GemmLayout<kBN, Q8>;
-    return cudaFuncSetAttribute(k_gemm<kBN, EPI, Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    using L = GemmLayout<kBN, Q8, PAIR>;
+    return cudaFuncSetAttribute(k_gemm<kBN, EPI, Q8, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+}
+
+template <int EPI>
+static cudaError_t configure_epi() {
+    cudaError_t e = configure_t<EPI, false, false>();
+    if (e == cudaSuccess) e = configure_t<EPI, true, false>();
+    if (e == cudaSuccess) e = configure_t<EPI, false, true>();
+    return e;
 }
 
 // Sets the shared-memory limit of every GEMM variant on the current device; runs at load,
 // before any stream capture.
 cudaError_t configure_gemm_kernels() {
-    cudaError_t e = cudaSuccess;
-    for (cudaError_t x : {configure_t<EPI_F32, false>(), configure_t<EPI_F32, true>(), configure_t<EPI_F16, false>(),
-                          configure_t<EPI_F16, true>(), configure_t<EPI_GEGLU, false>(), configure_t<EPI_GEGLU, true>(),
-                          configure_t<EPI_GELU_MUL, false>(), configure_t<EPI_GELU_MUL, true>()})
-        if (e == cudaSuccess) e = x;
+    cudaError_t e = configure_epi<EPI_F32>();
+    if (e == cudaSuccess) e = configure_epi<EPI_F16>();
+    if (e == cudaSuccess) e = configure_epi<EPI_GEGLU>();
+    if (e == cudaSuccess) e = configure_epi<EPI_GELU_MUL>();
     return e;
 }
 
-template <int EPI, bool Q8>
+template <int EPI, bool Q8, bool PAIR>
 static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
-    using L = GemmLayout<kBN, Q8>;
-    auto kern = k_gemm<kBN, EPI, Q8>;
+    using L = GemmLayout<kBN, Q8, PAIR>;
+    auto kern = k_gemm<kBN, EPI, Q8, PAIR>;
     GemmParams p{};
     p.M = g.m_rows;
     p.N = g.w->N;
@@ -417,9 +479,7 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
     p.aux = g.aux;
     p.ldaux = g.ldaux;
     p.err = g.err;
-    const int tiles = (g.m_rows / BM) * (g.w->N / kBN);
-    const int grid = tiles < g.num_sms ? tiles : g.num_sms;
-    const CUtensorMap& mb = Q8 ? g.w->map_q8 : g.w->map_f16;
+    const CUtensorMap& mb = Q8 ? g.w->map_q8 : (PAIR ? g.w->map_f16_half : g.w->map_f16);
     // Output map: boxes of 32 rows x 128 bytes (32 fp32 or 64 fp16 columns), 128-byte swizzle.
     const bool f32 = EPI == EPI_F32;
     const int out_cols = EPI == EPI_GEGLU ? g.w->N / 2 : g.w->N;
@@ -428,8 +488,35 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
     if (!encode_2d(&mc, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, f32 ? 4 : 2, g.out,
                    uint64_t(g.ldo), uint64_t(g.m_rows), f32 ? 32 : 64, 32, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
-    kern<<<grid, L::kThreads, L::kBytes, stream>>>(g.a->map, mb, g.w->map_scales, mc, p);
-    return cudaGetLastError();
+    if (!PAIR) {
+        const int tiles = (g.m_rows / BM) * (g.w->N / kBN);
+        const int grid = tiles < g.num_sms ? tiles : g.num_sms;
+        kern<<<grid, L::kThreads, L::kBytes, stream>>>(g.a->map, mb, g.w->map_scales, mc, p);
+        return cudaGetLastError();
+    }
+    // CTA pairs: clusters of 2, one pair per two SMs, each pair looping over 256-row tiles.
+    const int tiles = ((g.m_rows + 2 * BM - 1) / (2 * BM)) * (g.w->N / kBN);
+    const int pairs = tiles < g.num_sms / 2 ? tiles : g.num_sms / 2;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(L::kThreads);
+    cfg.dynamicSmemBytes = L::kBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, g.a->map, mb, g.w->map_scales, mc, p);
+}
+
+template <int EPI>
+static cudaError_t launch_epi(const GemmLaunch& g, cudaStream_t stream, bool q8, bool pair) {
+    if (q8) return launch_t<EPI, true, false>(g, stream);
+    if (pair) return launch_t<EPI, false, true>(g, stream);
+    return launch_t<EPI, false, false>(g, stream);
 }
 
 cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream) {
@@ -439,11 +526,12 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream) {
     // The Q8 path needs the Q8 planes; weights without them always take the fp16 path.
     if (!g.w->f16 && !g.w->q8) return cudaErrorInvalidValue;
     const bool q8 = g.w->q8 && (g.use_q8 || !g.w->f16);
+    const bool pair = !q8 && g.mode != GEMM_SINGLE;
     switch (g.epilogue) {
-    case EPI_F32: return q8 ? launch_t<EPI_F32, true>(g, stream) : launch_t<EPI_F32, false>(g, stream);
-    case EPI_F16: return q8 ? launch_t<EPI_F16, true>(g, stream) : launch_t<EPI_F16, false>(g, stream);
-    case EPI_GEGLU: return q8 ? launch_t<EPI_GEGLU, true>(g, stream) : launch_t<EPI_GEGLU, false>(g, stream);
-    case EPI_GELU_MUL: return q8 ? launch_t<EPI_GELU_MUL, true>(g, stream) : launch_t<EPI_GELU_MUL, false>(g, stream);
+    case EPI_F32: return launch_epi<EPI_F32>(g, stream, q8, pair);
+    case EPI_F16: return launch_epi<EPI_F16>(g, stream, q8, pair);
+    case EPI_GEGLU: return launch_epi<EPI_GEGLU>(g, stream, q8, pair);
+    case EPI_GELU_MUL: return launch_epi<EPI_GELU_MUL>(g, stream, q8, pair);
     default: return cudaErrorInvalidValue;
     }
 }

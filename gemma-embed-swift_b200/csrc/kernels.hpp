@@ -29,7 +29,7 @@ struct DevWeight {
     int8_t* q8 = nullptr;
     __half* scales_t = nullptr;
     __half* f16 = nullptr;
-    CUtensorMap map_q8, map_scales, map_f16;
+    CUtensorMap map_q8, map_scales, map_f16, map_f16_half;  // map_f16_half: boxes of BN/2 rows (CTA pairs)
 };
 
 // A row-major fp16 activation matrix that feeds GEMMs as the A operand.
@@ -42,6 +42,10 @@ struct DevActivation {
 bool encode_weight_maps(DevWeight& w, int bn);
 bool encode_activation_map(DevActivation& a);
 
+// Which fp16-path kernel a GEMM uses: CTA pairs (tcgen05.mma.cta_group::2, 256-row tiles)
+// or single CTAs (128-row tiles).  The Q8 path always runs on single CTAs.
+enum GemmMode : int { GEMM_AUTO = 0, GEMM_SINGLE = 1, GEMM_PAIR = 2 };
+
 struct GemmLaunch {
     const DevActivation* a;
     const DevWeight* w;
@@ -52,6 +56,7 @@ struct GemmLaunch {
     const float* aux = nullptr;
     int ldaux = 0;
     bool use_q8 = false;  // dequantise Q8 tiles in shared memory instead of reading fp16 weights
+    int mode = GEMM_AUTO;
     int* err;
     int num_sms;
 };

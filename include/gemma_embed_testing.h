@@ -19,11 +19,11 @@ extern "C" {
 /* Kernels.gemm (Metal/MetalForward.swift:513-557): out = a * W^T for a fp16 `a` [m][k]
  * (bit patterns) and a Q8_0 weight given as GGUF rows `w_q8_0` [n][k/32 * 34 bytes].
  * epilogue: 0 fp32 store, 1 fp16 store, 2 GeGLU over rows interleaved as the loader does
- * (out has n/2 columns), 3 gelu(acc) * aux (aux fp32 [m][n]).  use_q8 selects the
- * in-shared-memory dequantisation path instead of the fp16-resident weights.  Results are
- * returned as fp32 [m][n] (or [m][n/2]). */
+ * (out has n/2 columns), 3 gelu(acc) * aux (aux fp32 [m][n]).  path: 0 fp16-resident
+ * weights on single CTAs, 1 the in-shared-memory Q8 dequantisation, 2 fp16 weights on CTA
+ * pairs (tcgen05.mma.cta_group::2).  Results are returned as fp32 [m][n] (or [m][n/2]). */
 GE_API int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w_q8_0, int32_t n, int32_t epilogue,
-                        int32_t use_q8, const float* aux, float* out);
+                        int32_t path, const float* aux, float* out);
 
 /* Kernels.attention (Metal/MetalForward.swift:669-694): q [ntok][heads][hd], k and v
  * [ntok][kv_heads][hd] as fp16 bit patterns, sequences tiling [0, ntok); out receives fp16

@@ -24,6 +24,8 @@ def max_rel(got, want):
 
 
 def gemm(ge, a16, wq, n, epi, use_q8, aux=None):
+    """use_q8: False/0 fp16 weights on single CTAs, True/1 Q8 dequantised in shared memory,
+    2 fp16 weights on CTA pairs."""
     from importlib import import_module
     L = import_module("gemma-embed-swift_b200._lib").lib()
     m, k = a16.shape
@@ -62,12 +64,15 @@ def test_gemm_shapes_fp32(ge, synth, cuda_device, m, k, n):
     want = a.astype(np.float64) @ wd.T
     got16 = gemm(ge, a, wq, n, 0, use_q8=False)
     got8 = gemm(ge, a, wq, n, 0, use_q8=True)
+    gotp = gemm(ge, a, wq, n, 0, use_q8=2)
     assert max_rel(got16, want) < TOL_F32
     # The Q8 path dequantises in shared memory to the very same fp16 operand: identical bits.
     assert got8.tobytes() == got16.tobytes()
+    # CTA pairs multiply the same operands with 256-row instructions: identical bits.
+    assert gotp.tobytes() == got16.tobytes()
 
 
-@pytest.mark.parametrize("use_q8", [False, True])
+@pytest.mark.parametrize("use_q8", [False, True, 2])
 def test_gemm_epilogues(ge, synth, oracle, cuda_device, use_q8):
     m, k, ff = 300, 768, 1152
     a, wq_gate, wd_gate = make_case(synth, m, k, ff, seed=11)
