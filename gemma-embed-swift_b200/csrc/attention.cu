@@ -121,10 +121,13 @@ __global__ void __launch_bounds__(256) k_attention_simt(const __half* __restrict
 //   warp 0      TMA producer: the Q tile once, then K and V tiles of 64 keys into 2-slot rings
 //   warp 1      tcgen05.mma issuer and tensor-memory owner: S_j = Q K_j^T (128 x 64, fp32 in
 //               TMEM, two buffers) and O += P_j V_j (128 x 256, fp32 in TMEM)
-//   warps 2-5   softmax, one thread per query row: masks S_j, keeps the running maximum and
-//               sum, writes P_j (fp16, 128-byte swizzled) to shared memory, and rescales O in
-//               tensor memory only when the row maximum grows by more than kRescale; until then
-//               every term of the row uses the same stale maximum, so the result is exact
+//   warps 2-9   softmax, two threads per query row (one per 32-key half of a block; warps w
+//               and w + 4 share a tensor-memory lane quarter): mask S_j, exchange the row's
+//               block maximum through shared memory, keep running maximum and partial sums,
+//               write their half of P_j (fp16, 128-byte swizzled) to shared memory, and rescale
+//               their half of O in tensor memory only when the row maximum grows by more than
+//               kRescale; until then every term of the row uses the same stale maximum, so the
+//               result is exact
 // Tensor memory: O in columns [0, 256), the S buffers in [256, 320) and [320, 384).
 constexpr int kTcQ = 128;
 constexpr int kTcKeys = 64;
@@ -137,8 +140,10 @@ constexpr int kPBytes = kTcQ * kTcKeys * 2;   // 16 KB per buffer: [128 rows][64
 constexpr int kOffK = kQBytes;
 constexpr int kOffV = kOffK + 2 * kKVBytes;
 constexpr int kOffP = kOffV + 2 * kKVBytes;
-constexpr int kOffBar = kOffP + 2 * kPBytes;
-constexpr int kTcSmem = kOffBar + 256 + 1024;
+constexpr int kOffRed = kOffP + 2 * kPBytes;    // [2 halves][128 rows] floats: row maxima, then sums
+constexpr int kOffBar = kOffRed + 2 * kTcQ * 4;
+constexpr int kTcSmem = kOffBar + 128 + 1024;
+constexpr int kTcThreads = 320;
 constexpr uint32_t kTmemO = 0, kTmemS = 256;
 
 struct TcAttnParams {
@@ -154,7 +159,7 @@ __device__ __forceinline__ void drain(uint64_t* bar, uint32_t parity) {
     }
 }
 
-__global__ void __launch_bounds__(192, 1) k_attention_tc(const __grid_constant__ CUtensorMap mapQ,
+__global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_constant__ CUtensorMap mapQ,
                                                           const __grid_constant__ CUtensorMap mapK,
                                                           const __grid_constant__ CUtensorMap mapV, TcAttnParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -193,7 +198,7 @@ __global__ void __launch_bounds__(192, 1) k_attention_tc(const __grid_constant__
             mbar_init(&v_full[i], 1);
             mbar_init(&v_empty[i], 1);
             mbar_init(&s_full[i], 1);
-            mbar_init(&p_full[i], 128);
+            mbar_init(&p_full[i], 256);
             mbar_init(&pv_done[i], 1);
         }
         fence_mbar_init();
@@ -292,65 +297,80 @@ __global__ void __launch_bounds__(192, 1) k_attention_tc(const __grid_constant__
             if (ok && nblk > 0) issue_pv(nblk - 1);
         }
     } else {
-        // ---------------------------------------------------------- softmax (one thread per row)
-        const int quad = warp & 3;  // TMEM lane group this warp may access
+        // ---------------------------------------------------------- softmax (two threads per row)
+        const int quad = warp & 3;         // tensor-memory lane quarter of this warp
+        const int half = (warp - 2) >> 2;  // which 32 keys of each block, and which 128 O columns
         const int r = quad * 32 + lane;
         const int qi = int(q0) + r;
         const uint32_t lane_base = tmem + (uint32_t(quad * 32) << 16);
+        float* red = reinterpret_cast<float*>(smem + kOffRed);
+        // The two warps of a quarter meet on named barrier 1 + quad (64 threads).
+        auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory"); };
         // Keys this row sees: [row_lo, row_hi) of its sequence.
         const int row_lo = p.hw > 0 ? max(qi - p.hw, 0) : 0;
         const int row_hi = p.hw > 0 ? min(qi + p.hw + 1, int(len)) : int(len);
-        float m_used = -INFINITY, l = 0.f;  // running maximum (log2 units) and sum
+        float m_used = -INFINITY, l = 0.f;  // running maximum (log2 units) and this half's sum
+        // `ok` stays warp-uniform, and after a failed wait the loop keeps running without work,
+        // so both warps of a quarter reach every named barrier and every tcgen05 load or store
+        // is executed by a whole warp.
         bool ok = true;
+        auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+            const bool w = ok && mbar_wait(bar, parity, p.err);
+            ok = __all_sync(0xffffffffu, w);
+        };
         for (int j = 0; j < nblk; j++) {
             const int b = j & 1;
             const uint32_t ph = uint32_t((j >> 1) & 1);
-            if (!mbar_wait(&s_full[b], ph, p.err)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            uint32_t sr[64];
-            tmem_ld32(lane_base + kTmemS + b * kTcKeys, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-            tmem_ld32(lane_base + kTmemS + b * kTcKeys + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
-            tmem_wait_ld();
-            const int kb = k_start + j * kTcKeys;
-            // Scores in log2 units: p = 2^(s log2e - m), one FFMA and one ex2 per key.
-            float mb = -INFINITY;
-            if (kb >= row_lo && kb + kTcKeys <= row_hi) {  // every key of the block is visible
+            wait_all(&s_full[b], ph);
+            uint32_t sr[32];
+            float mh = -INFINITY;
+            const int kb = k_start + j * kTcKeys + half * 32;
+            if (ok) {
+                tc_fence_after();
+                tmem_ld32(lane_base + kTmemS + b * kTcKeys + half * 32, sr);
+                tmem_wait_ld();
+                // Scores in log2 units: p = 2^(s log2e - m), one FFMA and one ex2 per key.
+                if (kb >= row_lo && kb + 32 <= row_hi) {  // every key of this half is visible
 #pragma unroll
-                for (int i = 0; i < 64; i++) {
-                    const float t = __uint_as_float(sr[i]) * kLog2e;
-                    sr[i] = __float_as_uint(t);
-                    mb = fmaxf(mb, t);
-                }
-            } else {
+                    for (int i = 0; i < 32; i++) {
+                        const float t = __uint_as_float(sr[i]) * kLog2e;
+                        sr[i] = __float_as_uint(t);
+                        mh = fmaxf(mh, t);
+                    }
+                } else {
 #pragma unroll
-                for (int i = 0; i < 64; i++) {
-                    const int kj = kb + i;
-                    const float t = (kj >= row_lo && kj < row_hi) ? __uint_as_float(sr[i]) * kLog2e : -INFINITY;
-                    sr[i] = __float_as_uint(t);
-                    mb = fmaxf(mb, t);
+                    for (int i = 0; i < 32; i++) {
+                        const int kj = kb + i;
+                        const float t = (kj >= row_lo && kj < row_hi) ? __uint_as_float(sr[i]) * kLog2e : -INFINITY;
+                        sr[i] = __float_as_uint(t);
+                        mh = fmaxf(mh, t);
+                    }
                 }
             }
-            // Rescale O when this row's maximum grew past the threshold (warp-uniform decision:
-            // tensor-memory loads and stores are warp-collective).
+            // Row maximum of the block from both halves (the slot is rewritten only after the
+            // next pair_sync, by which time the partner has read it).
+            red[half * kTcQ + r] = mh;
+            pair_sync();
+            const float mb = fmaxf(mh, red[(1 - half) * kTcQ + r]);
+            pair_sync();
+            if (!ok) continue;
+            // Rescale this half of O when the row's maximum grew past the threshold (both halves
+            // decide alike; tensor-memory loads and stores are warp-collective).
             const bool grow = mb > m_used + kRescale && m_used != -INFINITY;
             if (__any_sync(0xffffffffu, grow)) {
                 const float alpha = grow ? ex2_approx(m_used - mb) : 1.0f;
-                if (j > 0 && !mbar_wait(&pv_done[(j - 1) & 1], uint32_t(((j - 1) >> 1) & 1), p.err)) {
-                    ok = false;
-                    break;
-                }
+                if (j > 0) wait_all(&pv_done[(j - 1) & 1], uint32_t(((j - 1) >> 1) & 1));
+                if (!ok) continue;
                 tc_fence_after();
 #pragma unroll 1
-                for (int c = 0; c < kTcHd / 32; c++) {
+                for (int c = 0; c < kTcHd / 64; c++) {
                     uint32_t o[32];
-                    tmem_ld32(lane_base + kTmemO + c * 32, o);
+                    const uint32_t col = kTmemO + uint32_t(half * (kTcHd / 2) + c * 32);
+                    tmem_ld32(lane_base + col, o);
                     tmem_wait_ld();
 #pragma unroll
                     for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tmem_st32(lane_base + kTmemO + c * 32, o);
+                    tmem_st32(lane_base + col, o);
                 }
                 tmem_wait_st();
                 if (grow) {
@@ -360,43 +380,46 @@ __global__ void __launch_bounds__(192, 1) k_attention_tc(const __grid_constant__
             }
             if (m_used == -INFINITY) m_used = mb;  // first block with a visible key (O and l are still 0)
             // P_j goes to buffer b once PV_{j-2}, which read that buffer, has completed.
-            if (j >= 2 && !mbar_wait(&pv_done[b], uint32_t(((j - 2) >> 1) & 1), p.err)) {
-                ok = false;
-                break;
-            }
+            if (j >= 2) wait_all(&pv_done[b], uint32_t(((j - 2) >> 1) & 1));
+            if (!ok) continue;
             uint8_t* prow = smem + kOffP + b * kPBytes + r * 128;
             float sum = 0.f;
             const float mu = m_used == -INFINITY ? 0.f : m_used;
 #pragma unroll
-            for (int c = 0; c < 8; c++) {  // 8 chunks of 8 keys = 16 bytes each
+            for (int c = 0; c < 4; c++) {  // 4 chunks of 8 keys = 16 bytes each
                 uint32_t w[4];
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
-                    const float p0 = ex2_approx(__uint_as_float(sr[c * 8 + 2 * e]) - mu);   // 2^-inf = 0
+                    const float p0 = ex2_approx(__uint_as_float(sr[c * 8 + 2 * e]) - mu);  // 2^-inf = 0
                     const float p1 = ex2_approx(__uint_as_float(sr[c * 8 + 2 * e + 1]) - mu);
                     sum += p0 + p1;
                     __half2 hp = __floats2half2_rn(p0, p1);
                     w[e] = *reinterpret_cast<uint32_t*>(&hp);
                 }
-                *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+                const int chunk = half * 4 + c;
+                *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
             }
             l += sum;
             fence_proxy_async_smem();
             tc_fence_before();
             mbar_arrive(&p_full[b]);
         }
-        // ---- epilogue: O / l for the rows of this sequence
+        // ---- epilogue: O / l for the rows of this sequence; each half stores its 128 columns
+        red[half * kTcQ + r] = l;
+        pair_sync();
+        const float lt = l + red[(1 - half) * kTcQ + r];
         if (ok && nblk > 0) {
             const int jl = nblk - 1;
-            if (mbar_wait(&pv_done[jl & 1], uint32_t((jl >> 1) & 1), p.err)) {
+            wait_all(&pv_done[jl & 1], uint32_t((jl >> 1) & 1));
+            if (ok) {
                 tc_fence_after();
-                const float inv = l > 0.f ? 1.0f / l : 0.f;
-                __half* orow = p.out + (long(seq_start) + qi) * long(p.heads) * kTcHd + h * kTcHd;
+                const float inv = lt > 0.f ? 1.0f / lt : 0.f;
+                __half* orow = p.out + (long(seq_start) + qi) * long(p.heads) * kTcHd + h * kTcHd + half * (kTcHd / 2);
                 const bool store = qi < int(len);
 #pragma unroll 1
-                for (int c = 0; c < kTcHd / 32; c++) {
+                for (int c = 0; c < kTcHd / 64; c++) {
                     uint32_t o[32];
-                    tmem_ld32(lane_base + kTmemO + c * 32, o);
+                    tmem_ld32(lane_base + kTmemO + uint32_t(half * (kTcHd / 2) + c * 32), o);
                     tmem_wait_ld();
                     if (store) {
                         uint32_t pk[16];
@@ -441,7 +464,7 @@ cudaError_t configure_attention_kernels() {
 static cudaError_t launch_tc(const AttnLaunch& a, cudaStream_t stream) {
     TcAttnParams p{a.work, a.out, a.heads, a.kv_heads, a.half_window, a.err};
     dim3 grid(a.work_items, a.heads);
-    k_attention_tc<<<grid, 192, kTcSmem, stream>>>(a.maps->q, a.maps->k, a.maps->v, p);
+    k_attention_tc<<<grid, kTcThreads, kTcSmem, stream>>>(a.maps->q, a.maps->k, a.maps->v, p);
     return cudaGetLastError();
 }
 
