@@ -290,11 +290,62 @@ cudaError_t launch_rmsnorm_rows(const float* x, int rows, int width, float pre, 
     return cudaGetLastError();
 }
 
-// pooled[s][c] = sum over the sequence's rows / length (Elementwise.metal:243-256).  One
-// block per sequence: warp w sums rows w, w + 8, ... of every column, then the 8 partial sums
-// of a column are added in warp order, so a sequence's mean depends only on its own rows.
-__global__ void k_mean_pool(const float* __restrict__ y, int width, const uint32_t* __restrict__ seqs,
-                            float* __restrict__ pooled) {
+// pooled[s][c] = sum over the sequence's rows / length (Elementwise.metal:243-256), in two
+// levels with a fixed order, so a sequence's mean depends only on its own rows:
+//   k_pool_partial: one block per (sequence, chunk of kPoolChunk rows counted from the
+//   sequence start); warp w sums rows w, w + 8, ... of the chunk, then the 8 warp sums of a
+//   column are added in warp order into partial[chunk][c];
+//   k_pool_final: one block per sequence adds its chunks in order and divides by the length.
+constexpr int kPoolChunk = 256;
+
+__global__ void k_pool_partial(const float* __restrict__ y, int width, const uint32_t* __restrict__ seqs,
+                               const uint32_t* __restrict__ chunk_base, float* __restrict__ partial) {
+    extern __shared__ float part[];  // [8][width]
+    const int s = blockIdx.y;
+    const uint32_t start = seqs[2 * s], len = seqs[2 * s + 1];
+    const uint32_t r0 = blockIdx.x * kPoolChunk;
+    if (r0 >= len) return;
+    const uint32_t r1 = min(len, r0 + kPoolChunk);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int c0 = lane * 4; c0 < width; c0 += 128) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (uint32_t r = r0 + warp; r < r1; r += 8) {
+            const float4 v = *reinterpret_cast<const float4*>(y + long(start + r) * width + c0);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        *reinterpret_cast<float4*>(part + warp * width + c0) = acc;
+    }
+    __syncthreads();
+    float* out = partial + (long(chunk_base[s]) + blockIdx.x) * width;
+    for (int c = threadIdx.x; c < width; c += blockDim.x) {
+        float acc = 0.f;
+        for (int w = 0; w < 8; w++) acc += part[w * width + c];
+        out[c] = acc;
+    }
+}
+
+__global__ void k_pool_final(const float* __restrict__ partial, int width, const uint32_t* __restrict__ seqs,
+                             const uint32_t* __restrict__ chunk_base, float* __restrict__ pooled) {
+    const int s = blockIdx.x;
+    const uint32_t len = seqs[2 * s + 1];
+    const uint32_t nchunks = (len + kPoolChunk - 1) / kPoolChunk;
+    const float* in = partial + long(chunk_base[s]) * width;
+    for (int c = threadIdx.x; c < width; c += blockDim.x) {
+        float acc = 0.f;
+        for (uint32_t k = 0; k < nchunks; k++) acc += in[long(k) * width + c];
+        pooled[long(s) * width + c] = acc / float(len);
+    }
+}
+
+int pool_chunks(uint32_t len) { return int((len + kPoolChunk - 1) / kPoolChunk); }
+
+// Single-launch mean pool for callers that only hold the sequence ranges on the device: one
+// block per sequence, warp w summing rows w, w + 8, ..., then the 8 warp sums in order.
+__global__ void k_mean_pool_seq(const float* __restrict__ y, int width, const uint32_t* __restrict__ seqs,
+                                float* __restrict__ pooled) {
     extern __shared__ float part[];  // [8][width]
     const uint32_t start = seqs[2 * blockIdx.x], len = seqs[2 * blockIdx.x + 1];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -317,50 +368,21 @@ __global__ void k_mean_pool(const float* __restrict__ y, int width, const uint32
     }
 }
 
-cudaError_t launch_mean_pool(const float* y, int width, const uint32_t* seqs, int nseq, float* pooled,
-                             cudaStream_t stream) {
+cudaError_t launch_mean_pool_seq(const float* y, int width, const uint32_t* seqs, int nseq, float* pooled,
+                                 cudaStream_t stream) {
     if (nseq <= 0) return cudaSuccess;
     if (width % 128) return cudaErrorInvalidValue;
-    k_mean_pool<<<nseq, 256, 8 * width * sizeof(float), stream>>>(y, width, seqs, pooled);
+    k_mean_pool_seq<<<nseq, 256, 8 * width * sizeof(float), stream>>>(y, width, seqs, pooled);
     return cudaGetLastError();
 }
 
-// out[s][n] = sum_k in[s][k] * (scale * q)[n][k], fp32: one warp per output column n.
-__global__ void k_dense_rows(const float* __restrict__ in, int nrows, const int8_t* __restrict__ q,
-                             const __half* __restrict__ st, int N, int K, float* __restrict__ out) {
-    const int n = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (n >= N) return;
-    const int8_t* qr = q + long(n) * K;
-    for (int s = 0; s < nrows; s++) {
-        const float* xr = in + long(s) * K;
-        float acc = 0.f;
-        for (int k = lane; k < K; k += 32) acc += xr[k] * (__half2float(st[long(k >> 5) * N + n]) * float(qr[k]));
-        acc = warp_sum(acc);
-        if (lane == 0) out[long(s) * N + n] = acc;
-    }
-}
-
-cudaError_t launch_dense_rows(const float* in, int nrows, const DevWeight& w, float* out, cudaStream_t stream) {
-    if (nrows <= 0) return cudaSuccess;
-    k_dense_rows<<<(w.N + kRowsPerBlock - 1) / kRowsPerBlock, 256, 0, stream>>>(in, nrows, w.q8, w.scales_t, w.N, w.K,
-                                                                                 out);
-    return cudaGetLastError();
-}
-
-}  // namespace ge
-
-namespace ge {
-
-// positions[start + i] = i for every sequence (PackedBatch.append, MetalForward.swift:17-21).
-__global__ void k_positions(const uint32_t* __restrict__ seqs, int32_t* __restrict__ positions) {
-    const uint32_t start = seqs[2 * blockIdx.x], len = seqs[2 * blockIdx.x + 1];
-    for (uint32_t i = threadIdx.x; i < len; i += blockDim.x) positions[start + i] = int32_t(i);
-}
-
-cudaError_t launch_positions(const uint32_t* seqs, int nseq, int32_t* positions, cudaStream_t stream) {
+cudaError_t launch_mean_pool(const float* y, int width, const uint32_t* seqs, int nseq, int max_chunks,
+                             const uint32_t* chunk_base, float* partial, float* pooled, cudaStream_t stream) {
     if (nseq <= 0) return cudaSuccess;
-    k_positions<<<nseq, 256, 0, stream>>>(seqs, positions);
+    if (width % 128) return cudaErrorInvalidValue;
+    k_pool_partial<<<dim3(max_chunks, nseq), 256, 8 * width * sizeof(float), stream>>>(y, width, seqs, chunk_base,
+                                                                                     partial);
+    k_pool_final<<<nseq, 256, 0, stream>>>(partial, width, seqs, chunk_base, pooled);
     return cudaGetLastError();
 }
 

@@ -28,7 +28,7 @@ constexpr int kBN = 256;
 // holds 128 rows of A and BN/2 rows of B per stage, so shared-memory traffic per MMA halves.
 template <int BN, bool Q8, bool PAIR = false>
 struct GemmLayout {
-    static constexpr int kStages = Q8 ? 3 : (PAIR ? 6 : 4);
+    static constexpr int kStages = Q8 ? 3 : ((PAIR || BN < 256) ? 6 : 4);
     static constexpr int kA = BM * BK * 2;
     static constexpr int kB = (PAIR ? BN / 2 : BN) * BK * 2;
     static constexpr int kB8 = Q8 ? BN * BK : 0;
@@ -442,10 +442,10 @@ bool encode_activation_map(DevActivation& a) {
                      CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int EPI, bool Q8, bool PAIR>
+template <int EPI, bool Q8, bool PAIR, int BN = kBN>
 static cudaError_t configure_t() {
-    using L = GemmLayout<kBN, Q8, PAIR>;
-    return cudaFuncSetAttribute(k_gemm<kBN, EPI, Q8, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    using L = GemmLayout<BN, Q8, PAIR>;
+    return cudaFuncSetAttribute(k_gemm<BN, EPI, Q8, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
 }
 
 template <int EPI>
@@ -453,6 +453,7 @@ static cudaError_t configure_epi() {
     cudaError_t e = configure_t<EPI, false, false>();
     if (e == cudaSuccess) e = configure_t<EPI, true, false>();
     if (e == cudaSuccess) e = configure_t<EPI, false, true>();
+    if (EPI != EPI_GEGLU && e == cudaSuccess) e = configure_t<EPI, false, false, 128>();
     return e;
 }
 
@@ -466,10 +467,10 @@ cudaError_t configure_gemm_kernels() {
     return e;
 }
 
-template <int EPI, bool Q8, bool PAIR>
+template <int EPI, bool Q8, bool PAIR, int BN = kBN>
 static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
-    using L = GemmLayout<kBN, Q8, PAIR>;
-    auto kern = k_gemm<kBN, EPI, Q8, PAIR>;
+    using L = GemmLayout<BN, Q8, PAIR>;
+    auto kern = k_gemm<BN, EPI, Q8, PAIR>;
     GemmParams p{};
     p.M = g.m_rows;
     p.N = g.w->N;
@@ -479,7 +480,8 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
     p.aux = g.aux;
     p.ldaux = g.ldaux;
     p.err = g.err;
-    const CUtensorMap& mb = Q8 ? g.w->map_q8 : (PAIR ? g.w->map_f16_half : g.w->map_f16);
+    // Weight boxes: kBN rows (map_f16, map_q8) or kBN / 2 rows (CTA pairs, 128-wide tiles).
+    const CUtensorMap& mb = Q8 ? g.w->map_q8 : ((PAIR || BN != kBN) ? g.w->map_f16_half : g.w->map_f16);
     // Output map: boxes of 32 rows x 128 bytes (32 fp32 or 64 fp16 columns), 128-byte swizzle.
     const bool f32 = EPI == EPI_F32;
     const int out_cols = EPI == EPI_GEGLU ? g.w->N / 2 : g.w->N;
@@ -489,13 +491,13 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
                    uint64_t(g.ldo), uint64_t(g.m_rows), f32 ? 32 : 64, 32, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
     if (!PAIR) {
-        const int tiles = (g.m_rows / BM) * (g.w->N / kBN);
+        const int tiles = (g.m_rows / BM) * (g.w->N / BN);
         const int grid = tiles < g.num_sms ? tiles : g.num_sms;
         kern<<<grid, L::kThreads, L::kBytes, stream>>>(g.a->map, mb, g.w->map_scales, mc, p);
         return cudaGetLastError();
     }
     // CTA pairs: clusters of 2, one pair per two SMs, each pair looping over 256-row tiles.
-    const int tiles = ((g.m_rows + 2 * BM - 1) / (2 * BM)) * (g.w->N / kBN);
+    const int tiles = ((g.m_rows + 2 * BM - 1) / (2 * BM)) * (g.w->N / BN);
     const int pairs = tiles < g.num_sms / 2 ? tiles : g.num_sms / 2;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * pairs);
@@ -513,9 +515,11 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
 }
 
 template <int EPI>
-static cudaError_t launch_epi(const GemmLaunch& g, cudaStream_t stream, bool q8, bool pair) {
+static cudaError_t launch_epi(const GemmLaunch& g, cudaStream_t stream, bool q8, bool pair, bool narrow) {
     if (q8) return launch_t<EPI, true, false>(g, stream);
     if (pair) return launch_t<EPI, false, true>(g, stream);
+    if constexpr (EPI != EPI_GEGLU)
+        if (narrow) return launch_t<EPI, false, false, 128>(g, stream);
     return launch_t<EPI, false, false>(g, stream);
 }
 
@@ -526,12 +530,15 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream) {
     // The Q8 path needs the Q8 planes; weights without them always take the fp16 path.
     if (!g.w->f16 && !g.w->q8) return cudaErrorInvalidValue;
     const bool q8 = g.w->q8 && (g.use_q8 || !g.w->f16);
-    const bool pair = !q8 && g.mode != GEMM_SINGLE;
+    const bool pair = !q8 && g.mode == GEMM_PAIR;
+    // 128-wide tiles balance the last wave of the narrow projections (N <= 1280) better.
+    const bool narrow = !q8 && !pair && g.epilogue != EPI_GEGLU &&
+                        (g.mode == GEMM_NARROW || (g.mode == GEMM_AUTO && g.w->N <= 1280));
     switch (g.epilogue) {
-    case EPI_F32: return launch_epi<EPI_F32>(g, stream, q8, pair);
-    case EPI_F16: return launch_epi<EPI_F16>(g, stream, q8, pair);
-    case EPI_GEGLU: return launch_epi<EPI_GEGLU>(g, stream, q8, pair);
-    case EPI_GELU_MUL: return launch_epi<EPI_GELU_MUL>(g, stream, q8, pair);
+    case EPI_F32: return launch_epi<EPI_F32>(g, stream, q8, pair, narrow);
+    case EPI_F16: return launch_epi<EPI_F16>(g, stream, q8, pair, narrow);
+    case EPI_GEGLU: return launch_epi<EPI_GEGLU>(g, stream, q8, pair, narrow);
+    case EPI_GELU_MUL: return launch_epi<EPI_GELU_MUL>(g, stream, q8, pair, narrow);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -42,9 +42,11 @@ struct DevActivation {
 bool encode_weight_maps(DevWeight& w, int bn);
 bool encode_activation_map(DevActivation& a);
 
-// Which fp16-path kernel a GEMM uses: CTA pairs (tcgen05.mma.cta_group::2, 256-row tiles)
-// or single CTAs (128-row tiles).  The Q8 path always runs on single CTAs.
-enum GemmMode : int { GEMM_AUTO = 0, GEMM_SINGLE = 1, GEMM_PAIR = 2 };
+// Which fp16-path kernel a GEMM uses: single CTAs with 128 x 256 tiles, single CTAs with
+// 128 x 128 tiles, or CTA pairs (tcgen05.mma.cta_group::2, 256 x 256 tiles).  AUTO takes
+// 128 x 128 tiles for N <= 1280 (except GeGLU) and 128 x 256 otherwise.  The Q8 path always
+// runs single CTAs with 128 x 256 tiles.
+enum GemmMode : int { GEMM_AUTO = 0, GEMM_SINGLE = 1, GEMM_PAIR = 2, GEMM_NARROW = 3 };
 
 struct GemmLaunch {
     const DevActivation* a;
@@ -91,9 +93,15 @@ cudaError_t launch_residual_norm(float* x, const __half* t, int rows, int width,
 cudaError_t launch_rmsnorm_rows(const float* x, int rows, int width, float pre, const float* w, float eps, float* out,
                                 cudaStream_t stream);
 
-// pooled[s] = mean over the sequence's rows of y (fp32).
-cudaError_t launch_mean_pool(const float* y, int width, const uint32_t* seqs, int nseq, float* pooled,
-                             cudaStream_t stream);
+// pooled[s] = mean over the sequence's rows of y (fp32), in two launches: partial sums of
+// chunks of rows (partial[chunk_base[s] + k], max_chunks = most chunks of any sequence),
+// then the per-sequence total.  pool_chunks(len) is a sequence's chunk count.
+int pool_chunks(uint32_t len);
+cudaError_t launch_mean_pool(const float* y, int width, const uint32_t* seqs, int nseq, int max_chunks,
+                             const uint32_t* chunk_base, float* partial, float* pooled, cudaStream_t stream);
+// The same mean in one launch, one block per sequence (sequence ranges on the device only).
+cudaError_t launch_mean_pool_seq(const float* y, int width, const uint32_t* seqs, int nseq, float* pooled,
+                                 cudaStream_t stream);
 
 // out[s][n] = sum_k in[s][k] * W[n][k] with W dequantised from Q8 planes on the fly, fp32.
 cudaError_t launch_dense_rows(const float* in, int nrows, const DevWeight& w, float* out, cudaStream_t stream);

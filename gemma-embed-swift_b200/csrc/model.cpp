@@ -300,11 +300,11 @@ static cudaError_t upload_weight(Device& d, DevWeight& w, const HostWeight& h) {
 
 static void free_workspace(Workspace& ws) {
     for (void* p : {(void*)ws.tokens, (void*)ws.positions, (void*)ws.seqs, (void*)ws.work, (void*)ws.x, (void*)ws.qkv16,
-                    (void*)ws.o16, (void*)ws.y, (void*)ws.ple, (void*)ws.pooled, (void*)ws.mid, (void*)ws.out,
+                    (void*)ws.o16, (void*)ws.y, (void*)ws.ple, (void*)ws.pooled, (void*)ws.chunk_base, (void*)ws.pool_partial, (void*)ws.mid, (void*)ws.out,
                     (void*)ws.h, (void*)ws.x16, (void*)ws.q, (void*)ws.k, (void*)ws.v, (void*)ws.attn, (void*)ws.act,
                     (void*)ws.g})
         if (p) cudaFree(p);
-    for (void* p : {(void*)ws.h_tokens, (void*)ws.h_positions, (void*)ws.h_seqs, (void*)ws.h_work, (void*)ws.h_out,
+    for (void* p : {(void*)ws.h_chunk_base, (void*)ws.h_tokens, (void*)ws.h_positions, (void*)ws.h_seqs, (void*)ws.h_work, (void*)ws.h_out,
                     (void*)ws.h_err})
         if (p) cudaFreeHost(p);
     ws = Workspace();
@@ -363,6 +363,9 @@ static cudaError_t ensure_workspace(const Config& c, Device& d, int rows, int se
         chk(A(&ws.g, r * size_t(c.per_layer)));
     }
     chk(A(&ws.pooled, size_t(S) * d_));
+    chk(A(&ws.chunk_base, size_t(S)));
+    chk(A(&ws.pool_partial, (r / 256 + size_t(S)) * d_));
+    chk(H(&ws.h_chunk_base, size_t(S)));
     chk(A(&ws.mid, size_t(S) * std::max(c.dense_head, 1)));
     chk(A(&ws.out, size_t(S) * c.out_dim));
     chk(H(&ws.h_tokens, r));
@@ -741,9 +744,15 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     Workspace& ws = d.ws;
     int64_t launches = 0;
     // ---- inputs
+    int max_chunks = 0;
+    uint32_t chunk_total = 0;
     for (int s = 0; s < nseq; s++) {
         ws.h_seqs[2 * s] = a.seqs[s].start;
         ws.h_seqs[2 * s + 1] = a.seqs[s].length;
+        ws.h_chunk_base[s] = chunk_total;
+        const int ch = pool_chunks(a.seqs[s].length);
+        chunk_total += uint32_t(ch);
+        max_chunks = std::max(max_chunks, ch);
     }
     build_work(a.seqs, nseq, qpi, ws.h_work);
     if (any512) build_work(a.seqs, nseq, qpi512, ws.h_work + 3 * size_t(nwork));
@@ -757,7 +766,8 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     }
     if (a.positions == nullptr) launches++;  // the positions kernel below
     if ((e = cudaMemcpyAsync(ws.seqs, ws.h_seqs, size_t(nseq) * 8, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
-        (e = cudaMemcpyAsync(ws.work, ws.h_work, size_t(nwork + nwork512) * 12, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+        (e = cudaMemcpyAsync(ws.work, ws.h_work, size_t(nwork + nwork512) * 12, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(ws.chunk_base, ws.h_chunk_base, size_t(nseq) * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess)
         return gpu_fail(e, "batch upload");
     if (a.positions) {
         memcpy(ws.h_positions, a.positions, size_t(ntok) * 4);
@@ -795,7 +805,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     // Every kernel launch goes through K: it counts launches and, when profiling, times the
     // first launch of each kernel class over `reps` back-to-back repetitions (the reference's
     // Profiler, Metal/Profiler.swift:16-88).
-    auto K = [&](const char* name, double flops, double bytes, auto&& fn) -> cudaError_t {
+    auto K = [&](const char* name, double flops, double bytes, auto&& fn, int kernels = 1) -> cudaError_t {
         if (a.profile) {
             ProfileEntry* pe = a.profile->find(name);
             if (pe) {
@@ -808,7 +818,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
                 for (int r = 0; r < a.profile->reps; r++) {
                     cudaError_t x = fn();
                     if (x != cudaSuccess) return x;
-                    launches++;
+                    launches += kernels;
                 }
                 cudaEventRecord(e1, ks);
                 cudaError_t x = cudaEventSynchronize(e1);
@@ -821,7 +831,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
                 return cudaSuccess;
             }
         }
-        launches++;
+        launches += kernels;
         return fn();
     };
     // Algorithmic work of a GEMM launch: the rows that hold tokens, not the padding.
@@ -946,7 +956,10 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         }
         // ---- pooling and head
         if (a.trace_layer < -1) {
-            CK(K("mean_pool", 0, double(ntok) * D * 4, [&] { return launch_mean_pool(ws.y, D, ws.seqs, nseq, ws.pooled, ks); }),
+            CK(K("mean_pool", 0, double(ntok) * D * 4, [&] {
+                     return launch_mean_pool(ws.y, D, ws.seqs, nseq, max_chunks, ws.chunk_base, ws.pool_partial,
+                                             ws.pooled, ks);
+                 }, 2),
                "mean pool");
             if (c.has_dense) {
                 CK(K("dense_head", 2.0 * nseq * D * c.dense_head, double(D) * c.dense_head * 4,
@@ -966,7 +979,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     // Captured CUDA graphs replay the whole launch sequence of a batch shape with one call
     // (kernel arguments, tensor maps included, are fixed per workspace and shape).
     const bool use_graph = !(m->flags & GE_LOAD_NO_GRAPHS) && !a.profile && a.trace_layer < -1;
-    GraphKey gk{rows, ntok, nseq, nwork, nwork512, reinterpret_cast<uintptr_t>(tokens)};
+    GraphKey gk{rows, ntok, nseq, nwork, nwork512, max_chunks, reinterpret_cast<uintptr_t>(tokens)};
     GraphEntry* ge_ = use_graph ? find_graph(d, gk) : nullptr;
     if (ge_) {
         if ((e = cudaGraphLaunch(ge_->exec, st)) != cudaSuccess) return gpu_fail(e, "graph launch");

@@ -47,7 +47,8 @@ struct LayerDev {
 struct Workspace {
     int cap_rows = 0, cap_seqs = 0, cap_work = 0;
     int32_t *tokens = nullptr, *positions = nullptr;
-    uint32_t *seqs = nullptr, *work = nullptr;
+    uint32_t *seqs = nullptr, *work = nullptr, *chunk_base = nullptr;
+    float* pool_partial = nullptr;  // [rows / 256 + seqs][hidden] partial sums of the mean pool
     float *x = nullptr, *y = nullptr, *ple = nullptr;
     __half* o16 = nullptr;  // fp16 output of the o, down and per-layer projections
     float *pooled = nullptr, *mid = nullptr, *out = nullptr;
@@ -60,18 +61,18 @@ struct Workspace {
     std::vector<std::pair<int, AttnMaps>> attn_maps;  // per KV head count, head-dim-256 layers
     // Pinned host staging.
     int32_t *h_tokens = nullptr, *h_positions = nullptr;
-    uint32_t *h_seqs = nullptr, *h_work = nullptr;
+    uint32_t *h_seqs = nullptr, *h_work = nullptr, *h_chunk_base = nullptr;
     float* h_out = nullptr;
     int* h_err = nullptr;
 };
 
 // A captured forward for one batch shape on one workspace.
 struct GraphKey {
-    int rows = 0, ntok = 0, nseq = 0, nwork = 0, nwork512 = 0;
+    int rows = 0, ntok = 0, nseq = 0, nwork = 0, nwork512 = 0, pool_chunks = 0;
     uintptr_t tokens = 0;  // the token buffer the embedding kernel reads
     bool operator==(const GraphKey& o) const {
         return rows == o.rows && ntok == o.ntok && nseq == o.nseq && nwork == o.nwork && nwork512 == o.nwork512 &&
-               tokens == o.tokens;
+               pool_chunks == o.pool_chunks && tokens == o.tokens;
     }
 };
 struct GraphEntry {

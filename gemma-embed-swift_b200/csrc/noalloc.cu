@@ -77,7 +77,7 @@ extern "C" int ge_pool_head_noalloc(ge_model* m, int32_t device_ordinal, const f
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : cudaStreamLegacy;
     // Each kernel writes every scratch element it later reads, so no call depends on what the
     // previous call left in the array and nothing needs clearing.
-    e = ge::launch_mean_pool(d_hidden, c.hidden, d_seqs, nseq, pooled, st);
+    e = ge::launch_mean_pool_seq(d_hidden, c.hidden, d_seqs, nseq, pooled, st);
     int launches = 1;
     if (e == cudaSuccess && c.has_dense) {
         e = ge::launch_dense_f32(pooled, nseq, dev->dense2, c.dense_head, c.hidden, mid, st);

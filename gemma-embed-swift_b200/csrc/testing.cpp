@@ -113,7 +113,7 @@ int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int3
     g.aux = static_cast<const float*>(daux.p);
     g.ldaux = n;
     g.use_q8 = use_q8 == 1;
-    g.mode = use_q8 == 2 ? ge::GEMM_PAIR : ge::GEMM_SINGLE;
+    g.mode = use_q8 == 2 ? ge::GEMM_PAIR : use_q8 == 3 ? ge::GEMM_NARROW : ge::GEMM_SINGLE;
     g.err = static_cast<int*>(derr.p);
     g.num_sms = sms;
     TRY(ge::launch_gemm(g, nullptr));

@@ -21,7 +21,8 @@ extern "C" {
  * epilogue: 0 fp32 store, 1 fp16 store, 2 GeGLU over rows interleaved as the loader does
  * (out has n/2 columns), 3 gelu(acc) * aux (aux fp32 [m][n]).  path: 0 fp16-resident
  * weights on single CTAs, 1 the in-shared-memory Q8 dequantisation, 2 fp16 weights on CTA
- * pairs (tcgen05.mma.cta_group::2).  Results are returned as fp32 [m][n] (or [m][n/2]). */
+ * pairs (tcgen05.mma.cta_group::2), 3 fp16 weights on single CTAs with 128-wide tiles (not
+ * for the GeGLU epilogue).  Results are returned as fp32 [m][n] (or [m][n/2]). */
 GE_API int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w_q8_0, int32_t n, int32_t epilogue,
                         int32_t path, const float* aux, float* out);
 

@@ -65,11 +65,14 @@ def test_gemm_shapes_fp32(ge, synth, cuda_device, m, k, n):
     got16 = gemm(ge, a, wq, n, 0, use_q8=False)
     got8 = gemm(ge, a, wq, n, 0, use_q8=True)
     gotp = gemm(ge, a, wq, n, 0, use_q8=2)
+    gotn = gemm(ge, a, wq, n, 0, use_q8=3)
     assert max_rel(got16, want) < TOL_F32
     # The Q8 path dequantises in shared memory to the very same fp16 operand: identical bits.
     assert got8.tobytes() == got16.tobytes()
     # CTA pairs multiply the same operands with 256-row instructions: identical bits.
     assert gotp.tobytes() == got16.tobytes()
+    # 128-wide tiles: the same per-element accumulation order, identical bits.
+    assert gotn.tobytes() == got16.tobytes()
 
 
 @pytest.mark.parametrize("use_q8", [False, True, 2])
@@ -83,6 +86,8 @@ def test_gemm_epilogues(ge, synth, oracle, cuda_device, use_q8):
     _, wq, wd = make_case(synth, m, k, n, seed=13)
     got = gemm(ge, a, wq, n, 1, use_q8)
     assert max_rel(got, a64 @ wd.T) < TOL_F16
+    if use_q8 is False:
+        assert gemm(ge, a, wq, n, 1, 3).tobytes() == got.tobytes()
     # GeGLU over rows interleaved in blocks of 128 (gate block j, up block j, ...)
     rows = []
     for j in range(ff // 128):
