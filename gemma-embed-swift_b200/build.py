@@ -60,7 +60,7 @@ def build(verbose: bool = False, extra=()) -> str:
     with cf.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
         objs = list(ex.map(lambda s: _compile(s, extra), srcs))
     if not os.path.exists(LIB) or os.path.getmtime(LIB) < max(os.path.getmtime(o) for o in objs):
-        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lpthread"]
+        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lpthread", "-Xlinker", "--no-undefined"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stderr}")

@@ -386,6 +386,18 @@ cudaError_t launch_mean_pool(const float* y, int width, const uint32_t* seqs, in
     return cudaGetLastError();
 }
 
+// positions[start + i] = i for every sequence (PackedBatch.append, MetalForward.swift:17-21).
+__global__ void k_positions(const uint32_t* __restrict__ seqs, int32_t* __restrict__ positions) {
+    const uint32_t start = seqs[2 * blockIdx.x], len = seqs[2 * blockIdx.x + 1];
+    for (uint32_t i = threadIdx.x; i < len; i += blockDim.x) positions[start + i] = int32_t(i);
+}
+
+cudaError_t launch_positions(const uint32_t* seqs, int nseq, int32_t* positions, cudaStream_t stream) {
+    if (nseq <= 0) return cudaSuccess;
+    k_positions<<<nseq, 256, 0, stream>>>(seqs, positions);
+    return cudaGetLastError();
+}
+
 // out[s][n] = sum_k in[s][k] * w[n][k] in fp32 with an fp32 weight matrix: one warp per n,
 // four input rows per pass so each weight load feeds four independent sums.
 __global__ void k_dense_f32(const float* __restrict__ in, int nrows, const float* __restrict__ w, int N, int K,

@@ -531,9 +531,9 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream) {
     if (!g.w->f16 && !g.w->q8) return cudaErrorInvalidValue;
     const bool q8 = g.w->q8 && (g.use_q8 || !g.w->f16);
     const bool pair = !q8 && g.mode == GEMM_PAIR;
-    // 128-wide tiles balance the last wave of the narrow projections (N <= 1280) better.
-    const bool narrow = !q8 && !pair && g.epilogue != EPI_GEGLU &&
-                        (g.mode == GEMM_NARROW || (g.mode == GEMM_AUTO && g.w->N <= 1280));
+    // 128-wide tiles read each A tile twice as often; measured slower on every forward shape,
+    // so they run only when asked for.
+    const bool narrow = !q8 && !pair && g.epilogue != EPI_GEGLU && g.mode == GEMM_NARROW;
     switch (g.epilogue) {
     case EPI_F32: return launch_epi<EPI_F32>(g, stream, q8, pair, narrow);
     case EPI_F16: return launch_epi<EPI_F16>(g, stream, q8, pair, narrow);

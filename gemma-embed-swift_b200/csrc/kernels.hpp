@@ -43,9 +43,9 @@ bool encode_weight_maps(DevWeight& w, int bn);
 bool encode_activation_map(DevActivation& a);
 
 // Which fp16-path kernel a GEMM uses: single CTAs with 128 x 256 tiles, single CTAs with
-// 128 x 128 tiles, or CTA pairs (tcgen05.mma.cta_group::2, 256 x 256 tiles).  AUTO takes
-// 128 x 128 tiles for N <= 1280 (except GeGLU) and 128 x 256 otherwise.  The Q8 path always
-// runs single CTAs with 128 x 256 tiles.
+// 128 x 128 tiles, or CTA pairs (tcgen05.mma.cta_group::2, 256 x 256 tiles).  AUTO is single
+// CTAs with 128 x 256 tiles, the fastest of the three on the forward's shapes.  The Q8 path
+// always runs single CTAs with 128 x 256 tiles.
 enum GemmMode : int { GEMM_AUTO = 0, GEMM_SINGLE = 1, GEMM_PAIR = 2, GEMM_NARROW = 3 };
 
 struct GemmLaunch {
@@ -102,9 +102,6 @@ cudaError_t launch_mean_pool(const float* y, int width, const uint32_t* seqs, in
 // The same mean in one launch, one block per sequence (sequence ranges on the device only).
 cudaError_t launch_mean_pool_seq(const float* y, int width, const uint32_t* seqs, int nseq, float* pooled,
                                  cudaStream_t stream);
-
-// out[s][n] = sum_k in[s][k] * W[n][k] with W dequantised from Q8 planes on the fly, fp32.
-cudaError_t launch_dense_rows(const float* in, int nrows, const DevWeight& w, float* out, cudaStream_t stream);
 
 // out[s][n] = sum_k in[s][k] * w[n][k], fp32 weights [N][K].
 cudaError_t launch_dense_f32(const float* in, int nrows, const float* w, int N, int K, float* out,
