@@ -294,12 +294,16 @@ def main():
     return 0
 
 
-def model_launches(model) -> int:
+def model_info(model):
     ctypes = importlib.import_module("ctypes")
     lib_mod = importlib.import_module(PKG + "._lib")
     info = lib_mod.GeInfo()
     lib_mod.lib().ge_info_get(model._h, ctypes.byref(info))
-    return int(info.kernel_launches)
+    return info
+
+
+def model_launches(model) -> int:
+    return int(model_info(model).kernel_launches)
 
 
 def reduce_max_sum(dist, ms, tokens):

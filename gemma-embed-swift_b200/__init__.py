@@ -31,6 +31,7 @@ STATUS = {
 }
 LOAD_NO_GRAPHS = 1
 LOAD_Q8_ONLY = 2
+LOAD_NO_PDL = 4
 
 
 class GemmaEmbedError(RuntimeError):
@@ -76,6 +77,7 @@ class LoadOptions:
     devices: Sequence[int] = (0,)
     use_graphs: bool = True
     q8_only: bool = False
+    programmatic_launch: bool = True  # overlap each kernel's set-up with its predecessor's tail
 
 
 @dataclass
@@ -167,7 +169,8 @@ class EmbeddingModel:
             mask |= 1 << int(d)
         o.device_mask = mask
         o.batch_token_budget = int(options.batch_token_budget)
-        o.flags = (0 if options.use_graphs else LOAD_NO_GRAPHS) | (LOAD_Q8_ONLY if options.q8_only else 0)
+        o.flags = ((0 if options.use_graphs else LOAD_NO_GRAPHS) | (LOAD_Q8_ONLY if options.q8_only else 0)
+                   | (0 if options.programmatic_launch else LOAD_NO_PDL))
         h = ctypes.c_void_p()
         _check(L.ge_load(str(path).encode(), ctypes.byref(o), ctypes.byref(h)), None)
         return cls(h, options)

@@ -27,6 +27,8 @@ __global__ void __launch_bounds__(256) k_attention_simt(const __half* __restrict
                                                         const __half* __restrict__ V, __half* __restrict__ O,
                                                         const uint32_t* __restrict__ work, int heads, int kvh,
                                                         int hw, float scale) {
+    pdl_wait();
+    pdl_launch_if_one_wave();
     constexpr int PER = HD / 32;
     extern __shared__ float sm[];
     float* qs = sm;                          // [32][HD]
@@ -216,6 +218,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_wait();  // q, k, v come from the previous kernel; the set-up above overlapped its tail
 
     if (warp == 0) {
         // ---------------------------------------------------------- TMA producer
@@ -240,6 +243,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                     tma_load_2d(smem + kOffV + b * kKVBytes + c * (kKVBytes / 4), &mapV, &v_full[b], kh * kTcHd + c * 64, row);
                 issued_v++;
             }
+            pdl_launch();  // this CTA's loads are all issued: the next kernel may be scheduled
             // Every issued load lands before the CTA exits, also after an error.
             drain(q_full, 0);
             for (int b = 0; b < 2; b++) {
@@ -464,17 +468,15 @@ cudaError_t configure_attention_kernels() {
 static cudaError_t launch_tc(const AttnLaunch& a, cudaStream_t stream) {
     TcAttnParams p{a.work, a.out, a.heads, a.kv_heads, a.half_window, a.err};
     dim3 grid(a.work_items, a.heads);
-    k_attention_tc<<<grid, kTcThreads, kTcSmem, stream>>>(a.maps->q, a.maps->k, a.maps->v, p);
-    return cudaGetLastError();
+    return launch_kernel(k_attention_tc, grid, dim3(kTcThreads), kTcSmem, stream, 1, a.maps->q, a.maps->k, a.maps->v, p);
 }
 
 template <int HD>
 static cudaError_t launch_simt(const AttnLaunch& a, cudaStream_t stream) {
     const int smem = simt_smem<HD>();
     dim3 grid(a.work_items, a.heads);
-    k_attention_simt<HD><<<grid, 256, smem, stream>>>(a.q, a.k, a.v, a.out, a.work, a.heads, a.kv_heads, a.half_window,
-                                                      1.0f);
-    return cudaGetLastError();
+    return launch_kernel(k_attention_simt<HD>, grid, dim3(256), smem, stream, 1, a.q, a.k, a.v, a.out, a.work, a.heads,
+                         a.kv_heads, a.half_window, 1.0f);
 }
 
 bool encode_attention_maps(AttnMaps& m, const __half* q, const __half* k, const __half* v, int rows, int heads, int kvh,

@@ -14,6 +14,18 @@
 
 namespace ge {
 
+#define CK_LAUNCH(expr)                \
+    do {                               \
+        const cudaError_t e_ = (expr); \
+        if (e_ != cudaSuccess) return e_; \
+    } while (0)
+
+namespace {
+thread_local bool t_programmatic = false;
+}  // namespace
+void set_programmatic_launch(bool on) { t_programmatic = on; }
+bool programmatic_launch() { return t_programmatic; }
+
 constexpr int kRowsPerBlock = 8;  // warps per 256-thread block
 
 // x = dequant(table row) * scale, h = rmsnorm(x) * w.  Embedding.swift semantics:
@@ -21,6 +33,8 @@ constexpr int kRowsPerBlock = 8;  // warps per 256-thread block
 __global__ void k_embed(const int32_t* __restrict__ tokens, int ntok, int rows, const int8_t* __restrict__ tq,
                         const __half* __restrict__ ts, int width, float scale, float* __restrict__ x,
                         __half* __restrict__ x16, const float* __restrict__ w, float eps, __half* __restrict__ h) {
+    pdl_wait();
+    pdl_launch_if_one_wave();
     const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -53,8 +67,8 @@ cudaError_t launch_embed(const int32_t* tokens, int ntok, int rows, const int8_t
                          int width, float scale, float* x, __half* x16, const float* norm_w, float eps, __half* h,
                          cudaStream_t stream) {
     if (rows <= 0) return cudaSuccess;
-    k_embed<<<(rows + kRowsPerBlock - 1) / kRowsPerBlock, 256, 0, stream>>>(tokens, ntok, rows, table_q, table_s, width,
-                                                                             scale, x, x16, norm_w, eps, h);
+    CK_LAUNCH(launch_kernel(k_embed, dim3((rows + kRowsPerBlock - 1) / kRowsPerBlock), dim3(256), 0, stream, 1, tokens,
+                            ntok, rows, table_q, table_s, width, scale, x, x16, norm_w, eps, h));
     return cudaGetLastError();
 }
 
@@ -62,13 +76,17 @@ cudaError_t launch_embed(const int32_t* tokens, int ntok, int rows, const int8_t
 // heads, [H, H+KV) key heads, [H+KV, H+2KV) value heads.  CPUReference.swift:225-235.
 // Lane l holds elements [Q*l, Q*l + Q) of each half of a head (Q = HD / 64), so every element
 // and its rotation partner HD/2 away sit in the same lane; the token's cos/sin pairs are read
-// once and reused for every query and key head.
-template <int HD>
+// once and reused for every query and key head.  All slots are loaded before the first is
+// normalised, so each warp keeps MAXS independent loads in flight.
+template <int HD, int MAXS>
 __global__ void k_qkv_norm_rope(const __half* __restrict__ qkv, int ntok, int rows, int heads, int kvh,
                                 const float* __restrict__ qw, const float* __restrict__ kw,
                                 const int32_t* __restrict__ pos, const float* __restrict__ rope, float eps,
                                 __half* __restrict__ q, __half* __restrict__ k, __half* __restrict__ v) {
+    pdl_wait();
+    pdl_launch_if_one_wave();
     constexpr int Q = HD / 64;  // elements per lane per half: 4 (hd 256) or 8 (hd 512)
+    constexpr int WQ = Q / 2;   // 32-bit words per lane per half
     constexpr int HALF = HD / 2;
     const int slots = heads + 2 * kvh;
     const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
@@ -76,6 +94,19 @@ __global__ void k_qkv_norm_rope(const __half* __restrict__ qkv, int ntok, int ro
     if (row >= rows) return;
     const int c = lane * Q;
     const bool live = row < ntok;
+    uint32_t raw[MAXS][2][WQ];
+    const __half* src_row = qkv + long(row) * slots * HD;
+#pragma unroll
+    for (int s = 0; s < MAXS; s++)
+#pragma unroll
+        for (int h = 0; h < 2; h++)
+#pragma unroll
+            for (int i = 0; i < WQ; i += 2) {
+                uint2 r = make_uint2(0u, 0u);
+                if (live && s < slots) r = *reinterpret_cast<const uint2*>(src_row + s * HD + h * HALF + c + 2 * i);
+                raw[s][h][i] = r.x;
+                raw[s][h][i + 1] = r.y;
+            }
     float cs_c[Q], cs_s[Q];
     if (live) {
         const float* cs = rope + long(pos[row]) * HD + 2 * c;  // [position][pair][cos, sin]
@@ -88,8 +119,9 @@ __global__ void k_qkv_norm_rope(const __half* __restrict__ qkv, int ntok, int ro
             cs_s[i + 1] = t.w;
         }
     }
-    const __half* src_row = qkv + long(row) * slots * HD;
-    for (int slot = 0; slot < slots; slot++) {
+#pragma unroll
+    for (int slot = 0; slot < MAXS; slot++) {
+        if (slot >= slots) break;
         __half* dst;
         const float* w = nullptr;
         if (slot < heads) {
@@ -102,22 +134,14 @@ __global__ void k_qkv_norm_rope(const __half* __restrict__ qkv, int ntok, int ro
             dst = v + long(row) * kvh * HD + (slot - heads - kvh) * HD;
         }
         float a[Q], b[Q];
-        if (live) {
-            const __half* src = src_row + slot * HD;
 #pragma unroll
-            for (int i = 0; i < Q; i += 4) {
-                const uint2 ra = *reinterpret_cast<const uint2*>(src + c + i);
-                const uint2 rb = *reinterpret_cast<const uint2*>(src + HALF + c + i);
-                const float2 a0 = __half22float2(*reinterpret_cast<const __half2*>(&ra.x));
-                const float2 a1 = __half22float2(*reinterpret_cast<const __half2*>(&ra.y));
-                const float2 b0 = __half22float2(*reinterpret_cast<const __half2*>(&rb.x));
-                const float2 b1 = __half22float2(*reinterpret_cast<const __half2*>(&rb.y));
-                a[i] = a0.x; a[i + 1] = a0.y; a[i + 2] = a1.x; a[i + 3] = a1.y;
-                b[i] = b0.x; b[i + 1] = b0.y; b[i + 2] = b1.x; b[i + 3] = b1.y;
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < Q; i++) a[i] = b[i] = 0.f;
+        for (int i = 0; i < WQ; i++) {
+            const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&raw[slot][0][i]));
+            const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&raw[slot][1][i]));
+            a[2 * i] = fa.x;
+            a[2 * i + 1] = fa.y;
+            b[2 * i] = fb.x;
+            b[2 * i + 1] = fb.y;
         }
         float ss = 0.f;
 #pragma unroll
@@ -150,17 +174,22 @@ __global__ void k_qkv_norm_rope(const __half* __restrict__ qkv, int ntok, int ro
     }
 }
 
+// Largest slot count per head dimension: 8 for hd 256 (4 query + 2 + 2 key/value heads), 6 for
+// hd 512 (4 query + 1 + 1).
+constexpr int kMaxSlots256 = 8, kMaxSlots512 = 6;
+
 cudaError_t launch_qkv_norm_rope(const __half* qkv, int ntok, int rows, int heads, int kv_heads, int hd,
                                       const float* q_w, const float* k_w, const int32_t* positions, const float* rope,
                                       float eps, __half* q, __half* k, __half* v, cudaStream_t stream) {
     if (rows <= 0) return cudaSuccess;
     const int blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
-    if (hd == 256)
-        k_qkv_norm_rope<256><<<blocks, 256, 0, stream>>>(qkv, ntok, rows, heads, kv_heads, q_w, k_w, positions, rope,
-                                                         eps, q, k, v);
-    else if (hd == 512)
-        k_qkv_norm_rope<512><<<blocks, 256, 0, stream>>>(qkv, ntok, rows, heads, kv_heads, q_w, k_w, positions, rope,
-                                                         eps, q, k, v);
+    const int slots = heads + 2 * kv_heads;
+    if (hd == 256 && slots <= kMaxSlots256)
+        CK_LAUNCH(launch_kernel(k_qkv_norm_rope<256, kMaxSlots256>, dim3(blocks), dim3(256), 0, stream, 1, qkv, ntok,
+                                rows, heads, kv_heads, q_w, k_w, positions, rope, eps, q, k, v));
+    else if (hd == 512 && slots <= kMaxSlots512)
+        CK_LAUNCH(launch_kernel(k_qkv_norm_rope<512, kMaxSlots512>, dim3(blocks), dim3(256), 0, stream, 1, qkv, ntok,
+                                rows, heads, kv_heads, q_w, k_w, positions, rope, eps, q, k, v));
     else
         return cudaErrorInvalidValue;
     return cudaGetLastError();
@@ -173,6 +202,8 @@ template <int W>
 __global__ void k_residual_norm(float* __restrict__ x, const __half* __restrict__ t, int rows,
                                 const float* __restrict__ wp, float scale, const float* __restrict__ wn, float eps,
                                 __half* __restrict__ h16, float* __restrict__ y32, __half* __restrict__ x16) {
+    pdl_wait();
+    pdl_launch_if_one_wave();
     constexpr int G = W / 256;  // groups of 8 per lane
     const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -256,9 +287,11 @@ cudaError_t launch_residual_norm(float* x, const __half* t, int rows, int width,
     if (rows <= 0) return cudaSuccess;
     const int blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
     if (width == 768)
-        k_residual_norm<768><<<blocks, 256, 0, stream>>>(x, t, rows, w_post, scale, w_next, eps, h16, y32, x16);
+        CK_LAUNCH(launch_kernel(k_residual_norm<768>, dim3(blocks), dim3(256), 0, stream, 1, x, t, rows, w_post, scale,
+                                w_next, eps, h16, y32, x16));
     else if (width == 512)
-        k_residual_norm<512><<<blocks, 256, 0, stream>>>(x, t, rows, w_post, scale, w_next, eps, h16, y32, x16);
+        CK_LAUNCH(launch_kernel(k_residual_norm<512>, dim3(blocks), dim3(256), 0, stream, 1, x, t, rows, w_post, scale,
+                                w_next, eps, h16, y32, x16));
     else
         return cudaErrorInvalidValue;
     return cudaGetLastError();
@@ -268,6 +301,8 @@ cudaError_t launch_residual_norm(float* x, const __half* t, int rows, int width,
 // CPUReference.swift:206-209 and Elementwise.metal:38-75 with preScale).
 __global__ void k_rmsnorm_rows(const float* __restrict__ x, long rows, int width, float pre,
                                const float* __restrict__ w, float eps, float* __restrict__ out) {
+    pdl_wait();
+    pdl_launch_if_one_wave();
     const long row = long(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (row >= rows) return;
@@ -286,7 +321,8 @@ __global__ void k_rmsnorm_rows(const float* __restrict__ x, long rows, int width
 cudaError_t launch_rmsnorm_rows(const float* x, int rows, int width, float pre, const float* w, float eps, float* out,
                                 cudaStream_t stream) {
     if (rows <= 0) return cudaSuccess;
-    k_rmsnorm_rows<<<(rows + kRowsPerBlock - 1) / kRowsPerBlock, 256, 0, stream>>>(x, rows, width, pre, w, eps, out);
+    CK_LAUNCH(launch_kernel(k_rmsnorm_rows, dim3((rows + kRowsPerBlock - 1) / kRowsPerBlock), dim3(256), 0, stream, 1,
+                            x, rows, width, pre, w, eps, out));
     return cudaGetLastError();
 }
 
@@ -300,6 +336,8 @@ constexpr int kPoolChunk = 256;
 
 __global__ void k_pool_partial(const float* __restrict__ y, int width, const uint32_t* __restrict__ seqs,
                                const uint32_t* __restrict__ chunk_base, float* __restrict__ partial) {
+    pdl_wait();
+    pdl_launch_if_one_wave();
     extern __shared__ float part[];  // [8][width]
     const int s = blockIdx.y;
     const uint32_t start = seqs[2 * s], len = seqs[2 * s + 1];
@@ -329,6 +367,8 @@ __global__ void k_pool_partial(const float* __restrict__ y, int width, const uin
 
 __global__ void k_pool_final(const float* __restrict__ partial, int width, const uint32_t* __restrict__ seqs,
                              const uint32_t* __restrict__ chunk_base, float* __restrict__ pooled) {
+    pdl_wait();
+    pdl_launch_if_one_wave();
     const int s = blockIdx.x;
     const uint32_t len = seqs[2 * s + 1];
     const uint32_t nchunks = (len + kPoolChunk - 1) / kPoolChunk;
@@ -346,6 +386,8 @@ int pool_chunks(uint32_t len) { return int((len + kPoolChunk - 1) / kPoolChunk);
 // block per sequence, warp w summing rows w, w + 8, ..., then the 8 warp sums in order.
 __global__ void k_mean_pool_seq(const float* __restrict__ y, int width, const uint32_t* __restrict__ seqs,
                                 float* __restrict__ pooled) {
+    pdl_wait();
+    pdl_launch_if_one_wave();
     extern __shared__ float part[];  // [8][width]
     const uint32_t start = seqs[2 * blockIdx.x], len = seqs[2 * blockIdx.x + 1];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -372,7 +414,8 @@ cudaError_t launch_mean_pool_seq(const float* y, int width, const uint32_t* seqs
                                  cudaStream_t stream) {
     if (nseq <= 0) return cudaSuccess;
     if (width % 128) return cudaErrorInvalidValue;
-    k_mean_pool_seq<<<nseq, 256, 8 * width * sizeof(float), stream>>>(y, width, seqs, pooled);
+    CK_LAUNCH(launch_kernel(k_mean_pool_seq, dim3(nseq), dim3(256), 8 * width * sizeof(float), stream, 1, y, width,
+                            seqs, pooled));
     return cudaGetLastError();
 }
 
@@ -380,21 +423,24 @@ cudaError_t launch_mean_pool(const float* y, int width, const uint32_t* seqs, in
                              const uint32_t* chunk_base, float* partial, float* pooled, cudaStream_t stream) {
     if (nseq <= 0) return cudaSuccess;
     if (width % 128) return cudaErrorInvalidValue;
-    k_pool_partial<<<dim3(max_chunks, nseq), 256, 8 * width * sizeof(float), stream>>>(y, width, seqs, chunk_base,
-                                                                                     partial);
-    k_pool_final<<<nseq, 256, 0, stream>>>(partial, width, seqs, chunk_base, pooled);
+    CK_LAUNCH(launch_kernel(k_pool_partial, dim3(max_chunks, nseq), dim3(256), 8 * width * sizeof(float), stream, 1, y,
+                            width, seqs, chunk_base, partial));
+    CK_LAUNCH(launch_kernel(k_pool_final, dim3(nseq), dim3(256), 0, stream, 1, partial, width, seqs, chunk_base,
+                            pooled));
     return cudaGetLastError();
 }
 
 // positions[start + i] = i for every sequence (PackedBatch.append, MetalForward.swift:17-21).
 __global__ void k_positions(const uint32_t* __restrict__ seqs, int32_t* __restrict__ positions) {
+    pdl_wait();
+    pdl_launch_if_one_wave();
     const uint32_t start = seqs[2 * blockIdx.x], len = seqs[2 * blockIdx.x + 1];
     for (uint32_t i = threadIdx.x; i < len; i += blockDim.x) positions[start + i] = int32_t(i);
 }
 
 cudaError_t launch_positions(const uint32_t* seqs, int nseq, int32_t* positions, cudaStream_t stream) {
     if (nseq <= 0) return cudaSuccess;
-    k_positions<<<nseq, 256, 0, stream>>>(seqs, positions);
+    CK_LAUNCH(launch_kernel(k_positions, dim3(nseq), dim3(256), 0, stream, 1, seqs, positions));
     return cudaGetLastError();
 }
 
@@ -402,6 +448,8 @@ cudaError_t launch_positions(const uint32_t* seqs, int nseq, int32_t* positions,
 // four input rows per pass so each weight load feeds four independent sums.
 __global__ void k_dense_f32(const float* __restrict__ in, int nrows, const float* __restrict__ w, int N, int K,
                             float* __restrict__ out) {
+    pdl_wait();
+    pdl_launch_if_one_wave();
     const int n = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (n >= N) return;
@@ -431,7 +479,8 @@ cudaError_t launch_dense_f32(const float* in, int nrows, const float* w, int N, 
                              cudaStream_t stream) {
     if (nrows <= 0) return cudaSuccess;
     if (K % 128) return cudaErrorInvalidValue;
-    k_dense_f32<<<(N + kRowsPerBlock - 1) / kRowsPerBlock, 256, 0, stream>>>(in, nrows, w, N, K, out);
+    CK_LAUNCH(launch_kernel(k_dense_f32, dim3((N + kRowsPerBlock - 1) / kRowsPerBlock), dim3(256), 0, stream, 1, in,
+                            nrows, w, N, K, out));
     return cudaGetLastError();
 }
 

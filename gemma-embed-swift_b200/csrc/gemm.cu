@@ -141,6 +141,8 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR>::kThreads, 1)
     if (PAIR) cluster_sync();  // the peer's barriers are initialised before any remote use
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // The set-up above overlaps the previous kernel's tail; A and the output are its data.
+    pdl_wait();
 
     if (warp == 4) {
         // ---------------------------------------------------------- TMA producer
@@ -182,6 +184,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR>::kThreads, 1)
                     }
                 }
             }
+            pdl_launch();  // this CTA's loads are all issued: the next kernel may be scheduled
             // Every issued load must land before the CTA exits, also after an error.  A pair's
             // loads complete on the leader's barriers, so the leader drains for both CTAs.
             if (crank == 0)
@@ -493,25 +496,14 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
     if (!PAIR) {
         const int tiles = (g.m_rows / BM) * (g.w->N / BN);
         const int grid = tiles < g.num_sms ? tiles : g.num_sms;
-        kern<<<grid, L::kThreads, L::kBytes, stream>>>(g.a->map, mb, g.w->map_scales, mc, p);
-        return cudaGetLastError();
+        return launch_kernel(kern, dim3(grid), dim3(L::kThreads), L::kBytes, stream, 1, g.a->map, mb, g.w->map_scales,
+                             mc, p);
     }
     // CTA pairs: clusters of 2, one pair per two SMs, each pair looping over 256-row tiles.
     const int tiles = ((g.m_rows + 2 * BM - 1) / (2 * BM)) * (g.w->N / BN);
     const int pairs = tiles < g.num_sms / 2 ? tiles : g.num_sms / 2;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * pairs);
-    cfg.blockDim = dim3(L::kThreads);
-    cfg.dynamicSmemBytes = L::kBytes;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, g.a->map, mb, g.w->map_scales, mc, p);
+    return launch_kernel(kern, dim3(2 * pairs), dim3(L::kThreads), L::kBytes, stream, 2, g.a->map, mb, g.w->map_scales,
+                         mc, p);
 }
 
 template <int EPI>

@@ -6,10 +6,47 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace ge {
 
 // Rows of every activation buffer are padded to this multiple: one tcgen05 M tile.
 constexpr int kRowTile = 128;
+
+// Launch policy of the calling thread: when set, kernels are launched with programmatic
+// stream serialisation, so a kernel's CTAs are scheduled while its predecessor drains and
+// wait for it in pdl_wait().  Every kernel of the library calls pdl_wait() before its first
+// access to activations, which keeps the launch order's data dependencies.
+void set_programmatic_launch(bool on);
+bool programmatic_launch();
+
+// cudaLaunchKernelEx with the calling thread's launch policy (and an optional cluster width).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          int cluster_x, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    unsigned n = 0;
+    if (programmatic_launch()) {
+        attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[n].val.programmaticStreamSerializationAllowed = 1;
+        n++;
+    }
+    if (cluster_x > 1) {
+        attr[n].id = cudaLaunchAttributeClusterDimension;
+        attr[n].val.clusterDim.x = unsigned(cluster_x);
+        attr[n].val.clusterDim.y = 1;
+        attr[n].val.clusterDim.z = 1;
+        n++;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // ------------------------------------------------------------------ GEMM
 enum GemmEpilogue : int {

@@ -512,7 +512,8 @@ int load_model(ge_model* m, const char* path, const ge_load_opts* opts) {
     if (c.layers <= 0 || (c.hidden != 512 && c.hidden != 768) || c.ff % 128 || c.heads <= 0)
         return set_error(m, GE_ERR_INVALID_GGUF, "invalid GGUF file: unsupported dimensions");
     for (auto& l : c.layer)
-        if ((l.hd != 256 && l.hd != 512) || l.kv <= 0 || c.heads % l.kv)
+        if ((l.hd != 256 && l.hd != 512) || l.kv <= 0 || c.heads % l.kv ||
+            c.heads + 2 * l.kv > (l.hd == 256 ? 8 : 6))  // the q/k/v norm kernel's slot capacity
             return set_error(m, GE_ERR_INVALID_GGUF, "invalid GGUF file: unsupported head layout");
     const GgufFile& f = m->file;
     const int d = c.hidden, ff = c.ff, pl = c.per_layer;
@@ -731,6 +732,11 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
                       std::string("GPU execution failed: ") + what + ": " + cudaGetErrorString(x));
     };
     if (e != cudaSuccess) return gpu_fail(e, "cudaSetDevice");
+    // Kernels of this forward overlap their set-up with their predecessor's tail unless disabled.
+    struct LaunchPolicy {
+        explicit LaunchPolicy(bool on) { set_programmatic_launch(on); }
+        ~LaunchPolicy() { set_programmatic_launch(false); }
+    } policy(!(m->flags & GE_LOAD_NO_PDL));
     const int ntok = a.ntok, nseq = a.nseq;
     const int rows = std::max(kRowTile, round_up(ntok, kRowTile));
     // Two work lists: blocks of the tensor-core kernel's query count, and of the CUDA-core

@@ -69,6 +69,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 }
 
 // ------------------------------------------------------------------ TMA
+// Programmatic dependent launch.  pdl_wait() returns once every grid this one depends on has
+// completed and its memory is visible (immediately when launched without the attribute);
+// every thread runs it before touching activations.  pdl_launch() lets the next kernel in the
+// stream be scheduled once every CTA of this grid has run it or exited; the next kernel's CTAs
+// then sit in their own pdl_wait() on whatever SM room is left.  Parked CTAs slow the CTAs
+// still working beside them, so the persistent kernels trigger once their last loads are
+// issued, and the grids of many short CTAs only when they fit in about one wave.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_if_one_wave() {
+    uint32_t nsm;
+    asm("mov.u32 %0, %%nsmid;" : "=r"(nsm));
+    if (gridDim.x * gridDim.y * gridDim.z <= 2 * nsm) pdl_launch();
+}
+
 __device__ __forceinline__ void tma_prefetch(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

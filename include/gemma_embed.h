@@ -58,6 +58,8 @@ typedef struct ge_load_opts {
 
 #define GE_LOAD_NO_GRAPHS 1u      /* launch kernels directly instead of replaying captured CUDA graphs */
 #define GE_LOAD_Q8_ONLY 2u        /* keep only the Q8_0 planes resident; every GEMM dequantises in shared memory */
+#define GE_LOAD_NO_PDL 4u         /* launch each kernel only after its predecessor completed (no programmatic
+                                     dependent launch); results are bit-identical either way */
 
 /* EmbedOptions (EmbedOptions.swift:34-56) minus the task prefix, which the tokenizer applies. */
 typedef struct ge_embed_opts {

@@ -134,3 +134,17 @@ def test_graph_replay_matches_direct_launches(ge, synth, cuda_device):
         second = synth.random_sequences(lens, seed=42, vocab=4096)
         for seqs in (first, second, first):
             assert graphed.embed_tokens(seqs).tobytes() == direct.embed_tokens(seqs).tobytes()
+
+
+@pytest.mark.parametrize("arch", ["gemma-embedding", "gemma-embedding2"])
+@pytest.mark.parametrize("use_graphs", [True, False])
+@pytest.mark.parametrize("option", ["programmatic_launch"])
+def test_launch_options_do_not_change_results(ge, synth, cuda_device, arch, use_graphs, option):
+    """Programmatic dependent launch (each kernel waits in-kernel for its predecessor) gives the
+    bits of plain serialised launches, graphed or direct."""
+    path = synth.model_path(arch, seed=1, layers=6, vocab=4096)
+    with ge.EmbeddingModel.load(path, ge.LoadOptions(use_graphs=use_graphs)) as on, \
+            ge.EmbeddingModel.load(path, ge.LoadOptions(use_graphs=use_graphs, **{option: False})) as off:
+        for seed, lens in ((51, [37, 300, 5, 129]), (52, [700, 1, 64]), (51, [37, 300, 5, 129])):
+            seqs = synth.random_sequences(lens, seed=seed, vocab=4096)
+            assert on.embed_tokens(seqs).tobytes() == off.embed_tokens(seqs).tobytes()
