@@ -266,6 +266,17 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR>::kThreads, 1)
             }
             sbuf = (sbuf + 1 == L::kStgBufs) ? 0 : sbuf + 1;
         };
+        // The accumulator is handed back to the MMA warp as soon as its last columns are in
+        // registers, before they are converted and stored.
+        auto release = [&](int a) {
+            tc_fence_before();
+            if (PAIR) {  // the accumulator is released to the leader, which issues the MMAs
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(mapa_shared(&tempty[a], 0));
+            } else {
+                mbar_arrive(&tempty[a]);
+            }
+        };
         int acc = 0;
         uint32_t acc_ph = 0;
         for (int t = first; t < tiles; t += step) {
@@ -276,63 +287,66 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR>::kThreads, 1)
             const int y = m0 + warp * 32;
             const long row = y + lane;
             const uint32_t taddr = tmem + (uint32_t(warp * 32) << 16) + uint32_t(acc * BN);
-            uint32_t r[32], u[32], packed[32];
+            uint32_t packed[32];
             if (EPI == EPI_F32) {
+                uint32_t r[32];
 #pragma unroll 1
                 for (int c = 0; c < BN / 32; c++) {
                     tmem_ld32(taddr + uint32_t(c * 32), r);
                     tmem_wait_ld();
+                    if (c == BN / 32 - 1) release(acc);
                     emit(r, n0 + c * 32, y, &mapC);
                 }
             } else if (EPI == EPI_GEGLU) {
                 // Columns [0, BN/2) of the tile are gate rows, [BN/2, BN) the matching up rows.
+                // Per 64 output columns: 64 gate and 64 up values in flight, one wait.
 #pragma unroll 1
                 for (int c = 0; c < BN / 128; c++) {
+                    uint32_t g[64], u[64];
+                    tmem_ld32(taddr + uint32_t(c * 64), *reinterpret_cast<uint32_t(*)[32]>(&g[0]));
+                    tmem_ld32(taddr + uint32_t(c * 64 + 32), *reinterpret_cast<uint32_t(*)[32]>(&g[32]));
+                    tmem_ld32(taddr + uint32_t(BN / 2 + c * 64), *reinterpret_cast<uint32_t(*)[32]>(&u[0]));
+                    tmem_ld32(taddr + uint32_t(BN / 2 + c * 64 + 32), *reinterpret_cast<uint32_t(*)[32]>(&u[32]));
+                    tmem_wait_ld();
+                    if (c == BN / 128 - 1) release(acc);
 #pragma unroll
-                    for (int half = 0; half < 2; half++) {
-                        tmem_ld32(taddr + uint32_t(c * 64 + half * 32), r);
-                        tmem_ld32(taddr + uint32_t(BN / 2 + c * 64 + half * 32), u);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 16; i++)
-                            packed[half * 16 + i] =
-                                pack_half2(gelu_tanh(__uint_as_float(r[2 * i])) * __uint_as_float(u[2 * i]),
-                                           gelu_tanh(__uint_as_float(r[2 * i + 1])) * __uint_as_float(u[2 * i + 1]));
-                    }
+                    for (int i = 0; i < 32; i++)
+                        packed[i] = pack_half2(gelu_fast(__uint_as_float(g[2 * i])) * __uint_as_float(u[2 * i]),
+                                               gelu_fast(__uint_as_float(g[2 * i + 1])) * __uint_as_float(u[2 * i + 1]));
                     emit(packed, n0 / 2 + c * 64, y, &mapC);
                 }
             } else if (EPI == EPI_F16 || EPI == EPI_GELU_MUL) {
+                // 128 columns in flight per wait, stored as two 64-column boxes.
 #pragma unroll 1
-                for (int c = 0; c < BN / 64; c++) {
+                for (int c = 0; c < BN / 128; c++) {
+                    uint32_t r[128];
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        tmem_ld32(taddr + uint32_t(c * 128 + q * 32), *reinterpret_cast<uint32_t(*)[32]>(&r[32 * q]));
+                    tmem_wait_ld();
+                    if (c == BN / 128 - 1) release(acc);
 #pragma unroll
                     for (int half = 0; half < 2; half++) {
-                        tmem_ld32(taddr + uint32_t(c * 64 + half * 32), r);
-                        tmem_wait_ld();
+                        const uint32_t* rv = r + 64 * half;
                         if (EPI == EPI_GELU_MUL) {
-                            const float4* ax = reinterpret_cast<const float4*>(p.aux + row * p.ldaux + n0 + c * 64 + half * 32);
+                            const float4* ax =
+                                reinterpret_cast<const float4*>(p.aux + row * p.ldaux + n0 + c * 128 + half * 64);
 #pragma unroll
-                            for (int i = 0; i < 8; i++) {
+                            for (int i = 0; i < 16; i++) {
                                 const float4 a = ax[i];
-                                packed[half * 16 + 2 * i] = pack_half2(gelu_tanh(__uint_as_float(r[4 * i])) * a.x,
-                                                                       gelu_tanh(__uint_as_float(r[4 * i + 1])) * a.y);
-                                packed[half * 16 + 2 * i + 1] = pack_half2(gelu_tanh(__uint_as_float(r[4 * i + 2])) * a.z,
-                                                                           gelu_tanh(__uint_as_float(r[4 * i + 3])) * a.w);
+                                packed[2 * i] = pack_half2(gelu_fast(__uint_as_float(rv[4 * i])) * a.x,
+                                                           gelu_fast(__uint_as_float(rv[4 * i + 1])) * a.y);
+                                packed[2 * i + 1] = pack_half2(gelu_fast(__uint_as_float(rv[4 * i + 2])) * a.z,
+                                                               gelu_fast(__uint_as_float(rv[4 * i + 3])) * a.w);
                             }
                         } else {
 #pragma unroll
-                            for (int i = 0; i < 16; i++)
-                                packed[half * 16 + i] = pack_half2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+                            for (int i = 0; i < 32; i++)
+                                packed[i] = pack_half2(__uint_as_float(rv[2 * i]), __uint_as_float(rv[2 * i + 1]));
                         }
+                        emit(packed, n0 + c * 128 + half * 64, y, &mapC);
                     }
-                    emit(packed, n0 + c * 64, y, &mapC);
                 }
-            }
-            tc_fence_before();
-            if (PAIR) {  // the accumulator is released to the leader, which issues the MMAs
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(mapa_shared(&tempty[acc], 0));
-            } else {
-                mbar_arrive(&tempty[acc]);
             }
             if (++acc == 2) {
                 acc = 0;

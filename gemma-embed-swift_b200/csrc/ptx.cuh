@@ -274,6 +274,16 @@ __device__ __forceinline__ float gelu_tanh(float x) {
     return 0.5f * x * (1.0f + tanhf(c * x * (1.0f + 0.044715f * x * x)));
 }
 
+// The same GELU through 0.5 * (1 + tanh(u)) = 1 / (1 + exp(-2u)): one ex2.approx and one
+// fast reciprocal, relative error near 1e-6 (well below the fp16 rounding of its outputs).
+// For x -> -inf the exponential overflows to +inf and the quotient is -0.
+__device__ __forceinline__ float gelu_fast(float x) {
+    constexpr float k0 = -2.0f * 0.79788456080286535587989211986876f * 1.4426950408889634f;  // -2c log2(e)
+    constexpr float k1 = k0 * 0.044715f;
+    const float e = ex2_approx(x * fmaf(x * x, k1, k0));
+    return __fdividef(x, 1.0f + e);
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
