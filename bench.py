@@ -257,13 +257,15 @@ def main():
         prof = model.profile(tokens, ranges, reps=a.profile_reps)
         fwd_ms = sum(p["ms_per_launch"] * p["launches_per_forward"] for p in prof)
         top = max(prof, key=lambda p: p["ms_per_launch"] * p["launches_per_forward"])
-        tensor = top["flops_per_launch"] > 0
+        # The binding roofline is the one the kernel runs closer to: tensor FLOP/s or HBM bytes/s.
+        sec = top["ms_per_launch"] / 1000.0
+        tf = top["flops_per_launch"] / sec / 1e12
+        gbs = top["bytes_per_launch"] / sec / 1e9
+        tensor = tf / pk["bf16_tflops"] > gbs / pk["hbm_gbs"]
         if tensor:
-            ach = top["flops_per_launch"] / (top["ms_per_launch"] / 1000.0) / 1e12
-            peak, unit = pk["bf16_tflops"], "TFLOP/s"
+            ach, peak, unit = tf, pk["bf16_tflops"], "TFLOP/s"
         else:
-            ach = top["bytes_per_launch"] / (top["ms_per_launch"] / 1000.0) / 1e9
-            peak, unit = pk["hbm_gbs"], "GB/s"
+            ach, peak, unit = gbs, pk["hbm_gbs"], "GB/s"
         roofline = {"kernel": top["name"], "bound": "tensor" if tensor else "hbm", "achieved": ach, "peak": peak,
                     "unit": unit, "frac": ach / peak, "traffic": None, "peak_source": pk["source"],
                     "share_of_forward": top["ms_per_launch"] * top["launches_per_forward"] / fwd_ms,

@@ -32,6 +32,7 @@ STATUS = {
 LOAD_NO_GRAPHS = 1
 LOAD_Q8_ONLY = 2
 LOAD_NO_PDL = 4
+LOAD_FUSED_RESIDUAL = 8
 
 
 class GemmaEmbedError(RuntimeError):
@@ -78,6 +79,7 @@ class LoadOptions:
     use_graphs: bool = True
     q8_only: bool = False
     programmatic_launch: bool = True  # overlap each kernel's set-up with its predecessor's tail
+    fused_residual: bool = False  # run each residual step inside the projection before it
 
 
 @dataclass
@@ -170,7 +172,8 @@ class EmbeddingModel:
         o.device_mask = mask
         o.batch_token_budget = int(options.batch_token_budget)
         o.flags = ((0 if options.use_graphs else LOAD_NO_GRAPHS) | (LOAD_Q8_ONLY if options.q8_only else 0)
-                   | (0 if options.programmatic_launch else LOAD_NO_PDL))
+                   | (0 if options.programmatic_launch else LOAD_NO_PDL)
+                   | (LOAD_FUSED_RESIDUAL if options.fused_residual else 0))
         h = ctypes.c_void_p()
         _check(L.ge_load(str(path).encode(), ctypes.byref(o), ctypes.byref(h)), None)
         return cls(h, options)

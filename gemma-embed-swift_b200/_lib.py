@@ -71,6 +71,8 @@ SIGNATURES = {
 TEST_SIGNATURES = {
     "ge_test_gemm": ([u16p, ctypes.c_int32, ctypes.c_int32, P(ctypes.c_uint8), ctypes.c_int32, ctypes.c_int32,
                       ctypes.c_int32, f32p, f32p], ctypes.c_int),
+    "ge_test_gemm_residual": ([u16p, ctypes.c_int32, ctypes.c_int32, P(ctypes.c_uint8), ctypes.c_int32, ctypes.c_int32,
+                               f32p, f32p, ctypes.c_float, f32p, ctypes.c_float, f32p, f32p], ctypes.c_int),
     "ge_test_attention": ([u16p, u16p, u16p, ctypes.c_int32, P(GeSeq), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                            ctypes.c_int32, ctypes.c_int32, u16p], ctypes.c_int),
     "ge_test_last_error": ([], ctypes.c_char_p),

@@ -15,6 +15,10 @@
 // Every wait is bounded: on timeout the kernel records GE_ERR_TIMEOUT and returns.
 #include <cudaTypedefs.h>
 
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "kernels.hpp"
 #include "ptx.cuh"
 
@@ -26,21 +30,30 @@ constexpr int kBN = 256;
 
 // PAIR: a 2-CTA cluster computes 256 x BN tiles with tcgen05.mma.cta_group::2; each CTA
 // holds 128 rows of A and BN/2 rows of B per stage, so shared-memory traffic per MMA halves.
-template <int BN, bool Q8, bool PAIR = false>
+// RES (EPI_RESIDUAL): clusters of N / BN CTAs share row blocks; the epilogue also stages
+// residual-stream tiles (kXin) and receives the cluster's per-row sums of squares (kXch).
+template <int BN, bool Q8, bool PAIR = false, bool RES = false>
 struct GemmLayout {
-    static constexpr int kStages = Q8 ? 3 : ((PAIR || BN < 256) ? 6 : 4);
+    static constexpr int kStages = RES ? (Q8 ? 2 : 3) : Q8 ? 3 : ((PAIR || BN < 256) ? 6 : 4);
     static constexpr int kA = BM * BK * 2;
     static constexpr int kB = (PAIR ? BN / 2 : BN) * BK * 2;
     static constexpr int kB8 = Q8 ? BN * BK : 0;
     static constexpr int kSc = Q8 ? 2 * BN * 2 : 0;
     static constexpr int kStage = (kA + kB + kB8 + kSc + 1023) / 1024 * 1024;
     // Epilogue staging: per epilogue warp, kStgBufs tiles of 32 rows x 128 bytes that TMA
-    // stores to global memory (one buffer on the Q8 path, whose stages are larger).
-    static constexpr int kStgBufs = Q8 ? 1 : 2;
+    // stores to global memory (one buffer on the Q8 path, whose stages are larger).  RES: four,
+    // which also receive the residual-stream tiles and are rewritten in place.
+    // RES on fp16 weights: eight epilogue warps, two per TMEM lane quarter, each owning half of
+    // the tile's columns (warps 0-3 and 6-9; warp w reads TMEM lanes 32 * (w % 4) + [0, 32)).
+    static constexpr int kEpiWarps = (RES && !Q8) ? 8 : 4;
+    static constexpr int kStgBufs = RES ? (kEpiWarps == 8 ? 2 : 4) : Q8 ? 1 : 2;
     static constexpr int kStgOff = kStages * kStage;
-    static constexpr int kBarOff = kStgOff + 4 * kStgBufs * 4096;
-    static constexpr int kBytes = kBarOff + 256 + 1024;  // barriers, TMEM slot, alignment slack
-    static constexpr int kThreads = Q8 ? 320 : 192;
+    static constexpr int kXchOff = kStgOff + kEpiWarps * kStgBufs * 4096;
+    static constexpr int kMaxCluster = 4;  // RES: [2 tile parities][2 rounds][kMaxCluster][128] floats
+    static constexpr int kHsumOff = kXchOff + (RES ? 2 * 2 * kMaxCluster * 128 * 4 : 0);
+    static constexpr int kBarOff = kHsumOff + (RES ? 2 * 2 * 2 * 128 * 4 : 0);  // [parity][round][half][128]
+    static constexpr int kBytes = kBarOff + 512 + 1024;  // barriers, TMEM slot, alignment slack
+    static constexpr int kThreads = (Q8 || kEpiWarps == 8) ? 320 : 192;
 };
 
 struct GemmParams {
@@ -50,7 +63,22 @@ struct GemmParams {
     const float* aux;
     int ldaux;
     int* err;
+    // EPI_RESIDUAL
+    const float* w_post;
+    const float* w_next;
+    float scale, eps;
+    int store_h, store_y;
 };
+
+// EPI_RESIDUAL output maps: the next norm's fp16 (boxes of 32 rows x 64) and fp32 (32 x 32)
+// results.  mapC is the residual stream's fp32 map, used to load and to store it.
+struct EpiMaps {
+    CUtensorMap h, y;
+};
+
+__device__ __forceinline__ float round_f16(uint32_t acc_bits) {
+    return __half2float(__float2half_rn(__uint_as_float(acc_bits)));
+}
 
 // Waits without giving up on another role's error (used to drain in-flight TMA loads).
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
@@ -81,11 +109,14 @@ __device__ __forceinline__ void dequant16(uint4 raw, __half2 s2, uint32_t (&o)[8
 }
 
 template <int BN, int EPI, bool Q8, bool PAIR>
-__global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR>::kThreads, 1)
+__global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>::kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-           const __grid_constant__ CUtensorMap mapS, const __grid_constant__ CUtensorMap mapC, GemmParams p) {
+           const __grid_constant__ CUtensorMap mapS, const __grid_constant__ CUtensorMap mapC,
+           const __grid_constant__ EpiMaps emaps, GemmParams p) {
+    constexpr bool RES = EPI == EPI_RESIDUAL;
     static_assert(!(PAIR && Q8), "the pair kernel reads fp16 weights");
-    using L = GemmLayout<BN, Q8, PAIR>;
+    static_assert(!(PAIR && RES), "row clusters and CTA pairs are exclusive");
+    using L = GemmLayout<BN, Q8, PAIR, RES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full_tma = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
@@ -93,20 +124,30 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR>::kThreads, 1)
     uint64_t* empty = full_b + L::kStages;
     uint64_t* tfull = empty + L::kStages;
     uint64_t* tempty = tfull + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    uint64_t* xin_bar = tempty + 2;   // RES: [epilogue warp][up to 4 buffers]
+    uint64_t* xch_bar = xin_bar + 32;  // RES: [tile parity][round]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xch_bar + 4);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tiles = p.N / BN;
     const int kb_count = p.K / BK;
     // Tiles in a fixed order: n fastest, so the CTAs working at one time share A rows in L2.
     // A pair's tile covers 256 rows: the pair leader (rank 0) the first 128, rank 1 the rest.
-    const uint32_t crank = PAIR ? cluster_ctarank() : 0;
-    const int tiles = n_tiles * (PAIR ? (p.M + 2 * BM - 1) / (2 * BM) : p.M / BM);
-    const int first = PAIR ? int(blockIdx.x >> 1) : int(blockIdx.x);
-    const int step = PAIR ? int(gridDim.x >> 1) : int(gridDim.x);
+    // A row cluster (RES) walks row blocks; its CTA of rank r always takes columns r * BN.
+    const uint32_t crank = (PAIR || RES) ? cluster_ctarank() : 0;
+    const bool leader = !PAIR || crank == 0;  // issues the MMAs and drains the loads
+    const uint32_t csize = RES ? cluster_nctarank() : PAIR ? 2u : 1u;
+    const int tiles = RES ? p.M / BM : n_tiles * (PAIR ? (p.M + 2 * BM - 1) / (2 * BM) : p.M / BM);
+    const int first = int(blockIdx.x / csize);
+    const int step = int(gridDim.x / csize);
     auto tile_origin = [&](int t, int& m0, int& n0) {
-        m0 = (t / n_tiles) * (PAIR ? 2 * BM : BM) + int(crank) * BM;
-        n0 = (t % n_tiles) * BN;
+        if (RES) {
+            m0 = t * BM;
+            n0 = int(crank) * BN;
+        } else {
+            m0 = (t / n_tiles) * (PAIR ? 2 * BM : BM) + int(crank) * BM;
+            n0 = (t % n_tiles) * BN;
+        }
     };
 
     if (threadIdx.x == 0) {
@@ -117,7 +158,17 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR>::kThreads, 1)
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], PAIR ? 8 : 128);  // PAIR: one arrival per epilogue warp of both CTAs
+            // PAIR: one arrival per epilogue warp of both CTAs; otherwise one per epilogue thread
+            mbar_init(&tempty[a], PAIR ? 8 : 32 * L::kEpiWarps);
+        }
+        if (RES) {
+            for (int i = 0; i < 32; i++) mbar_init(&xin_bar[i], 1);
+            // Each exchange barrier completes when every other CTA of the cluster has delivered
+            // its 128 row sums; its single arrival is this CTA's own arming for the next use.
+            for (int i = 0; i < 4; i++) {
+                mbar_init(&xch_bar[i], 1);
+                mbar_expect_tx(&xch_bar[i], (csize - 1) * 128 * 4);
+            }
         }
         fence_mbar_init();
     }
@@ -126,6 +177,10 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR>::kThreads, 1)
         tma_prefetch(&mapB);
         if (Q8) tma_prefetch(&mapS);
         tma_prefetch(&mapC);
+        if (RES) {
+            tma_prefetch(&emaps.h);
+            tma_prefetch(&emaps.y);
+        }
     }
     if (warp == 5) {
         if (PAIR) {
@@ -138,7 +193,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR>::kThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (PAIR) cluster_sync();  // the peer's barriers are initialised before any remote use
+    if (PAIR || RES) cluster_sync();  // the peers' barriers are initialised before any remote use
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     // The set-up above overlaps the previous kernel's tail; A and the output are its data.
@@ -187,7 +242,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR>::kThreads, 1)
             pdl_launch();  // this CTA's loads are all issued: the next kernel may be scheduled
             // Every issued load must land before the CTA exits, also after an error.  A pair's
             // loads complete on the leader's barriers, so the leader drains for both CTAs.
-            if (crank == 0)
+            if (leader)
                 for (int j = 0; j < L::kStages; j++) {
                     const long c = issued / L::kStages + (j < issued % L::kStages ? 1 : 0);
                     if (c > 0) drain_wait(&full_tma[j], uint32_t((c - 1) & 1));
@@ -195,7 +250,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR>::kThreads, 1)
         }
     } else if (warp == 5) {
         // ---------------------------------------------------------- MMA issuer
-        if (lane == 0 && crank == 0) {  // a pair's MMAs are issued by its leader alone
+        if (lane == 0 && leader) {  // a pair's MMAs are issued by its leader alone
             const uint32_t idesc = idesc_f16(PAIR ? 2 * BM : BM, BN);
             int s = 0, acc = 0;
             uint32_t ph = 0, acc_ph = 0;
@@ -243,12 +298,13 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR>::kThreads, 1)
                 }
             }
         }
-    } else if (warp < 4) {
+    } else if (warp < 4 || (L::kEpiWarps == 8 && warp >= 6)) {
         // ---------------------------------------------------------- epilogue
         // Each warp owns 32 accumulator rows (its TMEM lane quarter).  Per 128-byte column group
         // a thread packs its row's values, writes them 128-byte-swizzled into the warp's staging
         // buffer, and lane 0 TMA-stores the 32 x 128-byte box: full-line writes to global memory.
-        uint8_t* stg = smem + L::kStgOff + warp * L::kStgBufs * 4096;
+        const int epi = warp < 4 ? warp : warp - 2;  // epilogue warp index 0..7
+        uint8_t* stg = smem + L::kStgOff + epi * L::kStgBufs * 4096;
         int sbuf = 0;
         auto emit = [&](const uint32_t (&v)[32], int x, int y, const CUtensorMap* map) {
             if (lane == 0) bulk_wait_read<L::kStgBufs - 1>();
@@ -279,6 +335,199 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR>::kThreads, 1)
         };
         int acc = 0;
         uint32_t acc_ph = 0;
+        if constexpr (RES) {
+            // Residual epilogue, per tile of 128 rows x BN columns (this CTA's share of the row
+            // block).  A thread owns one row of HW columns: all BN with four epilogue warps, or
+            // one half with eight (the two warps of a TMEM lane quarter split the columns).
+            //   1. ss = sum of t^2 over the columns, t = fp16(acc); the halves of a row add
+            //      through shared memory (a named barrier per lane quarter)
+            //   2. exchange: the CTA's 128 row sums go to the other CTAs of the cluster
+            //      (st.async completing on their exchange barrier); sums add in rank order
+            //   3. x = (x + t * inv * w_post) * scale, 32 columns at a time: the x tile streams
+            //      through the warp's staging buffers by TMA (kStgBufs chunks ahead), the new
+            //      values go back to TMEM; ss2 = sum of the new x^2
+            //   4. ss2 as in 1-2
+            //   5. from TMEM: x stored back, y = x * inv2 * w_next stored as fp16 and/or fp32
+            // The order of every sum is fixed, so a row's results do not depend on the batch.
+            constexpr int NB = L::kStgBufs;
+            constexpr int HALVES = L::kEpiWarps / 4;
+            constexpr int HW = BN / HALVES;
+            const int quarter = warp & 3;
+            const int half = warp < 4 ? 0 : 1;
+            float* xch = reinterpret_cast<float*>(smem + L::kXchOff);
+            float* hsum = reinterpret_cast<float*>(smem + L::kHsumOff);
+            const int row_local = quarter * 32 + lane;
+            uint32_t xin_ph = 0u, xin_pending = 0u;  // bit b: phase parity / load in flight of buffer b
+            auto load_x = [&](int b, int x, int y) {
+                if (lane == 0) {
+                    mbar_expect_tx(&xin_bar[epi * 4 + b], 4096);
+                    tma_load_2d(stg + b * 4096, &mapC, &xin_bar[epi * 4 + b], x, y);
+                }
+                xin_pending |= 1u << b;
+            };
+            // Row sum over the CTA's columns, then over the cluster, in fixed order.
+            auto row_total = [&](float part, int par, int rd, uint32_t ph, float& total) -> bool {
+                if (HALVES == 2) {
+                    float* hs = hsum + ((par * 2 + rd) * 2) * 128;
+                    hs[half * 128 + row_local] = part;
+                    asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+                    part = hs[row_local] + hs[128 + row_local];
+                }
+                const int slot_index = par * 2 + rd;
+                float* slot = xch + slot_index * L::kMaxCluster * 128;
+                uint64_t* bar = &xch_bar[slot_index];
+                if (half == 0)
+                    for (uint32_t q = 0; q < csize; q++)
+                        if (q != crank)
+                            st_async_b32(mapa_shared(slot + crank * 128 + row_local, q), __float_as_uint(part),
+                                         mapa_shared(bar, q));
+                if (!mbar_wait(bar, ph, p.err)) return false;
+                float sum = 0.f;
+                for (uint32_t q = 0; q < csize; q++) sum += q == crank ? part : slot[q * 128 + row_local];
+                total = sum;
+                // Armed again for its next use, two tiles on; no peer can deliver for that use
+                // before this CTA has sent its sums of the tile in between.
+                if (threadIdx.x == 0) mbar_expect_tx(bar, (csize - 1) * 128 * 4);
+                return true;
+            };
+            constexpr int kchunks = HW / 32;
+            int k = 0;
+            bool ok = true;
+            for (int t = first; t < tiles && ok; t += step, k++) {
+                int m0, n0;
+                tile_origin(t, m0, n0);
+                const int c0 = n0 + half * HW;  // this warp's first column
+                const int y = m0 + quarter * 32;
+                // The first x chunks travel while the accumulator fills, once the previous
+                // tile's stores have left the buffers.
+                if (lane == 0) bulk_wait_read<0>();
+                __syncwarp();
+                for (int b = 0; b < NB; b++) load_x(b, c0 + 32 * b, y);
+                if (!mbar_wait(&tfull[acc], acc_ph, p.err)) break;
+                tc_fence_after();
+                const uint32_t taddr = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(acc * BN + half * HW);
+                const int par = k & 1;
+                const uint32_t xph = uint32_t(k >> 1) & 1u;
+                // 1.-2. sum of squares of the fp16-rounded projection: one partial per 128
+                // columns, added as (first + second) with four warps or eight alike
+                float ssh[2] = {0.f, 0.f};
+#pragma unroll
+                for (int c = 0; c < HW / 128; c++) {
+                    uint32_t r[128];
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        tmem_ld32(taddr + uint32_t(c * 128 + q * 32), *reinterpret_cast<uint32_t(*)[32]>(&r[32 * q]));
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 128; i++) {
+                        const float tv = round_f16(r[i]);
+                        ssh[c] += tv * tv;
+                    }
+                }
+                float total;
+                if (!row_total(HALVES == 2 ? ssh[0] : ssh[0] + ssh[1], par, 0, xph, total)) break;
+                const float inv = 1.0f / sqrtf(total / float(p.N) + p.eps);
+                // 3. the residual update (ss2 in per-128-column partials like ss)
+                float ss2a = 0.f, ss2b = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < kchunks; c++) {
+                    const int b = c % NB;
+                    if (!mbar_wait(&xin_bar[epi * 4 + b], (xin_ph >> b) & 1u, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    xin_ph ^= 1u << b;
+                    xin_pending &= ~(1u << b);
+                    uint32_t r[32];
+                    tmem_ld32(taddr + uint32_t(c * 32), r);
+                    const uint8_t* xb = stg + b * 4096 + lane * 128;
+                    float xv[32];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const float4 q = *reinterpret_cast<const float4*>(xb + ((j ^ (lane & 7)) * 16));
+                        xv[4 * j] = q.x;
+                        xv[4 * j + 1] = q.y;
+                        xv[4 * j + 2] = q.z;
+                        xv[4 * j + 3] = q.w;
+                    }
+                    // The buffer is read: it takes chunk c + NB.
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (c + NB < kchunks) load_x(b, c0 + (c + NB) * 32, y);
+                    tmem_wait_ld();
+                    const float4* wp4 = reinterpret_cast<const float4*>(p.w_post + c0 + c * 32);
+                    uint32_t vo[32];
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const float4 w = __ldg(wp4 + j);
+                        const float ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const int i = 4 * j + e;
+                            float v = xv[i] + round_f16(r[i]) * inv * ww[e];
+                            if (p.scale != 1.0f) v *= p.scale;
+                            vo[i] = __float_as_uint(v);
+                        }
+                    }
+                    float s2 = c >= 4 ? ss2b : ss2a;
+#pragma unroll
+                    for (int i = 0; i < 32; i++) s2 += __uint_as_float(vo[i]) * __uint_as_float(vo[i]);
+                    if (c >= 4)
+                        ss2b = s2;
+                    else
+                        ss2a = s2;
+                    tmem_st32(taddr + uint32_t(c * 32), vo);
+                }
+                if (!ok) break;
+                tmem_wait_st();
+                const bool next = p.store_h || p.store_y;
+                float inv2 = 0.f;
+                if (next) {
+                    if (!row_total(HALVES == 2 ? ss2a : ss2a + ss2b, par, 1, xph, total)) break;
+                    inv2 = 1.0f / sqrtf(total / float(p.N) + p.eps);
+                }
+                // 5. stores from TMEM, 64 columns at a time
+                sbuf = 0;
+#pragma unroll 1
+                for (int c = 0; c < HW / 64; c++) {
+                    uint32_t r[64];
+                    tmem_ld32(taddr + uint32_t(c * 64), *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+                    tmem_ld32(taddr + uint32_t(c * 64 + 32), *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+                    tmem_wait_ld();
+                    if (c == HW / 64 - 1) release(acc);
+                    emit(*reinterpret_cast<uint32_t(*)[32]>(&r[0]), c0 + c * 64, y, &mapC);
+                    emit(*reinterpret_cast<uint32_t(*)[32]>(&r[32]), c0 + c * 64 + 32, y, &mapC);
+                    if (!next) continue;
+                    const float4* wn4 = reinterpret_cast<const float4*>(p.w_next + c0 + c * 64);
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        const float4 w = __ldg(wn4 + j);
+                        r[4 * j] = __float_as_uint(__uint_as_float(r[4 * j]) * inv2 * w.x);
+                        r[4 * j + 1] = __float_as_uint(__uint_as_float(r[4 * j + 1]) * inv2 * w.y);
+                        r[4 * j + 2] = __float_as_uint(__uint_as_float(r[4 * j + 2]) * inv2 * w.z);
+                        r[4 * j + 3] = __float_as_uint(__uint_as_float(r[4 * j + 3]) * inv2 * w.w);
+                    }
+                    if (p.store_h) {
+                        uint32_t packed[32];
+#pragma unroll
+                        for (int i = 0; i < 32; i++)
+                            packed[i] = pack_half2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
+                        emit(packed, c0 + c * 64, y, &emaps.h);
+                    }
+                    if (p.store_y) {
+                        emit(*reinterpret_cast<uint32_t(*)[32]>(&r[0]), c0 + c * 64, y, &emaps.y);
+                        emit(*reinterpret_cast<uint32_t(*)[32]>(&r[32]), c0 + c * 64 + 32, y, &emaps.y);
+                    }
+                }
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_ph ^= 1;
+                }
+            }
+            // x loads still in flight after an error land before the CTA exits.
+            for (int b = 0; b < NB; b++)
+                if ((xin_pending >> b) & 1u) drain_wait(&xin_bar[epi * 4 + b], (xin_ph >> b) & 1u);
+        } else
         for (int t = first; t < tiles; t += step) {
             if (!mbar_wait(&tfull[acc], acc_ph, p.err)) break;
             tc_fence_after();
@@ -397,7 +646,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR>::kThreads, 1)
 
     tc_fence_before();
     __syncthreads();
-    if (PAIR) cluster_sync();  // neither CTA leaves while the other may still signal it
+    if (PAIR || RES) cluster_sync();  // no CTA leaves while another may still signal it
     if (warp == 5) {
         tc_fence_after();
         if (PAIR)
@@ -461,7 +710,7 @@ bool encode_activation_map(DevActivation& a) {
 
 template <int EPI, bool Q8, bool PAIR, int BN = kBN>
 static cudaError_t configure_t() {
-    using L = GemmLayout<BN, Q8, PAIR>;
+    using L = GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>;
     return cudaFuncSetAttribute(k_gemm<BN, EPI, Q8, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
 }
 
@@ -469,8 +718,10 @@ template <int EPI>
 static cudaError_t configure_epi() {
     cudaError_t e = configure_t<EPI, false, false>();
     if (e == cudaSuccess) e = configure_t<EPI, true, false>();
-    if (e == cudaSuccess) e = configure_t<EPI, false, true>();
-    if (EPI != EPI_GEGLU && e == cudaSuccess) e = configure_t<EPI, false, false, 128>();
+    if constexpr (EPI != EPI_RESIDUAL) {
+        if (e == cudaSuccess) e = configure_t<EPI, false, true>();
+        if (EPI != EPI_GEGLU && e == cudaSuccess) e = configure_t<EPI, false, false, 128>();
+    }
     return e;
 }
 
@@ -481,12 +732,49 @@ cudaError_t configure_gemm_kernels() {
     if (e == cudaSuccess) e = configure_epi<EPI_F16>();
     if (e == cudaSuccess) e = configure_epi<EPI_GEGLU>();
     if (e == cudaSuccess) e = configure_epi<EPI_GELU_MUL>();
+    if (e == cudaSuccess) e = configure_epi<EPI_RESIDUAL>();
     return e;
+}
+
+// Co-resident clusters of `csize` CTAs per device and kernel, measured once (persistent
+// cluster grids larger than this would run in waves).
+static std::mutex g_cluster_mu;
+static std::map<std::tuple<int, const void*, int>, int> g_cluster_cap;
+
+static int max_clusters(const void* kern, int csize, int threads, int smem, int num_sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const auto key = std::make_tuple(dev, kern, csize);
+    {
+        std::lock_guard<std::mutex> g(g_cluster_mu);
+        auto it = g_cluster_cap.find(key);
+        if (it != g_cluster_cap.end()) return it->second;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(csize * (num_sms / csize)));
+    cfg.blockDim = dim3(unsigned(threads));
+    cfg.dynamicSmemBytes = size_t(smem);
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = unsigned(csize);
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = num_sms / csize;
+    }
+    std::lock_guard<std::mutex> g(g_cluster_mu);
+    g_cluster_cap[key] = n;
+    return n;
 }
 
 template <int EPI, bool Q8, bool PAIR, int BN = kBN>
 static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
-    using L = GemmLayout<BN, Q8, PAIR>;
+    constexpr bool RES = EPI == EPI_RESIDUAL;
+    using L = GemmLayout<BN, Q8, PAIR, RES>;
     auto kern = k_gemm<BN, EPI, Q8, PAIR>;
     GemmParams p{};
     p.M = g.m_rows;
@@ -499,34 +787,69 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
     p.err = g.err;
     // Weight boxes: kBN rows (map_f16, map_q8) or kBN / 2 rows (CTA pairs, 128-wide tiles).
     const CUtensorMap& mb = Q8 ? g.w->map_q8 : ((PAIR || BN != kBN) ? g.w->map_f16_half : g.w->map_f16);
+    CUtensorMap mc;
+    EpiMaps em;
+    if (RES) {
+        // mapC is the residual stream (fp32, boxes of 32 rows x 32 columns, loaded and stored).
+        const int csize = g.w->N / BN;
+        if (!g.x || !g.w_post || g.w->N % BN || csize > L::kMaxCluster) return cudaErrorInvalidValue;
+        p.w_post = g.w_post;
+        p.w_next = g.w_next;
+        p.scale = g.scale;
+        p.eps = g.eps;
+        p.store_h = g.w_next && g.h16;
+        p.store_y = g.w_next && g.y32;
+        if (!encode_2d(&mc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.x, uint64_t(g.w->N), uint64_t(g.m_rows), 32, 32,
+                       CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorInvalidValue;
+        em.h = mc;
+        em.y = mc;
+        if (p.store_h && !encode_2d(&em.h, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.h16, uint64_t(g.w->N),
+                                    uint64_t(g.m_rows), 64, 32, CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorInvalidValue;
+        if (p.store_y && !encode_2d(&em.y, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.y32, uint64_t(g.w->N),
+                                    uint64_t(g.m_rows), 32, 32, CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorInvalidValue;
+        const int row_blocks = g.m_rows / BM;
+        const int cap = max_clusters(reinterpret_cast<const void*>(kern), csize, L::kThreads, L::kBytes, g.num_sms);
+        const int clusters = row_blocks < cap ? row_blocks : cap;
+        return launch_kernel(kern, dim3(csize * clusters), dim3(L::kThreads), L::kBytes, stream, csize, g.a->map, mb,
+                             g.w->map_scales, mc, em, p);
+    }
     // Output map: boxes of 32 rows x 128 bytes (32 fp32 or 64 fp16 columns), 128-byte swizzle.
     const bool f32 = EPI == EPI_F32;
     const int out_cols = EPI == EPI_GEGLU ? g.w->N / 2 : g.w->N;
     if (g.ldo < out_cols) return cudaErrorInvalidValue;
-    CUtensorMap mc;
     if (!encode_2d(&mc, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, f32 ? 4 : 2, g.out,
                    uint64_t(g.ldo), uint64_t(g.m_rows), f32 ? 32 : 64, 32, CU_TENSOR_MAP_SWIZZLE_128B))
         return cudaErrorInvalidValue;
+    em.h = mc;
+    em.y = mc;
     if (!PAIR) {
         const int tiles = (g.m_rows / BM) * (g.w->N / BN);
         const int grid = tiles < g.num_sms ? tiles : g.num_sms;
         return launch_kernel(kern, dim3(grid), dim3(L::kThreads), L::kBytes, stream, 1, g.a->map, mb, g.w->map_scales,
-                             mc, p);
+                             mc, em, p);
     }
-    // CTA pairs: clusters of 2, one pair per two SMs, each pair looping over 256-row tiles.
+    // CTA pairs: clusters of 2, each pair looping over 256-row tiles.
     const int tiles = ((g.m_rows + 2 * BM - 1) / (2 * BM)) * (g.w->N / BN);
-    const int pairs = tiles < g.num_sms / 2 ? tiles : g.num_sms / 2;
+    const int cap = max_clusters(reinterpret_cast<const void*>(kern), 2, L::kThreads, L::kBytes, g.num_sms);
+    const int pairs = tiles < cap ? tiles : cap;
     return launch_kernel(kern, dim3(2 * pairs), dim3(L::kThreads), L::kBytes, stream, 2, g.a->map, mb, g.w->map_scales,
-                         mc, p);
+                         mc, em, p);
 }
 
 template <int EPI>
 static cudaError_t launch_epi(const GemmLaunch& g, cudaStream_t stream, bool q8, bool pair, bool narrow) {
     if (q8) return launch_t<EPI, true, false>(g, stream);
-    if (pair) return launch_t<EPI, false, true>(g, stream);
-    if constexpr (EPI != EPI_GEGLU)
-        if (narrow) return launch_t<EPI, false, false, 128>(g, stream);
-    return launch_t<EPI, false, false>(g, stream);
+    if constexpr (EPI == EPI_RESIDUAL) {
+        return launch_t<EPI, false, false>(g, stream);
+    } else {
+        if (pair) return launch_t<EPI, false, true>(g, stream);
+        if constexpr (EPI != EPI_GEGLU)
+            if (narrow) return launch_t<EPI, false, false, 128>(g, stream);
+        return launch_t<EPI, false, false>(g, stream);
+    }
 }
 
 cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream) {
@@ -545,6 +868,9 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream) {
     case EPI_F16: return launch_epi<EPI_F16>(g, stream, q8, pair, narrow);
     case EPI_GEGLU: return launch_epi<EPI_GEGLU>(g, stream, q8, pair, narrow);
     case EPI_GELU_MUL: return launch_epi<EPI_GELU_MUL>(g, stream, q8, pair, narrow);
+    case EPI_RESIDUAL:
+        if (g.mode == GEMM_PAIR || g.mode == GEMM_NARROW) return cudaErrorInvalidValue;
+        return launch_epi<EPI_RESIDUAL>(g, stream, q8, false, false);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -54,6 +54,11 @@ enum GemmEpilogue : int {
     EPI_F16 = 1,    // out[m][n] = acc (fp16)
     EPI_GEGLU = 2,  // weight rows interleave gate and up in blocks of BN/2: out = gelu(gate) * up (fp16)
     EPI_GELU_MUL = 3,  // out = gelu(acc) * aux[m][n] (fp16), aux fp32 with row stride ldaux
+    // The residual step of k_residual_norm on whole rows: t = fp16(acc); x = (x + rmsnorm(t) *
+    // w_post) * scale; then optionally y = rmsnorm(x) * w_next stored as fp16 (h16) and/or fp32
+    // (y32).  N = the hidden size; the N / 256 CTAs of a cluster hold one row block's columns
+    // and exchange the per-row sums of squares through distributed shared memory.
+    EPI_RESIDUAL = 4,
 };
 
 
@@ -98,6 +103,15 @@ struct GemmLaunch {
     int mode = GEMM_AUTO;
     int* err;
     int num_sms;
+    // EPI_RESIDUAL only: the residual stream x [m_rows][N] (read and rewritten), its norm
+    // weights and the outputs of the next norm (either may be null; w_next null skips both).
+    float* x = nullptr;
+    const float* w_post = nullptr;
+    float scale = 1.0f;
+    const float* w_next = nullptr;
+    float eps = 1e-6f;
+    __half* h16 = nullptr;
+    float* y32 = nullptr;
 };
 cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream);
 // Kernel attributes (dynamic shared-memory limits) for the current device; call once per

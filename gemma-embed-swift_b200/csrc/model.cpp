@@ -803,6 +803,33 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         g.num_sms = d.num_sms;
         return launch_gemm(g, ks);
     };
+    // A projection fused with the residual step that follows it (x += rmsnorm(t) * w_post,
+    // then the next norm into h16 or y32): one launch instead of a GEMM and k_residual_norm,
+    // on request (GE_LOAD_FUSED_RESIDUAL).  Measured on B200 at 19.5k tokens it takes about
+    // as long as the pair it replaces: the A and B tiles each 128 x 256 tile reloads, plus the
+    // residual stream in and out, saturate the SM's L2 port.
+    const bool fused = (m->flags & GE_LOAD_FUSED_RESIDUAL) != 0;
+    auto gemm_residual = [&](const DevActivation& A, const DevWeight& W, const float* w_post, float scale,
+                             const float* w_next, __half* h16, float* y32) {
+        GemmLaunch g;
+        g.a = &A;
+        g.w = &W;
+        g.m_rows = rows;
+        g.out = nullptr;
+        g.ldo = W.N;
+        g.epilogue = EPI_RESIDUAL;
+        g.use_q8 = q8;
+        g.err = d.err;
+        g.num_sms = d.num_sms;
+        g.x = ws.x;
+        g.w_post = w_post;
+        g.scale = scale;
+        g.w_next = w_next;
+        g.eps = c.eps;
+        g.h16 = h16;
+        g.y32 = y32;
+        return launch_gemm(g, ks);
+    };
 #define CK(expr, what)                                  \
     do {                                                \
         cudaError_t e_ = (expr);                        \
@@ -914,22 +941,28 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
             const DevActivation* aa = nullptr;
             for (auto& x : ws.a_attn)
                 if (x.cols == qd) aa = &x;
-            CK(K("gemm_o", gemm_flops(L.o), gemm_bytes(L.o, 2), [&] { return gemm(*aa, L.o, ws.o16, D, EPI_F16); }),
-               "attention output");
-            CK(K("residual_norm", 0, double(ntok) * D * 12,
-                 [&] {
-                     return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_attn, 1.0f, L.ffn_norm, c.eps, ws.h, nullptr,
-                                                 nullptr, ks);
-                 }),
-               "post-attention residual");
+            if (fused) {
+                CK(K("gemm_o_residual", gemm_flops(L.o), gemm_bytes(L.o, 10),
+                     [&] { return gemm_residual(*aa, L.o, L.post_attn, 1.0f, L.ffn_norm, ws.h, nullptr); }),
+                   "attention output and residual");
+            } else {
+                CK(K("gemm_o", gemm_flops(L.o), gemm_bytes(L.o, 2), [&] { return gemm(*aa, L.o, ws.o16, D, EPI_F16); }),
+                   "attention output");
+                CK(K("residual_norm", 0, double(ntok) * D * 12,
+                     [&] {
+                         return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_attn, 1.0f, L.ffn_norm, c.eps, ws.h,
+                                                     nullptr, nullptr, ks);
+                     }),
+                   "post-attention residual");
+            }
             CK(K("gemm_gate_up", gemm_flops(L.gu), gemm_bytes(L.gu, 1), [&] { return gemm(ws.a_h, L.gu, ws.act, c.ff, EPI_GEGLU); }),
                "gate/up projection");
-            CK(K("gemm_down", gemm_flops(L.down), gemm_bytes(L.down, 2),
-                 [&] { return gemm(ws.a_act, L.down, ws.o16, D, EPI_F16); }),
-               "down projection");
             const bool last = l + 1 == c.layers;
             const float* next = last ? d.out_norm : d.layers[l + 1].attn_norm;
             if (c.has_ple) {
+                CK(K("gemm_down", gemm_flops(L.down), gemm_bytes(L.down, 2),
+                     [&] { return gemm(ws.a_act, L.down, ws.o16, D, EPI_F16); }),
+                   "down projection");
                 CK(K("residual_norm", 0, double(ntok) * D * 12,
                      [&] {
                          return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_ffw, 1.0f, nullptr, c.eps, nullptr, nullptr,
@@ -942,19 +975,39 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
                                      c.per_layer * c.layers);
                      }),
                    "per-layer gate");
-                CK(K("gemm_proj", gemm_flops(L.proj), gemm_bytes(L.proj, 2), [&] { return gemm(ws.a_g, L.proj, ws.o16, D, EPI_F16); }),
-                   "per-layer projection");
-                CK(K("residual_norm", 0, double(ntok) * D * 12,
+                if (fused) {
+                    CK(K("gemm_proj_residual", gemm_flops(L.proj), gemm_bytes(L.proj, last ? 12 : 10),
+                         [&] {
+                             return gemm_residual(ws.a_g, L.proj, L.post_norm, L.out_scale, next, last ? nullptr : ws.h,
+                                                  last ? ws.y : nullptr);
+                         }),
+                       "per-layer projection and residual");
+                } else {
+                    CK(K("gemm_proj", gemm_flops(L.proj), gemm_bytes(L.proj, 2),
+                         [&] { return gemm(ws.a_g, L.proj, ws.o16, D, EPI_F16); }),
+                       "per-layer projection");
+                    CK(K("residual_norm", 0, double(ntok) * D * 12,
+                         [&] {
+                             return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_norm, L.out_scale, next, c.eps,
+                                                         last ? nullptr : ws.h, last ? ws.y : nullptr, nullptr, ks);
+                         }),
+                       "per-layer residual");
+                }
+            } else if (fused) {
+                CK(K("gemm_down_residual", gemm_flops(L.down), gemm_bytes(L.down, last ? 12 : 10),
                      [&] {
-                         return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_norm, L.out_scale, next, c.eps,
-                                                     last ? nullptr : ws.h, last ? ws.y : nullptr, nullptr, ks);
+                         return gemm_residual(ws.a_act, L.down, L.post_ffw, 1.0f, next, last ? nullptr : ws.h,
+                                              last ? ws.y : nullptr);
                      }),
-                   "per-layer residual");
+                   "down projection and residual");
             } else {
+                CK(K("gemm_down", gemm_flops(L.down), gemm_bytes(L.down, 2),
+                     [&] { return gemm(ws.a_act, L.down, ws.o16, D, EPI_F16); }),
+                   "down projection");
                 CK(K("residual_norm", 0, double(ntok) * D * 12,
                      [&] {
-                         return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_ffw, 1.0f, next, c.eps, last ? nullptr : ws.h,
-                                                     last ? ws.y : nullptr, nullptr, ks);
+                         return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_ffw, 1.0f, next, c.eps,
+                                                     last ? nullptr : ws.h, last ? ws.y : nullptr, nullptr, ks);
                      }),
                    "post-ffn residual");
             }

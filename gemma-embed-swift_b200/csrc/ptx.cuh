@@ -127,6 +127,11 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
     return r;
 }
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+    return r;
+}
 // Every thread of every CTA of the cluster arrives and waits.
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -140,6 +145,14 @@ __device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
 // Arrive on an mbarrier given by its shared::cluster address (possibly another CTA's).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Asynchronous 4-byte store to shared::cluster address `addr` (this or another cluster CTA's
+// shared memory) that completes 4 transaction bytes on the mbarrier at `bar`, which lives in
+// the same CTA as `addr`.
+__device__ __forceinline__ void st_async_b32(uint32_t addr, uint32_t v, uint32_t bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr), "r"(v),
+                 "r"(bar)
+                 : "memory");
 }
 // TMA tile load by either CTA of a pair into its own shared memory, completing transaction
 // bytes on the mbarrier at shared::cluster address `bar` (the pair leader's).

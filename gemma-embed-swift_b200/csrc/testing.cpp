@@ -46,13 +46,8 @@ extern "C" {
 
 const char* ge_test_last_error(void) { return t_err.c_str(); }
 
-int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int32_t n, int32_t epilogue, int32_t use_q8,
-                 const float* aux, float* out) {
-    if (m <= 0 || k <= 0 || n <= 0 || k % 64 || n % 256 || !a || !w || !out || epilogue < 0 || epilogue > 3 ||
-        (epilogue == 3 && !aux))
-        return fail(GE_ERR_INVALID_OPTIONS, "invalid options: shapes must be k % 64 == 0 and n % 256 == 0");
-    const int rows = (m + ge::kRowTile - 1) / ge::kRowTile * ge::kRowTile;
-    // Host repack of the Q8_0 rows into the device planes the loader builds.
+// Host repack of Q8_0 rows [n][k/32 * 34 bytes] into the device planes the loader builds.
+static int upload_weight(const uint8_t* w, int n, int k, DevBuf& dq, DevBuf& ds, DevBuf& dh, ge::DevWeight& W) {
     std::vector<int8_t> q(size_t(n) * k);
     std::vector<uint16_t> st(size_t(n) * (k / 32)), f16(size_t(n) * k);
     for (int r = 0; r < n; r++)
@@ -67,21 +62,49 @@ int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int3
                 f16[size_t(r) * k + b * 32 + j] = f2h(h2f(s) * float(v));
             }
         }
-    int dev = 0, sms = 0;
-    TRY(cudaGetDevice(&dev));
-    TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    DevBuf da, dq, ds, dh, dout, daux, derr;
-    const int out_cols = epilogue == 2 ? n / 2 : n;
-    const size_t out_elem = epilogue == 0 ? 4 : 2;
-    TRY(da.alloc(size_t(rows) * k * 2));
-    TRY(cudaMemset(da.p, 0, size_t(rows) * k * 2));
-    TRY(cudaMemcpy(da.p, a, size_t(m) * k * 2, cudaMemcpyHostToDevice));
     TRY(dq.alloc(q.size()));
     TRY(cudaMemcpy(dq.p, q.data(), q.size(), cudaMemcpyHostToDevice));
     TRY(ds.alloc(st.size() * 2));
     TRY(cudaMemcpy(ds.p, st.data(), st.size() * 2, cudaMemcpyHostToDevice));
     TRY(dh.alloc(f16.size() * 2));
     TRY(cudaMemcpy(dh.p, f16.data(), f16.size() * 2, cudaMemcpyHostToDevice));
+    W.N = n;
+    W.K = k;
+    W.q8 = static_cast<int8_t*>(dq.p);
+    W.scales_t = static_cast<__half*>(ds.p);
+    W.f16 = static_cast<__half*>(dh.p);
+    if (!ge::encode_weight_maps(W, 256)) return fail(GE_ERR_GPU_FAILURE, "tensor map encoding failed");
+    return GE_OK;
+}
+
+static int upload_activation(const uint16_t* a, int m, int k, int rows, DevBuf& da, ge::DevActivation& A) {
+    TRY(da.alloc(size_t(rows) * k * 2));
+    TRY(cudaMemset(da.p, 0, size_t(rows) * k * 2));
+    TRY(cudaMemcpy(da.p, a, size_t(m) * k * 2, cudaMemcpyHostToDevice));
+    A.ptr = static_cast<__half*>(da.p);
+    A.rows = rows;
+    A.cols = k;
+    if (!ge::encode_activation_map(A)) return fail(GE_ERR_GPU_FAILURE, "tensor map encoding failed");
+    return GE_OK;
+}
+
+int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int32_t n, int32_t epilogue, int32_t use_q8,
+                 const float* aux, float* out) {
+    if (m <= 0 || k <= 0 || n <= 0 || k % 64 || n % 256 || !a || !w || !out || epilogue < 0 || epilogue > 3 ||
+        (epilogue == 3 && !aux))
+        return fail(GE_ERR_INVALID_OPTIONS, "invalid options: shapes must be k % 64 == 0 and n % 256 == 0");
+    const int rows = (m + ge::kRowTile - 1) / ge::kRowTile * ge::kRowTile;
+    int dev = 0, sms = 0;
+    TRY(cudaGetDevice(&dev));
+    TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    DevBuf da, dq, ds, dh, dout, daux, derr;
+    ge::DevWeight W;
+    ge::DevActivation A;
+    int rc = upload_weight(w, n, k, dq, ds, dh, W);
+    if (rc != GE_OK) return rc;
+    if ((rc = upload_activation(a, m, k, rows, da, A)) != GE_OK) return rc;
+    const int out_cols = epilogue == 2 ? n / 2 : n;
+    const size_t out_elem = epilogue == 0 ? 4 : 2;
     TRY(dout.alloc(size_t(rows) * out_cols * out_elem));
     TRY(derr.alloc(sizeof(int)));
     TRY(cudaMemset(derr.p, 0, sizeof(int)));
@@ -90,18 +113,6 @@ int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int3
         TRY(cudaMemset(daux.p, 0, size_t(rows) * n * 4));
         TRY(cudaMemcpy(daux.p, aux, size_t(m) * n * 4, cudaMemcpyHostToDevice));
     }
-    ge::DevWeight W;
-    W.N = n;
-    W.K = k;
-    W.q8 = static_cast<int8_t*>(dq.p);
-    W.scales_t = static_cast<__half*>(ds.p);
-    W.f16 = static_cast<__half*>(dh.p);
-    ge::DevActivation A;
-    A.ptr = static_cast<__half*>(da.p);
-    A.rows = rows;
-    A.cols = k;
-    if (!ge::encode_weight_maps(W, 256) || !ge::encode_activation_map(A))
-        return fail(GE_ERR_GPU_FAILURE, "tensor map encoding failed");
     TRY(ge::configure_gemm_kernels());
     ge::GemmLaunch g;
     g.a = &A;
@@ -128,6 +139,71 @@ int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int3
         TRY(cudaMemcpy(h.data(), dout.p, h.size() * 2, cudaMemcpyDeviceToHost));
         for (size_t i = 0; i < h.size(); i++) out[i] = h2f(h[i]);
     }
+    return GE_OK;
+}
+
+int ge_test_gemm_residual(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int32_t n, int32_t path, float* x,
+                          const float* w_post, float scale, const float* w_next, float eps, float* h_out, float* y_out) {
+    if (m <= 0 || k <= 0 || n <= 0 || k % 64 || n % 256 || n > 1024 || !a || !w || !x || !w_post || path < 0 ||
+        path > 1)
+        return fail(GE_ERR_INVALID_OPTIONS, "invalid options: k % 64 == 0, n a multiple of 256 up to 1024");
+    const int rows = (m + ge::kRowTile - 1) / ge::kRowTile * ge::kRowTile;
+    int dev = 0, sms = 0;
+    TRY(cudaGetDevice(&dev));
+    TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    DevBuf da, dq, ds, dh, dx, dwp, dwn, dh16, dy, derr;
+    ge::DevWeight W;
+    ge::DevActivation A;
+    int rc = upload_weight(w, n, k, dq, ds, dh, W);
+    if (rc != GE_OK) return rc;
+    if ((rc = upload_activation(a, m, k, rows, da, A)) != GE_OK) return rc;
+    const size_t xe = size_t(rows) * n;
+    TRY(dx.alloc(xe * 4));
+    TRY(cudaMemset(dx.p, 0, xe * 4));
+    TRY(cudaMemcpy(dx.p, x, size_t(m) * n * 4, cudaMemcpyHostToDevice));
+    TRY(dwp.alloc(size_t(n) * 4));
+    TRY(cudaMemcpy(dwp.p, w_post, size_t(n) * 4, cudaMemcpyHostToDevice));
+    if (w_next) {
+        TRY(dwn.alloc(size_t(n) * 4));
+        TRY(cudaMemcpy(dwn.p, w_next, size_t(n) * 4, cudaMemcpyHostToDevice));
+    }
+    TRY(dh16.alloc(xe * 2));
+    TRY(cudaMemset(dh16.p, 0xFF, xe * 2));
+    TRY(dy.alloc(xe * 4));
+    TRY(cudaMemset(dy.p, 0xFF, xe * 4));
+    TRY(derr.alloc(sizeof(int)));
+    TRY(cudaMemset(derr.p, 0, sizeof(int)));
+    TRY(ge::configure_gemm_kernels());
+    ge::GemmLaunch g;
+    g.a = &A;
+    g.w = &W;
+    g.m_rows = rows;
+    g.out = nullptr;
+    g.ldo = n;
+    g.epilogue = ge::EPI_RESIDUAL;
+    g.use_q8 = path == 1;
+    g.mode = ge::GEMM_SINGLE;
+    g.err = static_cast<int*>(derr.p);
+    g.num_sms = sms;
+    g.x = static_cast<float*>(dx.p);
+    g.w_post = static_cast<const float*>(dwp.p);
+    g.scale = scale;
+    g.w_next = w_next ? static_cast<const float*>(dwn.p) : nullptr;
+    g.eps = eps;
+    g.h16 = h_out ? static_cast<__half*>(dh16.p) : nullptr;
+    g.y32 = y_out ? static_cast<float*>(dy.p) : nullptr;
+    TRY(ge::launch_gemm(g, nullptr));
+    TRY(cudaDeviceSynchronize());
+    int herr = 0;
+    TRY(cudaMemcpy(&herr, derr.p, sizeof(int), cudaMemcpyDeviceToHost));
+    if (herr) return fail(herr, "GPU execution failed: a device-side wait timed out");
+    TRY(cudaMemcpy(x, dx.p, size_t(m) * n * 4, cudaMemcpyDeviceToHost));
+    if (h_out) {
+        std::vector<uint16_t> h(size_t(m) * n);
+        TRY(cudaMemcpy(h.data(), dh16.p, h.size() * 2, cudaMemcpyDeviceToHost));
+        for (size_t i = 0; i < h.size(); i++) h_out[i] = h2f(h[i]);
+    }
+    if (y_out) TRY(cudaMemcpy(y_out, dy.p, size_t(m) * n * 4, cudaMemcpyDeviceToHost));
     return GE_OK;
 }
 

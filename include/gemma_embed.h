@@ -60,6 +60,8 @@ typedef struct ge_load_opts {
 #define GE_LOAD_Q8_ONLY 2u        /* keep only the Q8_0 planes resident; every GEMM dequantises in shared memory */
 #define GE_LOAD_NO_PDL 4u         /* launch each kernel only after its predecessor completed (no programmatic
                                      dependent launch); results are bit-identical either way */
+#define GE_LOAD_FUSED_RESIDUAL 8u /* fuse each residual step into the projection before it (row clusters of
+                                     hidden/256 CTAs exchanging row sums through distributed shared memory) */
 
 /* EmbedOptions (EmbedOptions.swift:34-56) minus the task prefix, which the tokenizer applies. */
 typedef struct ge_embed_opts {

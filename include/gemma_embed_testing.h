@@ -26,6 +26,15 @@ extern "C" {
 GE_API int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w_q8_0, int32_t n, int32_t epilogue,
                         int32_t path, const float* aux, float* out);
 
+/* The attention-output / down projection fused with the residual step (CPUReference.swift:
+ * 239-243 and 252-256, Elementwise.metal:260-354): t = fp16(a * W^T); x = (x + rmsnorm(t) *
+ * w_post) * scale in place on x [m][n] fp32; then, when w_next is given, y = rmsnorm(x) *
+ * w_next returned as fp16 values in h_out and/or fp32 in y_out (either may be NULL).  n is
+ * the hidden size, a multiple of 256 up to 1024.  path: 0 fp16-resident weights, 1 Q8. */
+GE_API int ge_test_gemm_residual(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w_q8_0, int32_t n,
+                                 int32_t path, float* x, const float* w_post, float scale, const float* w_next,
+                                 float eps, float* h_out, float* y_out);
+
 /* Kernels.attention (Metal/MetalForward.swift:669-694): q [ntok][heads][hd], k and v
  * [ntok][kv_heads][hd] as fp16 bit patterns, sequences tiling [0, ntok); out receives fp16
  * bit patterns [ntok][heads][hd].  half_window 0 is global attention. */

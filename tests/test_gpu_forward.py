@@ -148,3 +148,24 @@ def test_launch_options_do_not_change_results(ge, synth, cuda_device, arch, use_
         for seed, lens in ((51, [37, 300, 5, 129]), (52, [700, 1, 64]), (51, [37, 300, 5, 129])):
             seqs = synth.random_sequences(lens, seed=seed, vocab=4096)
             assert on.embed_tokens(seqs).tobytes() == off.embed_tokens(seqs).tobytes()
+
+
+@pytest.mark.parametrize("arch", ["gemma-embedding", "gemma-embedding2"])
+def test_fused_residual_forward(ge, synth, oracle, cuda_device, arch):
+    """The residual steps fused into their projections (row clusters, GE_LOAD_FUSED_RESIDUAL):
+    oracle parity at the same cosine bar and bit-identical vectors across batch compositions
+    (small batches take the Q8 path, large ones fp16 weights)."""
+    path = synth.model_path(arch, seed=1, layers=6, vocab=4096)
+    ref = oracle.OracleModel(path)
+    with ge.EmbeddingModel.load(path, ge.LoadOptions(fused_residual=True)) as model:
+        seqs = synth.random_sequences([1, 64, 300, 700], seed=71, vocab=4096)
+        got = model.embed_tokens(seqs)
+        for s, g in zip(seqs, got):
+            c = cosine(g, ref.forward(s))
+            assert c >= COSINE_MIN, (arch, len(s), c)
+        pool = synth.random_sequences([400, 250, 333], seed=72, vocab=4096)
+        subject = synth.random_sequences([150], seed=73, vocab=4096)[0]
+        alone = model.embed_tokens([subject])[0]
+        packed = model.embed_tokens(pool + [subject])[-1]
+        assert alone.tobytes() == packed.tobytes()
+    ref.close()

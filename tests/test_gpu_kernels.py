@@ -158,3 +158,67 @@ def test_attention_packed_sequences(ge, oracle, cuda_device, heads, kvh, hd, hw,
         assert not np.isnan(g).any()
         assert max_rel(g, want) < TOL_F16, (n, heads, kvh, hd, hw)
         s += n
+
+
+def gemm_residual(ge, a16, wq, n, path, x, w_post, scale, w_next, eps, want_h=True, want_y=True):
+    from importlib import import_module
+    L = import_module("gemma-embed-swift_b200._lib").lib()
+    m, k = a16.shape
+    fp = ctypes.POINTER(ctypes.c_float)
+    a = np.ascontiguousarray(a16.view(np.uint16))
+    w = np.ascontiguousarray(wq)
+    x = np.array(x, np.float32, copy=True)
+    w_post = np.ascontiguousarray(w_post, np.float32)
+    wn = None if w_next is None else np.ascontiguousarray(w_next, np.float32)
+    h = np.zeros((m, n), np.float32) if want_h else None
+    y = np.zeros((m, n), np.float32) if want_y else None
+    rc = L.ge_test_gemm_residual(a.ctypes.data_as(ctypes.POINTER(ctypes.c_uint16)), m, k,
+                                 w.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), n, path,
+                                 x.ctypes.data_as(fp), w_post.ctypes.data_as(fp), scale,
+                                 None if wn is None else wn.ctypes.data_as(fp), eps,
+                                 None if h is None else h.ctypes.data_as(fp),
+                                 None if y is None else y.ctypes.data_as(fp))
+    assert rc == 0, L.ge_test_last_error()
+    return x, h, y
+
+
+def residual_reference(t16, x, w_post, scale, w_next, eps):
+    """k_residual_norm in float64 on the fp16-rounded projection (CPUReference.swift:239-243)."""
+    t = t16.astype(np.float64)
+    inv = 1.0 / np.sqrt((t * t).mean(axis=1, keepdims=True) + eps)
+    v = (x.astype(np.float64) + t * inv * w_post) * scale
+    y = None
+    if w_next is not None:
+        inv2 = 1.0 / np.sqrt((v * v).mean(axis=1, keepdims=True) + eps)
+        y = v * inv2 * w_next
+    return v, y
+
+
+@pytest.mark.parametrize("k,n,scale", [(768, 768, 1.0), (1152, 768, 1.0), (512, 512, 1.0), (2048, 512, 0.7)])
+def test_gemm_residual_epilogue(ge, synth, cuda_device, k, n, scale):
+    """The projection fused with the residual step and the next norm, on row clusters of n / 256
+    CTAs: the residual stream to 1e-5, the next norm's fp32 output to 1e-5 and fp16 output to
+    one fp16 rounding, against float64 on the fp16 projection the unfused path stores; fp16
+    and Q8 weights bit for bit."""
+    m = 700
+    a, wq, _ = make_case(synth, m, k, n, seed=31)
+    rng = np.random.default_rng(32)
+    x = rng.normal(scale=3.0, size=(m, n)).astype(np.float32)
+    w_post = rng.uniform(0.5, 1.5, size=n).astype(np.float32)
+    w_next = rng.uniform(0.5, 1.5, size=n).astype(np.float32)
+    t16 = gemm(ge, a, wq, n, 1, False)  # the fp16 projection
+    want_x, want_y = residual_reference(t16, x, w_post, scale, w_next, 1e-6)
+    got_x, got_h, got_y = gemm_residual(ge, a, wq, n, 0, x, w_post, scale, w_next, 1e-6)
+    assert max_rel(got_x, want_x) < 1e-5
+    assert max_rel(got_y, want_y) < 1e-5
+    assert max_rel(got_h, want_y) < TOL_F16
+    assert np.array_equal(got_h, got_y.astype(np.float16).astype(np.float32))
+    qx, qh, qy = gemm_residual(ge, a, wq, n, 1, x, w_post, scale, w_next, 1e-6)
+    assert qx.tobytes() == got_x.tobytes() and qh.tobytes() == got_h.tobytes() and qy.tobytes() == got_y.tobytes()
+    # without the next norm only the residual stream changes
+    nx, _, _ = gemm_residual(ge, a, wq, n, 0, x, w_post, scale, None, 1e-6, want_h=False, want_y=False)
+    assert nx.tobytes() == got_x.tobytes()
+    # rows do not depend on the batch around them
+    sx, sh, _ = gemm_residual(ge, np.ascontiguousarray(a[130:131]), wq, n, 0, x[130:131], w_post, scale, w_next, 1e-6,
+                              want_y=False)
+    assert sx.tobytes() == got_x[130:131].tobytes() and sh.tobytes() == got_h[130:131].tobytes()
