@@ -266,8 +266,11 @@ def main():
             ach, peak, unit = tf, pk["bf16_tflops"], "TFLOP/s"
         else:
             ach, peak, unit = gbs, pk["hbm_gbs"], "GB/s"
+        traffic = NCU_DRAM_BYTES_CONFIG2.get(top["name"]) if a.config == 2 and a.arch == "gemma-embedding" else None
         roofline = {"kernel": top["name"], "bound": "tensor" if tensor else "hbm", "achieved": ach, "peak": peak,
-                    "unit": unit, "frac": ach / peak, "traffic": None, "peak_source": pk["source"],
+                    "unit": unit, "frac": ach / peak, "traffic": traffic,
+                    "traffic_source": "profiles/layer_config2_ncu_full.md" if traffic else None,
+                    "peak_source": pk["source"],
                     "share_of_forward": top["ms_per_launch"] * top["launches_per_forward"] / fwd_ms,
                     "launches_per_forward": top["launches_per_forward"]}
 
@@ -294,6 +297,15 @@ def main():
     if dist is not None:
         dist.destroy_process_group()
     return 0
+
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of each kernel class, from the
+# one-layer `ncu --set full` capture at config 2 summarised in profiles/layer_config2_ncu_full.md
+# (cold caches: reads include operands a normal run finds in L2).
+NCU_DRAM_BYTES_CONFIG2 = {
+    "gemm_qkv": 36.31e6, "qkv_norm_rope": 59.16e6, "attention_sliding": 53.08e6, "gemm_o": 31.62e6,
+    "residual_norm": 123.39e6, "gemm_gate_up": 36.70e6, "gemm_down": 49.47e6,
+}
 
 
 def model_info(model):
