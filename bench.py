@@ -238,16 +238,19 @@ def main():
         model.forward_packed(tokens, positions, ranges)
     barrier()
     torch.cuda.synchronize()
+    info0 = model_info(model)
     t0 = time.perf_counter()
     for _ in range(a.steps):
         out = model.forward_packed(tokens, positions, ranges)
     t1 = time.perf_counter()
     barrier()
+    info1 = model_info(model)
     e2e_ms, _ = reduce_max_sum(dist, (t1 - t0) * 1000.0, 0)
     e2e = tok_sum / (e2e_ms / 1000.0)
-    nwork = sum((n + 31) // 32 for _, n in ranges)
-    h2d = ntok * 4 * 2 + nseq * 8 + nwork * 12
-    d2h = nseq * od * 4 + 4
+    # bytes the library copied per step (ids, positions, sequence ranges, attention schedule up;
+    # status word and pooled vectors down), counted by the library itself
+    h2d = (info1.host_to_device_bytes - info0.host_to_device_bytes) // a.steps
+    d2h = (info1.device_to_host_bytes - info0.device_to_host_bytes) // a.steps
 
     # ---- per-kernel roofline (rank 0): the kernel class with the largest share of a forward
     pk = peaks()

@@ -35,7 +35,8 @@ class GeInfo(ctypes.Structure):
                                       "max_tokens")] + [
         ("norm_epsilon", ctypes.c_float), ("quantization", ctypes.c_char * 16), ("file_size", ctypes.c_int64),
         ("device_count", ctypes.c_int32), ("eos_id", ctypes.c_int32), ("bos_id", ctypes.c_int32),
-        ("device_name", ctypes.c_char * 128), ("kernel_launches", ctypes.c_int64)]
+        ("device_name", ctypes.c_char * 128), ("kernel_launches", ctypes.c_int64),
+        ("host_to_device_bytes", ctypes.c_int64), ("device_to_host_bytes", ctypes.c_int64)]
 
 
 class GeKernelTime(ctypes.Structure):

@@ -224,6 +224,8 @@ int ge_info_get(const ge_model* m, ge_info* info) {
     info->bos_id = c.bos_id;
     if (!m->devs.empty()) snprintf(info->device_name, sizeof info->device_name, "%s", m->devs[0].name.c_str());
     info->kernel_launches = m->launches.load();
+    info->host_to_device_bytes = m->h2d_bytes.load();
+    info->device_to_host_bytes = m->d2h_bytes.load();
     return GE_OK;
 }
 

@@ -10,6 +10,9 @@
 // `queries_per_item` queries of a sequence (AttentionWork, MetalForward.swift:45-58); a
 // block's key range is clipped to the window once for the whole block
 // (Attention.metal:66-74), so its result depends only on its own sequence.
+#include <algorithm>
+#include <vector>
+
 #include "kernels.hpp"
 #include "ptx.cuh"
 
@@ -119,17 +122,25 @@ __global__ void __launch_bounds__(256) k_attention_simt(const __half* __restrict
 }
 
 // ---------------------------------------------------------------------------------------
-// Tensor-core kernel (head dim 256): one CTA per (work item of 128 queries, query head).
-//   warp 0      TMA producer: the Q tile once, then K and V tiles of 64 keys into 2-slot rings
+// Tensor-core kernel (head dim 256), persistent: CTA c walks its own range of work items,
+// assigned on the host longest-processing-time first by key blocks.  An item is T = 128 / G tokens of one sequence
+// with the G query heads that share one KV head (G = H / KV): row t * G + g of its Q tile is
+// token t0 + t, head kh * G + g (one 3-D TMA box per 64 dims), so each K and V tile serves
+// all G heads and a short sequence fills its tile with heads instead of padding.
+//   warp 0      TMA producer: per item the Q tile, once the previous item's last S has read
+//               the buffer, then K and V tiles of 64 keys into 2-slot rings that run on from
+//               item to item
 //   warp 1      tcgen05.mma issuer and tensor-memory owner: S_j = Q K_j^T (128 x 64, fp32 in
-//               TMEM, two buffers) and O += P_j V_j (128 x 256, fp32 in TMEM)
-//   warps 2-9   softmax, two threads per query row (one per 32-key half of a block; warps w
-//               and w + 4 share a tensor-memory lane quarter): mask S_j, exchange the row's
-//               block maximum through shared memory, keep running maximum and partial sums,
-//               write their half of P_j (fp16, 128-byte swizzled) to shared memory, and rescale
+//               TMEM, two buffers) and O += P_j V_j (128 x 256, fp32 in TMEM); an item's
+//               first PV waits until the previous item's O has been read out, so the next
+//               item's Q load and first S overlap the previous item's epilogue
+//   warps 2-9   softmax, two threads per row (one per 32-key half of a block; warps w and
+//               w + 4 share a tensor-memory lane quarter): mask S_j, exchange the row's block
+//               maximum through shared memory, keep running maximum and partial sums, write
+//               their half of P_j (fp16, 128-byte swizzled) to shared memory, and rescale
 //               their half of O in tensor memory only when the row maximum grows by more than
 //               kRescale; until then every term of the row uses the same stale maximum, so the
-//               result is exact
+//               result is exact.  Then O / l for their half of the row.
 // Tensor memory: O in columns [0, 256), the S buffers in [256, 320) and [320, 384).
 constexpr int kTcQ = 128;
 constexpr int kTcKeys = 64;
@@ -144,14 +155,15 @@ constexpr int kOffV = kOffK + 2 * kKVBytes;
 constexpr int kOffP = kOffV + 2 * kKVBytes;
 constexpr int kOffRed = kOffP + 2 * kPBytes;    // [2 halves][128 rows] floats: row maxima, then sums
 constexpr int kOffBar = kOffRed + 2 * kTcQ * 4;
-constexpr int kTcSmem = kOffBar + 128 + 1024;
+constexpr int kTcSmem = kOffBar + 256 + 1024;
 constexpr int kTcThreads = 320;
 constexpr uint32_t kTmemO = 0, kTmemS = 256;
 
 struct TcAttnParams {
-    const uint32_t* work;
+    const uint4* work;       // (sequence start, sequence length, first token, KV head), grouped by CTA
+    const uint32_t* offset;  // CTA c's items are [offset[c], offset[c + 1])
     __half* out;
-    int heads, kvh, hw;
+    int heads, group, tokens, hw;  // G = heads / KV heads, T = tokens per item = 128 / G
     int* err;
 };
 
@@ -161,6 +173,19 @@ __device__ __forceinline__ void drain(uint64_t* bar, uint32_t parity) {
     }
 }
 
+// Key blocks of an item: the whole sequence, or the window of all its tokens
+// (Attention.metal:66-74), starting on a multiple of kTcKeys from the sequence start.
+__device__ __forceinline__ void item_keys(const uint4& w, const TcAttnParams& p, int& k_start, int& nblk) {
+    const int len = int(w.y), t0 = int(w.z);
+    int ks = 0, ke = len;
+    if (p.hw > 0) {
+        ks = max(t0 - p.hw, 0);
+        ke = min(t0 + p.tokens - 1 + p.hw + 1, len);
+    }
+    k_start = ks / kTcKeys * kTcKeys;
+    nblk = (ke - k_start + kTcKeys - 1) / kTcKeys;
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_constant__ CUtensorMap mapQ,
                                                           const __grid_constant__ CUtensorMap mapK,
                                                           const __grid_constant__ CUtensorMap mapV, TcAttnParams p) {
@@ -168,32 +193,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
     uint64_t* q_full = bars;
-    uint64_t* k_full = bars + 1;
-    uint64_t* k_empty = bars + 3;
-    uint64_t* v_full = bars + 5;
-    uint64_t* v_empty = bars + 7;
-    uint64_t* s_full = bars + 9;
-    uint64_t* p_full = bars + 11;
-    uint64_t* pv_done = bars + 13;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+    uint64_t* q_empty = bars + 1;
+    uint64_t* k_full = bars + 2;
+    uint64_t* k_empty = bars + 4;
+    uint64_t* v_full = bars + 6;
+    uint64_t* v_empty = bars + 8;
+    uint64_t* s_full = bars + 10;
+    uint64_t* p_full = bars + 12;
+    uint64_t* pv_done = bars + 14;
+    uint64_t* o_empty = bars + 16;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
 
-    const uint32_t seq_start = p.work[3 * blockIdx.x], len = p.work[3 * blockIdx.x + 1], q0 = p.work[3 * blockIdx.x + 2];
-    const int h = blockIdx.y;
-    const int kh = h / (p.heads / p.kvh);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-    // Key blocks: the whole sequence, or the window of the whole query block
-    // (Attention.metal:66-74), starting on a multiple of kTcKeys from the sequence start.
-    int k_start = 0, k_end = int(len);
-    if (p.hw > 0) {
-        k_start = max(int(q0) - p.hw, 0);
-        k_end = min(int(q0) + kTcQ - 1 + p.hw + 1, int(len));
-    }
-    k_start = k_start / kTcKeys * kTcKeys;
-    const int nblk = (k_end - k_start + kTcKeys - 1) / kTcKeys;
+    const int live_rows = p.group * p.tokens;
+    const uint32_t q_bytes = uint32_t(4 * 128 * live_rows);  // 4 boxes of live_rows x 128 bytes
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
         for (int i = 0; i < 2; i++) {
             mbar_init(&k_full[i], 1);
             mbar_init(&k_empty[i], 1);
@@ -203,6 +220,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
             mbar_init(&p_full[i], 256);
             mbar_init(&pv_done[i], 1);
         }
+        mbar_init(o_empty, 256);
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
@@ -224,28 +242,44 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
         // ---------------------------------------------------------- TMA producer
         if (lane == 0) {
             bool ok = true;
-            int issued_k = 0, issued_v = 0;
-            mbar_expect_tx(q_full, kQBytes);
-            for (int c = 0; c < 4; c++)
-                tma_load_2d(smem + c * (kQBytes / 4), &mapQ, q_full, h * kTcHd + c * 64, int(seq_start + q0));
-            for (int j = 0; j < nblk && ok; j++) {
-                const int b = j & 1;
-                const uint32_t ph = uint32_t((j >> 1) & 1);
-                const int row = int(seq_start) + k_start + j * kTcKeys;
-                if (!mbar_wait(&k_empty[b], ph ^ 1, p.err)) break;
-                mbar_expect_tx(&k_full[b], kKVBytes);
+            int gb = 0, issued_q = 0, issued_k = 0, issued_v = 0;
+            for (int it = int(p.offset[blockIdx.x]), li = 0; it < int(p.offset[blockIdx.x + 1]) && ok; it++, li++) {
+                const uint4 w = p.work[it];
+                int k_start, nblk;
+                item_keys(w, p, k_start, nblk);
+                const int kh = int(w.w);
+                if (!mbar_wait(q_empty, uint32_t(li & 1) ^ 1u, p.err)) break;
+                mbar_expect_tx(q_full, q_bytes);
                 for (int c = 0; c < 4; c++)
-                    tma_load_2d(smem + kOffK + b * kKVBytes + c * (kKVBytes / 4), &mapK, &k_full[b], kh * kTcHd + c * 64, row);
-                issued_k++;
-                if (!mbar_wait(&v_empty[b], ph ^ 1, p.err)) break;
-                mbar_expect_tx(&v_full[b], kKVBytes);
-                for (int c = 0; c < 4; c++)
-                    tma_load_2d(smem + kOffV + b * kKVBytes + c * (kKVBytes / 4), &mapV, &v_full[b], kh * kTcHd + c * 64, row);
-                issued_v++;
+                    tma_load_3d(smem + c * (kQBytes / 4), &mapQ, q_full, c * 64, kh * p.group, int(w.x + w.z));
+                issued_q++;
+                for (int j = 0; j < nblk; j++, gb++) {
+                    const int b = gb & 1;
+                    const uint32_t ph = uint32_t((gb >> 1) & 1);
+                    const int row = int(w.x) + k_start + j * kTcKeys;
+                    if (!mbar_wait(&k_empty[b], ph ^ 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&k_full[b], kKVBytes);
+                    for (int c = 0; c < 4; c++)
+                        tma_load_2d(smem + kOffK + b * kKVBytes + c * (kKVBytes / 4), &mapK, &k_full[b],
+                                    kh * kTcHd + c * 64, row);
+                    issued_k++;
+                    if (!mbar_wait(&v_empty[b], ph ^ 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&v_full[b], kKVBytes);
+                    for (int c = 0; c < 4; c++)
+                        tma_load_2d(smem + kOffV + b * kKVBytes + c * (kKVBytes / 4), &mapV, &v_full[b],
+                                    kh * kTcHd + c * 64, row);
+                    issued_v++;
+                }
             }
             pdl_launch();  // this CTA's loads are all issued: the next kernel may be scheduled
             // Every issued load lands before the CTA exits, also after an error.
-            drain(q_full, 0);
+            if (issued_q > 0) drain(q_full, uint32_t((issued_q - 1) & 1));
             for (int b = 0; b < 2; b++) {
                 const int ck = issued_k / 2 + (b < issued_k % 2 ? 1 : 0);
                 const int cv = issued_v / 2 + (b < issued_v % 2 ? 1 : 0);
@@ -259,10 +293,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
             const uint32_t id_s = idesc_f16(kTcQ, kTcKeys);            // K-major Q and K
             const uint32_t id_o = idesc_f16(kTcQ, kTcHd, 0, 1);        // K-major P, MN-major V
             const uint32_t q_addr = smem_u32(smem);
-            bool ok = mbar_wait(q_full, 0, p.err);
-            auto issue_pv = [&](int j) -> bool {
-                const int b = j & 1;
-                const uint32_t ph = uint32_t((j >> 1) & 1);
+            bool ok = true;
+            // PV of global block g; the first block of item li overwrites O once the previous
+            // item's O has been read out.
+            auto issue_pv = [&](int g, bool first, int li) -> bool {
+                const int b = g & 1;
+                const uint32_t ph = uint32_t((g >> 1) & 1);
+                if (first && li > 0 && !mbar_wait(o_empty, uint32_t((li - 1) & 1), p.err)) return false;
                 if (!mbar_wait(&p_full[b], ph, p.err) || !mbar_wait(&v_full[b], ph, p.err)) return false;
                 tc_fence_after();
                 const uint32_t pa = smem_u32(smem + kOffP + b * kPBytes);
@@ -272,49 +309,57 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                     const uint64_t ad = sw128_desc(pa + kk * 32, 16, 1024);
                     // V chunk of 64 dims = one [64 keys][128 B] box; 16 keys advance 2048 B.
                     const uint64_t bd = sw128_desc(va + kk * 2048, kKVBytes / 4, 1024);
-                    umma_f16(tmem + kTmemO, ad, bd, id_o, (j | kk) != 0);
+                    umma_f16(tmem + kTmemO, ad, bd, id_o, !(first && kk == 0));
                 }
                 umma_commit(&v_empty[b]);
                 umma_commit(&pv_done[b]);
                 return true;
             };
-            for (int j = 0; j < nblk && ok; j++) {
-                const int b = j & 1;
-                const uint32_t ph = uint32_t((j >> 1) & 1);
-                if (!mbar_wait(&k_full[b], ph, p.err)) {
-                    ok = false;
-                    break;
-                }
+            int gb = 0;
+            for (int it = int(p.offset[blockIdx.x]), li = 0; it < int(p.offset[blockIdx.x + 1]) && ok; it++, li++) {
+                const uint4 w = p.work[it];
+                int k_start, nblk;
+                item_keys(w, p, k_start, nblk);
+                if (!mbar_wait(q_full, uint32_t(li & 1), p.err)) break;
                 tc_fence_after();
-                const uint32_t ka = smem_u32(smem + kOffK + b * kKVBytes);
+                for (int j = 0; j < nblk; j++, gb++) {
+                    const int b = gb & 1;
+                    const uint32_t ph = uint32_t((gb >> 1) & 1);
+                    if (!mbar_wait(&k_full[b], ph, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t ka = smem_u32(smem + kOffK + b * kKVBytes);
 #pragma unroll
-                for (int kk = 0; kk < kTcHd / 16; kk++) {
-                    const int c = kk >> 2, w = kk & 3;  // 64-dim chunk, 16-dim step inside it
-                    const uint64_t ad = sw128_desc(q_addr + c * (kQBytes / 4) + w * 32, 16, 1024);
-                    const uint64_t bd = sw128_desc(ka + c * (kKVBytes / 4) + w * 32, 16, 1024);
-                    umma_f16(tmem + kTmemS + b * kTcKeys, ad, bd, id_s, kk != 0);
+                    for (int kk = 0; kk < kTcHd / 16; kk++) {
+                        const int c = kk >> 2, wq = kk & 3;  // 64-dim chunk, 16-dim step inside it
+                        const uint64_t ad = sw128_desc(q_addr + c * (kQBytes / 4) + wq * 32, 16, 1024);
+                        const uint64_t bd = sw128_desc(ka + c * (kKVBytes / 4) + wq * 32, 16, 1024);
+                        umma_f16(tmem + kTmemS + b * kTcKeys, ad, bd, id_s, kk != 0);
+                    }
+                    umma_commit(&k_empty[b]);
+                    umma_commit(&s_full[b]);
+                    if (j == nblk - 1) umma_commit(q_empty);  // every S of the item has read Q
+                    if (j > 0 && !issue_pv(gb - 1, j == 1, li)) {
+                        ok = false;
+                        break;
+                    }
                 }
-                umma_commit(&k_empty[b]);
-                umma_commit(&s_full[b]);
-                if (j > 0 && !issue_pv(j - 1)) ok = false;
+                if (ok && !issue_pv(gb - 1, nblk == 1, li)) ok = false;
             }
-            if (ok && nblk > 0) issue_pv(nblk - 1);
         }
     } else {
         // ---------------------------------------------------------- softmax (two threads per row)
         const int quad = warp & 3;         // tensor-memory lane quarter of this warp
         const int half = (warp - 2) >> 2;  // which 32 keys of each block, and which 128 O columns
         const int r = quad * 32 + lane;
-        const int qi = int(q0) + r;
+        const int rt = r / p.group, rg = r - rt * p.group;  // token and head of this row in a tile
         const uint32_t lane_base = tmem + (uint32_t(quad * 32) << 16);
         float* red = reinterpret_cast<float*>(smem + kOffRed);
         // The two warps of a quarter meet on named barrier 1 + quad (64 threads).
         auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory"); };
-        // Keys this row sees: [row_lo, row_hi) of its sequence.
-        const int row_lo = p.hw > 0 ? max(qi - p.hw, 0) : 0;
-        const int row_hi = p.hw > 0 ? min(qi + p.hw + 1, int(len)) : int(len);
-        float m_used = -INFINITY, l = 0.f;  // running maximum (log2 units) and this half's sum
-        // `ok` stays warp-uniform, and after a failed wait the loop keeps running without work,
+        // `ok` stays warp-uniform, and after a failed wait the loops keep running without work,
         // so both warps of a quarter reach every named barrier and every tcgen05 load or store
         // is executed by a whole warp.
         bool ok = true;
@@ -322,120 +367,138 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
             const bool w = ok && mbar_wait(bar, parity, p.err);
             ok = __all_sync(0xffffffffu, w);
         };
-        for (int j = 0; j < nblk; j++) {
-            const int b = j & 1;
-            const uint32_t ph = uint32_t((j >> 1) & 1);
-            wait_all(&s_full[b], ph);
-            uint32_t sr[32];
-            float mh = -INFINITY;
-            const int kb = k_start + j * kTcKeys + half * 32;
-            if (ok) {
-                tc_fence_after();
-                tmem_ld32(lane_base + kTmemS + b * kTcKeys + half * 32, sr);
-                tmem_wait_ld();
-                // Scores in log2 units: p = 2^(s log2e - m), one FFMA and one ex2 per key.
-                if (kb >= row_lo && kb + 32 <= row_hi) {  // every key of this half is visible
-#pragma unroll
-                    for (int i = 0; i < 32; i++) {
-                        const float t = __uint_as_float(sr[i]) * kLog2e;
-                        sr[i] = __float_as_uint(t);
-                        mh = fmaxf(mh, t);
-                    }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 32; i++) {
-                        const int kj = kb + i;
-                        const float t = (kj >= row_lo && kj < row_hi) ? __uint_as_float(sr[i]) * kLog2e : -INFINITY;
-                        sr[i] = __float_as_uint(t);
-                        mh = fmaxf(mh, t);
-                    }
-                }
-            }
-            // Row maximum of the block from both halves (the slot is rewritten only after the
-            // next pair_sync, by which time the partner has read it).
-            red[half * kTcQ + r] = mh;
-            pair_sync();
-            const float mb = fmaxf(mh, red[(1 - half) * kTcQ + r]);
-            pair_sync();
-            if (!ok) continue;
-            // Rescale this half of O when the row's maximum grew past the threshold (both halves
-            // decide alike; tensor-memory loads and stores are warp-collective).
-            const bool grow = mb > m_used + kRescale && m_used != -INFINITY;
-            if (__any_sync(0xffffffffu, grow)) {
-                const float alpha = grow ? ex2_approx(m_used - mb) : 1.0f;
-                if (j > 0) wait_all(&pv_done[(j - 1) & 1], uint32_t(((j - 1) >> 1) & 1));
-                if (!ok) continue;
-                tc_fence_after();
-#pragma unroll 1
-                for (int c = 0; c < kTcHd / 64; c++) {
-                    uint32_t o[32];
-                    const uint32_t col = kTmemO + uint32_t(half * (kTcHd / 2) + c * 32);
-                    tmem_ld32(lane_base + col, o);
+        int gb = 0;
+        for (int it = int(p.offset[blockIdx.x]); it < int(p.offset[blockIdx.x + 1]); it++) {
+            const uint4 w = p.work[it];
+            int k_start, nblk;
+            item_keys(w, p, k_start, nblk);
+            const int len = int(w.y);
+            const int qi = int(w.z) + rt;  // this row's token within its sequence
+            const int h = int(w.w) * p.group + rg;
+            const bool live = r < live_rows && qi < len;
+            // Keys this row sees: [row_lo, row_hi) of its sequence.
+            const int row_lo = p.hw > 0 ? max(qi - p.hw, 0) : 0;
+            const int row_hi = p.hw > 0 ? min(qi + p.hw + 1, len) : len;
+            float m_used = -INFINITY, l = 0.f;  // running maximum (log2 units) and this half's sum
+            for (int j = 0; j < nblk; j++, gb++) {
+                const int b = gb & 1;
+                const uint32_t ph = uint32_t((gb >> 1) & 1);
+                wait_all(&s_full[b], ph);
+                uint32_t sr[32];
+                float mh = -INFINITY;
+                const int kb = k_start + j * kTcKeys + half * 32;
+                if (ok) {
+                    tc_fence_after();
+                    tmem_ld32(lane_base + kTmemS + b * kTcKeys + half * 32, sr);
                     tmem_wait_ld();
+                    // Scores in log2 units: p = 2^(s log2e - m), one FFMA and one ex2 per key.
+                    if (kb >= row_lo && kb + 32 <= row_hi) {  // every key of this half is visible
 #pragma unroll
-                    for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-                    tmem_st32(lane_base + col, o);
-                }
-                tmem_wait_st();
-                if (grow) {
-                    l *= alpha;
-                    m_used = mb;
-                }
-            }
-            if (m_used == -INFINITY) m_used = mb;  // first block with a visible key (O and l are still 0)
-            // P_j goes to buffer b once PV_{j-2}, which read that buffer, has completed.
-            if (j >= 2) wait_all(&pv_done[b], uint32_t(((j - 2) >> 1) & 1));
-            if (!ok) continue;
-            uint8_t* prow = smem + kOffP + b * kPBytes + r * 128;
-            float sum = 0.f;
-            const float mu = m_used == -INFINITY ? 0.f : m_used;
-#pragma unroll
-            for (int c = 0; c < 4; c++) {  // 4 chunks of 8 keys = 16 bytes each
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 4; e++) {
-                    const float p0 = ex2_approx(__uint_as_float(sr[c * 8 + 2 * e]) - mu);  // 2^-inf = 0
-                    const float p1 = ex2_approx(__uint_as_float(sr[c * 8 + 2 * e + 1]) - mu);
-                    sum += p0 + p1;
-                    __half2 hp = __floats2half2_rn(p0, p1);
-                    w[e] = *reinterpret_cast<uint32_t*>(&hp);
-                }
-                const int chunk = half * 4 + c;
-                *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
-            }
-            l += sum;
-            fence_proxy_async_smem();
-            tc_fence_before();
-            mbar_arrive(&p_full[b]);
-        }
-        // ---- epilogue: O / l for the rows of this sequence; each half stores its 128 columns
-        red[half * kTcQ + r] = l;
-        pair_sync();
-        const float lt = l + red[(1 - half) * kTcQ + r];
-        if (ok && nblk > 0) {
-            const int jl = nblk - 1;
-            wait_all(&pv_done[jl & 1], uint32_t((jl >> 1) & 1));
-            if (ok) {
-                tc_fence_after();
-                const float inv = lt > 0.f ? 1.0f / lt : 0.f;
-                __half* orow = p.out + (long(seq_start) + qi) * long(p.heads) * kTcHd + h * kTcHd + half * (kTcHd / 2);
-                const bool store = qi < int(len);
-#pragma unroll 1
-                for (int c = 0; c < kTcHd / 64; c++) {
-                    uint32_t o[32];
-                    tmem_ld32(lane_base + kTmemO + uint32_t(half * (kTcHd / 2) + c * 32), o);
-                    tmem_wait_ld();
-                    if (store) {
-                        uint32_t pk[16];
-#pragma unroll
-                        for (int i = 0; i < 16; i++) {
-                            __half2 hv = __floats2half2_rn(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
-                            pk[i] = *reinterpret_cast<uint32_t*>(&hv);
+                        for (int i = 0; i < 32; i++) {
+                            const float t = __uint_as_float(sr[i]) * kLog2e;
+                            sr[i] = __float_as_uint(t);
+                            mh = fmaxf(mh, t);
                         }
-                        uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+                    } else {
 #pragma unroll
-                        for (int i = 0; i < 4; i++) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+                        for (int i = 0; i < 32; i++) {
+                            const int kj = kb + i;
+                            const float t = (kj >= row_lo && kj < row_hi) ? __uint_as_float(sr[i]) * kLog2e : -INFINITY;
+                            sr[i] = __float_as_uint(t);
+                            mh = fmaxf(mh, t);
+                        }
                     }
+                }
+                // Row maximum of the block from both halves (the slot is rewritten only after the
+                // next pair_sync, by which time the partner has read it).
+                red[half * kTcQ + r] = mh;
+                pair_sync();
+                const float mb = fmaxf(mh, red[(1 - half) * kTcQ + r]);
+                pair_sync();
+                if (!ok) continue;
+                // Rescale this half of O when the row's maximum grew past the threshold (both
+                // halves decide alike; tensor-memory loads and stores are warp-collective).
+                const bool grow = mb > m_used + kRescale && m_used != -INFINITY;
+                if (__any_sync(0xffffffffu, grow)) {
+                    const float alpha = grow ? ex2_approx(m_used - mb) : 1.0f;
+                    if (j > 0) wait_all(&pv_done[(gb - 1) & 1], uint32_t(((gb - 1) >> 1) & 1));
+                    if (!ok) continue;
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int c = 0; c < kTcHd / 64; c++) {
+                        uint32_t o[32];
+                        const uint32_t col = kTmemO + uint32_t(half * (kTcHd / 2) + c * 32);
+                        tmem_ld32(lane_base + col, o);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+                        tmem_st32(lane_base + col, o);
+                    }
+                    tmem_wait_st();
+                    if (grow) {
+                        l *= alpha;
+                        m_used = mb;
+                    }
+                }
+                if (m_used == -INFINITY) m_used = mb;  // first block with a visible key (O and l are still 0)
+                // P goes to buffer b once the PV two blocks back, which read that buffer, has completed.
+                if (gb >= 2) wait_all(&pv_done[b], uint32_t(((gb - 2) >> 1) & 1));
+                if (!ok) continue;
+                uint8_t* prow = smem + kOffP + b * kPBytes + r * 128;
+                float sum = 0.f;
+                const float mu = m_used == -INFINITY ? 0.f : m_used;
+#pragma unroll
+                for (int c = 0; c < 4; c++) {  // 4 chunks of 8 keys = 16 bytes each
+                    uint32_t wv[4];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const float p0 = ex2_approx(__uint_as_float(sr[c * 8 + 2 * e]) - mu);  // 2^-inf = 0
+                        const float p1 = ex2_approx(__uint_as_float(sr[c * 8 + 2 * e + 1]) - mu);
+                        sum += p0 + p1;
+                        __half2 hp = __floats2half2_rn(p0, p1);
+                        wv[e] = *reinterpret_cast<uint32_t*>(&hp);
+                    }
+                    const int chunk = half * 4 + c;
+                    *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) * 16)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+                }
+                l += sum;
+                fence_proxy_async_smem();
+                tc_fence_before();
+                mbar_arrive(&p_full[b]);
+            }
+            // ---- epilogue: O / l of the live rows; each half stores its 128 columns, then O is
+            // handed back for the next item's first PV
+            red[half * kTcQ + r] = l;
+            pair_sync();
+            const float lt = l + red[(1 - half) * kTcQ + r];
+            pair_sync();  // the slots are free for the next item's first block
+            if (ok) {
+                wait_all(&pv_done[(gb - 1) & 1], uint32_t(((gb - 1) >> 1) & 1));
+                if (ok) {
+                    tc_fence_after();
+                    const float inv = lt > 0.f ? 1.0f / lt : 0.f;
+                    __half* orow = p.out + ((long(w.x) + qi) * p.heads + h) * long(kTcHd) + half * (kTcHd / 2);
+#pragma unroll 1
+                    for (int c = 0; c < kTcHd / 64; c++) {
+                        uint32_t o[32];
+                        tmem_ld32(lane_base + kTmemO + uint32_t(half * (kTcHd / 2) + c * 32), o);
+                        tmem_wait_ld();
+                        if (live) {
+                            uint32_t pk[16];
+#pragma unroll
+                            for (int i = 0; i < 16; i++) {
+                                __half2 hv = __floats2half2_rn(__uint_as_float(o[2 * i]) * inv,
+                                                               __uint_as_float(o[2 * i + 1]) * inv);
+                                pk[i] = *reinterpret_cast<uint32_t*>(&hv);
+                            }
+                            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+                            for (int i = 0; i < 4; i++)
+                                dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+                        }
+                    }
+                    tc_fence_before();
+                    mbar_arrive(o_empty);
                 }
             }
         }
@@ -449,7 +512,66 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
     }
 }
 
-int attention_queries_per_item(int hd) { return hd == kTcHd ? kTcQ : kSimtQueries; }
+static_assert(kSimtQueries == kSimtQueriesPerItem, "work list and kernel agree");
+
+int build_attention_work(const uint32_t* sl, int nseq, int kvh, int group, int hw, int max_ctas, uint32_t* out,
+                         int* ctas) {
+    const int T = attention_tokens_per_item(group);
+    struct Item {
+        uint32_t start, len, t0, kh;
+        int cost;
+    };
+    std::vector<Item> items;
+    for (int s = 0; s < nseq; s++)
+        for (uint32_t t0 = 0; t0 < sl[2 * s + 1]; t0 += uint32_t(T))
+            for (int kh = 0; kh < kvh; kh++) {
+                const int len = int(sl[2 * s + 1]);
+                int ks = 0, ke = len;
+                if (hw > 0) {
+                    ks = std::max(int(t0) - hw, 0);
+                    ke = std::min(int(t0) + T - 1 + hw + 1, len);
+                }
+                ks = ks / kTcKeys * kTcKeys;
+                // An item costs its key blocks plus about two blocks of set-up and epilogue.
+                items.push_back({sl[2 * s], sl[2 * s + 1], t0, uint32_t(kh), (ke - ks + kTcKeys - 1) / kTcKeys + 2});
+            }
+    const int n = int(items.size());
+    const int grid = std::max(1, std::min(n, max_ctas));
+    if (ctas) *ctas = n ? grid : 0;
+    if (n == 0) return 0;
+    const int words = 4 * n + grid + 1;
+    if (!out) return words;
+    std::stable_sort(items.begin(), items.end(), [](const Item& a, const Item& b) { return a.cost > b.cost; });
+    // Each item goes to the least-loaded CTA so far (lowest index on ties): deterministic.
+    std::vector<std::pair<long, int>> heap;
+    for (int c = 0; c < grid; c++) heap.push_back({0, c});
+    auto cmp = [](const std::pair<long, int>& a, const std::pair<long, int>& b) {
+        return a.first != b.first ? a.first > b.first : a.second > b.second;
+    };
+    std::make_heap(heap.begin(), heap.end(), cmp);
+    std::vector<int> owner(static_cast<size_t>(n)), count(static_cast<size_t>(grid), 0);
+    for (int i = 0; i < n; i++) {
+        std::pop_heap(heap.begin(), heap.end(), cmp);
+        auto& top = heap.back();
+        owner[size_t(i)] = top.second;
+        count[size_t(top.second)]++;
+        top.first += items[size_t(i)].cost;
+        std::push_heap(heap.begin(), heap.end(), cmp);
+    }
+    uint32_t* off = out + 4 * size_t(n);
+    off[0] = 0;
+    for (int c = 0; c < grid; c++) off[c + 1] = off[c] + uint32_t(count[size_t(c)]);
+    std::vector<uint32_t> next(off, off + grid);
+    for (int i = 0; i < n; i++) {
+        const Item& it = items[size_t(i)];
+        uint32_t* w = out + 4 * size_t(next[size_t(owner[size_t(i)])]++);
+        w[0] = it.start;
+        w[1] = it.len;
+        w[2] = it.t0;
+        w[3] = it.kh;
+    }
+    return words;
+}
 
 template <int HD>
 static int simt_smem() {
@@ -466,9 +588,12 @@ cudaError_t configure_attention_kernels() {
 }
 
 static cudaError_t launch_tc(const AttnLaunch& a, cudaStream_t stream) {
-    TcAttnParams p{a.work, a.out, a.heads, a.kv_heads, a.half_window, a.err};
-    dim3 grid(a.work_items, a.heads);
-    return launch_kernel(k_attention_tc, grid, dim3(kTcThreads), kTcSmem, stream, 1, a.maps->q, a.maps->k, a.maps->v, p);
+    const int group = a.heads / a.kv_heads;
+    if (group > kTcQ) return cudaErrorInvalidValue;
+    TcAttnParams p{reinterpret_cast<const uint4*>(a.work), a.work + 4 * size_t(a.sched_items), a.out, a.heads, group,
+                   attention_tokens_per_item(group), a.half_window, a.err};
+    return launch_kernel(k_attention_tc, dim3(a.work_items), dim3(kTcThreads), kTcSmem, stream, 1, a.maps->q,
+                         a.maps->k, a.maps->v, p);
 }
 
 template <int HD>
@@ -479,16 +604,21 @@ static cudaError_t launch_simt(const AttnLaunch& a, cudaStream_t stream) {
                          a.kv_heads, a.half_window, 1.0f);
 }
 
+// Q as [rows][heads][hd] with boxes of 64 dims x G heads x T tokens (one work item's tile,
+// row t * G + g); K and V as [rows][kv_heads * hd] with boxes of 64 dims x 64 keys.
 bool encode_attention_maps(AttnMaps& m, const __half* q, const __half* k, const __half* v, int rows, int heads, int kvh,
                            int hd) {
-    return encode_fp16_map(&m.q, q, uint64_t(heads) * hd, rows, 64, kTcQ) &&
+    const int group = heads / kvh;
+    if (hd != kTcHd || heads % kvh || group > kTcQ) return false;
+    return encode_fp16_map_3d(&m.q, q, uint64_t(hd), uint64_t(heads), uint64_t(rows), 64, uint32_t(group),
+                              uint32_t(attention_tokens_per_item(group))) &&
            encode_fp16_map(&m.k, k, uint64_t(kvh) * hd, rows, 64, kTcKeys) &&
            encode_fp16_map(&m.v, v, uint64_t(kvh) * hd, rows, 64, kTcKeys);
 }
 
 cudaError_t launch_attention(const AttnLaunch& a, cudaStream_t stream) {
     if (a.work_items <= 0) return cudaSuccess;
-    if (a.heads % a.kv_heads || a.queries_per_item != attention_queries_per_item(a.hd)) return cudaErrorInvalidValue;
+    if (a.heads % a.kv_heads) return cudaErrorInvalidValue;
     if (a.hd == kTcHd) return a.maps ? launch_tc(a, stream) : cudaErrorInvalidValue;
     if (a.hd == 512) return launch_simt<512>(a, stream);
     return cudaErrorInvalidValue;

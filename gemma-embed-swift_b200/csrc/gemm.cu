@@ -703,6 +703,19 @@ bool encode_fp16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t
                      CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+bool encode_fp16_map_3d(CUtensorMap* map, const void* ptr, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0,
+                        uint32_t b1, uint32_t b2) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
+    cuuint32_t box[3] = {b0, b1, b2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool encode_activation_map(DevActivation& a) {
     return encode_2d(&a.map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.ptr, a.cols, a.rows, BK, BM,
                      CU_TENSOR_MAP_SWIZZLE_128B);

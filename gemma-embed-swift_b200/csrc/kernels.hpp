@@ -171,21 +171,39 @@ bool encode_attention_maps(AttnMaps& m, const __half* q, const __half* k, const 
 // A 2-D fp16 tensor map with 128-byte swizzle over a row-major [outer][inner] matrix.
 bool encode_fp16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint32_t box_inner,
                      uint32_t box_outer);
+// The same over a dense [d2][d1][d0] array with boxes b0 x b1 x b2.
+bool encode_fp16_map_3d(CUtensorMap* map, const void* ptr, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0,
+                        uint32_t b1, uint32_t b2);
 
 struct AttnLaunch {
     const __half* q;  // [rows][heads * hd]
     const __half* k;  // [rows][kv_heads * hd]
     const __half* v;
     __half* out;      // [rows][heads * hd]
-    const uint32_t* work;  // (seq_start, seq_len, q0) triples
-    int work_items;
+    // head dim 256: the schedule build_attention_work writes (items grouped by CTA, then the
+    // CTAs' item offsets); head dim 512: (seq_start, seq_len, first query) triples per 32 queries
+    const uint32_t* work;
+    int work_items;   // head dim 256: the schedule's CTA count; head dim 512: triples
+    int sched_items = 0;  // head dim 256: items in the schedule
     int heads, kv_heads, hd;
     int half_window;  // 0: global attention
-    int queries_per_item;
     int* err;
+    int num_sms = 148;
     const AttnMaps* maps = nullptr;  // required for head dim 256 (tensor-core kernel)
 };
 cudaError_t launch_attention(const AttnLaunch& a, cudaStream_t stream);
-int attention_queries_per_item(int hd);
+// Tokens of one tensor-core work item: its 128-row Q tile holds `group` heads per token.
+inline int attention_tokens_per_item(int group) { return 128 / group; }
+// Queries per work item of the CUDA-core kernel (head dim 512).
+constexpr int kSimtQueriesPerItem = 32;
+// The tensor-core kernel's schedule for packed sequences (start, length pairs): one item per
+// block of attention_tokens_per_item(group) tokens and KV head (group = heads / kv_heads),
+// spread over min(items, max_ctas) CTAs by longest-processing-time-first on the item's key
+// blocks under `half_window` (0: global).  Layout: the items as (seq_start, seq_len, first
+// token, KV head), grouped by CTA, then CTA c's item range [off[c], off[c + 1]) as ctas + 1
+// offsets.  Returns the words written (or needed, when `out` is null); `ctas` receives the CTA
+// count.
+int build_attention_work(const uint32_t* seq_start_len, int nseq, int kv_heads, int group, int half_window,
+                         int max_ctas, uint32_t* out, int* ctas);
 
 }  // namespace ge

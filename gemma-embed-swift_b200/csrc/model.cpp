@@ -346,7 +346,7 @@ static cudaError_t ensure_workspace(const Config& c, Device& d, int rows, int se
     chk(A(&ws.tokens, r));
     chk(A(&ws.positions, r));
     chk(A(&ws.seqs, 2 * size_t(S)));
-    chk(A(&ws.work, 3 * size_t(W)));
+    chk(A(&ws.work, size_t(W)));
     chk(A(&ws.x, r * d_));
     chk(A(&ws.qkv16, r * qkvd));
     chk(A(&ws.o16, r * d_));
@@ -371,7 +371,7 @@ static cudaError_t ensure_workspace(const Config& c, Device& d, int rows, int se
     chk(H(&ws.h_tokens, r));
     chk(H(&ws.h_positions, r));
     chk(H(&ws.h_seqs, 2 * size_t(S)));
-    chk(H(&ws.h_work, 3 * size_t(W)));
+    chk(H(&ws.h_work, size_t(W)));
     chk(H(&ws.h_out, size_t(S) * std::max(c.out_dim, c.hidden)));
     chk(H(&ws.h_err, 1));
     if (err != cudaSuccess) {
@@ -511,9 +511,13 @@ int load_model(ge_model* m, const char* path, const ge_load_opts* opts) {
     if (!read_config(m->file, c, le)) return set_error(m, le.code, le.msg);
     if (c.layers <= 0 || (c.hidden != 512 && c.hidden != 768) || c.ff % 128 || c.heads <= 0)
         return set_error(m, GE_ERR_INVALID_GGUF, "invalid GGUF file: unsupported dimensions");
+    int kv256 = 0;  // every head-dim-256 layer shares one attention work list
+    for (auto& l : c.layer)
+        if (l.hd == 256 && kv256 == 0) kv256 = l.kv;
     for (auto& l : c.layer)
         if ((l.hd != 256 && l.hd != 512) || l.kv <= 0 || c.heads % l.kv ||
-            c.heads + 2 * l.kv > (l.hd == 256 ? 8 : 6))  // the q/k/v norm kernel's slot capacity
+            c.heads + 2 * l.kv > (l.hd == 256 ? 8 : 6) ||  // the q/k/v norm kernel's slot capacity
+            (l.hd == 256 && l.kv != kv256))  // one attention work list for every head-dim-256 layer
             return set_error(m, GE_ERR_INVALID_GGUF, "invalid GGUF file: unsupported head layout");
     const GgufFile& f = m->file;
     const int d = c.hidden, ff = c.ff, pl = c.per_layer;
@@ -739,14 +743,35 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     } policy(!(m->flags & GE_LOAD_NO_PDL));
     const int ntok = a.ntok, nseq = a.nseq;
     const int rows = std::max(kRowTile, round_up(ntok, kRowTile));
-    // Two work lists: blocks of the tensor-core kernel's query count, and of the CUDA-core
-    // kernel's for head-dim-512 layers, stored back to back.
-    bool any512 = false;
-    for (auto& l : c.layer) any512 = any512 || l.hd == 512;
-    const int qpi = attention_queries_per_item(256), qpi512 = attention_queries_per_item(512);
-    const int nwork = build_work(a.seqs, nseq, qpi, nullptr);
-    const int nwork512 = any512 ? build_work(a.seqs, nseq, qpi512, nullptr) : 0;
-    if ((e = ensure_workspace(c, d, rows, nseq, nwork + nwork512)) != cudaSuccess) return gpu_fail(e, "workspace");
+    // Attention work stored back to back, each part starting on 16 bytes: the tensor-core
+    // kernel's schedules for sliding and for global head-dim-256 layers (items of T tokens x
+    // the query heads of one KV head, spread over CTAs by key blocks), and the CUDA-core
+    // kernel's list for head-dim-512 layers (3 words per 32 queries).
+    static_assert(sizeof(ge_seq) == 8, "ge_seq is a (start, length) pair of uint32");
+    const uint32_t* seq_pairs = reinterpret_cast<const uint32_t*>(a.seqs);
+    int kv256 = 0;
+    bool any512 = false, slide256 = false, global256 = false;
+    for (auto& l : c.layer) {
+        if (l.hd == 256) {
+            kv256 = l.kv;
+            (l.sliding ? slide256 : global256) = true;
+        }
+        any512 = any512 || l.hd == 512;
+    }
+    const int group = kv256 ? c.heads / kv256 : 1;
+    const int hw_slide = c.sliding_window / 2;
+    int sched[4] = {0, 0, 0, 0};  // items and CTAs of the sliding, then the global schedule
+    int words[2] = {0, 0};
+    for (int k = 0; k < 2; k++) {
+        if (!(k == 0 ? slide256 : global256)) continue;
+        words[k] = build_attention_work(seq_pairs, nseq, kv256, group, k == 0 ? hw_slide : 0, d.num_sms, nullptr,
+                                        &sched[2 * k + 1]);
+        sched[2 * k] = words[k] ? (words[k] - sched[2 * k + 1] - 1) / 4 : 0;
+        words[k] = (words[k] + 3) & ~3;
+    }
+    const int nwork512 = any512 ? build_work(a.seqs, nseq, kSimtQueriesPerItem, nullptr) : 0;
+    const int work_words = words[0] + words[1] + 3 * nwork512;
+    if ((e = ensure_workspace(c, d, rows, nseq, work_words)) != cudaSuccess) return gpu_fail(e, "workspace");
     Workspace& ws = d.ws;
     int64_t launches = 0;
     // ---- inputs
@@ -760,22 +785,28 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         chunk_total += uint32_t(ch);
         max_chunks = std::max(max_chunks, ch);
     }
-    build_work(a.seqs, nseq, qpi, ws.h_work);
-    if (any512) build_work(a.seqs, nseq, qpi512, ws.h_work + 3 * size_t(nwork));
+    for (int k = 0; k < 2; k++)
+        if (words[k])
+            build_attention_work(seq_pairs, nseq, kv256, group, k == 0 ? hw_slide : 0, d.num_sms,
+                                 ws.h_work + (k == 0 ? 0 : words[0]), nullptr);
+    if (any512) build_work(a.seqs, nseq, kSimtQueriesPerItem, ws.h_work + words[0] + words[1]);
     const int32_t* tokens = ws.tokens;
+    int64_t h2d = int64_t(nseq) * 8 + int64_t(work_words) * 4 + int64_t(nseq) * 4;  // seqs, work, chunk bases
     if (a.tokens_on_device) {
         tokens = a.tokens;
     } else {
+        h2d += int64_t(ntok) * 4;
         memcpy(ws.h_tokens, a.tokens, size_t(ntok) * 4);
         if ((e = cudaMemcpyAsync(ws.tokens, ws.h_tokens, size_t(ntok) * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess)
             return gpu_fail(e, "token upload");
     }
     if (a.positions == nullptr) launches++;  // the positions kernel below
     if ((e = cudaMemcpyAsync(ws.seqs, ws.h_seqs, size_t(nseq) * 8, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
-        (e = cudaMemcpyAsync(ws.work, ws.h_work, size_t(nwork + nwork512) * 12, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(ws.work, ws.h_work, size_t(work_words) * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
         (e = cudaMemcpyAsync(ws.chunk_base, ws.h_chunk_base, size_t(nseq) * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess)
         return gpu_fail(e, "batch upload");
     if (a.positions) {
+        h2d += int64_t(ntok) * 4;
         memcpy(ws.h_positions, a.positions, size_t(ntok) * 4);
         e = cudaMemcpyAsync(ws.positions, ws.h_positions, size_t(ntok) * 4, cudaMemcpyHostToDevice, st);
     } else {
@@ -924,13 +955,15 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
             al.v = ws.v;
             al.out = ws.attn;
             const bool tc = lc.hd == 256;
-            al.work = tc ? ws.work : ws.work + 3 * size_t(nwork);
-            al.work_items = tc ? nwork : nwork512;
+            const int k = lc.sliding ? 0 : 1;
+            al.work = tc ? ws.work + (k == 0 ? 0 : words[0]) : ws.work + words[0] + words[1];
+            al.work_items = tc ? sched[2 * k + 1] : nwork512;
+            al.sched_items = tc ? sched[2 * k] : 0;
+            al.num_sms = d.num_sms;
             al.heads = c.heads;
             al.kv_heads = lc.kv;
             al.hd = lc.hd;
             al.half_window = lc.sliding ? c.sliding_window / 2 : 0;
-            al.queries_per_item = tc ? qpi : qpi512;
             al.err = d.err;
             for (auto& x : ws.attn_maps)
                 if (tc && x.first == lc.kv) al.maps = &x.second;
@@ -1038,7 +1071,14 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     // Captured CUDA graphs replay the whole launch sequence of a batch shape with one call
     // (kernel arguments, tensor maps included, are fixed per workspace and shape).
     const bool use_graph = !(m->flags & GE_LOAD_NO_GRAPHS) && !a.profile && a.trace_layer < -1;
-    GraphKey gk{rows, ntok, nseq, nwork, nwork512, max_chunks, reinterpret_cast<uintptr_t>(tokens)};
+    GraphKey gk;
+    gk.rows = rows;
+    gk.ntok = ntok;
+    gk.nseq = nseq;
+    gk.nwork512 = nwork512;
+    gk.pool_chunks = max_chunks;
+    for (int k = 0; k < 4; k++) gk.sched[k] = sched[k];
+    gk.tokens = reinterpret_cast<uintptr_t>(tokens);
     GraphEntry* ge_ = use_graph ? find_graph(d, gk) : nullptr;
     if (ge_) {
         if ((e = cudaGraphLaunch(ge_->exec, st)) != cudaSuccess) return gpu_fail(e, "graph launch");
@@ -1071,11 +1111,13 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     const size_t out_elems = a.trace_layer >= -1 ? size_t(ntok) * D : size_t(nseq) * width;
     float* host_out = a.trace_layer >= -1 ? a.trace_out : a.out;
     m->launches += launches;
+    m->h2d_bytes += h2d;
     if (a.out_on_device && a.trace_layer < -1) {
         CK(cudaMemcpyAsync(a.out, result, out_elems * 4, cudaMemcpyDeviceToDevice, st), "result copy");
         return GE_OK;
     }
     CK(cudaMemcpyAsync(ws.h_err, d.err, sizeof(int), cudaMemcpyDeviceToHost, st), "error readback");
+    m->d2h_bytes += int64_t(sizeof(int)) + int64_t(out_elems) * 4;
     if (a.trace_layer >= -1) {
         // The trace spans ntok rows of D, which may exceed the pooled staging buffer.
         CK(cudaMemcpyAsync(host_out, result, out_elems * 4, cudaMemcpyDeviceToHost, st), "trace readback");

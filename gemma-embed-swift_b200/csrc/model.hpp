@@ -68,11 +68,13 @@ struct Workspace {
 
 // A captured forward for one batch shape on one workspace.
 struct GraphKey {
-    int rows = 0, ntok = 0, nseq = 0, nwork = 0, nwork512 = 0, pool_chunks = 0;
-    uintptr_t tokens = 0;  // the token buffer the embedding kernel reads
+    int rows = 0, ntok = 0, nseq = 0, nwork512 = 0, pool_chunks = 0;
+    int sched[4] = {0, 0, 0, 0};  // attention schedules: (items, CTAs) for sliding and global layers
+    uintptr_t tokens = 0;         // the token buffer the embedding kernel reads
     bool operator==(const GraphKey& o) const {
-        return rows == o.rows && ntok == o.ntok && nseq == o.nseq && nwork == o.nwork && nwork512 == o.nwork512 &&
-               pool_chunks == o.pool_chunks && tokens == o.tokens;
+        return rows == o.rows && ntok == o.ntok && nseq == o.nseq && nwork512 == o.nwork512 &&
+               pool_chunks == o.pool_chunks && tokens == o.tokens && sched[0] == o.sched[0] && sched[1] == o.sched[1] &&
+               sched[2] == o.sched[2] && sched[3] == o.sched[3];
     }
 };
 struct GraphEntry {
@@ -112,6 +114,7 @@ struct ge_model {
     uint32_t flags = 0;
     int64_t file_size = 0;
     std::atomic<int64_t> launches{0};  // kernel launches issued by this model so far
+    std::atomic<int64_t> h2d_bytes{0}, d2h_bytes{0};  // host <-> device copies of the forwards so far
 };
 
 namespace ge {

@@ -219,14 +219,29 @@ int ge_test_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
     }
     if (next != uint64_t(ntok)) return fail(GE_ERR_INVALID_OPTIONS, "lengths do not sum to ntok");
     const int rows = (ntok + ge::kRowTile - 1) / ge::kRowTile * ge::kRowTile;
-    const int qpi = ge::attention_queries_per_item(hd);
+    int dev = 0, sms = 0;
+    TRY(cudaGetDevice(&dev));
+    TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     std::vector<uint32_t> work;
-    for (int s = 0; s < nseq; s++)
-        for (uint32_t q0 = 0; q0 < seqs[s].length; q0 += uint32_t(qpi)) {
-            work.push_back(seqs[s].start);
-            work.push_back(seqs[s].length);
-            work.push_back(q0);
+    int items = 0, ctas = 0;
+    if (hd == 256) {
+        std::vector<uint32_t> pairs;
+        for (int s = 0; s < nseq; s++) {
+            pairs.push_back(seqs[s].start);
+            pairs.push_back(seqs[s].length);
         }
+        const int words = ge::build_attention_work(pairs.data(), nseq, kvh, heads / kvh, half_window, sms, nullptr, &ctas);
+        work.resize(size_t(words));
+        ge::build_attention_work(pairs.data(), nseq, kvh, heads / kvh, half_window, sms, work.data(), nullptr);
+        items = (words - ctas - 1) / 4;
+    } else {
+        for (int s = 0; s < nseq; s++)
+            for (uint32_t q0 = 0; q0 < seqs[s].length; q0 += uint32_t(ge::kSimtQueriesPerItem), items++) {
+                work.push_back(seqs[s].start);
+                work.push_back(seqs[s].length);
+                work.push_back(q0);
+            }
+    }
     DevBuf dq, dk, dv, dout, dwork, derr;
     const size_t qn = size_t(rows) * heads * hd, kn = size_t(rows) * kvh * hd;
     TRY(dq.alloc(qn * 2));
@@ -251,13 +266,14 @@ int ge_test_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
     al.v = static_cast<const __half*>(dv.p);
     al.out = static_cast<__half*>(dout.p);
     al.work = static_cast<const uint32_t*>(dwork.p);
-    al.work_items = int(work.size() / 3);
+    al.work_items = hd == 256 ? ctas : items;
+    al.sched_items = items;
     al.heads = heads;
     al.kv_heads = kvh;
     al.hd = hd;
     al.half_window = half_window;
-    al.queries_per_item = qpi;
     al.err = static_cast<int*>(derr.p);
+    al.num_sms = sms;
     ge::AttnMaps maps;
     if (hd == 256) {
         if (!ge::encode_attention_maps(maps, al.q, al.k, al.v, rows, heads, kvh, hd))

@@ -92,6 +92,8 @@ typedef struct ge_info {
     int32_t bos_id;
     char device_name[128];
     int64_t kernel_launches; /* CUDA kernels this model has launched so far, on all devices */
+    int64_t host_to_device_bytes; /* bytes the forwards so far copied from host to device */
+    int64_t device_to_host_bytes; /* and from device to host */
 } ge_info;
 
 /* One kernel class of a profiling forward (ge_profile). */

@@ -135,7 +135,10 @@ def attention(ge, q, k, v, lens, heads, kvh, hd, hw):
 
 
 CONFIGS = [(3, 1, 256, 512), (3, 1, 256, 0), (4, 2, 256, 512), (4, 1, 512, 0), (4, 1, 512, 512)]
-LENGTHS = [[1, 7, 64], [1024, 5], [2048], [2048, 3, 1024, 7]]
+# The last case packs more work items than the GPU has SMs, so the tensor-core kernel's
+# persistent CTAs each take several items of different lengths.
+LENGTHS = [[1, 7, 64], [1024, 5], [2048], [2048, 3, 1024, 7],
+           [int(x) for x in np.random.default_rng(17).integers(1, 600, 48)]]
 
 
 @pytest.mark.parametrize("heads,kvh,hd,hw", CONFIGS)
