@@ -72,13 +72,14 @@ cudaError_t launch_embed(const int32_t* tokens, int ntok, int rows, const int8_t
     return cudaGetLastError();
 }
 
-// One warp per token, over the head slots of its fused projection row: slots [0, H) are query
-// heads, [H, H+KV) key heads, [H+KV, H+2KV) value heads.  CPUReference.swift:225-235.
-// Lane l holds elements [Q*l, Q*l + Q) of each half of a head (Q = HD / 64), so every element
-// and its rotation partner HD/2 away sit in the same lane; the token's cos/sin pairs are read
-// once and reused for every query and key head.  All slots are loaded before the first is
-// normalised, so each warp keeps MAXS independent loads in flight.
-template <int HD, int MAXS>
+// One warp per TPW tokens, over the S head slots of each token's fused projection row: slots
+// [0, H) are query heads, [H, H+KV) key heads, [H+KV, H+2KV) value heads.
+// CPUReference.swift:225-235.  Lane l holds elements [Q*l, Q*l + Q) of each half of a head
+// (Q = HD / 64), so every element and its rotation partner HD/2 away sit in the same lane; a
+// token's cos/sin pairs are read once and reused for every query and key head.  Every slot of
+// every token is loaded before the first is normalised, so each warp keeps TPW * S * 2
+// independent loads in flight.
+template <int HD, int S, int TPW>
 __global__ void k_qkv_norm_rope(const __half* __restrict__ qkv, int ntok, int rows, int heads, int kvh,
                                 const float* __restrict__ qw, const float* __restrict__ kw,
                                 const int32_t* __restrict__ pos, const float* __restrict__ rope, float eps,
@@ -88,111 +89,138 @@ __global__ void k_qkv_norm_rope(const __half* __restrict__ qkv, int ntok, int ro
     constexpr int Q = HD / 64;  // elements per lane per half: 4 (hd 256) or 8 (hd 512)
     constexpr int WQ = Q / 2;   // 32-bit words per lane per half
     constexpr int HALF = HD / 2;
-    const int slots = heads + 2 * kvh;
-    const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+    const int row0 = (blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5)) * TPW;
     const int lane = threadIdx.x & 31;
-    if (row >= rows) return;
     const int c = lane * Q;
-    const bool live = row < ntok;
-    uint32_t raw[MAXS][2][WQ];
-    const __half* src_row = qkv + long(row) * slots * HD;
+    uint32_t raw[TPW][S][2][WQ];
+    int32_t pv[TPW];
 #pragma unroll
-    for (int s = 0; s < MAXS; s++)
+    for (int t = 0; t < TPW; t++) {
+        const int row = row0 + t;
+        const bool live = row < ntok;
+        const __half* src_row = qkv + long(row) * S * HD;
+        pv[t] = live ? pos[row] : 0;
 #pragma unroll
-        for (int h = 0; h < 2; h++)
+        for (int s = 0; s < S; s++)
 #pragma unroll
-            for (int i = 0; i < WQ; i += 2) {
-                uint2 r = make_uint2(0u, 0u);
-                if (live && s < slots) r = *reinterpret_cast<const uint2*>(src_row + s * HD + h * HALF + c + 2 * i);
-                raw[s][h][i] = r.x;
-                raw[s][h][i + 1] = r.y;
-            }
-    float cs_c[Q], cs_s[Q];
-    if (live) {
-        const float* cs = rope + long(pos[row]) * HD + 2 * c;  // [position][pair][cos, sin]
+            for (int h = 0; h < 2; h++)
 #pragma unroll
-        for (int i = 0; i < Q; i += 2) {
-            const float4 t = *reinterpret_cast<const float4*>(cs + 2 * i);
-            cs_c[i] = t.x;
-            cs_s[i] = t.y;
-            cs_c[i + 1] = t.z;
-            cs_s[i + 1] = t.w;
-        }
+                for (int i = 0; i < WQ; i += 2) {
+                    uint2 r = make_uint2(0u, 0u);
+                    if (live) r = *reinterpret_cast<const uint2*>(src_row + s * HD + h * HALF + c + 2 * i);
+                    raw[t][s][h][i] = r.x;
+                    raw[t][s][h][i + 1] = r.y;
+                }
     }
 #pragma unroll
-    for (int slot = 0; slot < MAXS; slot++) {
-        if (slot >= slots) break;
-        __half* dst;
-        const float* w = nullptr;
-        if (slot < heads) {
-            dst = q + long(row) * heads * HD + slot * HD;
-            w = qw;
-        } else if (slot < heads + kvh) {
-            dst = k + long(row) * kvh * HD + (slot - heads) * HD;
-            w = kw;
-        } else {
-            dst = v + long(row) * kvh * HD + (slot - heads - kvh) * HD;
-        }
-        float a[Q], b[Q];
+    for (int t = 0; t < TPW; t++) {
+        const int row = row0 + t;
+        if (row >= rows) break;
+        const bool live = row < ntok;
+        float cs_c[Q], cs_s[Q];
+        if (live) {
+            const float* cs = rope + long(pv[t]) * HD + 2 * c;  // [position][pair][cos, sin]
 #pragma unroll
-        for (int i = 0; i < WQ; i++) {
-            const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&raw[slot][0][i]));
-            const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&raw[slot][1][i]));
-            a[2 * i] = fa.x;
-            a[2 * i + 1] = fa.y;
-            b[2 * i] = fb.x;
-            b[2 * i + 1] = fb.y;
-        }
-        float ss = 0.f;
-#pragma unroll
-        for (int i = 0; i < Q; i++) ss += a[i] * a[i] + b[i] * b[i];
-        ss = warp_sum(ss);
-        const float inv = 1.0f / sqrtf(ss / float(HD) + eps);
-#pragma unroll
-        for (int i = 0; i < Q; i++) {
-            a[i] = a[i] * inv * (w ? w[c + i] : 1.0f);
-            b[i] = b[i] * inv * (w ? w[HALF + c + i] : 1.0f);
-        }
-        if (w && live) {  // NeoX rotation of the pairs (c + i, HALF + c + i)
-#pragma unroll
-            for (int i = 0; i < Q; i++) {
-                const float a0 = a[i], b0 = b[i];
-                a[i] = a0 * cs_c[i] - b0 * cs_s[i];
-                b[i] = a0 * cs_s[i] + b0 * cs_c[i];
+            for (int i = 0; i < Q; i += 2) {
+                const float4 f = *reinterpret_cast<const float4*>(cs + 2 * i);
+                cs_c[i] = f.x;
+                cs_s[i] = f.y;
+                cs_c[i + 1] = f.z;
+                cs_s[i + 1] = f.w;
             }
         }
 #pragma unroll
-        for (int i = 0; i < Q; i += 4) {
-            uint2 oa, ob;
-            *reinterpret_cast<__half2*>(&oa.x) = __floats2half2_rn(a[i], a[i + 1]);
-            *reinterpret_cast<__half2*>(&oa.y) = __floats2half2_rn(a[i + 2], a[i + 3]);
-            *reinterpret_cast<__half2*>(&ob.x) = __floats2half2_rn(b[i], b[i + 1]);
-            *reinterpret_cast<__half2*>(&ob.y) = __floats2half2_rn(b[i + 2], b[i + 3]);
-            *reinterpret_cast<uint2*>(dst + c + i) = oa;
-            *reinterpret_cast<uint2*>(dst + HALF + c + i) = ob;
+        for (int slot = 0; slot < S; slot++) {
+            __half* dst;
+            const float* w = nullptr;
+            if (slot < heads) {
+                dst = q + long(row) * heads * HD + slot * HD;
+                w = qw;
+            } else if (slot < heads + kvh) {
+                dst = k + long(row) * kvh * HD + (slot - heads) * HD;
+                w = kw;
+            } else {
+                dst = v + long(row) * kvh * HD + (slot - heads - kvh) * HD;
+            }
+            float a[Q], b[Q];
+#pragma unroll
+            for (int i = 0; i < WQ; i++) {
+                const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&raw[t][slot][0][i]));
+                const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&raw[t][slot][1][i]));
+                a[2 * i] = fa.x;
+                a[2 * i + 1] = fa.y;
+                b[2 * i] = fb.x;
+                b[2 * i + 1] = fb.y;
+            }
+            float ss = 0.f;
+#pragma unroll
+            for (int i = 0; i < Q; i++) ss += a[i] * a[i] + b[i] * b[i];
+            ss = warp_sum(ss);
+            const float inv = 1.0f / sqrtf(ss / float(HD) + eps);
+#pragma unroll
+            for (int i = 0; i < Q; i++) {
+                a[i] = a[i] * inv * (w ? w[c + i] : 1.0f);
+                b[i] = b[i] * inv * (w ? w[HALF + c + i] : 1.0f);
+            }
+            if (w && live) {  // NeoX rotation of the pairs (c + i, HALF + c + i)
+#pragma unroll
+                for (int i = 0; i < Q; i++) {
+                    const float a0 = a[i], b0 = b[i];
+                    a[i] = a0 * cs_c[i] - b0 * cs_s[i];
+                    b[i] = a0 * cs_s[i] + b0 * cs_c[i];
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < Q; i += 4) {
+                uint2 oa, ob;
+                *reinterpret_cast<__half2*>(&oa.x) = __floats2half2_rn(a[i], a[i + 1]);
+                *reinterpret_cast<__half2*>(&oa.y) = __floats2half2_rn(a[i + 2], a[i + 3]);
+                *reinterpret_cast<__half2*>(&ob.x) = __floats2half2_rn(b[i], b[i + 1]);
+                *reinterpret_cast<__half2*>(&ob.y) = __floats2half2_rn(b[i + 2], b[i + 3]);
+                *reinterpret_cast<uint2*>(dst + c + i) = oa;
+                *reinterpret_cast<uint2*>(dst + HALF + c + i) = ob;
+            }
         }
     }
 }
 
-// Largest slot count per head dimension: 8 for hd 256 (4 query + 2 + 2 key/value heads), 6 for
-// hd 512 (4 query + 1 + 1).
-constexpr int kMaxSlots256 = 8, kMaxSlots512 = 6;
-
-cudaError_t launch_qkv_norm_rope(const __half* qkv, int ntok, int rows, int heads, int kv_heads, int hd,
-                                      const float* q_w, const float* k_w, const int32_t* positions, const float* rope,
-                                      float eps, __half* q, __half* k, __half* v, cudaStream_t stream) {
-    if (rows <= 0) return cudaSuccess;
+template <int HD, int S>
+static cudaError_t launch_qkv_t(const __half* qkv, int ntok, int rows, int heads, int kv_heads, const float* q_w,
+                                const float* k_w, const int32_t* positions, const float* rope, float eps, __half* q,
+                                __half* k, __half* v, cudaStream_t stream) {
+    // Two tokens per warp once the grid is many waves deep; one keeps small batches spread
+    // over every SM.
+    if (rows >= 8192) {
+        const int blocks = (rows + kRowsPerBlock * 2 - 1) / (kRowsPerBlock * 2);
+        return launch_kernel(k_qkv_norm_rope<HD, S, 2>, dim3(blocks), dim3(256), 0, stream, 1, qkv, ntok, rows, heads,
+                             kv_heads, q_w, k_w, positions, rope, eps, q, k, v);
+    }
     const int blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
-    const int slots = heads + 2 * kv_heads;
-    if (hd == 256 && slots <= kMaxSlots256)
-        CK_LAUNCH(launch_kernel(k_qkv_norm_rope<256, kMaxSlots256>, dim3(blocks), dim3(256), 0, stream, 1, qkv, ntok,
-                                rows, heads, kv_heads, q_w, k_w, positions, rope, eps, q, k, v));
-    else if (hd == 512 && slots <= kMaxSlots512)
-        CK_LAUNCH(launch_kernel(k_qkv_norm_rope<512, kMaxSlots512>, dim3(blocks), dim3(256), 0, stream, 1, qkv, ntok,
-                                rows, heads, kv_heads, q_w, k_w, positions, rope, eps, q, k, v));
-    else
-        return cudaErrorInvalidValue;
-    return cudaGetLastError();
+    return launch_kernel(k_qkv_norm_rope<HD, S, 1>, dim3(blocks), dim3(256), 0, stream, 1, qkv, ntok, rows, heads,
+                         kv_heads, q_w, k_w, positions, rope, eps, q, k, v);
+}
+
+// Head slots per token: heads + 2 kv_heads, 3..8 for head dim 256 and 3..6 for 512 (the
+// loader rejects other layouts).
+cudaError_t launch_qkv_norm_rope(const __half* qkv, int ntok, int rows, int heads, int kv_heads, int hd,
+                                 const float* q_w, const float* k_w, const int32_t* positions, const float* rope,
+                                 float eps, __half* q, __half* k, __half* v, cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+#define QKV_CASE(HD, S)                                                                                         \
+    if (hd == HD && heads + 2 * kv_heads == S)                                                                  \
+        return launch_qkv_t<HD, S>(qkv, ntok, rows, heads, kv_heads, q_w, k_w, positions, rope, eps, q, k, v, stream);
+    QKV_CASE(256, 3)
+    QKV_CASE(256, 4)
+    QKV_CASE(256, 5)
+    QKV_CASE(256, 6)
+    QKV_CASE(256, 7)
+    QKV_CASE(256, 8)
+    QKV_CASE(512, 3)
+    QKV_CASE(512, 4)
+    QKV_CASE(512, 5)
+    QKV_CASE(512, 6)
+#undef QKV_CASE
+    return cudaErrorInvalidValue;
 }
 
 // x = (x + rmsnorm(t) * w_post) * scale, then optionally the next norm of x.
