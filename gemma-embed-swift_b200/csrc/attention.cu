@@ -354,7 +354,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
         const int quad = warp & 3;         // tensor-memory lane quarter of this warp
         const int half = (warp - 2) >> 2;  // which 32 keys of each block, and which 128 O columns
         const int r = quad * 32 + lane;
-        const int rt = r / p.group, rg = r - rt * p.group;  // token and head of this row in a tile
+        const int rt = r / p.group;  // token of this row within a tile (rows are token * G + head)
         const uint32_t lane_base = tmem + (uint32_t(quad * 32) << 16);
         float* red = reinterpret_cast<float*>(smem + kOffRed);
         // The two warps of a quarter meet on named barrier 1 + quad (64 threads).
@@ -374,8 +374,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
             item_keys(w, p, k_start, nblk);
             const int len = int(w.y);
             const int qi = int(w.z) + rt;  // this row's token within its sequence
-            const int h = int(w.w) * p.group + rg;
-            const bool live = r < live_rows && qi < len;
             // Keys this row sees: [row_lo, row_hi) of its sequence.
             const int row_lo = p.hw > 0 ? max(qi - p.hw, 0) : 0;
             const int row_hi = p.hw > 0 ? min(qi + p.hw + 1, len) : len;
@@ -477,28 +475,49 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                 if (ok) {
                     tc_fence_after();
                     const float inv = lt > 0.f ? 1.0f / lt : 0.f;
-                    __half* orow = p.out + ((long(w.x) + qi) * p.heads + h) * long(kTcHd) + half * (kTcHd / 2);
+                    // O leaves through this half's P buffer (free: the item's last PV has run, and
+                    // the next item writes P only after both halves pass its first pair_sync):
+                    // each thread writes its row's 64 columns, then each warp stores 4 rows of
+                    // 128 bytes per instruction.
+                    uint8_t* stg = smem + kOffP + half * kPBytes;
 #pragma unroll 1
-                    for (int c = 0; c < kTcHd / 64; c++) {
-                        uint32_t o[32];
-                        tmem_ld32(lane_base + kTmemO + uint32_t(half * (kTcHd / 2) + c * 32), o);
+                    for (int rd = 0; rd < 2; rd++) {
+                        uint32_t o[64];
+                        const uint32_t col = kTmemO + uint32_t(half * (kTcHd / 2) + rd * 64);
+                        tmem_ld32(lane_base + col, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+                        tmem_ld32(lane_base + col + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
                         tmem_wait_ld();
-                        if (live) {
-                            uint32_t pk[16];
-#pragma unroll
-                            for (int i = 0; i < 16; i++) {
-                                __half2 hv = __floats2half2_rn(__uint_as_float(o[2 * i]) * inv,
-                                                               __uint_as_float(o[2 * i + 1]) * inv);
-                                pk[i] = *reinterpret_cast<uint32_t*>(&hv);
-                            }
-                            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-                            for (int i = 0; i < 4; i++)
-                                dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+                        if (rd == 1) {  // O is read: the next item's first PV may overwrite it
+                            tc_fence_before();
+                            mbar_arrive(o_empty);
                         }
+                        uint8_t* srow = stg + r * 128;
+#pragma unroll
+                        for (int j = 0; j < 8; j++) {
+                            uint32_t pk[4];
+#pragma unroll
+                            for (int e = 0; e < 4; e++) {
+                                __half2 hv = __floats2half2_rn(__uint_as_float(o[8 * j + 2 * e]) * inv,
+                                                               __uint_as_float(o[8 * j + 2 * e + 1]) * inv);
+                                pk[e] = *reinterpret_cast<uint32_t*>(&hv);
+                            }
+                            *reinterpret_cast<uint4*>(srow + ((j ^ (r & 7)) * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        }
+                        __syncwarp();
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const int rr = quad * 32 + i * 4 + (lane >> 3), ch = lane & 7;
+                            const int rrt = rr / p.group, rrg = rr - rrt * p.group;
+                            const int qr = int(w.z) + rrt;
+                            const uint4 val = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((ch ^ (rr & 7)) * 16));
+                            if (rr < live_rows && qr < len) {
+                                __half* dst = p.out + ((long(w.x) + qr) * p.heads + int(w.w) * p.group + rrg) * long(kTcHd) +
+                                              half * (kTcHd / 2) + rd * 64 + ch * 8;
+                                *reinterpret_cast<uint4*>(dst) = val;
+                            }
+                        }
+                        __syncwarp();
                     }
-                    tc_fence_before();
-                    mbar_arrive(o_empty);
                 }
             }
         }
