@@ -306,8 +306,8 @@ def main():
 # one-layer `ncu --set full` capture at config 2 summarised in profiles/layer_config2_ncu_full.md
 # (cold caches: reads include operands a normal run finds in L2).
 NCU_DRAM_BYTES_CONFIG2 = {
-    "gemm_qkv": 36.31e6, "qkv_norm_rope": 59.16e6, "attention_sliding": 53.08e6, "gemm_o": 31.62e6,
-    "residual_norm": 123.39e6, "gemm_gate_up": 36.70e6, "gemm_down": 49.47e6,
+    "gemm_qkv": 35.89e6, "qkv_norm_rope": 56.56e6, "attention_sliding": 52.57e6, "gemm_o": 31.60e6,
+    "residual_norm": 124.52e6, "gemm_gate_up": 37.62e6, "gemm_down": 50.51e6,
 }
 
 
