@@ -226,9 +226,13 @@ cudaError_t launch_qkv_norm_rope(const __half* qkv, int ntok, int rows, int head
 // x = (x + rmsnorm(t) * w_post) * scale, then optionally the next norm of x.
 // CPUReference.swift:239-243, 252-256, 266-269 and Elementwise.metal:260-354.  One warp per
 // row; lane l holds the 8-element groups l, l + 32, ... (W / 256 groups) in registers.
-template <int W>
+// PAIR applies a second residual step (t2, w_post2) to the result before the next norm, so a
+// layer's attention residual can be recomputed (identically: same code, same order) in its FFN
+// residual instead of being stored and reloaded; store_x = false skips the store of x.
+template <int W, bool PAIR>
 __global__ void k_residual_norm(float* __restrict__ x, const __half* __restrict__ t, int rows,
-                                const float* __restrict__ wp, float scale, const float* __restrict__ wn, float eps,
+                                const float* __restrict__ wp, float scale, const __half* __restrict__ t2,
+                                const float* __restrict__ wp2, int store_x, const float* __restrict__ wn, float eps,
                                 __half* __restrict__ h16, float* __restrict__ y32, __half* __restrict__ x16) {
     pdl_wait();
     pdl_launch_if_one_wave();
@@ -239,11 +243,13 @@ __global__ void k_residual_norm(float* __restrict__ x, const __half* __restrict_
     float* xr = x + long(row) * W;
     const __half* tr = t + long(row) * W;
     float tv[G][8], xv[G][8];
-    float ss = 0.f;
+    uint4 t2raw[PAIR ? G : 1];
+    float ss = 0.f, ss_b = 0.f;
 #pragma unroll
     for (int g = 0; g < G; g++) {
         const int c = (lane + 32 * g) * 8;
         const uint4 raw = *reinterpret_cast<const uint4*>(tr + c);
+        if (PAIR) t2raw[g] = *reinterpret_cast<const uint4*>(t2 + long(row) * W + c);
         const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
@@ -257,8 +263,24 @@ __global__ void k_residual_norm(float* __restrict__ x, const __half* __restrict_
         xv[g][0] = a.x; xv[g][1] = a.y; xv[g][2] = a.z; xv[g][3] = a.w;
         xv[g][4] = b.x; xv[g][5] = b.y; xv[g][6] = b.z; xv[g][7] = b.w;
     }
+    if (PAIR) {
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            const __half2* h2 = reinterpret_cast<const __half2*>(&t2raw[g]);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float2 f = __half22float2(h2[i]);
+                ss_b += f.x * f.x + f.y * f.y;
+            }
+        }
+    }
     ss = warp_sum(ss);
     const float inv = 1.0f / sqrtf(ss / float(W) + eps);
+    float inv_b = 0.f;
+    if (PAIR) {
+        ss_b = warp_sum(ss_b);
+        inv_b = 1.0f / sqrtf(ss_b / float(W) + eps);
+    }
     float ss2 = 0.f;
 #pragma unroll
     for (int g = 0; g < G; g++) {
@@ -271,10 +293,25 @@ __global__ void k_residual_norm(float* __restrict__ x, const __half* __restrict_
             float v = xv[g][i] + tv[g][i] * inv * ww[i];
             if (scale != 1.0f) v *= scale;
             xv[g][i] = v;
-            ss2 += v * v;
         }
-        *reinterpret_cast<float4*>(xr + c) = make_float4(xv[g][0], xv[g][1], xv[g][2], xv[g][3]);
-        *reinterpret_cast<float4*>(xr + c + 4) = make_float4(xv[g][4], xv[g][5], xv[g][6], xv[g][7]);
+        if (PAIR) {
+            const float4 u0 = *reinterpret_cast<const float4*>(wp2 + c);
+            const float4 u1 = *reinterpret_cast<const float4*>(wp2 + c + 4);
+            const float uu[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+            const __half2* h2 = reinterpret_cast<const __half2*>(&t2raw[g]);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float2 f = __half22float2(h2[i]);
+                xv[g][2 * i] = xv[g][2 * i] + f.x * inv_b * uu[2 * i];
+                xv[g][2 * i + 1] = xv[g][2 * i + 1] + f.y * inv_b * uu[2 * i + 1];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) ss2 += xv[g][i] * xv[g][i];
+        if (store_x) {
+            *reinterpret_cast<float4*>(xr + c) = make_float4(xv[g][0], xv[g][1], xv[g][2], xv[g][3]);
+            *reinterpret_cast<float4*>(xr + c + 4) = make_float4(xv[g][4], xv[g][5], xv[g][6], xv[g][7]);
+        }
         if (x16) {
             uint4 o;
             __half2* o2 = reinterpret_cast<__half2*>(&o);
@@ -309,20 +346,36 @@ __global__ void k_residual_norm(float* __restrict__ x, const __half* __restrict_
     }
 }
 
+cudaError_t launch_residual(const ResidualStep& r, int rows, int width, cudaStream_t stream) {
+    if (rows <= 0) return cudaSuccess;
+    const int blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
+    const int store_x = r.store_x ? 1 : 0;
+#define RES_CASE(W, P)                                                                                                \
+    if (width == W && (r.t2 != nullptr) == P)                                                                         \
+        return launch_kernel(k_residual_norm<W, P>, dim3(blocks), dim3(256), 0, stream, 1, r.x, r.t, rows, r.w_post,    \
+                             r.scale, r.t2, r.w_post2, store_x, r.w_next, r.eps, r.h16, r.y32, r.x16);
+    RES_CASE(768, false)
+    RES_CASE(768, true)
+    RES_CASE(512, false)
+    RES_CASE(512, true)
+#undef RES_CASE
+    return cudaErrorInvalidValue;
+}
+
 cudaError_t launch_residual_norm(float* x, const __half* t, int rows, int width, const float* w_post, float scale,
                                  const float* w_next, float eps, __half* h16, float* y32, __half* x16,
                                  cudaStream_t stream) {
-    if (rows <= 0) return cudaSuccess;
-    const int blocks = (rows + kRowsPerBlock - 1) / kRowsPerBlock;
-    if (width == 768)
-        CK_LAUNCH(launch_kernel(k_residual_norm<768>, dim3(blocks), dim3(256), 0, stream, 1, x, t, rows, w_post, scale,
-                                w_next, eps, h16, y32, x16));
-    else if (width == 512)
-        CK_LAUNCH(launch_kernel(k_residual_norm<512>, dim3(blocks), dim3(256), 0, stream, 1, x, t, rows, w_post, scale,
-                                w_next, eps, h16, y32, x16));
-    else
-        return cudaErrorInvalidValue;
-    return cudaGetLastError();
+    ResidualStep r;
+    r.x = x;
+    r.t = t;
+    r.w_post = w_post;
+    r.scale = scale;
+    r.w_next = w_next;
+    r.eps = eps;
+    r.h16 = h16;
+    r.y32 = y32;
+    r.x16 = x16;
+    return launch_residual(r, rows, width, stream);
 }
 
 // out = rmsnorm(x * pre) * w over `width`-wide rows (the per-layer-input norm,
@@ -472,8 +525,10 @@ cudaError_t launch_positions(const uint32_t* seqs, int nseq, int32_t* positions,
     return cudaGetLastError();
 }
 
-// out[s][n] = sum_k in[s][k] * w[n][k] in fp32 with an fp32 weight matrix: one warp per n,
-// four input rows per pass so each weight load feeds four independent sums.
+// out[s][n] = sum_k in[s][k] * w[n][k] in fp32 with an fp32 weight matrix: one warp per n and
+// block of kDenseRows input rows (grid.y), four rows per pass so each weight load feeds four
+// independent sums.
+constexpr int kDenseRows = 16;
 __global__ void k_dense_f32(const float* __restrict__ in, int nrows, const float* __restrict__ w, int N, int K,
                             float* __restrict__ out) {
     pdl_wait();
@@ -482,9 +537,11 @@ __global__ void k_dense_f32(const float* __restrict__ in, int nrows, const float
     const int lane = threadIdx.x & 31;
     if (n >= N) return;
     const float* wr = w + long(n) * K;
-    for (int s0 = 0; s0 < nrows; s0 += 4) {
-        const int ns = min(4, nrows - s0);
+    const int s_end = min(nrows, int(blockIdx.y + 1) * kDenseRows);
+    for (int s0 = int(blockIdx.y) * kDenseRows; s0 < s_end; s0 += 4) {
+        const int ns = min(4, s_end - s0);
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 6
         for (int k = lane * 4; k < K; k += 128) {
             const float4 wv = *reinterpret_cast<const float4*>(wr + k);
 #pragma unroll
@@ -507,8 +564,8 @@ cudaError_t launch_dense_f32(const float* in, int nrows, const float* w, int N, 
                              cudaStream_t stream) {
     if (nrows <= 0) return cudaSuccess;
     if (K % 128) return cudaErrorInvalidValue;
-    CK_LAUNCH(launch_kernel(k_dense_f32, dim3((N + kRowsPerBlock - 1) / kRowsPerBlock), dim3(256), 0, stream, 1, in,
-                            nrows, w, N, K, out));
+    const dim3 grid((N + kRowsPerBlock - 1) / kRowsPerBlock, (nrows + kDenseRows - 1) / kDenseRows);
+    CK_LAUNCH(launch_kernel(k_dense_f32, grid, dim3(256), 0, stream, 1, in, nrows, w, N, K, out));
     return cudaGetLastError();
 }
 

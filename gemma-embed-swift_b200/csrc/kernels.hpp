@@ -139,6 +139,24 @@ cudaError_t launch_qkv_norm_rope(const __half* qkv, int ntok, int rows, int head
 cudaError_t launch_residual_norm(float* x, const __half* t, int rows, int width, const float* w_post, float scale,
                                  const float* w_next, float eps, __half* h16, float* y32, __half* x16,
                                  cudaStream_t stream);
+// The general residual step: x' = (x + rmsnorm(t) * w_post) * scale, then, when t2 is set,
+// x' += rmsnorm(t2) * w_post2; x' is stored when store_x, and the next norm of x' goes to h16
+// / y32 when w_next is set (x16 = fp16(x') if set).
+struct ResidualStep {
+    float* x = nullptr;
+    const __half* t = nullptr;
+    const float* w_post = nullptr;
+    float scale = 1.0f;
+    const __half* t2 = nullptr;
+    const float* w_post2 = nullptr;
+    bool store_x = true;
+    const float* w_next = nullptr;
+    float eps = 1e-6f;
+    __half* h16 = nullptr;
+    float* y32 = nullptr;
+    __half* x16 = nullptr;
+};
+cudaError_t launch_residual(const ResidualStep& r, int rows, int width, cudaStream_t stream);
 
 // Per-row RMSNorm of `width`-wide chunks with a pre-scale: out = fp16(rmsnorm(x * pre) * w).
 cudaError_t launch_rmsnorm_rows(const float* x, int rows, int width, float pre, const float* w, float eps, float* out,

@@ -300,7 +300,7 @@ static cudaError_t upload_weight(Device& d, DevWeight& w, const HostWeight& h) {
 
 static void free_workspace(Workspace& ws) {
     for (void* p : {(void*)ws.tokens, (void*)ws.positions, (void*)ws.seqs, (void*)ws.work, (void*)ws.x, (void*)ws.qkv16,
-                    (void*)ws.o16, (void*)ws.y, (void*)ws.ple, (void*)ws.pooled, (void*)ws.chunk_base, (void*)ws.pool_partial, (void*)ws.mid, (void*)ws.out,
+                    (void*)ws.o16, (void*)ws.d16, (void*)ws.y, (void*)ws.ple, (void*)ws.pooled, (void*)ws.chunk_base, (void*)ws.pool_partial, (void*)ws.mid, (void*)ws.out,
                     (void*)ws.h, (void*)ws.x16, (void*)ws.q, (void*)ws.k, (void*)ws.v, (void*)ws.attn, (void*)ws.act,
                     (void*)ws.g})
         if (p) cudaFree(p);
@@ -350,6 +350,7 @@ static cudaError_t ensure_workspace(const Config& c, Device& d, int rows, int se
     chk(A(&ws.x, r * d_));
     chk(A(&ws.qkv16, r * qkvd));
     chk(A(&ws.o16, r * d_));
+    chk(A(&ws.d16, r * d_));
     chk(A(&ws.y, r * d_));
     chk(A(&ws.h, r * d_));
     chk(A(&ws.q, r * qd));
@@ -981,12 +982,31 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
             } else {
                 CK(K("gemm_o", gemm_flops(L.o), gemm_bytes(L.o, 2), [&] { return gemm(*aa, L.o, ws.o16, D, EPI_F16); }),
                    "attention output");
-                CK(K("residual_norm", 0, double(ntok) * D * 12,
-                     [&] {
-                         return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_attn, 1.0f, L.ffn_norm, c.eps, ws.h,
-                                                     nullptr, nullptr, ks);
-                     }),
-                   "post-attention residual");
+                if (c.has_ple) {
+                    CK(K("residual_norm", 0, double(ntok) * D * 12,
+                         [&] {
+                             return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_attn, 1.0f, L.ffn_norm, c.eps,
+                                                         ws.h, nullptr, nullptr, ks);
+                         }),
+                       "post-attention residual");
+                } else {
+                    // The attention residual x1 = x + rmsnorm(t_o) * w feeds only the FFN norm
+                    // here; the FFN residual recomputes it from x and t_o instead of a store
+                    // and a reload (8 + 14 bytes per element instead of 12 + 12).
+                    CK(K("residual_attn", 0, double(ntok) * D * 8,
+                         [&] {
+                             ResidualStep r;
+                             r.x = ws.x;
+                             r.t = ws.o16;
+                             r.w_post = L.post_attn;
+                             r.store_x = false;
+                             r.w_next = L.ffn_norm;
+                             r.eps = c.eps;
+                             r.h16 = ws.h;
+                             return launch_residual(r, rows, D, ks);
+                         }),
+                       "post-attention residual");
+                }
             }
             CK(K("gemm_gate_up", gemm_flops(L.gu), gemm_bytes(L.gu, 1), [&] { return gemm(ws.a_h, L.gu, ws.act, c.ff, EPI_GEGLU); }),
                "gate/up projection");
@@ -1035,12 +1055,21 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
                    "down projection and residual");
             } else {
                 CK(K("gemm_down", gemm_flops(L.down), gemm_bytes(L.down, 2),
-                     [&] { return gemm(ws.a_act, L.down, ws.o16, D, EPI_F16); }),
+                     [&] { return gemm(ws.a_act, L.down, ws.d16, D, EPI_F16); }),
                    "down projection");
-                CK(K("residual_norm", 0, double(ntok) * D * 12,
+                CK(K("residual_ffn", 0, double(ntok) * D * 14,
                      [&] {
-                         return launch_residual_norm(ws.x, ws.o16, rows, D, L.post_ffw, 1.0f, next, c.eps,
-                                                     last ? nullptr : ws.h, last ? ws.y : nullptr, nullptr, ks);
+                         ResidualStep r;
+                         r.x = ws.x;
+                         r.t = ws.o16;
+                         r.w_post = L.post_attn;
+                         r.t2 = ws.d16;
+                         r.w_post2 = L.post_ffw;
+                         r.w_next = next;
+                         r.eps = c.eps;
+                         r.h16 = last ? nullptr : ws.h;
+                         r.y32 = last ? ws.y : nullptr;
+                         return launch_residual(r, rows, D, ks);
                      }),
                    "post-ffn residual");
             }

@@ -50,7 +50,8 @@ struct Workspace {
     uint32_t *seqs = nullptr, *work = nullptr, *chunk_base = nullptr;
     float* pool_partial = nullptr;  // [rows / 256 + seqs][hidden] partial sums of the mean pool
     float *x = nullptr, *y = nullptr, *ple = nullptr;
-    __half* o16 = nullptr;  // fp16 output of the o, down and per-layer projections
+    __half* o16 = nullptr;  // fp16 output of the o (and, with per-layer inputs, down and per-layer) projections
+    __half* d16 = nullptr;  // fp16 output of the down projection, beside o16 until the FFN residual
     float *pooled = nullptr, *mid = nullptr, *out = nullptr;
     __half *qkv16 = nullptr;  // fused q|k|v projection output
     __half *h = nullptr, *x16 = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *act = nullptr,
