@@ -324,12 +324,14 @@ def model_launches(model) -> int:
 
 
 def reduce_max_sum(dist, ms, tokens):
+    """The job's time is the slowest rank's; its work is every rank's tokens."""
     if dist is None:
         return ms, tokens
     import torch
-    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    n = torch.tensor([tokens], dtype=torch.float64, device="cuda")
+    n = torch.tensor([tokens], dtype=torch.float64, device=dev)
     dist.all_reduce(n, op=dist.ReduceOp.SUM)
     return float(t.item()), int(n.item())
 

@@ -76,6 +76,10 @@ TEST_SIGNATURES = {
                                f32p, f32p, ctypes.c_float, f32p, ctypes.c_float, f32p, f32p], ctypes.c_int),
     "ge_test_attention": ([u16p, u16p, u16p, ctypes.c_int32, P(GeSeq), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                            ctypes.c_int32, ctypes.c_int32, u16p], ctypes.c_int),
+    "ge_test_shard": ([P(GeSeq), ctypes.c_int32, ctypes.c_int32, P(ctypes.c_int32)], ctypes.c_int),
+    "ge_test_attention_schedule": ([P(GeSeq), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                    ctypes.c_int32, P(ctypes.c_uint32), ctypes.c_int32, P(ctypes.c_int32),
+                                    P(ctypes.c_int32)], ctypes.c_int),
     "ge_test_last_error": ([], ctypes.c_char_p),
 }
 

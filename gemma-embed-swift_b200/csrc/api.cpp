@@ -17,6 +17,28 @@ int load_model(ge_model* m, const char* path, const ge_load_opts* opts);
 void free_model(ge_model* m);
 }  // namespace ge
 
+namespace ge {
+
+// Sequences per device: longest first onto the least-loaded device, with a cost that counts
+// attention's quadratic term, keeping each device's sequences in their original order.
+std::vector<std::vector<int>> shard_sequences(const ge_seq* seqs, int nseq, int ndev) {
+    std::vector<int> order(nseq);
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return seqs[a].length > seqs[b].length; });
+    std::vector<double> load(ndev, 0.0);
+    std::vector<std::vector<int>> parts(ndev);
+    for (int i : order) {
+        const int dv = int(std::min_element(load.begin(), load.end()) - load.begin());
+        const double n = seqs[i].length;
+        load[dv] += n + n * n / 2048.0;
+        parts[dv].push_back(i);
+    }
+    for (auto& p : parts) std::sort(p.begin(), p.end());
+    return parts;
+}
+
+}  // namespace ge
+
 namespace {
 
 thread_local std::string t_last_error;
@@ -58,24 +80,6 @@ int check_batch(ge_model* m, const int32_t* tokens, const int32_t* positions, in
     return GE_OK;
 }
 
-// Sequences per device: longest first onto the least-loaded device, with a cost that counts
-// attention's quadratic term, keeping each device's sequences in their original order.
-std::vector<std::vector<int>> shard(const ge_seq* seqs, int nseq, int ndev) {
-    std::vector<int> order(nseq);
-    std::iota(order.begin(), order.end(), 0);
-    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return seqs[a].length > seqs[b].length; });
-    std::vector<double> load(ndev, 0.0);
-    std::vector<std::vector<int>> parts(ndev);
-    for (int i : order) {
-        const int dv = int(std::min_element(load.begin(), load.end()) - load.begin());
-        const double n = seqs[i].length;
-        load[dv] += n + n * n / 2048.0;
-        parts[dv].push_back(i);
-    }
-    for (auto& p : parts) std::sort(p.begin(), p.end());
-    return parts;
-}
-
 int forward_packed_locked(ge_model* m, const int32_t* tokens, const int32_t* positions, int32_t ntok, const ge_seq* seqs,
                           int32_t nseq, float* out) {
     const int ndev = int(m->devs.size());
@@ -92,7 +96,7 @@ int forward_packed_locked(ge_model* m, const int32_t* tokens, const int32_t* pos
     }
     // Multi-GPU: each device packs its own share of the sequences, runs it on its own host
     // thread and stream, and its pooled rows go back to their original positions.
-    auto parts = shard(seqs, nseq, ndev);
+    auto parts = ge::shard_sequences(seqs, nseq, ndev);
     std::vector<int> rc(ndev, GE_OK);
     std::vector<std::string> msgs(ndev);
     std::vector<std::thread> th;

@@ -161,6 +161,9 @@ struct ForwardArgs {
 };
 int run_forward(ge_model* m, Device& d, const ForwardArgs& a);
 GraphEntry* find_graph(Device& d, const GraphKey& k);
+// The multi-GPU dispatcher's split of a packed batch: the sequence indices of each device,
+// longest first onto the least-loaded device (cost n + n^2 / 2048), each in original order.
+std::vector<std::vector<int>> shard_sequences(const ge_seq* seqs, int nseq, int ndev);
 void store_graph(Device& d, const GraphKey& k, cudaGraphExec_t exec, int64_t launches);
 void clear_graphs(Device& d);
 int set_error(ge_model* m, int code, const std::string& msg);

@@ -6,6 +6,7 @@
 
 #include "gemma_embed_testing.h"
 #include "kernels.hpp"
+#include "model.hpp"
 
 namespace {
 
@@ -45,6 +46,34 @@ float h2f(uint16_t b) {
 extern "C" {
 
 const char* ge_test_last_error(void) { return t_err.c_str(); }
+
+int ge_test_shard(const ge_seq* seqs, int32_t nseq, int32_t ndev, int32_t* device_of_seq) {
+    if (nseq < 0 || ndev <= 0 || (nseq > 0 && (!seqs || !device_of_seq)))
+        return fail(GE_ERR_INVALID_OPTIONS, "invalid options");
+    const auto parts = ge::shard_sequences(seqs, nseq, ndev);
+    for (int d = 0; d < ndev; d++)
+        for (int i : parts[size_t(d)]) device_of_seq[i] = d;
+    return GE_OK;
+}
+
+int ge_test_attention_schedule(const ge_seq* seqs, int32_t nseq, int32_t kvh, int32_t group, int32_t half_window,
+                               int32_t max_ctas, uint32_t* out, int32_t out_cap, int32_t* ctas, int32_t* words) {
+    if (nseq < 0 || kvh <= 0 || group <= 0 || group > 128 || half_window < 0 || max_ctas <= 0 || !ctas || !words ||
+        (nseq > 0 && !seqs))
+        return fail(GE_ERR_INVALID_OPTIONS, "invalid options");
+    std::vector<uint32_t> pairs;
+    for (int s = 0; s < nseq; s++) {
+        pairs.push_back(seqs[s].start);
+        pairs.push_back(seqs[s].length);
+    }
+    int c = 0;
+    const int need = ge::build_attention_work(pairs.data(), nseq, kvh, group, half_window, max_ctas, nullptr, &c);
+    *ctas = c;
+    *words = need;
+    if (need > out_cap || (need > 0 && !out)) return fail(GE_ERR_INVALID_OPTIONS, "output capacity too small");
+    if (need > 0) ge::build_attention_work(pairs.data(), nseq, kvh, group, half_window, max_ctas, out, nullptr);
+    return GE_OK;
+}
 
 // Host repack of Q8_0 rows [n][k/32 * 34 bytes] into the device planes the loader builds.
 static int upload_weight(const uint8_t* w, int n, int k, DevBuf& dq, DevBuf& ds, DevBuf& dh, ge::DevWeight& W) {

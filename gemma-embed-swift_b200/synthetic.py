@@ -275,8 +275,9 @@ def metadata(arch: Arch) -> list:
     return kv
 
 
-def write_gguf(path: str, arch: Arch, tensors: list, alignment: int = 32) -> None:
-    kvs = metadata(arch)
+def write_gguf(path: str, arch: Arch, tensors: list, alignment: int = 32, kvs: list | None = None) -> None:
+    """GGUF v3 with `arch`'s metadata (or the given key/value records) and `tensors`."""
+    kvs = metadata(arch) if kvs is None else kvs
     head = b"GGUF" + struct.pack("<IQQ", 3, len(tensors), len(kvs)) + b"".join(kvs)
     infos = []
     offset = 0

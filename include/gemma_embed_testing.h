@@ -42,6 +42,21 @@ GE_API int ge_test_attention(const uint16_t* q, const uint16_t* k, const uint16_
                              int32_t nseq, int32_t heads, int32_t kv_heads, int32_t hd, int32_t half_window,
                              uint16_t* out);
 
+/* Host logic, no GPU needed. */
+
+/* The multi-GPU dispatcher's split of a packed batch (ge_forward_packed on a model loaded on
+ * several devices): device_of_seq[i] receives the device index (0..ndev-1) of sequence i. */
+GE_API int ge_test_shard(const ge_seq* seqs, int32_t nseq, int32_t ndev, int32_t* device_of_seq);
+
+/* The tensor-core attention kernel's schedule (head dim 256): items of 128 / group tokens and
+ * one KV head, spread over at most max_ctas CTAs by key blocks under half_window (0: global).
+ * Writes the schedule's words to out (capacity out_cap words): the items as (seq_start,
+ * seq_len, first token, KV head) grouped by CTA, then ctas + 1 offsets.  *ctas and *words
+ * receive the CTA count and the words written. */
+GE_API int ge_test_attention_schedule(const ge_seq* seqs, int32_t nseq, int32_t kv_heads, int32_t group,
+                                      int32_t half_window, int32_t max_ctas, uint32_t* out, int32_t out_cap,
+                                      int32_t* ctas, int32_t* words);
+
 /* Message of the calling thread's last failed ge_test_* call. */
 GE_API const char* ge_test_last_error(void);
 

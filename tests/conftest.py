@@ -39,3 +39,9 @@ def cuda_device():
     major, _ = torch.cuda.get_device_capability(0)
     assert major == 10, "GPU tests need an sm_100 (B200) device"
     return 0
+
+
+@pytest.fixture(scope="session")
+def cuda_available():
+    import torch
+    return torch.cuda.is_available()
