@@ -1,12 +1,15 @@
 """B200 EmbeddingGemma text encoder behind the reference's EmbeddingModel API.
 
-Python mirror of `Sources/GemmaEmbed/EmbeddingModel.swift` and `EmbedOptions.swift` over the
-C ABI of libgemma_embed_cuda.so (include/gemma_embed.h).  Texts are passed pre-tokenised
-(lists of token ids): the tokenizer (`Tokenizer/Tokenizer.swift`) is outside this package.
+Python mirror of `Sources/GemmaEmbed/EmbeddingModel.swift`, `EmbedOptions.swift` and
+`Tokenizer/Tokenizer.swift` over the C ABI of libgemma_embed_cuda.so (include/gemma_embed.h).
+Texts are strings (tokenised by the library's C++ tokenizer from the GGUF vocabulary, behind
+the task prefix of `EmbedOptions.task`) or pre-tokenised lists of token ids.
 
     model = EmbeddingModel.load(path)
-    docs = model.embed([[2, 651, 1], [2, 9, 10, 1]])            # list[Embedding]
-    raw = model.embed_tokens([[2, 651, 1]])                    # pooled, unnormalised [n][768]
+    docs = model.embed(["first document", "second document"])    # list[Embedding]
+    query = model.embed("a question", EmbedOptions(task=TaskPrefix.query()))
+    ids = model.tokenizer.encode("some text")                      # [bos, ..., eos]
+    raw = model.embed_tokens([[2, 651, 1]])                        # pooled, unnormalised [n][768]
 """
 from __future__ import annotations
 
@@ -19,7 +22,7 @@ import numpy as np
 from . import _lib
 
 __all__ = ["EmbeddingModel", "EmbedOptions", "LoadOptions", "Embedding", "EmbeddingProgress", "ModelInfo",
-           "GemmaEmbedError", "TaskPrefix", "ALLOWED_DIMENSIONS"]
+           "GemmaEmbedError", "TaskPrefix", "Tokenizer", "ALLOWED_DIMENSIONS"]
 
 ALLOWED_DIMENSIONS = (768, 512, 256, 128)
 
@@ -45,16 +48,40 @@ class GemmaEmbedError(RuntimeError):
         super().__init__(f"{self.case}: {message}")
 
 
+def _text_out(call) -> bytes:
+    """Runs `call(buffer, cap, &len)` with the library's buffer convention (the full length comes
+    back; a second call gets it all when the first buffer was too small)."""
+    n = ctypes.c_int64(0)
+    buf = ctypes.create_string_buffer(256)
+    call(buf, 256, ctypes.byref(n))
+    if n.value > 256:
+        buf = ctypes.create_string_buffer(int(n.value))
+        call(buf, n.value, ctypes.byref(n))
+    return buf.raw[:n.value]
+
+
 class TaskPrefix:
-    """The instruction prefixes of EmbedOptions.swift:6-31, for callers that tokenise."""
+    """TaskPrefix (EmbedOptions.swift:5-32): each member is the prefix string itself
+    (TaskPrefix.prefix), built by the library's ge_task_prefix."""
+
+    DOCUMENT, QUERY, CLUSTERING, CLASSIFICATION, SIMILARITY, NONE = range(6)
+
+    @staticmethod
+    def prefix(task: int, arg: Optional[str] = None) -> str:
+        L = _lib.lib()
+        a = None if arg is None else arg.encode()
+
+        def call(buf, cap, n):
+            _check(L.ge_task_prefix(task, a, buf, cap, n))
+        return _text_out(call).decode()
 
     @staticmethod
     def document(title: Optional[str] = None) -> str:
-        return f"title: {title or 'none'} | text: "
+        return TaskPrefix.prefix(TaskPrefix.DOCUMENT, title)
 
     @staticmethod
     def query(task: Optional[str] = None) -> str:
-        return f"task: {task or 'search result'} | query: "
+        return TaskPrefix.prefix(TaskPrefix.QUERY, task)
 
     clustering = "task: clustering | query: "
     classification = "task: classification | query: "
@@ -64,11 +91,91 @@ class TaskPrefix:
 
 @dataclass
 class EmbedOptions:
-    """EmbedOptions (EmbedOptions.swift:34-56) without the task prefix, which tokenisation applies."""
+    """EmbedOptions (EmbedOptions.swift:34-56).  `task` is the prefix string (TaskPrefix);
+    it applies to string texts, not to pre-tokenised ones."""
+    task: str = "title: none | text: "
     max_tokens: int = 2048
     dimensions: int = 768
     normalise: bool = True
     batch_size: Optional[int] = None
+
+
+class Tokenizer:
+    """Tokenizer (Tokenizer/Tokenizer.swift:10-328) of a GGUF file, in the library's C++.
+
+    `Tokenizer.load(path)` reads only the file's tokenizer metadata (no weights, no GPU);
+    `EmbeddingModel.tokenizer` is the loaded model's own."""
+
+    def __init__(self, handle, owner=None):
+        self._h = handle
+        self._owner = owner  # the EmbeddingModel that owns a borrowed handle
+        info = _lib.GeTokenizerInfo()
+        _check(_lib.lib().ge_tokenizer_get_info(handle, ctypes.byref(info)))
+        self.bos_id, self.eos_id, self.pad_id = info.bos_id, info.eos_id, info.pad_id
+        self.unknown_id = None if info.unknown_id < 0 else info.unknown_id
+        self.vocabulary_size = info.vocabulary_size
+        self.add_bos, self.add_eos = bool(info.add_bos), bool(info.add_eos)
+
+    @classmethod
+    def load(cls, path: str) -> "Tokenizer":
+        """Tokenizer(gguf:) (Tokenizer.swift:40-56)."""
+        h = ctypes.c_void_p()
+        _check(_lib.lib().ge_tokenizer_load(str(path).encode(), ctypes.byref(h)), None)
+        return cls(h)
+
+    def close(self):
+        if self._h and self._owner is None:
+            _lib.lib().ge_tokenizer_free(self._h)
+        self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def encode(self, text, add_special_tokens: bool = True, parse_special_tokens: bool = False) -> list:
+        """encode(_:addSpecialTokens:parseSpecialTokens:) (Tokenizer.swift:105-117); `text` is a
+        str or UTF-8 bytes."""
+        data = text.encode() if isinstance(text, str) else bytes(text)
+        flags = (1 if add_special_tokens else 0) | (2 if parse_special_tokens else 0)
+        L = _lib.lib()
+        n = ctypes.c_int64(0)
+        cap = len(data) + 8
+        out = np.zeros(cap, dtype=np.int32)
+        _check(L.ge_tokenize(self._h, data, len(data), flags, _ptr(out, ctypes.c_int32), cap, ctypes.byref(n)))
+        if n.value > cap:
+            out = np.zeros(int(n.value), dtype=np.int32)
+            _check(L.ge_tokenize(self._h, data, len(data), flags, _ptr(out, ctypes.c_int32), n.value, ctypes.byref(n)))
+        return out[:n.value].tolist()
+
+    def decode_bytes(self, ids) -> bytes:
+        """decode(_:) (Tokenizer.swift:120-147) as UTF-8 bytes."""
+        a = _i32(ids)
+        L = _lib.lib()
+
+        def call(buf, cap, n):
+            _check(L.ge_detokenize(self._h, _ptr(a, ctypes.c_int32), len(a), buf, cap, n))
+        return _text_out(call)
+
+    def decode(self, ids) -> str:
+        """decode(_:): invalid UTF-8 left by split byte tokens shows as U+FFFD, as
+        String(decoding:as:) does."""
+        return self.decode_bytes(ids).decode("utf-8", errors="replace")
+
+    def piece(self, token_id: int) -> Optional[str]:
+        """piece(_:) (Tokenizer.swift:150-153): None outside the vocabulary."""
+        if not 0 <= token_id < self.vocabulary_size:
+            return None
+        L = _lib.lib()
+
+        def call(buf, cap, n):
+            _check(L.ge_token_piece(self._h, token_id, buf, cap, n))
+        return _text_out(call).decode("utf-8", errors="replace")
+
+    def is_control(self, token_id: int) -> bool:
+        """isControl(_:) (Tokenizer.swift:155-158)."""
+        return bool(_lib.lib().ge_token_is_control(self._h, token_id))
 
 
 @dataclass
@@ -147,6 +254,7 @@ class EmbeddingModel:
 
     def __init__(self, handle, options: LoadOptions):
         self._h = handle
+        self._tokenizer = None
         self.options = options
         info = _lib.GeInfo()
         _check(_lib.lib().ge_info_get(handle, ctypes.byref(info)), handle)
@@ -178,7 +286,20 @@ class EmbeddingModel:
         _check(L.ge_load(str(path).encode(), ctypes.byref(o), ctypes.byref(h)), None)
         return cls(h, options)
 
+    @property
+    def tokenizer(self) -> Tokenizer:
+        """EmbeddingModel.tokenizer (EmbeddingModel.swift:26)."""
+        if self._tokenizer is None:
+            h = _lib.lib().ge_model_tokenizer(self._h)
+            if not h:
+                raise GemmaEmbedError(4, "unsupportedArchitecture: tokenizer model missing")
+            self._tokenizer = Tokenizer(ctypes.c_void_p(h), owner=self)
+        return self._tokenizer
+
     def close(self):
+        if self._tokenizer is not None:
+            self._tokenizer._h = None
+            self._tokenizer = None
         if self._h:
             _lib.lib().ge_free(self._h)
             self._h = None
@@ -259,38 +380,51 @@ class EmbeddingModel:
     # -------------------------------------------------------------- EmbeddingModel API
     def embed(self, texts, options: Optional[EmbedOptions] = None,
               progress: Optional[Callable[[EmbeddingProgress], Optional[bool]]] = None) -> list:
-        """embed(_ texts:options:progress:) (EmbeddingModel.swift:145-175) over token-id lists.
+        """embed(_ texts:options:progress:) (EmbeddingModel.swift:145-175).
 
-        A single list of ints embeds one text and returns one Embedding.  `progress` runs after
+        `texts` is a str (one text, returns one Embedding), a list of str, a list of ints (one
+        pre-tokenised text) or a list of int lists.  Strings get `options.task` in front and
+        are tokenised by the library; token ids are taken as they are.  `progress` runs after
         every batch; returning True cancels the call between batches (GemmaEmbedError
         'cancelled')."""
         options = options or EmbedOptions()
-        single = len(texts) > 0 and np.isscalar(texts[0])
-        seqs = [_i32(texts)] if single else [_i32(t) for t in texts]
-        n = len(seqs)
-        if n == 0:
-            o = _lib.GeEmbedOpts(options.max_tokens, options.dimensions, int(options.normalise),
-                                 options.batch_size or 0)
-            _check(_lib.lib().ge_embed_tokens(self._h, None, None, 0, ctypes.byref(o), None, None, None,
-                                             _lib.PROGRESS_FN(0), None), self._h)
-            return []
-        ptrs = (_lib.i32p * n)(*[_ptr(s, ctypes.c_int32) for s in seqs])
-        lens = np.array([len(s) for s in seqs], dtype=np.int32)
+        if options.batch_size is not None and options.batch_size < 1:
+            raise GemmaEmbedError(9, "invalid options: batchSize must be at least 1")
+        as_text = isinstance(texts, (str, bytes)) or (len(texts) > 0 and isinstance(texts[0], (str, bytes)))
+        single = isinstance(texts, (str, bytes)) or (len(texts) > 0 and np.isscalar(texts[0]) and not as_text)
+        if as_text:
+            items = [texts] if single else list(texts)
+            data = [t.encode() if isinstance(t, str) else bytes(t) for t in items]
+        else:
+            data = [_i32(texts)] if single else [_i32(t) for t in texts]
+        n = len(data)
         dims = options.dimensions
+        o = _lib.GeEmbedOpts(options.max_tokens, dims, int(options.normalise), options.batch_size or 0)
+        L = _lib.lib()
+        if n == 0:
+            _check(L.ge_embed_tokens(self._h, None, None, 0, ctypes.byref(o), None, None, None,
+                                     _lib.PROGRESS_FN(0), None), self._h)
+            return []
         out = np.zeros((n, dims if dims > 0 else 1), dtype=np.float32)
         counts = np.zeros(n, dtype=np.int32)
         trunc = np.zeros(n, dtype=np.int32)
-        if options.batch_size is not None and options.batch_size < 1:
-            raise GemmaEmbedError(9, "invalid options: batchSize must be at least 1")
-        o = _lib.GeEmbedOpts(options.max_tokens, dims, int(options.normalise), options.batch_size or 0)
         cb = _lib.PROGRESS_FN(0)
         if progress is not None:
             def _cb(done, total, tokens, user):
                 return 1 if progress(EmbeddingProgress(done, total, tokens)) else 0
             cb = _lib.PROGRESS_FN(_cb)
-        _check(_lib.lib().ge_embed_tokens(self._h, ptrs, _ptr(lens, ctypes.c_int32), n, ctypes.byref(o),
-                                         _ptr(out, ctypes.c_float), _ptr(counts, ctypes.c_int32),
-                                         _ptr(trunc, ctypes.c_int32), cb, None), self._h)
+        if as_text:
+            ptrs = (ctypes.c_char_p * n)(*data)
+            lens = np.array([len(d) for d in data], dtype=np.int64)
+            _check(L.ge_embed_texts(self._h, ptrs, _ptr(lens, ctypes.c_int64), n, options.task.encode(),
+                                    ctypes.byref(o), _ptr(out, ctypes.c_float), _ptr(counts, ctypes.c_int32),
+                                    _ptr(trunc, ctypes.c_int32), cb, None), self._h)
+        else:
+            ptrs = (_lib.i32p * n)(*[_ptr(s, ctypes.c_int32) for s in data])
+            lens = np.array([len(s) for s in data], dtype=np.int32)
+            _check(L.ge_embed_tokens(self._h, ptrs, _ptr(lens, ctypes.c_int32), n, ctypes.byref(o),
+                                     _ptr(out, ctypes.c_float), _ptr(counts, ctypes.c_int32),
+                                     _ptr(trunc, ctypes.c_int32), cb, None), self._h)
         res = [Embedding(out[i].copy(), int(counts[i]), bool(trunc[i])) for i in range(n)]
         return res[0] if single else res
 

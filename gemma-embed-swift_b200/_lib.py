@@ -44,6 +44,11 @@ class GeKernelTime(ctypes.Structure):
                 ("bytes_per_launch", ctypes.c_double), ("launches_per_forward", ctypes.c_int32)]
 
 
+class GeTokenizerInfo(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("bos_id", "eos_id", "pad_id", "unknown_id", "vocabulary_size",
+                                             "add_bos", "add_eos")]
+
+
 PROGRESS_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p)
 
 # Every entry point of include/gemma_embed.h with its argument and result types.
@@ -66,6 +71,18 @@ SIGNATURES = {
                               ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
     "ge_batches": ([i64p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, i64p, i32p, i32p], ctypes.c_int),
     "ge_finish": ([f32p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, f32p], ctypes.c_int),
+    "ge_tokenizer_load": ([ctypes.c_char_p, P(ctypes.c_void_p)], ctypes.c_int),
+    "ge_tokenizer_free": ([ctypes.c_void_p], None),
+    "ge_model_tokenizer": ([ctypes.c_void_p], ctypes.c_void_p),
+    "ge_tokenizer_get_info": ([ctypes.c_void_p, P(GeTokenizerInfo)], ctypes.c_int),
+    "ge_tokenize": ([ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int64, ctypes.c_uint32, i32p, ctypes.c_int64, i64p],
+                    ctypes.c_int),
+    "ge_detokenize": ([ctypes.c_void_p, i32p, ctypes.c_int64, P(ctypes.c_char), ctypes.c_int64, i64p], ctypes.c_int),
+    "ge_token_piece": ([ctypes.c_void_p, ctypes.c_int32, P(ctypes.c_char), ctypes.c_int64, i64p], ctypes.c_int),
+    "ge_token_is_control": ([ctypes.c_void_p, ctypes.c_int32], ctypes.c_int),
+    "ge_task_prefix": ([ctypes.c_int32, ctypes.c_char_p, P(ctypes.c_char), ctypes.c_int64, i64p], ctypes.c_int),
+    "ge_embed_texts": ([ctypes.c_void_p, P(ctypes.c_char_p), i64p, ctypes.c_int32, ctypes.c_char_p, P(GeEmbedOpts),
+                        f32p, i32p, i32p, PROGRESS_FN, ctypes.c_void_p], ctypes.c_int),
 }
 
 # Kernel-level entry points of include/gemma_embed_testing.h.

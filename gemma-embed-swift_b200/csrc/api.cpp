@@ -5,6 +5,8 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
+#include <memory>
 #include <mutex>
 #include <numeric>
 #include <thread>
@@ -131,6 +133,84 @@ int forward_packed_locked(ge_model* m, const int32_t* tokens, const int32_t* pos
     return GE_OK;
 }
 
+// Option checks of EmbeddingModel.embed (EmbeddingModel.swift:147-153); fills `o` with the
+// defaults overridden by `opts`.
+int check_embed_opts(ge_model* m, const ge_embed_opts* opts, int32_t count, ge_embed_opts& o) {
+    ge_embed_opts_default(&o);
+    if (opts) o = *opts;
+    const ge::Config& c = m->cfg;
+    if (!(o.dimensions == 768 || o.dimensions == 512 || o.dimensions == 256 || o.dimensions == 128) ||
+        o.dimensions > c.out_dim)
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: dimensions must be one of [768, 512, 256, 128]");
+    if (o.max_tokens < 2 || o.max_tokens > c.max_tokens)
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS,
+                             "invalid options: maxTokens must be between 2 and " + std::to_string(c.max_tokens));
+    if (o.batch_size < 0) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: batchSize must be at least 1");
+    if (count < 0) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: negative text count");
+    return GE_OK;
+}
+
+// prepare's truncation (EmbeddingModel.swift:189-196): past max_tokens keep the first
+// max_tokens - 1 ids and end with EOS.
+void truncate_keeping_eos(ge_model* m, const ge_embed_opts& o, std::vector<int32_t>& ids, int32_t* token_counts,
+                          int32_t* truncated, int32_t i) {
+    const bool cut = int64_t(ids.size()) > o.max_tokens;
+    if (cut) {
+        ids.resize(size_t(o.max_tokens - 1));
+        ids.push_back(m->cfg.eos_id);
+    }
+    if (token_counts) token_counts[i] = int32_t(ids.size());
+    if (truncated) truncated[i] = cut ? 1 : 0;
+}
+
+// The batch loop of EmbeddingModel.embed (EmbeddingModel.swift:155-174): batches planned over
+// the prepared lengths, one packed forward each, then finish into the caller's rows.
+int embed_prepared(ge_model* m, const std::vector<std::vector<int32_t>>& prepared, const ge_embed_opts& o, float* out,
+                   ge_progress_fn progress, void* user) {
+    const ge::Config& c = m->cfg;
+    const int32_t count = int32_t(prepared.size());
+    std::vector<int64_t> costs(static_cast<size_t>(count));
+    for (int32_t i = 0; i < count; i++) costs[size_t(i)] = int64_t(prepared[size_t(i)].size());
+    const int64_t budget = m->budget;
+    std::vector<int32_t> ranges(2 * size_t(count));
+    int32_t nr = 0;
+    ge_batches(costs.data(), count, 1, o.batch_size, &budget, ranges.data(), &nr);
+    int32_t done_texts = 0;
+    int64_t done_tokens = 0;
+    std::vector<float> pooled;
+    std::vector<int32_t> toks;
+    std::vector<ge_seq> seqs;
+    for (int32_t r = 0; r < nr; r++) {
+        const int32_t b = ranges[2 * size_t(r)], e = ranges[2 * size_t(r) + 1];
+        toks.clear();
+        seqs.clear();
+        for (int32_t i = b; i < e; i++) {
+            seqs.push_back({uint32_t(toks.size()), uint32_t(prepared[size_t(i)].size())});
+            toks.insert(toks.end(), prepared[size_t(i)].begin(), prepared[size_t(i)].end());
+        }
+        pooled.resize(size_t(e - b) * size_t(c.out_dim));
+        int rc = ge_forward_packed(m, toks.data(), nullptr, int32_t(toks.size()), seqs.data(), int32_t(seqs.size()),
+                                   pooled.data());
+        if (rc) return rc;
+        for (int32_t i = b; i < e; i++)
+            ge_finish(pooled.data() + size_t(i - b) * size_t(c.out_dim), c.out_dim, o.dimensions, o.normalise,
+                      out + size_t(i) * size_t(o.dimensions));
+        done_texts += e - b;
+        done_tokens += int64_t(toks.size());
+        if (progress && progress(done_texts, count, done_tokens, user) != 0 && r + 1 < nr)
+            return ge::set_error(m, GE_ERR_CANCELLED, "embedding was cancelled");
+    }
+    return GE_OK;
+}
+
+// Writes the first min(size, cap) bytes of `s` and its full size (the buffer convention of the
+// tokenizer entry points).
+int copy_out(const std::string& s, char* text, int64_t cap, int64_t* len) {
+    *len = int64_t(s.size());
+    if (cap > 0) memcpy(text, s.data(), size_t(std::min<int64_t>(cap, *len)));
+    return GE_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -166,16 +246,21 @@ int ge_load(const char* path, const ge_load_opts* opts, ge_model** out) {
     if (rc == GE_OK) {
         // One forward over a short sequence initialises every kernel before the first request
         // (EmbeddingModel.swift:111-114).
-        const int32_t warm[4] = {m->cfg.bos_id, 3, 4, m->cfg.eos_id};
-        bool ids_ok = true;
+        std::vector<int32_t> warm;
+        if (m->tokenizer) {
+            static const char kWarm[] = "warm up";
+            m->tokenizer->t.encode(reinterpret_cast<const uint8_t*>(kWarm), sizeof kWarm - 1, true, false, warm);
+        }
+        if (warm.empty()) warm = {m->cfg.bos_id, 3, 4, m->cfg.eos_id};
+        bool ids_ok = int(warm.size()) <= m->cfg.max_tokens;
         for (int32_t t : warm) ids_ok = ids_ok && t >= 0 && t < m->cfg.vocab;
         if (ids_ok) {
-            ge_seq s{0, 4};
+            ge_seq s{0, uint32_t(warm.size())};
             std::vector<float> v(size_t(m->cfg.out_dim));
             for (auto& d : m->devs) {
                 ge::ForwardArgs a;
-                a.tokens = warm;
-                a.ntok = 4;
+                a.tokens = warm.data();
+                a.ntok = int32_t(warm.size());
                 a.seqs = &s;
                 a.nseq = 1;
                 a.out = v.data();
@@ -385,65 +470,167 @@ int ge_embed_tokens(ge_model* m, const int32_t* const* texts, const int32_t* len
                     ge_progress_fn progress, void* user) {
     if (!m) return GE_ERR_INVALID_OPTIONS;
     ge_embed_opts o;
-    ge_embed_opts_default(&o);
-    if (opts) o = *opts;
-    const ge::Config& c = m->cfg;
-    // Option checks of EmbeddingModel.embed (EmbeddingModel.swift:147-153).
-    if (!(o.dimensions == 768 || o.dimensions == 512 || o.dimensions == 256 || o.dimensions == 128) ||
-        o.dimensions > c.out_dim)
-        return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: dimensions must be one of [768, 512, 256, 128]");
-    if (o.max_tokens < 2 || o.max_tokens > c.max_tokens)
-        return ge::set_error(m, GE_ERR_INVALID_OPTIONS,
-                             "invalid options: maxTokens must be between 2 and " + std::to_string(c.max_tokens));
-    if (o.batch_size < 0) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: batchSize must be at least 1");
-    if (count < 0) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: negative text count");
-    if (count == 0) return GE_OK;
+    int rc = check_embed_opts(m, opts, count, o);
+    if (rc || count == 0) return rc;
     if (!texts || !lengths || !out) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: NULL array");
-    // prepare: truncation keeps EOS (EmbeddingModel.swift:189-196).
-    std::vector<std::vector<int32_t>> prepared(count);
+    std::vector<std::vector<int32_t>> prepared(static_cast<size_t>(count));
     for (int32_t i = 0; i < count; i++) {
         if (lengths[i] <= 0 || !texts[i])
             return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: text " + std::to_string(i) + " has no tokens");
-        std::vector<int32_t>& ids = prepared[i];
-        if (lengths[i] > o.max_tokens) {
-            ids.assign(texts[i], texts[i] + (o.max_tokens - 1));
-            ids.push_back(c.eos_id);
-        } else {
-            ids.assign(texts[i], texts[i] + lengths[i]);
-        }
-        if (token_counts) token_counts[i] = int32_t(ids.size());
-        if (truncated) truncated[i] = lengths[i] > o.max_tokens ? 1 : 0;
+        prepared[size_t(i)].assign(texts[i], texts[i] + lengths[i]);
+        truncate_keeping_eos(m, o, prepared[size_t(i)], token_counts, truncated, i);
     }
-    std::vector<int64_t> costs(count);
-    for (int32_t i = 0; i < count; i++) costs[i] = int64_t(prepared[i].size());
-    const int64_t budget = m->budget;
-    std::vector<int32_t> ranges(2 * size_t(count));
-    int32_t nr = 0;
-    ge_batches(costs.data(), count, 1, o.batch_size, &budget, ranges.data(), &nr);
-    int32_t done_texts = 0;
-    int64_t done_tokens = 0;
-    std::vector<float> pooled;
-    for (int32_t r = 0; r < nr; r++) {
-        const int32_t b = ranges[2 * r], e = ranges[2 * r + 1];
-        std::vector<int32_t> toks;
-        std::vector<ge_seq> seqs;
-        for (int32_t i = b; i < e; i++) {
-            seqs.push_back({uint32_t(toks.size()), uint32_t(prepared[i].size())});
-            toks.insert(toks.end(), prepared[i].begin(), prepared[i].end());
+    return embed_prepared(m, prepared, o, out, progress, user);
+}
+
+int ge_embed_texts(ge_model* m, const char* const* texts, const int64_t* lengths, int32_t count, const char* prefix,
+                   const ge_embed_opts* opts, float* out, int32_t* token_counts, int32_t* truncated,
+                   ge_progress_fn progress, void* user) {
+    if (!m) return GE_ERR_INVALID_OPTIONS;
+    ge_embed_opts o;
+    int rc = check_embed_opts(m, opts, count, o);
+    if (rc || count == 0) return rc;
+    if (!texts || !lengths || !out) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: NULL array");
+    if (!m->tokenizer)
+        return ge::set_error(m, GE_ERR_UNSUPPORTED_ARCHITECTURE, "unsupported architecture: tokenizer model missing");
+    for (int32_t i = 0; i < count; i++)
+        if (lengths[i] < 0 || (lengths[i] > 0 && !texts[i]))
+            return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: text " + std::to_string(i) + " is NULL");
+    const ge::Tokenizer& tk = m->tokenizer->t;
+    const std::string pre = prefix ? std::string(prefix) : std::string();
+    std::vector<std::vector<int32_t>> prepared(static_cast<size_t>(count));
+    // prepare (EmbeddingModel.swift:189-196) for every text, spread over host threads in
+    // chunks; each text's ids depend on that text alone.
+    int64_t bytes = 0;
+    for (int32_t i = 0; i < count; i++) bytes += lengths[i] + int64_t(pre.size());
+    const int hw = int(std::max(1u, std::thread::hardware_concurrency()));
+    const int nthreads = int(std::min<int64_t>({int64_t(hw), int64_t(count), std::max<int64_t>(1, bytes / 16384), 64}));
+    std::atomic<int32_t> next{0};
+    constexpr int32_t kChunk = 8;
+    auto work = [&]() {
+        std::string joined;
+        for (;;) {
+            const int32_t b = next.fetch_add(kChunk);
+            if (b >= count) break;
+            for (int32_t i = b; i < std::min(count, b + kChunk); i++) {
+                joined.assign(pre);
+                joined.append(texts[i] ? texts[i] : "", size_t(lengths[i]));
+                tk.encode(reinterpret_cast<const uint8_t*>(joined.data()), joined.size(), true, false, prepared[size_t(i)]);
+            }
         }
-        pooled.resize(size_t(e - b) * c.out_dim);
-        int rc = ge_forward_packed(m, toks.data(), nullptr, int32_t(toks.size()), seqs.data(), int32_t(seqs.size()),
-                                   pooled.data());
-        if (rc) return rc;
-        for (int32_t i = b; i < e; i++)
-            ge_finish(pooled.data() + size_t(i - b) * c.out_dim, c.out_dim, o.dimensions, o.normalise,
-                      out + size_t(i) * o.dimensions);
-        done_texts += e - b;
-        done_tokens += int64_t(toks.size());
-        if (progress && progress(done_texts, count, done_tokens, user) != 0 && r + 1 < nr)
-            return ge::set_error(m, GE_ERR_CANCELLED, "embedding was cancelled");
+    };
+    if (nthreads <= 1) {
+        work();
+    } else {
+        std::vector<std::thread> th;
+        for (int t = 1; t < nthreads; t++) th.emplace_back(work);
+        work();
+        for (auto& t : th) t.join();
     }
+    for (int32_t i = 0; i < count; i++) {
+        if (prepared[size_t(i)].empty())  // no BOS/EOS in the metadata and an empty text
+            return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: text " + std::to_string(i) + " has no tokens");
+        truncate_keeping_eos(m, o, prepared[size_t(i)], token_counts, truncated, i);
+    }
+    return embed_prepared(m, prepared, o, out, progress, user);
+}
+
+int ge_tokenizer_load(const char* path, ge_tokenizer** out) {
+    if (!out) {
+        t_last_error = "invalid options: output handle is NULL";
+        return GE_ERR_INVALID_OPTIONS;
+    }
+    *out = nullptr;
+    if (!path) {
+        t_last_error = "invalid options: weight path is NULL";
+        return GE_ERR_INVALID_OPTIONS;
+    }
+    ge::GgufFile f;
+    ge::GgufError err;
+    std::unique_ptr<ge_tokenizer> tk(new ge_tokenizer);
+    if (f.open(path, err) || tk->t.build(f, err)) {
+        t_last_error = err.message;
+        return err.code;
+    }
+    *out = tk.release();
     return GE_OK;
+}
+
+void ge_tokenizer_free(ge_tokenizer* t) { delete t; }
+
+const ge_tokenizer* ge_model_tokenizer(const ge_model* m) { return m ? m->tokenizer.get() : nullptr; }
+
+int ge_tokenizer_get_info(const ge_tokenizer* t, ge_tokenizer_info* info) {
+    if (!t || !info) return GE_ERR_INVALID_OPTIONS;
+    info->bos_id = t->t.bos_id;
+    info->eos_id = t->t.eos_id;
+    info->pad_id = t->t.pad_id;
+    info->unknown_id = t->t.unknown_id;
+    info->vocabulary_size = t->t.vocabulary_size();
+    info->add_bos = t->t.add_bos ? 1 : 0;
+    info->add_eos = t->t.add_eos ? 1 : 0;
+    return GE_OK;
+}
+
+int ge_tokenize(const ge_tokenizer* t, const char* text, int64_t len, uint32_t flags, int32_t* ids, int64_t cap,
+                int64_t* count) {
+    if (!t || !count || len < 0 || cap < 0 || (len > 0 && !text) || (cap > 0 && !ids)) {
+        t_last_error = "invalid options: NULL argument or negative size";
+        return GE_ERR_INVALID_OPTIONS;
+    }
+    thread_local std::vector<int32_t> v;
+    v.clear();
+    t->t.encode(reinterpret_cast<const uint8_t*>(text), size_t(len), (flags & GE_ENCODE_ADD_SPECIAL) != 0,
+                (flags & GE_ENCODE_PARSE_SPECIAL) != 0, v);
+    *count = int64_t(v.size());
+    if (cap > 0) memcpy(ids, v.data(), size_t(std::min<int64_t>(cap, *count)) * sizeof(int32_t));
+    return GE_OK;
+}
+
+int ge_detokenize(const ge_tokenizer* t, const int32_t* ids, int64_t n, char* text, int64_t cap, int64_t* len) {
+    if (!t || !len || n < 0 || cap < 0 || (n > 0 && !ids) || (cap > 0 && !text)) {
+        t_last_error = "invalid options: NULL argument or negative size";
+        return GE_ERR_INVALID_OPTIONS;
+    }
+    std::string s;
+    t->t.decode(ids, size_t(n), s);
+    return copy_out(s, text, cap, len);
+}
+
+int ge_token_piece(const ge_tokenizer* t, int32_t id, char* text, int64_t cap, int64_t* len) {
+    if (!t || !len || cap < 0 || (cap > 0 && !text)) {
+        t_last_error = "invalid options: NULL argument or negative size";
+        return GE_ERR_INVALID_OPTIONS;
+    }
+    const std::string* p = t->t.piece(id);
+    if (!p) {
+        t_last_error = "invalid options: token id " + std::to_string(id) + " is outside the vocabulary";
+        *len = 0;
+        return GE_ERR_INVALID_OPTIONS;
+    }
+    return copy_out(*p, text, cap, len);
+}
+
+int ge_token_is_control(const ge_tokenizer* t, int32_t id) { return t && t->t.is_control(id) ? 1 : 0; }
+
+int ge_task_prefix(int32_t task, const char* arg, char* text, int64_t cap, int64_t* len) {
+    if (!len || cap < 0 || (cap > 0 && !text)) {
+        t_last_error = "invalid options: NULL argument or negative size";
+        return GE_ERR_INVALID_OPTIONS;
+    }
+    std::string s;
+    switch (task) {
+    case GE_TASK_DOCUMENT: s = "title: " + std::string(arg ? arg : "none") + " | text: "; break;
+    case GE_TASK_QUERY: s = "task: " + std::string(arg ? arg : "search result") + " | query: "; break;
+    case GE_TASK_CLUSTERING: s = "task: clustering | query: "; break;
+    case GE_TASK_CLASSIFICATION: s = "task: classification | query: "; break;
+    case GE_TASK_SIMILARITY: s = "task: sentence similarity | query: "; break;
+    case GE_TASK_NONE: break;
+    default:
+        t_last_error = "invalid options: unknown task " + std::to_string(task);
+        return GE_ERR_INVALID_OPTIONS;
+    }
+    return copy_out(s, text, cap, len);
 }
 
 }  // extern "C"

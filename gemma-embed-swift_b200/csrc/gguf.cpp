@@ -260,6 +260,29 @@ bool GgufFile::get_bool_array(const std::string& key, std::vector<bool>& out) co
     return true;
 }
 
+bool GgufFile::get_bool(const std::string& key, bool& out) const {
+    auto it = metadata.find(key);
+    if (it == metadata.end() || it->second.type != 7) return false;
+    out = it->second.raw[0] != 0;
+    return true;
+}
+
+bool GgufFile::get_string_array(const std::string& key, std::vector<std::string>& out) const {
+    auto it = metadata.find(key);
+    if (it == metadata.end() || it->second.type != 9 || it->second.elem != 8) return false;
+    // The directory walk in open() already checked every element against the file end.
+    const uint8_t* p = it->second.raw;
+    out.clear();
+    out.reserve(it->second.count);
+    for (uint64_t i = 0; i < it->second.count; i++) {
+        uint64_t n;
+        memcpy(&n, p, 8);
+        out.emplace_back(reinterpret_cast<const char*>(p + 8), n);
+        p += 8 + n;
+    }
+    return true;
+}
+
 bool GgufFile::get_string_array_count(const std::string& key, int64_t& out) const {
     auto it = metadata.find(key);
     if (it == metadata.end() || it->second.type != 9 || it->second.elem != 8) return false;

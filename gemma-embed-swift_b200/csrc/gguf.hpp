@@ -64,6 +64,9 @@ public:
     // Integer array (int32/uint32 elements) and bool array accessors.
     bool get_int_array(const std::string& key, std::vector<int32_t>& out) const;
     bool get_bool_array(const std::string& key, std::vector<bool>& out) const;
+    bool get_bool(const std::string& key, bool& out) const;
+    // String array (tokenizer.ggml.tokens, tokenizer.ggml.merges).
+    bool get_string_array(const std::string& key, std::vector<std::string>& out) const;
     // Element count of a string array.
     bool get_string_array_count(const std::string& key, int64_t& out) const;
 

@@ -574,6 +574,19 @@ int load_model(ge_model* m, const char* path, const ge_load_opts* opts) {
                 return set_error(m, le.code, le.msg);
         }
     }
+    // ---- tokenizer (EmbeddingModel.swift:85): a file that names a tokenizer model must carry a
+    // valid gemma4 one; a file without tokenizer.ggml.model still loads for token-id input and
+    // the text entry points report the missing tokenizer.
+    {
+        std::string tm;
+        if (f.get_string("tokenizer.ggml.model", tm)) {
+            std::unique_ptr<ge_tokenizer> tk(new ge_tokenizer);
+            if (tk->t.build(f, ge_err)) return set_error(m, ge_err.code, ge_err.message);
+            if (tk->t.vocabulary_size() != c.vocab)
+                return set_error(m, GE_ERR_INVALID_GGUF, "invalid GGUF file: the tokenizer and token_embd.weight disagree on the vocabulary size");
+            m->tokenizer = std::move(tk);
+        }
+    }
     // ---- host-side repack
     const bool want_f16 = !(m->flags & GE_LOAD_Q8_ONLY);
     std::vector<HostWeight> hw;

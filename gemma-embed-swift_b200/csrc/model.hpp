@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -12,6 +13,7 @@
 #include "gemma_embed.h"
 #include "gguf.hpp"
 #include "kernels.hpp"
+#include "tokenizer.hpp"
 
 namespace ge {
 
@@ -105,6 +107,10 @@ struct Device {
 
 }  // namespace ge
 
+struct ge_tokenizer {
+    ge::Tokenizer t;
+};
+
 struct ge_model {
     ge::Config cfg;
     ge::GgufFile file;
@@ -116,6 +122,7 @@ struct ge_model {
     int64_t file_size = 0;
     std::atomic<int64_t> launches{0};  // kernel launches issued by this model so far
     std::atomic<int64_t> h2d_bytes{0}, d2h_bytes{0};  // host <-> device copies of the forwards so far
+    std::unique_ptr<ge_tokenizer> tokenizer;  // null when the file carries no tokenizer
 };
 
 namespace ge {

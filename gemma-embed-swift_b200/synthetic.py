@@ -231,6 +231,260 @@ def build_tensors(arch: Arch, seed: int) -> list:
     return t
 
 
+# --------------------------------------------------------------------------- tokenizer vocabulary
+# A gemma4-style vocabulary for the synthetic files, laid out like the real one
+# (Sources/GemmaEmbed/Tokenizer/Tokenizer.swift:30-32 token types): control and user-defined
+# tokens first, unused slots, the 256 `<0xXX>` byte tokens, whole newline runs, then the
+# pieces of a byte-pair encoding trained here on seeded synthetic prose, then unused filler up
+# to the model's vocabulary size.  Spaces are U+2581 inside pieces, as in SentencePiece.
+TOKEN_NORMAL, TOKEN_UNKNOWN, TOKEN_CONTROL, TOKEN_USER_DEFINED, TOKEN_UNUSED, TOKEN_BYTE = 1, 2, 3, 4, 5, 6
+SPACE_MARK = "▁"
+SPECIAL_TOKENS = [("<pad>", TOKEN_CONTROL), ("<eos>", TOKEN_CONTROL), ("<bos>", TOKEN_CONTROL),
+                  ("<unk>", TOKEN_UNKNOWN), ("<mask>", TOKEN_USER_DEFINED), ("<start_of_turn>", TOKEN_CONTROL),
+                  ("<end_of_turn>", TOKEN_CONTROL), ("<sep>", TOKEN_USER_DEFINED), ("<sep><sep>", TOKEN_USER_DEFINED)]
+PAD_ID, EOS_ID, BOS_ID, UNK_ID = 0, 1, 2, 3
+UNUSED_HEAD = 64
+NEWLINE_RUNS = 31
+TOKENIZER_MERGES = 3000
+TRAIN_SEED = 20260
+TRAIN_WORDS = 60000
+LEXICON_SEED = 777
+LEXICON_WORDS = 3000
+
+_CONS = ["b", "c", "d", "f", "g", "h", "j", "k", "l", "m", "n", "p", "r", "s", "t", "v", "w", "z",
+         "st", "tr", "pl", "ch", "sh", "th", "br", "gr", "qu"]
+_VOWELS = ["a", "e", "i", "o", "u", "y", "ai", "ou", "ea", "io"]
+_CODAS = ["", "", "", "n", "s", "r", "l", "t", "m", "nd", "st", "ng"]
+_ACCENTED = "éèêàäôöüñøçå"
+_CYRILLIC = "".join(chr(c) for c in range(0x430, 0x44A))
+_SENTENCE_END = [".", ".", ".", "?", "!"]
+_SEPARATORS = [(700, " "), (60, "  "), (140, "\n"), (70, "\n\n"), (20, "\n\n\n"), (10, "\t")]
+
+
+def _lexicon() -> list:
+    rng = SeededRandom(LEXICON_SEED)
+    words = []
+    for _ in range(LEXICON_WORDS):
+        r = rng.next() % 100
+        if r < 6:    # one to three characters of a 160-character CJK block (3-byte UTF-8)
+            words.append("".join(chr(0x4E00 + rng.next() % 160) for _ in range(1 + rng.next() % 3)))
+        elif r < 10:  # Cyrillic (2-byte UTF-8)
+            words.append("".join(_CYRILLIC[rng.next() % len(_CYRILLIC)] for _ in range(2 + rng.next() % 6)))
+        elif r < 13:  # numbers
+            words.append(str(rng.next() % (10 ** (1 + rng.next() % 5))))
+        else:
+            w = "".join(_CONS[rng.next() % len(_CONS)] + _VOWELS[rng.next() % len(_VOWELS)]
+                        for _ in range(1 + rng.next() % 3))
+            w += _CODAS[rng.next() % len(_CODAS)]
+            if rng.next() % 10 == 0:
+                k = rng.next() % len(w)
+                w = w[:k] + _ACCENTED[rng.next() % len(_ACCENTED)] + w[k + 1:]
+            words.append(w)
+    return words
+
+
+_LEX_CACHE: list = []
+
+
+def synthetic_text(seed: int, n_words: int, extra_chars: str = "") -> str:
+    """Seeded prose over a fixed synthetic lexicon with Zipf word frequencies: sentences with
+    capitals, commas, brackets and quotes, separated by single and double spaces, newline runs
+    and tabs.  `extra_chars` are sprinkled after some words (characters outside the trained
+    alphabet exercise the byte fallback)."""
+    import bisect
+    if not _LEX_CACHE:
+        lex = _lexicon()
+        cum, acc = [], 0.0
+        for i in range(len(lex)):
+            acc += 1.0 / (i + 1)
+            cum.append(acc)
+        _LEX_CACHE.extend([lex, cum])
+    lex, cum = _LEX_CACHE
+    rng = SeededRandom(seed)
+    sep_total = sum(w for w, _ in _SEPARATORS)
+    parts = []
+    run, cap = 0, True
+    for i in range(n_words):
+        w = lex[min(bisect.bisect_left(cum, (rng.next() >> 11) / float(1 << 53) * cum[-1]), len(lex) - 1)]
+        if cap and w[0].isalpha():
+            w = w[0].upper() + w[1:]
+        cap = False
+        r = rng.next() % 1000
+        if r < 60:
+            w += ","
+        elif r < 70:
+            w = "(" + w + ")"
+        elif r < 75:
+            w = '"' + w + '"'
+        elif r < 85 and extra_chars:
+            w += extra_chars[rng.next() % len(extra_chars)]
+        parts.append(w)
+        run += 1
+        if i == n_words - 1:
+            break
+        if run >= 4 and rng.next() % 10 == 0:
+            parts.append(_SENTENCE_END[rng.next() % len(_SENTENCE_END)])
+            run, cap = 0, True
+            x = rng.next() % sep_total
+            for weight, sep in _SEPARATORS:
+                if x < weight:
+                    parts.append(sep)
+                    break
+                x -= weight
+        else:
+            parts.append(" ")
+    return "".join(parts)
+
+
+def _training_words(text: str) -> dict:
+    """Word counts for BPE training: newline runs dropped, each remaining segment cut before
+    every run of U+2581, so a word is its leading space marks plus the text up to the next."""
+    import re
+    counts: dict = {}
+    for seg in re.split("\n+", text.replace(" ", SPACE_MARK)):
+        for w in re.findall(f"{SPACE_MARK}*[^{SPACE_MARK}]+|{SPACE_MARK}+$", seg):
+            counts[w] = counts.get(w, 0) + 1
+    return counts
+
+
+def train_bpe(counts: dict, n_merges: int, min_char_count: int = 3):
+    """Byte-pair training over word counts: the alphabet is every character seen at least
+    `min_char_count` times (most frequent first, then by code point); each step merges the
+    most frequent adjacent pair of known symbols (ties: the smaller pair of strings) until
+    `n_merges` merges or no pair occurs twice.  Returns (alphabet, [(left, right), ...])."""
+    import heapq
+    char_count: dict = {}
+    for w, c in counts.items():
+        for ch in w:
+            char_count[ch] = char_count.get(ch, 0) + c
+    alphabet = sorted((ch for ch, c in char_count.items() if c >= min_char_count),
+                      key=lambda ch: (-char_count[ch], ch))
+    known = set(alphabet)
+    keys = sorted(counts)
+    words = [list(w) for w in keys]
+    freq = [counts[w] for w in keys]
+    pairs: dict = {}
+    where: dict = {}
+
+    def account(i, sign, touched):
+        syms = words[i]
+        for a, b in zip(syms, syms[1:]):
+            if a in known and b in known:
+                p = (a, b)
+                pairs[p] = pairs.get(p, 0) + sign * freq[i]
+                touched.add(p)
+                if sign > 0:
+                    where.setdefault(p, set()).add(i)
+
+    touched: set = set()
+    for i in range(len(words)):
+        account(i, 1, touched)
+    heap = [(-c, a, b) for (a, b), c in pairs.items() if c >= 2]
+    heapq.heapify(heap)
+    merges = []
+    while heap and len(merges) < n_merges:
+        negc, a, b = heapq.heappop(heap)
+        if pairs.get((a, b), 0) != -negc:
+            continue
+        merged = a + b
+        merges.append((a, b))
+        known.add(merged)
+        touched = set()
+        for i in sorted(where.pop((a, b), ())):
+            account(i, -1, touched)
+            syms, out, k = words[i], [], 0
+            while k < len(syms):
+                if k + 1 < len(syms) and syms[k] == a and syms[k + 1] == b:
+                    out.append(merged)
+                    k += 2
+                else:
+                    out.append(syms[k])
+                    k += 1
+            words[i] = out
+            account(i, 1, touched)
+        pairs.pop((a, b), None)
+        for p in sorted(touched):
+            c = pairs.get(p, 0)
+            if c >= 2 and p != (a, b):
+                heapq.heappush(heap, (-c, p[0], p[1]))
+    return alphabet, merges
+
+
+_TRAINED: list = []
+
+
+def trained_bpe():
+    """The alphabet and merges every synthetic vocabulary shares (trained once per process)."""
+    if not _TRAINED:
+        text = synthetic_text(TRAIN_SEED, TRAIN_WORDS)
+        _TRAINED.extend(train_bpe(_training_words(text), TOKENIZER_MERGES))
+    return _TRAINED[0], _TRAINED[1]
+
+
+def tokenizer_vocab(vocab_size: int):
+    """(tokens, types, merges) of exactly `vocab_size` entries, or None when the trained
+    vocabulary does not fit.  The trained part does not depend on `vocab_size`, so token ids
+    agree across files of different sizes.  One trained piece is listed twice (the tokenizer
+    maps a piece to its first id)."""
+    alphabet, merges = trained_bpe()
+    tokens, types, seen = [], [], set()
+
+    def add(t, ty):
+        tokens.append(t)
+        types.append(ty)
+        seen.add(t)
+
+    for t, ty in SPECIAL_TOKENS:
+        add(t, ty)
+    for k in range(UNUSED_HEAD):
+        add(f"<unused{k}>", TOKEN_UNUSED)
+    for b in range(256):
+        add(f"<0x{b:02X}>", TOKEN_BYTE)
+    for k in range(1, NEWLINE_RUNS + 1):
+        add("\n" * k, TOKEN_NORMAL)
+    for ch in alphabet:
+        if ch not in seen:
+            add(ch, TOKEN_NORMAL)
+    first = None
+    for a, b in merges:
+        if a + b not in seen:
+            add(a + b, TOKEN_NORMAL)
+            first = first or a + b
+    add(first, TOKEN_NORMAL)
+    if len(tokens) > vocab_size:
+        return None
+    k = UNUSED_HEAD
+    while len(tokens) < vocab_size:
+        add(f"<unused{k}>", TOKEN_UNUSED)
+        k += 1
+    return tokens, types, [f"{a} {b}" for a, b in merges]
+
+
+def tokenizer_metadata(vocab_size: int, add_bos: bool = True, add_eos: bool = True):
+    """GGUF key/value records of the synthetic gemma4 tokenizer, or None (see tokenizer_vocab)."""
+    v = tokenizer_vocab(vocab_size)
+    if v is None:
+        return None
+    tokens, types, merges = v
+
+    def strings(xs):
+        bs = [x.encode() for x in xs]
+        return struct.pack("<IQ", 8, len(bs)) + b"".join(struct.pack("<Q", len(b)) + b for b in bs)
+
+    return [
+        _kv("tokenizer.ggml.model", 8, _str("gemma4")),
+        _kv("tokenizer.ggml.tokens", 9, strings(tokens)),
+        _kv("tokenizer.ggml.token_type", 9, struct.pack("<IQ", 5, len(types)) + np.array(types, np.int32).tobytes()),
+        _kv("tokenizer.ggml.merges", 9, strings(merges)),
+        _kv("tokenizer.ggml.bos_token_id", 4, struct.pack("<I", BOS_ID)),
+        _kv("tokenizer.ggml.eos_token_id", 4, struct.pack("<I", EOS_ID)),
+        _kv("tokenizer.ggml.padding_token_id", 4, struct.pack("<I", PAD_ID)),
+        _kv("tokenizer.ggml.unknown_token_id", 4, struct.pack("<I", UNK_ID)),
+        _kv("tokenizer.ggml.add_bos_token", 7, bytes([1 if add_bos else 0])),
+        _kv("tokenizer.ggml.add_eos_token", 7, bytes([1 if add_eos else 0])),
+    ]
+
+
 # --------------------------------------------------------------------------- GGUF v3 writer
 def _str(s: str) -> bytes:
     b = s.encode()
@@ -266,11 +520,15 @@ def metadata(arch: Arch) -> list:
         _kv(f"{a}.attention.layer_norm_rms_epsilon", 6, struct.pack("<f", arch.eps)),
         _kv(f"{a}.rope.freq_base", 6, struct.pack("<f", arch.rope_global)),
         _kv(f"{a}.rope.freq_base_swa", 6, struct.pack("<f", arch.rope_swa)),
-        _kv("tokenizer.ggml.bos_token_id", 4, struct.pack("<I", 2)),
-        _kv("tokenizer.ggml.eos_token_id", 4, struct.pack("<I", 1)),
     ]
+    tok = tokenizer_metadata(arch.vocab)
+    if tok is not None:
+        return kv + tok
+    # Too small a vocabulary for the trained pieces: placeholder tokens and no tokenizer model.
     toks = [f"<t{i}>".encode() for i in range(arch.vocab)]
     body = b"".join(struct.pack("<Q", len(s)) + s for s in toks)
+    kv.append(_kv("tokenizer.ggml.bos_token_id", 4, struct.pack("<I", BOS_ID)))
+    kv.append(_kv("tokenizer.ggml.eos_token_id", 4, struct.pack("<I", EOS_ID)))
     kv.append(_kv("tokenizer.ggml.tokens", 9, struct.pack("<IQ", 8, arch.vocab) + body))
     return kv
 
@@ -305,7 +563,7 @@ def cache_dir() -> str:
     return d
 
 
-FORMAT_VERSION = 1
+FORMAT_VERSION = 2
 
 
 def model_path(arch: str = "gemma-embedding", seed: int = 0, layers: int | None = None,

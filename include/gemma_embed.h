@@ -63,7 +63,8 @@ typedef struct ge_load_opts {
 #define GE_LOAD_FUSED_RESIDUAL 8u /* fuse each residual step into the projection before it (row clusters of
                                      hidden/256 CTAs exchanging row sums through distributed shared memory) */
 
-/* EmbedOptions (EmbedOptions.swift:34-56) minus the task prefix, which the tokenizer applies. */
+/* EmbedOptions (EmbedOptions.swift:34-56) minus the task prefix, which ge_embed_texts takes
+ * as a string (ge_task_prefix). */
 typedef struct ge_embed_opts {
     int32_t max_tokens; /* default 2048; 2 .. ge_info.max_tokens */
     int32_t dimensions; /* 768, 512, 256 or 128 (Matryoshka prefix) */
@@ -165,6 +166,82 @@ GE_API int ge_profile(ge_model* model, const int32_t* tokens, int32_t ntok, cons
 GE_API int ge_embed_tokens(ge_model* model, const int32_t* const* texts, const int32_t* lengths, int32_t count,
                            const ge_embed_opts* opts, float* out, int32_t* token_counts, int32_t* truncated,
                            ge_progress_fn progress, void* user);
+
+/* ---- Tokenizer (Sources/GemmaEmbed/Tokenizer/Tokenizer.swift) ------------------------------ */
+
+typedef struct ge_tokenizer ge_tokenizer;
+
+/* Tokenizer's public properties (Tokenizer.swift:11-15) and its add-BOS/EOS flags. */
+typedef struct ge_tokenizer_info {
+    int32_t bos_id;
+    int32_t eos_id;
+    int32_t pad_id;
+    int32_t unknown_id;      /* -1 when the file names none (unknownId == nil) */
+    int32_t vocabulary_size;
+    int32_t add_bos;         /* tokenizer.ggml.add_bos_token, default 1 */
+    int32_t add_eos;         /* tokenizer.ggml.add_eos_token, default 0 */
+} ge_tokenizer_info;
+
+#define GE_ENCODE_ADD_SPECIAL 1u   /* encode(addSpecialTokens: true): BOS and EOS as the metadata asks */
+#define GE_ENCODE_PARSE_SPECIAL 2u /* encode(parseSpecialTokens: true): control-token text becomes its id */
+
+/* Tokenizer(gguf:) (Tokenizer.swift:40-56) over a GGUF file's tokenizer metadata alone: no
+ * weights are read and no GPU is touched.  Fails with GE_ERR_UNSUPPORTED_ARCHITECTURE unless
+ * tokenizer.ggml.model is "gemma4", GE_ERR_MISSING_METADATA without tokens, token types,
+ * merges or BOS/EOS ids.  On failure *out is NULL and ge_last_error(NULL) holds the message. */
+GE_API int ge_tokenizer_load(const char* gguf_path, ge_tokenizer** out);
+GE_API void ge_tokenizer_free(ge_tokenizer* tokenizer);
+
+/* EmbeddingModel.tokenizer (EmbeddingModel.swift:26): the loaded model's tokenizer, owned by
+ * the model; NULL when its file carries no tokenizer.ggml.model. */
+GE_API const ge_tokenizer* ge_model_tokenizer(const ge_model* model);
+
+GE_API int ge_tokenizer_get_info(const ge_tokenizer* tokenizer, ge_tokenizer_info* info);
+
+/* encode(_:addSpecialTokens:parseSpecialTokens:) (Tokenizer.swift:105-117) of `len` bytes of
+ * UTF-8.  Sets *count to the full id count and writes the first min(count, cap) ids; a caller
+ * whose buffer was too small calls again with cap >= *count.  `ids` may be NULL when cap is 0.
+ * Safe to call from several threads at once. */
+GE_API int ge_tokenize(const ge_tokenizer* tokenizer, const char* text, int64_t len, uint32_t flags, int32_t* ids,
+                       int64_t cap, int64_t* count);
+
+/* decode(_:) (Tokenizer.swift:120-147): UTF-8 bytes (not NUL-terminated; byte tokens may leave
+ * an incomplete sequence, which the reference's String(decoding:) shows as U+FFFD).  Sets *len
+ * to the full byte count and writes the first min(len, cap) bytes.  Ids outside the vocabulary
+ * are skipped. */
+GE_API int ge_detokenize(const ge_tokenizer* tokenizer, const int32_t* ids, int64_t n, char* text, int64_t cap,
+                         int64_t* len);
+
+/* piece(_:) (Tokenizer.swift:150-153): the vocabulary text of `id`, in the same buffer
+ * convention as ge_detokenize; GE_ERR_INVALID_OPTIONS for an id outside the vocabulary (nil). */
+GE_API int ge_token_piece(const ge_tokenizer* tokenizer, int32_t id, char* text, int64_t cap, int64_t* len);
+
+/* isControl(_:) (Tokenizer.swift:155-158): 1 for a control token, else 0. */
+GE_API int ge_token_is_control(const ge_tokenizer* tokenizer, int32_t id);
+
+/* TaskPrefix (EmbedOptions.swift:5-32). */
+typedef enum ge_task {
+    GE_TASK_DOCUMENT = 0,       /* "title: <arg or none> | text: " */
+    GE_TASK_QUERY = 1,          /* "task: <arg or search result> | query: " */
+    GE_TASK_CLUSTERING = 2,     /* "task: clustering | query: " */
+    GE_TASK_CLASSIFICATION = 3, /* "task: classification | query: " */
+    GE_TASK_SIMILARITY = 4,     /* "task: sentence similarity | query: " */
+    GE_TASK_NONE = 5            /* "" */
+} ge_task;
+
+/* TaskPrefix.prefix (EmbedOptions.swift:22-31): the prefix string of `task`; `arg` (UTF-8,
+ * NUL-terminated, may be NULL) is the document title or the query's task description.  Same
+ * buffer convention as ge_detokenize. */
+GE_API int ge_task_prefix(int32_t task, const char* arg, char* text, int64_t cap, int64_t* len);
+
+/* EmbeddingModel.embed(_:options:progress:) (EmbeddingModel.swift:145-175) on texts: each text
+ * is `prefix` + text (prepare, 189-196: encoded with BOS/EOS as the metadata asks, truncated to
+ * max_tokens keeping EOS), then batched, run and finished as ge_embed_tokens does.  `texts[i]`
+ * holds lengths[i] bytes of UTF-8 (an empty text is allowed); `prefix` is NUL-terminated UTF-8
+ * (ge_task_prefix), NULL for none.  The texts are encoded on several host threads. */
+GE_API int ge_embed_texts(ge_model* model, const char* const* texts, const int64_t* lengths, int32_t count,
+                          const char* prefix, const ge_embed_opts* opts, float* out, int32_t* token_counts,
+                          int32_t* truncated, ge_progress_fn progress, void* user);
 
 /* No counterpart in the reference.  The last stage of the forward -- mean-pool over each
  * sequence, then the dense head (or the output projection) -- for callers that cannot allocate
