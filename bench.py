@@ -10,10 +10,14 @@ including BOS/EOS (Embedding.tokenCount).
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 `value` times K device-resident forwards (ids already in HBM) with CUDA events, max over
-ranks.  `e2e` times the same K steps through the public C ABI call with host buffers
-(ge_forward_packed: host->device ids and positions, device->host pooled vectors inside the
-timed region).  `--impl reference` times the CPU oracle (the restated CPUReference.forward,
-the only runnable form of the reference's path here) on the host cores.
+ranks.  `e2e` times the same K steps through the public API with host buffers
+(EmbeddingModel.embed on the batch's token ids -> ge_embed_tokens: host->device ids,
+device->host pooled vectors inside the timed region).  `e2e_text` does the same from strings
+(EmbeddingModel.embed on texts -> ge_embed_texts, tokenisation with the document prefix
+inside the timed region) on seeded synthetic texts cut to the batch's lengths, and
+`tokenizer` compares the library's tokenizer with the oracle's restatement on one thread.
+`--impl reference` times the CPU oracle (the restated CPUReference.forward, the only
+runnable form of the reference's path here) on the host cores.
 """
 from __future__ import annotations
 
@@ -260,6 +264,25 @@ def main():
     h2d = (info1.host_to_device_bytes - info0.host_to_device_bytes) // a.steps
     d2h = (info1.device_to_host_bytes - info0.device_to_host_bytes) // a.steps
 
+    # ---- end to end from strings: the same lengths as seeded synthetic prose, tokenised inside
+    # the timed region (EmbeddingModel.embed on texts with the default document prefix)
+    tk = model.tokenizer
+    strings = text_batch(synth, tk, [len(q) for q in seqs], seed=1000 + rank)
+    sopts = ge.EmbedOptions(max_tokens=opts.max_tokens, dimensions=256)
+    for _ in range(2):
+        model.embed(strings, sopts)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        sout = model.embed(strings, sopts)
+    t1 = time.perf_counter()
+    barrier()
+    text_tokens = sum(e.token_count for e in sout)
+    et_ms, et_tok = reduce_max_sum(dist, (t1 - t0) * 1000.0, text_tokens * a.steps)
+    e2e_text = {"value": et_tok / (et_ms / 1000.0), "unit": "tokens/s", "tokens_per_step": et_tok // a.steps,
+                "api": "ge_embed_texts (EmbeddingModel.embed on strings), document prefix, 256-d normalised output"}
+    tok_stats = tokenizer_throughput(synth, tk, path) if rank == 0 else None
+
     # ---- per-kernel roofline (rank 0): the kernel class with the largest share of a forward
     pk = peaks()
     roofline = None
@@ -300,6 +323,7 @@ def main():
                            "l2": "working set larger than L2 (fp16 weights 203 MB + ~0.5 GB of activations per step)"},
                 "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "api": "ge_embed_tokens (EmbeddingModel.embed), 256-d normalised output"},
+                "e2e_text": e2e_text, "tokenizer": tok_stats,
                 "gpu_launches": int(launches), "clocks": clock_info, "roofline": roofline, "cpu_baseline": cpu,
                 "latency_ms_p50": pct(step_ms, 50), "latency_ms_p99": pct(step_ms, 99),
                 "kernels": [{k: (round(v, 5) if isinstance(v, float) else v) for k, v in p.items()} for p in prof]}
@@ -320,6 +344,42 @@ NCU_DRAM_BYTES_CONFIG2 = {
 
 
 BATCH_BUDGET = 65536
+
+
+def text_batch(synth, tk, lengths, seed):
+    """Seeded synthetic prose, one text per length, each cut so that with the document prefix
+    and BOS/EOS it encodes to about that many tokens."""
+    prefix = len(tk.encode("title: none | text: ", add_special_tokens=False))
+    out = []
+    for i, n in enumerate(lengths):
+        body = tk.encode(synth.synthetic_text(seed * 1000 + i, n + 16), add_special_tokens=False)
+        out.append(tk.decode(body[:max(1, n - prefix - 2)]))
+    return out
+
+
+def tokenizer_throughput(synth, tk, path, seconds=3.0):
+    """Tokens/s of the library's tokenizer and of the oracle's Python restatement on one thread,
+    over texts unseen by the warm-up (the library keeps a per-thread cache of word ids)."""
+    from oracle.tokenizer import Tokenizer as OracleTokenizer
+    warm = [synth.synthetic_text(7000 + i, 300) for i in range(20)]
+    texts = [synth.synthetic_text(8000 + i, 300) for i in range(200)]
+    for t in warm:
+        tk.encode(t)
+    n, t0 = 0, time.perf_counter()
+    for t in texts:
+        n += len(tk.encode(t))
+    lib_tps = n / (time.perf_counter() - t0)
+    orc = OracleTokenizer.from_gguf(path)
+    n, done, t0 = 0, 0, time.perf_counter()
+    for t in texts:
+        n += len(orc.encode(t))
+        done += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    orc_tps = n / (time.perf_counter() - t0)
+    return {"value": lib_tps, "unit": "tokens/s", "threads": 1, "api": "ge_tokenize",
+            "cpu_baseline": {"value": orc_tps, "unit": "tokens/s", "cores": 1, "kind": "port",
+                            "sample": f"{done} synthetic texts of 300 words"}}
 
 
 def pct(sorted_values, q):

@@ -11,6 +11,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
 #include <numeric>
 
 #include "gemma_embed.h"
@@ -63,14 +64,14 @@ struct Symbol {
     int32_t sym;  // interned string id, -1 when the string is no piece or merge half
 };
 
+// A candidate merge.  `order` = rank << 32 | left index: the reference's min-heap order on
+// (rank, left) (Tokenizer.swift:296-298) as one integer.
 struct Bigram {
-    int32_t rank, left, right, left_length, right_length, result;
+    uint64_t order;
+    int32_t right, left_length, right_length, result;
 };
 
-// Min-heap order on (rank, left index) (Tokenizer.swift:296-298), as a max-heap comparator.
-inline bool heap_after(const Bigram& a, const Bigram& b) {
-    return a.rank > b.rank || (a.rank == b.rank && a.left > b.left);
-}
+inline bool heap_after(const Bigram& a, const Bigram& b) { return a.order > b.order; }
 
 struct Scratch {
     std::vector<uint8_t> escaped;
@@ -83,7 +84,62 @@ Scratch& scratch() {
     return s;
 }
 
+struct WordCache {
+    uint64_t owner = 0;  // instance id of the tokenizer the entries belong to
+    std::unordered_map<std::string, std::vector<int32_t>> map;
+};
+
+WordCache& word_cache() {
+    thread_local WordCache c;
+    return c;
+}
+
+constexpr size_t kWordCacheEntries = 1 << 16;
+
+std::atomic<uint64_t> g_instances{0};
+
+// True when the last character of `s` (split as a word is) is U+2581.
+bool ends_with_space_char(const std::string& s) {
+    size_t off = 0, last = 0, last_len = 0;
+    while (off < s.size()) {
+        const size_t len = std::min(s.size() - off, size_t(utf8_length(uint8_t(s[off]))));
+        last = off;
+        last_len = len;
+        off += len;
+    }
+    return last_len == 3 && memcmp(s.data() + last, kSpace, 3) == 0;
+}
+
 }  // namespace
+
+void FlatMap64::reset(size_t expected) {
+    size_t cap = 16;
+    while (cap < 2 * expected) cap <<= 1;
+    slots_.assign(cap, Slot{kEmpty, 0});
+    mask_ = cap - 1;
+    size_ = 0;
+}
+
+void FlatMap64::grow() {
+    std::vector<Slot> old;
+    old.swap(slots_);
+    reset(old.size());
+    for (const Slot& s : old)
+        if (s.key != kEmpty) insert(s.key, s.value);
+}
+
+bool FlatMap64::insert(uint64_t key, uint64_t value) {
+    if (slots_.empty() || 2 * (size_ + 1) > slots_.size()) grow();
+    for (size_t i = hash(key) & mask_;; i = (i + 1) & mask_) {
+        Slot& s = slots_[i];
+        if (s.key == key) return false;
+        if (s.key == kEmpty) {
+            s = Slot{key, value};
+            size_++;
+            return true;
+        }
+    }
+}
 
 int32_t Tokenizer::intern(const std::string& s) {
     auto it = symbols_.find(s);
@@ -94,14 +150,16 @@ int32_t Tokenizer::intern(const std::string& s) {
     symbol_token_.push_back(p == piece_to_id_.end() ? -1 : p->second);
     // A string no longer than the sequence its lead byte starts can be one character of a
     // word (a shorter one ends a word in mid-sequence).
-    if (!s.empty() && int(s.size()) <= utf8_length(uint8_t(s[0])))
-        char_symbols_.emplace(char_key(reinterpret_cast<const uint8_t*>(s.data()), int(s.size())), id);
+    if (s.size() == 1) byte_symbols_[uint8_t(s[0])] = id;
+    else if (!s.empty() && int(s.size()) <= utf8_length(uint8_t(s[0])))
+        char_symbols_.insert(char_key(reinterpret_cast<const uint8_t*>(s.data()), int(s.size())), uint64_t(id));
     return id;
 }
 
 int32_t Tokenizer::char_symbol(const uint8_t* p, int len) const {
-    auto it = char_symbols_.find(char_key(p, len));
-    return it == char_symbols_.end() ? -1 : it->second;
+    if (len == 1) return byte_symbols_[p[0]];
+    const uint64_t* v = char_symbols_.find(char_key(p, len));
+    return v ? int32_t(*v) : -1;
 }
 
 void Tokenizer::build(std::vector<std::string> tokens, std::vector<int32_t> types, const std::vector<std::string>& merges,
@@ -117,8 +175,11 @@ void Tokenizer::build(std::vector<std::string> tokens, std::vector<int32_t> type
     piece_to_id_.clear();
     symbols_.clear();
     symbol_token_.clear();
-    char_symbols_.clear();
-    merges_.clear();
+    for (int32_t& b : byte_symbols_) b = -1;
+    split_words_ = true;
+    instance_id_ = ++g_instances;
+    char_symbols_.reset(1024);
+    merges_.reset(merges.size());
     specials_.clear();
     piece_to_id_.reserve(pieces_.size());
     for (size_t i = 0; i < pieces_.size(); i++) piece_to_id_.emplace(pieces_[i], int32_t(i));  // first id wins
@@ -127,7 +188,6 @@ void Tokenizer::build(std::vector<std::string> tokens, std::vector<int32_t> type
     for (const std::string& p : pieces_) intern(p);
     // Merge rules "left right", split at the first space after the first byte; the first rank
     // of a repeated pair wins (Tokenizer.swift:75-81).
-    merges_.reserve(merges.size());
     std::string left, right;
     for (size_t r = 0; r < merges.size(); r++) {
         const std::string& m = merges[r];
@@ -137,11 +197,13 @@ void Tokenizer::build(std::vector<std::string> tokens, std::vector<int32_t> type
         left.assign(m, 0, split);
         right.assign(m, split + 1, std::string::npos);
         if (right.empty()) continue;  // an empty half never matches a symbol
+        if (right.size() >= 3 && memcmp(right.data(), kSpace, 3) == 0 && !ends_with_space_char(left))
+            split_words_ = false;  // this merge can join across a word start
         const int32_t a = intern(left), b = intern(right);
         const uint64_t key = pair_key(a, b);
-        if (merges_.count(key)) continue;
+        if (merges_.find(key)) continue;
         const int32_t res = intern(left + right);
-        merges_.emplace(key, Merge{int32_t(r), res});
+        merges_.insert(key, (uint64_t(r) << 32) | uint32_t(res));
     }
     for (int b = 0; b < 256; b++) {
         char name[8];
@@ -256,20 +318,59 @@ void Tokenizer::encode_fragment(const uint8_t* p, size_t n, std::vector<int32_t>
 }
 
 void Tokenizer::encode_word(const uint8_t* w, size_t n, bool all_newlines, std::vector<int32_t>& out) const {
+    if (all_newlines) {
+        auto it = symbols_.find(std::string(reinterpret_cast<const char*>(w), n));
+        const bool whole = it != symbols_.end() && symbol_token_[size_t(it->second)] >= 0;
+        merge_word(w, n, whole ? it->second : -1, out);
+        return;
+    }
+    if (!split_words_) {
+        merge_word(w, n, -1, out);
+        return;
+    }
+    // No merge joins a symbol ending in another character to one starting with U+2581, so
+    // each U+2581 that follows another character starts a word that merges on its own; a
+    // word's ids depend on its bytes alone and are kept in a per-thread cache.
+    WordCache& cache = word_cache();
+    if (cache.owner != instance_id_ || cache.map.size() > kWordCacheEntries) {
+        cache.map.clear();
+        cache.owner = instance_id_;
+    }
+    size_t begin = 0, off = 0;
+    bool prev_space = false;
+    auto flush = [&](size_t end) {
+        if (end == begin) return;
+        std::string key(reinterpret_cast<const char*>(w + begin), end - begin);
+        auto it = cache.map.find(key);
+        if (it == cache.map.end()) {
+            std::vector<int32_t> ids;
+            merge_word(w + begin, end - begin, -1, ids);
+            it = cache.map.emplace(std::move(key), std::move(ids)).first;
+        }
+        out.insert(out.end(), it->second.begin(), it->second.end());
+    };
+    while (off < n) {
+        const size_t len = std::min(n - off, size_t(utf8_length(w[off])));
+        const bool space = len == 3 && w[off] == kSpace[0] && w[off + 1] == kSpace[1] && w[off + 2] == kSpace[2];
+        if (space && !prev_space && off > begin) {
+            flush(off);
+            begin = off;
+        }
+        prev_space = space;
+        off += len;
+    }
+    flush(n);
+}
+
+void Tokenizer::merge_word(const uint8_t* w, size_t n, int32_t whole, std::vector<int32_t>& out) const {
     Scratch& sc = scratch();
     std::vector<Symbol>& syms = sc.symbols;
     std::vector<Bigram>& heap = sc.heap;
     syms.clear();
     heap.clear();
-    bool whole = false;
-    if (all_newlines) {
-        auto it = symbols_.find(std::string(reinterpret_cast<const char*>(w), n));
-        if (it != symbols_.end() && symbol_token_[size_t(it->second)] >= 0) {
-            syms.push_back({0, int32_t(n), -1, -1, it->second});
-            whole = true;
-        }
-    }
-    if (!whole) {
+    if (whole >= 0) {
+        syms.push_back({0, int32_t(n), -1, -1, whole});
+    } else {
         size_t off = 0;
         while (off < n) {
             const int len = int(std::min(n - off, size_t(utf8_length(w[off]))));
@@ -283,9 +384,9 @@ void Tokenizer::encode_word(const uint8_t* w, size_t n, bool all_newlines, std::
         const Symbol& a = syms[size_t(l)];
         const Symbol& b = syms[size_t(r)];
         if (a.sym < 0 || b.sym < 0) return;
-        auto it = merges_.find(pair_key(a.sym, b.sym));
-        if (it == merges_.end()) return;
-        heap.push_back({it->second.rank, l, r, a.length, b.length, it->second.result});
+        const uint64_t* m = merges_.find(pair_key(a.sym, b.sym));
+        if (!m) return;
+        heap.push_back({(*m & 0xFFFFFFFF00000000ull) | uint32_t(l), r, a.length, b.length, int32_t(uint32_t(*m))});
         std::push_heap(heap.begin(), heap.end(), heap_after);
     };
     for (size_t i = 1; i < syms.size(); i++) push(int32_t(i - 1), int32_t(i));
@@ -293,16 +394,17 @@ void Tokenizer::encode_word(const uint8_t* w, size_t n, bool all_newlines, std::
         std::pop_heap(heap.begin(), heap.end(), heap_after);
         const Bigram bg = heap.back();
         heap.pop_back();
-        Symbol& l = syms[size_t(bg.left)];
+        const int32_t left = int32_t(uint32_t(bg.order));
+        Symbol& l = syms[size_t(left)];
         Symbol& r = syms[size_t(bg.right)];
         if (l.length == 0 || r.length == 0 || l.length != bg.left_length || r.length != bg.right_length) continue;
         l.length += r.length;
         l.sym = bg.result;
         r.length = 0;
         l.next = r.next;
-        if (r.next >= 0) syms[size_t(r.next)].prev = bg.left;
-        push(l.prev, bg.left);
-        push(bg.left, l.next);
+        if (r.next >= 0) syms[size_t(r.next)].prev = left;
+        push(l.prev, left);
+        push(left, l.next);
     }
     for (const Symbol& s : syms) {
         if (s.length == 0) continue;

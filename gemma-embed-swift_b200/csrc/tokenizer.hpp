@@ -25,6 +25,39 @@ namespace ge {
 class GgufFile;
 struct GgufError;
 
+// Open-addressing hash table from 64-bit keys to 64-bit values (linear probing, power-of-two
+// capacity, never more than half full).  Keys must not be ~0, the empty marker.
+class FlatMap64 {
+public:
+    void reset(size_t expected);
+    // Inserts (key, value) unless the key is present; returns false when it was.
+    bool insert(uint64_t key, uint64_t value);
+    const uint64_t* find(uint64_t key) const {
+        if (slots_.empty()) return nullptr;
+        for (size_t i = hash(key) & mask_;; i = (i + 1) & mask_) {
+            const Slot& s = slots_[i];
+            if (s.key == key) return &s.value;
+            if (s.key == kEmpty) return nullptr;
+        }
+    }
+    size_t size() const { return size_; }
+
+private:
+    static constexpr uint64_t kEmpty = ~0ull;
+    struct Slot {
+        uint64_t key, value;
+    };
+    static size_t hash(uint64_t k) {
+        k ^= k >> 33;
+        k *= 0xff51afd7ed558ccdull;
+        k ^= k >> 33;
+        return size_t(k);
+    }
+    void grow();
+    std::vector<Slot> slots_;
+    size_t mask_ = 0, size_ = 0;
+};
+
 class Tokenizer {
 public:
     enum TokenType : int32_t { kNormal = 1, kUnknown = 2, kControl = 3, kUserDefined = 4, kUnused = 5, kByte = 6 };
@@ -53,10 +86,6 @@ public:
     bool add_bos = true, add_eos = false;
 
 private:
-    struct Merge {
-        int32_t rank;
-        int32_t result;  // symbol id of left + right
-    };
     struct Special {
         int32_t id;
         std::string text;
@@ -66,6 +95,8 @@ private:
     int32_t char_symbol(const uint8_t* p, int len) const;
     void encode_fragment(const uint8_t* p, size_t n, std::vector<int32_t>& out) const;
     void encode_word(const uint8_t* w, size_t n, bool all_newlines, std::vector<int32_t>& out) const;
+    // The merge loop over one word; `whole` >= 0 makes the word a single symbol.
+    void merge_word(const uint8_t* w, size_t n, int32_t whole, std::vector<int32_t>& out) const;
 
     std::vector<std::string> pieces_;
     std::vector<int32_t> types_;
@@ -74,10 +105,13 @@ private:
     // results -- gets a symbol id; merges are keyed by the two halves' symbol ids.
     std::unordered_map<std::string, int32_t> symbols_;
     std::vector<int32_t> symbol_token_;                // symbol id -> token id, or -1 (not a piece)
-    std::unordered_map<uint64_t, int32_t> char_symbols_;  // one UTF-8 character (1..4 bytes) -> symbol id
-    std::unordered_map<uint64_t, Merge> merges_;      // (left symbol << 32 | right symbol) -> merge
+    int32_t byte_symbols_[256];  // one-byte character -> symbol id, or -1
+    FlatMap64 char_symbols_;     // one UTF-8 character of 2..4 bytes -> symbol id
+    FlatMap64 merges_;           // (left symbol << 32 | right symbol) -> (rank << 32 | result symbol)
     int32_t byte_to_id_[256];
     std::vector<Special> specials_;  // control, user-defined and unknown tokens, longest first
+    bool split_words_ = true;         // no merge joins across a U+2581 that follows another character
+    uint64_t instance_id_ = 0;        // distinguishes tokenizers in the per-thread word cache
 };
 
 }  // namespace ge

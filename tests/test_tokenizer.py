@@ -173,10 +173,15 @@ def _write_vocab(synth, path, tokens, merges, model="gemma4", drop=(), types_len
     synth.write_gguf(path, arch, [], kvs=[r for k, r in kvs if k not in drop])
 
 
-@pytest.fixture(scope="module")
-def edge_pair(ge, synth, tmp_path_factory):
+@pytest.fixture(scope="module", params=["words-split", "merges-cross-words"])
+def edge_pair(ge, synth, tmp_path_factory, request):
+    """The hand-made vocabulary, and a variant whose merges join a symbol to a following
+    U+2581 (the library then cannot encode words separately)."""
     tokens, merges = _edge_vocab()
-    path = str(tmp_path_factory.mktemp("tok") / "edge.gguf")
+    if request.param == "merges-cross-words":
+        tokens = tokens + [("b▁a", 1), ("c▁", 1), ("▁▁", 1)]
+        merges = ["b ▁a", "▁ ▁", "c ▁"] + merges
+    path = str(tmp_path_factory.mktemp("tok") / f"edge-{request.param}.gguf")
     _write_vocab(synth, path, tokens, merges)
     return ge.Tokenizer.load(path), OracleTokenizer.from_gguf(path)
 
@@ -184,11 +189,12 @@ def edge_pair(ge, synth, tmp_path_factory):
 def test_edge_vocabulary_matches_oracle(edge_pair):
     """Merges whose halves or result are not pieces, repeated merges (first rank wins),
     malformed merge lines, a repeated piece (first id wins), missing and lower-case byte
-    tokens, specials that overlap or share a length, and input that is not valid UTF-8."""
+    tokens, specials that overlap or share a length, merges across word starts, and input
+    that is not valid UTF-8."""
     lib, orc = edge_pair
     assert lib.unknown_id is None and orc.unknown_id is None
-    alphabet = [b"a", b"b", b"c", b"x", b"y", b"q", b"r", b" ", b"\n", "é".encode(), b"<", b">", b"A", b"\xf0",
-                b"\xff", b"\xc3", "▁".encode(), b"<ab>", b"<abc>", b"<x>", b"<y>"]
+    alphabet = [b"a", b"b", b"c", b"x", b"y", b"q", b"r", b" ", b" ", b"\n", "é".encode(), b"<", b">", b"A",
+                b"\xf0", b"\xff", b"\xc3", "▁".encode(), b"<ab>", b"<abc>", b"<x>", b"<y>", b" a", b"b a"]
     rng = np.random.default_rng(5)
     for _ in range(3000):
         s = b"".join(alphabet[int(i)] for i in rng.integers(0, len(alphabet), int(rng.integers(0, 24))))
