@@ -338,8 +338,8 @@ def main():
 # one-layer `ncu --set full` capture at config 2 summarised in profiles/layer_config2_ncu_full.md
 # (cold caches: reads include operands a normal run finds in L2).
 NCU_DRAM_BYTES_CONFIG2 = {
-    "gemm_qkv": 35.89e6, "qkv_norm_rope": 56.56e6, "attention_sliding": 52.57e6, "gemm_o": 31.60e6,
-    "residual_norm": 124.52e6, "gemm_gate_up": 37.62e6, "gemm_down": 50.51e6,
+    "gemm_qkv": 35.83e6, "qkv_norm_rope": 57.39e6, "attention_sliding": 53.24e6, "gemm_o": 31.75e6,
+    "residual_attn": 101.38e6, "gemm_gate_up": 39.70e6, "gemm_down": 49.08e6, "residual_ffn": 157.23e6,
 }
 
 
