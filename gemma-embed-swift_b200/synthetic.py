@@ -241,9 +241,12 @@ TOKEN_NORMAL, TOKEN_UNKNOWN, TOKEN_CONTROL, TOKEN_USER_DEFINED, TOKEN_UNUSED, TO
 SPACE_MARK = "▁"
 SPECIAL_TOKENS = [("<pad>", TOKEN_CONTROL), ("<eos>", TOKEN_CONTROL), ("<bos>", TOKEN_CONTROL),
                   ("<unk>", TOKEN_UNKNOWN), ("<mask>", TOKEN_USER_DEFINED), ("<start_of_turn>", TOKEN_CONTROL),
-                  ("<end_of_turn>", TOKEN_CONTROL), ("<sep>", TOKEN_USER_DEFINED), ("<sep><sep>", TOKEN_USER_DEFINED)]
+                  ("<end_of_turn>", TOKEN_CONTROL), ("<sep>", TOKEN_USER_DEFINED), ("<sep><sep>", TOKEN_USER_DEFINED),
+                  # the frames of image and audio rows in a text sequence (Model/InputRow.swift:23-26)
+                  ("<|image>", TOKEN_CONTROL), ("<image|>", TOKEN_CONTROL), ("<|audio>", TOKEN_CONTROL),
+                  ("<audio|>", TOKEN_CONTROL)]
 PAD_ID, EOS_ID, BOS_ID, UNK_ID = 0, 1, 2, 3
-UNUSED_HEAD = 64
+UNUSED_HEAD = 60
 NEWLINE_RUNS = 31
 TOKENIZER_MERGES = 3000
 TRAIN_SEED = 20260
@@ -563,7 +566,7 @@ def cache_dir() -> str:
     return d
 
 
-FORMAT_VERSION = 2
+FORMAT_VERSION = 3
 
 
 def model_path(arch: str = "gemma-embedding", seed: int = 0, layers: int | None = None,
@@ -575,6 +578,92 @@ def model_path(arch: str = "gemma-embedding", seed: int = 0, layers: int | None 
     if not os.path.exists(path):
         write_gguf(path, a, build_tensors(a, seed))
     return path
+
+
+# --------------------------------------------------------------------------- image encoder (mmproj)
+# A gemma4v image encoder file laid out like the real mmproj (tensor names, shapes, storage
+# types and metadata keys of Tests/GemmaEmbedTests/Fixtures/mmproj.json, vision part), with the
+# shapes of BASELINE config 4: 16 layers, hidden 768, 12 heads of 64, MLP 3072, 16x16 patches,
+# projected to the text model's width.
+VISION = dict(hidden=768, layers=16, heads=12, ff=3072, patch=16, positions=10240)
+
+
+def vision_tensors(seed: int, projection_dim: int, hidden: int = 768, layers: int = 16, heads: int = 12,
+                   ff: int = 3072, patch: int = 16, positions: int = 10240) -> list:
+    d, hd, area = hidden, hidden // heads, patch * patch * 3
+    t = []
+    name = "v.patch_embd.weight"
+    w = floats(_tensor_seed(seed, name), d * area, (3.0 / area) ** 0.5)
+    t.append(Tensor(name, [patch, patch, 3, d], GGML_F32, w.astype(np.float32).tobytes()))
+    name = "v.position_embd.weight"
+    w = floats(_tensor_seed(seed, name), d * positions * 2, 0.5)
+    t.append(Tensor(name, [d, positions, 2], GGML_F32, w.astype(np.float32).tobytes()))
+    qk_w = hd ** -0.25
+    for i in range(layers):
+        p = f"v.blk.{i}."
+        t.append(_f32_tensor(p + "ln1.weight", d, seed, 1.0, 0.1))
+        t.append(_q8_tensor(p + "attn_q.weight", d, d, seed, (3.0 / d) ** 0.5))
+        t.append(_q8_tensor(p + "attn_k.weight", d, d, seed, (3.0 / d) ** 0.5))
+        t.append(_q8_tensor(p + "attn_v.weight", d, d, seed, (3.0 / d) ** 0.5))
+        t.append(_q8_tensor(p + "attn_out.weight", d, d, seed, (3.0 / d) ** 0.5))
+        t.append(_f32_tensor(p + "attn_q_norm.weight", hd, seed, qk_w, 0.1))
+        t.append(_f32_tensor(p + "attn_k_norm.weight", hd, seed, qk_w, 0.1))
+        t.append(_f32_tensor(p + "attn_post_norm.weight", d, seed, 1.0, 0.1))
+        t.append(_f32_tensor(p + "ln2.weight", d, seed, 1.0, 0.1))
+        t.append(_q8_tensor(p + "ffn_gate.weight", d, ff, seed, (3.0 / d) ** 0.5))
+        t.append(_q8_tensor(p + "ffn_up.weight", d, ff, seed, (3.0 / d) ** 0.5))
+        t.append(_q8_tensor(p + "ffn_down.weight", ff, d, seed, (3.0 / ff) ** 0.5))
+        t.append(_f32_tensor(p + "ffn_post_norm.weight", d, seed, 1.0, 0.1))
+    t.append(_q8_tensor("mm.input_projection.weight", d, projection_dim, seed, (3.0 / d) ** 0.5))
+    return t
+
+
+def vision_metadata(projection_dim: int, hidden: int = 768, layers: int = 16, heads: int = 12, ff: int = 3072,
+                    patch: int = 16, positions: int = 10240, eps: float = 1e-6) -> list:
+    del positions  # carried by the position table's shape
+    f3 = lambda v: struct.pack("<IQ", 6, 3) + np.array(v, np.float32).tobytes()
+    u32 = lambda v: struct.pack("<I", v)
+    return [
+        _kv("general.architecture", 8, _str("clip")),
+        _kv("general.type", 8, _str("mmproj")),
+        _kv("general.name", 8, _str("synthetic-gemma4v")),
+        _kv("general.alignment", 4, u32(32)),
+        _kv("clip.has_vision_encoder", 7, b"\x01"),
+        _kv("clip.vision.projection_dim", 4, u32(projection_dim)),
+        _kv("clip.vision.image_size", 4, u32(224)),
+        _kv("clip.vision.patch_size", 4, u32(patch)),
+        _kv("clip.vision.embedding_length", 4, u32(hidden)),
+        _kv("clip.vision.feed_forward_length", 4, u32(ff)),
+        _kv("clip.vision.block_count", 4, u32(layers)),
+        _kv("clip.vision.attention.head_count", 4, u32(heads)),
+        _kv("clip.vision.image_mean", 9, f3([0.0, 0.0, 0.0])),
+        _kv("clip.vision.image_std", 9, f3([1.0, 1.0, 1.0])),
+        _kv("clip.vision.projector_type", 8, _str("gemma4v")),
+        _kv("clip.vision.attention.layer_norm_epsilon", 6, struct.pack("<f", eps)),
+    ]
+
+
+def mmproj_path(seed: int = 0, projection_dim: int = 768, layers: int = VISION["layers"],
+                positions: int = VISION["positions"]) -> str:
+    """Path of the synthetic image encoder for (seed, projection width, layers), written on first use."""
+    name = f"mmproj-gemma4v-s{seed}-p{projection_dim}-l{layers}-n{positions}-f{FORMAT_VERSION}.gguf"
+    path = os.path.join(cache_dir(), name)
+    if not os.path.exists(path):
+        kw = dict(VISION, layers=layers, positions=positions)
+        arch = Arch(name="clip", hidden=kw["hidden"], layers=layers, heads=kw["heads"], head_dim_swa=0,
+                    head_dim_global=0, kv_swa=0, kv_global=0, ff=kw["ff"], per_layer=0, out_dim=0, dense_head=0)
+        write_gguf(path, arch, vision_tensors(seed, projection_dim, **kw), kvs=vision_metadata(projection_dim, **kw))
+    return path
+
+
+def synthetic_images(count: int, seed: int, width: int = 768, height: int = 768) -> list:
+    """RGB8 images (height x width x 3, uint8) with pixels uniform in 0..255 from SeededRandom(seed)."""
+    out = []
+    n = width * height * 3
+    for i in range(count):
+        r = draws(seed, n, start=i * n)
+        out.append((r >> np.uint64(56)).astype(np.uint8).reshape(height, width, 3))
+    return out
 
 
 # --------------------------------------------------------------------------- inputs

@@ -27,6 +27,13 @@ class OrInfo(ctypes.Structure):
         ("rope_base", ctypes.c_float * 64)]
 
 
+class OrVisionInfo(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("hidden", "layers", "heads", "head_dim", "ff", "patch", "projection_dim",
+                                             "position_count", "merge")] + [
+        ("eps", ctypes.c_float), ("rope_theta", ctypes.c_float), ("mean", ctypes.c_float * 3),
+        ("std", ctypes.c_float * 3)]
+
+
 def build() -> str:
     subprocess.run(["make", "-s", "-C", HERE], check=True)
     return LIB_PATH
@@ -61,6 +68,19 @@ def lib():
         L.or_seeded_next.restype = ctypes.c_uint64
         L.or_set_threads.argtypes = [ctypes.c_int]
         L.or_threads.restype = ctypes.c_int
+        u8p = P(ctypes.c_uint8)
+        L.or_forward_rows.argtypes = [ctypes.c_void_p, i32p, ctypes.c_int32, f32p, ctypes.c_int64, f32p, TRACE_FN,
+                                      ctypes.c_void_p]
+        L.or_vision_open.argtypes = [ctypes.c_char_p, P(ctypes.c_void_p), ctypes.c_char_p, ctypes.c_int]
+        L.or_vision_get_info.argtypes = [ctypes.c_void_p, P(OrVisionInfo)]
+        L.or_vision_forward.argtypes = [ctypes.c_void_p, f32p, ctypes.c_int32, ctypes.c_int32, f32p, TRACE_FN,
+                                        ctypes.c_void_p]
+        L.or_target_size.argtypes = [ctypes.c_int32] * 5 + [i32p, i32p]
+        L.or_fit_image.argtypes = [u8p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, u8p]
+        L.or_patchify.argtypes = [u8p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, f32p, f32p, f32p]
+        L.or_round_f16.argtypes = [ctypes.c_float]
+        L.or_round_f16.restype = ctypes.c_float
+        L.or_tensor_shape.argtypes = [ctypes.c_void_p, ctypes.c_char_p, i64p, i32p]
         _lib = L
     return _lib
 
@@ -124,12 +144,129 @@ class OracleModel:
             raise OracleError(rc, "forward rejected its input")
         return out
 
+    def forward_rows(self, ids, vectors, trace: dict | None = None) -> np.ndarray:
+        """Pooled vector of one sequence whose ids -(r + 1) are rows r of `vectors` (unscaled)."""
+        toks = np.ascontiguousarray(ids, dtype=np.int32)
+        vec = np.ascontiguousarray(vectors, dtype=np.float32).reshape(-1, self.info.hidden)
+        out = np.zeros(self.info.out_dim, dtype=np.float32)
+        cb = _trace_cb(trace)
+        rc = lib().or_forward_rows(self._h, toks.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)), len(toks),
+                                   vec.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), vec.shape[0],
+                                   out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), cb, None)
+        if rc:
+            raise OracleError(rc, "forward rejected its input")
+        return out
+
     def dequantize_row(self, tensor: str, row: int, width: int) -> np.ndarray:
         out = np.zeros(width, dtype=np.float32)
         rc = lib().or_dequantize_row(self._h, tensor.encode(), row, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), width)
         if rc:
             raise OracleError(rc, f"cannot dequantize {tensor}[{row}]")
         return out
+
+
+def _trace_cb(trace):
+    if trace is None:
+        return TRACE_FN(0)
+
+    def _cb(name, data, n, user):
+        trace[name.decode()] = np.ctypeslib.as_array(data, shape=(n,)).copy()
+    return TRACE_FN(_cb)
+
+
+class OracleVision:
+    """CPUVisionReference over an mmproj file: one image per `forward` call."""
+
+    def __init__(self, path: str):
+        L = lib()
+        h = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(512)
+        rc = L.or_vision_open(path.encode(), ctypes.byref(h), err, 512)
+        if rc:
+            raise OracleError(rc, err.value.decode())
+        self._h = h
+        info = OrVisionInfo()
+        L.or_vision_get_info(h, ctypes.byref(info))
+        self.info = info
+
+    def close(self):
+        if self._h:
+            lib().or_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, patches, grid_x: int, grid_y: int, trace: dict | None = None) -> np.ndarray:
+        """The projected rows ([tokens][projection_dim]) of one prepared image."""
+        pt = np.ascontiguousarray(patches, dtype=np.float32)
+        m = self.info.merge
+        out = np.zeros(((grid_x // m) * (grid_y // m), self.info.projection_dim), dtype=np.float32)
+        cb = _trace_cb(trace)
+        rc = lib().or_vision_forward(self._h, pt.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), grid_x, grid_y,
+                                     out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), cb, None)
+        if rc:
+            raise OracleError(rc, "vision forward rejected its input")
+        return out
+
+    def prepare(self, rgb, max_image_tokens: int = 256):
+        """ImagePreprocessor.prepare on a decoded image: (patches, grid_x, grid_y)."""
+        i = self.info
+        align = i.patch * i.merge
+        h, w = rgb.shape[:2]
+        tw, th = target_size(w, h, align, 70 * align * align, max_image_tokens * align * align)
+        img = fit_image(rgb, tw, th)
+        return patchify(img, i.patch, list(i.mean), list(i.std)), tw // i.patch, th // i.patch
+
+
+def target_size(width, height, alignment, min_pixels, max_pixels):
+    tw, th = ctypes.c_int32(0), ctypes.c_int32(0)
+    lib().or_target_size(width, height, alignment, min_pixels, max_pixels, ctypes.byref(tw), ctypes.byref(th))
+    return tw.value, th.value
+
+
+def fit_image(rgb, tw: int, th: int) -> np.ndarray:
+    a = np.ascontiguousarray(rgb, dtype=np.uint8)
+    out = np.zeros((th, tw, 3), dtype=np.uint8)
+    u8 = ctypes.POINTER(ctypes.c_uint8)
+    lib().or_fit_image(a.ctypes.data_as(u8), a.shape[1], a.shape[0], tw, th, out.ctypes.data_as(u8))
+    return out
+
+
+def patchify(rgb, patch: int, mean, std) -> np.ndarray:
+    a = np.ascontiguousarray(rgb, dtype=np.uint8)
+    h, w = a.shape[:2]
+    out = np.zeros(((h // patch) * (w // patch), 3 * patch * patch), dtype=np.float32)
+    mn = np.array(mean, np.float32)
+    sd = np.array(std, np.float32)
+    f32 = ctypes.POINTER(ctypes.c_float)
+    lib().or_patchify(a.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), w, h, patch, mn.ctypes.data_as(f32),
+                      sd.ctypes.data_as(f32), out.ctypes.data_as(f32))
+    return out
+
+
+def tensor(handle, name: str) -> np.ndarray:
+    """A whole tensor of an open oracle file, dequantised, as [rows][contiguous dimension]."""
+    shape = np.zeros(4, np.int64)
+    nd = ctypes.c_int32(0)
+    rc = lib().or_tensor_shape(handle, name.encode(), shape.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
+                               ctypes.byref(nd))
+    if rc:
+        raise OracleError(rc, f"no tensor {name}")
+    cols = int(shape[0])
+    rows = int(np.prod(shape)) // cols
+    out = np.zeros((rows, cols), np.float32)
+    f32 = ctypes.POINTER(ctypes.c_float)
+    for r in range(rows):
+        lib().or_dequantize_row(handle, name.encode(), r, out[r].ctypes.data_as(f32), cols)
+    return out
+
+
+def round_f16(x: float) -> float:
+    return lib().or_round_f16(x)
 
 
 def matmul(x, w):

@@ -60,6 +60,7 @@ struct or_model {
     float* rope[MAX_LAYERS]; /* per layer (shared by head dim and base) */
     int rope_owner[MAX_LAYERS];
     float out_scale[MAX_LAYERS];
+    or_vinfo vinfo; /* an mmproj file opened by or_vision_open */
 };
 
 static int set_err(char* err, int errlen, int code, const char* fmt, ...) {
@@ -341,6 +342,14 @@ int or_dequantize_row(or_model* m, const char* name, int64_t row, float* out, in
     if (!t) return OR_ERR_MISSING_TENSOR;
     if (row < 0 || row >= tensor_rows(t) || n < tensor_cols(t)) return OR_ERR_INVALID_OPTIONS;
     dequant_row(t, row, out);
+    return OR_OK;
+}
+
+int or_tensor_shape(or_model* m, const char* name, int64_t* shape, int32_t* ndim) {
+    tensor_t* t = find_tensor(m, name);
+    if (!t) return OR_ERR_MISSING_TENSOR;
+    *ndim = t->ndim;
+    for (int i = 0; i < 4; i++) shape[i] = i < t->ndim ? t->shape[i] : 1;
     return OR_OK;
 }
 
@@ -707,16 +716,28 @@ static tensor_t* layer_tensor(or_model* m, int l, const char* suffix) {
  * same without lines 206-210 and 259-270, and the pooled mean of rmsnorm(x, output_norm)
  * goes through dense_2 then dense_3. */
 int or_forward(or_model* m, const int32_t* tokens, int32_t T, float* pooled, or_trace_fn tr, void* user) {
+    return or_forward_rows(m, tokens, T, NULL, 0, pooled, tr, user);
+}
+
+/* A token id below zero, -(r + 1), is row r of `vectors` ([vector_rows][hidden]), entered into
+ * the residual stream unscaled (InputRow.vector, CPUReference.swift:191-202). */
+int or_forward_rows(or_model* m, const int32_t* tokens, int32_t T, const float* vectors, int64_t vector_rows,
+                    float* pooled, or_trace_fn tr, void* user) {
     const or_info* I = &m->info;
     const int64_t d = I->hidden, ff = I->ff, pl = I->per_layer, L = I->layers;
     const float eps = I->eps;
     if (T <= 0 || T > I->max_tokens) return OR_ERR_INVALID_OPTIONS;
     for (int t = 0; t < T; t++)
-        if (tokens[t] < 0 || tokens[t] >= I->vocab) return OR_ERR_INVALID_OPTIONS;
+        if (tokens[t] >= I->vocab || (tokens[t] < 0 && (int64_t)(-(int64_t)tokens[t] - 1) >= vector_rows))
+            return OR_ERR_INVALID_OPTIONS;
     char name[64];
     float* x = (float*)malloc((size_t)(T * d) * 4);
     tensor_t* emb = find_tensor(m, "token_embd.weight");
     for (int64_t t = 0; t < T; t++) {
+        if (tokens[t] < 0) {
+            memcpy(x + t * d, vectors + (-(int64_t)tokens[t] - 1) * d, (size_t)d * 4);
+            continue;
+        }
         dequant_row(emb, tokens[t], x + t * d);
         for (int64_t i = 0; i < d; i++) x[t * d + i] *= m->embedding_scale;
     }
@@ -888,4 +909,467 @@ uint64_t or_seeded_next(uint64_t* state) {
     z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
     z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
     return z ^ (z >> 31);
+}
+
+/* ------------------------------------------------------------------ vision tower */
+static int kv_string_is(const kv_t* kv, const char* want) {
+    if (!kv || kv->type != 8) return 0;
+    uint64_t n;
+    memcpy(&n, kv->raw, 8);
+    return n == strlen(want) && memcmp(kv->raw + 8, want, n) == 0;
+}
+
+static void kv_string_copy(const kv_t* kv, char* out, size_t cap) {
+    out[0] = 0;
+    if (!kv || kv->type != 8) return;
+    uint64_t n;
+    memcpy(&n, kv->raw, 8);
+    if (n >= cap) n = cap - 1;
+    memcpy(out, kv->raw + 8, n);
+    out[n] = 0;
+}
+
+/* VisionConfig.init (VisionConfig.swift:42-81). */
+static int read_vision_config(or_model* m, char* err, int errlen) {
+    char got[64];
+    const kv_t* a = find_kv(m, "general.architecture");
+    if (!kv_string_is(a, "clip")) {
+        kv_string_copy(a, got, sizeof got);
+        return set_err(err, errlen, OR_ERR_INVALID_GGUF, "image encoder architecture is '%s', expected clip", got);
+    }
+    const kv_t* pr = find_kv(m, "clip.vision.projector_type");
+    if (!kv_string_is(pr, "gemma4v")) {
+        kv_string_copy(pr, got, sizeof got);
+        return set_err(err, errlen, OR_ERR_INVALID_GGUF, "image projector is '%s', expected gemma4v", got);
+    }
+    or_vinfo* V = &m->vinfo;
+#define VINT(dst, k)                                                                                            \
+    do {                                                                                                        \
+        const kv_t* kv_ = find_kv(m, "clip.vision." k);                                                         \
+        int64_t v_;                                                                                             \
+        if (!kv_ || !kv_int(kv_, &v_)) return set_err(err, errlen, OR_ERR_MISSING_METADATA, "weight file lacks metadata key clip.vision." k); \
+        dst = (int32_t)v_;                                                                                      \
+    } while (0)
+    const kv_t* e = find_kv(m, "clip.vision.attention.layer_norm_epsilon");
+    if (!e || !kv_float(e, &V->eps))
+        return set_err(err, errlen, OR_ERR_MISSING_METADATA, "weight file lacks metadata key clip.vision.attention.layer_norm_epsilon");
+    VINT(V->hidden, "embedding_length");
+    VINT(V->heads, "attention.head_count");
+    if (V->heads <= 0 || V->hidden % V->heads)
+        return set_err(err, errlen, OR_ERR_INVALID_GGUF, "vision width %d does not split into %d heads", V->hidden, V->heads);
+    VINT(V->layers, "block_count");
+    VINT(V->patch, "patch_size");
+    VINT(V->projection_dim, "projection_dim");
+    VINT(V->ff, "feed_forward_length");
+#undef VINT
+    const char* fk[2] = {"clip.vision.image_mean", "clip.vision.image_std"};
+    float* fd[2] = {V->mean, V->std};
+    for (int i = 0; i < 2; i++) {
+        const kv_t* kv = find_kv(m, fk[i]);
+        if (!kv || kv->type != 9 || kv->elem != 6 || kv->count != 3)
+            return set_err(err, errlen, OR_ERR_MISSING_METADATA, "weight file lacks metadata key %s", fk[i]);
+        memcpy(fd[i], kv->raw, 12);
+    }
+    if (V->layers <= 0 || V->layers > MAX_LAYERS)
+        return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: %d vision layers", V->layers);
+    V->head_dim = V->hidden / V->heads;
+    V->merge = 3;            /* VisionConfig.swift:29-33: fixed by llama.cpp for gemma4v */
+    V->rope_theta = 100.0f;
+    return OR_OK;
+}
+
+/* VisionWeights.init's shape and type checks (VisionWeights.swift:37-83). */
+static int vision_tensor(or_model* m, const char* name, int nd, const int64_t* shape, int types_mask, char* err,
+                         int errlen) {
+    tensor_t* t = find_tensor(m, name);
+    if (!t) return set_err(err, errlen, OR_ERR_MISSING_TENSOR, "weight file lacks tensor %s", name);
+    if (shape) {
+        int ok = t->ndim == nd;
+        for (int i = 0; ok && i < nd; i++) ok = t->shape[i] == shape[i];
+        if (!ok) return set_err(err, errlen, OR_ERR_SHAPE_MISMATCH, "tensor %s has an unexpected shape", name);
+    }
+    int bit = t->type == T_F32 ? 1 : t->type == T_F16 ? 2 : t->type == T_Q8_0 ? 4 : t->type == T_BF16 ? 8 : 0;
+    if (!(bit & types_mask))
+        return set_err(err, errlen, OR_ERR_UNSUPPORTED_TENSOR_TYPE, "tensor %s uses unsupported storage type %u", name, t->type);
+    return OR_OK;
+}
+
+static int check_vision_weights(or_model* m, char* err, int errlen) {
+    const or_vinfo* V = &m->vinfo;
+    const int64_t d = V->hidden, p = V->patch, ff = V->ff, hd = V->head_dim;
+    const int ANY = 1 | 2 | 4 | 8, F32 = 1;
+    int rc;
+    int64_t s4[4] = {p, p, 3, d};
+    if ((rc = vision_tensor(m, "v.patch_embd.weight", 4, s4, 1 | 2, err, errlen))) return rc;
+    if ((rc = vision_tensor(m, "v.position_embd.weight", 0, NULL, F32, err, errlen))) return rc;
+    tensor_t* pos = find_tensor(m, "v.position_embd.weight");
+    if (pos->ndim != 3 || pos->shape[0] != d || pos->shape[2] != 2 || pos->shape[1] <= 0)
+        return set_err(err, errlen, OR_ERR_INVALID_GGUF, "v.position_embd.weight has an unexpected shape");
+    m->vinfo.position_count = (int32_t)pos->shape[1];
+    int64_t sp[2] = {d, V->projection_dim};
+    if ((rc = vision_tensor(m, "mm.input_projection.weight", 2, sp, ANY, err, errlen))) return rc;
+    char name[128];
+    struct { const char* suffix; int nd; int64_t s0, s1; int types; } L[] = {
+        {"ln1.weight", 1, d, 0, F32},          {"attn_q.weight", 2, d, d, ANY},       {"attn_k.weight", 2, d, d, ANY},
+        {"attn_v.weight", 2, d, d, ANY},       {"attn_out.weight", 2, d, d, ANY},     {"attn_q_norm.weight", 1, hd, 0, F32},
+        {"attn_k_norm.weight", 1, hd, 0, F32}, {"attn_post_norm.weight", 1, d, 0, F32}, {"ln2.weight", 1, d, 0, F32},
+        {"ffn_gate.weight", 2, d, ff, ANY},    {"ffn_up.weight", 2, d, ff, ANY},      {"ffn_down.weight", 2, ff, d, ANY},
+        {"ffn_post_norm.weight", 1, d, 0, F32},
+    };
+    for (int l = 0; l < V->layers; l++)
+        for (size_t i = 0; i < sizeof L / sizeof L[0]; i++) {
+            snprintf(name, sizeof name, "v.blk.%d.%s", l, L[i].suffix);
+            int64_t sh[2] = {L[i].s0, L[i].s1};
+            if ((rc = vision_tensor(m, name, L[i].nd, sh, L[i].types, err, errlen))) return rc;
+        }
+    return OR_OK;
+}
+
+int or_vision_open(const char* path, or_model** out, char* err, int errlen) {
+    *out = NULL;
+    or_model* m = (or_model*)calloc(1, sizeof(or_model));
+    int rc = parse_gguf(m, path, err, errlen);
+    if (!rc) rc = read_vision_config(m, err, errlen);
+    if (!rc) rc = check_vision_weights(m, err, errlen);
+    if (rc) {
+        or_close(m);
+        return rc;
+    }
+    *out = m;
+    return OR_OK;
+}
+
+int or_vision_get_info(const or_model* v, or_vinfo* info) {
+    *info = v->vinfo;
+    return OR_OK;
+}
+
+/* CPUVisionReference.geluQuick (CPUVisionReference.swift:40-42). */
+static float gelu_quick(float x) { return x / (1.0f + expf(-1.702f * x)); }
+
+/* CPUVisionReference.rope2D (CPUVisionReference.swift:46-62): the first half of each head
+ * rotates by the patch column, the second by the patch row, each a NeoX rotation of hd / 2
+ * dims; `table` holds hd / 4 (cos, sin) pairs per position. */
+static void rope_2d(float* x, int64_t tokens, int64_t heads, int64_t hd, const float* table, const int32_t* px,
+                    const int32_t* py) {
+    const int64_t half = hd / 2, quarter = half / 2;
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < tokens; t++)
+        for (int axis = 0; axis < 2; axis++) {
+            const int64_t offset = axis ? half : 0, pos = axis ? py[t] : px[t];
+            for (int64_t h = 0; h < heads; h++) {
+                float* o = x + (t * heads + h) * hd + offset;
+                for (int64_t i = 0; i < quarter; i++) {
+                    const float c = table[(pos * quarter + i) * 2], s = table[(pos * quarter + i) * 2 + 1];
+                    const float a = o[i], b = o[i + quarter];
+                    o[i] = a * c - b * s;
+                    o[i + quarter] = a * s + b * c;
+                }
+            }
+        }
+}
+
+/* CPUVisionReference.forward (CPUVisionReference.swift:89-165). */
+int or_vision_forward(or_model* m, const float* patches, int32_t gx, int32_t gy, float* out, or_trace_fn tr, void* user) {
+    const or_vinfo* V = &m->vinfo;
+    const int64_t d = V->hidden, P = (int64_t)gx * gy, heads = V->heads, hd = V->head_dim, ff = V->ff;
+    const int64_t area = (int64_t)V->patch * V->patch * 3;
+    const float eps = V->eps;
+    if (gx <= 0 || gy <= 0 || gx % V->merge || gy % V->merge || gx > V->position_count || gy > V->position_count)
+        return OR_ERR_INVALID_OPTIONS;
+    char name[64];
+    float* x = (float*)malloc((size_t)(P * d) * 4);
+    or_matmul(patches, P, area, matrix(m, find_tensor(m, "v.patch_embd.weight")), d, x);
+    trace(tr, user, "inp", x, P * d);
+    int32_t* px = (int32_t*)malloc((size_t)P * 4);
+    int32_t* py = (int32_t*)malloc((size_t)P * 4);
+    for (int64_t t = 0; t < P; t++) {
+        px[t] = (int32_t)(t % gx);
+        py[t] = (int32_t)(t / gx);
+    }
+    /* v.position_embd.weight as [2 * n][d]: the column table, then the row table. */
+    const float* pos = (const float*)find_tensor(m, "v.position_embd.weight")->data;
+    for (int64_t t = 0; t < P; t++) {
+        for (int64_t i = 0; i < d; i++) x[t * d + i] += pos[(int64_t)px[t] * d + i];
+        for (int64_t i = 0; i < d; i++) x[t * d + i] += pos[((int64_t)V->position_count + py[t]) * d + i];
+    }
+    trace(tr, user, "pos_embd", x, P * d);
+    const int32_t npos = gx > gy ? gx : gy;
+    float* table = (float*)malloc((size_t)npos * (size_t)(hd / 4) * 2 * 4);
+    or_rope_table((int32_t)(hd / 2), V->rope_theta, npos, table);
+
+    float* a = (float*)malloc((size_t)(P * d) * 4);
+    float* q = (float*)malloc((size_t)(P * d) * 4);
+    float* k = (float*)malloc((size_t)(P * d) * 4);
+    float* v = (float*)malloc((size_t)(P * d) * 4);
+    float* attn = (float*)malloc((size_t)(P * d) * 4);
+    float* o = (float*)malloc((size_t)(P * d) * 4);
+    float* gate = (float*)malloc((size_t)(P * ff) * 4);
+    float* up = (float*)malloc((size_t)(P * ff) * 4);
+#define VW(l, suffix) (snprintf(name, sizeof name, "v.blk.%d." suffix, l), matrix(m, find_tensor(m, name)))
+#define TRACE(fmt, l, data, n) (snprintf(name, sizeof name, fmt, l), trace(tr, user, name, data, n))
+    for (int l = 0; l < V->layers; l++) {
+        or_rmsnorm(x, P, d, VW(l, "ln1.weight"), eps, a);
+        TRACE("layer_inp_normed-%d", l, a, P * d);
+        or_matmul(a, P, d, VW(l, "attn_q.weight"), d, q);
+        or_matmul(a, P, d, VW(l, "attn_k.weight"), d, k);
+        or_matmul(a, P, d, VW(l, "attn_v.weight"), d, v);
+        TRACE("Vcur-%d", l, v, P * d);
+        or_rmsnorm(q, P * heads, hd, VW(l, "attn_q_norm.weight"), eps, q);
+        or_rmsnorm(k, P * heads, hd, VW(l, "attn_k_norm.weight"), eps, k);
+        TRACE("Qcur-%d", l, q, P * d);
+        TRACE("Kcur-%d", l, k, P * d);
+        rope_2d(q, P, heads, hd, table, px, py);
+        rope_2d(k, P, heads, hd, table, px, py);
+        TRACE("Qcur_pos-%d", l, q, P * d);
+        TRACE("Kcur_pos-%d", l, k, P * d);
+        or_rmsnorm(v, P * heads, hd, NULL, eps, v);
+        TRACE("Vcur_normed-%d", l, v, P * d);
+        or_attention(q, k, v, (int32_t)P, (int32_t)heads, (int32_t)heads, (int32_t)hd, 1.0f, 0, attn);
+        TRACE("kqv_out-%d", l, attn, P * d);
+        or_matmul(attn, P, d, VW(l, "attn_out.weight"), d, o);
+        TRACE("attn_out-%d", l, o, P * d);
+        or_rmsnorm(o, P, d, VW(l, "attn_post_norm.weight"), eps, o);
+        TRACE("attn_post_normed-%d", l, o, P * d);
+        for (int64_t i = 0; i < P * d; i++) x[i] += o[i];
+        TRACE("ffn_inp-%d", l, x, P * d);
+        or_rmsnorm(x, P, d, VW(l, "ln2.weight"), eps, a);
+        TRACE("ffn_inp_normed-%d", l, a, P * d);
+        or_matmul(a, P, d, VW(l, "ffn_gate.weight"), ff, gate);
+        or_matmul(a, P, d, VW(l, "ffn_up.weight"), ff, up);
+        TRACE("ffn_gate-%d", l, gate, P * ff);
+        TRACE("ffn_up-%d", l, up, P * ff);
+        for (int64_t i = 0; i < P * ff; i++) gate[i] = gelu_quick(gate[i]) * up[i];
+        TRACE("ffn_geglu_quick-%d", l, gate, P * ff);
+        or_matmul(gate, P, ff, VW(l, "ffn_down.weight"), d, o);
+        TRACE("ffn_out-%d", l, o, P * d);
+        or_rmsnorm(o, P, d, VW(l, "ffn_post_norm.weight"), eps, o);
+        TRACE("ffn_post_normed-%d", l, o, P * d);
+        for (int64_t i = 0; i < P * d; i++) x[i] += o[i];
+        TRACE("layer_out-%d", l, x, P * d);
+    }
+#undef VW
+#undef TRACE
+    /* CPUVisionReference.pool (CPUVisionReference.swift:66-84). */
+    const int64_t mg = V->merge, tx = gx / mg, T = tx * (gy / mg);
+    float* pooled = (float*)calloc((size_t)(T * d), 4);
+    const float pool_scale = sqrtf((float)d) / (float)(mg * mg);
+    for (int64_t oy = 0; oy < gy / mg; oy++)
+        for (int64_t ox = 0; ox < tx; ox++) {
+            float* dst = pooled + (oy * tx + ox) * d;
+            for (int64_t ky = 0; ky < mg; ky++)
+                for (int64_t kx = 0; kx < mg; kx++) {
+                    const float* src = x + ((oy * mg + ky) * gx + ox * mg + kx) * d;
+                    for (int64_t i = 0; i < d; i++) dst[i] += src[i];
+                }
+            for (int64_t i = 0; i < d; i++) dst[i] *= pool_scale;
+        }
+    trace(tr, user, "pooled", pooled, T * d);
+    or_rmsnorm(pooled, T, d, NULL, eps, pooled);
+    or_matmul(pooled, T, d, matrix(m, find_tensor(m, "mm.input_projection.weight")), V->projection_dim, out);
+    trace(tr, user, "projected", out, T * V->projection_dim);
+    free(x); free(px); free(py); free(table); free(a); free(q); free(k); free(v); free(attn); free(o); free(gate);
+    free(up); free(pooled);
+    return OR_OK;
+}
+
+/* ------------------------------------------------------------------ image preprocessing */
+void or_target_size(int32_t width, int32_t height, int32_t alignment, int32_t min_pixels, int32_t max_pixels,
+                    int32_t* out_w, int32_t* out_h) {
+    const float f = (float)alignment;
+#define ROUND_BY(x) ((int32_t)roundf((x) / f) * alignment)
+#define CEIL_BY(x) ((int32_t)ceilf((x) / f) * alignment)
+#define FLOOR_BY(x) ((int32_t)floorf((x) / f) * alignment)
+    int32_t w = ROUND_BY((float)width), h = ROUND_BY((float)height);
+    if (w < alignment) w = alignment;
+    if (h < alignment) h = alignment;
+    if (max_pixels > 0 && (int64_t)w * h > max_pixels) {
+        const float beta = sqrtf((float)height * (float)width / (float)max_pixels);
+        h = FLOOR_BY((float)height / beta);
+        w = FLOOR_BY((float)width / beta);
+        if (h < alignment) h = alignment;
+        if (w < alignment) w = alignment;
+    } else if (min_pixels > 0 && (int64_t)w * h < min_pixels) {
+        const float beta = sqrtf((float)min_pixels / ((float)height * (float)width));
+        h = CEIL_BY((float)height * beta);
+        w = CEIL_BY((float)width * beta);
+    }
+#undef ROUND_BY
+#undef CEIL_BY
+#undef FLOOR_BY
+    *out_w = w;
+    *out_h = h;
+}
+
+/* ImageResizer.Kernel (ImageResizer.swift:82-128): Pillow's bicubic taps (a = -0.5) in
+ * 22-bit fixed point. */
+enum { RS_PRECISION = 22 };
+
+static double bicubic(double x) {
+    const double a = -0.5;
+    x = fabs(x);
+    if (x < 1) return ((a + 2) * x - (a + 3)) * x * x + 1;
+    if (x < 2) return (((x - 5) * x + 8) * x - 4) * a;
+    return 0;
+}
+
+typedef struct {
+    int size;
+    int* start;
+    int* count;
+    int32_t* weights;
+} rs_kernel;
+
+static rs_kernel rs_make(int in_size, int out_size) {
+    rs_kernel k;
+    const double support_base = 2.0, scale = (double)in_size / (double)out_size;
+    const double filter_scale = scale > 1.0 ? scale : 1.0, support = support_base * filter_scale;
+    k.size = (int)ceil(support) * 2 + 1;
+    k.start = (int*)calloc((size_t)out_size, sizeof(int));
+    k.count = (int*)calloc((size_t)out_size, sizeof(int));
+    k.weights = (int32_t*)calloc((size_t)out_size * (size_t)k.size, sizeof(int32_t));
+    double* pre = (double*)calloc((size_t)out_size * (size_t)k.size, sizeof(double));
+    for (int xx = 0; xx < out_size; xx++) {
+        const double center = ((double)xx + 0.5) * scale, ss = 1.0 / filter_scale;
+        double ww = 0.0;
+        int xmin = (int)(center - support + 0.5);
+        if (xmin < 0) xmin = 0;
+        int xmax = (int)(center + support + 0.5);
+        if (xmax > in_size) xmax = in_size;
+        xmax -= xmin;
+        for (int x = 0; x < xmax; x++) {
+            const double w = bicubic(((double)(x + xmin) - center + 0.5) * ss);
+            pre[(size_t)xx * k.size + x] = w;
+            ww += w;
+        }
+        if (ww != 0)
+            for (int x = 0; x < xmax; x++) pre[(size_t)xx * k.size + x] /= ww;
+        k.start[xx] = xmin;
+        k.count[xx] = xmax;
+    }
+    const double fxp = (double)(1 << RS_PRECISION);
+    for (size_t i = 0; i < (size_t)out_size * (size_t)k.size; i++)
+        k.weights[i] = (int32_t)(pre[i] * fxp + (pre[i] < 0 ? -0.5 : 0.5));
+    free(pre);
+    return k;
+}
+
+static void rs_free(rs_kernel* k) {
+    free(k->start);
+    free(k->count);
+    free(k->weights);
+}
+
+static uint8_t clip8(int32_t v) {
+    const int32_t s = v >> RS_PRECISION;
+    return (uint8_t)(s < 0 ? 0 : s > 255 ? 255 : s);
+}
+
+/* Sums wrap in 32 bits like the reference's &+ and &*. */
+static int32_t wrap_mad(int32_t acc, int32_t a, int32_t b) { return (int32_t)((uint32_t)acc + (uint32_t)a * (uint32_t)b); }
+
+/* resizeBicubic (ImageResizer.swift:53-66, 130-176): a horizontal pass, then a vertical pass. */
+static uint8_t* resize_bicubic(const uint8_t* in, int w, int h, int tw, int th) {
+    const uint8_t* cur = in;
+    uint8_t* horiz = NULL;
+    int cw = w;
+    if (tw != w) {
+        rs_kernel k = rs_make(w, tw);
+        horiz = (uint8_t*)malloc((size_t)tw * h * 3);
+        for (int yy = 0; yy < h; yy++)
+            for (int xx = 0; xx < tw; xx++) {
+                int32_t s[3] = {1 << (RS_PRECISION - 1), 1 << (RS_PRECISION - 1), 1 << (RS_PRECISION - 1)};
+                const uint8_t* p = in + ((size_t)yy * w + k.start[xx]) * 3;
+                for (int x = 0; x < k.count[xx]; x++, p += 3) {
+                    const int32_t wt = k.weights[(size_t)xx * k.size + x];
+                    for (int c = 0; c < 3; c++) s[c] = wrap_mad(s[c], p[c], wt);
+                }
+                for (int c = 0; c < 3; c++) horiz[((size_t)yy * tw + xx) * 3 + c] = clip8(s[c]);
+            }
+        rs_free(&k);
+        cur = horiz;
+        cw = tw;
+    }
+    uint8_t* out = (uint8_t*)malloc((size_t)cw * th * 3);
+    if (th != h) {
+        rs_kernel k = rs_make(h, th);
+        const size_t row = (size_t)cw * 3;
+        int32_t* acc = (int32_t*)malloc(row * 4);
+        for (int yy = 0; yy < th; yy++) {
+            for (size_t i = 0; i < row; i++) acc[i] = 1 << (RS_PRECISION - 1);
+            for (int y = 0; y < k.count[yy]; y++) {
+                const int32_t wt = k.weights[(size_t)yy * k.size + y];
+                const uint8_t* src = cur + (size_t)(k.start[yy] + y) * row;
+                for (size_t i = 0; i < row; i++) acc[i] = wrap_mad(acc[i], src[i], wt);
+            }
+            for (size_t i = 0; i < row; i++) out[(size_t)yy * row + i] = clip8(acc[i]);
+        }
+        free(acc);
+        rs_free(&k);
+    } else {
+        memcpy(out, cur, (size_t)cw * th * 3);
+    }
+    free(horiz);
+    return out;
+}
+
+void or_fit_image(const uint8_t* in, int32_t w, int32_t h, int32_t tw, int32_t th, uint8_t* out) {
+    if (w == tw && h == th) {
+        memcpy(out, in, (size_t)w * h * 3);
+        return;
+    }
+    const float sx = (float)tw / (float)w, sy = (float)th / (float)h, scale = sx < sy ? sx : sy;
+    int fw = (int)ceilf((float)w * scale), fh = (int)ceilf((float)h * scale);
+    if (fw > tw) fw = tw;
+    if (fh > th) fh = th;
+    uint8_t* fitted = resize_bicubic(in, w, h, fw, fh);
+    memset(out, 0, (size_t)tw * th * 3);
+    const int ox = (tw - fw) / 2, oy = (th - fh) / 2;
+    for (int y = 0; y < fh; y++) memcpy(out + ((size_t)(y + oy) * tw + ox) * 3, fitted + (size_t)y * fw * 3, (size_t)fw * 3);
+    free(fitted);
+}
+
+/* Round to the nearest fp16 value (ties to even), for normal, subnormal and overflowing inputs. */
+float or_round_f16(float x) {
+    uint32_t b;
+    memcpy(&b, &x, 4);
+    const uint32_t sign = b & 0x80000000u, mag = b & 0x7fffffffu;
+    if (mag >= 0x7f800000u) return x; /* inf, nan */
+    float a;
+    memcpy(&a, &mag, 4);
+    if (a >= 65520.0f) { /* rounds past the largest finite fp16 */
+        uint32_t inf = sign | 0x7f800000u;
+        float r;
+        memcpy(&r, &inf, 4);
+        return r;
+    }
+    /* Spacing of fp16 values around a: 2^(e - 10) for normals (e >= -14), 2^-24 below. */
+    int e;
+    frexpf(a, &e); /* a = f * 2^e, f in [0.5, 1) */
+    int exp2 = e - 1;
+    if (exp2 < -14) exp2 = -14;
+    const float ulp = ldexpf(1.0f, exp2 - 10);
+    const float q = a / ulp;          /* exact: a scaled by a power of two */
+    float r = nearbyintf(q) * ulp;    /* round half to even in the default rounding mode */
+    uint32_t rb;
+    memcpy(&rb, &r, 4);
+    rb |= sign;
+    memcpy(&r, &rb, 4);
+    return r;
+}
+
+void or_patchify(const uint8_t* rgb, int32_t w, int32_t h, int32_t p, const float* mean, const float* std, float* patches) {
+    const int32_t gx = w / p, gy = h / p;
+    const int64_t area = (int64_t)p * p * 3;
+    for (int32_t py = 0; py < gy; py++)
+        for (int32_t px = 0; px < gx; px++) {
+            const int64_t i = (int64_t)py * gx + px;
+            for (int c = 0; c < 3; c++)
+                for (int ky = 0; ky < p; ky++)
+                    for (int kx = 0; kx < p; kx++) {
+                        const uint8_t byte = rgb[(((int64_t)py * p + ky) * w + px * p + kx) * 3 + c];
+                        const float f = ((float)byte / 255.0f - mean[c]) / std[c];
+                        patches[i * area + (int64_t)c * p * p + ky * p + kx] = or_round_f16(2.0f * f - 1.0f);
+                    }
+        }
 }

@@ -65,8 +65,43 @@ int or_threads(void);
 /* CPUReference.forward(tokens:trace:): the pooled, unnormalised vector of one sequence. */
 int or_forward(or_model* m, const int32_t* tokens, int32_t T, float* pooled, or_trace_fn trace, void* user);
 
+/* CPUReference.forward(rows:trace:) with vector rows: an id -(r + 1) is row r of `vectors`
+ * ([vector_rows][hidden]), entered unscaled. */
+int or_forward_rows(or_model* m, const int32_t* tokens, int32_t T, const float* vectors, int64_t vector_rows,
+                    float* pooled, or_trace_fn trace, void* user);
+
+/* ne shape (contiguous dimension first, unused dimensions 1) and dimension count of a tensor. */
+int or_tensor_shape(or_model* m, const char* tensor, int64_t* shape, int32_t* ndim);
+
 /* WeightTensor.dequantizeRow for any tensor by name. */
 int or_dequantize_row(or_model* m, const char* tensor, int64_t row, float* out, int64_t n);
+
+/* ---- gemma4v vision tower (Sources/GemmaEmbed/Model/VisionConfig.swift, VisionWeights.swift,
+ * CPUVisionReference.swift) and image preprocessing (Image/ImageResizer.swift,
+ * Image/ImagePreprocessor.swift). */
+typedef struct {
+    int32_t hidden, layers, heads, head_dim, ff, patch, projection_dim, position_count, merge;
+    float eps, rope_theta;
+    float mean[3], std[3];
+} or_vinfo;
+
+/* VisionConfig(gguf:) and VisionWeights(gguf:config:) over an mmproj file. */
+int or_vision_open(const char* path, or_model** out, char* err, int errlen);
+int or_vision_get_info(const or_model* v, or_vinfo* info);
+/* CPUVisionReference.forward: `patches` is [grid_y * grid_x][3 * patch^2] (PreparedImage.patches);
+ * writes (grid_x / merge) * (grid_y / merge) rows of projection_dim floats. */
+int or_vision_forward(or_model* v, const float* patches, int32_t grid_x, int32_t grid_y, float* out, or_trace_fn trace,
+                      void* user);
+/* ImageResizer.targetSize (ImageResizer.swift:11-29). */
+void or_target_size(int32_t width, int32_t height, int32_t alignment, int32_t min_pixels, int32_t max_pixels,
+                    int32_t* out_width, int32_t* out_height);
+/* ImageResizer.fit (ImageResizer.swift:33-49): RGB8 `in` (w x h) to `out` (tw x th). */
+void or_fit_image(const uint8_t* in, int32_t w, int32_t h, int32_t tw, int32_t th, uint8_t* out);
+/* PreparedImage(resized:patchSize:mergeSize:mean:std:) (ImagePreprocessor.swift:31-60): patch rows
+ * [gy * gx][3 * p^2], element c * p^2 + ky * p + kx, each rounded to fp16. */
+void or_patchify(const uint8_t* rgb, int32_t w, int32_t h, int32_t p, const float* mean, const float* std, float* patches);
+/* Float(Float16(x)): round to the nearest fp16 value, ties to even. */
+float or_round_f16(float x);
 
 /* Static pieces, exposed for unit tests. */
 void or_matmul(const float* x, int64_t m, int64_t k, const float* w, int64_t n, float* y);
