@@ -21,8 +21,8 @@ import numpy as np
 
 from . import _lib
 
-__all__ = ["EmbeddingModel", "EmbedOptions", "LoadOptions", "Embedding", "EmbeddingProgress", "ModelInfo",
-           "GemmaEmbedError", "TaskPrefix", "Tokenizer", "ALLOWED_DIMENSIONS"]
+__all__ = ["EmbeddingModel", "EmbedOptions", "LoadOptions", "ImageEmbedOptions", "Embedding", "EmbeddingProgress",
+           "ModelInfo", "GemmaEmbedError", "TaskPrefix", "Tokenizer", "ALLOWED_DIMENSIONS"]
 
 ALLOWED_DIMENSIONS = (768, 512, 256, 128)
 
@@ -30,7 +30,8 @@ ALLOWED_DIMENSIONS = (768, 512, 256, 128)
 STATUS = {
     0: "ok", 1: "fileNotReadable", 2: "invalidGGUF", 3: "unsupportedTensorType", 4: "unsupportedArchitecture",
     5: "missingTensor", 6: "missingMetadata", 7: "tensorShapeMismatch", 8: "noDevice", 9: "invalidOptions",
-    10: "gpuFailure", 11: "outOfMemory", 12: "timeout", 13: "cancelled",
+    10: "gpuFailure", 11: "outOfMemory", 12: "timeout", 13: "cancelled", 14: "imageDecoding",
+    15: "imageEncoderNotLoaded",
 }
 LOAD_NO_GRAPHS = 1
 LOAD_Q8_ONLY = 2
@@ -187,6 +188,17 @@ class LoadOptions:
     q8_only: bool = False
     programmatic_launch: bool = True  # overlap each kernel's set-up with its predecessor's tail
     fused_residual: bool = False  # run each residual step inside the projection before it
+    image_encoder: Optional[str] = None  # LoadOptions.imageEncoder: the mmproj GGUF
+    image_patch_budget: int = 4096       # ImageEmbedOptions.patchBudget: patches per image batch
+
+
+@dataclass
+class ImageEmbedOptions:
+    """ImageEmbedOptions (EmbedOptions.swift:59-88)."""
+    dimensions: int = 768
+    normalise: bool = True
+    max_image_tokens: int = 256
+    batch_size: Optional[int] = None
 
 
 @dataclass
@@ -223,6 +235,25 @@ class ModelInfo:
     device_name: str
     eos_id: int
     bos_id: int
+    # ImageEncoderInfo (VisionConfig.swift:5-17); zeros without an image encoder.
+    image_layer_count: int = 0
+    image_hidden_size: int = 0
+    image_patch_size: int = 0
+    image_projection_dim: int = 0
+
+
+def _images(images):
+    """ge_image views of HxWx3 uint8 arrays (kept alive by the returned list)."""
+    arrs = [np.ascontiguousarray(np.asarray(im, dtype=np.uint8)) for im in images]
+    for a in arrs:
+        if a.ndim != 3 or a.shape[2] != 3:
+            raise GemmaEmbedError(14, "imageDecoding: an image must be a height x width x 3 array of uint8")
+    c = (_lib.GeImage * max(len(arrs), 1))()
+    for i, a in enumerate(arrs):
+        c[i].rgb = a.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8))
+        c[i].width = a.shape[1]
+        c[i].height = a.shape[0]
+    return c, arrs
 
 
 def _check(rc: int, handle=None):
@@ -265,7 +296,9 @@ class EmbeddingModel:
             head_count=info.head_count, vocabulary_size=info.vocabulary_size, sliding_window=info.sliding_window,
             max_tokens=info.max_tokens, norm_epsilon=info.norm_epsilon, quantization=info.quantization.decode(),
             file_size=info.file_size, device_count=info.device_count, device_name=info.device_name.decode(),
-            eos_id=info.eos_id, bos_id=info.bos_id)
+            eos_id=info.eos_id, bos_id=info.bos_id, image_layer_count=info.image_layer_count,
+            image_hidden_size=info.image_hidden_size, image_patch_size=info.image_patch_size,
+            image_projection_dim=info.image_projection_dim)
 
     @classmethod
     def load(cls, path: str, options: Optional[LoadOptions] = None) -> "EmbeddingModel":
@@ -282,6 +315,8 @@ class EmbeddingModel:
         o.flags = ((0 if options.use_graphs else LOAD_NO_GRAPHS) | (LOAD_Q8_ONLY if options.q8_only else 0)
                    | (0 if options.programmatic_launch else LOAD_NO_PDL)
                    | (LOAD_FUSED_RESIDUAL if options.fused_residual else 0))
+        o.image_encoder_path = str(options.image_encoder).encode() if options.image_encoder else None
+        o.image_patch_budget = int(options.image_patch_budget)
         h = ctypes.c_void_p()
         _check(L.ge_load(str(path).encode(), ctypes.byref(o), ctypes.byref(h)), None)
         return cls(h, options)
@@ -427,6 +462,53 @@ class EmbeddingModel:
                                      _ptr(trunc, ctypes.c_int32), cb, None), self._h)
         res = [Embedding(out[i].copy(), int(counts[i]), bool(trunc[i])) for i in range(n)]
         return res[0] if single else res
+
+    def embed_images(self, images, options: Optional[ImageEmbedOptions] = None,
+                     progress: Optional[Callable[[EmbeddingProgress], Optional[bool]]] = None) -> list:
+        """embed(images:options:progress:) (ImageEmbedding.swift:17-33) over decoded images, each a
+        height x width x 3 uint8 array; a single array embeds one image and returns one Embedding."""
+        options = options or ImageEmbedOptions()
+        single = isinstance(images, np.ndarray) and images.ndim == 3
+        items = [images] if single else list(images)
+        c, keep = _images(items)
+        n = len(items)
+        if options.batch_size is not None and options.batch_size < 1:
+            raise GemmaEmbedError(9, "invalid options: batchSize must be at least 1")
+        o = _lib.GeImageOpts(options.dimensions, int(options.normalise), options.max_image_tokens,
+                             options.batch_size or 0)
+        out = np.zeros((max(n, 1), options.dimensions if options.dimensions > 0 else 1), dtype=np.float32)
+        counts = np.zeros(max(n, 1), dtype=np.int32)
+        cb = _lib.PROGRESS_FN(0)
+        if progress is not None:
+            def _cb(done, total, tokens, user):
+                return 1 if progress(EmbeddingProgress(done, total, tokens)) else 0
+            cb = _lib.PROGRESS_FN(_cb)
+        _check(_lib.lib().ge_embed_images(self._h, c, n, ctypes.byref(o), _ptr(out, ctypes.c_float),
+                                          _ptr(counts, ctypes.c_int32), cb, None), self._h)
+        del keep
+        res = [Embedding(out[i].copy(), int(counts[i]), False) for i in range(n)]
+        return res[0] if single else res
+
+    def image_vectors(self, images, max_image_tokens: int = 256) -> list:
+        """MetalForward.imageVectors (Metal/MetalForward.swift:227-238): each image's projected rows."""
+        items = list(images)
+        c, keep = _images(items)
+        n = len(items)
+        L = _lib.lib()
+        per = [L.ge_image_tokens(self._h, a.shape[1], a.shape[0], max_image_tokens) for a in keep]
+        if any(t < 0 for t in per):
+            raise GemmaEmbedError(15, "imageEncoderNotLoaded: no image encoder is loaded")
+        cap = max(sum(per), 1)
+        out = np.zeros((cap, self.info.image_projection_dim or 1), dtype=np.float32)
+        rows = np.zeros(max(n, 1), dtype=np.int32)
+        _check(L.ge_image_vectors(self._h, c, n, max_image_tokens, _ptr(out, ctypes.c_float), cap,
+                                  _ptr(rows, ctypes.c_int32)), self._h)
+        del keep
+        res, r0 = [], 0
+        for i in range(n):
+            res.append(out[r0:r0 + rows[i]].copy())
+            r0 += int(rows[i])
+        return res
 
     @staticmethod
     def similarity(a: Embedding, b: Embedding) -> float:

@@ -20,7 +20,16 @@ class GeSeq(ctypes.Structure):
 
 
 class GeLoadOpts(ctypes.Structure):
-    _fields_ = [("device_mask", ctypes.c_uint32), ("batch_token_budget", ctypes.c_int32), ("flags", ctypes.c_uint32)]
+    _fields_ = [("device_mask", ctypes.c_uint32), ("batch_token_budget", ctypes.c_int32), ("flags", ctypes.c_uint32),
+                ("image_encoder_path", ctypes.c_char_p), ("image_patch_budget", ctypes.c_int32)]
+
+
+class GeImage(ctypes.Structure):
+    _fields_ = [("rgb", ctypes.POINTER(ctypes.c_uint8)), ("width", ctypes.c_int32), ("height", ctypes.c_int32)]
+
+
+class GeImageOpts(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("dimensions", "normalise", "max_image_tokens", "batch_size")]
 
 
 class GeEmbedOpts(ctypes.Structure):
@@ -36,7 +45,9 @@ class GeInfo(ctypes.Structure):
         ("norm_epsilon", ctypes.c_float), ("quantization", ctypes.c_char * 16), ("file_size", ctypes.c_int64),
         ("device_count", ctypes.c_int32), ("eos_id", ctypes.c_int32), ("bos_id", ctypes.c_int32),
         ("device_name", ctypes.c_char * 128), ("kernel_launches", ctypes.c_int64),
-        ("host_to_device_bytes", ctypes.c_int64), ("device_to_host_bytes", ctypes.c_int64)]
+        ("host_to_device_bytes", ctypes.c_int64), ("device_to_host_bytes", ctypes.c_int64)] + [
+        (n, ctypes.c_int32) for n in ("image_layer_count", "image_hidden_size", "image_patch_size",
+                                      "image_projection_dim")]
 
 
 class GeKernelTime(ctypes.Structure):
@@ -81,6 +92,12 @@ SIGNATURES = {
     "ge_token_piece": ([ctypes.c_void_p, ctypes.c_int32, P(ctypes.c_char), ctypes.c_int64, i64p], ctypes.c_int),
     "ge_token_is_control": ([ctypes.c_void_p, ctypes.c_int32], ctypes.c_int),
     "ge_task_prefix": ([ctypes.c_int32, ctypes.c_char_p, P(ctypes.c_char), ctypes.c_int64, i64p], ctypes.c_int),
+    "ge_image_opts_default": ([P(GeImageOpts)], None),
+    "ge_embed_images": ([ctypes.c_void_p, P(GeImage), ctypes.c_int32, P(GeImageOpts), f32p, i32p, PROGRESS_FN,
+                         ctypes.c_void_p], ctypes.c_int),
+    "ge_image_tokens": ([ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32], ctypes.c_int32),
+    "ge_image_vectors": ([ctypes.c_void_p, P(GeImage), ctypes.c_int32, ctypes.c_int32, f32p, ctypes.c_int64, i32p],
+                         ctypes.c_int),
     "ge_embed_texts": ([ctypes.c_void_p, P(ctypes.c_char_p), i64p, ctypes.c_int32, ctypes.c_char_p, P(GeEmbedOpts),
                         f32p, i32p, i32p, PROGRESS_FN, ctypes.c_void_p], ctypes.c_int),
 }
@@ -97,6 +114,10 @@ TEST_SIGNATURES = {
     "ge_test_attention_schedule": ([P(GeSeq), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                     ctypes.c_int32, P(ctypes.c_uint32), ctypes.c_int32, P(ctypes.c_int32),
                                     P(ctypes.c_int32)], ctypes.c_int),
+    "ge_test_image_prepare": ([ctypes.c_int32] * 3 + [P(ctypes.c_uint8), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                               P(ctypes.c_uint8), ctypes.c_int64, i32p, i32p], ctypes.c_int),
+    "ge_test_patchify": ([P(ctypes.c_uint8), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, f32p, f32p, u16p,
+                          ctypes.c_int32], ctypes.c_int),
     "ge_test_last_error": ([], ctypes.c_char_p),
 }
 

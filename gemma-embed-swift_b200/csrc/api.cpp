@@ -203,6 +203,65 @@ int embed_prepared(ge_model* m, const std::vector<std::vector<int32_t>>& prepare
     return GE_OK;
 }
 
+// The image forward of MetalForward.run(images:) (Metal/MetalForward.swift:211-219) on one
+// device: the vision tower over the images, then the text tower over each image's
+// [bos, <|image>, rows..., <image|>, eos] with the rows read from the tower's output.
+// `pooled` receives n rows of the output width.
+int images_on_device(ge_model* m, ge::Device& d, const ge::PreparedImage* const* ims, int n, float* pooled,
+                     std::string* error) {
+    int rc = ge::run_vision(m, d, ims, n, error);
+    if (rc) return rc;
+    std::vector<int32_t> toks;
+    std::vector<ge_seq> seqs;
+    int32_t row = 0;
+    for (int i = 0; i < n; i++) {
+        seqs.push_back({uint32_t(toks.size()), uint32_t(ims[i]->tokens() + 4)});
+        toks.push_back(m->cfg.bos_id);
+        toks.push_back(m->image_begin);
+        for (int t = 0; t < ims[i]->tokens(); t++) toks.push_back(-(row + t) - 1);
+        toks.push_back(m->image_end);
+        toks.push_back(m->cfg.eos_id);
+        row += ims[i]->tokens();
+    }
+    ge::ForwardArgs a;
+    a.tokens = toks.data();
+    a.ntok = int(toks.size());
+    a.seqs = seqs.data();
+    a.nseq = int(seqs.size());
+    a.out = pooled;
+    a.error = error;
+    a.vectors = d.vis.ws.vectors;
+    a.vector_rows = row;
+    return ge::run_forward(m, d, a);
+}
+
+// Prepares images on host threads (ImageEmbedding.prepare, ImageEmbedding.swift:75-103).
+int prepare_images(ge_model* m, const ge_image* images, int32_t count, int max_image_tokens,
+                   std::vector<ge::PreparedImage>& out) {
+    for (int32_t i = 0; i < count; i++)
+        if (!images[i].rgb || images[i].width <= 0 || images[i].height <= 0)
+            return ge::set_error(m, GE_ERR_IMAGE_DECODING, "cannot decode image: image " + std::to_string(i) + " has no pixels");
+    out.assign(size_t(count), ge::PreparedImage());
+    std::atomic<int32_t> next{0};
+    auto work = [&]() {
+        for (int32_t i = next++; i < count; i = next++)
+            ge::prepare_image(m->vcfg, images[i].rgb, images[i].width, images[i].height, max_image_tokens, out[size_t(i)]);
+    };
+    const int nt = int(std::min<int64_t>({int64_t(std::max(1u, std::thread::hardware_concurrency())), int64_t(count), 32}));
+    std::vector<std::thread> th;
+    for (int t = 1; t < nt; t++) th.emplace_back(work);
+    work();
+    for (auto& t : th) t.join();
+    for (int32_t i = 0; i < count; i++) {
+        const int rows = out[size_t(i)].tokens() + 4;
+        if (rows > m->cfg.max_tokens)
+            return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: image " + std::to_string(i) + " needs " +
+                                                                std::to_string(rows) + " rows, the text model takes " +
+                                                                std::to_string(m->cfg.max_tokens));
+    }
+    return GE_OK;
+}
+
 // Writes the first min(size, cap) bytes of `s` and its full size (the buffer convention of the
 // tokenizer entry points).
 int copy_out(const std::string& s, char* text, int64_t cap, int64_t* len) {
@@ -220,6 +279,8 @@ void ge_load_opts_default(ge_load_opts* o) {
     o->device_mask = 1;
     o->batch_token_budget = 8192;
     o->flags = 0;
+    o->image_encoder_path = nullptr;
+    o->image_patch_budget = 4096;
 }
 
 void ge_embed_opts_default(ge_embed_opts* o) {
@@ -242,7 +303,9 @@ int ge_load(const char* path, const ge_load_opts* opts, ge_model** out) {
     if (opts) o = *opts;
     m->budget = std::max(64, o.batch_token_budget);
     m->flags = o.flags;
+    m->patch_budget = o.image_patch_budget > 0 ? o.image_patch_budget : 4096;
     int rc = ge::load_model(m, path, &o);
+    if (rc == GE_OK && o.image_encoder_path) rc = ge::load_vision(m, o.image_encoder_path);
     if (rc == GE_OK) {
         // One forward over a short sequence initialises every kernel before the first request
         // (EmbeddingModel.swift:111-114).
@@ -315,6 +378,12 @@ int ge_info_get(const ge_model* m, ge_info* info) {
     info->kernel_launches = m->launches.load();
     info->host_to_device_bytes = m->h2d_bytes.load();
     info->device_to_host_bytes = m->d2h_bytes.load();
+    if (m->has_vision) {
+        info->image_layer_count = m->vcfg.layers;
+        info->image_hidden_size = m->vcfg.hidden;
+        info->image_patch_size = m->vcfg.patch;
+        info->image_projection_dim = m->vcfg.projection_dim;
+    }
     return GE_OK;
 }
 
@@ -533,6 +602,151 @@ int ge_embed_texts(ge_model* m, const char* const* texts, const int64_t* lengths
         truncate_keeping_eos(m, o, prepared[size_t(i)], token_counts, truncated, i);
     }
     return embed_prepared(m, prepared, o, out, progress, user);
+}
+
+void ge_image_opts_default(ge_image_opts* o) {
+    if (!o) return;
+    o->dimensions = 768;
+    o->normalise = 1;
+    o->max_image_tokens = 256;
+    o->batch_size = 0;
+}
+
+int ge_embed_images(ge_model* m, const ge_image* images, int32_t count, const ge_image_opts* opts, float* out,
+                    int32_t* token_counts, ge_progress_fn progress, void* user) {
+    if (!m) return GE_ERR_INVALID_OPTIONS;
+    ge_image_opts o;
+    ge_image_opts_default(&o);
+    if (opts) o = *opts;
+    // forEachImageBatch's checks (ImageEmbedding.swift:55-64).
+    if (!m->has_vision)
+        return ge::set_error(m, GE_ERR_IMAGE_ENCODER_NOT_LOADED,
+                             "no image encoder is loaded; pass the mmproj GGUF when loading the model");
+    if (!(o.dimensions == 768 || o.dimensions == 512 || o.dimensions == 256 || o.dimensions == 128) ||
+        o.dimensions > m->cfg.out_dim)
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: dimensions must be one of [768, 512, 256, 128]");
+    if (o.max_image_tokens < 1 || o.max_image_tokens > m->vcfg.native_max_image_tokens)
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: maxImageTokens must be between 1 and " +
+                                                            std::to_string(m->vcfg.native_max_image_tokens));
+    if (o.batch_size < 0) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: batchSize must be at least 1");
+    if (count < 0) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: negative image count");
+    if (count == 0) return GE_OK;
+    if (!images || !out) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: NULL array");
+    std::vector<ge::PreparedImage> prepared;
+    int rc = prepare_images(m, images, count, o.max_image_tokens, prepared);
+    if (rc) return rc;
+    std::vector<int64_t> costs(static_cast<size_t>(count));
+    for (int32_t i = 0; i < count; i++) costs[size_t(i)] = prepared[size_t(i)].patches();
+    const int64_t budget = m->patch_budget;
+    std::vector<int32_t> ranges(2 * size_t(count));
+    int32_t nr = 0;
+    ge_batches(costs.data(), count, 1, o.batch_size, &budget, ranges.data(), &nr);
+    std::lock_guard<std::mutex> g(m->mu);
+    const int od = m->cfg.out_dim, ndev = int(m->devs.size());
+    int32_t done = 0;
+    int64_t done_tokens = 0;
+    for (int32_t r = 0; r < nr; r++) {
+        const int32_t b = ranges[2 * size_t(r)], e = ranges[2 * size_t(r) + 1];
+        const int n = e - b;
+        std::vector<float> pooled(size_t(n) * od);
+        // Images of a batch spread over the devices, largest first onto the least-loaded one.
+        std::vector<std::vector<int>> parts(size_t(std::max(1, std::min(ndev, n))));
+        {
+            std::vector<int> order(static_cast<size_t>(n));
+            std::iota(order.begin(), order.end(), 0);
+            std::stable_sort(order.begin(), order.end(), [&](int x, int y) { return costs[size_t(b + x)] > costs[size_t(b + y)]; });
+            std::vector<int64_t> load(parts.size(), 0);
+            for (int i : order) {
+                const size_t dv = size_t(std::min_element(load.begin(), load.end()) - load.begin());
+                load[dv] += costs[size_t(b + i)];
+                parts[dv].push_back(i);
+            }
+            for (auto& p : parts) std::sort(p.begin(), p.end());
+        }
+        std::vector<int> rcs(parts.size(), GE_OK);
+        std::vector<std::string> msgs(parts.size());
+        auto run_part = [&](size_t dv) {
+            const auto& idx = parts[dv];
+            if (idx.empty()) return;
+            std::vector<const ge::PreparedImage*> ims;
+            for (int i : idx) ims.push_back(&prepared[size_t(b + i)]);
+            std::vector<float> po(idx.size() * size_t(od));
+            rcs[dv] = images_on_device(m, m->devs[dv], ims.data(), int(ims.size()), po.data(), &msgs[dv]);
+            if (rcs[dv] == GE_OK)
+                for (size_t k = 0; k < idx.size(); k++)
+                    memcpy(pooled.data() + size_t(idx[k]) * od, po.data() + k * od, size_t(od) * sizeof(float));
+        };
+        if (parts.size() == 1) {
+            run_part(0);
+        } else {
+            std::vector<std::thread> th;
+            for (size_t dv = 0; dv < parts.size(); dv++) th.emplace_back(run_part, dv);
+            for (auto& t : th) t.join();
+        }
+        for (size_t dv = 0; dv < parts.size(); dv++)
+            if (rcs[dv] != GE_OK) return ge::set_error(m, rcs[dv], msgs[dv]);
+        for (int32_t i = b; i < e; i++) {
+            ge_finish(pooled.data() + size_t(i - b) * od, od, o.dimensions, o.normalise, out + size_t(i) * o.dimensions);
+            const int rows = prepared[size_t(i)].tokens() + 4;  // EmbeddingModel.imageFrameRows
+            if (token_counts) token_counts[i] = rows;
+            done_tokens += rows;
+        }
+        done += n;
+        if (progress && progress(done, count, done_tokens, user) != 0 && r + 1 < nr)
+            return ge::set_error(m, GE_ERR_CANCELLED, "embedding was cancelled");
+    }
+    return GE_OK;
+}
+
+int32_t ge_image_tokens(const ge_model* m, int32_t width, int32_t height, int32_t max_image_tokens) {
+    if (!m || !m->has_vision || width <= 0 || height <= 0 || max_image_tokens <= 0) return -1;
+    const ge::VisionConfig& c = m->vcfg;
+    const int a = c.alignment();
+    int tw = 0, th = 0;
+    ge::image_target_size(width, height, a, c.min_image_tokens * a * a, max_image_tokens * a * a, tw, th);
+    return (tw / a) * (th / a);
+}
+
+int ge_image_vectors(ge_model* m, const ge_image* images, int32_t count, int32_t max_image_tokens, float* out,
+                     int64_t cap_rows, int32_t* rows_per_image) {
+    if (!m) return GE_ERR_INVALID_OPTIONS;
+    if (!m->has_vision)
+        return ge::set_error(m, GE_ERR_IMAGE_ENCODER_NOT_LOADED,
+                             "no image encoder is loaded; pass the mmproj GGUF when loading the model");
+    if (max_image_tokens < 1 || max_image_tokens > m->vcfg.native_max_image_tokens)
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: maxImageTokens must be between 1 and " +
+                                                            std::to_string(m->vcfg.native_max_image_tokens));
+    if (count < 0) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: negative image count");
+    if (count == 0) return GE_OK;
+    if (!images || !out) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: NULL array");
+    std::vector<ge::PreparedImage> prepared;
+    int rc = prepare_images(m, images, count, max_image_tokens, prepared);
+    if (rc) return rc;
+    int64_t rows = 0;
+    for (auto& p : prepared) rows += p.tokens();
+    if (rows > cap_rows)
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: the images need " + std::to_string(rows) +
+                                                            " rows, the output holds " + std::to_string(cap_rows));
+    std::lock_guard<std::mutex> g(m->mu);
+    ge::Device& d = m->devs[0];
+    std::vector<const ge::PreparedImage*> ims;
+    for (auto& p : prepared) ims.push_back(&p);
+    rc = ge::run_vision(m, d, ims.data(), count, nullptr);
+    if (rc) return rc;
+    const size_t bytes = size_t(rows) * m->vcfg.projection_dim * sizeof(float);
+    cudaError_t e = cudaMemcpyAsync(out, d.vis.ws.vectors, bytes, cudaMemcpyDeviceToHost, d.stream);
+    int h_err = 0;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&h_err, d.err, sizeof(int), cudaMemcpyDeviceToHost, d.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d.stream);
+    if (e != cudaSuccess)
+        return ge::set_error(m, GE_ERR_GPU_FAILURE, std::string("GPU execution failed: ") + cudaGetErrorString(e));
+    if (h_err) {
+        cudaMemset(d.err, 0, sizeof(int));
+        return ge::set_error(m, h_err, "GPU execution failed: a device-side wait gave up (code " + std::to_string(h_err) + ")");
+    }
+    m->d2h_bytes += int64_t(bytes);
+    for (int32_t i = 0; i < count && rows_per_image; i++) rows_per_image[i] = prepared[size_t(i)].tokens();
+    return GE_OK;
 }
 
 int ge_tokenizer_load(const char* path, ge_tokenizer** out) {

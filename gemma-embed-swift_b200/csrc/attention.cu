@@ -603,6 +603,7 @@ cudaError_t configure_attention_kernels() {
     cudaError_t e = cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(k_attention_simt<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, simt_smem<512>());
+    if (e == cudaSuccess) e = configure_attention64();
     return e;
 }
 

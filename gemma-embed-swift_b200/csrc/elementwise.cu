@@ -29,10 +29,12 @@ bool programmatic_launch() { return t_programmatic; }
 constexpr int kRowsPerBlock = 8;  // warps per 256-thread block
 
 // x = dequant(table row) * scale, h = rmsnorm(x) * w.  Embedding.swift semantics:
-// CPUReference.swift:190-203 (token rows) and Elementwise.metal:8-35 (padding rows zeroed).
+// CPUReference.swift:190-203 (token rows) and Elementwise.metal:8-35 (padding rows zeroed);
+// an id -(r + 1) takes row r of `vectors` unscaled (an image or audio row, Elementwise.metal:26-30).
 __global__ void k_embed(const int32_t* __restrict__ tokens, int ntok, int rows, const int8_t* __restrict__ tq,
                         const __half* __restrict__ ts, int width, float scale, float* __restrict__ x,
-                        __half* __restrict__ x16, const float* __restrict__ w, float eps, __half* __restrict__ h) {
+                        __half* __restrict__ x16, const float* __restrict__ w, float eps, __half* __restrict__ h,
+                        const float* __restrict__ vectors) {
     pdl_wait();
     pdl_launch_if_one_wave();
     const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
@@ -49,14 +51,24 @@ __global__ void k_embed(const int32_t* __restrict__ tokens, int ntok, int rows, 
         return;
     }
     const long id = tokens[row];
-    const int8_t* q = tq + id * width;
-    const __half* s = ts + id * (width / 32);
     float ss = 0.f;
-    for (int i = lane; i < width; i += 32) {
-        const float v = (__half2float(s[i >> 5]) * float(q[i])) * scale;
-        xr[i] = v;
-        ss += v * v;
-        if (x16) x16[long(row) * width + i] = __float2half_rn(v);
+    if (id < 0) {
+        const float* vr = vectors + (-id - 1) * width;
+        for (int i = lane; i < width; i += 32) {
+            const float v = vr[i];
+            xr[i] = v;
+            ss += v * v;
+            if (x16) x16[long(row) * width + i] = __float2half_rn(v);
+        }
+    } else {
+        const int8_t* q = tq + id * width;
+        const __half* s = ts + id * (width / 32);
+        for (int i = lane; i < width; i += 32) {
+            const float v = (__half2float(s[i >> 5]) * float(q[i])) * scale;
+            xr[i] = v;
+            ss += v * v;
+            if (x16) x16[long(row) * width + i] = __float2half_rn(v);
+        }
     }
     ss = warp_sum(ss);
     const float inv = 1.0f / sqrtf(ss / float(width) + eps);
@@ -65,10 +77,10 @@ __global__ void k_embed(const int32_t* __restrict__ tokens, int ntok, int rows, 
 
 cudaError_t launch_embed(const int32_t* tokens, int ntok, int rows, const int8_t* table_q, const __half* table_s,
                          int width, float scale, float* x, __half* x16, const float* norm_w, float eps, __half* h,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, const float* vectors) {
     if (rows <= 0) return cudaSuccess;
     CK_LAUNCH(launch_kernel(k_embed, dim3((rows + kRowsPerBlock - 1) / kRowsPerBlock), dim3(256), 0, stream, 1, tokens,
-                            ntok, rows, table_q, table_s, width, scale, x, x16, norm_w, eps, h));
+                            ntok, rows, table_q, table_s, width, scale, x, x16, norm_w, eps, h, vectors));
     return cudaGetLastError();
 }
 

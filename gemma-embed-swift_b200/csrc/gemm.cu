@@ -87,11 +87,6 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
-__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
-    __half2 h = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t*>(&h);
-}
-
 // Dequantises 16 int8 values with one fp16 scale into 8 half2 words (exact q, one rounding).
 __device__ __forceinline__ void dequant16(uint4 raw, __half2 s2, uint32_t (&o)[8]) {
     const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
@@ -546,7 +541,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
                     if (c == BN / 32 - 1) release(acc);
                     emit(r, n0 + c * 32, y, &mapC);
                 }
-            } else if (EPI == EPI_GEGLU) {
+            } else if (epi_is_geglu(EPI)) {
                 // Columns [0, BN/2) of the tile are gate rows, [BN/2, BN) the matching up rows.
                 // Per 64 output columns: 64 gate and 64 up values in flight, one wait.
 #pragma unroll 1
@@ -559,9 +554,12 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
                     tmem_wait_ld();
                     if (c == BN / 128 - 1) release(acc);
 #pragma unroll
-                    for (int i = 0; i < 32; i++)
-                        packed[i] = pack_half2(gelu_fast(__uint_as_float(g[2 * i])) * __uint_as_float(u[2 * i]),
-                                               gelu_fast(__uint_as_float(g[2 * i + 1])) * __uint_as_float(u[2 * i + 1]));
+                    for (int i = 0; i < 32; i++) {
+                        const float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
+                        const float a0 = EPI == EPI_GEGLU ? gelu_fast(g0) : gelu_quick_fast(g0);
+                        const float a1 = EPI == EPI_GEGLU ? gelu_fast(g1) : gelu_quick_fast(g1);
+                        packed[i] = pack_half2(a0 * __uint_as_float(u[2 * i]), a1 * __uint_as_float(u[2 * i + 1]));
+                    }
                     emit(packed, n0 / 2 + c * 64, y, &mapC);
                 }
             } else if (EPI == EPI_F16 || EPI == EPI_GELU_MUL) {
@@ -733,7 +731,7 @@ static cudaError_t configure_epi() {
     if (e == cudaSuccess) e = configure_t<EPI, true, false>();
     if constexpr (EPI != EPI_RESIDUAL) {
         if (e == cudaSuccess) e = configure_t<EPI, false, true>();
-        if (EPI != EPI_GEGLU && e == cudaSuccess) e = configure_t<EPI, false, false, 128>();
+        if (!epi_is_geglu(EPI) && e == cudaSuccess) e = configure_t<EPI, false, false, 128>();
     }
     return e;
 }
@@ -746,6 +744,7 @@ cudaError_t configure_gemm_kernels() {
     if (e == cudaSuccess) e = configure_epi<EPI_GEGLU>();
     if (e == cudaSuccess) e = configure_epi<EPI_GELU_MUL>();
     if (e == cudaSuccess) e = configure_epi<EPI_RESIDUAL>();
+    if (e == cudaSuccess) e = configure_epi<EPI_GEGLU_QUICK>();
     return e;
 }
 
@@ -831,7 +830,7 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
     }
     // Output map: boxes of 32 rows x 128 bytes (32 fp32 or 64 fp16 columns), 128-byte swizzle.
     const bool f32 = EPI == EPI_F32;
-    const int out_cols = EPI == EPI_GEGLU ? g.w->N / 2 : g.w->N;
+    const int out_cols = epi_is_geglu(EPI) ? g.w->N / 2 : g.w->N;
     if (g.ldo < out_cols) return cudaErrorInvalidValue;
     if (!encode_2d(&mc, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, f32 ? 4 : 2, g.out,
                    uint64_t(g.ldo), uint64_t(g.m_rows), f32 ? 32 : 64, 32, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -859,7 +858,7 @@ static cudaError_t launch_epi(const GemmLaunch& g, cudaStream_t stream, bool q8,
         return launch_t<EPI, false, false>(g, stream);
     } else {
         if (pair) return launch_t<EPI, false, true>(g, stream);
-        if constexpr (EPI != EPI_GEGLU)
+        if constexpr (!epi_is_geglu(EPI))
             if (narrow) return launch_t<EPI, false, false, 128>(g, stream);
         return launch_t<EPI, false, false>(g, stream);
     }
@@ -875,12 +874,13 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream) {
     const bool pair = !q8 && g.mode == GEMM_PAIR;
     // 128-wide tiles read each A tile twice as often; measured slower on every forward shape,
     // so they run only when asked for.
-    const bool narrow = !q8 && !pair && g.epilogue != EPI_GEGLU && g.mode == GEMM_NARROW;
+    const bool narrow = !q8 && !pair && !epi_is_geglu(g.epilogue) && g.mode == GEMM_NARROW;
     switch (g.epilogue) {
     case EPI_F32: return launch_epi<EPI_F32>(g, stream, q8, pair, narrow);
     case EPI_F16: return launch_epi<EPI_F16>(g, stream, q8, pair, narrow);
     case EPI_GEGLU: return launch_epi<EPI_GEGLU>(g, stream, q8, pair, narrow);
     case EPI_GELU_MUL: return launch_epi<EPI_GELU_MUL>(g, stream, q8, pair, narrow);
+    case EPI_GEGLU_QUICK: return launch_epi<EPI_GEGLU_QUICK>(g, stream, q8, pair, narrow);
     case EPI_RESIDUAL:
         if (g.mode == GEMM_PAIR || g.mode == GEMM_NARROW) return cudaErrorInvalidValue;
         return launch_epi<EPI_RESIDUAL>(g, stream, q8, false, false);

@@ -260,6 +260,14 @@ bool GgufFile::get_bool_array(const std::string& key, std::vector<bool>& out) co
     return true;
 }
 
+bool GgufFile::get_float_array(const std::string& key, std::vector<float>& out) const {
+    auto it = metadata.find(key);
+    if (it == metadata.end() || it->second.type != 9 || it->second.elem != 6) return false;
+    out.resize(it->second.count);
+    memcpy(out.data(), it->second.raw, it->second.count * 4);
+    return true;
+}
+
 bool GgufFile::get_bool(const std::string& key, bool& out) const {
     auto it = metadata.find(key);
     if (it == metadata.end() || it->second.type != 7) return false;

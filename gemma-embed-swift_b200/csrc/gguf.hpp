@@ -65,6 +65,7 @@ public:
     bool get_int_array(const std::string& key, std::vector<int32_t>& out) const;
     bool get_bool_array(const std::string& key, std::vector<bool>& out) const;
     bool get_bool(const std::string& key, bool& out) const;
+    bool get_float_array(const std::string& key, std::vector<float>& out) const;  // float32 elements
     // String array (tokenizer.ggml.tokens, tokenizer.ggml.merges).
     bool get_string_array(const std::string& key, std::vector<std::string>& out) const;
     // Element count of a string array.

@@ -59,7 +59,10 @@ enum GemmEpilogue : int {
     // (y32).  N = the hidden size; the N / 256 CTAs of a cluster hold one row block's columns
     // and exchange the per-row sums of squares through distributed shared memory.
     EPI_RESIDUAL = 4,
+    // As EPI_GEGLU with the quick GELU of the vision tower: out = gate / (1 + exp(-1.702 gate)) * up.
+    EPI_GEGLU_QUICK = 5,
 };
+__host__ __device__ constexpr bool epi_is_geglu(int epi) { return epi == EPI_GEGLU || epi == EPI_GEGLU_QUICK; }
 
 
 // One GEMM weight as the device keeps it: the Q8_0 planes (int8 values [N][K] and the fp16
@@ -121,10 +124,11 @@ cudaError_t configure_attention_kernels();
 
 // ------------------------------------------------------------------ elementwise
 // x[t] = q8row(table[id]) * scale for t < ntok, 0 for padded rows; h = rmsnorm(x) * w (fp16).
-// Optionally also x16 = fp16(x) (the per-layer-input GEMM's operand).
+// Optionally also x16 = fp16(x) (the per-layer-input GEMM's operand).  An id -(r + 1) takes
+// row r of `vectors` ([*][width] fp32, device) unscaled; ids below zero need `vectors`.
 cudaError_t launch_embed(const int32_t* tokens, int ntok, int rows, const int8_t* table_q, const __half* table_s,
                          int width, float scale, float* x, __half* x16, const float* norm_w, float eps, __half* h,
-                         cudaStream_t stream);
+                         cudaStream_t stream, const float* vectors = nullptr);
 
 // Per (token, head): q, k = rope(rmsnorm(head) * w); v = rmsnorm(head). Reads the fused
 // projection output qkv (fp16, [rows][(H + 2 KV) * hd]) and writes fp16 q, k, v; rows at or
@@ -178,6 +182,51 @@ cudaError_t launch_dense_f32(const float* in, int nrows, const float* w, int N, 
 
 // positions[start + i] = i over the sequences (start, length) pairs.
 cudaError_t launch_positions(const uint32_t* seqs, int nseq, int32_t* positions, cudaStream_t stream);
+
+// ------------------------------------------------------------------ vision tower
+// One image of a vision batch: its bytes in the batch's RGB buffer (rows of gx * patch pixels,
+// 3 bytes each), its patch grid, and where its patch rows and its pooled token rows start.
+struct VisionImage {
+    uint64_t rgb_offset;
+    int32_t gx, gy;
+    uint32_t patch_start, token_start;
+};
+struct NormParams {
+    float mean[3], std[3];
+};
+// patches[patch_start + py * gx + px][c * p^2 + ky * p + kx] = fp16(2 (byte / 255 - mean[c]) /
+// std[c] - 1), columns [3 p^2, kpad) zero (PreparedImage.init, ImagePreprocessor.swift:31-60).
+cudaError_t launch_patchify(const uint8_t* rgb, const VisionImage* imgs, int nimg, int max_patches, int p, int kpad,
+                            const NormParams& np, __half* patches, cudaStream_t stream);
+// x[r] = (x[r] + pos[px]) + pos[npos + py] with (px, py) = (xy & 0xffff, xy >> 16); h = fp16(
+// rmsnorm(x) * w); rows at or past ntok get h = 0.
+cudaError_t launch_patch_position_norm(float* x, const uint32_t* xy, int ntok, int rows, int d, const float* pos,
+                                       int npos, const float* w, float eps, __half* h, cudaStream_t stream);
+// Per token and head of 64: q, k = rope2d(rmsnorm(head) * w), v = rmsnorm(head); reads the fused
+// [rows][3 heads * 64] projection, writes [rows][heads * 64] each (zeros past ntok).  `rope` is
+// [position][16][cos, sin] (RopeTable with head dim 32).
+cudaError_t launch_vision_qkv_norm_rope(const __half* qkv, int ntok, int rows, int heads, const float* qw,
+                                        const float* kw, const uint32_t* xy, const float* rope, float eps, __half* q,
+                                        __half* k, __half* v, cudaStream_t stream);
+// out[token_start + t] = fp16(rmsnorm(scale * sum of the token's merge x merge patch rows)).
+cudaError_t launch_pool_patches_norm(const float* x, const VisionImage* imgs, int nimg, int max_tokens, int d, int merge,
+                                     float scale, float eps, __half* out, cudaStream_t stream);
+
+// Tensor-core attention for head dim 64 without a mask inside each sequence (the vision
+// tower's, Shaders/Attention.metal:190-312): q, k, v [rows][heads * 64] fp16, out the same.
+// `work` is build_attention_work's schedule with kv_heads = heads and group 1.
+struct Attn64Launch {
+    const __half* q;
+    const __half* k;
+    const __half* v;
+    __half* out;
+    int rows, heads;
+    const uint32_t* work;  // items, then the CTAs' item offsets
+    int sched_items, ctas;
+    int* err;
+};
+cudaError_t launch_attention64(const Attn64Launch& a, cudaStream_t stream);
+cudaError_t configure_attention64();  // part of configure_attention_kernels
 
 // ------------------------------------------------------------------ attention
 // TMA descriptors of the q, k and v buffers for the tensor-core attention kernel.

@@ -3,6 +3,7 @@
 // ModelConfig / ModelWeights (Model/ModelConfig.swift:54-112, Model/Weights.swift:92-132) and
 // MetalForward.execute / encode (Metal/MetalForward.swift:310-423).
 #include "model.hpp"
+#include "weights.hpp"
 
 #include <math.h>
 #include <string.h>
@@ -34,25 +35,7 @@ int set_error(ge_model* m, int code, const std::string& msg) {
 namespace {
 
 constexpr int kQ8GemmMaxRows = 256;  // batches at or below this many rows read Q8 weights directly
-constexpr int kBN = 256;
 
-int round_up(int v, int m) { return (v + m - 1) / m * m; }
-
-float half_bits_to_float(uint16_t h) {
-    __half_raw r;
-    r.x = h;
-    return __half2float(__half(r));
-}
-uint16_t float_to_half_bits(float f) {
-    __half h = __float2half_rn(f);
-    return __half_raw(h).x;
-}
-
-// ------------------------------------------------------------------ config
-struct LoadError {
-    int code;
-    std::string msg;
-};
 
 bool read_config(const GgufFile& f, Config& c, LoadError& e) {
     if (!f.get_string("general.architecture", c.arch)) c.arch.clear();
@@ -142,161 +125,9 @@ bool read_config(const GgufFile& f, Config& c, LoadError& e) {
     return true;
 }
 
-// ModelWeights' shape and type checks (Weights.swift:93-98).
-const GgufTensor* need_tensor(const GgufFile& f, const std::string& name, std::vector<int64_t> shape, bool f32_only,
-                              LoadError& e) {
-    const GgufTensor* t = f.tensor(name);
-    auto fmt = [](const std::vector<int64_t>& s) {
-        std::string r = "[";
-        for (size_t i = 0; i < s.size(); i++) r += (i ? ", " : "") + std::to_string(s[i]);
-        return r + "]";
-    };
-    if (!t) {
-        e = {GE_ERR_MISSING_TENSOR, "weight file lacks tensor " + name};
-        return nullptr;
-    }
-    if (t->shape != shape) {
-        e = {GE_ERR_SHAPE_MISMATCH, "tensor " + name + " has shape " + fmt(t->shape) + ", expected " + fmt(shape)};
-        return nullptr;
-    }
-    if (f32_only && t->type != GGML_F32) {
-        e = {GE_ERR_UNSUPPORTED_TENSOR_TYPE, "tensor " + name + " uses unsupported storage type " + std::to_string(t->type)};
-        return nullptr;
-    }
-    return t;
-}
-
-// Dequantised fp32 row of a tensor (WeightTensor.dequantizeRow, Weights.swift:19-43).
-void dequant_row(const GgufTensor& t, int64_t row, float* out) {
-    const int64_t n = t.cols();
-    const uint8_t* p = t.data + row * (n / ggml_block_elems(t.type) * ggml_block_bytes(t.type));
-    switch (t.type) {
-    case GGML_F32: memcpy(out, p, size_t(n) * 4); break;
-    case GGML_F16:
-        for (int64_t i = 0; i < n; i++) {
-            uint16_t h;
-            memcpy(&h, p + 2 * i, 2);
-            out[i] = half_bits_to_float(h);
-        }
-        break;
-    case GGML_BF16:
-        for (int64_t i = 0; i < n; i++) {
-            uint16_t h;
-            memcpy(&h, p + 2 * i, 2);
-            uint32_t b = uint32_t(h) << 16;
-            memcpy(&out[i], &b, 4);
-        }
-        break;
-    case GGML_Q8_0:
-        for (int64_t b = 0; b < n / 32; b++) {
-            uint16_t h;
-            memcpy(&h, p + b * 34, 2);
-            const float s = half_bits_to_float(h);
-            for (int j = 0; j < 32; j++) out[b * 32 + j] = s * float(int8_t(p[b * 34 + 2 + j]));
-        }
-        break;
-    }
-}
-
-template <class F>
-void parallel_rows(int64_t rows, F fn) {
-    const int nt = std::max(1, std::min<int>(16, int(std::thread::hardware_concurrency())));
-    std::vector<std::thread> th;
-    for (int t = 0; t < nt; t++)
-        th.emplace_back([=]() {
-            for (int64_t r = t; r < rows; r += nt) fn(r);
-        });
-    for (auto& x : th) x.join();
-}
-
-// A GEMM weight assembled on the host from one or more GGUF tensors stacked along N.
-// `rows_of(dst_row)` names the (tensor, source row) each destination row comes from.
-struct HostWeight {
-    int N = 0, K = 0;
-    bool q8 = true;
-    std::vector<int8_t> q;
-    std::vector<uint16_t> scales_t;  // [K/32][N]
-    std::vector<uint16_t> f16;       // [N][K]
-};
-
-template <class RowFn>
-HostWeight build_weight(int N, int K, bool want_f16, RowFn src) {
-    HostWeight w;
-    w.N = N;
-    w.K = K;
-    const GgufTensor* t0 = src(0).first;
-    w.q8 = t0->type == GGML_Q8_0;
-    for (int r = 1; r < N && w.q8; r++) w.q8 = src(r).first->type == GGML_Q8_0;
-    if (w.q8) {
-        w.q.resize(size_t(N) * K);
-        w.scales_t.resize(size_t(N) * (K / 32));
-    }
-    if (want_f16 || !w.q8) w.f16.resize(size_t(N) * K);
-    parallel_rows(N, [&](int64_t r) {
-        auto s = src(int(r));
-        const GgufTensor& t = *s.first;
-        if (w.q8) {
-            const uint8_t* p = t.data + int64_t(s.second) * (K / 32) * 34;
-            for (int b = 0; b < K / 32; b++) {
-                uint16_t h;
-                memcpy(&h, p + b * 34, 2);
-                w.scales_t[size_t(b) * N + r] = h;
-                const float sc = half_bits_to_float(h);
-                for (int j = 0; j < 32; j++) {
-                    const int8_t qv = int8_t(p[b * 34 + 2 + j]);
-                    w.q[size_t(r) * K + b * 32 + j] = qv;
-                    // scale * q is exact in fp32; one round to nearest gives the fp16 operand.
-                    if (!w.f16.empty()) w.f16[size_t(r) * K + b * 32 + j] = float_to_half_bits(sc * float(qv));
-                }
-            }
-        } else {
-            std::vector<float> row(K);
-            dequant_row(t, s.second, row.data());
-            for (int k = 0; k < K; k++) w.f16[size_t(r) * K + k] = float_to_half_bits(row[k]);
-        }
-    });
-    return w;
-}
-
-std::vector<float> dequant_matrix(const GgufTensor& t) {
-    std::vector<float> out(size_t(t.elements()));
-    parallel_rows(t.rows(), [&](int64_t r) { dequant_row(t, r, out.data() + r * t.cols()); });
-    return out;
-}
-
 }  // namespace
 
 // ------------------------------------------------------------------ device memory helpers
-template <class T>
-static cudaError_t dev_alloc(Device& d, T** p, size_t count) {
-    void* q = nullptr;
-    cudaError_t e = cudaMalloc(&q, std::max<size_t>(count, 1) * sizeof(T));
-    if (e != cudaSuccess) return e;
-    d.allocations.push_back(q);
-    *p = static_cast<T*>(q);
-    return cudaSuccess;
-}
-
-template <class T>
-static cudaError_t dev_upload(Device& d, T** p, const T* src, size_t count) {
-    cudaError_t e = dev_alloc(d, p, count);
-    if (e == cudaSuccess && count) e = cudaMemcpy(*p, src, count * sizeof(T), cudaMemcpyHostToDevice);
-    return e;
-}
-
-static cudaError_t upload_weight(Device& d, DevWeight& w, const HostWeight& h) {
-    w.N = h.N;
-    w.K = h.K;
-    cudaError_t e = cudaSuccess;
-    if (h.q8) {
-        e = dev_upload(d, &w.q8, h.q.data(), h.q.size());
-        if (e == cudaSuccess) e = dev_upload(d, reinterpret_cast<uint16_t**>(&w.scales_t), h.scales_t.data(), h.scales_t.size());
-    }
-    if (e == cudaSuccess && !h.f16.empty())
-        e = dev_upload(d, reinterpret_cast<uint16_t**>(&w.f16), h.f16.data(), h.f16.size());
-    if (e == cudaSuccess && !encode_weight_maps(w, kBN)) e = cudaErrorInvalidValue;
-    return e;
-}
 
 static void free_workspace(Workspace& ws) {
     for (void* p : {(void*)ws.tokens, (void*)ws.positions, (void*)ws.seqs, (void*)ws.work, (void*)ws.x, (void*)ws.qkv16,
@@ -435,15 +266,15 @@ static int load_device(ge_model* m, Device& d, const std::vector<HostWeight>& hw
                          std::string("device upload failed: ") + cudaGetErrorString(x));
     };
     if (e != cudaSuccess) return fail(e);
-    if ((e = dev_alloc(d, &d.err, 1)) != cudaSuccess || (e = cudaMemset(d.err, 0, sizeof(int))) != cudaSuccess) return fail(e);
+    if ((e = dev_alloc(d.allocations, &d.err, 1)) != cudaSuccess || (e = cudaMemset(d.err, 0, sizeof(int))) != cudaSuccess) return fail(e);
     // Token embedding table: int8 plane [V][d] and fp16 scales [V][d/32].
-    if ((e = dev_upload(d, &d.emb_q, emb.q.data(), emb.q.size())) != cudaSuccess) return fail(e);
-    if ((e = dev_upload(d, reinterpret_cast<uint16_t**>(&d.emb_s), emb.scales_t.data(), emb.scales_t.size())) != cudaSuccess)
+    if ((e = dev_upload(d.allocations, &d.emb_q, emb.q.data(), emb.q.size())) != cudaSuccess) return fail(e);
+    if ((e = dev_upload(d.allocations, reinterpret_cast<uint16_t**>(&d.emb_s), emb.scales_t.data(), emb.scales_t.size())) != cudaSuccess)
         return fail(e);
     size_t ni = 0, wi = 0;
     cudaError_t norm_err = cudaSuccess;
     auto norm = [&](float** p) {
-        cudaError_t x = dev_upload(d, p, norms[ni].data(), norms[ni].size());
+        cudaError_t x = dev_upload(d.allocations, p, norms[ni].data(), norms[ni].size());
         if (norm_err == cudaSuccess) norm_err = x;
         ni++;
     };
@@ -451,10 +282,10 @@ static int load_device(ge_model* m, Device& d, const std::vector<HostWeight>& hw
     for (int l = 0; l < c.layers; l++) {
         LayerDev& L = d.layers[l];
         for (DevWeight* w : {&L.qkv, &L.o, &L.gu, &L.down})
-            if ((e = upload_weight(d, *w, hw[wi++])) != cudaSuccess) return fail(e);
+            if ((e = upload_weight(d.allocations, *w, hw[wi++])) != cudaSuccess) return fail(e);
         if (c.has_ple)
             for (DevWeight* w : {&L.inp_gate, &L.proj})
-                if ((e = upload_weight(d, *w, hw[wi++])) != cudaSuccess) return fail(e);
+                if ((e = upload_weight(d.allocations, *w, hw[wi++])) != cudaSuccess) return fail(e);
         norm(&L.attn_norm);
         norm(&L.q_norm);
         norm(&L.k_norm);
@@ -469,19 +300,19 @@ static int load_device(ge_model* m, Device& d, const std::vector<HostWeight>& hw
     norm(&d.out_norm);
     if (c.has_ple) {
         norm(&d.pl_norm);
-        if ((e = upload_weight(d, d.plp, *plp)) != cudaSuccess) return fail(e);
+        if ((e = upload_weight(d.allocations, d.plp, *plp)) != cudaSuccess) return fail(e);
     }
     if (norm_err != cudaSuccess) return fail(norm_err);
     for (const std::vector<float>& r : ropes) {
         float* p = nullptr;
-        if ((e = dev_upload(d, &p, r.data(), r.size())) != cudaSuccess) return fail(e);
+        if ((e = dev_upload(d.allocations, &p, r.data(), r.size())) != cudaSuccess) return fail(e);
         d.rope.push_back(p);
     }
     if (c.has_dense) {
-        if ((e = dev_upload(d, &d.dense2, dense2.data(), dense2.size())) != cudaSuccess) return fail(e);
-        if ((e = dev_upload(d, &d.dense3, dense3.data(), dense3.size())) != cudaSuccess) return fail(e);
+        if ((e = dev_upload(d.allocations, &d.dense2, dense2.data(), dense2.size())) != cudaSuccess) return fail(e);
+        if ((e = dev_upload(d.allocations, &d.dense3, dense3.data(), dense3.size())) != cudaSuccess) return fail(e);
     }
-    if (c.has_output && (e = dev_upload(d, &d.output, output.data(), output.size())) != cudaSuccess) return fail(e);
+    if (c.has_output && (e = dev_upload(d.allocations, &d.output, output.data(), output.size())) != cudaSuccess) return fail(e);
     if ((e = noalloc_setup(d.ordinal)) != cudaSuccess) return fail(e);
     if ((e = configure_gemm_kernels()) != cudaSuccess || (e = configure_attention_kernels()) != cudaSuccess)
         return fail(e);
@@ -495,6 +326,7 @@ static void free_device(Device& d) {
     }
     clear_graphs(d);
     free_workspace(d.ws);
+    free_vision(d);
     for (void* p : d.allocations) cudaFree(p);
     d.allocations.clear();
     if (d.stream) cudaStreamDestroy(d.stream);
@@ -936,7 +768,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         CK(K("embed", 0, double(ntok) * D * (1 + 2.0 / 32 + 4 + 2),
              [&] {
                  return launch_embed(tokens, ntok, rows, d.emb_q, d.emb_s, D, c.emb_scale, ws.x, c.has_ple ? ws.x16 : nullptr,
-                                     d.layers[0].attn_norm, c.eps, ws.h, ks);
+                                     d.layers[0].attn_norm, c.eps, ws.h, ks, a.vectors);
              }),
            "embed");
         if (c.has_ple) {
@@ -1121,6 +953,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     gk.pool_chunks = max_chunks;
     for (int k = 0; k < 4; k++) gk.sched[k] = sched[k];
     gk.tokens = reinterpret_cast<uintptr_t>(tokens);
+    gk.vectors = reinterpret_cast<uintptr_t>(a.vectors);
     GraphEntry* ge_ = use_graph ? find_graph(d, gk) : nullptr;
     if (ge_) {
         if ((e = cudaGraphLaunch(ge_->exec, st)) != cudaSuccess) return gpu_fail(e, "graph launch");

@@ -14,6 +14,7 @@
 #include "gguf.hpp"
 #include "kernels.hpp"
 #include "tokenizer.hpp"
+#include "vision.hpp"
 
 namespace ge {
 
@@ -74,9 +75,11 @@ struct GraphKey {
     int rows = 0, ntok = 0, nseq = 0, nwork512 = 0, pool_chunks = 0;
     int sched[4] = {0, 0, 0, 0};  // attention schedules: (items, CTAs) for sliding and global layers
     uintptr_t tokens = 0;         // the token buffer the embedding kernel reads
+    uintptr_t vectors = 0;        // and the vector rows it copies (image or audio rows), if any
     bool operator==(const GraphKey& o) const {
         return rows == o.rows && ntok == o.ntok && nseq == o.nseq && nwork512 == o.nwork512 &&
-               pool_chunks == o.pool_chunks && tokens == o.tokens && sched[0] == o.sched[0] && sched[1] == o.sched[1] &&
+               pool_chunks == o.pool_chunks && tokens == o.tokens && vectors == o.vectors && sched[0] == o.sched[0] &&
+               sched[1] == o.sched[1] &&
                sched[2] == o.sched[2] && sched[3] == o.sched[3];
     }
 };
@@ -103,6 +106,7 @@ struct Device {
     std::vector<GraphEntry> graphs;  // at most kMaxGraphs, least recently used evicted
     uint64_t graph_clock = 0;
     std::vector<void*> allocations;
+    VisionDev vis;  // the image encoder's weights and workspace, when one is loaded
 };
 
 }  // namespace ge
@@ -123,6 +127,13 @@ struct ge_model {
     std::atomic<int64_t> launches{0};  // kernel launches issued by this model so far
     std::atomic<int64_t> h2d_bytes{0}, d2h_bytes{0};  // host <-> device copies of the forwards so far
     std::unique_ptr<ge_tokenizer> tokenizer;  // null when the file carries no tokenizer
+    // The image encoder (LoadOptions.imageEncoder): its file, configuration and the tokens that
+    // frame an image's rows in the text sequence (SpanMarkers.image, Model/InputRow.swift:43-45).
+    bool has_vision = false;
+    ge::GgufFile vision_file;
+    ge::VisionConfig vcfg;
+    int32_t image_begin = -1, image_end = -1;
+    int patch_budget = 4096;  // ImageEmbedOptions.patchBudget unless the load options raise it
 };
 
 namespace ge {
@@ -165,8 +176,17 @@ struct ForwardArgs {
     float* trace_out = nullptr;
     std::string* error = nullptr;   // where failures are reported; nullptr: the model's last_error
     ProfileSink* profile = nullptr;  // time each kernel class instead of only running it
+    // Device rows ([vector_rows][hidden] fp32) that ids below zero stand for: id -(r + 1) is
+    // row r (an image's projected rows).  Checked by the caller.
+    const float* vectors = nullptr;
+    int vector_rows = 0;
 };
 int run_forward(ge_model* m, Device& d, const ForwardArgs& a);
+// The image encoder: load (after the text model) and one forward over prepared images, whose
+// projected rows land in d.vis.ws.vectors (image i's rows from sum of earlier token counts).
+int load_vision(ge_model* m, const char* path);
+void free_vision(Device& d);
+int run_vision(ge_model* m, Device& d, const PreparedImage* const* imgs, int n, std::string* error);
 GraphEntry* find_graph(Device& d, const GraphKey& k);
 // The multi-GPU dispatcher's split of a packed batch: the sequence indices of each device,
 // longest first onto the least-loaded device (cost n + n^2 / 2048), each in original order.

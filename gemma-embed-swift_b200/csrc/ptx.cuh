@@ -306,6 +306,19 @@ __device__ __forceinline__ float gelu_fast(float x) {
     return __fdividef(x, 1.0f + e);
 }
 
+// Two floats rounded to fp16 and packed as one 32-bit word (the first in the low half).
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// The vision tower's quick GELU, x * sigmoid(1.702 x) (CPUVisionReference.geluQuick,
+// Model/CPUVisionReference.swift:40-42), with one ex2.approx and a fast divide.
+__device__ __forceinline__ float gelu_quick_fast(float x) {
+    constexpr float k = -1.702f * 1.4426950408889634f;  // -1.702 log2(e)
+    return __fdividef(x, 1.0f + ex2_approx(x * k));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -7,6 +7,7 @@
 #include "gemma_embed_testing.h"
 #include "kernels.hpp"
 #include "model.hpp"
+#include "vision.hpp"
 
 namespace {
 
@@ -119,8 +120,8 @@ static int upload_activation(const uint16_t* a, int m, int k, int rows, DevBuf& 
 
 int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int32_t n, int32_t epilogue, int32_t use_q8,
                  const float* aux, float* out) {
-    if (m <= 0 || k <= 0 || n <= 0 || k % 64 || n % 256 || !a || !w || !out || epilogue < 0 || epilogue > 3 ||
-        (epilogue == 3 && !aux))
+    if (m <= 0 || k <= 0 || n <= 0 || k % 64 || n % 256 || !a || !w || !out || epilogue < 0 || epilogue > 5 ||
+        epilogue == ge::EPI_RESIDUAL || (epilogue == 3 && !aux))
         return fail(GE_ERR_INVALID_OPTIONS, "invalid options: shapes must be k % 64 == 0 and n % 256 == 0");
     const int rows = (m + ge::kRowTile - 1) / ge::kRowTile * ge::kRowTile;
     int dev = 0, sms = 0;
@@ -132,7 +133,7 @@ int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int3
     int rc = upload_weight(w, n, k, dq, ds, dh, W);
     if (rc != GE_OK) return rc;
     if ((rc = upload_activation(a, m, k, rows, da, A)) != GE_OK) return rc;
-    const int out_cols = epilogue == 2 ? n / 2 : n;
+    const int out_cols = ge::epi_is_geglu(epilogue) ? n / 2 : n;
     const size_t out_elem = epilogue == 0 ? 4 : 2;
     TRY(dout.alloc(size_t(rows) * out_cols * out_elem));
     TRY(derr.alloc(sizeof(int)));
@@ -239,7 +240,7 @@ int ge_test_gemm_residual(const uint16_t* a, int32_t m, int32_t k, const uint8_t
 int ge_test_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, int32_t ntok, const ge_seq* seqs,
                       int32_t nseq, int32_t heads, int32_t kvh, int32_t hd, int32_t half_window, uint16_t* out) {
     if (ntok <= 0 || nseq <= 0 || !q || !k || !v || !seqs || !out || heads <= 0 || kvh <= 0 || heads % kvh ||
-        (hd != 256 && hd != 512) || half_window < 0)
+        (hd != 64 && hd != 256 && hd != 512) || half_window < 0 || (hd == 64 && (kvh != heads || half_window != 0)))
         return fail(GE_ERR_INVALID_OPTIONS, "invalid options");
     uint64_t next = 0;
     for (int s = 0; s < nseq; s++) {
@@ -253,7 +254,7 @@ int ge_test_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
     TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     std::vector<uint32_t> work;
     int items = 0, ctas = 0;
-    if (hd == 256) {
+    if (hd == 256 || hd == 64) {
         std::vector<uint32_t> pairs;
         for (int s = 0; s < nseq; s++) {
             pairs.push_back(seqs[s].start);
@@ -303,6 +304,26 @@ int ge_test_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
     al.half_window = half_window;
     al.err = static_cast<int*>(derr.p);
     al.num_sms = sms;
+    if (hd == 64) {
+        ge::Attn64Launch a6;
+        a6.q = al.q;
+        a6.k = al.k;
+        a6.v = al.v;
+        a6.out = al.out;
+        a6.rows = rows;
+        a6.heads = heads;
+        a6.work = al.work;
+        a6.sched_items = items;
+        a6.ctas = ctas;
+        a6.err = al.err;
+        TRY(ge::launch_attention64(a6, nullptr));
+        TRY(cudaDeviceSynchronize());
+        int herr = 0;
+        TRY(cudaMemcpy(&herr, derr.p, sizeof(int), cudaMemcpyDeviceToHost));
+        if (herr) return fail(herr, "GPU execution failed: a device-side wait timed out");
+        TRY(cudaMemcpy(out, dout.p, size_t(ntok) * heads * hd * 2, cudaMemcpyDeviceToHost));
+        return GE_OK;
+    }
     ge::AttnMaps maps;
     if (hd == 256) {
         if (!ge::encode_attention_maps(maps, al.q, al.k, al.v, rows, heads, kvh, hd))
@@ -315,6 +336,49 @@ int ge_test_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
     TRY(cudaMemcpy(&herr, derr.p, sizeof(int), cudaMemcpyDeviceToHost));
     if (herr) return fail(herr, "GPU execution failed: a device-side wait timed out");
     TRY(cudaMemcpy(out, dout.p, size_t(ntok) * heads * hd * 2, cudaMemcpyDeviceToHost));
+    return GE_OK;
+}
+
+int ge_test_image_prepare(int32_t patch, int32_t merge, int32_t min_tokens, const uint8_t* rgb, int32_t w, int32_t h,
+                          int32_t max_tokens, uint8_t* out, int64_t cap, int32_t* tw, int32_t* th) {
+    if (patch <= 0 || merge <= 0 || !rgb || w <= 0 || h <= 0 || max_tokens <= 0 || !tw || !th)
+        return fail(GE_ERR_INVALID_OPTIONS, "invalid options");
+    ge::VisionConfig c;
+    c.patch = patch;
+    c.merge = merge;
+    c.min_image_tokens = min_tokens;
+    ge::PreparedImage im;
+    ge::prepare_image(c, rgb, w, h, max_tokens, im);
+    *tw = im.width;
+    *th = im.height;
+    if (int64_t(im.rgb.size()) > cap || (cap > 0 && !out)) return fail(GE_ERR_INVALID_OPTIONS, "output capacity too small");
+    memcpy(out, im.rgb.data(), im.rgb.size());
+    return GE_OK;
+}
+
+int ge_test_patchify(const uint8_t* rgb, int32_t w, int32_t h, int32_t patch, const float* mean, const float* std_,
+                     uint16_t* out, int32_t kpad) {
+    if (!rgb || w <= 0 || h <= 0 || patch <= 0 || w % patch || h % patch || !mean || !std_ || !out ||
+        kpad < 3 * patch * patch)
+        return fail(GE_ERR_INVALID_OPTIONS, "invalid options");
+    const int gx = w / patch, gy = h / patch;
+    const size_t bytes = size_t(w) * h * 3, n = size_t(gx) * gy * kpad;
+    DevBuf drgb, dimg, dout;
+    TRY(drgb.alloc(bytes));
+    TRY(dimg.alloc(sizeof(ge::VisionImage)));
+    TRY(dout.alloc(n * 2));
+    TRY(cudaMemcpy(drgb.p, rgb, bytes, cudaMemcpyHostToDevice));
+    const ge::VisionImage im{0, gx, gy, 0, 0};
+    TRY(cudaMemcpy(dimg.p, &im, sizeof im, cudaMemcpyHostToDevice));
+    ge::NormParams np;
+    for (int i = 0; i < 3; i++) {
+        np.mean[i] = mean[i];
+        np.std[i] = std_[i];
+    }
+    TRY(ge::launch_patchify(static_cast<const uint8_t*>(drgb.p), static_cast<const ge::VisionImage*>(dimg.p), 1, gx * gy,
+                            patch, kpad, np, static_cast<__half*>(dout.p), nullptr));
+    TRY(cudaDeviceSynchronize());
+    TRY(cudaMemcpy(out, dout.p, n * 2, cudaMemcpyDeviceToHost));
     return GE_OK;
 }
 

@@ -38,7 +38,9 @@ typedef enum ge_status {
     GE_ERR_GPU_FAILURE = 10,           /* .gpuFailure */
     GE_ERR_OUT_OF_MEMORY = 11,         /* workspace growth failed (a .gpuFailure in the reference) */
     GE_ERR_TIMEOUT = 12,               /* a bounded device-side wait gave up (a .gpuFailure in the reference) */
-    GE_ERR_CANCELLED = 13              /* .cancelled */
+    GE_ERR_CANCELLED = 13,             /* .cancelled */
+    GE_ERR_IMAGE_DECODING = 14,        /* .imageDecoding: an image's pixels or size are unusable */
+    GE_ERR_IMAGE_ENCODER_NOT_LOADED = 15 /* .imageEncoderNotLoaded */
 } ge_status;
 
 typedef struct ge_model ge_model;
@@ -54,6 +56,12 @@ typedef struct ge_load_opts {
     uint32_t device_mask;       /* bit i selects CUDA device i; 0 selects device 0 */
     int32_t batch_token_budget; /* LoadOptions.batchTokenBudget; default 8192, at least 64 */
     uint32_t flags;             /* GE_LOAD_* bits */
+    /* LoadOptions.imageEncoder: the mmproj GGUF whose gemma4v tower ge_embed_images needs;
+     * NULL loads none (EmbedOptions.swift:183-187). */
+    const char* image_encoder_path;
+    /* Image patches per GPU batch when ge_image_opts.batch_size is 0; default 4096
+     * (ImageEmbedOptions.patchBudget, EmbedOptions.swift:84-87), at least one image per batch. */
+    int32_t image_patch_budget;
 } ge_load_opts;
 
 #define GE_LOAD_NO_GRAPHS 1u      /* launch kernels directly instead of replaying captured CUDA graphs */
@@ -95,6 +103,11 @@ typedef struct ge_info {
     int64_t kernel_launches; /* CUDA kernels this model has launched so far, on all devices */
     int64_t host_to_device_bytes; /* bytes the forwards so far copied from host to device */
     int64_t device_to_host_bytes; /* and from device to host */
+    /* ImageEncoderInfo (VisionConfig.swift:5-17); all zero without an image encoder. */
+    int32_t image_layer_count;
+    int32_t image_hidden_size;
+    int32_t image_patch_size;
+    int32_t image_projection_dim;
 } ge_info;
 
 /* One kernel class of a profiling forward (ge_profile). */
@@ -242,6 +255,44 @@ GE_API int ge_task_prefix(int32_t task, const char* arg, char* text, int64_t cap
 GE_API int ge_embed_texts(ge_model* model, const char* const* texts, const int64_t* lengths, int32_t count,
                           const char* prefix, const ge_embed_opts* opts, float* out, int32_t* token_counts,
                           int32_t* truncated, ge_progress_fn progress, void* user);
+
+/* ---- Images (ImageEmbedding.swift, Metal/VisionTower.swift) -------------------------------- */
+
+/* A decoded image: `height` rows of `width` RGB8 pixels, interleaved (RGBImage,
+ * Image/ImageInput.swift:17-26).  Decoding files (JPEG, PNG) is the caller's. */
+typedef struct ge_image {
+    const uint8_t* rgb;
+    int32_t width;
+    int32_t height;
+} ge_image;
+
+/* ImageEmbedOptions (EmbedOptions.swift:59-88). */
+typedef struct ge_image_opts {
+    int32_t dimensions;       /* 768, 512, 256 or 128 */
+    int32_t normalise;
+    int32_t max_image_tokens; /* 1 .. 1120; default 256 */
+    int32_t batch_size;       /* images per batch; 0 packs by the load options' patch budget */
+} ge_image_opts;
+
+GE_API void ge_image_opts_default(ge_image_opts* opts);
+
+/* EmbeddingModel.embed(images:options:progress:) (ImageEmbedding.swift:17-33): each image is
+ * resized to its patch grid (ImagePreprocessor.prepare), run through the vision tower, and its
+ * rows, framed as [bos, <|image>, rows..., <image|>, eos], through the text tower, then finished
+ * like a text.  `out` receives count * dimensions floats; `token_counts` (may be NULL) the rows
+ * the text tower saw (image tokens + 4).  GE_ERR_IMAGE_ENCODER_NOT_LOADED without an encoder. */
+GE_API int ge_embed_images(ge_model* model, const ge_image* images, int32_t count, const ge_image_opts* opts, float* out,
+                           int32_t* token_counts, ge_progress_fn progress, void* user);
+
+/* PreparedImage.tokenCount (Image/ImagePreprocessor.swift:25-27) of a width x height image at
+ * `max_image_tokens`: the rows ge_image_vectors returns for it; -1 without an image encoder. */
+GE_API int32_t ge_image_tokens(const ge_model* model, int32_t width, int32_t height, int32_t max_image_tokens);
+
+/* MetalForward.imageVectors (Metal/MetalForward.swift:227-238): the vision tower's projected rows
+ * of each image, concatenated in order ([sum of rows][projection_dim] floats, at most cap_rows
+ * rows); rows_per_image (count entries) receives each image's token count. */
+GE_API int ge_image_vectors(ge_model* model, const ge_image* images, int32_t count, int32_t max_image_tokens,
+                            float* out, int64_t cap_rows, int32_t* rows_per_image);
 
 /* No counterpart in the reference.  The last stage of the forward -- mean-pool over each
  * sequence, then the dense head (or the output projection) -- for callers that cannot allocate

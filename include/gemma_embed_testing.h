@@ -19,7 +19,8 @@ extern "C" {
 /* Kernels.gemm (Metal/MetalForward.swift:513-557): out = a * W^T for a fp16 `a` [m][k]
  * (bit patterns) and a Q8_0 weight given as GGUF rows `w_q8_0` [n][k/32 * 34 bytes].
  * epilogue: 0 fp32 store, 1 fp16 store, 2 GeGLU over rows interleaved as the loader does
- * (out has n/2 columns), 3 gelu(acc) * aux (aux fp32 [m][n]).  path: 0 fp16-resident
+ * (out has n/2 columns), 3 gelu(acc) * aux (aux fp32 [m][n]), 5 the vision tower's GeGLU
+ * with the quick GELU (interleaved like 2).  path: 0 fp16-resident
  * weights on single CTAs, 1 the in-shared-memory Q8 dequantisation, 2 fp16 weights on CTA
  * pairs (tcgen05.mma.cta_group::2), 3 fp16 weights on single CTAs with 128-wide tiles (not
  * for the GeGLU epilogue).  Results are returned as fp32 [m][n] (or [m][n/2]). */
@@ -38,6 +39,7 @@ GE_API int ge_test_gemm_residual(const uint16_t* a, int32_t m, int32_t k, const 
 /* Kernels.attention (Metal/MetalForward.swift:669-694): q [ntok][heads][hd], k and v
  * [ntok][kv_heads][hd] as fp16 bit patterns, sequences tiling [0, ntok); out receives fp16
  * bit patterns [ntok][heads][hd].  half_window 0 is global attention. */
+/* Head dim 64 (heads == kv_heads, no window) runs the vision tower's tensor-core kernel. */
 GE_API int ge_test_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, int32_t ntok, const ge_seq* seqs,
                              int32_t nseq, int32_t heads, int32_t kv_heads, int32_t hd, int32_t half_window,
                              uint16_t* out);
@@ -58,6 +60,17 @@ GE_API int ge_test_attention_schedule(const ge_seq* seqs, int32_t nseq, int32_t 
                                       int32_t* ctas, int32_t* words);
 
 /* Message of the calling thread's last failed ge_test_* call. */
+/* ImagePreprocessor.prepare's sizing and resampling (Image/ImagePreprocessor.swift:87-97,
+ * Image/ImageResizer.swift) on the host, without a model: the resized RGB8 image (tw x th) for
+ * patch size `patch`, merge window `merge`, at least `min_tokens` and at most `max_tokens` tokens. */
+GE_API int ge_test_image_prepare(int32_t patch, int32_t merge, int32_t min_tokens, const uint8_t* rgb, int32_t w,
+                                 int32_t h, int32_t max_tokens, uint8_t* out, int64_t cap, int32_t* tw, int32_t* th);
+
+/* k_patchify on one image whose sides are multiples of `patch`: fp16 patch rows
+ * [(h / patch) * (w / patch)][kpad] (PreparedImage.patches, columns past 3 patch^2 zero). */
+GE_API int ge_test_patchify(const uint8_t* rgb, int32_t w, int32_t h, int32_t patch, const float* mean, const float* std,
+                            uint16_t* out, int32_t kpad);
+
 GE_API const char* ge_test_last_error(void);
 
 #ifdef __cplusplus
