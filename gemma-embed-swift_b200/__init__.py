@@ -393,6 +393,30 @@ class EmbeddingModel:
                  "flops_per_launch": out[i].flops_per_launch, "bytes_per_launch": out[i].bytes_per_launch,
                  "launches_per_forward": out[i].launches_per_forward} for i in range(cnt.value)]
 
+    def profile_images(self, images, max_image_tokens: int = 256, reps: int = 5) -> list:
+        """Profiler.profileImages (Metal/Profiler.swift:114-200): "image_forward" (vision and text
+        towers) and "vision_tower" in ms, then each vision kernel class like `profile`."""
+        c, keep = _images(list(images))
+        cap = 64
+        out = (_lib.GeKernelTime * cap)()
+        cnt = ctypes.c_int32(0)
+        _check(_lib.lib().ge_profile_images(self._h, c, len(keep), max_image_tokens, reps, out, cap, ctypes.byref(cnt)),
+               self._h)
+        return [{"name": out[i].name.decode(), "ms_per_launch": out[i].ms_per_launch,
+                 "flops_per_launch": out[i].flops_per_launch, "bytes_per_launch": out[i].bytes_per_launch,
+                 "launches_per_forward": out[i].launches_per_forward} for i in range(cnt.value)]
+
+    def image_forward_device(self, d_rgb, sizes, d_out, stream=None, device: int = 0) -> None:
+        """ge_image_forward_device: pixels already on the GPU (`d_rgb`, images back to back at their
+        tower sizes (width, height) in `sizes`) to pooled rows in `d_out`, on `stream`."""
+        c = (_lib.GeImage * max(len(sizes), 1))()
+        for i, (w, h) in enumerate(sizes):
+            c[i].width = int(w)
+            c[i].height = int(h)
+        _check(_lib.lib().ge_image_forward_device(self._h, device, ctypes.c_void_p(int(d_rgb)), c, len(sizes),
+                                                  ctypes.c_void_p(int(d_out)), ctypes.c_void_p(int(stream or 0))),
+               self._h)
+
     def pool_head_noalloc(self, d_hidden, ntok: int, d_seqs, nseq: int, d_out, stream=None, device: int = 0) -> None:
         """Mean-pool and head over caller-owned device buffers without allocating (ge_pool_head_noalloc),
         for callers that cannot allocate device memory.  Arguments are torch CUDA tensors or raw

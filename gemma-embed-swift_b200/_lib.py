@@ -95,6 +95,10 @@ SIGNATURES = {
     "ge_image_opts_default": ([P(GeImageOpts)], None),
     "ge_embed_images": ([ctypes.c_void_p, P(GeImage), ctypes.c_int32, P(GeImageOpts), f32p, i32p, PROGRESS_FN,
                          ctypes.c_void_p], ctypes.c_int),
+    "ge_image_forward_device": ([ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, P(GeImage), ctypes.c_int32,
+                                 ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "ge_profile_images": ([ctypes.c_void_p, P(GeImage), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                           P(GeKernelTime), ctypes.c_int32, i32p], ctypes.c_int),
     "ge_image_tokens": ([ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32], ctypes.c_int32),
     "ge_image_vectors": ([ctypes.c_void_p, P(GeImage), ctypes.c_int32, ctypes.c_int32, f32p, ctypes.c_int64, i32p],
                          ctypes.c_int),

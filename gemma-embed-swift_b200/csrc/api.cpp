@@ -208,8 +208,15 @@ int embed_prepared(ge_model* m, const std::vector<std::vector<int32_t>>& prepare
 // [bos, <|image>, rows..., <image|>, eos] with the rows read from the tower's output.
 // `pooled` receives n rows of the output width.
 int images_on_device(ge_model* m, ge::Device& d, const ge::PreparedImage* const* ims, int n, float* pooled,
-                     std::string* error) {
-    int rc = ge::run_vision(m, d, ims, n, error);
+                     std::string* error, cudaStream_t stream = nullptr, const uint8_t* d_rgb = nullptr,
+                     bool out_on_device = false) {
+    ge::VisionArgs va;
+    va.imgs = ims;
+    va.n = n;
+    va.d_rgb = d_rgb;
+    va.stream = stream;
+    va.error = error;
+    int rc = ge::run_vision(m, d, va);
     if (rc) return rc;
     std::vector<int32_t> toks;
     std::vector<ge_seq> seqs;
@@ -229,6 +236,8 @@ int images_on_device(ge_model* m, ge::Device& d, const ge::PreparedImage* const*
     a.seqs = seqs.data();
     a.nseq = int(seqs.size());
     a.out = pooled;
+    a.out_on_device = out_on_device;
+    a.stream = stream;
     a.error = error;
     a.vectors = d.vis.ws.vectors;
     a.vector_rows = row;
@@ -731,7 +740,10 @@ int ge_image_vectors(ge_model* m, const ge_image* images, int32_t count, int32_t
     ge::Device& d = m->devs[0];
     std::vector<const ge::PreparedImage*> ims;
     for (auto& p : prepared) ims.push_back(&p);
-    rc = ge::run_vision(m, d, ims.data(), count, nullptr);
+    ge::VisionArgs va;
+    va.imgs = ims.data();
+    va.n = count;
+    rc = ge::run_vision(m, d, va);
     if (rc) return rc;
     const size_t bytes = size_t(rows) * m->vcfg.projection_dim * sizeof(float);
     cudaError_t e = cudaMemcpyAsync(out, d.vis.ws.vectors, bytes, cudaMemcpyDeviceToHost, d.stream);
@@ -746,6 +758,128 @@ int ge_image_vectors(ge_model* m, const ge_image* images, int32_t count, int32_t
     }
     m->d2h_bytes += int64_t(bytes);
     for (int32_t i = 0; i < count && rows_per_image; i++) rows_per_image[i] = prepared[size_t(i)].tokens();
+    return GE_OK;
+}
+
+int ge_image_forward_device(ge_model* m, int32_t device_ordinal, const uint8_t* d_rgb, const ge_image* images,
+                            int32_t count, float* d_pooled, void* stream) {
+    if (!m) return GE_ERR_INVALID_OPTIONS;
+    if (!m->has_vision)
+        return ge::set_error(m, GE_ERR_IMAGE_ENCODER_NOT_LOADED,
+                             "no image encoder is loaded; pass the mmproj GGUF when loading the model");
+    std::lock_guard<std::mutex> g(m->mu);
+    ge::Device* dev = nullptr;
+    for (auto& d : m->devs)
+        if (d.ordinal == device_ordinal) dev = &d;
+    if (!dev) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: the model is not loaded on that device");
+    if (count < 0 || (count > 0 && (!d_rgb || !images || !d_pooled)))
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: bad sizes or NULL arrays");
+    if (count == 0) return GE_OK;
+    const ge::VisionConfig& c = m->vcfg;
+    std::vector<ge::PreparedImage> ims(static_cast<size_t>(count));
+    std::vector<const ge::PreparedImage*> ptrs;
+    for (int32_t i = 0; i < count; i++) {
+        const int a = c.alignment();
+        if (images[i].width <= 0 || images[i].height <= 0 || images[i].width % a || images[i].height % a)
+            return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: image " + std::to_string(i) +
+                                                                " is not at a tower size (sides multiples of " +
+                                                                std::to_string(a) + ")");
+        ge::PreparedImage& p = ims[size_t(i)];
+        p.width = images[i].width;
+        p.height = images[i].height;
+        p.gx = p.width / c.patch;
+        p.gy = p.height / c.patch;
+        p.merge = c.merge;
+        if (p.tokens() + 4 > m->cfg.max_tokens)
+            return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: image " + std::to_string(i) + " needs " +
+                                                                std::to_string(p.tokens() + 4) + " rows");
+        ptrs.push_back(&p);
+    }
+    return images_on_device(m, *dev, ptrs.data(), count, d_pooled, nullptr,
+                            stream ? static_cast<cudaStream_t>(stream) : cudaStreamLegacy, d_rgb, true);
+}
+
+int ge_profile_images(ge_model* m, const ge_image* images, int32_t count, int32_t max_image_tokens, int32_t reps,
+                      ge_kernel_time* out, int32_t cap, int32_t* n_out) {
+    if (!m) return GE_ERR_INVALID_OPTIONS;
+    if (!m->has_vision)
+        return ge::set_error(m, GE_ERR_IMAGE_ENCODER_NOT_LOADED,
+                             "no image encoder is loaded; pass the mmproj GGUF when loading the model");
+    if (count <= 0 || !images || reps < 1 || !n_out || (cap > 0 && !out))
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: images, reps or outputs");
+    if (max_image_tokens < 1 || max_image_tokens > m->vcfg.native_max_image_tokens)
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: maxImageTokens out of range");
+    std::vector<ge::PreparedImage> prepared;
+    int rc = prepare_images(m, images, count, max_image_tokens, prepared);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> g(m->mu);
+    ge::Device& d = m->devs[0];
+    std::vector<const ge::PreparedImage*> ims;
+    for (auto& p : prepared) ims.push_back(&p);
+    std::vector<float> pooled(size_t(count) * m->cfg.out_dim);
+    // One ordinary run uploads the pixels; the timed runs read them where they landed.
+    if ((rc = images_on_device(m, d, ims.data(), count, pooled.data(), nullptr))) return rc;
+    const uint8_t* d_rgb = d.vis.ws.rgb;
+    cudaEvent_t e0, e1, e2;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventCreate(&e2);
+    // The whole image forward (vision and text towers) and the vision tower alone, mean of reps.
+    float whole = 0.f, tower = 0.f;
+    for (int r = 0; r < reps && rc == GE_OK; r++) {
+        cudaEventRecord(e0, d.stream);
+        ge::VisionArgs va;
+        va.imgs = ims.data();
+        va.n = count;
+        va.d_rgb = d_rgb;
+        rc = ge::run_vision(m, d, va);
+        cudaEventRecord(e1, d.stream);
+        if (rc == GE_OK) rc = images_on_device(m, d, ims.data(), count, pooled.data(), nullptr, nullptr, d_rgb);
+        cudaEventRecord(e2, d.stream);
+        cudaEventSynchronize(e2);
+        float t1 = 0.f, t2 = 0.f, t3 = 0.f;
+        cudaEventElapsedTime(&t1, e0, e1);
+        cudaEventElapsedTime(&t2, e1, e2);
+        tower += t1;
+        whole += t2;
+        (void)t3;
+    }
+    ge::ProfileSink sink;
+    sink.reps = reps;
+    if (rc == GE_OK) {
+        ge::VisionArgs va;
+        va.imgs = ims.data();
+        va.n = count;
+        va.d_rgb = d_rgb;
+        va.profile = &sink;
+        rc = ge::run_vision(m, d, va);
+        cudaStreamSynchronize(d.stream);
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaEventDestroy(e2);
+    if (rc) return rc;
+    double patches = 0, tokens = 0;
+    for (auto* p : ims) {
+        patches += p->patches();
+        tokens += p->tokens();
+    }
+    std::vector<ge_kernel_time> all;
+    auto add = [&](const std::string& name, double ms, double flops, double bytes, int per) {
+        ge_kernel_time k;
+        memset(&k, 0, sizeof k);
+        snprintf(k.name, sizeof k.name, "%s", name.c_str());
+        k.ms_per_launch = ms;
+        k.flops_per_launch = flops;
+        k.bytes_per_launch = bytes;
+        k.launches_per_forward = per;
+        all.push_back(k);
+    };
+    add("image_forward", double(whole) / reps, 0, 0, 1);
+    add("vision_tower", double(tower) / reps, 0, 0, 1);
+    for (auto& e : sink.entries) add(e.name, e.ms, e.flops, e.bytes, e.occurrences);
+    *n_out = int32_t(all.size());
+    for (int32_t i = 0; i < std::min<int32_t>(cap, int32_t(all.size())); i++) out[i] = all[size_t(i)];
     return GE_OK;
 }
 

@@ -392,20 +392,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                     // Scores in log2 units: p = 2^(s log2e - m), one FFMA and one ex2 per key.
                     if (kb >= row_lo && kb + 32 <= row_hi) {  // every key of this half is visible
 #pragma unroll
-                        for (int i = 0; i < 32; i++) {
-                            const float t = __uint_as_float(sr[i]) * kLog2e;
-                            sr[i] = __float_as_uint(t);
-                            mh = fmaxf(mh, t);
-                        }
+                        for (int i = 0; i < 32; i++) sr[i] = __float_as_uint(__uint_as_float(sr[i]) * kLog2e);
                     } else {
 #pragma unroll
                         for (int i = 0; i < 32; i++) {
                             const int kj = kb + i;
                             const float t = (kj >= row_lo && kj < row_hi) ? __uint_as_float(sr[i]) * kLog2e : -INFINITY;
                             sr[i] = __float_as_uint(t);
-                            mh = fmaxf(mh, t);
                         }
                     }
+                    // Eight independent partial maxima instead of one 32-long dependency chain.
+                    float mp[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) mp[i] = __uint_as_float(sr[i]);
+#pragma unroll
+                    for (int i = 8; i < 32; i++) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(sr[i]));
+                    mh = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
                 }
                 // Row maximum of the block from both halves (the slot is rewritten only after the
                 // next pair_sync, by which time the partner has read it).
@@ -443,7 +445,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                 if (gb >= 2) wait_all(&pv_done[b], uint32_t(((gb - 2) >> 1) & 1));
                 if (!ok) continue;
                 uint8_t* prow = smem + kOffP + b * kPBytes + r * 128;
-                float sum = 0.f;
+                float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
                 const float mu = m_used == -INFINITY ? 0.f : m_used;
 #pragma unroll
                 for (int c = 0; c < 4; c++) {  // 4 chunks of 8 keys = 16 bytes each
@@ -452,14 +454,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                     for (int e = 0; e < 4; e++) {
                         const float p0 = ex2_approx(__uint_as_float(sr[c * 8 + 2 * e]) - mu);  // 2^-inf = 0
                         const float p1 = ex2_approx(__uint_as_float(sr[c * 8 + 2 * e + 1]) - mu);
-                        sum += p0 + p1;
+                        ps[2 * e] += p0;
+                        ps[2 * e + 1] += p1;
                         __half2 hp = __floats2half2_rn(p0, p1);
                         wv[e] = *reinterpret_cast<uint32_t*>(&hp);
                     }
                     const int chunk = half * 4 + c;
                     *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) * 16)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
                 }
-                l += sum;
+                l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
                 fence_proxy_async_smem();
                 tc_fence_before();
                 mbar_arrive(&p_full[b]);

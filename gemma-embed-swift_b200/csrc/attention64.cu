@@ -10,10 +10,10 @@
 //   warp 1      tcgen05.mma issuer: S_j = Q K_j^T (M 128, N 128, K 64) into one of two
 //               tensor-memory buffers, then O += P_{j-1} V_{j-1} (M 128, N 64, K 128) with P
 //               from shared memory.
-//   warps 2-9   softmax, two threads per query row (64 keys each): scores to log2 units,
-//               running maximum with a lazy rescale of O (only when the maximum grows by more
-//               than kRescale), P in fp16 into a 128-byte-swizzled buffer, and at the end of an
-//               item O / l stored as fp16.
+//   warps 2-9   softmax, two threads per query row (64 keys each): running maximum with a
+//               lazy rescale of O (only when the maximum grows by more than kRescaleRaw),
+//               P = 2^(s log2e - m log2e) in fp16 into a 128-byte-swizzled buffer, and at the end
+//               of an item O / l stored as fp16.
 // Tensor memory: S buffers in columns [0, 128) and [128, 256), O in [256, 320).
 // Every wait is bounded (mbar_wait); after an error the kernel drains its loads and returns.
 #include "kernels.hpp"
@@ -23,8 +23,10 @@ namespace ge {
 
 namespace {
 constexpr int kQ = 128, kKeys = 128, kHd = 64, kStages = 3;
-constexpr float kRescale = 8.0f;  // log2 units
 constexpr float kLog2e = 1.4426950408889634f;
+// O is rescaled only when a row's maximum grows by more than this (2^8 in probability); until
+// then every term of the row shares the stale maximum, so the result is exact.
+constexpr float kRescaleRaw = 8.0f / kLog2e;
 constexpr int kTileBytes = kKeys * kHd * 2;       // 16 KB: [128 rows][64 dims] = [128][128 B]
 constexpr int kOffK = kTileBytes;                 // Q at 0
 constexpr int kOffV = kOffK + kStages * kTileBytes;
@@ -229,6 +231,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention64(const __grid_consta
             for (int j = 0; j < nblk; j++, gb++) {
                 const int b = gb & 1;
                 wait_all(&s_full[b], uint32_t((gb >> 1) & 1));
+                // Raw scores; the maximum is kept in the same units and each probability is
+                // 2^(s log2e - m log2e), one FFMA and one ex2 per key.
                 uint32_t sr[64];
                 float mh = -INFINITY;
                 const int kb = j * kKeys + half * 64;
@@ -237,30 +241,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention64(const __grid_consta
                     tmem_ld32(lane_base + kTmemS + b * kKeys + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
                     tmem_ld32(lane_base + kTmemS + b * kKeys + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
                     tmem_wait_ld();
-                    if (kb + 64 <= len) {
+                    if (kb + 64 > len) {
 #pragma unroll
-                        for (int i = 0; i < 64; i++) {
-                            const float t = __uint_as_float(sr[i]) * kLog2e;
-                            sr[i] = __float_as_uint(t);
-                            mh = fmaxf(mh, t);
-                        }
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 64; i++) {
-                            const float t = kb + i < len ? __uint_as_float(sr[i]) * kLog2e : -INFINITY;
-                            sr[i] = __float_as_uint(t);
-                            mh = fmaxf(mh, t);
-                        }
+                        for (int i = 0; i < 64; i++)
+                            if (kb + i >= len) sr[i] = __float_as_uint(-INFINITY);
                     }
+                    // Eight independent partial maxima instead of one 64-long dependency chain.
+                    float mp[8];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) mp[i] = __uint_as_float(sr[i]);
+#pragma unroll
+                    for (int i = 8; i < 64; i++) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(sr[i]));
+                    mh = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
                 }
                 red[half * kQ + r] = mh;
                 pair_sync();
                 const float mb = fmaxf(mh, red[(1 - half) * kQ + r]);
                 pair_sync();
                 if (!ok) continue;
-                const bool grow = mb > m_used + kRescale && m_used != -INFINITY;
+                const bool grow = mb > m_used + kRescaleRaw && m_used != -INFINITY;
                 if (__any_sync(0xffffffffu, grow)) {
-                    const float alpha = grow ? ex2_approx(m_used - mb) : 1.0f;
+                    const float alpha = grow ? ex2_approx((m_used - mb) * kLog2e) : 1.0f;
                     if (j > 0) wait_all(&pv_done[(gb - 1) & 1], uint32_t(((gb - 1) >> 1) & 1));
                     if (!ok) continue;
                     tc_fence_after();
@@ -282,21 +283,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention64(const __grid_consta
                 if (gb >= 2) wait_all(&pv_done[b], uint32_t(((gb - 2) >> 1) & 1));
                 if (!ok) continue;
                 uint8_t* prow = smem + kOffP + b * kPBytes + half * (kPBytes / 2) + r * 128;
-                float sum = 0.f;
-                const float mu = m_used == -INFINITY ? 0.f : m_used;
+                float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
+                const float nmu = m_used == -INFINITY ? 0.f : -m_used * kLog2e;
 #pragma unroll
                 for (int c = 0; c < 8; c++) {  // 8 chunks of 8 keys = 16 bytes each
                     uint32_t wv[4];
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
-                        const float p0 = ex2_approx(__uint_as_float(sr[c * 8 + 2 * e]) - mu);
-                        const float p1 = ex2_approx(__uint_as_float(sr[c * 8 + 2 * e + 1]) - mu);
-                        sum += p0 + p1;
+                        const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c * 8 + 2 * e]), kLog2e, nmu));
+                        const float p1 = ex2_approx(fmaf(__uint_as_float(sr[c * 8 + 2 * e + 1]), kLog2e, nmu));
+                        ps[2 * e] += p0;
+                        ps[2 * e + 1] += p1;
                         wv[e] = pack_half2(p0, p1);
                     }
                     *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) * 16)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
                 }
-                l += sum;
+                l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
                 fence_proxy_async_smem();
                 tc_fence_before();
                 mbar_arrive(&p_full[b]);

@@ -186,7 +186,15 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a);
 // projected rows land in d.vis.ws.vectors (image i's rows from sum of earlier token counts).
 int load_vision(ge_model* m, const char* path);
 void free_vision(Device& d);
-int run_vision(ge_model* m, Device& d, const PreparedImage* const* imgs, int n, std::string* error);
+struct VisionArgs {
+    const PreparedImage* const* imgs = nullptr;  // grids, and the host pixels unless d_rgb is set
+    int n = 0;
+    const uint8_t* d_rgb = nullptr;  // device: every image's pixels back to back (skips the upload)
+    cudaStream_t stream = nullptr;   // nullptr: the device's own stream
+    std::string* error = nullptr;    // nullptr: the model's last_error
+    ProfileSink* profile = nullptr;  // time each kernel class instead of only running it
+};
+int run_vision(ge_model* m, Device& d, const VisionArgs& a);
 GraphEntry* find_graph(Device& d, const GraphKey& k);
 // The multi-GPU dispatcher's split of a packed batch: the sequence indices of each device,
 // longest first onto the least-loaded device (cost n + n^2 / 2048), each in original order.

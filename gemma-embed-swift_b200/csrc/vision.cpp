@@ -312,10 +312,12 @@ int load_vision(ge_model* m, const char* path) {
     return GE_OK;
 }
 
-int run_vision(ge_model* m, Device& d, const PreparedImage* const* imgs, int n, std::string* error) {
+int run_vision(ge_model* m, Device& d, const VisionArgs& a) {
     const VisionConfig& c = m->vcfg;
+    const PreparedImage* const* imgs = a.imgs;
+    const int n = a.n;
     auto report = [&](int code, const std::string& msg) {
-        if (error) *error = msg;
+        if (a.error) *a.error = msg;
         else m->last_error = msg;
         return code;
     };
@@ -336,13 +338,14 @@ int run_vision(ge_model* m, Device& d, const PreparedImage* const* imgs, int n, 
     for (int i = 0; i < n; i++) {
         const PreparedImage& im = *imgs[i];
         if (im.gx <= 0 || im.gy <= 0 || im.gx % c.merge || im.gy % c.merge || im.gx > c.positions ||
-            im.gy > c.positions || im.gx > 0xffff || im.gy > 0xffff)
+            im.gy > c.positions || im.gx > 0xffff || im.gy > 0xffff ||
+            (!a.d_rgb && im.rgb.size() != size_t(im.gx) * im.gy * c.patch * c.patch * 3))
             return report(GE_ERR_INVALID_OPTIONS, "invalid options: image " + std::to_string(i) + " has an unusable patch grid");
         patches += im.patches();
         tokens += im.tokens();
         max_patches = std::max(max_patches, im.patches());
         max_tokens = std::max(max_tokens, im.tokens());
-        rgb += im.rgb.size();
+        rgb += size_t(im.gx) * im.gy * c.patch * c.patch * 3;
     }
     const int rows = std::max(kRowTile, (patches + kRowTile - 1) / kRowTile * kRowTile);
     const int trows = std::max(kRowTile, (tokens + kRowTile - 1) / kRowTile * kRowTile);
@@ -355,28 +358,31 @@ int run_vision(ge_model* m, Device& d, const PreparedImage* const* imgs, int n, 
     int ctas = 0;
     const int words = build_attention_work(seq_pairs.data(), n, c.heads, 1, 0, d.num_sms, nullptr, &ctas);
     const int items = words ? (words - ctas - 1) / 4 : 0;
-    if ((e = ensure_vision_workspace(c, d, rows, trows, n, rgb, words)) != cudaSuccess) return gpu_fail(e, "workspace");
+    if ((e = ensure_vision_workspace(c, d, rows, trows, n, a.d_rgb ? 0 : rgb, words)) != cudaSuccess)
+        return gpu_fail(e, "workspace");
     VisionWorkspace& ws = d.vis.ws;
     // ---- host staging and uploads
     size_t off = 0;
     for (int i = 0, ps = 0, ts = 0; i < n; i++) {
         const PreparedImage& im = *imgs[i];
-        memcpy(ws.h_rgb + off, im.rgb.data(), im.rgb.size());
+        const size_t bytes = size_t(im.gx) * im.gy * c.patch * c.patch * 3;
+        if (!a.d_rgb) memcpy(ws.h_rgb + off, im.rgb.data(), bytes);
         ws.h_imgs[i] = VisionImage{uint64_t(off), im.gx, im.gy, uint32_t(ps), uint32_t(ts)};
         for (int k = 0; k < im.patches(); k++)
             ws.h_xy[ps + k] = uint32_t(k % im.gx) | (uint32_t(k / im.gx) << 16);
-        off += im.rgb.size();
+        off += bytes;
         ps += im.patches();
         ts += im.tokens();
     }
     build_attention_work(seq_pairs.data(), n, c.heads, 1, 0, d.num_sms, ws.h_work, nullptr);
-    cudaStream_t st = d.stream;
-    if ((e = cudaMemcpyAsync(ws.rgb, ws.h_rgb, rgb, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
+    cudaStream_t st = a.stream ? a.stream : d.stream;
+    const uint8_t* src = a.d_rgb ? a.d_rgb : ws.rgb;
+    if ((!a.d_rgb && (e = cudaMemcpyAsync(ws.rgb, ws.h_rgb, rgb, cudaMemcpyHostToDevice, st)) != cudaSuccess) ||
         (e = cudaMemcpyAsync(ws.imgs, ws.h_imgs, size_t(n) * sizeof(VisionImage), cudaMemcpyHostToDevice, st)) != cudaSuccess ||
         (e = cudaMemcpyAsync(ws.xy, ws.h_xy, size_t(patches) * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
         (e = cudaMemcpyAsync(ws.work, ws.h_work, size_t(words) * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess)
         return gpu_fail(e, "image upload");
-    m->h2d_bytes += int64_t(rgb + size_t(n) * sizeof(VisionImage) + size_t(patches) * 4 + size_t(words) * 4);
+    m->h2d_bytes += int64_t((a.d_rgb ? 0 : rgb) + size_t(n) * sizeof(VisionImage) + size_t(patches) * 4 + size_t(words) * 4);
     // Padding rows of the GEMM operands are zero (VisionTower.upload, VisionTower.swift:145-146).
     if (rows > patches &&
         (e = cudaMemsetAsync(ws.patches + size_t(patches) * c.kpad(), 0, size_t(rows - patches) * c.kpad() * 2, st)) != cudaSuccess)
@@ -388,6 +394,38 @@ int run_vision(ge_model* m, Device& d, const PreparedImage* const* imgs, int n, 
     const VisionDev& v = d.vis;
     const int D = c.hidden;
     int64_t launches = 0;
+    // Every launch goes through K: counted, and when profiling the first launch of each kernel
+    // class is timed over `reps` back-to-back repetitions (Profiler.profileImages,
+    // Metal/Profiler.swift:114-200).
+    auto K = [&](const char* name, double flops, double bytes, auto&& fn) -> cudaError_t {
+        if (a.profile) {
+            ProfileEntry* pe = a.profile->find(name);
+            if (pe) {
+                pe->occurrences++;
+            } else {
+                cudaEvent_t e0, e1;
+                cudaEventCreate(&e0);
+                cudaEventCreate(&e1);
+                cudaEventRecord(e0, st);
+                for (int r = 0; r < a.profile->reps; r++) {
+                    const cudaError_t x = fn();
+                    if (x != cudaSuccess) return x;
+                    launches++;
+                }
+                cudaEventRecord(e1, st);
+                const cudaError_t x = cudaEventSynchronize(e1);
+                float ms = 0.f;
+                cudaEventElapsedTime(&ms, e0, e1);
+                cudaEventDestroy(e0);
+                cudaEventDestroy(e1);
+                if (x != cudaSuccess) return x;
+                a.profile->add(name, double(ms) / a.profile->reps, flops, bytes);
+                return cudaSuccess;
+            }
+        }
+        launches++;
+        return fn();
+    };
     auto gemm = [&](const DevActivation& A, const DevWeight& W, int m_rows, void* out, int ldo, int epi) {
         GemmLaunch g;
         g.a = &A;
@@ -398,28 +436,39 @@ int run_vision(ge_model* m, Device& d, const PreparedImage* const* imgs, int n, 
         g.epilogue = epi;
         g.err = d.err;
         g.num_sms = d.num_sms;
-        launches++;
         return launch_gemm(g, st);
     };
-#define VK(expr, what)                                      \
-    do {                                                    \
-        cudaError_t e_ = (expr);                            \
-        if (e_ != cudaSuccess) return gpu_fail(e_, what);   \
-        launches++;                                         \
+    // Algorithmic work: token rows only.
+    auto gf = [&](const DevWeight& W, int nrows) { return 2.0 * nrows * W.N * double(W.K); };
+    auto gbytes = [&](const DevWeight& W, int nrows, int out_cols, double out_bytes) {
+        return double(nrows) * W.K * 2 + double(W.N) * W.K * 2 + double(nrows) * out_cols * out_bytes;
+    };
+    double att_flops = 0;
+    for (int i = 0; i < n; i++) att_flops += 4.0 * double(imgs[i]->patches()) * imgs[i]->patches() * D;
+#define VK(name, flops, bytes, expr, what)                                             \
+    do {                                                                               \
+        cudaError_t e_ = K(name, flops, bytes, [&] { return (expr); });                \
+        if (e_ != cudaSuccess) return gpu_fail(e_, what);                              \
     } while (0)
     NormParams np;
     for (int i = 0; i < 3; i++) {
         np.mean[i] = c.mean[i];
         np.std[i] = c.std[i];
     }
-    VK(launch_patchify(ws.rgb, ws.imgs, n, max_patches, c.patch, c.kpad(), np, ws.patches, st), "patchify");
-    if ((e = gemm(ws.a_patches, v.patch, rows, ws.x, D, EPI_F32)) != cudaSuccess) return gpu_fail(e, "patch embedding");
-    VK(launch_patch_position_norm(ws.x, ws.xy, patches, rows, D, v.pos, c.positions, v.layers[0].ln1, c.eps, ws.h, st),
+    const double P = patches;
+    VK("patchify", 0, double(rgb) + P * c.kpad() * 2,
+       launch_patchify(src, ws.imgs, n, max_patches, c.patch, c.kpad(), np, ws.patches, st), "patchify");
+    VK("gemm_patch", gf(v.patch, patches), gbytes(v.patch, patches, D, 4),
+       gemm(ws.a_patches, v.patch, rows, ws.x, D, EPI_F32), "patch embedding");
+    VK("position_norm", 0, P * D * 14,
+       launch_patch_position_norm(ws.x, ws.xy, patches, rows, D, v.pos, c.positions, v.layers[0].ln1, c.eps, ws.h, st),
        "position rows");
     for (int l = 0; l < c.layers; l++) {
         const VisionLayerDev& L = v.layers[size_t(l)];
-        if ((e = gemm(ws.a_h, L.qkv, rows, ws.qkv, 3 * D, EPI_F16)) != cudaSuccess) return gpu_fail(e, "qkv projection");
-        VK(launch_vision_qkv_norm_rope(ws.qkv, patches, rows, c.heads, L.q_norm, L.k_norm, ws.xy, v.rope, c.eps, ws.q,
+        VK("gemm_qkv", gf(L.qkv, patches), gbytes(L.qkv, patches, 3 * D, 2),
+           gemm(ws.a_h, L.qkv, rows, ws.qkv, 3 * D, EPI_F16), "qkv projection");
+        VK("qkv_norm_rope", 0, P * 3 * D * 4,
+           launch_vision_qkv_norm_rope(ws.qkv, patches, rows, c.heads, L.q_norm, L.k_norm, ws.xy, v.rope, c.eps, ws.q,
                                        ws.k, ws.v, st),
            "q/k/v norm and rope");
         Attn64Launch at;
@@ -433,22 +482,28 @@ int run_vision(ge_model* m, Device& d, const PreparedImage* const* imgs, int n, 
         at.sched_items = items;
         at.ctas = ctas;
         at.err = d.err;
-        VK(launch_attention64(at, st), "attention");
-        if ((e = gemm(ws.a_attn, L.o, rows, ws.o16, D, EPI_F16)) != cudaSuccess) return gpu_fail(e, "attention output");
-        VK(launch_residual_norm(ws.x, ws.o16, patches, D, L.post_attn, 1.0f, L.ln2, c.eps, ws.h, nullptr, nullptr, st),
+        VK("attention", att_flops, P * D * 2 * 4, launch_attention64(at, st), "attention");
+        VK("gemm_o", gf(L.o, patches), gbytes(L.o, patches, D, 2), gemm(ws.a_attn, L.o, rows, ws.o16, D, EPI_F16),
+           "attention output");
+        VK("residual_attn", 0, P * D * 14,
+           launch_residual_norm(ws.x, ws.o16, patches, D, L.post_attn, 1.0f, L.ln2, c.eps, ws.h, nullptr, nullptr, st),
            "attention residual");
-        if ((e = gemm(ws.a_h, L.gu, rows, ws.act, c.ff, EPI_GEGLU_QUICK)) != cudaSuccess) return gpu_fail(e, "gate/up");
-        if ((e = gemm(ws.a_act, L.down, rows, ws.o16, D, EPI_F16)) != cudaSuccess) return gpu_fail(e, "down");
+        VK("gemm_gate_up", gf(L.gu, patches), gbytes(L.gu, patches, c.ff, 2),
+           gemm(ws.a_h, L.gu, rows, ws.act, c.ff, EPI_GEGLU_QUICK), "gate/up");
+        VK("gemm_down", gf(L.down, patches), gbytes(L.down, patches, D, 2),
+           gemm(ws.a_act, L.down, rows, ws.o16, D, EPI_F16), "down");
         const float* next = l + 1 < c.layers ? v.layers[size_t(l) + 1].ln1 : nullptr;
-        VK(launch_residual_norm(ws.x, ws.o16, patches, D, L.post_ffn, 1.0f, next, c.eps, next ? ws.h : nullptr, nullptr,
+        VK("residual_ffn", 0, P * D * (next ? 14 : 12),
+           launch_residual_norm(ws.x, ws.o16, patches, D, L.post_ffn, 1.0f, next, c.eps, next ? ws.h : nullptr, nullptr,
                                 nullptr, st),
            "ffn residual");
     }
-    VK(launch_pool_patches_norm(ws.x, ws.imgs, n, max_tokens, D, c.merge, sqrtf(float(D)) / float(c.merge * c.merge), c.eps,
-                                ws.pooled, st),
+    VK("pool", 0, P * D * 4 + double(tokens) * D * 2,
+       launch_pool_patches_norm(ws.x, ws.imgs, n, max_tokens, D, c.merge, sqrtf(float(D)) / float(c.merge * c.merge),
+                                c.eps, ws.pooled, st),
        "pool");
-    if ((e = gemm(ws.a_pooled, v.proj, trows, ws.vectors, c.projection_dim, EPI_F32)) != cudaSuccess)
-        return gpu_fail(e, "projection");
+    VK("gemm_projection", gf(v.proj, tokens), gbytes(v.proj, tokens, c.projection_dim, 4),
+       gemm(ws.a_pooled, v.proj, trows, ws.vectors, c.projection_dim, EPI_F32), "projection");
 #undef VK
     m->launches += launches;
     return GE_OK;

@@ -85,8 +85,8 @@ __global__ void k_patch_position_norm(float* __restrict__ x, const uint32_t* __r
 // One warp per token over its 3 H heads of 64 (q | k | v in the fused projection row).  Lane l
 // holds dims 2l and 2l + 1 of every head: lanes 0-15 the first half (rotated by the patch
 // column), lanes 16-31 the second (by the patch row); a dim's NeoX partner 16 dims away sits
-// in lane l ^ 8.  q and k: weighted RMSNorm then the rotation; v: unweighted RMSNorm.  All
-// heads of a token are loaded before the first is normalised.
+// in lane l ^ 8.  q and k: weighted RMSNorm then the rotation; v: unweighted RMSNorm.  The
+// heads of q (then k, then v) are loaded together before the first is normalised.
 template <int H>
 __global__ void k_vision_qkv_norm_rope(const __half* __restrict__ qkv, int ntok, int rows,
                                        const float* __restrict__ qw, const float* __restrict__ kw,
@@ -112,9 +112,6 @@ __global__ void k_vision_qkv_norm_rope(const __half* __restrict__ qkv, int ntok,
         return;
     }
     const uint32_t* src = reinterpret_cast<const uint32_t*>(qkv + long(row) * 3 * D) + lane;
-    uint32_t raw[3 * H];
-#pragma unroll
-    for (int s = 0; s < 3 * H; s++) raw[s] = src[s * 32];
     const uint32_t c = xy[row];
     const int axis = lane >> 4;
     const int posi = axis ? int(c >> 16) : int(c & 0xffffu);
@@ -123,31 +120,39 @@ __global__ void k_vision_qkv_norm_rope(const __half* __restrict__ qkv, int ntok,
     const float4 cs = *reinterpret_cast<const float4*>(rope + (long(posi) * 16 + (j0 & 15)) * 2);
     const float2 wq = *reinterpret_cast<const float2*>(qw + 2 * lane);
     const float2 wk = *reinterpret_cast<const float2*>(kw + 2 * lane);
+    // q, then k, then v: the H heads of each loaded together (H independent loads in flight).
+#pragma unroll 1
+    for (int g = 0; g < 3; g++) {
+        uint32_t raw[H];
 #pragma unroll
-    for (int s = 0; s < 3 * H; s++) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&raw[s]));
-        const float ss = warp_sum(f.x * f.x + f.y * f.y);
-        const float inv = 1.0f / sqrtf(ss / 64.0f + eps);
-        uint32_t outw;
-        if (s < 2 * H) {
-            const float2 wv = s < H ? wq : wk;
-            const float u0 = f.x * inv * wv.x, u1 = f.y * inv * wv.y;
-            const float p0 = __shfl_xor_sync(0xffffffffu, u0, 8);
-            const float p1 = __shfl_xor_sync(0xffffffffu, u1, 8);
-            float r0, r1;
-            if (first) {
-                r0 = u0 * cs.x - p0 * cs.y;
-                r1 = u1 * cs.z - p1 * cs.w;
+        for (int hh = 0; hh < H; hh++) raw[hh] = src[(g * H + hh) * 32];
+#pragma unroll
+        for (int hh = 0; hh < H; hh++) {
+            const int s = g * H + hh;
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&raw[hh]));
+            const float ss = warp_sum(f.x * f.x + f.y * f.y);
+            const float inv = 1.0f / sqrtf(ss / 64.0f + eps);
+            uint32_t outw;
+            if (s < 2 * H) {
+                const float2 wv = s < H ? wq : wk;
+                const float u0 = f.x * inv * wv.x, u1 = f.y * inv * wv.y;
+                const float p0 = __shfl_xor_sync(0xffffffffu, u0, 8);
+                const float p1 = __shfl_xor_sync(0xffffffffu, u1, 8);
+                float r0, r1;
+                if (first) {
+                    r0 = u0 * cs.x - p0 * cs.y;
+                    r1 = u1 * cs.z - p1 * cs.w;
+                } else {
+                    r0 = p0 * cs.y + u0 * cs.x;
+                    r1 = p1 * cs.w + u1 * cs.z;
+                }
+                outw = pack_half2(r0, r1);
+                uint32_t* dst = s < H ? q32 : k32;
+                dst[(base + (s % H) * 64) / 2] = outw;
             } else {
-                r0 = p0 * cs.y + u0 * cs.x;
-                r1 = p1 * cs.w + u1 * cs.z;
+                outw = pack_half2(f.x * inv, f.y * inv);
+                v32[(base + (s - 2 * H) * 64) / 2] = outw;
             }
-            outw = pack_half2(r0, r1);
-            uint32_t* dst = s < H ? q32 : k32;
-            dst[(base + (s % H) * 64) / 2] = outw;
-        } else {
-            outw = pack_half2(f.x * inv, f.y * inv);
-            v32[(base + (s - 2 * H) * 64) / 2] = outw;
         }
     }
 }

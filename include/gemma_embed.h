@@ -284,6 +284,21 @@ GE_API void ge_image_opts_default(ge_image_opts* opts);
 GE_API int ge_embed_images(ge_model* model, const ge_image* images, int32_t count, const ge_image_opts* opts, float* out,
                            int32_t* token_counts, ge_progress_fn progress, void* user);
 
+/* The image forward (vision and text towers, MetalForward.run(images:)) over device-resident
+ * pixels on the caller's stream, without synchronising: `d_rgb` holds the images back to back,
+ * each already at its tower size (images[i].width x height, sides multiples of patch * merge;
+ * images[i].rgb is ignored); d_pooled receives [count][output_dimensions] pooled, unnormalised
+ * fp32 rows.  The device counterpart of ge_embed_images' forward, for callers (and the
+ * benchmark) whose pixels are already on the GPU.  NULL stream: the legacy default stream. */
+GE_API int ge_image_forward_device(ge_model* model, int32_t device_ordinal, const uint8_t* d_rgb, const ge_image* images,
+                                   int32_t count, float* d_pooled, void* stream);
+
+/* Profiler.profileImages (Metal/Profiler.swift:114-200): on the first device, the whole image
+ * forward ("image_forward") and the vision tower alone ("vision_tower"), mean over `reps`, then
+ * each vision kernel class's first launch timed over `reps` back-to-back repetitions. */
+GE_API int ge_profile_images(ge_model* model, const ge_image* images, int32_t count, int32_t max_image_tokens,
+                             int32_t reps, ge_kernel_time* out, int32_t cap, int32_t* count_out);
+
 /* PreparedImage.tokenCount (Image/ImagePreprocessor.swift:25-27) of a width x height image at
  * `max_image_tokens`: the rows ge_image_vectors returns for it; -1 without an image encoder. */
 GE_API int32_t ge_image_tokens(const ge_model* model, int32_t width, int32_t height, int32_t max_image_tokens);
