@@ -21,8 +21,8 @@ import numpy as np
 
 from . import _lib
 
-__all__ = ["EmbeddingModel", "EmbedOptions", "LoadOptions", "ImageEmbedOptions", "Embedding", "EmbeddingProgress",
-           "ModelInfo", "GemmaEmbedError", "TaskPrefix", "Tokenizer", "ALLOWED_DIMENSIONS"]
+__all__ = ["EmbeddingModel", "EmbedOptions", "LoadOptions", "ImageEmbedOptions", "MultimodalEmbedOptions", "Embedding",
+           "EmbeddingProgress", "ModelInfo", "GemmaEmbedError", "TaskPrefix", "Tokenizer", "ALLOWED_DIMENSIONS"]
 
 ALLOWED_DIMENSIONS = (768, 512, 256, 128)
 
@@ -31,7 +31,7 @@ STATUS = {
     0: "ok", 1: "fileNotReadable", 2: "invalidGGUF", 3: "unsupportedTensorType", 4: "unsupportedArchitecture",
     5: "missingTensor", 6: "missingMetadata", 7: "tensorShapeMismatch", 8: "noDevice", 9: "invalidOptions",
     10: "gpuFailure", 11: "outOfMemory", 12: "timeout", 13: "cancelled", 14: "imageDecoding",
-    15: "imageEncoderNotLoaded",
+    15: "imageEncoderNotLoaded", 16: "audioDecoding", 17: "audioEncoderNotLoaded",
 }
 LOAD_NO_GRAPHS = 1
 LOAD_Q8_ONLY = 2
@@ -190,6 +190,17 @@ class LoadOptions:
     fused_residual: bool = False  # run each residual step inside the projection before it
     image_encoder: Optional[str] = None  # LoadOptions.imageEncoder: the mmproj GGUF
     image_patch_budget: int = 4096       # ImageEmbedOptions.patchBudget: patches per image batch
+
+
+@dataclass
+class MultimodalEmbedOptions:
+    """MultimodalEmbedOptions (EmbedOptions.swift:117-147)."""
+    task: str = "title: none | text: "
+    max_tokens: int = 2048
+    dimensions: int = 768
+    normalise: bool = True
+    max_image_tokens: int = 256
+    batch_size: Optional[int] = None
 
 
 @dataclass
@@ -512,6 +523,48 @@ class EmbeddingModel:
         del keep
         res = [Embedding(out[i].copy(), int(counts[i]), False) for i in range(n)]
         return res[0] if single else res
+
+    def embed_multimodal(self, inputs, options: Optional[MultimodalEmbedOptions] = None,
+                         progress: Optional[Callable[[EmbeddingProgress], Optional[bool]]] = None) -> list:
+        """embed(_ inputs: [MultimodalInput], options:progress:) (MultimodalEmbedding.swift:100-206).
+        Each input is a list of parts in reading order: str (text) or a height x width x 3 uint8
+        array (an image)."""
+        options = options or MultimodalEmbedOptions()
+        if options.batch_size is not None and options.batch_size < 1:
+            raise GemmaEmbedError(9, "invalid options: batchSize must be at least 1")
+        keep, arrays = [], []
+        c_inputs = (_lib.GeMultimodalInput * max(len(inputs), 1))()
+        for i, parts in enumerate(inputs):
+            cp = (_lib.GePart * max(len(parts), 1))()
+            for k, part in enumerate(parts):
+                if isinstance(part, (str, bytes)):
+                    data = part.encode() if isinstance(part, str) else bytes(part)
+                    keep.append(data)
+                    cp[k].kind, cp[k].text, cp[k].text_len = 0, data, len(data)
+                else:
+                    c, arrs = _images([part])
+                    arrays.append(arrs)
+                    cp[k].kind = 1
+                    cp[k].image = c[0]
+            keep.append(cp)
+            c_inputs[i].parts = cp
+            c_inputs[i].count = len(parts)
+        n = len(inputs)
+        o = _lib.GeMultimodalOpts(options.max_tokens, options.dimensions, int(options.normalise),
+                                  options.max_image_tokens, options.batch_size or 0)
+        out = np.zeros((max(n, 1), options.dimensions if options.dimensions > 0 else 1), dtype=np.float32)
+        counts = np.zeros(max(n, 1), dtype=np.int32)
+        trunc = np.zeros(max(n, 1), dtype=np.int32)
+        cb = _lib.PROGRESS_FN(0)
+        if progress is not None:
+            def _cb(done, total, tokens, user):
+                return 1 if progress(EmbeddingProgress(done, total, tokens)) else 0
+            cb = _lib.PROGRESS_FN(_cb)
+        _check(_lib.lib().ge_embed_multimodal(self._h, c_inputs, n, options.task.encode(), ctypes.byref(o),
+                                              _ptr(out, ctypes.c_float), _ptr(counts, ctypes.c_int32),
+                                              _ptr(trunc, ctypes.c_int32), cb, None), self._h)
+        del keep, arrays
+        return [Embedding(out[i].copy(), int(counts[i]), bool(trunc[i])) for i in range(n)]
 
     def image_vectors(self, images, max_image_tokens: int = 256) -> list:
         """MetalForward.imageVectors (Metal/MetalForward.swift:227-238): each image's projected rows."""

@@ -28,6 +28,18 @@ class GeImage(ctypes.Structure):
     _fields_ = [("rgb", ctypes.POINTER(ctypes.c_uint8)), ("width", ctypes.c_int32), ("height", ctypes.c_int32)]
 
 
+class GePart(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("text", ctypes.c_char_p), ("text_len", ctypes.c_int64), ("image", GeImage)]
+
+
+class GeMultimodalInput(ctypes.Structure):
+    _fields_ = [("parts", ctypes.POINTER(GePart)), ("count", ctypes.c_int32)]
+
+
+class GeMultimodalOpts(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("max_tokens", "dimensions", "normalise", "max_image_tokens", "batch_size")]
+
+
 class GeImageOpts(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in ("dimensions", "normalise", "max_image_tokens", "batch_size")]
 
@@ -93,6 +105,9 @@ SIGNATURES = {
     "ge_token_is_control": ([ctypes.c_void_p, ctypes.c_int32], ctypes.c_int),
     "ge_task_prefix": ([ctypes.c_int32, ctypes.c_char_p, P(ctypes.c_char), ctypes.c_int64, i64p], ctypes.c_int),
     "ge_image_opts_default": ([P(GeImageOpts)], None),
+    "ge_multimodal_opts_default": ([P(GeMultimodalOpts)], None),
+    "ge_embed_multimodal": ([ctypes.c_void_p, P(GeMultimodalInput), ctypes.c_int32, ctypes.c_char_p, P(GeMultimodalOpts),
+                             f32p, i32p, i32p, PROGRESS_FN, ctypes.c_void_p], ctypes.c_int),
     "ge_embed_images": ([ctypes.c_void_p, P(GeImage), ctypes.c_int32, P(GeImageOpts), f32p, i32p, PROGRESS_FN,
                          ctypes.c_void_p], ctypes.c_int),
     "ge_image_forward_device": ([ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, P(GeImage), ctypes.c_int32,
@@ -122,6 +137,8 @@ TEST_SIGNATURES = {
                                P(ctypes.c_uint8), ctypes.c_int64, i32p, i32p], ctypes.c_int),
     "ge_test_patchify": ([P(ctypes.c_uint8), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, f32p, f32p, u16p,
                           ctypes.c_int32], ctypes.c_int),
+    "ge_test_multimodal_sequence": ([ctypes.c_char_p, i32p, P(ctypes.c_char_p), ctypes.c_int32, i32p] +
+                                    [ctypes.c_int32] * 7 + [i32p, ctypes.c_int32, i32p, i32p], ctypes.c_int),
     "ge_test_last_error": ([], ctypes.c_char_p),
 }
 

@@ -13,6 +13,7 @@
 
 #include "gemma_embed.h"
 #include "model.hpp"
+#include "multimodal.hpp"
 
 namespace ge {
 int load_model(ge_model* m, const char* path, const ge_load_opts* opts);
@@ -880,6 +881,169 @@ int ge_profile_images(ge_model* m, const ge_image* images, int32_t count, int32_
     for (auto& e : sink.entries) add(e.name, e.ms, e.flops, e.bytes, e.occurrences);
     *n_out = int32_t(all.size());
     for (int32_t i = 0; i < std::min<int32_t>(cap, int32_t(all.size())); i++) out[i] = all[size_t(i)];
+    return GE_OK;
+}
+
+void ge_multimodal_opts_default(ge_multimodal_opts* o) {
+    if (!o) return;
+    o->max_tokens = 2048;
+    o->dimensions = 768;
+    o->normalise = 1;
+    o->max_image_tokens = 256;
+    o->batch_size = 0;
+}
+
+int ge_embed_multimodal(ge_model* m, const ge_multimodal_input* inputs, int32_t count, const char* prefix,
+                        const ge_multimodal_opts* opts, float* out, int32_t* token_counts, int32_t* truncated,
+                        ge_progress_fn progress, void* user) {
+    if (!m) return GE_ERR_INVALID_OPTIONS;
+    ge_multimodal_opts o;
+    ge_multimodal_opts_default(&o);
+    if (opts) o = *opts;
+    const ge::Config& c = m->cfg;
+    // The option checks of embed(_ inputs:) (MultimodalEmbedding.swift:107-131).
+    if (!(o.dimensions == 768 || o.dimensions == 512 || o.dimensions == 256 || o.dimensions == 128) ||
+        o.dimensions > c.out_dim)
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: dimensions must be one of [768, 512, 256, 128]");
+    if (o.max_tokens < 2 || o.max_tokens > c.max_tokens)
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS,
+                             "invalid options: maxTokens must be between 2 and " + std::to_string(c.max_tokens));
+    if (o.batch_size < 0) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: batchSize must be at least 1");
+    if (count < 0) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: negative input count");
+    if (count > 0 && (!inputs || !out)) return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: NULL array");
+    bool any_image = false, any_audio = false;
+    for (int32_t i = 0; i < count; i++) {
+        if (inputs[i].count < 0 || (inputs[i].count > 0 && !inputs[i].parts))
+            return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: input " + std::to_string(i) + " has no parts array");
+        for (int32_t k = 0; k < inputs[i].count; k++) {
+            const ge_part& p = inputs[i].parts[k];
+            if (p.kind == GE_PART_IMAGE) any_image = true;
+            else if (p.kind == GE_PART_AUDIO) any_audio = true;
+            else if (p.kind != GE_PART_TEXT || p.text_len < 0 || (p.text_len > 0 && !p.text))
+                return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: input " + std::to_string(i) + ", part " +
+                                                                    std::to_string(k) + " is malformed");
+        }
+    }
+    if (m->has_vision) {
+        if (o.max_image_tokens < 1 || o.max_image_tokens > m->vcfg.native_max_image_tokens)
+            return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: maxImageTokens must be between 1 and " +
+                                                                std::to_string(m->vcfg.native_max_image_tokens));
+    } else if (any_image) {
+        return ge::set_error(m, GE_ERR_IMAGE_ENCODER_NOT_LOADED,
+                             "no image encoder is loaded; pass the mmproj GGUF when loading the model");
+    }
+    if (any_audio)
+        return ge::set_error(m, GE_ERR_AUDIO_ENCODER_NOT_LOADED,
+                             "no audio encoder is loaded; pass the mmproj GGUF as LoadOptions.audioEncoder when loading the model");
+    if (count == 0) return GE_OK;
+    if (!m->tokenizer)
+        return ge::set_error(m, GE_ERR_UNSUPPORTED_ARCHITECTURE, "unsupported architecture: tokenizer model missing");
+    // Images of every input, in order, prepared on host threads.
+    std::vector<ge_image> imgs;
+    std::vector<int32_t> first_image(static_cast<size_t>(count) + 1, 0);
+    for (int32_t i = 0; i < count; i++) {
+        first_image[size_t(i)] = int32_t(imgs.size());
+        for (int32_t k = 0; k < inputs[i].count; k++)
+            if (inputs[i].parts[k].kind == GE_PART_IMAGE) imgs.push_back(inputs[i].parts[k].image);
+    }
+    first_image[size_t(count)] = int32_t(imgs.size());
+    std::vector<ge::PreparedImage> prepared;
+    if (!imgs.empty()) {
+        int rc = prepare_images(m, imgs.data(), int32_t(imgs.size()), o.max_image_tokens, prepared);
+        if (rc) return rc;
+    }
+    // One sequence per input (MultimodalSequence, MultimodalEmbedding.swift:43-83).
+    const ge::Tokenizer& tk = m->tokenizer->t;
+    auto encode = [&](const std::string& t, std::vector<int32_t>& ids) {
+        ids.clear();
+        tk.encode(reinterpret_cast<const uint8_t*>(t.data()), t.size(), false, false, ids);
+    };
+    const std::string pre = prefix ? std::string(prefix) : std::string();
+    std::vector<std::vector<int32_t>> seqs(static_cast<size_t>(count));
+    std::vector<int64_t> costs(2 * static_cast<size_t>(count));
+    for (int32_t i = 0; i < count; i++) {
+        std::vector<ge::SeqPart> parts;
+        std::vector<ge::EncoderSpan> spans;
+        int32_t img = first_image[size_t(i)];
+        int64_t patches = 0;
+        for (int32_t k = 0; k < inputs[i].count; k++) {
+            const ge_part& p = inputs[i].parts[k];
+            ge::SeqPart sp;
+            sp.kind = p.kind;
+            if (p.kind == GE_PART_TEXT) {
+                sp.text.assign(p.text ? p.text : "", size_t(p.text_len));
+            } else {
+                const ge::PreparedImage& im = prepared[size_t(img++)];
+                spans.push_back({im.tokens(), m->image_begin, m->image_end});
+                patches += im.patches();
+            }
+            parts.push_back(std::move(sp));
+        }
+        bool cut = false;
+        if (!ge::multimodal_sequence(pre, parts, spans, o.max_tokens, c.bos_id, c.eos_id, encode, seqs[size_t(i)], cut))
+            return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: input " + std::to_string(i) +
+                                                                ": its images and clips alone need more than maxTokens (" +
+                                                                std::to_string(o.max_tokens) + ") rows");
+        if (token_counts) token_counts[i] = int32_t(seqs[size_t(i)].size());
+        if (truncated) truncated[i] = cut ? 1 : 0;
+        costs[2 * size_t(i)] = int64_t(seqs[size_t(i)].size());
+        costs[2 * size_t(i) + 1] = patches;
+    }
+    const int64_t budgets[2] = {m->budget, m->patch_budget};
+    std::vector<int32_t> ranges(2 * static_cast<size_t>(count));
+    int32_t nr = 0;
+    ge_batches(costs.data(), count, 2, o.batch_size, budgets, ranges.data(), &nr);
+    std::lock_guard<std::mutex> g(m->mu);
+    ge::Device& d = m->devs[0];
+    const int od = c.out_dim;
+    int32_t done = 0;
+    int64_t done_tokens = 0;
+    for (int32_t r = 0; r < nr; r++) {
+        const int32_t b = ranges[2 * size_t(r)], e = ranges[2 * size_t(r) + 1];
+        // Image rows fill the vectors buffer from row 0, input after input (MultimodalEmbedding.swift:173-192).
+        std::vector<const ge::PreparedImage*> ims;
+        for (int32_t i = first_image[size_t(b)]; i < first_image[size_t(e)]; i++) ims.push_back(&prepared[size_t(i)]);
+        if (!ims.empty()) {
+            ge::VisionArgs va;
+            va.imgs = ims.data();
+            va.n = int(ims.size());
+            const int rc = ge::run_vision(m, d, va);
+            if (rc) return rc;
+        }
+        std::vector<int32_t> toks;
+        std::vector<ge_seq> sq;
+        int32_t row_base = 0;
+        for (int32_t i = b; i < e; i++) {
+            sq.push_back({uint32_t(toks.size()), uint32_t(seqs[size_t(i)].size())});
+            int32_t rows = 0;
+            for (int32_t id : seqs[size_t(i)]) {
+                if (id < 0) {
+                    toks.push_back(id - row_base);  // -(local + 1) -> -(row_base + local + 1)
+                    rows++;
+                } else {
+                    toks.push_back(id);
+                }
+            }
+            row_base += rows;
+        }
+        std::vector<float> pooled(size_t(e - b) * od);
+        ge::ForwardArgs a;
+        a.tokens = toks.data();
+        a.ntok = int(toks.size());
+        a.seqs = sq.data();
+        a.nseq = int(sq.size());
+        a.out = pooled.data();
+        a.vectors = ims.empty() ? nullptr : d.vis.ws.vectors;
+        a.vector_rows = row_base;
+        const int rc = ge::run_forward(m, d, a);
+        if (rc) return rc;
+        for (int32_t i = b; i < e; i++)
+            ge_finish(pooled.data() + size_t(i - b) * od, od, o.dimensions, o.normalise, out + size_t(i) * o.dimensions);
+        done += e - b;
+        done_tokens += int64_t(toks.size());
+        if (progress && progress(done, count, done_tokens, user) != 0 && r + 1 < nr)
+            return ge::set_error(m, GE_ERR_CANCELLED, "embedding was cancelled");
+    }
     return GE_OK;
 }
 

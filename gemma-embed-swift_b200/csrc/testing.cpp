@@ -8,6 +8,7 @@
 #include "kernels.hpp"
 #include "model.hpp"
 #include "vision.hpp"
+#include "multimodal.hpp"
 
 namespace {
 
@@ -379,6 +380,51 @@ int ge_test_patchify(const uint8_t* rgb, int32_t w, int32_t h, int32_t patch, co
                             patch, kpad, np, static_cast<__half*>(dout.p), nullptr));
     TRY(cudaDeviceSynchronize());
     TRY(cudaMemcpy(out, dout.p, n * 2, cudaMemcpyDeviceToHost));
+    return GE_OK;
+}
+
+int ge_test_multimodal_sequence(const char* prefix, const int32_t* kinds, const char* const* texts, int32_t nparts,
+                                const int32_t* span_rows, int32_t max_tokens, int32_t bos, int32_t eos,
+                                int32_t image_begin, int32_t image_end, int32_t audio_begin, int32_t audio_end,
+                                int32_t* ids, int32_t cap, int32_t* count, int32_t* truncated) {
+    if (nparts < 0 || (nparts > 0 && !kinds) || !count || !truncated || cap < 0 || (cap > 0 && !ids))
+        return fail(GE_ERR_INVALID_OPTIONS, "invalid options");
+    std::vector<ge::SeqPart> parts;
+    std::vector<ge::EncoderSpan> spans;
+    for (int32_t i = 0; i < nparts; i++) {
+        ge::SeqPart p;
+        p.kind = kinds[i];
+        if (p.kind == ge::kPartText) {
+            p.text = texts && texts[i] ? texts[i] : "";
+        } else {
+            ge::EncoderSpan sp;
+            sp.rows = span_rows ? span_rows[spans.size()] : 0;
+            sp.begin = p.kind == ge::kPartImage ? image_begin : audio_begin;
+            sp.end = p.kind == ge::kPartImage ? image_end : audio_end;
+            spans.push_back(sp);
+        }
+        parts.push_back(p);
+    }
+    // One id per Unicode scalar of the UTF-8 text.
+    auto scalars = [](const std::string& t, std::vector<int32_t>& out) {
+        out.clear();
+        for (size_t i = 0; i < t.size();) {
+            const uint8_t b = uint8_t(t[i]);
+            int n = b < 0x80 ? 1 : (b & 0xE0) == 0xC0 ? 2 : (b & 0xF0) == 0xE0 ? 3 : 4;
+            int32_t cp = n == 1 ? b : n == 2 ? (b & 0x1F) : n == 3 ? (b & 0x0F) : (b & 0x07);
+            for (int k = 1; k < n && i + size_t(k) < t.size(); k++) cp = (cp << 6) | (uint8_t(t[i + size_t(k)]) & 0x3F);
+            out.push_back(cp);
+            i += size_t(n);
+        }
+    };
+    std::vector<int32_t> v;
+    bool cut = false;
+    if (!ge::multimodal_sequence(prefix ? prefix : "", parts, spans, max_tokens, bos, eos, scalars, v, cut))
+        return fail(GE_ERR_INVALID_OPTIONS, "the spans alone do not fit");
+    *count = int32_t(v.size());
+    *truncated = cut ? 1 : 0;
+    if (int32_t(v.size()) > cap) return fail(GE_ERR_INVALID_OPTIONS, "output capacity too small");
+    std::copy(v.begin(), v.end(), ids);
     return GE_OK;
 }
 

@@ -40,7 +40,9 @@ typedef enum ge_status {
     GE_ERR_TIMEOUT = 12,               /* a bounded device-side wait gave up (a .gpuFailure in the reference) */
     GE_ERR_CANCELLED = 13,             /* .cancelled */
     GE_ERR_IMAGE_DECODING = 14,        /* .imageDecoding: an image's pixels or size are unusable */
-    GE_ERR_IMAGE_ENCODER_NOT_LOADED = 15 /* .imageEncoderNotLoaded */
+    GE_ERR_IMAGE_ENCODER_NOT_LOADED = 15, /* .imageEncoderNotLoaded */
+    GE_ERR_AUDIO_DECODING = 16,        /* .audioDecoding */
+    GE_ERR_AUDIO_ENCODER_NOT_LOADED = 17 /* .audioEncoderNotLoaded */
 } ge_status;
 
 typedef struct ge_model ge_model;
@@ -308,6 +310,47 @@ GE_API int32_t ge_image_tokens(const ge_model* model, int32_t width, int32_t hei
  * rows); rows_per_image (count entries) receives each image's token count. */
 GE_API int ge_image_vectors(ge_model* model, const ge_image* images, int32_t count, int32_t max_image_tokens,
                             float* out, int64_t cap_rows, int32_t* rows_per_image);
+
+/* ---- Mixed inputs (MultimodalEmbedding.swift) ---------------------------------------------- */
+
+/* MultimodalInput.Part (MultimodalEmbedding.swift:7-12). */
+typedef enum ge_part_kind { GE_PART_TEXT = 0, GE_PART_IMAGE = 1, GE_PART_AUDIO = 2 } ge_part_kind;
+
+typedef struct ge_part {
+    int32_t kind;      /* ge_part_kind */
+    const char* text;  /* GE_PART_TEXT: text_len bytes of UTF-8 */
+    int64_t text_len;
+    ge_image image;    /* GE_PART_IMAGE: decoded pixels */
+} ge_part;
+
+/* MultimodalInput (MultimodalEmbedding.swift:5-24): text, images and clips in reading order. */
+typedef struct ge_multimodal_input {
+    const ge_part* parts;
+    int32_t count;
+} ge_multimodal_input;
+
+/* MultimodalEmbedOptions (EmbedOptions.swift:117-147) minus the task prefix (a string argument). */
+typedef struct ge_multimodal_opts {
+    int32_t max_tokens;       /* default 2048 */
+    int32_t dimensions;
+    int32_t normalise;
+    int32_t max_image_tokens; /* default 256 */
+    int32_t batch_size;       /* inputs per batch; 0 packs by the token and patch budgets */
+} ge_multimodal_opts;
+
+GE_API void ge_multimodal_opts_default(ge_multimodal_opts* opts);
+
+/* EmbeddingModel.embed(_ inputs: [MultimodalInput], options:progress:)
+ * (MultimodalEmbedding.swift:100-206): each input becomes one text-tower sequence,
+ * [bos] tok(prefix + text) [<|image>] rows... [<image|>] tok(text) ... [eos] with its images'
+ * rows from the vision tower, text cut from the end when it does not fit max_tokens; then
+ * finish.  `prefix` (NUL-terminated, NULL for none) is the task prefix.  `token_counts` and
+ * `truncated` (may be NULL) receive each input's rows and whether text was cut.  An input whose
+ * images alone exceed max_tokens is refused (GE_ERR_INVALID_OPTIONS); audio parts need an audio
+ * encoder (GE_ERR_AUDIO_ENCODER_NOT_LOADED).  Runs on the first device. */
+GE_API int ge_embed_multimodal(ge_model* model, const ge_multimodal_input* inputs, int32_t count, const char* prefix,
+                               const ge_multimodal_opts* opts, float* out, int32_t* token_counts, int32_t* truncated,
+                               ge_progress_fn progress, void* user);
 
 /* No counterpart in the reference.  The last stage of the forward -- mean-pool over each
  * sequence, then the dense head (or the output projection) -- for callers that cannot allocate

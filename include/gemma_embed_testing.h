@@ -71,6 +71,18 @@ GE_API int ge_test_image_prepare(int32_t patch, int32_t merge, int32_t min_token
 GE_API int ge_test_patchify(const uint8_t* rgb, int32_t w, int32_t h, int32_t patch, const float* mean, const float* std,
                             uint16_t* out, int32_t kpad);
 
+/* MultimodalSequence.init (MultimodalEmbedding.swift:43-83) with one id per Unicode scalar
+ * standing in for the tokenizer, as the reference's MultimodalSequenceTests do: parts given by
+ * kind (0 text, 1 image, 2 audio) and, for text, NUL-terminated UTF-8; `span_rows` holds the
+ * rows of each image or clip in order; images are framed by (image_begin, image_end), clips by
+ * (audio_begin, audio_end).  Writes the ids (capacity `cap`), their count and whether text was
+ * cut; returns GE_ERR_INVALID_OPTIONS when the spans alone do not fit (the reference's nil). */
+GE_API int ge_test_multimodal_sequence(const char* prefix, const int32_t* kinds, const char* const* texts,
+                                       int32_t nparts, const int32_t* span_rows, int32_t max_tokens, int32_t bos,
+                                       int32_t eos, int32_t image_begin, int32_t image_end, int32_t audio_begin,
+                                       int32_t audio_end, int32_t* ids, int32_t cap, int32_t* count,
+                                       int32_t* truncated);
+
 GE_API const char* ge_test_last_error(void);
 
 #ifdef __cplusplus

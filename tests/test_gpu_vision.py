@@ -209,3 +209,45 @@ def test_image_options_and_errors(ge, synth, vision_model):
         assert e.value.case == "imageEncoderNotLoaded"
     finally:
         text_only.close()
+
+
+def test_multimodal_inputs_match_oracle(ge, vision_model):
+    """embed(_ inputs: [MultimodalInput]) (MultimodalEmbedding.swift:100-206) against the oracle:
+    its tokenizer, vision tower and layout (oracle/multimodal.py), then the text tower over the
+    sequence with the input's image rows."""
+    from oracle import multimodal as om
+    model, vis, ref, tok = vision_model
+    begin = tok.encode("<|image>", False, True)[0]
+    end = tok.encode("<image|>", False, True)[0]
+    ims = images()
+    inputs = [["a photo of gawy stait", ims[1], "and more words"], [ims[2]], ["only text here"],
+              [ims[0], ims[3], "two pictures"]]
+    prefix = ge.TaskPrefix.document()
+    opts = ge.MultimodalEmbedOptions(task=prefix, normalise=False, max_image_tokens=100)
+    got = model.embed_multimodal(inputs, opts)
+    for parts, e in zip(inputs, got):
+        rows, oparts, spans = [], [], []
+        for p in parts:
+            if isinstance(p, str):
+                oparts.append(("text", p))
+            else:
+                patches, gx, gy = vis.prepare(p, max_image_tokens=100)
+                r = vis.forward(patches, gx, gy)
+                rows.append(r)
+                oparts.append(("image", None))
+                spans.append((r.shape[0], begin, end))
+        ids, cut = om.sequence(prefix, oparts, spans, 2048, 2, 1, lambda t: tok.encode(t, False))
+        assert e.token_count == len(ids) and not e.truncated
+        vec = np.concatenate(rows) if rows else np.zeros((1, 768), np.float32)
+        want = ref.forward_rows(np.array(ids, np.int32), vec)
+        assert cosine(e.vector, want) > COSINE_MIN
+    # A text-only input is the text embedding, bit for bit.
+    text = model.embed("only text here", ge.EmbedOptions(task=prefix, normalise=False))
+    assert text.vector.tobytes() == got[2].vector.tobytes()
+    # Text is cut from the end when the images leave too little room; frames stay whole.
+    small = model.embed_multimodal([["some leading text " * 20, ims[2]]],
+                                   ge.MultimodalEmbedOptions(max_tokens=120, max_image_tokens=100))[0]
+    assert small.truncated and small.token_count == 120
+    with pytest.raises(ge.GemmaEmbedError) as exc:
+        model.embed_multimodal([[ims[2]]], ge.MultimodalEmbedOptions(max_tokens=50, max_image_tokens=100))
+    assert exc.value.case == "invalidOptions"
