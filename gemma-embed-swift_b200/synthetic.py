@@ -666,6 +666,118 @@ def synthetic_images(count: int, seed: int, width: int = 768, height: int = 768)
     return out
 
 
+# --------------------------------------------------------------------------- audio encoder (mmproj)
+# A gemma4a audio encoder file laid out like the audio part of the real mmproj (tensor names,
+# shapes, storage types, clamp scalars and metadata keys of Tests/GemmaEmbedTests/Fixtures/
+# mmproj.json), with the shapes of BASELINE config 5: 12 Conformer layers, hidden 1024, 8 heads
+# of 128, FFN 4096, 128 mel bins, `a.pre_encode.out` 1024 -> 1536, projected to the text width.
+AUDIO = dict(hidden=1024, layers=12, heads=8, ff=4096, mel=128, out_width=1536)
+# The linears that carry `.input_min/.input_max/.output_min/.output_max` in the real file.
+AUDIO_CLAMPED = ("ffn_up", "ffn_down", "attn_q", "attn_k", "attn_v", "attn_out", "conv_pw1", "conv_pw2",
+                 "ffn_up_1", "ffn_down_1")
+AUDIO_BOUNDS = dict(input_min=-2.5, input_max=2.5, output_min=-4.0, output_max=4.0)
+
+
+def _scalar(name: str, value: float) -> "Tensor":
+    return Tensor(name, [1], GGML_F32, np.array([value], np.float32).tobytes())
+
+
+def _uniform_f32(name: str, shape: list, seed: int, scale: float) -> "Tensor":
+    n = int(np.prod(shape))
+    w = floats(_tensor_seed(seed, name), n, scale)
+    return Tensor(name, shape, GGML_F32, w.astype(np.float32).tobytes())
+
+
+def audio_tensors(seed: int, projection_dim: int, hidden: int = 1024, layers: int = 12, heads: int = 8,
+                  ff: int = 4096, mel: int = 128, out_width: int = 1536) -> list:
+    d, hd = hidden, hidden // heads
+    t = []
+    t.append(_uniform_f32("a.conv1d.0.weight", [3, 3, 1, 128], seed, (3.0 / 9) ** 0.5))
+    t.append(_f32_tensor("a.conv1d.0.norm.weight", 128, seed, 1.0, 0.1))
+    t.append(_uniform_f32("a.conv1d.1.weight", [3, 3, 128, 32], seed, (3.0 / 1152) ** 0.5))
+    t.append(_f32_tensor("a.conv1d.1.norm.weight", 32, seed, 1.0, 0.1))
+    sub = (mel // 4) * 32
+    t.append(_uniform_f32("a.input_projection.weight", [sub, d], seed, (3.0 / sub) ** 0.5))
+    for i in range(layers):
+        p = f"a.blk.{i}."
+
+        def lin(suffix, n_in, n_out):
+            t.append(_q8_tensor(p + suffix + ".weight", n_in, n_out, seed, (3.0 / n_in) ** 0.5))
+            if suffix in AUDIO_CLAMPED:
+                for k, v in AUDIO_BOUNDS.items():
+                    t.append(_scalar(p + suffix + "." + k, v))
+        t.append(_f32_tensor(p + "ffn_norm.weight", d, seed, 1.0, 0.1))
+        lin("ffn_up", d, ff)
+        lin("ffn_down", ff, d)
+        t.append(_f32_tensor(p + "ffn_post_norm.weight", d, seed, 1.0, 0.1))
+        t.append(_f32_tensor(p + "attn_pre_norm.weight", d, seed, 1.0, 0.1))
+        for s in ("attn_q", "attn_k", "attn_v", "attn_out", "attn_k_rel"):
+            lin(s, d, d)
+        t.append(_f32_tensor(p + "per_dim_scale.weight", hd, seed, 1.0, 0.2))
+        t.append(_f32_tensor(p + "attn_post_norm.weight", d, seed, 1.0, 0.1))
+        t.append(_f32_tensor(p + "conv_norm.weight", d, seed, 1.0, 0.1))
+        lin("conv_pw1", d, 2 * d)
+        t.append(_uniform_f32(p + "conv_dw.weight", [5, d], seed, 0.5))
+        t.append(_f32_tensor(p + "norm_conv.weight", d, seed, 1.0, 0.1))
+        lin("conv_pw2", d, d)
+        t.append(_f32_tensor(p + "ffn_norm_1.weight", d, seed, 1.0, 0.1))
+        lin("ffn_up_1", d, ff)
+        lin("ffn_down_1", ff, d)
+        t.append(_f32_tensor(p + "ffn_post_norm_1.weight", d, seed, 1.0, 0.1))
+        t.append(_f32_tensor(p + "ln2.weight", d, seed, 1.0, 0.1))
+    t.append(_q8_tensor("a.pre_encode.out.weight", d, out_width, seed, (3.0 / d) ** 0.5))
+    t.append(_uniform_f32("a.pre_encode.out.bias", [out_width], seed, 0.1))
+    t.append(_q8_tensor("mm.a.input_projection.weight", out_width, projection_dim, seed, (3.0 / out_width) ** 0.5))
+    return t
+
+
+def audio_metadata(projection_dim: int, hidden: int = 1024, layers: int = 12, heads: int = 8, ff: int = 4096,
+                   mel: int = 128, out_width: int = 1536) -> list:
+    del out_width  # carried by a.pre_encode.out's shape
+    u32 = lambda v: struct.pack("<I", v)
+    return [
+        _kv("general.architecture", 8, _str("clip")),
+        _kv("general.type", 8, _str("mmproj")),
+        _kv("general.name", 8, _str("synthetic-gemma4a")),
+        _kv("general.alignment", 4, u32(32)),
+        _kv("clip.has_vision_encoder", 7, b"\x00"),
+        _kv("clip.has_audio_encoder", 7, b"\x01"),
+        _kv("clip.audio.projection_dim", 4, u32(projection_dim)),
+        _kv("clip.audio.embedding_length", 4, u32(hidden)),
+        _kv("clip.audio.feed_forward_length", 4, u32(ff)),
+        _kv("clip.audio.block_count", 4, u32(layers)),
+        _kv("clip.audio.attention.head_count", 4, u32(heads)),
+        _kv("clip.audio.projector_type", 8, _str("gemma4a")),
+        _kv("clip.audio.num_mel_bins", 4, u32(mel)),
+        _kv("clip.audio.attention.layer_norm_epsilon", 6, struct.pack("<f", 1e-6)),
+    ]
+
+
+def audio_path(seed: int = 0, projection_dim: int = 768, layers: int = AUDIO["layers"], hidden: int = AUDIO["hidden"],
+               heads: int = AUDIO["heads"], ff: int = AUDIO["ff"]) -> str:
+    """Path of the synthetic audio encoder for (seed, projection width, shape), written on first use."""
+    name = f"mmproj-gemma4a-s{seed}-p{projection_dim}-l{layers}-d{hidden}-h{heads}-f{ff}-v{FORMAT_VERSION}.gguf"
+    path = os.path.join(cache_dir(), name)
+    if not os.path.exists(path):
+        kw = dict(AUDIO, layers=layers, hidden=hidden, heads=heads, ff=ff)
+        arch = Arch(name="clip", hidden=hidden, layers=layers, heads=heads, head_dim_swa=0, head_dim_global=0,
+                    kv_swa=0, kv_global=0, ff=ff, per_layer=0, out_dim=0, dense_head=0)
+        write_gguf(path, arch, audio_tensors(seed, projection_dim, **kw), kvs=audio_metadata(projection_dim, **kw))
+    return path
+
+
+def synthetic_pcm(count: int, seconds: float, seed: int, rate: int = 16000) -> list:
+    """Gaussian-noise PCM clips (float32 at `rate`, mono) with standard deviation 0.1 from SeededRandom(seed)."""
+    n = int(round(seconds * rate))
+    out = []
+    for i in range(count):
+        u = floats(seed, 2 * n, 1.0, start=i * 2 * n).astype(np.float64).reshape(2, n)
+        u1 = np.clip((u[0] + 1.0) / 2.0, 1e-12, 1.0)
+        g = np.sqrt(-2.0 * np.log(u1)) * np.cos(np.pi * u[1])
+        out.append((0.1 * g).astype(np.float32))
+    return out
+
+
 # --------------------------------------------------------------------------- inputs
 def config_sequences(config: int, seed: int = 0, vocab: int = VOCAB, scale_texts: int = 1) -> list:
     """Token-id sequences of a benchmark configuration, drawn from `SeededRandom(seed)`.

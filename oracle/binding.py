@@ -34,6 +34,14 @@ class OrVisionInfo(ctypes.Structure):
         ("std", ctypes.c_float * 3)]
 
 
+class OrAudioInfo(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("hidden", "layers", "heads", "head_dim", "ff", "mel_bins",
+                                             "projection_dim", "output_width", "window", "relative_positions",
+                                             "dw_kernel")] + [
+        ("sub_channels", ctypes.c_int32 * 2), ("eps", ctypes.c_float), ("softcap", ctypes.c_float),
+        ("ff_residual", ctypes.c_float)]
+
+
 def build() -> str:
     subprocess.run(["make", "-s", "-C", HERE], check=True)
     return LIB_PATH
@@ -81,6 +89,21 @@ def lib():
         L.or_round_f16.argtypes = [ctypes.c_float]
         L.or_round_f16.restype = ctypes.c_float
         L.or_tensor_shape.argtypes = [ctypes.c_void_p, ctypes.c_char_p, i64p, i32p]
+        L.or_audio_open.argtypes = [ctypes.c_char_p, P(ctypes.c_void_p), ctypes.c_char_p, ctypes.c_int]
+        L.or_audio_get_info.argtypes = [ctypes.c_void_p, P(OrAudioInfo)]
+        L.or_audio_forward.argtypes = [ctypes.c_void_p, f32p, ctypes.c_int32, f32p, TRACE_FN, ctypes.c_void_p]
+        L.or_audio_sinusoid.argtypes = [ctypes.c_int32, ctypes.c_int32, f32p]
+        L.or_audio_attention.argtypes = [f32p, f32p, f32p, f32p] + [ctypes.c_int32] * 4 + [ctypes.c_float, f32p]
+        L.or_audio_depthwise.argtypes = [f32p, ctypes.c_int32, ctypes.c_int32, f32p, ctypes.c_int32, f32p]
+        L.or_audio_frame_count.argtypes = [ctypes.c_int64]
+        L.or_audio_frame_count.restype = ctypes.c_int32
+        L.or_audio_tokens_for_frames.argtypes = [ctypes.c_int32]
+        L.or_audio_tokens_for_frames.restype = ctypes.c_int32
+        L.or_audio_token_count.argtypes = [ctypes.c_int64]
+        L.or_audio_token_count.restype = ctypes.c_int64
+        L.or_audio_tables.argtypes = [ctypes.c_int32, f32p, f32p, f32p, f32p, i32p, i32p, i32p]
+        L.or_audio_log_mel.argtypes = [f32p, ctypes.c_int64, ctypes.c_int32, f32p]
+        L.or_audio_log_mel.restype = ctypes.c_int32
         _lib = L
     return _lib
 
@@ -220,6 +243,103 @@ class OracleVision:
         tw, th = target_size(w, h, align, 70 * align * align, max_image_tokens * align * align)
         img = fit_image(rgb, tw, th)
         return patchify(img, i.patch, list(i.mean), list(i.std)), tw // i.patch, th // i.patch
+
+
+class OracleAudio:
+    """CPUAudioReference over an mmproj file: one 30-second chunk per `forward` call."""
+
+    CHUNK_SAMPLES = 30 * 16000
+
+    def __init__(self, path: str):
+        L = lib()
+        h = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(512)
+        rc = L.or_audio_open(path.encode(), ctypes.byref(h), err, 512)
+        if rc:
+            raise OracleError(rc, err.value.decode())
+        self._h = h
+        info = OrAudioInfo()
+        L.or_audio_get_info(h, ctypes.byref(info))
+        self.info = info
+
+    def close(self):
+        if self._h:
+            lib().or_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, mel, trace: dict | None = None) -> np.ndarray:
+        """The projected rows ([tokens][projection_dim]) of one chunk's log-mel frames ([frames][mel_bins])."""
+        m = np.ascontiguousarray(mel, dtype=np.float32)
+        frames = m.shape[0]
+        out = np.zeros((tokens_for_frames(frames), self.info.projection_dim), dtype=np.float32)
+        cb = _trace_cb(trace)
+        rc = lib().or_audio_forward(self._h, m.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), frames,
+                                    out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), cb, None)
+        if rc:
+            raise OracleError(rc, "audio forward rejected its input")
+        return out
+
+    def prepare(self, samples) -> list:
+        """AudioFrontEnd.prepare: the log-mel frames of each 30-second chunk of a 16 kHz clip."""
+        return [log_mel(c, self.info.mel_bins) for c in chunks(samples)]
+
+    def embed_rows(self, samples) -> np.ndarray:
+        """All of a clip's projected rows, chunk after chunk."""
+        return np.concatenate([self.forward(m) for m in self.prepare(samples)], axis=0)
+
+
+def chunks(samples) -> list:
+    s = np.ascontiguousarray(samples, dtype=np.float32)
+    n = OracleAudio.CHUNK_SAMPLES
+    return [s[i:i + n] for i in range(0, len(s), n)]
+
+
+def frame_count(samples: int) -> int:
+    return lib().or_audio_frame_count(samples)
+
+
+def tokens_for_frames(frames: int) -> int:
+    return lib().or_audio_tokens_for_frames(frames)
+
+
+def audio_token_count(samples: int) -> int:
+    return lib().or_audio_token_count(samples)
+
+
+def audio_tables(mel_bins: int = 128) -> dict:
+    f32 = ctypes.POINTER(ctypes.c_float)
+    i32 = ctypes.POINTER(ctypes.c_int32)
+    t = dict(hann=np.zeros(512, np.float32), sin=np.zeros(512, np.float32), cos=np.zeros(512, np.float32),
+             filters=np.zeros((mel_bins, 257), np.float32), lo=np.zeros(mel_bins, np.int32),
+             hi=np.zeros(mel_bins, np.int32), bitrev=np.zeros(512, np.int32))
+    lib().or_audio_tables(mel_bins, t["hann"].ctypes.data_as(f32), t["sin"].ctypes.data_as(f32),
+                          t["cos"].ctypes.data_as(f32), t["filters"].ctypes.data_as(f32), t["lo"].ctypes.data_as(i32),
+                          t["hi"].ctypes.data_as(i32), t["bitrev"].ctypes.data_as(i32))
+    return t
+
+
+def log_mel(samples, mel_bins: int = 128) -> np.ndarray:
+    """AudioFrontEnd.logMel of one chunk (at most 480000 samples): [frames][mel_bins]."""
+    s = np.ascontiguousarray(samples, dtype=np.float32)
+    frames = frame_count(len(s))
+    if frames < 1:
+        raise OracleError(16, f"the clip has {len(s)} samples at 16 kHz; at least 2 are needed for one frame")
+    out = np.zeros((frames, mel_bins), np.float32)
+    f32 = ctypes.POINTER(ctypes.c_float)
+    lib().or_audio_log_mel(s.ctypes.data_as(f32), len(s), mel_bins, out.ctypes.data_as(f32))
+    return out
+
+
+def audio_sinusoid(position: int, width: int) -> np.ndarray:
+    out = np.zeros(width, np.float32)
+    lib().or_audio_sinusoid(position, width, out.ctypes.data_as(ctypes.POINTER(ctypes.c_float)))
+    return out
 
 
 def target_size(width, height, alignment, min_pixels, max_pixels):

@@ -10,6 +10,7 @@
 #include "oracle.h"
 
 #include <errno.h>
+#include <float.h>
 #include <fcntl.h>
 #include <math.h>
 #include <omp.h>
@@ -61,6 +62,7 @@ struct or_model {
     int rope_owner[MAX_LAYERS];
     float out_scale[MAX_LAYERS];
     or_vinfo vinfo; /* an mmproj file opened by or_vision_open */
+    or_ainfo ainfo; /* an mmproj file opened by or_audio_open */
 };
 
 static int set_err(char* err, int errlen, int code, const char* fmt, ...) {
@@ -1372,4 +1374,430 @@ void or_patchify(const uint8_t* rgb, int32_t w, int32_t h, int32_t p, const floa
                         patches[i * area + (int64_t)c * p * p + ky * p + kx] = or_round_f16(2.0f * f - 1.0f);
                     }
         }
+}
+
+/* ------------------------------------------------------------------ gemma4a audio tower */
+/* AudioConfig.init (AudioConfig.swift:50-85). */
+static int read_audio_config(or_model* m, char* err, int errlen) {
+    char got[64];
+    const kv_t* a = find_kv(m, "general.architecture");
+    if (!kv_string_is(a, "clip")) {
+        kv_string_copy(a, got, sizeof got);
+        return set_err(err, errlen, OR_ERR_INVALID_GGUF, "audio encoder architecture is '%s', expected clip", got);
+    }
+    const kv_t* has = find_kv(m, "clip.has_audio_encoder");
+    if (!has || has->type != 7 || has->raw[0] == 0)
+        return set_err(err, errlen, OR_ERR_INVALID_GGUF, "the mmproj file has no audio encoder (clip.has_audio_encoder)");
+    const kv_t* pr = find_kv(m, "clip.audio.projector_type");
+    if (!kv_string_is(pr, "gemma4a")) {
+        kv_string_copy(pr, got, sizeof got);
+        return set_err(err, errlen, OR_ERR_INVALID_GGUF, "audio projector is '%s', expected gemma4a", got);
+    }
+    or_ainfo* A = &m->ainfo;
+#define AINT(dst, k)                                                                                            \
+    do {                                                                                                        \
+        const kv_t* kv_ = find_kv(m, "clip.audio." k);                                                          \
+        int64_t v_;                                                                                             \
+        if (!kv_ || !kv_int(kv_, &v_)) return set_err(err, errlen, OR_ERR_MISSING_METADATA, "weight file lacks metadata key clip.audio." k); \
+        dst = (int32_t)v_;                                                                                      \
+    } while (0)
+    AINT(A->hidden, "embedding_length");
+    AINT(A->heads, "attention.head_count");
+    if (A->heads <= 0 || A->hidden % A->heads)
+        return set_err(err, errlen, OR_ERR_INVALID_GGUF, "audio width %d does not split into %d heads", A->hidden, A->heads);
+    AINT(A->mel_bins, "num_mel_bins");
+    if (A->mel_bins % 4)
+        return set_err(err, errlen, OR_ERR_INVALID_GGUF, "%d mel bins do not survive two stride-2 convolutions evenly", A->mel_bins);
+    AINT(A->layers, "block_count");
+    AINT(A->ff, "feed_forward_length");
+    AINT(A->projection_dim, "projection_dim");
+#undef AINT
+    tensor_t* o = find_tensor(m, "a.pre_encode.out.weight");
+    if (!o || o->ndim != 2 || o->shape[0] != A->hidden)
+        return set_err(err, errlen, OR_ERR_INVALID_GGUF, "a.pre_encode.out.weight is missing or not [%d, n]", A->hidden);
+    A->output_width = (int32_t)o->shape[1];
+    if (A->layers <= 0 || A->layers > MAX_LAYERS)
+        return set_err(err, errlen, OR_ERR_INVALID_GGUF, "invalid GGUF file: %d audio layers", A->layers);
+    A->head_dim = A->hidden / A->heads;
+    A->eps = 1e-6f; /* AudioConfig.swift:26-27: fixed, the file's epsilon is ignored */
+    A->window = 12;
+    A->relative_positions = 13;
+    A->softcap = 50.0f;
+    A->ff_residual = 0.5f;
+    A->dw_kernel = 5;
+    A->sub_channels[0] = 128;
+    A->sub_channels[1] = 32;
+    return OR_OK;
+}
+
+/* AudioWeights.init's checks (AudioWeights.swift:67-135). */
+static int audio_linear_check(or_model* m, const char* base, int64_t in, int64_t out, char* err, int errlen) {
+    char name[128];
+    int64_t s[2] = {in, out};
+    int rc;
+    snprintf(name, sizeof name, "%s.weight", base);
+    if ((rc = vision_tensor(m, name, 2, s, 1 | 2 | 4 | 8, err, errlen))) return rc;
+    snprintf(name, sizeof name, "%s.bias", base);
+    if (find_tensor(m, name) && (rc = vision_tensor(m, name, 1, &s[1], 1, err, errlen))) return rc;
+    static const char* bounds[4] = {"input_min", "input_max", "output_min", "output_max"};
+    const int64_t one = 1;
+    for (int i = 0; i < 4; i++) {
+        snprintf(name, sizeof name, "%s.%s", base, bounds[i]);
+        if (find_tensor(m, name) && (rc = vision_tensor(m, name, 1, &one, 1, err, errlen))) return rc;
+    }
+    return OR_OK;
+}
+
+static int check_audio_weights(or_model* m, char* err, int errlen) {
+    const or_ainfo* A = &m->ainfo;
+    const int64_t d = A->hidden, ff = A->ff;
+    int rc;
+    char name[128];
+    int64_t in_c = 1;
+    for (int i = 0; i < 2; i++) {
+        int64_t s[4] = {3, 3, in_c, A->sub_channels[i]};
+        snprintf(name, sizeof name, "a.conv1d.%d.weight", i);
+        if ((rc = vision_tensor(m, name, 4, s, 1, err, errlen))) return rc;
+        snprintf(name, sizeof name, "a.conv1d.%d.norm.weight", i);
+        if ((rc = vision_tensor(m, name, 1, &s[3], 1, err, errlen))) return rc;
+        in_c = A->sub_channels[i];
+    }
+    if ((rc = audio_linear_check(m, "a.input_projection", (int64_t)(A->mel_bins / 4) * A->sub_channels[1], d, err, errlen))) return rc;
+    if ((rc = audio_linear_check(m, "a.pre_encode.out", d, A->output_width, err, errlen))) return rc;
+    if ((rc = audio_linear_check(m, "mm.a.input_projection", A->output_width, A->projection_dim, err, errlen))) return rc;
+    struct { const char* s; int64_t in, out; } lin[] = {
+        {"ffn_up", d, ff},   {"ffn_down", ff, d}, {"attn_q", d, d},    {"attn_k", d, d},      {"attn_v", d, d},
+        {"attn_out", d, d},  {"attn_k_rel", d, d}, {"conv_pw1", d, 2 * d}, {"conv_pw2", d, d}, {"ffn_up_1", d, ff},
+        {"ffn_down_1", ff, d},
+    };
+    static const char* norms[] = {"ffn_norm", "ffn_post_norm", "attn_pre_norm", "attn_post_norm", "conv_norm",
+                                  "norm_conv", "ffn_norm_1", "ffn_post_norm_1", "ln2"};
+    for (int l = 0; l < A->layers; l++) {
+        for (size_t i = 0; i < sizeof lin / sizeof lin[0]; i++) {
+            snprintf(name, sizeof name, "a.blk.%d.%s", l, lin[i].s);
+            if ((rc = audio_linear_check(m, name, lin[i].in, lin[i].out, err, errlen))) return rc;
+        }
+        for (size_t i = 0; i < sizeof norms / sizeof norms[0]; i++) {
+            snprintf(name, sizeof name, "a.blk.%d.%s.weight", l, norms[i]);
+            if ((rc = vision_tensor(m, name, 1, &d, 1, err, errlen))) return rc;
+        }
+        const int64_t hd = A->head_dim, dw[2] = {A->dw_kernel, d};
+        snprintf(name, sizeof name, "a.blk.%d.per_dim_scale.weight", l);
+        if ((rc = vision_tensor(m, name, 1, &hd, 1, err, errlen))) return rc;
+        snprintf(name, sizeof name, "a.blk.%d.conv_dw.weight", l);
+        if ((rc = vision_tensor(m, name, 2, dw, 1, err, errlen))) return rc;
+    }
+    return OR_OK;
+}
+
+int or_audio_open(const char* path, or_model** out, char* err, int errlen) {
+    *out = NULL;
+    or_model* m = (or_model*)calloc(1, sizeof(or_model));
+    int rc = parse_gguf(m, path, err, errlen);
+    if (!rc) rc = read_audio_config(m, err, errlen);
+    if (!rc) rc = check_audio_weights(m, err, errlen);
+    if (rc) {
+        or_close(m);
+        return rc;
+    }
+    *out = m;
+    return OR_OK;
+}
+
+int or_audio_get_info(const or_model* a, or_ainfo* info) {
+    *info = a->ainfo;
+    return OR_OK;
+}
+
+/* A ClippedLinear's scalar bound, the float range when absent (AudioWeights.swift:89-92). */
+static float audio_bound(or_model* m, const char* base, const char* which, float dflt) {
+    char name[128];
+    snprintf(name, sizeof name, "%s.%s", base, which);
+    tensor_t* t = find_tensor(m, name);
+    if (!t) return dflt;
+    float v;
+    memcpy(&v, t->data, 4);
+    return v;
+}
+
+static void clamp_into(const float* x, int64_t n, float lo, float hi, float* out) {
+    for (int64_t i = 0; i < n; i++) out[i] = fminf(fmaxf(x[i], lo), hi);
+}
+
+/* CPUAudioReference.linear (CPUAudioReference.swift:51-62): clamp(clamp(x) @ W^T) (+ bias). */
+static void audio_linear(or_model* m, const char* base, const float* x, int64_t rows, int64_t in, int64_t out, float* y) {
+    char name[128];
+    const float in_lo = audio_bound(m, base, "input_min", -FLT_MAX), in_hi = audio_bound(m, base, "input_max", FLT_MAX);
+    const float out_lo = audio_bound(m, base, "output_min", -FLT_MAX), out_hi = audio_bound(m, base, "output_max", FLT_MAX);
+    float* tmp = NULL;
+    if (in_lo != -FLT_MAX || in_hi != FLT_MAX) {
+        tmp = (float*)malloc((size_t)(rows * in) * 4);
+        clamp_into(x, rows * in, in_lo, in_hi, tmp);
+        x = tmp;
+    }
+    snprintf(name, sizeof name, "%s.weight", base);
+    or_matmul(x, rows, in, matrix(m, find_tensor(m, name)), out, y);
+    if (out_lo != -FLT_MAX || out_hi != FLT_MAX) clamp_into(y, rows * out, out_lo, out_hi, y);
+    snprintf(name, sizeof name, "%s.bias", base);
+    tensor_t* b = find_tensor(m, name);
+    if (b) {
+        const float* bv = (const float*)b->data;
+        for (int64_t r = 0; r < rows; r++)
+            for (int64_t i = 0; i < out; i++) y[r * out + i] += bv[i];
+    }
+    free(tmp);
+}
+
+/* CPUAudioReference.subsample (CPUAudioReference.swift:67-101): conv kernel 3, stride 2, pad 1
+ * over [time][freq][channels] with fp16-rounded inputs, then LayerNorm over the output channels
+ * times the norm weight, then ReLU. The weight is [out][channels][3][3]. */
+static float* audio_subsample(const float* x, int32_t time, int32_t freq, int32_t channels, const float* w,
+                              int32_t out_c, const float* norm, float eps, int32_t* out_time, int32_t* out_freq) {
+    const int32_t ot_n = (time - 1) / 2 + 1, of_n = (freq - 1) / 2 + 1;
+    const int64_t taps = 9LL * channels;
+    float* out = (float*)malloc((size_t)ot_n * of_n * out_c * 4);
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int32_t ot = 0; ot < ot_n; ot++) {
+        float* patch = (float*)malloc((size_t)(of_n * taps) * 4);
+        float* col = (float*)malloc((size_t)of_n * out_c * 4);
+        for (int32_t of = 0; of < of_n; of++)
+            for (int kh = 0; kh < 3; kh++) {
+                const int32_t t = 2 * ot + kh - 1;
+                for (int kw = 0; kw < 3; kw++) {
+                    const int32_t f = 2 * of + kw - 1;
+                    const int inside = t >= 0 && t < time && f >= 0 && f < freq;
+                    for (int32_t c = 0; c < channels; c++)
+                        patch[of * taps + c * 9 + kh * 3 + kw] =
+                            inside ? or_round_f16(x[((int64_t)t * freq + f) * channels + c]) : 0.0f;
+                }
+            }
+        for (int32_t of = 0; of < of_n; of++)
+            for (int32_t o = 0; o < out_c; o++) {
+                const float* a = patch + of * taps;
+                const float* b = w + (int64_t)o * taps;
+                float s = 0;
+                for (int64_t i = 0; i < taps; i++) s += a[i] * b[i];
+                col[of * out_c + o] = s;
+            }
+        for (int32_t of = 0; of < of_n; of++) {
+            const float* c = col + of * out_c;
+            float mean = 0, var = 0;
+            for (int32_t i = 0; i < out_c; i++) mean += c[i];
+            mean /= (float)out_c;
+            for (int32_t i = 0; i < out_c; i++) var += (c[i] - mean) * (c[i] - mean);
+            var /= (float)out_c;
+            const float scale = 1.0f / sqrtf(var + eps);
+            float* o = out + ((int64_t)ot * of_n + of) * out_c;
+            for (int32_t i = 0; i < out_c; i++) o[i] = fmaxf(0.0f, (c[i] - mean) * scale * norm[i]);
+        }
+        free(patch);
+        free(col);
+    }
+    *out_time = ot_n;
+    *out_freq = of_n;
+    return out;
+}
+
+/* CPUAudioReference.sinusoid (CPUAudioReference.swift:105-115). */
+void or_audio_sinusoid(int32_t position, int32_t width, float* out) {
+    const int32_t ts = width / 2;
+    const float inc = logf(10000.0f) / (float)(ts - 1 > 1 ? ts - 1 : 1);
+    for (int32_t i = 0; i < ts; i++) {
+        const float scaled = (float)position * expf(-(float)i * inc);
+        out[i] = sinf(scaled);
+        out[i + ts] = cosf(scaled);
+    }
+}
+
+/* CPUAudioReference.attention (CPUAudioReference.swift:127-165): query t sees keys t-11..t,
+ * scored by content plus the relative key of their distance, capped at softcap*tanh(s/softcap). */
+void or_audio_attention(const float* q, const float* k, const float* v, const float* rel, int32_t tokens, int32_t heads,
+                        int32_t hd, int32_t window, float softcap, float* out) {
+    const int64_t width = (int64_t)heads * hd;
+    memset(out, 0, sizeof(float) * (size_t)(tokens * width));
+#pragma omp parallel for collapse(2) schedule(static)
+    for (int32_t h = 0; h < heads; h++)
+        for (int32_t t = 0; t < tokens; t++) {
+            float sc[64];
+            const int32_t first = t - window + 1 > 0 ? t - window + 1 : 0;
+            const float* qr = q + t * width + (int64_t)h * hd;
+            float mx = -INFINITY;
+            for (int32_t j = first; j <= t; j++) {
+                const float* kr = k + j * width + (int64_t)h * hd;
+                const float* rr = rel + (int64_t)(t - j) * width + (int64_t)h * hd;
+                float s = 0, r = 0;
+                for (int32_t i = 0; i < hd; i++) s += qr[i] * kr[i];
+                for (int32_t i = 0; i < hd; i++) r += qr[i] * rr[i];
+                const float c = softcap * tanhf((s + r) / softcap);
+                sc[j - first] = c;
+                mx = fmaxf(mx, c);
+            }
+            float sum = 0;
+            for (int32_t j = first; j <= t; j++) {
+                sc[j - first] = expf(sc[j - first] - mx);
+                sum += sc[j - first];
+            }
+            float* o = out + t * width + (int64_t)h * hd;
+            for (int32_t j = first; j <= t; j++) {
+                const float p = sc[j - first] / sum;
+                const float* vr = v + j * width + (int64_t)h * hd;
+                for (int32_t i = 0; i < hd; i++) o[i] += p * vr[i];
+            }
+        }
+}
+
+/* CPUAudioReference.depthwiseCausal (CPUAudioReference.swift:168-181): w is [width][kernel]. */
+void or_audio_depthwise(const float* x, int32_t tokens, int32_t width, const float* w, int32_t kernel, float* out) {
+#pragma omp parallel for schedule(static)
+    for (int32_t t = 0; t < tokens; t++)
+        for (int32_t c = 0; c < width; c++) {
+            float s = 0;
+            for (int32_t kk = 0; kk < kernel; kk++) {
+                const int32_t src = t + kk - (kernel - 1);
+                if (src >= 0) s += x[(int64_t)src * width + c] * w[(int64_t)c * kernel + kk];
+            }
+            out[(int64_t)t * width + c] = s;
+        }
+}
+
+static float silu(float x) { return x / (1.0f + expf(-x)); }
+static float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+/* CPUAudioReference.forward (CPUAudioReference.swift:186-283) over one chunk of `frames` log-mel
+ * frames: writes tokens_for_frames(frames) rows of projection_dim values. */
+int or_audio_forward(or_model* m, const float* mel, int32_t frames, float* out, or_trace_fn tr, void* user) {
+    const or_ainfo* A = &m->ainfo;
+    const int64_t d = A->hidden, heads = A->heads, hd = A->head_dim, ff = A->ff;
+    const float eps = A->eps;
+    if (frames < 1) return OR_ERR_INVALID_OPTIONS;
+    char name[96], base[64];
+    trace(tr, user, "mel", mel, (int64_t)frames * A->mel_bins);
+    int32_t time = frames, freq = A->mel_bins, channels = 1;
+    float* act = (float*)malloc((size_t)frames * A->mel_bins * 4);
+    memcpy(act, mel, (size_t)frames * A->mel_bins * 4);
+    for (int i = 0; i < 2; i++) {
+        snprintf(name, sizeof name, "a.conv1d.%d.weight", i);
+        const float* w = matrix(m, find_tensor(m, name));
+        snprintf(name, sizeof name, "a.conv1d.%d.norm.weight", i);
+        const float* nw = matrix(m, find_tensor(m, name));
+        int32_t ot, of;
+        float* next = audio_subsample(act, time, freq, channels, w, A->sub_channels[i], nw, eps, &ot, &of);
+        free(act);
+        act = next;
+        time = ot;
+        freq = of;
+        channels = A->sub_channels[i];
+        snprintf(name, sizeof name, "subsample-%d", i);
+        trace(tr, user, name, act, (int64_t)time * freq * channels);
+    }
+    const int64_t T = time;
+    float* x = (float*)malloc((size_t)(T * d) * 4);
+    audio_linear(m, "a.input_projection", act, T, (int64_t)freq * channels, d, x);
+    free(act);
+    trace(tr, user, "encoder_in", x, T * d);
+    float* h = (float*)malloc((size_t)(T * d) * 4);
+    float* up = (float*)malloc((size_t)(T * (ff > 2 * d ? ff : 2 * d)) * 4);
+    float* down = (float*)malloc((size_t)(T * d) * 4);
+    float* q = (float*)malloc((size_t)(T * d) * 4);
+    float* k = (float*)malloc((size_t)(T * d) * 4);
+    float* v = (float*)malloc((size_t)(T * d) * 4);
+    float* attn = (float*)malloc((size_t)(T * d) * 4);
+    float* rel = (float*)malloc((size_t)(A->relative_positions * d) * 4);
+    float* table = (float*)malloc((size_t)(A->relative_positions * d) * 4);
+    for (int32_t p = 0; p < A->relative_positions; p++) or_audio_sinusoid(p, (int32_t)d, table + p * d);
+    const float qscale = (1.0f / sqrtf((float)hd)) / logf(2.0f);
+    const float kscale = logf(1.0f + expf(1.0f)) / logf(2.0f);
+#define AW(l, suffix) (snprintf(name, sizeof name, "a.blk.%d." suffix, l), matrix(m, find_tensor(m, name)))
+#define LIN(l, suffix, src, in, outw, dst) (snprintf(base, sizeof base, "a.blk.%d." suffix, l), audio_linear(m, base, src, T, in, outw, dst))
+#define TRACE(fmt, l, data, n) (snprintf(name, sizeof name, fmt, l), trace(tr, user, name, data, n))
+    for (int l = 0; l < A->layers; l++) {
+        /* feed-forward 1, half step */
+        or_rmsnorm(x, T, d, AW(l, "ffn_norm.weight"), eps, h);
+        TRACE("ffn1_normed-%d", l, h, T * d);
+        LIN(l, "ffn_up", h, d, ff, up);
+        TRACE("ffn1_up-%d", l, up, T * ff);
+        for (int64_t i = 0; i < T * ff; i++) up[i] = silu(up[i]);
+        LIN(l, "ffn_down", up, ff, d, down);
+        TRACE("ffn1_down-%d", l, down, T * d);
+        or_rmsnorm(down, T, d, AW(l, "ffn_post_norm.weight"), eps, down);
+        TRACE("ffn1_post_normed-%d", l, down, T * d);
+        for (int64_t i = 0; i < T * d; i++) x[i] += A->ff_residual * down[i];
+        TRACE("after_ffn1-%d", l, x, T * d);
+        /* attention */
+        or_rmsnorm(x, T, d, AW(l, "attn_pre_norm.weight"), eps, h);
+        TRACE("attn_normed-%d", l, h, T * d);
+        LIN(l, "attn_q", h, d, d, q);
+        LIN(l, "attn_k", h, d, d, k);
+        LIN(l, "attn_v", h, d, d, v);
+        TRACE("v-%d", l, v, T * d);
+        const float* pds = AW(l, "per_dim_scale.weight");
+        for (int64_t t = 0; t < T; t++)
+            for (int64_t hh = 0; hh < heads; hh++)
+                for (int64_t i = 0; i < hd; i++) q[(t * heads + hh) * hd + i] *= qscale * pds[i];
+        for (int64_t i = 0; i < T * d; i++) k[i] *= kscale;
+        TRACE("q_scaled-%d", l, q, T * d);
+        TRACE("k_scaled-%d", l, k, T * d);
+        snprintf(base, sizeof base, "a.blk.%d.attn_k_rel", l);
+        audio_linear(m, base, table, A->relative_positions, d, d, rel);
+        TRACE("k_rel-%d", l, rel, A->relative_positions * d);
+        or_audio_attention(q, k, v, rel, (int32_t)T, (int32_t)heads, (int32_t)hd, A->window, A->softcap, attn);
+        TRACE("attn-%d", l, attn, T * d);
+        LIN(l, "attn_out", attn, d, d, down);
+        TRACE("attn_out-%d", l, down, T * d);
+        or_rmsnorm(down, T, d, AW(l, "attn_post_norm.weight"), eps, down);
+        for (int64_t i = 0; i < T * d; i++) x[i] += down[i];
+        TRACE("after_attn-%d", l, x, T * d);
+        /* convolution module */
+        or_rmsnorm(x, T, d, AW(l, "conv_norm.weight"), eps, h);
+        TRACE("conv_normed-%d", l, h, T * d);
+        LIN(l, "conv_pw1", h, d, 2 * d, up);
+        TRACE("conv_pw1-%d", l, up, T * 2 * d);
+        for (int64_t t = 0; t < T; t++)
+            for (int64_t i = 0; i < d; i++) h[t * d + i] = up[t * 2 * d + i] * sigmoidf_(up[t * 2 * d + d + i]);
+        TRACE("conv_glu-%d", l, h, T * d);
+        or_audio_depthwise(h, (int32_t)T, (int32_t)d, AW(l, "conv_dw.weight"), A->dw_kernel, down);
+        TRACE("conv_dw-%d", l, down, T * d);
+        or_rmsnorm(down, T, d, AW(l, "norm_conv.weight"), eps, down);
+        for (int64_t i = 0; i < T * d; i++) down[i] = silu(down[i]);
+        TRACE("conv_silu-%d", l, down, T * d);
+        LIN(l, "conv_pw2", down, d, d, attn);
+        TRACE("conv_pw2-%d", l, attn, T * d);
+        for (int64_t i = 0; i < T * d; i++) x[i] += attn[i];
+        TRACE("after_conv-%d", l, x, T * d);
+        /* feed-forward 2, half step */
+        or_rmsnorm(x, T, d, AW(l, "ffn_norm_1.weight"), eps, h);
+        TRACE("ffn2_normed-%d", l, h, T * d);
+        LIN(l, "ffn_up_1", h, d, ff, up);
+        TRACE("ffn2_up-%d", l, up, T * ff);
+        for (int64_t i = 0; i < T * ff; i++) up[i] = silu(up[i]);
+        LIN(l, "ffn_down_1", up, ff, d, down);
+        TRACE("ffn2_down-%d", l, down, T * d);
+        or_rmsnorm(down, T, d, AW(l, "ffn_post_norm_1.weight"), eps, down);
+        for (int64_t i = 0; i < T * d; i++) x[i] += A->ff_residual * down[i];
+        TRACE("after_ffn2-%d", l, x, T * d);
+        or_rmsnorm(x, T, d, AW(l, "ln2.weight"), eps, x);
+        TRACE("layer_out-%d", l, x, T * d);
+    }
+#undef AW
+#undef LIN
+#undef TRACE
+    const int64_t ow = A->output_width;
+    float* o = (float*)malloc((size_t)(T * ow) * 4);
+    audio_linear(m, "a.pre_encode.out", x, T, d, ow, o);
+    trace(tr, user, "out_proj", o, T * ow);
+    or_rmsnorm(o, T, ow, NULL, eps, o);
+    audio_linear(m, "mm.a.input_projection", o, T, ow, A->projection_dim, out);
+    trace(tr, user, "projected", out, T * A->projection_dim);
+    free(o);
+    free(x);
+    free(h);
+    free(up);
+    free(down);
+    free(q);
+    free(k);
+    free(v);
+    free(attn);
+    free(rel);
+    free(table);
+    return OR_OK;
 }

@@ -103,6 +103,34 @@ void or_patchify(const uint8_t* rgb, int32_t w, int32_t h, int32_t p, const floa
 /* Float(Float16(x)): round to the nearest fp16 value, ties to even. */
 float or_round_f16(float x);
 
+/* ---- gemma4a audio tower (Sources/GemmaEmbed/Model/AudioConfig.swift, AudioWeights.swift,
+ * CPUAudioReference.swift) and the log-mel front end (Audio/AudioPreprocessor.swift, in logmel.c). */
+typedef struct {
+    int32_t hidden, layers, heads, head_dim, ff, mel_bins, projection_dim, output_width;
+    int32_t window, relative_positions, dw_kernel, sub_channels[2];
+    float eps, softcap, ff_residual;
+} or_ainfo;
+
+/* AudioConfig(gguf:) and AudioWeights(gguf:config:) over an mmproj file. */
+int or_audio_open(const char* path, or_model** out, char* err, int errlen);
+int or_audio_get_info(const or_model* a, or_ainfo* info);
+/* CPUAudioReference.forward on one chunk: `mel` is [frames][mel_bins]; writes
+ * or_audio_tokens_for_frames(frames) rows of projection_dim floats. */
+int or_audio_forward(or_model* a, const float* mel, int32_t frames, float* out, or_trace_fn trace, void* user);
+void or_audio_sinusoid(int32_t position, int32_t width, float* out);
+void or_audio_attention(const float* q, const float* k, const float* v, const float* rel, int32_t tokens, int32_t heads,
+                        int32_t hd, int32_t window, float softcap, float* out);
+void or_audio_depthwise(const float* x, int32_t tokens, int32_t width, const float* w, int32_t kernel, float* out);
+/* AudioFrontEnd (AudioPreprocessor.swift:74-95): frames of one chunk, tokens from frames, tokens of a clip. */
+int32_t or_audio_frame_count(int64_t samples);
+int32_t or_audio_tokens_for_frames(int32_t frames);
+int64_t or_audio_token_count(int64_t samples);
+/* AudioFrontEnd.init's tables: hann/sin/cos [512], filters [mel_bins][257], bands [mel_bins], bitrev [512]. */
+void or_audio_tables(int32_t mel_bins, float* hann, float* sin_t, float* cos_t, float* filters, int32_t* band_lo,
+                     int32_t* band_hi, int32_t* bitrev);
+/* AudioFrontEnd.logMel on one chunk of n <= 480000 samples: writes frame_count(n) rows of mel_bins. */
+int32_t or_audio_log_mel(const float* samples, int64_t n, int32_t mel_bins, float* out);
+
 /* Static pieces, exposed for unit tests. */
 void or_matmul(const float* x, int64_t m, int64_t k, const float* w, int64_t n, float* y);
 void or_rmsnorm(const float* x, int64_t rows, int64_t width, const float* weight, float eps, float* out);
