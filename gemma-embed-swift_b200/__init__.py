@@ -21,7 +21,8 @@ import numpy as np
 
 from . import _lib
 
-__all__ = ["EmbeddingModel", "EmbedOptions", "LoadOptions", "ImageEmbedOptions", "MultimodalEmbedOptions", "Embedding",
+__all__ = ["EmbeddingModel", "EmbedOptions", "LoadOptions", "ImageEmbedOptions", "MultimodalEmbedOptions", "AudioEmbedOptions",
+           "audio_tokens", "Embedding",
            "EmbeddingProgress", "ModelInfo", "GemmaEmbedError", "TaskPrefix", "Tokenizer", "ALLOWED_DIMENSIONS"]
 
 ALLOWED_DIMENSIONS = (768, 512, 256, 128)
@@ -190,6 +191,8 @@ class LoadOptions:
     fused_residual: bool = False  # run each residual step inside the projection before it
     image_encoder: Optional[str] = None  # LoadOptions.imageEncoder: the mmproj GGUF
     image_patch_budget: int = 4096       # ImageEmbedOptions.patchBudget: patches per image batch
+    audio_encoder: Optional[str] = None  # LoadOptions.audioEncoder: the mmproj GGUF with a gemma4a tower
+    audio_frame_budget: int = 96000      # log-mel frames per audio batch (AudioEmbedOptions.frameBudget)
 
 
 @dataclass
@@ -209,6 +212,15 @@ class ImageEmbedOptions:
     dimensions: int = 768
     normalise: bool = True
     max_image_tokens: int = 256
+    batch_size: Optional[int] = None
+
+
+@dataclass
+class AudioEmbedOptions:
+    """AudioEmbedOptions (EmbedOptions.swift:91-114)."""
+    dimensions: int = 768
+    normalise: bool = True
+    max_tokens: Optional[int] = None  # None: the model's limit
     batch_size: Optional[int] = None
 
 
@@ -251,6 +263,39 @@ class ModelInfo:
     image_hidden_size: int = 0
     image_patch_size: int = 0
     image_projection_dim: int = 0
+    # AudioEncoderInfo (AudioConfig.swift:5-19); zeros without an audio encoder.
+    audio_layer_count: int = 0
+    audio_hidden_size: int = 0
+    audio_head_count: int = 0
+    audio_feed_forward_size: int = 0
+    audio_mel_bins: int = 0
+    audio_projection_dim: int = 0
+
+
+AUDIO_SAMPLE_RATE = 16000
+
+
+def audio_tokens(samples: int) -> int:
+    """AudioFrontEnd.tokenCount(samples:) (Audio/AudioPreprocessor.swift:86-95)."""
+    return int(_lib.lib().ge_audio_tokens(int(samples)))
+
+
+def _audios(clips):
+    """ge_audio views of 16 kHz mono float32 sample arrays (kept alive by the returned list).  A
+    clip may also be given as (samples, sample_rate, channels)."""
+    c = (_lib.GeAudio * max(len(clips), 1))()
+    keep = []
+    for i, clip in enumerate(clips):
+        rate, channels = AUDIO_SAMPLE_RATE, 1
+        if isinstance(clip, tuple):
+            clip, rate, channels = clip
+        a = np.ascontiguousarray(np.asarray(clip, dtype=np.float32).reshape(-1))
+        keep.append(a)
+        c[i].samples = a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+        c[i].count = a.size // max(int(channels), 1) if channels > 0 else a.size
+        c[i].sample_rate = int(rate)
+        c[i].channels = int(channels)
+    return c, keep
 
 
 def _images(images):
@@ -309,7 +354,10 @@ class EmbeddingModel:
             file_size=info.file_size, device_count=info.device_count, device_name=info.device_name.decode(),
             eos_id=info.eos_id, bos_id=info.bos_id, image_layer_count=info.image_layer_count,
             image_hidden_size=info.image_hidden_size, image_patch_size=info.image_patch_size,
-            image_projection_dim=info.image_projection_dim)
+            image_projection_dim=info.image_projection_dim, audio_layer_count=info.audio_layer_count,
+            audio_hidden_size=info.audio_hidden_size, audio_head_count=info.audio_head_count,
+            audio_feed_forward_size=info.audio_feed_forward_size, audio_mel_bins=info.audio_mel_bins,
+            audio_projection_dim=info.audio_projection_dim)
 
     @classmethod
     def load(cls, path: str, options: Optional[LoadOptions] = None) -> "EmbeddingModel":
@@ -328,6 +376,8 @@ class EmbeddingModel:
                    | (LOAD_FUSED_RESIDUAL if options.fused_residual else 0))
         o.image_encoder_path = str(options.image_encoder).encode() if options.image_encoder else None
         o.image_patch_budget = int(options.image_patch_budget)
+        o.audio_encoder_path = str(options.audio_encoder).encode() if options.audio_encoder else None
+        o.audio_frame_budget = int(options.audio_frame_budget)
         h = ctypes.c_void_p()
         _check(L.ge_load(str(path).encode(), ctypes.byref(o), ctypes.byref(h)), None)
         return cls(h, options)
@@ -565,6 +615,75 @@ class EmbeddingModel:
                                               _ptr(trunc, ctypes.c_int32), cb, None), self._h)
         del keep, arrays
         return [Embedding(out[i].copy(), int(counts[i]), bool(trunc[i])) for i in range(n)]
+
+    def embed_audios(self, clips, options: Optional[AudioEmbedOptions] = None,
+                     progress: Optional[Callable[[EmbeddingProgress], Optional[bool]]] = None) -> list:
+        """embed(audios:options:progress:) (AudioEmbedding.swift:17-33) over PCM clips: 16 kHz mono
+        float32 arrays (or (samples, rate, channels) tuples, which must also be 16 kHz mono); a
+        single 1-D array embeds one clip and returns one Embedding."""
+        options = options or AudioEmbedOptions()
+        single = isinstance(clips, np.ndarray) and clips.ndim == 1
+        items = [clips] if single else list(clips)
+        c, keep = _audios(items)
+        n = len(items)
+        if options.batch_size is not None and options.batch_size < 1:
+            raise GemmaEmbedError(9, "invalid options: batchSize must be at least 1")
+        o = _lib.GeAudioOpts(options.dimensions, int(options.normalise), options.max_tokens or 0,
+                             options.batch_size or 0)
+        out = np.zeros((max(n, 1), options.dimensions if options.dimensions > 0 else 1), dtype=np.float32)
+        counts = np.zeros(max(n, 1), dtype=np.int32)
+        cb = _lib.PROGRESS_FN(0)
+        if progress is not None:
+            def _cb(done, total, tokens, user):
+                return 1 if progress(EmbeddingProgress(done, total, tokens)) else 0
+            cb = _lib.PROGRESS_FN(_cb)
+        _check(_lib.lib().ge_embed_audios(self._h, c, n, ctypes.byref(o), _ptr(out, ctypes.c_float),
+                                          _ptr(counts, ctypes.c_int32), cb, None), self._h)
+        del keep
+        res = [Embedding(out[i].copy(), int(counts[i]), False) for i in range(n)]
+        return res[0] if single else res
+
+    def audio_vectors(self, clips) -> list:
+        """The audio tower's projected rows of each clip (MetalForward's audio rows)."""
+        items = list(clips)
+        c, keep = _audios(items)
+        n = len(items)
+        L = _lib.lib()
+        per = [int(L.ge_audio_tokens(int(c[i].count))) for i in range(n)]
+        cap = max(sum(per), 1)
+        out = np.zeros((cap, self.info.audio_projection_dim or 1), dtype=np.float32)
+        rows = np.zeros(max(n, 1), dtype=np.int32)
+        _check(L.ge_audio_vectors(self._h, c, n, _ptr(out, ctypes.c_float), cap, _ptr(rows, ctypes.c_int32)), self._h)
+        del keep
+        res, r0 = [], 0
+        for i in range(n):
+            res.append(out[r0:r0 + rows[i]].copy())
+            r0 += int(rows[i])
+        return res
+
+    def audio_forward_device(self, d_pcm, counts, d_out, stream=None, device: int = 0) -> None:
+        """ge_audio_forward_device: 16 kHz samples already on the GPU (`d_pcm`, clips back to back with
+        the sample counts in `counts`) to pooled rows in `d_out`, on `stream`."""
+        c = (_lib.GeAudio * max(len(counts), 1))()
+        for i, n in enumerate(counts):
+            c[i].count = int(n)
+            c[i].sample_rate = AUDIO_SAMPLE_RATE
+            c[i].channels = 1
+        _check(_lib.lib().ge_audio_forward_device(self._h, device, ctypes.c_void_p(int(d_pcm)), c, len(counts),
+                                                  ctypes.c_void_p(int(d_out)), ctypes.c_void_p(int(stream or 0))),
+               self._h)
+
+    def profile_audios(self, clips, reps: int = 5) -> list:
+        """Profiler.profileAudio (Metal/Profiler.swift:202-295): "audio_forward" (audio and text
+        towers) and "audio_tower" in ms, then each audio kernel class like `profile`."""
+        c, keep = _audios(list(clips))
+        cap = 64
+        out = (_lib.GeKernelTime * cap)()
+        cnt = ctypes.c_int32(0)
+        _check(_lib.lib().ge_profile_audios(self._h, c, len(keep), reps, out, cap, ctypes.byref(cnt)), self._h)
+        return [{"name": out[i].name.decode(), "ms_per_launch": out[i].ms_per_launch,
+                 "flops_per_launch": out[i].flops_per_launch, "bytes_per_launch": out[i].bytes_per_launch,
+                 "launches_per_forward": out[i].launches_per_forward} for i in range(cnt.value)]
 
     def image_vectors(self, images, max_image_tokens: int = 256) -> list:
         """MetalForward.imageVectors (Metal/MetalForward.swift:227-238): each image's projected rows."""

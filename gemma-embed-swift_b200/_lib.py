@@ -21,7 +21,17 @@ class GeSeq(ctypes.Structure):
 
 class GeLoadOpts(ctypes.Structure):
     _fields_ = [("device_mask", ctypes.c_uint32), ("batch_token_budget", ctypes.c_int32), ("flags", ctypes.c_uint32),
-                ("image_encoder_path", ctypes.c_char_p), ("image_patch_budget", ctypes.c_int32)]
+                ("image_encoder_path", ctypes.c_char_p), ("image_patch_budget", ctypes.c_int32),
+                ("audio_encoder_path", ctypes.c_char_p), ("audio_frame_budget", ctypes.c_int32)]
+
+
+class GeAudio(ctypes.Structure):
+    _fields_ = [("samples", ctypes.POINTER(ctypes.c_float)), ("count", ctypes.c_int64), ("sample_rate", ctypes.c_int32),
+                ("channels", ctypes.c_int32)]
+
+
+class GeAudioOpts(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("dimensions", "normalise", "max_tokens", "batch_size")]
 
 
 class GeImage(ctypes.Structure):
@@ -59,7 +69,9 @@ class GeInfo(ctypes.Structure):
         ("device_name", ctypes.c_char * 128), ("kernel_launches", ctypes.c_int64),
         ("host_to_device_bytes", ctypes.c_int64), ("device_to_host_bytes", ctypes.c_int64)] + [
         (n, ctypes.c_int32) for n in ("image_layer_count", "image_hidden_size", "image_patch_size",
-                                      "image_projection_dim")]
+                                      "image_projection_dim", "audio_layer_count", "audio_hidden_size",
+                                      "audio_head_count", "audio_feed_forward_size", "audio_mel_bins",
+                                      "audio_projection_dim")]
 
 
 class GeKernelTime(ctypes.Structure):
@@ -117,6 +129,15 @@ SIGNATURES = {
     "ge_image_tokens": ([ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32], ctypes.c_int32),
     "ge_image_vectors": ([ctypes.c_void_p, P(GeImage), ctypes.c_int32, ctypes.c_int32, f32p, ctypes.c_int64, i32p],
                          ctypes.c_int),
+    "ge_audio_opts_default": ([P(GeAudioOpts)], None),
+    "ge_audio_tokens": ([ctypes.c_int64], ctypes.c_int64),
+    "ge_embed_audios": ([ctypes.c_void_p, P(GeAudio), ctypes.c_int32, P(GeAudioOpts), f32p, i32p, PROGRESS_FN,
+                         ctypes.c_void_p], ctypes.c_int),
+    "ge_audio_vectors": ([ctypes.c_void_p, P(GeAudio), ctypes.c_int32, f32p, ctypes.c_int64, i32p], ctypes.c_int),
+    "ge_audio_forward_device": ([ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p, P(GeAudio), ctypes.c_int32,
+                                 ctypes.c_void_p, ctypes.c_void_p], ctypes.c_int),
+    "ge_profile_audios": ([ctypes.c_void_p, P(GeAudio), ctypes.c_int32, ctypes.c_int32, P(GeKernelTime),
+                           ctypes.c_int32, i32p], ctypes.c_int),
     "ge_embed_texts": ([ctypes.c_void_p, P(ctypes.c_char_p), i64p, ctypes.c_int32, ctypes.c_char_p, P(GeEmbedOpts),
                         f32p, i32p, i32p, PROGRESS_FN, ctypes.c_void_p], ctypes.c_int),
 }
@@ -139,6 +160,7 @@ TEST_SIGNATURES = {
                           ctypes.c_int32], ctypes.c_int),
     "ge_test_multimodal_sequence": ([ctypes.c_char_p, i32p, P(ctypes.c_char_p), ctypes.c_int32, i32p] +
                                     [ctypes.c_int32] * 7 + [i32p, ctypes.c_int32, i32p, i32p], ctypes.c_int),
+    "ge_test_log_mel": ([f32p, ctypes.c_int64, ctypes.c_int32, f32p, i32p], ctypes.c_int),
     "ge_test_last_error": ([], ctypes.c_char_p),
 }
 

@@ -47,7 +47,9 @@ def _compile(src: str, extra) -> str:
         return obj
     cmd = [nvcc()] + ARCH + COMMON + list(extra) + ["-c", src, "-o", obj]
     if src.endswith(".cpp"):
-        cmd = [nvcc()] + COMMON + list(extra) + ["-x", "c++", "-c", src, "-o", obj]
+        # Host code is compiled without floating-point contraction: the image resampler and the
+        # audio front end's tables reproduce the reference's separately rounded operations.
+        cmd = [nvcc()] + COMMON + list(extra) + ["-Xcompiler", "-ffp-contract=off", "-x", "c++", "-c", src, "-o", obj]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"nvcc failed on {src}:\n{r.stderr}")

@@ -68,6 +68,8 @@ struct GemmParams {
     const float* w_next;
     float scale, eps;
     int store_h, store_y;
+    // clamp epilogues (aux holds the optional bias)
+    float lo1, hi1, lo2, hi2;
 };
 
 // EPI_RESIDUAL output maps: the next norm's fp16 (boxes of 32 rows x 64) and fp32 (32 x 32)
@@ -532,13 +534,22 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
             const long row = y + lane;
             const uint32_t taddr = tmem + (uint32_t(warp * 32) << 16) + uint32_t(acc * BN);
             uint32_t packed[32];
-            if (EPI == EPI_F32) {
+            if (EPI == EPI_F32 || EPI == EPI_CLAMP_F32) {
                 uint32_t r[32];
 #pragma unroll 1
                 for (int c = 0; c < BN / 32; c++) {
                     tmem_ld32(taddr + uint32_t(c * 32), r);
                     tmem_wait_ld();
                     if (c == BN / 32 - 1) release(acc);
+                    if (EPI == EPI_CLAMP_F32) {
+                        const float* b = p.aux ? p.aux + n0 + c * 32 : nullptr;
+#pragma unroll
+                        for (int i = 0; i < 32; i++) {
+                            float v = fminf(fmaxf(__uint_as_float(r[i]), p.lo1), p.hi1);
+                            if (b) v += b[i];
+                            r[i] = __float_as_uint(v);
+                        }
+                    }
                     emit(r, n0 + c * 32, y, &mapC);
                 }
             } else if (epi_is_geglu(EPI)) {
@@ -556,13 +567,25 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
 #pragma unroll
                     for (int i = 0; i < 32; i++) {
                         const float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
-                        const float a0 = EPI == EPI_GEGLU ? gelu_fast(g0) : gelu_quick_fast(g0);
-                        const float a1 = EPI == EPI_GEGLU ? gelu_fast(g1) : gelu_quick_fast(g1);
-                        packed[i] = pack_half2(a0 * __uint_as_float(u[2 * i]), a1 * __uint_as_float(u[2 * i + 1]));
+                        float u0 = __uint_as_float(u[2 * i]), u1 = __uint_as_float(u[2 * i + 1]);
+                        float a0, a1;
+                        if (EPI == EPI_GEGLU) {
+                            a0 = gelu_fast(g0);
+                            a1 = gelu_fast(g1);
+                        } else if (EPI == EPI_GEGLU_QUICK) {
+                            a0 = gelu_quick_fast(g0);
+                            a1 = gelu_quick_fast(g1);
+                        } else {
+                            a0 = sigmoid_fast(fminf(fmaxf(g0, p.lo1), p.hi1));
+                            a1 = sigmoid_fast(fminf(fmaxf(g1, p.lo1), p.hi1));
+                            u0 = fminf(fmaxf(u0, p.lo1), p.hi1);
+                            u1 = fminf(fmaxf(u1, p.lo1), p.hi1);
+                        }
+                        packed[i] = pack_half2(a0 * u0, a1 * u1);
                     }
                     emit(packed, n0 / 2 + c * 64, y, &mapC);
                 }
-            } else if (EPI == EPI_F16 || EPI == EPI_GELU_MUL) {
+            } else if (EPI == EPI_F16 || EPI == EPI_GELU_MUL || EPI == EPI_CLAMP_F16 || EPI == EPI_CLAMP_SILU) {
                 // 128 columns in flight per wait, stored as two 64-column boxes.
 #pragma unroll 1
                 for (int c = 0; c < BN / 128; c++) {
@@ -585,6 +608,22 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
                                                            gelu_fast(__uint_as_float(rv[4 * i + 1])) * a.y);
                                 packed[2 * i + 1] = pack_half2(gelu_fast(__uint_as_float(rv[4 * i + 2])) * a.z,
                                                                gelu_fast(__uint_as_float(rv[4 * i + 3])) * a.w);
+                            }
+                        } else if (EPI == EPI_CLAMP_F16 || EPI == EPI_CLAMP_SILU) {
+                            const float* b = p.aux ? p.aux + n0 + c * 128 + half * 64 : nullptr;
+#pragma unroll
+                            for (int i = 0; i < 32; i++) {
+                                float v0 = fminf(fmaxf(__uint_as_float(rv[2 * i]), p.lo1), p.hi1);
+                                float v1 = fminf(fmaxf(__uint_as_float(rv[2 * i + 1]), p.lo1), p.hi1);
+                                if (b) {
+                                    v0 += b[2 * i];
+                                    v1 += b[2 * i + 1];
+                                }
+                                if (EPI == EPI_CLAMP_SILU) {
+                                    v0 = fminf(fmaxf(silu_fast(v0), p.lo2), p.hi2);
+                                    v1 = fminf(fmaxf(silu_fast(v1), p.lo2), p.hi2);
+                                }
+                                packed[i] = pack_half2(v0, v1);
                             }
                         } else {
 #pragma unroll
@@ -687,9 +726,10 @@ bool encode_weight_maps(DevWeight& w, int bn) {
                        CU_TENSOR_MAP_SWIZZLE_NONE) &&
              encode_2d(&w.map_scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.scales_t, w.N, w.K / 32, bn, 2,
                        CU_TENSOR_MAP_SWIZZLE_NONE);
+    // A weight narrower than a full tile (N = bn / 2) gets a full-tile map of its own height.
     if (ok && w.f16)
-        ok = encode_2d(&w.map_f16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.f16, w.K, w.N, BK, bn,
-                       CU_TENSOR_MAP_SWIZZLE_128B) &&
+        ok = encode_2d(&w.map_f16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.f16, w.K, w.N, BK,
+                       uint32_t(w.N < bn ? w.N : bn), CU_TENSOR_MAP_SWIZZLE_128B) &&
              encode_2d(&w.map_f16_half, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.f16, w.K, w.N, BK, bn / 2,
                        CU_TENSOR_MAP_SWIZZLE_128B);
     return ok;
@@ -745,6 +785,10 @@ cudaError_t configure_gemm_kernels() {
     if (e == cudaSuccess) e = configure_epi<EPI_GELU_MUL>();
     if (e == cudaSuccess) e = configure_epi<EPI_RESIDUAL>();
     if (e == cudaSuccess) e = configure_epi<EPI_GEGLU_QUICK>();
+    if (e == cudaSuccess) e = configure_epi<EPI_CLAMP_F32>();
+    if (e == cudaSuccess) e = configure_epi<EPI_CLAMP_F16>();
+    if (e == cudaSuccess) e = configure_epi<EPI_CLAMP_SILU>();
+    if (e == cudaSuccess) e = configure_epi<EPI_GLU>();
     return e;
 }
 
@@ -794,9 +838,13 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
     p.K = g.w->K;
     p.out = g.out;
     p.ldo = g.ldo;
-    p.aux = g.aux;
+    p.aux = epi_is_clamp(EPI) ? g.bias : g.aux;
     p.ldaux = g.ldaux;
     p.err = g.err;
+    p.lo1 = g.clamp_lo;
+    p.hi1 = g.clamp_hi;
+    p.lo2 = g.act_lo;
+    p.hi2 = g.act_hi;
     // Weight boxes: kBN rows (map_f16, map_q8) or kBN / 2 rows (CTA pairs, 128-wide tiles).
     const CUtensorMap& mb = Q8 ? g.w->map_q8 : ((PAIR || BN != kBN) ? g.w->map_f16_half : g.w->map_f16);
     CUtensorMap mc;
@@ -829,7 +877,7 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
                              g.w->map_scales, mc, em, p);
     }
     // Output map: boxes of 32 rows x 128 bytes (32 fp32 or 64 fp16 columns), 128-byte swizzle.
-    const bool f32 = EPI == EPI_F32;
+    const bool f32 = EPI == EPI_F32 || EPI == EPI_CLAMP_F32;
     const int out_cols = epi_is_geglu(EPI) ? g.w->N / 2 : g.w->N;
     if (g.ldo < out_cols) return cudaErrorInvalidValue;
     if (!encode_2d(&mc, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, f32 ? 4 : 2, g.out,
@@ -866,21 +914,27 @@ static cudaError_t launch_epi(const GemmLaunch& g, cudaStream_t stream, bool q8,
 
 cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream) {
     if (g.m_rows <= 0) return cudaSuccess;
-    if (g.m_rows % BM || g.w->N % kBN || g.w->K % BK || g.a->cols != g.w->K || g.a->rows < g.m_rows)
-        return cudaErrorInvalidValue;
     // The Q8 path needs the Q8 planes; weights without them always take the fp16 path.
     if (!g.w->f16 && !g.w->q8) return cudaErrorInvalidValue;
     const bool q8 = g.w->q8 && (g.use_q8 || !g.w->f16);
     const bool pair = !q8 && g.mode == GEMM_PAIR;
     // 128-wide tiles read each A tile twice as often; measured slower on every forward shape,
-    // so they run only when asked for.
-    const bool narrow = !q8 && !pair && !epi_is_geglu(g.epilogue) && g.mode == GEMM_NARROW;
+    // so they run only when asked for (or when N is a multiple of 128 but not of 256).
+    const bool narrow = !q8 && !pair && !epi_is_geglu(g.epilogue) &&
+                        (g.mode == GEMM_NARROW || (g.w->N % kBN && g.w->N % (kBN / 2) == 0 && g.mode == GEMM_AUTO));
+    if (g.m_rows % BM || g.w->N % (narrow ? kBN / 2 : kBN) || g.w->K % BK || g.a->cols != g.w->K ||
+        g.a->rows < g.m_rows)
+        return cudaErrorInvalidValue;
     switch (g.epilogue) {
     case EPI_F32: return launch_epi<EPI_F32>(g, stream, q8, pair, narrow);
     case EPI_F16: return launch_epi<EPI_F16>(g, stream, q8, pair, narrow);
     case EPI_GEGLU: return launch_epi<EPI_GEGLU>(g, stream, q8, pair, narrow);
     case EPI_GELU_MUL: return launch_epi<EPI_GELU_MUL>(g, stream, q8, pair, narrow);
     case EPI_GEGLU_QUICK: return launch_epi<EPI_GEGLU_QUICK>(g, stream, q8, pair, narrow);
+    case EPI_CLAMP_F32: return launch_epi<EPI_CLAMP_F32>(g, stream, q8, pair, narrow);
+    case EPI_CLAMP_F16: return launch_epi<EPI_CLAMP_F16>(g, stream, q8, pair, narrow);
+    case EPI_CLAMP_SILU: return launch_epi<EPI_CLAMP_SILU>(g, stream, q8, pair, narrow);
+    case EPI_GLU: return launch_epi<EPI_GLU>(g, stream, q8, pair, narrow);
     case EPI_RESIDUAL:
         if (g.mode == GEMM_PAIR || g.mode == GEMM_NARROW) return cudaErrorInvalidValue;
         return launch_epi<EPI_RESIDUAL>(g, stream, q8, false, false);

@@ -61,8 +61,23 @@ enum GemmEpilogue : int {
     EPI_RESIDUAL = 4,
     // As EPI_GEGLU with the quick GELU of the vision tower: out = gate / (1 + exp(-1.702 gate)) * up.
     EPI_GEGLU_QUICK = 5,
+    // The audio tower's clipped linears (Gemma4ClippableLinear): v = clamp(acc, lo, hi) + bias[n]
+    // (bias optional), stored as fp32 (EPI_CLAMP_F32) or fp16 (EPI_CLAMP_F16).
+    EPI_CLAMP_F32 = 6,
+    EPI_CLAMP_F16 = 7,
+    // out = clamp(silu(clamp(acc, lo, hi) + bias[n]), act_lo, act_hi) (fp16): a clipped linear, the
+    // SiLU after it, and the next clipped linear's input clamp.
+    EPI_CLAMP_SILU = 8,
+    // Gate/up interleaved as EPI_GEGLU: out = clamp(up) * sigmoid(clamp(gate)) (fp16), the
+    // convolution module's GLU over a clipped pointwise linear.
+    EPI_GLU = 9,
 };
-__host__ __device__ constexpr bool epi_is_geglu(int epi) { return epi == EPI_GEGLU || epi == EPI_GEGLU_QUICK; }
+__host__ __device__ constexpr bool epi_is_geglu(int epi) {
+    return epi == EPI_GEGLU || epi == EPI_GEGLU_QUICK || epi == EPI_GLU;
+}
+__host__ __device__ constexpr bool epi_is_clamp(int epi) {
+    return epi == EPI_CLAMP_F32 || epi == EPI_CLAMP_F16 || epi == EPI_CLAMP_SILU || epi == EPI_GLU;
+}
 
 
 // One GEMM weight as the device keeps it: the Q8_0 planes (int8 values [N][K] and the fp16
@@ -115,6 +130,11 @@ struct GemmLaunch {
     float eps = 1e-6f;
     __half* h16 = nullptr;
     float* y32 = nullptr;
+    // Clamp epilogues: the output bounds, the post-activation bounds (EPI_CLAMP_SILU) and an
+    // optional fp32 bias per output column.
+    float clamp_lo = -3.402823466e38f, clamp_hi = 3.402823466e38f;
+    float act_lo = -3.402823466e38f, act_hi = 3.402823466e38f;
+    const float* bias = nullptr;
 };
 cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream);
 // Kernel attributes (dynamic shared-memory limits) for the current device; call once per
@@ -211,6 +231,69 @@ cudaError_t launch_vision_qkv_norm_rope(const __half* qkv, int ntok, int rows, i
 // out[token_start + t] = fp16(rmsnorm(scale * sum of the token's merge x merge patch rows)).
 cudaError_t launch_pool_patches_norm(const float* x, const VisionImage* imgs, int nimg, int max_tokens, int d, int merge,
                                      float scale, float eps, __half* out, cudaStream_t stream);
+
+// ------------------------------------------------------------------ audio tower
+// One 30-second (or shorter, final) chunk of a clip in a packed audio batch: where its samples,
+// log-mel frames, first-convolution rows and token rows start, and how many there are.
+struct AudioChunk {
+    int64_t pcm_offset;
+    int32_t samples, frames, mel_row, t0, t0_row, tokens, token_row, pad;
+};
+// The front end's tables on the device (AudioFrontEnd.init): periodic Hann, twiddles and the
+// bit-reversal of the 512-point FFT, and per mel filter its band [lo, hi) of bins (whole groups
+// of four) with the offset of its weights in `w`.
+struct MelTables {
+    const float *hann, *cos_t, *sin_t, *w;
+    const int *bitrev, *band;  // band: lo[mel], hi[mel], off[mel]
+    int nw, mel;
+};
+cudaError_t launch_log_mel(const float* pcm, const AudioChunk* chunks, int nchunks, int frames_total,
+                           const MelTables& t, float* out, int num_sms, cudaStream_t stream);
+cudaError_t configure_audio_kernels();
+// First convolution (1 -> 128 channels, 3x3, stride 2) with LayerNorm and ReLU: out is
+// [conv0 rows][64][128] fp16.  w is [128][9] (kh * 3 + kw), nw [128].
+cudaError_t launch_audio_conv0(const float* mel, const AudioChunk* chunks, int nchunks, int t0_total, const float* w,
+                               const float* nw, float eps, __half* out, cudaStream_t stream);
+// The second convolution's patches: a [trows * 32][1152] fp16, K = (kh * 3 + kw) * 128 + c.
+cudaError_t launch_audio_im2col(const __half* c0, const AudioChunk* chunks, int nchunks, int tokens, int trows, __half* a,
+                                cudaStream_t stream);
+// LayerNorm over the 32 channels in columns [0, 32) of c1 ([trows * 32][128] fp32), weight,
+// ReLU, clamp; a2 is [trows][1024] fp16 (frequency * 32 + channel).
+cudaError_t launch_audio_subsample_norm(const float* c1, int trows, const float* nw, float eps, float lo, float hi,
+                                        __half* a2, cudaStream_t stream);
+// A row step of the Conformer on [rows][width]: optionally x += rmsnorm(branch) * branch_w (or
+// x += branch when branch_w is null), then x = rmsnorm(x) * final_w, x stored when store_x; then
+// h = rmsnorm(x) * next_w (next_norm 1; next_w null: no weight) or h = x (next_norm 0), written
+// to nout fp16 outputs each with its own clamp.
+struct AudioRowStep {
+    float* x = nullptr;
+    const __half* branch = nullptr;
+    const float* branch_w = nullptr;
+    const float* final_w = nullptr;
+    const float* next_w = nullptr;
+    int next_norm = 0, nout = 0, store_x = 0, rows = 0;
+    __half* out[3] = {nullptr, nullptr, nullptr};
+    float lo[3] = {0, 0, 0}, hi[3] = {0, 0, 0};
+    float eps = 1e-6f;
+};
+cudaError_t launch_audio_rows(const AudioRowStep& s, int width, cudaStream_t stream);
+// Local causal attention of the audio tower: q, k, v [rows][heads * 128] fp16 (clamped linear
+// outputs); scores (q * qscale) . (k * kscale + rel[t - j]) over j = max(chunk start, t - 11)
+// .. t, capped at softcap tanh(s / softcap); out clamped to [lo, hi] as fp16.
+struct AudioAttnLaunch {
+    const __half *q, *k, *v;
+    const float* rel;     // [13][heads * 128]
+    const float* qscale;  // [128]
+    float kscale, softcap, lo, hi;
+    const int* chunk_start;  // [rows]
+    int rows, heads, head_dim;
+    __half* out;
+};
+cudaError_t launch_audio_attention(const AudioAttnLaunch& a, cudaStream_t stream);
+// Causal depthwise conv (kernel 5, within each chunk), RMS norm with nw, SiLU, clamp: glu and
+// out are [rows][width] fp16, dw_t [5][width].
+cudaError_t launch_audio_dwconv(const __half* glu, const int* chunk_start, int rows, int width, const float* dw_t,
+                                const float* nw, float eps, float lo, float hi, __half* out, cudaStream_t stream);
 
 // Tensor-core attention for head dim 64 without a mask inside each sequence (the vision
 // tower's, Shaders/Attention.metal:190-312): q, k, v [rows][heads * 64] fp16, out the same.

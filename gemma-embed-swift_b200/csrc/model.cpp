@@ -314,7 +314,8 @@ static int load_device(ge_model* m, Device& d, const std::vector<HostWeight>& hw
     }
     if (c.has_output && (e = dev_upload(d.allocations, &d.output, output.data(), output.size())) != cudaSuccess) return fail(e);
     if ((e = noalloc_setup(d.ordinal)) != cudaSuccess) return fail(e);
-    if ((e = configure_gemm_kernels()) != cudaSuccess || (e = configure_attention_kernels()) != cudaSuccess)
+    if ((e = configure_gemm_kernels()) != cudaSuccess || (e = configure_attention_kernels()) != cudaSuccess ||
+        (e = configure_audio_kernels()) != cudaSuccess)
         return fail(e);
     return GE_OK;
 }
@@ -327,6 +328,7 @@ static void free_device(Device& d) {
     clear_graphs(d);
     free_workspace(d.ws);
     free_vision(d);
+    free_audio(d);
     for (void* p : d.allocations) cudaFree(p);
     d.allocations.clear();
     if (d.stream) cudaStreamDestroy(d.stream);

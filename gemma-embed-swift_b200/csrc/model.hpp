@@ -13,6 +13,7 @@
 #include "gemma_embed.h"
 #include "gguf.hpp"
 #include "kernels.hpp"
+#include "audio.hpp"
 #include "tokenizer.hpp"
 #include "vision.hpp"
 
@@ -107,6 +108,7 @@ struct Device {
     uint64_t graph_clock = 0;
     std::vector<void*> allocations;
     VisionDev vis;  // the image encoder's weights and workspace, when one is loaded
+    AudioDev aud;   // the audio encoder's weights and workspace, when one is loaded
 };
 
 }  // namespace ge
@@ -134,6 +136,12 @@ struct ge_model {
     ge::VisionConfig vcfg;
     int32_t image_begin = -1, image_end = -1;
     int patch_budget = 4096;  // ImageEmbedOptions.patchBudget unless the load options raise it
+    // The audio encoder (LoadOptions.audioEncoder) and the tokens that frame a clip's rows.
+    bool has_audio = false;
+    ge::GgufFile audio_file;
+    ge::AudioConfig acfg;
+    int32_t audio_begin = -1, audio_end = -1;
+    int64_t frame_budget = 96000;  // log-mel frames per audio batch
 };
 
 namespace ge {
@@ -195,6 +203,19 @@ struct VisionArgs {
     ProfileSink* profile = nullptr;  // time each kernel class instead of only running it
 };
 int run_vision(ge_model* m, Device& d, const VisionArgs& a);
+// The audio encoder: load (after the text model) and one forward over prepared clips, whose
+// projected rows land in d.aud.ws.vectors (clip i's rows after the earlier clips' rows).
+int load_audio(ge_model* m, const char* path);
+void free_audio(Device& d);
+struct AudioArgs {
+    const PreparedAudio* const* clips = nullptr;  // sample counts, and the host samples unless d_pcm is set
+    int n = 0;
+    const float* d_pcm = nullptr;   // device: samples at each clip's device_offset (skips the upload)
+    cudaStream_t stream = nullptr;  // nullptr: the device's own stream
+    std::string* error = nullptr;   // nullptr: the model's last_error
+    ProfileSink* profile = nullptr;  // time each kernel class instead of only running it
+};
+int run_audio(ge_model* m, Device& d, const AudioArgs& a);
 GraphEntry* find_graph(Device& d, const GraphKey& k);
 // The multi-GPU dispatcher's split of a packed batch: the sequence indices of each device,
 // longest first onto the least-loaded device (cost n + n^2 / 2048), each in original order.

@@ -319,6 +319,14 @@ __device__ __forceinline__ float gelu_quick_fast(float x) {
     return __fdividef(x, 1.0f + ex2_approx(x * k));
 }
 
+// x * sigmoid(x) and sigmoid(x) with the hardware exp2 and a fast divide.
+__device__ __forceinline__ float silu_fast(float x) {
+    return __fdividef(x, 1.0f + ex2_approx(x * -1.4426950408889634f));
+}
+__device__ __forceinline__ float sigmoid_fast(float x) {
+    return __fdividef(1.0f, 1.0f + ex2_approx(x * -1.4426950408889634f));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

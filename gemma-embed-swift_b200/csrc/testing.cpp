@@ -383,6 +383,57 @@ int ge_test_patchify(const uint8_t* rgb, int32_t w, int32_t h, int32_t patch, co
     return GE_OK;
 }
 
+int ge_test_log_mel(const float* samples, int64_t n, int32_t mel_bins, float* out, int32_t* frames) {
+    if (!samples || n < ge::kAudioMinimumSamples || n > ge::kAudioChunkSamples || mel_bins != 128 || !out || !frames)
+        return fail(GE_ERR_INVALID_OPTIONS, "invalid options");
+    float hann[512], sin_t[512], cos_t[512];
+    int bitrev[512];
+    std::vector<int> band;
+    std::vector<float> w;
+    ge::audio_front_tables(mel_bins, hann, sin_t, cos_t, bitrev, band, w);
+    const int nf = ge::audio_frame_count(n);
+    DevBuf dpcm, dch, dout, dh, dc, ds, dw, db, dband;
+    TRY(dpcm.alloc(size_t(n) * 4));
+    TRY(dch.alloc(sizeof(ge::AudioChunk)));
+    TRY(dout.alloc(size_t(nf) * mel_bins * 4));
+    TRY(dh.alloc(512 * 4));
+    TRY(dc.alloc(512 * 4));
+    TRY(ds.alloc(512 * 4));
+    TRY(db.alloc(512 * 4));
+    TRY(dw.alloc(w.size() * 4));
+    TRY(dband.alloc(band.size() * 4));
+    TRY(cudaMemcpy(dpcm.p, samples, size_t(n) * 4, cudaMemcpyHostToDevice));
+    ge::AudioChunk ch{};
+    ch.samples = int(n);
+    ch.frames = nf;
+    TRY(cudaMemcpy(dch.p, &ch, sizeof ch, cudaMemcpyHostToDevice));
+    TRY(cudaMemcpy(dh.p, hann, 512 * 4, cudaMemcpyHostToDevice));
+    TRY(cudaMemcpy(dc.p, cos_t, 512 * 4, cudaMemcpyHostToDevice));
+    TRY(cudaMemcpy(ds.p, sin_t, 512 * 4, cudaMemcpyHostToDevice));
+    TRY(cudaMemcpy(db.p, bitrev, 512 * 4, cudaMemcpyHostToDevice));
+    TRY(cudaMemcpy(dw.p, w.data(), w.size() * 4, cudaMemcpyHostToDevice));
+    TRY(cudaMemcpy(dband.p, band.data(), band.size() * 4, cudaMemcpyHostToDevice));
+    ge::MelTables t;
+    t.hann = static_cast<const float*>(dh.p);
+    t.cos_t = static_cast<const float*>(dc.p);
+    t.sin_t = static_cast<const float*>(ds.p);
+    t.w = static_cast<const float*>(dw.p);
+    t.bitrev = static_cast<const int*>(db.p);
+    t.band = static_cast<const int*>(dband.p);
+    t.nw = int(w.size());
+    t.mel = mel_bins;
+    int dev = 0, sms = 148;
+    TRY(cudaGetDevice(&dev));
+    TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    TRY(ge::configure_audio_kernels());
+    TRY(ge::launch_log_mel(static_cast<const float*>(dpcm.p), static_cast<const ge::AudioChunk*>(dch.p), 1, nf, t,
+                           static_cast<float*>(dout.p), sms, nullptr));
+    TRY(cudaDeviceSynchronize());
+    TRY(cudaMemcpy(out, dout.p, size_t(nf) * mel_bins * 4, cudaMemcpyDeviceToHost));
+    *frames = nf;
+    return GE_OK;
+}
+
 int ge_test_multimodal_sequence(const char* prefix, const int32_t* kinds, const char* const* texts, int32_t nparts,
                                 const int32_t* span_rows, int32_t max_tokens, int32_t bos, int32_t eos,
                                 int32_t image_begin, int32_t image_end, int32_t audio_begin, int32_t audio_end,

@@ -64,6 +64,13 @@ typedef struct ge_load_opts {
     /* Image patches per GPU batch when ge_image_opts.batch_size is 0; default 4096
      * (ImageEmbedOptions.patchBudget, EmbedOptions.swift:84-87), at least one image per batch. */
     int32_t image_patch_budget;
+    /* LoadOptions.audioEncoder: the mmproj GGUF whose gemma4a tower ge_embed_audios needs; NULL
+     * loads none (EmbedOptions.swift:188-191). */
+    const char* audio_encoder_path;
+    /* Log-mel frames per GPU batch when ge_audio_opts.batch_size is 0; default 96000 (16 minutes
+     * of audio; the reference's AudioEmbedOptions.frameBudget is 12000, sized for an Apple GPU),
+     * at least one clip per batch. */
+    int32_t audio_frame_budget;
 } ge_load_opts;
 
 #define GE_LOAD_NO_GRAPHS 1u      /* launch kernels directly instead of replaying captured CUDA graphs */
@@ -110,6 +117,13 @@ typedef struct ge_info {
     int32_t image_hidden_size;
     int32_t image_patch_size;
     int32_t image_projection_dim;
+    /* AudioEncoderInfo (AudioConfig.swift:5-19); all zero without an audio encoder. */
+    int32_t audio_layer_count;
+    int32_t audio_hidden_size;
+    int32_t audio_head_count;
+    int32_t audio_feed_forward_size;
+    int32_t audio_mel_bins;
+    int32_t audio_projection_dim;
 } ge_info;
 
 /* One kernel class of a profiling forward (ge_profile). */
@@ -310,6 +324,61 @@ GE_API int32_t ge_image_tokens(const ge_model* model, int32_t width, int32_t hei
  * rows); rows_per_image (count entries) receives each image's token count. */
 GE_API int ge_image_vectors(ge_model* model, const ge_image* images, int32_t count, int32_t max_image_tokens,
                             float* out, int64_t cap_rows, int32_t* rows_per_image);
+
+/* ---- Audio (AudioEmbedding.swift, Metal/AudioTower.swift) -------------------------------- */
+
+/* AudioInput.samples (Audio/AudioInput.swift:12): `count` PCM samples in -1 .. 1 at
+ * `sample_rate` Hz, `channels` interleaved.  The library takes 16 kHz mono; decoding files and
+ * downmixing or resampling to 16 kHz mono are the caller's (GE_ERR_AUDIO_DECODING otherwise). */
+typedef struct ge_audio {
+    const float* samples;
+    int64_t count;
+    int32_t sample_rate;
+    int32_t channels;
+} ge_audio;
+
+/* AudioEmbedOptions (EmbedOptions.swift:91-114). */
+typedef struct ge_audio_opts {
+    int32_t dimensions; /* 768, 512, 256 or 128 */
+    int32_t normalise;
+    int32_t max_tokens; /* rows per clip including the 4 frame rows; 0: ge_info.max_tokens */
+    int32_t batch_size; /* clips per batch; 0 packs by the load options' frame budget */
+} ge_audio_opts;
+
+GE_API void ge_audio_opts_default(ge_audio_opts* opts);
+
+/* AudioFrontEnd.tokenCount(samples:) (Audio/AudioPreprocessor.swift:86-95): the rows a clip of
+ * `samples` 16 kHz samples gives the text tower, before the 4 frame rows; 0 below 2 samples. */
+GE_API int64_t ge_audio_tokens(int64_t samples);
+
+/* EmbeddingModel.embed(audios:options:progress:) (AudioEmbedding.swift:17-33): each clip is cut
+ * into 30-second chunks, turned into log-mel frames and run through the audio tower on the GPU;
+ * its rows, framed as [bos, <|audio>, rows..., <audio|>, eos], go through the text tower and are
+ * finished like a text.  `out` receives count * dimensions floats; `token_counts` (may be NULL)
+ * the rows the text tower saw (clip tokens + 4).  A clip needing more than max_tokens rows is
+ * refused (GE_ERR_INVALID_OPTIONS; audio is never cut); GE_ERR_AUDIO_ENCODER_NOT_LOADED without
+ * an encoder.  Clips of a batch spread over the model's devices. */
+GE_API int ge_embed_audios(ge_model* model, const ge_audio* clips, int32_t count, const ge_audio_opts* opts, float* out,
+                           int32_t* token_counts, ge_progress_fn progress, void* user);
+
+/* The audio tower's projected rows of each clip, concatenated in order ([sum of rows]
+ * [projection_dim] floats, at most cap_rows rows); rows_per_clip (count entries) receives each
+ * clip's token count.  Runs on the first device. */
+GE_API int ge_audio_vectors(ge_model* model, const ge_audio* clips, int32_t count, float* out, int64_t cap_rows,
+                            int32_t* rows_per_clip);
+
+/* The audio forward (audio and text towers) over device-resident samples on the caller's
+ * stream, without synchronising: `d_pcm` holds the clips' 16 kHz samples back to back
+ * (clips[i].count each; clips[i].samples is ignored); d_pooled receives [count]
+ * [output_dimensions] pooled, unnormalised fp32 rows.  NULL stream: the legacy default stream. */
+GE_API int ge_audio_forward_device(ge_model* model, int32_t device_ordinal, const float* d_pcm, const ge_audio* clips,
+                                   int32_t count, float* d_pooled, void* stream);
+
+/* Profiler.profileAudio (Metal/Profiler.swift:202-295): on the first device, the whole audio
+ * forward ("audio_forward") and the audio tower alone ("audio_tower"), mean over `reps`, then
+ * each audio kernel class's first launch timed over `reps` back-to-back repetitions. */
+GE_API int ge_profile_audios(ge_model* model, const ge_audio* clips, int32_t count, int32_t reps, ge_kernel_time* out,
+                             int32_t cap, int32_t* count_out);
 
 /* ---- Mixed inputs (MultimodalEmbedding.swift) ---------------------------------------------- */
 

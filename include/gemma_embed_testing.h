@@ -83,6 +83,11 @@ GE_API int ge_test_multimodal_sequence(const char* prefix, const int32_t* kinds,
                                        int32_t audio_end, int32_t* ids, int32_t cap, int32_t* count,
                                        int32_t* truncated);
 
+/* AudioFrontEnd.logMel (Audio/AudioPreprocessor.swift:144-202) of one chunk of `n` 16 kHz
+ * samples (2 .. 480000) on the GPU: writes frame_count(n) rows of `mel_bins` (128) floats to
+ * `out` and the frame count to `frames`. */
+GE_API int ge_test_log_mel(const float* samples, int64_t n, int32_t mel_bins, float* out, int32_t* frames);
+
 GE_API const char* ge_test_last_error(void);
 
 #ifdef __cplusplus

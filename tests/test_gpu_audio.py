@@ -1,0 +1,213 @@
+"""The audio path on the GPU against the CPU oracle (MetalAudioForwardTests and
+AudioEmbeddingTests, Tests/GemmaEmbedTests/MetalAudioForwardTests.swift and
+AudioEmbeddingTests.swift): the log-mel front end bit for bit, the audio tower's projected rows
+at cosine > 0.99999 per row (MetalAudioForwardTests.swift:76), whole clip embeddings against the
+oracle's audio + text towers, clips that span two 30-second chunks, bit-identical results
+whatever the batch, and the API's refusals."""
+import ctypes
+from importlib import import_module
+
+import numpy as np
+import pytest
+
+from oracle import binding as B
+from oracle.tokenizer import Tokenizer as OracleTokenizer
+
+pytestmark = pytest.mark.gpu
+
+COSINE_MIN = 0.99999
+# The GPU-shaped audio encoder: head dim 128 as the real one, fewer and narrower layers.
+SMALL = dict(layers=2, hidden=512, heads=4, ff=1024)
+
+
+def cosine(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(a @ b / np.linalg.norm(a) / np.linalg.norm(b))
+
+
+def lib():
+    return import_module("gemma-embed-swift_b200._lib")
+
+
+def gpu_log_mel(samples):
+    s = np.ascontiguousarray(samples, np.float32)
+    frames = ctypes.c_int32(0)
+    out = np.zeros((B.frame_count(len(s)), 128), np.float32)
+    f32 = ctypes.POINTER(ctypes.c_float)
+    L = lib().lib()
+    rc = L.ge_test_log_mel(s.ctypes.data_as(f32), len(s), 128, out.ctypes.data_as(f32), ctypes.byref(frames))
+    assert rc == 0, L.ge_test_last_error()
+    assert frames.value == out.shape[0]
+    return out
+
+
+def signals():
+    rng = np.random.default_rng(7)
+    t = np.arange(24000) / 16000
+    return {
+        "sine": (0.5 * np.sin(2 * np.pi * 440 * t)).astype(np.float32),
+        "noise": rng.normal(0, 0.1, 16000).astype(np.float32),
+        "loud": rng.uniform(-1, 1, 7000).astype(np.float32),
+        "silence": np.zeros(3200, np.float32),
+        "two": np.array([0.3, -0.2], np.float32),
+        "odd": rng.normal(0, 0.2, 4801).astype(np.float32),
+        "chunk": rng.normal(0, 0.05, 480000).astype(np.float32),
+    }
+
+
+@pytest.mark.parametrize("name", list(signals()))
+def test_log_mel_bit_exact(cuda_device, name):
+    """k_log_mel equals AudioFrontEnd.logMel (oracle or_audio_log_mel) bit for bit: the same
+    butterflies in the same order with separately rounded operations, the same four-bin sums."""
+    s = signals()[name]
+    got = gpu_log_mel(s)
+    want = B.log_mel(s)
+    assert got.shape == want.shape
+    diff = got.view(np.int32).astype(np.int64) - want.view(np.int32).astype(np.int64)
+    # The last step is a double-precision log rounded to float: CUDA's and the host's log may
+    # differ in the double's last place, which reaches the float only at a rounding boundary.
+    assert np.abs(diff).max() <= 1, name
+    assert np.count_nonzero(diff) <= max(1, got.size // 100000), name
+
+
+# ------------------------------------------------------------------ the whole audio path
+@pytest.fixture(scope="module")
+def audio_model(ge, synth, cuda_device):
+    text = synth.model_path("gemma-embedding", seed=1, layers=6, vocab=4096)
+    enc = synth.audio_path(seed=4, **SMALL)
+    model = ge.EmbeddingModel.load(text, ge.LoadOptions(audio_encoder=enc))
+    aud = B.OracleAudio(enc)
+    ref = B.OracleModel(text)
+    yield model, aud, ref, OracleTokenizer.from_gguf(text)
+    model.close()
+    aud.close()
+    ref.close()
+
+
+def clips():
+    rng = np.random.default_rng(21)
+    t = np.arange(20000) / 16000
+    return [rng.normal(0, 0.1, 16000).astype(np.float32),             # 1 s: 25 rows
+            (0.4 * np.sin(2 * np.pi * 523 * t)).astype(np.float32),  # 1.25 s
+            rng.normal(0, 0.05, 4800).astype(np.float32),             # 0.3 s: 8 rows
+            rng.uniform(-0.5, 0.5, 3000).astype(np.float32)]
+
+
+def long_clip():
+    """35 s: a full 30-second chunk and a 5-second one (750 + 125 rows)."""
+    return np.random.default_rng(5).normal(0, 0.08, 560000).astype(np.float32)
+
+
+def test_audio_info(audio_model):
+    info = audio_model[0].info
+    assert (info.audio_layer_count, info.audio_hidden_size, info.audio_head_count, info.audio_feed_forward_size,
+            info.audio_mel_bins, info.audio_projection_dim) == (2, 512, 4, 1024, 128, 768)
+
+
+def test_audio_tower_rows_match_oracle(audio_model):
+    """MetalAudioForwardTests.testAudioTowerMatchesCPUReferenceAndLlamaCpp: every projected row
+    at cosine > 0.99999 against the CPU reference, chunk by chunk."""
+    model, aud, _, _ = audio_model
+    cs = clips() + [long_clip()]
+    got = model.audio_vectors(cs)
+    for c, rows in zip(cs, got):
+        want = aud.embed_rows(c)
+        assert rows.shape == want.shape, (len(c), rows.shape, want.shape)
+        worst = min(cosine(a, b) for a, b in zip(rows, want))
+        assert worst > COSINE_MIN, (len(c), worst)
+
+
+def test_audio_embeddings_match_oracle(ge, audio_model):
+    """The text tower over [bos, <|audio>, rows, <audio|>, eos] against the oracle's forward over
+    the oracle's rows."""
+    model, aud, ref, tok = audio_model
+    begin = tok.encode("<|audio>", False, True)
+    end = tok.encode("<audio|>", False, True)
+    assert len(begin) == 1 and len(end) == 1
+    cs = clips() + [long_clip()]
+    got = model.embed_audios(cs, ge.AudioEmbedOptions(normalise=False))
+    for c, e in zip(cs, got):
+        rows = aud.embed_rows(c)
+        T = rows.shape[0]
+        ids = np.array([2, begin[0]] + [-(r + 1) for r in range(T)] + [end[0], 1], np.int32)
+        want = ref.forward_rows(ids, rows)
+        assert e.token_count == T + 4 == B.audio_token_count(len(c)) + 4
+        assert cosine(e.vector, want) > COSINE_MIN
+
+
+def test_audio_batch_independence_bit_exact(ge, audio_model):
+    """A clip embeds the same alone, first or last in a batch, and one clip per batch or all
+    together, bit for bit."""
+    model = audio_model[0]
+    cs = clips()
+    alone = model.embed_audios([cs[1]])[0].vector
+    first = model.embed_audios([cs[1]] + cs[2:] + cs[:1])[0].vector
+    last = model.embed_audios(cs[2:] + cs[:1] + [cs[1]])[-1].vector
+    assert alone.tobytes() == first.tobytes() == last.tobytes()
+    one_at_a_time = model.embed_audios(cs, ge.AudioEmbedOptions(batch_size=1))
+    together = model.embed_audios(cs)
+    for a, b in zip(one_at_a_time, together):
+        assert a.vector.tobytes() == b.vector.tobytes()
+
+
+def test_audio_device_forward_matches_host_api(ge, audio_model):
+    """ge_audio_forward_device on device-resident samples gives the pooled rows of embed_audios."""
+    import torch
+    model = audio_model[0]
+    cs = clips()
+    host = model.embed_audios(cs, ge.AudioEmbedOptions(normalise=False))
+    pcm = torch.from_numpy(np.concatenate(cs)).cuda()
+    out = torch.zeros((len(cs), model.info.output_dimensions), dtype=torch.float32, device="cuda")
+    model.audio_forward_device(pcm.data_ptr(), [len(c) for c in cs], out.data_ptr(),
+                               stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    for e, row in zip(host, out.cpu().numpy()):
+        assert np.array_equal(e.vector, row)
+
+
+def test_audio_options_and_errors(ge, synth, audio_model):
+    model = audio_model[0]
+    c = clips()[0]
+    one = model.embed_audios(c, ge.AudioEmbedOptions(dimensions=256))
+    assert one.vector.shape == (256,) and abs(float(np.linalg.norm(one.vector)) - 1) < 1e-5
+    assert one.token_count == 25 + 4
+    assert model.embed_audios([], ge.AudioEmbedOptions()) == []
+    for bad in (ge.AudioEmbedOptions(dimensions=100), ge.AudioEmbedOptions(max_tokens=4),
+                ge.AudioEmbedOptions(max_tokens=model.info.max_tokens + 1), ge.AudioEmbedOptions(batch_size=0)):
+        with pytest.raises(ge.GemmaEmbedError) as e:
+            model.embed_audios([c], bad)
+        assert e.value.case == "invalidOptions"
+    # A clip needing more rows than max_tokens is refused, not cut (AudioEmbedding.swift:86-91).
+    with pytest.raises(ge.GemmaEmbedError) as e:
+        model.embed_audios([c], ge.AudioEmbedOptions(max_tokens=28))
+    assert e.value.case == "invalidOptions"
+    assert model.embed_audios([c], ge.AudioEmbedOptions(max_tokens=29))[0].token_count == 29
+    for bad_clip in (np.zeros(1, np.float32), np.zeros(0, np.float32), (c, 44100, 1), (np.repeat(c, 2), 16000, 2)):
+        with pytest.raises(ge.GemmaEmbedError) as e:
+            model.embed_audios([bad_clip])
+        assert e.value.case == "audioDecoding"
+    text_only = ge.EmbeddingModel.load(synth.model_path("gemma-embedding", seed=1, layers=6, vocab=4096))
+    try:
+        with pytest.raises(ge.GemmaEmbedError) as e:
+            text_only.embed_audios([c])
+        assert e.value.case == "audioEncoderNotLoaded"
+    finally:
+        text_only.close()
+
+
+def test_audio_encoder_load_refusals(ge, synth, cuda_device):
+    text = synth.model_path("gemma-embedding", seed=1, layers=6, vocab=4096)
+    # projects to 512, the text model is 768 wide (MetalForward.swift:90-92)
+    with pytest.raises(ge.GemmaEmbedError) as e:
+        ge.EmbeddingModel.load(text, ge.LoadOptions(audio_encoder=synth.audio_path(seed=4, projection_dim=512, **SMALL)))
+    assert e.value.case == "invalidGGUF"
+    # head dim 64: a shape the kernels are not built for
+    with pytest.raises(ge.GemmaEmbedError) as e:
+        ge.EmbeddingModel.load(text, ge.LoadOptions(audio_encoder=synth.audio_path(seed=4, layers=1, hidden=512,
+                                                                                     heads=8, ff=1024)))
+    assert e.value.case == "unsupportedArchitecture"
+    # an image-only mmproj has no audio encoder
+    with pytest.raises(ge.GemmaEmbedError) as e:
+        ge.EmbeddingModel.load(text, ge.LoadOptions(audio_encoder=synth.mmproj_path(seed=2, layers=2, positions=64)))
+    assert e.value.case == "invalidGGUF"
