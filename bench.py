@@ -18,6 +18,11 @@ inside the timed region) on seeded synthetic texts cut to the batch's lengths, a
 `tokenizer` compares the library's tokenizer with the oracle's restatement on one thread.
 `--impl reference` times the CPU oracle (the restated CPUReference.forward, the only
 runnable form of the reference's path here) on the host cores.
+
+`--config 4` runs BASELINE config 4 instead (32 synthetic 768x768 images per rank through the
+vision and text towers, images/s) and `--config 5` BASELINE config 5 (16 clips x 60 s of
+Gaussian-noise PCM per rank through the log-mel front end, the audio tower and the text tower,
+audio seconds per second), each with the same value / e2e / roofline / cpu_baseline keys.
 """
 from __future__ import annotations
 
@@ -173,8 +178,11 @@ def main():
         import torch.distributed as dist
         dist.init_process_group(backend="nccl" if a.impl == "ours" else "gloo",
                                 timeout=datetime.timedelta(seconds=300))
-    if a.config == 4:
-        rc = run_images_reference(a, rank, world) if a.impl == "reference" else run_images(a, rank, world, local)
+    if a.config in (4, 5):
+        if a.config == 4:
+            rc = run_images_reference(a, rank, world) if a.impl == "reference" else run_images(a, rank, world, local)
+        else:
+            rc = run_audios_reference(a, rank, world) if a.impl == "reference" else run_audios(a, rank, world, local)
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()
@@ -563,6 +571,188 @@ def run_images_reference(a, rank, world):
             "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     vis.close()
+    ref.close()
+    return 0
+
+
+CLIPS_PER_RANK = 16
+CLIP_SECONDS = 60.0
+
+
+def audio_oracle_step(aud, ref, tok, clip):
+    """One clip through the oracle: the log-mel front end, the audio tower chunk by chunk, the
+    text tower over [bos, <|audio>, rows, <audio|>, eos]."""
+    import numpy as np
+    rows = aud.embed_rows(clip)
+    begin = tok.encode("<|audio>", False, True)[0]
+    end = tok.encode("<audio|>", False, True)[0]
+    ids = [2, begin] + [-(r + 1) for r in range(rows.shape[0])] + [end, 1]
+    ref.forward_rows(np.array(ids, np.int32), rows)
+
+
+def audios_cpu_baseline(text_path, enc, clip):
+    from oracle import binding
+    from oracle.tokenizer import Tokenizer as OracleTokenizer
+    binding.set_threads(host_threads())
+    aud, ref = binding.OracleAudio(enc), binding.OracleModel(text_path)
+    tok = OracleTokenizer.from_gguf(text_path)
+    t0 = time.perf_counter()
+    audio_oracle_step(aud, ref, tok, clip)
+    dt = time.perf_counter() - t0
+    cores = binding.threads()
+    aud.close()
+    ref.close()
+    secs = len(clip) / 16000.0
+    return {"value": secs / dt, "unit": "audio s/s", "cores": cores, "kind": "port",
+            "sample": f"one {secs:.0f} s clip of the batch (2 chunks, 1500 rows), audio and text towers, {dt:.1f} s"}
+
+
+def run_audios(a, rank, world, local):
+    """16 clips x 60 s of Gaussian-noise PCM at 16 kHz per rank (two 30-second
+    chunks and 1500 rows each) through the log-mel front end, the audio tower (12 Conformer layers,
+    1024 wide) and the text tower; one step is the whole batch."""
+    import numpy as np
+    import torch
+    ge = importlib.import_module(PKG)
+    synth = importlib.import_module(PKG + ".synthetic")
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    if rank == 0:
+        text_path, enc = synth.model_path(a.arch, seed=0), synth.audio_path(seed=0)
+    barrier()
+    if rank != 0:
+        text_path, enc = synth.model_path(a.arch, seed=0), synth.audio_path(seed=0)
+    model = ge.EmbeddingModel.load(text_path, ge.LoadOptions(devices=(local,), batch_token_budget=BATCH_BUDGET,
+                                                            audio_encoder=enc, audio_frame_budget=1 << 22))
+    clips = synth.synthetic_pcm(CLIPS_PER_RANK, CLIP_SECONDS, seed=300 + rank)
+    n = len(clips)
+    counts = [len(c) for c in clips]
+    rows_per_clip = ge.audio_tokens(counts[0])
+    od = model.info.output_dimensions
+    d_pcm = torch.from_numpy(np.concatenate(clips)).cuda()
+    d_out = torch.empty((n, od), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+
+    def step_device():
+        model.audio_forward_device(d_pcm.data_ptr(), counts, d_out.data_ptr(), stream=stream.cuda_stream, device=local)
+
+    for _ in range(max(a.warmup, 3)):
+        step_device()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    time.sleep(0.3)
+    launches0 = model_launches(model)
+    barrier()
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(a.steps + 1)]
+    ev[0].record(stream)
+    for i in range(a.steps):
+        step_device()
+        ev[i + 1].record(stream)
+    torch.cuda.synchronize()
+    step_ms = sorted(ev[i].elapsed_time(ev[i + 1]) for i in range(a.steps))
+    barrier()
+    clock_info = clocks.stop()
+    launches = model_launches(model) - launches0
+    audio_s = sum(counts) / 16000.0
+    ms_max, s_sum = reduce_max_sum(dist, ev[0].elapsed_time(ev[-1]), audio_s * a.steps)
+    value = s_sum / (ms_max / 1000.0)
+    # ---- end to end: EmbeddingModel.embed(audios:) on host samples (upload, front end, both
+    # towers, 256-d normalised vectors back)
+    opts = ge.AudioEmbedOptions(dimensions=256)
+    for _ in range(2):
+        model.embed_audios(clips, opts)
+    barrier()
+    torch.cuda.synchronize()
+    info0 = model_info(model)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        model.embed_audios(clips, opts)
+    t1 = time.perf_counter()
+    barrier()
+    info1 = model_info(model)
+    e2e_ms, _ = reduce_max_sum(dist, (t1 - t0) * 1000.0, 0)
+    e2e = s_sum / (e2e_ms / 1000.0)
+    h2d = (info1.host_to_device_bytes - info0.host_to_device_bytes) // a.steps
+    d2h = (info1.device_to_host_bytes - info0.device_to_host_bytes) // a.steps
+    pk = peaks()
+    roofline, prof = None, []
+    if rank == 0:
+        prof = model.profile_audios(clips, reps=3)
+        kern = [p for p in prof if p["name"] not in ("audio_forward", "audio_tower")]
+        top = max(kern, key=lambda p: p["ms_per_launch"] * p["launches_per_forward"])
+        sec = top["ms_per_launch"] / 1000.0
+        tf = top["flops_per_launch"] / sec / 1e12
+        gbs = top["bytes_per_launch"] / sec / 1e9
+        tensor = tf / pk["bf16_tflops"] > gbs / pk["hbm_gbs"]
+        ach, peak, unit = (tf, pk["bf16_tflops"], "TFLOP/s") if tensor else (gbs, pk["hbm_gbs"], "GB/s")
+        tower_ms = sum(p["ms_per_launch"] * p["launches_per_forward"] for p in kern)
+        roofline = {"kernel": "audio " + top["name"], "bound": "tensor" if tensor else "hbm", "achieved": ach,
+                    "peak": peak, "unit": unit, "frac": ach / peak, "traffic": None, "peak_source": pk["source"],
+                    "share_of_audio_tower": top["ms_per_launch"] * top["launches_per_forward"] / tower_ms,
+                    "launches_per_forward": top["launches_per_forward"]}
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cpu = audios_cpu_baseline(text_path, enc, clips[0])
+    if rank == 0:
+        metric = "embedded audio seconds/sec (config 5: 16 clips x 60 s, 1500 rows each)"
+        line = {"metric": metric, "value": value, "unit": "audio s/s", "n_gpus": world, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": ms_max / a.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+                "config": {"workload": "config 5", "arch": a.arch + " + gemma4a (12 layers, 1024, 8 heads, FFN 4096)",
+                           "clips_per_rank": n, "seconds_per_clip": CLIP_SECONDS, "rows_per_clip": rows_per_clip,
+                           "text_rows_per_rank": (rows_per_clip + 4) * n, "parallelism": f"dp{world}",
+                           "l2": "working set larger than L2 (about 4 GB of activations per step)"},
+                "clips_per_s": value / CLIP_SECONDS, "latency_ms_p50": pct(step_ms, 50),
+                "latency_ms_p99": pct(step_ms, 99),
+                "e2e": {"value": e2e, "unit": "audio s/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                        "api": "ge_embed_audios (EmbeddingModel.embed(audios:)), 256-d normalised output"},
+                "gpu_launches": int(launches), "clocks": clock_info, "roofline": roofline, "cpu_baseline": cpu,
+                "kernels": [{k: (round(v, 5) if isinstance(v, float) else v) for k, v in p.items()} for p in prof]}
+        print(json.dumps(line), flush=True)
+    model.close()
+    return 0
+
+
+def run_audios_reference(a, rank, world):
+    """--impl reference --config 5: the oracle's audio path (its restated AudioFrontEnd,
+    CPUAudioReference and CPUReference) on the host cores, one 60-second clip per step."""
+    if rank != 0:
+        return 0
+    synth = importlib.import_module(PKG + ".synthetic")
+    from oracle import binding
+    from oracle.tokenizer import Tokenizer as OracleTokenizer
+    text_path, enc = synth.model_path(a.arch, seed=0), synth.audio_path(seed=0)
+    clips = synth.synthetic_pcm(max(a.steps + a.warmup, 1), CLIP_SECONDS, seed=300)
+    binding.set_threads(host_threads())
+    aud, ref = binding.OracleAudio(enc), binding.OracleModel(text_path)
+    tok = OracleTokenizer.from_gguf(text_path)
+    for i in range(a.warmup):
+        audio_oracle_step(aud, ref, tok, clips[i])
+    t0 = time.perf_counter()
+    for i in range(a.steps):
+        audio_oracle_step(aud, ref, tok, clips[a.warmup + i])
+    dt = time.perf_counter() - t0
+    value = a.steps * CLIP_SECONDS / dt
+    cores = binding.threads()
+    line = {"impl": "reference", "metric": "embedded audio seconds/sec (config 5: 16 clips x 60 s, 1500 rows each)",
+            "value": value, "unit": "audio s/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": dt * 1000 / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config 5", "arch": a.arch + " + gemma4a", "step": "one 60 s clip of the seeded batch"},
+            "cpu_baseline": {"value": value, "unit": "audio s/s", "cores": cores, "kind": "port",
+                             "sample": f"{a.steps} clips of 60 s, audio and text towers"},
+            "e2e": {"value": value, "unit": "audio s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    aud.close()
     ref.close()
     return 0
 
