@@ -577,8 +577,9 @@ class EmbeddingModel:
     def embed_multimodal(self, inputs, options: Optional[MultimodalEmbedOptions] = None,
                          progress: Optional[Callable[[EmbeddingProgress], Optional[bool]]] = None) -> list:
         """embed(_ inputs: [MultimodalInput], options:progress:) (MultimodalEmbedding.swift:100-206).
-        Each input is a list of parts in reading order: str (text) or a height x width x 3 uint8
-        array (an image)."""
+        Each input is a list of parts in reading order: str (text), a height x width x 3 uint8
+        array (an image), or a 1-D float32 array of 16 kHz mono samples or a (samples, rate,
+        channels) tuple (a clip)."""
         options = options or MultimodalEmbedOptions()
         if options.batch_size is not None and options.batch_size < 1:
             raise GemmaEmbedError(9, "invalid options: batchSize must be at least 1")
@@ -591,6 +592,11 @@ class EmbeddingModel:
                     data = part.encode() if isinstance(part, str) else bytes(part)
                     keep.append(data)
                     cp[k].kind, cp[k].text, cp[k].text_len = 0, data, len(data)
+                elif isinstance(part, tuple) or np.asarray(part).ndim == 1:
+                    c, arrs = _audios([part])
+                    arrays.append(arrs)
+                    cp[k].kind = 2
+                    cp[k].audio = c[0]
                 else:
                     c, arrs = _images([part])
                     arrays.append(arrs)

@@ -39,7 +39,8 @@ class GeImage(ctypes.Structure):
 
 
 class GePart(ctypes.Structure):
-    _fields_ = [("kind", ctypes.c_int32), ("text", ctypes.c_char_p), ("text_len", ctypes.c_int64), ("image", GeImage)]
+    _fields_ = [("kind", ctypes.c_int32), ("text", ctypes.c_char_p), ("text_len", ctypes.c_int64), ("image", GeImage),
+                ("audio", GeAudio)]
 
 
 class GeMultimodalInput(ctypes.Structure):

@@ -1274,24 +1274,34 @@ int ge_embed_multimodal(ge_model* m, const ge_multimodal_input* inputs, int32_t 
         return ge::set_error(m, GE_ERR_IMAGE_ENCODER_NOT_LOADED,
                              "no image encoder is loaded; pass the mmproj GGUF when loading the model");
     }
-    if (any_audio)
+    if (any_audio && !m->has_audio)
         return ge::set_error(m, GE_ERR_AUDIO_ENCODER_NOT_LOADED,
                              "no audio encoder is loaded; pass the mmproj GGUF as LoadOptions.audioEncoder when loading the model");
     if (count == 0) return GE_OK;
     if (!m->tokenizer)
         return ge::set_error(m, GE_ERR_UNSUPPORTED_ARCHITECTURE, "unsupported architecture: tokenizer model missing");
-    // Images of every input, in order, prepared on host threads.
+    // Images and clips of every input, in order, prepared on host threads.
     std::vector<ge_image> imgs;
-    std::vector<int32_t> first_image(static_cast<size_t>(count) + 1, 0);
+    std::vector<ge_audio> auds;
+    std::vector<int32_t> first_image(static_cast<size_t>(count) + 1, 0), first_clip(static_cast<size_t>(count) + 1, 0);
     for (int32_t i = 0; i < count; i++) {
         first_image[size_t(i)] = int32_t(imgs.size());
-        for (int32_t k = 0; k < inputs[i].count; k++)
+        first_clip[size_t(i)] = int32_t(auds.size());
+        for (int32_t k = 0; k < inputs[i].count; k++) {
             if (inputs[i].parts[k].kind == GE_PART_IMAGE) imgs.push_back(inputs[i].parts[k].image);
+            if (inputs[i].parts[k].kind == GE_PART_AUDIO) auds.push_back(inputs[i].parts[k].audio);
+        }
     }
     first_image[size_t(count)] = int32_t(imgs.size());
+    first_clip[size_t(count)] = int32_t(auds.size());
     std::vector<ge::PreparedImage> prepared;
     if (!imgs.empty()) {
         int rc = prepare_images(m, imgs.data(), int32_t(imgs.size()), o.max_image_tokens, prepared);
+        if (rc) return rc;
+    }
+    std::vector<ge::PreparedAudio> clips;
+    if (!auds.empty()) {
+        int rc = prepare_audios(m, auds.data(), int32_t(auds.size()), INT32_MAX, clips);
         if (rc) return rc;
     }
     // One sequence per input (MultimodalSequence, MultimodalEmbedding.swift:43-83).
@@ -1302,22 +1312,26 @@ int ge_embed_multimodal(ge_model* m, const ge_multimodal_input* inputs, int32_t 
     };
     const std::string pre = prefix ? std::string(prefix) : std::string();
     std::vector<std::vector<int32_t>> seqs(static_cast<size_t>(count));
-    std::vector<int64_t> costs(2 * static_cast<size_t>(count));
+    std::vector<int64_t> costs(3 * static_cast<size_t>(count));
     for (int32_t i = 0; i < count; i++) {
         std::vector<ge::SeqPart> parts;
         std::vector<ge::EncoderSpan> spans;
-        int32_t img = first_image[size_t(i)];
-        int64_t patches = 0;
+        int32_t img = first_image[size_t(i)], clip = first_clip[size_t(i)];
+        int64_t patches = 0, frames = 0;
         for (int32_t k = 0; k < inputs[i].count; k++) {
             const ge_part& p = inputs[i].parts[k];
             ge::SeqPart sp;
             sp.kind = p.kind;
             if (p.kind == GE_PART_TEXT) {
                 sp.text.assign(p.text ? p.text : "", size_t(p.text_len));
-            } else {
+            } else if (p.kind == GE_PART_IMAGE) {
                 const ge::PreparedImage& im = prepared[size_t(img++)];
                 spans.push_back({im.tokens(), m->image_begin, m->image_end});
                 patches += im.patches();
+            } else {
+                const ge::PreparedAudio& au = clips[size_t(clip++)];
+                spans.push_back({au.tokens(), m->audio_begin, m->audio_end});
+                frames += au.frames();
             }
             parts.push_back(std::move(sp));
         }
@@ -1328,28 +1342,39 @@ int ge_embed_multimodal(ge_model* m, const ge_multimodal_input* inputs, int32_t 
                                                                 std::to_string(o.max_tokens) + ") rows");
         if (token_counts) token_counts[i] = int32_t(seqs[size_t(i)].size());
         if (truncated) truncated[i] = cut ? 1 : 0;
-        costs[2 * size_t(i)] = int64_t(seqs[size_t(i)].size());
-        costs[2 * size_t(i) + 1] = patches;
+        costs[3 * size_t(i)] = int64_t(seqs[size_t(i)].size());
+        costs[3 * size_t(i) + 1] = patches;
+        costs[3 * size_t(i) + 2] = frames;
     }
-    const int64_t budgets[2] = {m->budget, m->patch_budget};
+    // The three budgets of MultimodalEmbedding.swift:143-145: tokens, image patches, audio frames.
+    const int64_t budgets[3] = {m->budget, m->patch_budget, m->frame_budget};
     std::vector<int32_t> ranges(2 * static_cast<size_t>(count));
     int32_t nr = 0;
-    ge_batches(costs.data(), count, 2, o.batch_size, budgets, ranges.data(), &nr);
+    ge_batches(costs.data(), count, 3, o.batch_size, budgets, ranges.data(), &nr);
     std::lock_guard<std::mutex> g(m->mu);
     ge::Device& d = m->devs[0];
-    const int od = c.out_dim;
+    const int od = c.out_dim, hidden = c.hidden;
     int32_t done = 0;
     int64_t done_tokens = 0;
     for (int32_t r = 0; r < nr; r++) {
         const int32_t b = ranges[2 * size_t(r)], e = ranges[2 * size_t(r) + 1];
-        // Image rows fill the vectors buffer from row 0, input after input (MultimodalEmbedding.swift:173-192).
+        // The towers over the batch's images and clips (MultimodalEmbedding.swift:173-192).
         std::vector<const ge::PreparedImage*> ims;
         for (int32_t i = first_image[size_t(b)]; i < first_image[size_t(e)]; i++) ims.push_back(&prepared[size_t(i)]);
+        std::vector<const ge::PreparedAudio*> cls;
+        for (int32_t i = first_clip[size_t(b)]; i < first_clip[size_t(e)]; i++) cls.push_back(&clips[size_t(i)]);
         if (!ims.empty()) {
             ge::VisionArgs va;
             va.imgs = ims.data();
             va.n = int(ims.size());
             const int rc = ge::run_vision(m, d, va);
+            if (rc) return rc;
+        }
+        if (!cls.empty()) {
+            ge::AudioArgs aa;
+            aa.clips = cls.data();
+            aa.n = int(cls.size());
+            const int rc = ge::run_audio(m, d, aa);
             if (rc) return rc;
         }
         std::vector<int32_t> toks;
@@ -1368,6 +1393,40 @@ int ge_embed_multimodal(ge_model* m, const ge_multimodal_input* inputs, int32_t 
             }
             row_base += rows;
         }
+        // With one kind of encoder the rows are already in sequence order in its output; with both,
+        // each span's rows are copied into one buffer in the order the sequences number them.
+        const float* vectors = nullptr;
+        if (!ims.empty() && cls.empty()) vectors = d.vis.ws.vectors;
+        if (ims.empty() && !cls.empty()) vectors = d.aud.ws.vectors;
+        if (!ims.empty() && !cls.empty()) {
+            const size_t need = size_t(std::max(row_base, 1)) * hidden;
+            cudaError_t ce = cudaSetDevice(d.ordinal);
+            if (ce == cudaSuccess && d.mm_vectors_cap < need) {
+                if (d.mm_vectors) cudaFree(d.mm_vectors);
+                d.mm_vectors = nullptr;
+                d.mm_vectors_cap = 0;
+                ce = cudaMalloc(&d.mm_vectors, need * sizeof(float));
+                if (ce == cudaSuccess) d.mm_vectors_cap = need;
+            }
+            size_t dst = 0, img_row = 0, clip_row = 0;
+            int32_t ii = first_image[size_t(b)], ci = first_clip[size_t(b)];
+            for (int32_t i = b; i < e && ce == cudaSuccess; i++)
+                for (int32_t k = 0; k < inputs[i].count && ce == cudaSuccess; k++) {
+                    const int kind = inputs[i].parts[k].kind;
+                    if (kind == GE_PART_TEXT) continue;
+                    const bool is_img = kind == GE_PART_IMAGE;
+                    const size_t n = is_img ? size_t(prepared[size_t(ii++)].tokens()) : size_t(clips[size_t(ci++)].tokens());
+                    const float* src = is_img ? d.vis.ws.vectors + img_row * hidden : d.aud.ws.vectors + clip_row * hidden;
+                    ce = cudaMemcpyAsync(d.mm_vectors + dst * hidden, src, n * hidden * sizeof(float),
+                                         cudaMemcpyDeviceToDevice, d.stream);
+                    (is_img ? img_row : clip_row) += n;
+                    dst += n;
+                }
+            if (ce != cudaSuccess)
+                return ge::set_error(m, ce == cudaErrorMemoryAllocation ? GE_ERR_OUT_OF_MEMORY : GE_ERR_GPU_FAILURE,
+                                     std::string("GPU execution failed: mixed rows: ") + cudaGetErrorString(ce));
+            vectors = d.mm_vectors;
+        }
         std::vector<float> pooled(size_t(e - b) * od);
         ge::ForwardArgs a;
         a.tokens = toks.data();
@@ -1375,7 +1434,7 @@ int ge_embed_multimodal(ge_model* m, const ge_multimodal_input* inputs, int32_t 
         a.seqs = sq.data();
         a.nseq = int(sq.size());
         a.out = pooled.data();
-        a.vectors = ims.empty() ? nullptr : d.vis.ws.vectors;
+        a.vectors = vectors;
         a.vector_rows = row_base;
         const int rc = ge::run_forward(m, d, a);
         if (rc) return rc;

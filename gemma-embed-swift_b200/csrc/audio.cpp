@@ -11,6 +11,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <thread>
 
 #include "model.hpp"
 #include "weights.hpp"
@@ -188,8 +189,9 @@ std::vector<float> vec_of(const GgufTensor* t) {
 
 void free_audio_workspace(AudioWorkspace& ws) {
     for (void* p : ws.allocations) cudaFree(p);
-    for (void* p : {(void*)ws.h_chunks, (void*)ws.h_cs})
+    for (void* p : {(void*)ws.h_chunks, (void*)ws.h_cs, (void*)ws.h_pcm})
         if (p) cudaFreeHost(p);
+    if (ws.pcm_copied) cudaEventDestroy(ws.pcm_copied);
     ws = AudioWorkspace();
 }
 
@@ -234,6 +236,8 @@ cudaError_t ensure_audio_workspace(const AudioConfig& c, Device& d, int trows, i
     A(&ws.vectors, r * size_t(c.projection_dim));
     if (err == cudaSuccess) err = cudaMallocHost(reinterpret_cast<void**>(&ws.h_chunks), size_t(C) * sizeof(AudioChunk));
     if (err == cudaSuccess) err = cudaMallocHost(reinterpret_cast<void**>(&ws.h_cs), r * sizeof(int));
+    if (err == cudaSuccess && P > 1) err = cudaMallocHost(reinterpret_cast<void**>(&ws.h_pcm), P * sizeof(float));
+    if (err == cudaSuccess) err = cudaEventCreateWithFlags(&ws.pcm_copied, cudaEventDisableTiming);
     if (err != cudaSuccess) {
         free_audio_workspace(ws);
         return err;
@@ -540,12 +544,27 @@ int run_audio(ge_model* m, Device& d, const AudioArgs& a) {
     for (int r = tokens; r < trows; r++) ws.h_cs[r] = r;
     cudaStream_t st = a.stream ? a.stream : d.stream;
     if (!a.d_pcm) {
-        int64_t off = 0;
-        for (int i = 0; i < a.n && e == cudaSuccess; i++) {
-            const PreparedAudio& p = *a.clips[i];
-            e = cudaMemcpyAsync(ws.pcm + off, p.samples, size_t(p.count) * 4, cudaMemcpyHostToDevice, st);
-            off += p.count;
-        }
+        // The clips are gathered into pinned memory on several host threads (the previous upload
+        // out of it has finished first), then copied to the device in one transfer.
+        if ((e = cudaEventSynchronize(ws.pcm_copied)) != cudaSuccess) return gpu_fail(e, "audio staging");
+        std::vector<int64_t> start(size_t(a.n) + 1, 0);
+        for (int i = 0; i < a.n; i++) start[size_t(i) + 1] = start[size_t(i)] + a.clips[i]->count;
+        const int64_t per = std::max<int64_t>(int64_t(1) << 18, (pcm + 7) / 8);
+        const int nt = int(std::min<int64_t>(8, (pcm + per - 1) / per));
+        auto gather = [&](int ti) {
+            const int64_t b = int64_t(ti) * per, end = std::min(pcm, b + per);
+            for (int i = 0; i < a.n; i++) {
+                const int64_t lo = std::max(b, start[size_t(i)]), hi = std::min(end, start[size_t(i) + 1]);
+                if (lo < hi)
+                    memcpy(ws.h_pcm + lo, a.clips[i]->samples + (lo - start[size_t(i)]), size_t(hi - lo) * sizeof(float));
+            }
+        };
+        std::vector<std::thread> th;
+        for (int ti = 1; ti < nt; ti++) th.emplace_back(gather, ti);
+        gather(0);
+        for (auto& x : th) x.join();
+        e = cudaMemcpyAsync(ws.pcm, ws.h_pcm, size_t(pcm) * 4, cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaEventRecord(ws.pcm_copied, st);
     }
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(ws.chunks, ws.h_chunks, size_t(nch) * sizeof(AudioChunk), cudaMemcpyHostToDevice, st);

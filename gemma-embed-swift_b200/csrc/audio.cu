@@ -49,10 +49,16 @@ __device__ __forceinline__ float clampf(float v, float lo, float hi) { return fm
 }  // namespace
 
 // ---------------------------------------------------------------------------- log-mel
-// One warp per frame: the windowed frame is written bit-reversed into the warp's buffer, nine
+// One warp per frame: the windowed frame is written bit-reversed into the warp's buffers, nine
 // in-place radix-2 levels follow with the reference's twiddles and operation order (separately
 // rounded multiplies and adds, no fused multiply-add), then the magnitudes and, per mel filter,
-// four-bin fp32 partial sums added into a double, floored at fp32(0.001) and logged.
+// four-bin fp32 partial sums added into a double, floored at fp32(0.001) and logged.  Real and
+// imaginary parts sit in separate arrays with one padding word per 32 elements, which keeps the
+// bit-reversed stores and the butterflies' strided accesses on distinct banks.
+__device__ __forceinline__ int fft_pad(int i) { return i + (i >> 5); }
+constexpr int kFftPadded = kFft + kFft / 32;
+constexpr int kLogMelWarpFloats = 2 * kFftPadded + 264;
+
 __global__ void __launch_bounds__(256) k_log_mel(const float* __restrict__ pcm, const AudioChunk* __restrict__ chunks,
                                                  int nchunks, int frames_total, MelTables t, float* __restrict__ out) {
     extern __shared__ float sm[];
@@ -64,8 +70,9 @@ __global__ void __launch_bounds__(256) k_log_mel(const float* __restrict__ pcm, 
     int* band = bitrev + kFft;  // lo[mel], hi[mel], off[mel]
     float* bufs = reinterpret_cast<float*>(band + 3 * t.mel);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* buf = bufs + warp * (2 * kFft + 264);
-    float* mag = buf + 2 * kFft;
+    float* re = bufs + warp * kLogMelWarpFloats;
+    float* im = re + kFftPadded;
+    float* mag = im + kFftPadded;
     for (int i = threadIdx.x; i < kFft; i += blockDim.x) {
         hann[i] = t.hann[i];
         cos_t[i] = t.cos_t[i];
@@ -84,9 +91,9 @@ __global__ void __launch_bounds__(256) k_log_mel(const float* __restrict__ pcm, 
         for (int j = lane; j < kFft; j += 32) {
             const int idx = fl * kHop + j - kPadLeft;
             const float x = (idx >= 0 && idx < ch.samples) ? s[idx] : 0.0f;
-            const int r = bitrev[j];
-            buf[2 * r] = __fmul_rn(hann[j], x);
-            buf[2 * r + 1] = 0.0f;
+            const int r = fft_pad(bitrev[j]);
+            re[r] = __fmul_rn(hann[j], x);
+            im[r] = 0.0f;
         }
         __syncwarp();
 #pragma unroll 1
@@ -95,19 +102,22 @@ __global__ void __launch_bounds__(256) k_log_mel(const float* __restrict__ pcm, 
 #pragma unroll 4
             for (int b = lane; b < kFft / 2; b += 32) {
                 const int k = b & (half - 1);
-                const int ev = 2 * ((b >> lg) * count + k), od = ev + 2 * half;
-                const float re = cos_t[k * step], im = -sin_t[k * step];
-                const float ro = buf[od], io = buf[od + 1], er = buf[ev], ei = buf[ev + 1];
-                const float a = __fmul_rn(re, ro), bq = __fmul_rn(im, io), c = __fmul_rn(re, io), d = __fmul_rn(im, ro);
-                buf[ev] = __fsub_rn(__fadd_rn(er, a), bq);
-                buf[ev + 1] = __fadd_rn(__fadd_rn(ei, c), d);
-                buf[od] = __fadd_rn(__fsub_rn(er, a), bq);
-                buf[od + 1] = __fsub_rn(__fsub_rn(ei, c), d);
+                const int e = (b >> lg) * count + k;
+                const int ev = fft_pad(e), od = fft_pad(e + half);
+                const float c = cos_t[k * step], sn = -sin_t[k * step];
+                const float ro = re[od], io = im[od], er = re[ev], ei = im[ev];
+                const float a = __fmul_rn(c, ro), bq = __fmul_rn(sn, io), cq = __fmul_rn(c, io), d = __fmul_rn(sn, ro);
+                re[ev] = __fsub_rn(__fadd_rn(er, a), bq);
+                im[ev] = __fadd_rn(__fadd_rn(ei, cq), d);
+                re[od] = __fadd_rn(__fsub_rn(er, a), bq);
+                im[od] = __fsub_rn(__fsub_rn(ei, cq), d);
             }
             __syncwarp();
         }
-        for (int j = lane; j < kBins; j += 32)
-            mag[j] = __fsqrt_rn(__fadd_rn(__fmul_rn(buf[2 * j], buf[2 * j]), __fmul_rn(buf[2 * j + 1], buf[2 * j + 1])));
+        for (int j = lane; j < kBins; j += 32) {
+            const float x = re[fft_pad(j)], y = im[fft_pad(j)];
+            mag[j] = __fsqrt_rn(__fadd_rn(__fmul_rn(x, x), __fmul_rn(y, y)));
+        }
         __syncwarp();
         for (int m = lane; m < t.mel; m += 32) {
             const int lo = band[m], hi = band[t.mel + m];
@@ -130,7 +140,7 @@ __global__ void __launch_bounds__(256) k_log_mel(const float* __restrict__ pcm, 
 }
 
 size_t log_mel_smem(const MelTables& t) {
-    return size_t(3 * kFft + t.nw) * 4 + size_t(kFft + 3 * t.mel) * 4 + size_t(8) * (2 * kFft + 264) * 4;
+    return size_t(3 * kFft + t.nw) * 4 + size_t(kFft + 3 * t.mel) * 4 + size_t(8) * kLogMelWarpFloats * 4;
 }
 
 cudaError_t launch_log_mel(const float* pcm, const AudioChunk* chunks, int nchunks, int frames_total,
@@ -145,52 +155,58 @@ cudaError_t launch_log_mel(const float* pcm, const AudioChunk* chunks, int nchun
 
 cudaError_t configure_audio_kernels() {
     // The largest table set the launcher accepts: 128 filters of at most 257 weights each.
-    const size_t most = size_t(3 * kFft + kMel * kBins) * 4 + size_t(kFft + 3 * kMel) * 4 + size_t(8) * (2 * kFft + 264) * 4;
+    const size_t most = size_t(3 * kFft + kMel * kBins) * 4 + size_t(kFft + 3 * kMel) * 4 + size_t(8) * kLogMelWarpFloats * 4;
     return cudaFuncSetAttribute(k_log_mel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(std::min<size_t>(most, 227 * 1024)));
 }
 
 // ---------------------------------------------------------------------------- subsampling
-// One block per conv0 output time row; warp w computes frequencies 8w..8w+7, lane l channels
-// 4l..4l+3.  The three mel rows it reads are staged fp16-rounded (ggml's im2col runs in fp16).
+// One warp per conv0 output time row (8 per block); lane l computes channels 4l..4l+3 with their
+// 36 taps in registers, for the 64 output frequencies in turn.  The three mel rows a warp reads
+// are staged fp16-rounded (ggml's im2col runs in fp16).
 __global__ void __launch_bounds__(256) k_audio_conv0(const float* __restrict__ mel, const AudioChunk* __restrict__ chunks,
-                                                     int nchunks, const float* __restrict__ w, const float* __restrict__ nw,
-                                                     float eps, __half* __restrict__ out) {
-    __shared__ float in[3][kMel];
-    __shared__ float ws[kC0 * 9];
-    __shared__ float ns[kC0];
-    const int r0 = blockIdx.x;
-    for (int i = threadIdx.x; i < kC0 * 9; i += 256) ws[i] = w[i];
-    if (threadIdx.x < kC0) ns[threadIdx.x] = nw[threadIdx.x];
+                                                     int nchunks, int t0_total, const float* __restrict__ w,
+                                                     const float* __restrict__ nw, float eps, __half* __restrict__ out) {
+    __shared__ float in[8][3][kMel];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float wr[4][9], ns[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        ns[j] = nw[4 * lane + j];
+#pragma unroll
+        for (int k = 0; k < 9; k++) wr[j][k] = w[(4 * lane + j) * 9 + k];
+    }
     pdl_wait();
     pdl_launch_if_one_wave();
+    const int r0 = blockIdx.x * 8 + warp;
+    if (r0 >= t0_total) return;
     const AudioChunk ch = chunks[chunk_of<&AudioChunk::t0_row>(chunks, nchunks, r0)];
     const int ot = r0 - ch.t0_row;
-    for (int i = threadIdx.x; i < 3 * kMel; i += 256) {
+    float(*x3)[kMel] = in[warp];
+    for (int i = lane; i < 3 * kMel; i += 32) {
         const int kh = i / kMel, fq = i % kMel, tt = 2 * ot + kh - 1;
         const float v = (tt >= 0 && tt < ch.frames) ? mel[size_t(ch.mel_row + tt) * kMel + fq] : 0.0f;
-        in[kh][fq] = __half2float(__float2half_rn(v));
+        x3[kh][fq] = __half2float(__float2half_rn(v));
     }
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int of = warp * 8; of < warp * 8 + 8; of++) {
+    __syncwarp();
+    __half* dst = out + size_t(r0) * kF0 * kC0 + 4 * lane;
+#pragma unroll 2
+    for (int of = 0; of < kF0; of++) {
         float x[9];
 #pragma unroll
         for (int kh = 0; kh < 3; kh++)
 #pragma unroll
             for (int kw = 0; kw < 3; kw++) {
                 const int fq = 2 * of + kw - 1;
-                x[kh * 3 + kw] = (fq >= 0 && fq < kMel) ? in[kh][fq] : 0.0f;
+                x[kh * 3 + kw] = fq >= 0 ? x3[kh][fq] : 0.0f;  // fq < 128 always
             }
-        float c[4];
-        float sum = 0.f;
+        float c[4], sum = 0.f;
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            const float* wr = ws + (4 * lane + j) * 9;
-            float a = 0.f;
+            float acc = 0.f;
 #pragma unroll
-            for (int k = 0; k < 9; k++) a += wr[k] * x[k];
-            c[j] = a;
-            sum += a;
+            for (int k = 0; k < 9; k++) acc += wr[j][k] * x[k];
+            c[j] = acc;
+            sum += acc;
         }
         const float mean = warp_sum(sum) / float(kC0);
         float var = 0.f;
@@ -199,16 +215,17 @@ __global__ void __launch_bounds__(256) k_audio_conv0(const float* __restrict__ m
         var = warp_sum(var) / float(kC0);
         const float scale = 1.0f / sqrtf(var + eps);
         uint2 o;
-        o.x = pack_half2(fmaxf(0.f, (c[0] - mean) * scale * ns[4 * lane]), fmaxf(0.f, (c[1] - mean) * scale * ns[4 * lane + 1]));
-        o.y = pack_half2(fmaxf(0.f, (c[2] - mean) * scale * ns[4 * lane + 2]), fmaxf(0.f, (c[3] - mean) * scale * ns[4 * lane + 3]));
-        *reinterpret_cast<uint2*>(out + (size_t(r0) * kF0 + of) * kC0 + 4 * lane) = o;
+        o.x = pack_half2(fmaxf(0.f, (c[0] - mean) * scale * ns[0]), fmaxf(0.f, (c[1] - mean) * scale * ns[1]));
+        o.y = pack_half2(fmaxf(0.f, (c[2] - mean) * scale * ns[2]), fmaxf(0.f, (c[3] - mean) * scale * ns[3]));
+        *reinterpret_cast<uint2*>(dst + of * kC0) = o;
     }
 }
 
 cudaError_t launch_audio_conv0(const float* mel, const AudioChunk* chunks, int nchunks, int t0_total, const float* w,
                                const float* nw, float eps, __half* out, cudaStream_t stream) {
     if (t0_total <= 0) return cudaSuccess;
-    CK_LAUNCH(launch_kernel(k_audio_conv0, dim3(t0_total), dim3(256), 0, stream, 1, mel, chunks, nchunks, w, nw, eps, out));
+    CK_LAUNCH(launch_kernel(k_audio_conv0, dim3((t0_total + 7) / 8), dim3(256), 0, stream, 1, mel, chunks, nchunks,
+                            t0_total, w, nw, eps, out));
     return cudaGetLastError();
 }
 
@@ -378,7 +395,9 @@ cudaError_t launch_audio_rows(const AudioRowStep& s, int width, cudaStream_t str
 // ---------------------------------------------------------------------------- attention
 // Block: 32 query rows of one head (8 warps x 4 rows).  Keys and values of rows r0 - 11 ..
 // r0 + 31 are staged as fp16; query row t reads keys max(chunk start, t - 11) .. t.  Lane l holds
-// head dims 4l .. 4l + 3.  The score is kscale (q' . k) + q' . rel[t - j] with q' the scaled query.
+// head dims 4l .. 4l + 3 and sums its part of every key's score; one reduce-scatter leaves key m's
+// score on lanes 2m and 2m + 1, which apply the soft cap and the exponent.  The score is
+// q' . (kscale k + rel[t - j]) with q' the scaled query.
 constexpr int kAttnRows = 32, kAttnWin = 12, kAttnHd = 128;
 __global__ void __launch_bounds__(256) k_audio_attention(AudioAttnLaunch a) {
     __shared__ __align__(16) __half ks[kAttnRows + kAttnWin - 1][kAttnHd];
@@ -411,49 +430,60 @@ __global__ void __launch_bounds__(256) k_audio_attention(AudioAttnLaunch a) {
         const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
         return make_float4(lo.x, lo.y, hi.x, hi.y);
     };
+    const int idx = lane >> 1;  // the key whose score this lane holds after the reduce-scatter
+    // The four rows of a warp are independent; unrolled, their shuffle chains overlap.
+#pragma unroll
     for (int i = 0; i < kAttnRows / 8; i++) {
         const int t = r0 + warp * (kAttnRows / 8) + i;
-        if (t >= a.rows) break;
+        if (t >= a.rows) continue;
         const float4 qv = ld4(a.q + size_t(t) * W + h * kAttnHd + 4 * lane);
         const float q0 = qv.x * qs.x, q1 = qv.y * qs.y, q2 = qv.z * qs.z, q3 = qv.w * qs.w;
-        const int cs = a.chunk_start[t];
-        const int first = max(cs, t - (kAttnWin - 1));
+        const int first = max(a.chunk_start[t], t - (kAttnWin - 1));
         const int n = t - first + 1;  // keys, oldest first: j = first + m
-        float sc[kAttnWin];
-        float mx = -FLT_MAX;
+        // Partial scores over this lane's 4 dims: q' . (k kscale + rel[t - j]).
+        float v[16];
+#pragma unroll
+        for (int m = 0; m < 16; m++) v[m] = 0.f;
 #pragma unroll
         for (int m = 0; m < kAttnWin; m++) {
             if (m < n) {
-                const int j = first + m, dist = t - j;
+                const int j = first + m;
                 const float4 kk = ld4(&ks[j - base][4 * lane]);
-                const float4 rr = *reinterpret_cast<const float4*>(&rel[dist][4 * lane]);
-                float part = q0 * kk.x + q1 * kk.y + q2 * kk.z + q3 * kk.w;
-                float pr = q0 * rr.x + q1 * rr.y + q2 * rr.z + q3 * rr.w;
-                part = warp_sum(part);
-                pr = warp_sum(pr);
-                const float c = a.softcap * tanhf((part * a.kscale + pr) / a.softcap);
-                sc[m] = c;
-                mx = fmaxf(mx, c);
+                const float4 rr = *reinterpret_cast<const float4*>(&rel[t - j][4 * lane]);
+                v[m] = q0 * fmaf(kk.x, a.kscale, rr.x) + q1 * fmaf(kk.y, a.kscale, rr.y) +
+                       q2 * fmaf(kk.z, a.kscale, rr.z) + q3 * fmaf(kk.w, a.kscale, rr.w);
             }
         }
-        float sum = 0.f;
+        // Reduce-scatter of the 16 partial sums over the warp: lanes 2m and 2m + 1 end with key m's score.
 #pragma unroll
-        for (int m = 0; m < kAttnWin; m++)
-            if (m < n) {
-                sc[m] = expf(sc[m] - mx);
-                sum += sc[m];
+        for (int o = 16, cnt = 8; o >= 2; o >>= 1, cnt >>= 1) {
+            const bool upper = lane & o;
+#pragma unroll
+            for (int k = 0; k < cnt; k++) {
+                const float send = upper ? v[k] : v[k + cnt];
+                const float keep = upper ? v[k + cnt] : v[k];
+                v[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
             }
+        }
+        const float sfull = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+        const bool valid = idx < n;
+        const float c = valid ? a.softcap * tanhf(sfull / a.softcap) : -FLT_MAX;
+        const float mx = warp_max(c);
+        const float e = valid ? expf(c - mx) : 0.f;
+        const float sum = warp_sum((lane & 1) ? 0.f : e);
+        const float p = e / sum;
         float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
 #pragma unroll
-        for (int m = 0; m < kAttnWin; m++)
+        for (int m = 0; m < kAttnWin; m++) {
+            const float pm = __shfl_sync(0xffffffffu, p, 2 * m);
             if (m < n) {
-                const float p = sc[m] / sum;
                 const float4 vv = ld4(&vs[first + m - base][4 * lane]);
-                o0 += p * vv.x;
-                o1 += p * vv.y;
-                o2 += p * vv.z;
-                o3 += p * vv.w;
+                o0 += pm * vv.x;
+                o1 += pm * vv.y;
+                o2 += pm * vv.z;
+                o3 += pm * vv.w;
             }
+        }
         uint2 o;
         o.x = pack_half2(clampf(o0, a.lo, a.hi), clampf(o1, a.lo, a.hi));
         o.y = pack_half2(clampf(o2, a.lo, a.hi), clampf(o3, a.lo, a.hi));
@@ -469,69 +499,102 @@ cudaError_t launch_audio_attention(const AudioAttnLaunch& a, cudaStream_t stream
 }
 
 // ---------------------------------------------------------------------------- depthwise conv
-// One warp per row; lane l holds channels (32 i + l) * 8 + [0, 8).  dw_t is [5][W] (tap-major),
-// tap 4 on the current row; rows before the chunk's first row contribute nothing.
+// A block computes R consecutive rows; thread i owns channels C i .. C i + C - 1 (C = W / 256)
+// with their 5 taps in registers.  The R + 4 source rows are loaded once into registers and each
+// is added into every output row within reach (tap 4 on the current row; rows before the output
+// row's chunk start contribute nothing).  The RMS norms of the R rows share one block reduction.  dw_t is [5][W] (tap-major).
+template <int C>
+__device__ __forceinline__ void load_halves(const __half* p, float* v) {
+    if constexpr (C == 4) {
+        const uint2 u = *reinterpret_cast<const uint2*>(p);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+        v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
+    } else if constexpr (C == 8) {
+        const uint4 u = *reinterpret_cast<const uint4*>(p);
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float2 f = __half22float2(h[e]);
+            v[2 * e] = f.x, v[2 * e + 1] = f.y;
+        }
+    } else if constexpr (C == 2) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(p));
+        v[0] = f.x, v[1] = f.y;
+    } else {
+#pragma unroll
+        for (int e = 0; e < C; e++) v[e] = __half2float(p[e]);
+    }
+}
+
 template <int W>
 __global__ void __launch_bounds__(256) k_audio_dwconv(const __half* __restrict__ glu, const int* __restrict__ chunk_start,
                                                       int rows, const float* __restrict__ dw_t, const float* __restrict__ nw,
                                                       float eps, float lo, float hi, __half* __restrict__ out) {
-    constexpr int G = W / 256;  // groups of 8 channels per lane
+    constexpr int C = W / 256, R = C > 4 ? 4 : 8;
+    __shared__ float red[R][8];
+    const int c0 = threadIdx.x * C, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float w[5][C], nv[C];
+#pragma unroll
+    for (int e = 0; e < C; e++) {
+        nv[e] = nw[c0 + e];
+#pragma unroll
+        for (int k = 0; k < 5; k++) w[k][e] = dw_t[k * W + c0 + e];
+    }
     pdl_wait();
     pdl_launch_if_one_wave();
-    const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (t >= rows) return;
-    const int cs = chunk_start[t];
-    float acc[G][8];
+    const int r0 = blockIdx.x * R;
+    int cs[R];
 #pragma unroll
-    for (int i = 0; i < G; i++)
+    for (int rr = 0; rr < R; rr++) cs[rr] = r0 + rr < rows ? chunk_start[r0 + rr] : r0 + rr;
+    // Every source row first (clamped into the buffer, so all loads issue together), then the taps.
+    float x[R + 4][C];
 #pragma unroll
-        for (int e = 0; e < 8; e++) acc[i][e] = 0.f;
+    for (int si = 0; si < R + 4; si++) {
+        const int src = min(max(r0 - 4 + si, 0), rows - 1);
+        load_halves<C>(glu + size_t(src) * W + c0, x[si]);
+    }
+    float acc[R][C];
 #pragma unroll
-    for (int k = 0; k < 5; k++) {
-        const int src = t + k - 4;
-        if (src < cs) continue;
+    for (int rr = 0; rr < R; rr++) {
 #pragma unroll
-        for (int i = 0; i < G; i++) {
-            const int c = (i * 32 + lane) * 8;
-            const uint4 u = *reinterpret_cast<const uint4*>(glu + size_t(src) * W + c);
-            const __half2* hv = reinterpret_cast<const __half2*>(&u);
-            const float4 w0 = *reinterpret_cast<const float4*>(dw_t + k * W + c);
-            const float4 w1 = *reinterpret_cast<const float4*>(dw_t + k * W + c + 4);
-            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        for (int e = 0; e < C; e++) acc[rr][e] = 0.f;
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const float2 f = __half22float2(hv[e]);
-                acc[i][2 * e] += f.x * wv[2 * e];
-                acc[i][2 * e + 1] += f.y * wv[2 * e + 1];
-            }
+        for (int k = 0; k < 5; k++) {
+            const int src = r0 + rr + k - 4;  // source row si = rr + k
+            if (src < cs[rr] || src < 0) continue;
+#pragma unroll
+            for (int e = 0; e < C; e++) acc[rr][e] += x[rr + k][e] * w[k][e];
         }
     }
-    float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < G; i++)
+    for (int rr = 0; rr < R; rr++) {
+        float ss = 0.f;
 #pragma unroll
-        for (int e = 0; e < 8; e++) ss += acc[i][e] * acc[i][e];
-    ss = warp_sum(ss);
-    const float inv = 1.0f / sqrtf(ss / float(W) + eps);
+        for (int e = 0; e < C; e++) ss += acc[rr][e] * acc[rr][e];
+        ss = warp_sum(ss);
+        if (lane == 0) red[rr][warp] = ss;
+    }
+    __syncthreads();
 #pragma unroll
-    for (int i = 0; i < G; i++) {
-        const int c = (i * 32 + lane) * 8;
-        uint32_t pk[4];
+    for (int rr = 0; rr < R; rr++) {
+        const int t = r0 + rr;
+        if (t >= rows) break;
+        float ss = 0.f;
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-            float y0 = acc[i][2 * e] * inv * nw[c + 2 * e], y1 = acc[i][2 * e + 1] * inv * nw[c + 2 * e + 1];
-            y0 = y0 / (1.0f + expf(-y0));
-            y1 = y1 / (1.0f + expf(-y1));
-            pk[e] = pack_half2(clampf(y0, lo, hi), clampf(y1, lo, hi));
-        }
-        *reinterpret_cast<uint4*>(out + size_t(t) * W + c) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        for (int k = 0; k < 8; k++) ss += red[rr][k];
+        const float inv = 1.0f / sqrtf(ss / float(W) + eps);
+        __half* dst = out + size_t(t) * W + c0;
+#pragma unroll
+        for (int e = 0; e < C; e++) dst[e] = __float2half_rn(clampf(silu_fast(acc[rr][e] * inv * nv[e]), lo, hi));
     }
 }
 
 cudaError_t launch_audio_dwconv(const __half* glu, const int* chunk_start, int rows, int width, const float* dw_t,
                                 const float* nw, float eps, float lo, float hi, __half* out, cudaStream_t stream) {
     if (rows <= 0) return cudaSuccess;
-    const dim3 grid((rows + 7) / 8);
+    const int r = width / 256 > 4 ? 4 : 8;
+    const dim3 grid((rows + r - 1) / r);
     switch (width) {
     case 512: CK_LAUNCH(launch_kernel(k_audio_dwconv<512>, grid, dim3(256), 0, stream, 1, glu, chunk_start, rows, dw_t, nw, eps, lo, hi, out)); break;
     case 768: CK_LAUNCH(launch_kernel(k_audio_dwconv<768>, grid, dim3(256), 0, stream, 1, glu, chunk_start, rows, dw_t, nw, eps, lo, hi, out)); break;

@@ -329,6 +329,9 @@ static void free_device(Device& d) {
     free_workspace(d.ws);
     free_vision(d);
     free_audio(d);
+    if (d.mm_vectors) cudaFree(d.mm_vectors);
+    d.mm_vectors = nullptr;
+    d.mm_vectors_cap = 0;
     for (void* p : d.allocations) cudaFree(p);
     d.allocations.clear();
     if (d.stream) cudaStreamDestroy(d.stream);

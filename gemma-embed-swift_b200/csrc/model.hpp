@@ -109,6 +109,9 @@ struct Device {
     std::vector<void*> allocations;
     VisionDev vis;  // the image encoder's weights and workspace, when one is loaded
     AudioDev aud;   // the audio encoder's weights and workspace, when one is loaded
+    // Mixed inputs with both images and clips: their rows gathered in sequence order.
+    float* mm_vectors = nullptr;
+    size_t mm_vectors_cap = 0;  // floats
 };
 
 }  // namespace ge

@@ -390,6 +390,7 @@ typedef struct ge_part {
     const char* text;  /* GE_PART_TEXT: text_len bytes of UTF-8 */
     int64_t text_len;
     ge_image image;    /* GE_PART_IMAGE: decoded pixels */
+    ge_audio audio;    /* GE_PART_AUDIO: 16 kHz mono samples */
 } ge_part;
 
 /* MultimodalInput (MultimodalEmbedding.swift:5-24): text, images and clips in reading order. */
@@ -404,7 +405,7 @@ typedef struct ge_multimodal_opts {
     int32_t dimensions;
     int32_t normalise;
     int32_t max_image_tokens; /* default 256 */
-    int32_t batch_size;       /* inputs per batch; 0 packs by the token and patch budgets */
+    int32_t batch_size;       /* inputs per batch; 0 packs by the token, patch and frame budgets */
 } ge_multimodal_opts;
 
 GE_API void ge_multimodal_opts_default(ge_multimodal_opts* opts);
@@ -412,11 +413,12 @@ GE_API void ge_multimodal_opts_default(ge_multimodal_opts* opts);
 /* EmbeddingModel.embed(_ inputs: [MultimodalInput], options:progress:)
  * (MultimodalEmbedding.swift:100-206): each input becomes one text-tower sequence,
  * [bos] tok(prefix + text) [<|image>] rows... [<image|>] tok(text) ... [eos] with its images'
- * rows from the vision tower, text cut from the end when it does not fit max_tokens; then
- * finish.  `prefix` (NUL-terminated, NULL for none) is the task prefix.  `token_counts` and
+ * rows from the vision tower and its clips' [<|audio>] rows... [<audio|>] from the audio tower,
+ * text cut from the end when it does not fit max_tokens; then finish.  `prefix` (NUL-terminated, NULL for none) is the task prefix.  `token_counts` and
  * `truncated` (may be NULL) receive each input's rows and whether text was cut.  An input whose
- * images alone exceed max_tokens is refused (GE_ERR_INVALID_OPTIONS); audio parts need an audio
- * encoder (GE_ERR_AUDIO_ENCODER_NOT_LOADED).  Runs on the first device. */
+ * images and clips alone exceed max_tokens is refused (GE_ERR_INVALID_OPTIONS); image parts need
+ * an image encoder and audio parts an audio encoder (GE_ERR_*_ENCODER_NOT_LOADED).  Runs on the
+ * first device. */
 GE_API int ge_embed_multimodal(ge_model* model, const ge_multimodal_input* inputs, int32_t count, const char* prefix,
                                const ge_multimodal_opts* opts, float* out, int32_t* token_counts, int32_t* truncated,
                                ge_progress_fn progress, void* user);

@@ -211,3 +211,58 @@ def test_audio_encoder_load_refusals(ge, synth, cuda_device):
     with pytest.raises(ge.GemmaEmbedError) as e:
         ge.EmbeddingModel.load(text, ge.LoadOptions(audio_encoder=synth.mmproj_path(seed=2, layers=2, positions=64)))
     assert e.value.case == "invalidGGUF"
+
+
+def test_multimodal_text_images_and_clips_match_oracle(ge, synth, cuda_device):
+    """embed(_ inputs: [MultimodalInput]) (MultimodalEmbedding.swift:100-206) with text, images and
+    clips in one input: the oracle's towers and layout (oracle/multimodal.py), then the text tower
+    over the sequence with the input's rows in reading order."""
+    from oracle import multimodal as om
+    text = synth.model_path("gemma-embedding", seed=1, layers=6, vocab=4096)
+    mmproj = synth.mmproj_path(seed=2, layers=2, positions=64)
+    enc = synth.audio_path(seed=4, **SMALL)
+    model = ge.EmbeddingModel.load(text, ge.LoadOptions(image_encoder=mmproj, audio_encoder=enc,
+                                                        image_patch_budget=1 << 20))
+    vis, aud, ref = B.OracleVision(mmproj), B.OracleAudio(enc), B.OracleModel(text)
+    tok = OracleTokenizer.from_gguf(text)
+    try:
+        marks = {k: tok.encode(k, False, True)[0] for k in ("<|image>", "<image|>", "<|audio>", "<audio|>")}
+        rng = np.random.default_rng(31)
+        img = rng.integers(0, 256, (240, 320, 3), dtype=np.uint8)
+        cs = clips()
+        inputs = [["a spoken gawy stait", cs[0], "and the end"], [cs[1]], [img, cs[2], "both kinds"],
+                  [cs[3], img, cs[0]], ["only text here"]]
+        prefix = ge.TaskPrefix.document()
+        got = model.embed_multimodal(inputs, ge.MultimodalEmbedOptions(task=prefix, normalise=False,
+                                                                       max_image_tokens=100))
+        for parts, e in zip(inputs, got):
+            rows, oparts, spans = [], [], []
+            for p in parts:
+                if isinstance(p, str):
+                    oparts.append(("text", p))
+                elif p.ndim == 3:
+                    patches, gx, gy = vis.prepare(p, max_image_tokens=100)
+                    r = vis.forward(patches, gx, gy)
+                    rows.append(r)
+                    oparts.append(("image", None))
+                    spans.append((r.shape[0], marks["<|image>"], marks["<image|>"]))
+                else:
+                    r = aud.embed_rows(p)
+                    rows.append(r)
+                    oparts.append(("audio", None))
+                    spans.append((r.shape[0], marks["<|audio>"], marks["<audio|>"]))
+            ids, cut = om.sequence(prefix, oparts, spans, 2048, 2, 1, lambda t: tok.encode(t, False))
+            assert e.token_count == len(ids) and not e.truncated
+            vec = np.concatenate(rows) if rows else np.zeros((1, 768), np.float32)
+            want = ref.forward_rows(np.array(ids, np.int32), vec)
+            assert cosine(e.vector, want) > COSINE_MIN
+        # A clip-only input equals embed(audios:) on that clip, bit for bit.
+        alone = model.embed_audios([cs[1]], ge.AudioEmbedOptions(normalise=False))[0]
+        only = model.embed_multimodal([[cs[1]]], ge.MultimodalEmbedOptions(task="", normalise=False))[0]
+        assert only.token_count == alone.token_count
+        assert only.vector.tobytes() == alone.vector.tobytes()
+    finally:
+        model.close()
+        vis.close()
+        aud.close()
+        ref.close()
