@@ -331,6 +331,11 @@ int prepare_audios(ge_model* m, const ge_audio* clips, int32_t count, int max_ro
             return ge::set_error(m, GE_ERR_AUDIO_DECODING, "cannot decode audio: " + name + ": the clip has " +
                                                                std::to_string(c.count) +
                                                                " samples at 16 kHz; at least 2 are needed for one frame");
+        // A final 30-second chunk of one sample has no frame; the reference stops on a
+        // precondition there (AudioPreprocessor.swift:144), so such a clip is refused.
+        if (c.count % ge::kAudioChunkSamples == 1)
+            return ge::set_error(m, GE_ERR_AUDIO_DECODING, "cannot decode audio: " + name + ": its last 30-second chunk "
+                                                               "has 1 sample; at least 2 are needed for one frame");
         ge::PreparedAudio& p = out[size_t(i)];
         p.samples = c.samples;
         p.count = c.count;
@@ -1128,9 +1133,11 @@ int ge_audio_forward_device(ge_model* m, int32_t device_ordinal, const float* d_
     std::vector<const ge::PreparedAudio*> ptrs;
     int64_t off = 0;
     for (int32_t i = 0; i < count; i++) {
-        if (clips[i].sample_rate != 16000 || clips[i].channels != 1 || clips[i].count < ge::kAudioMinimumSamples)
+        if (clips[i].sample_rate != 16000 || clips[i].channels != 1 || clips[i].count < ge::kAudioMinimumSamples ||
+            clips[i].count % ge::kAudioChunkSamples == 1)
             return ge::set_error(m, GE_ERR_AUDIO_DECODING, "cannot decode audio: clip " + std::to_string(i) +
-                                                               " is not 16 kHz mono with at least 2 samples");
+                                                               " is not 16 kHz mono with at least 2 samples in every "
+                                                               "30-second chunk");
         cl[size_t(i)].count = clips[i].count;
         cl[size_t(i)].device_offset = off;
         off += clips[i].count;

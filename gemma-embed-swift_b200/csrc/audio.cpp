@@ -515,6 +515,9 @@ int run_audio(ge_model* m, Device& d, const AudioArgs& a) {
         if (p.count < kAudioMinimumSamples)
             return report(GE_ERR_AUDIO_DECODING, "cannot decode audio: clip " + std::to_string(i) + " has " +
                                                      std::to_string(p.count) + " samples at 16 kHz; at least 2 are needed for one frame");
+        if (p.count % kAudioChunkSamples == 1)
+            return report(GE_ERR_AUDIO_DECODING, "cannot decode audio: clip " + std::to_string(i) +
+                                                     ": its last 30-second chunk has 1 sample");
         const int64_t base = a.d_pcm ? p.device_offset : pcm;
         for (int64_t off = 0; off < p.count; off += kAudioChunkSamples) {
             AudioChunk ch{};

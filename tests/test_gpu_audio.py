@@ -266,3 +266,24 @@ def test_multimodal_text_images_and_clips_match_oracle(ge, synth, cuda_device):
         vis.close()
         aud.close()
         ref.close()
+
+
+def test_audio_chunk_edges_match_oracle(ge, audio_model):
+    """Clips at the front end's edges: two samples (one frame, one row), exactly one 30-second
+    chunk (750 rows), and two samples past it (a second chunk of one frame and one row).  One
+    sample past it leaves a chunk without a frame, where the reference stops on a precondition
+    (AudioPreprocessor.swift:144): refused."""
+    model, aud, _, _ = audio_model
+    rng = np.random.default_rng(41)
+    cs = [np.array([0.25, -0.5], np.float32), rng.normal(0, 0.05, 480000).astype(np.float32),
+          rng.normal(0, 0.05, 480002).astype(np.float32)]
+    got = model.audio_vectors(cs)
+    assert [g.shape[0] for g in got] == [1, 750, 751]
+    with pytest.raises(ge.GemmaEmbedError) as e:
+        model.embed_audios([np.zeros(480001, np.float32)])
+    assert e.value.case == "audioDecoding"
+    for c, rows in zip(cs, got):
+        want = aud.embed_rows(c)
+        assert rows.shape == want.shape
+        worst = min(cosine(a, b) for a, b in zip(rows, want))
+        assert worst > COSINE_MIN, (len(c), worst)
