@@ -49,15 +49,15 @@ __device__ __forceinline__ float clampf(float v, float lo, float hi) { return fm
 }  // namespace
 
 // ---------------------------------------------------------------------------- log-mel
-// One warp per frame: the windowed frame is written bit-reversed into the warp's buffers, nine
-// in-place radix-2 levels follow with the reference's twiddles and operation order (separately
-// rounded multiplies and adds, no fused multiply-add), then the magnitudes and, per mel filter,
-// four-bin fp32 partial sums added into a double, floored at fp32(0.001) and logged.  Real and
-// imaginary parts sit in separate arrays with one padding word per 32 elements, which keeps the
-// bit-reversed stores and the butterflies' strided accesses on distinct banks.
-__device__ __forceinline__ int fft_pad(int i) { return i + (i >> 5); }
-constexpr int kFftPadded = kFft + kFft / 32;
-constexpr int kLogMelWarpFloats = 2 * kFftPadded + 264;
+// One warp per frame, the whole 512-point FFT in registers: after the bit-reversed copy, element
+// i sits in lane i % 32, register i / 32.  Lane l therefore loads the 16 consecutive window
+// samples from rev5(l) * 16 (register r takes sample rev5(l) * 16 + rev4(r)).  The nine radix-2
+// levels use the reference's twiddles and operation order in separately rounded fp32 (no fused
+// multiply-add): the five levels whose partners are fewer than 32 elements apart exchange
+// values between lanes by shuffle (both partners compute the same products, each keeps its own
+// output), the four others pair registers within a lane.  Then the magnitudes and, per mel
+// filter, four-bin fp32 partial sums added into a double, floored at fp32(0.001) and logged.
+constexpr int kLogMelWarpFloats = 264;  // magnitudes of the warp's frame
 
 __global__ void __launch_bounds__(256) k_log_mel(const float* __restrict__ pcm, const AudioChunk* __restrict__ chunks,
                                                  int nchunks, int frames_total, MelTables t, float* __restrict__ out) {
@@ -66,58 +66,90 @@ __global__ void __launch_bounds__(256) k_log_mel(const float* __restrict__ pcm, 
     float* cos_t = hann + kFft;
     float* sin_t = cos_t + kFft;
     float* fw = sin_t + kFft;
-    int* bitrev = reinterpret_cast<int*>(fw + t.nw);
-    int* band = bitrev + kFft;  // lo[mel], hi[mel], off[mel]
-    float* bufs = reinterpret_cast<float*>(band + 3 * t.mel);
+    int* band = reinterpret_cast<int*>(fw + t.nw);  // lo[mel], hi[mel], off[mel]
+    float* mags = reinterpret_cast<float*>(band + 3 * t.mel);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* re = bufs + warp * kLogMelWarpFloats;
-    float* im = re + kFftPadded;
-    float* mag = im + kFftPadded;
+    float* mag = mags + warp * kLogMelWarpFloats;
     for (int i = threadIdx.x; i < kFft; i += blockDim.x) {
         hann[i] = t.hann[i];
         cos_t[i] = t.cos_t[i];
         sin_t[i] = t.sin_t[i];
-        bitrev[i] = t.bitrev[i];
     }
     for (int i = threadIdx.x; i < t.nw; i += blockDim.x) fw[i] = t.w[i];
     for (int i = threadIdx.x; i < 3 * t.mel; i += blockDim.x) band[i] = t.band[i];
     pdl_wait();
     __syncthreads();
+    const int j0 = int(__brev(uint32_t(lane)) >> 27) * 16;  // rev5(lane) * 16
     for (int f = blockIdx.x * 8 + warp; f < frames_total; f += gridDim.x * 8) {
         const AudioChunk ch = chunks[chunk_of<&AudioChunk::mel_row>(chunks, nchunks, f)];
         const int fl = f - ch.mel_row;
         const float* s = pcm + ch.pcm_offset;
         // padded[p] = chunk[p - 160] (160 zeros in front, zeros past the end)
-        for (int j = lane; j < kFft; j += 32) {
-            const int idx = fl * kHop + j - kPadLeft;
-            const float x = (idx >= 0 && idx < ch.samples) ? s[idx] : 0.0f;
-            const int r = fft_pad(bitrev[j]);
-            re[r] = __fmul_rn(hann[j], x);
+        const int idx0 = fl * kHop + j0 - kPadLeft;
+        float w16[16];
+        if (idx0 >= 0 && idx0 + 16 <= ch.samples && (reinterpret_cast<uintptr_t>(s + idx0) & 15) == 0) {
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const float4 v = *reinterpret_cast<const float4*>(s + idx0 + 4 * q);
+                w16[4 * q] = v.x, w16[4 * q + 1] = v.y, w16[4 * q + 2] = v.z, w16[4 * q + 3] = v.w;
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < 16; q++) {
+                const int idx = idx0 + q;
+                w16[q] = (idx >= 0 && idx < ch.samples) ? s[idx] : 0.0f;
+            }
+        }
+        float re[16], im[16];
+#pragma unroll
+        for (int r = 0; r < 16; r++) {
+            const int q = int(__brev(uint32_t(r)) >> 28);  // rev4(r)
+            re[r] = __fmul_rn(hann[j0 + q], w16[q]);
             im[r] = 0.0f;
         }
-        __syncwarp();
-#pragma unroll 1
-        for (int lg = 0; lg < 9; lg++) {
-            const int half = 1 << lg, count = half << 1, step = kFft / count;
-#pragma unroll 4
-            for (int b = lane; b < kFft / 2; b += 32) {
-                const int k = b & (half - 1);
-                const int e = (b >> lg) * count + k;
-                const int ev = fft_pad(e), od = fft_pad(e + half);
-                const float c = cos_t[k * step], sn = -sin_t[k * step];
-                const float ro = re[od], io = im[od], er = re[ev], ei = im[ev];
+#pragma unroll
+        for (int lg = 0; lg < 5; lg++) {  // partners in other lanes
+            const int half = 1 << lg, step = kFft / (half << 1);
+            const int k = lane & (half - 1);
+            const float c = cos_t[k * step], sn = -sin_t[k * step];
+            const bool odd = lane & half;
+#pragma unroll
+            for (int r = 0; r < 16; r++) {
+                const float pre = __shfl_xor_sync(0xffffffffu, re[r], half);
+                const float pim = __shfl_xor_sync(0xffffffffu, im[r], half);
+                const float er = odd ? pre : re[r], ei = odd ? pim : im[r];
+                const float ro = odd ? re[r] : pre, io = odd ? im[r] : pim;
                 const float a = __fmul_rn(c, ro), bq = __fmul_rn(sn, io), cq = __fmul_rn(c, io), d = __fmul_rn(sn, ro);
-                re[ev] = __fsub_rn(__fadd_rn(er, a), bq);
-                im[ev] = __fadd_rn(__fadd_rn(ei, cq), d);
-                re[od] = __fadd_rn(__fsub_rn(er, a), bq);
-                im[od] = __fsub_rn(__fsub_rn(ei, cq), d);
+                if (odd) {
+                    re[r] = __fadd_rn(__fsub_rn(er, a), bq);
+                    im[r] = __fsub_rn(__fsub_rn(ei, cq), d);
+                } else {
+                    re[r] = __fsub_rn(__fadd_rn(er, a), bq);
+                    im[r] = __fadd_rn(__fadd_rn(ei, cq), d);
+                }
             }
-            __syncwarp();
         }
-        for (int j = lane; j < kBins; j += 32) {
-            const float x = re[fft_pad(j)], y = im[fft_pad(j)];
-            mag[j] = __fsqrt_rn(__fadd_rn(__fmul_rn(x, x), __fmul_rn(y, y)));
+#pragma unroll
+        for (int lg = 5; lg < 9; lg++) {  // partners in the same lane, h registers apart
+            const int h = 1 << (lg - 5), step = kFft / (2 << lg);
+#pragma unroll
+            for (int r = 0; r < 16; r++) {
+                if (r & h) continue;
+                const int k = 32 * (r & (h - 1)) + lane;
+                const float c = cos_t[k * step], sn = -sin_t[k * step];
+                const float er = re[r], ei = im[r], ro = re[r + h], io = im[r + h];
+                const float a = __fmul_rn(c, ro), bq = __fmul_rn(sn, io), cq = __fmul_rn(c, io), d = __fmul_rn(sn, ro);
+                re[r] = __fsub_rn(__fadd_rn(er, a), bq);
+                im[r] = __fadd_rn(__fadd_rn(ei, cq), d);
+                re[r + h] = __fadd_rn(__fsub_rn(er, a), bq);
+                im[r + h] = __fsub_rn(__fsub_rn(ei, cq), d);
+            }
         }
+        // Bins 0..256: element j is in lane j % 32, register j / 32.
+#pragma unroll
+        for (int r = 0; r < 8; r++)
+            mag[32 * r + lane] = __fsqrt_rn(__fadd_rn(__fmul_rn(re[r], re[r]), __fmul_rn(im[r], im[r])));
+        if (lane == 0) mag[256] = __fsqrt_rn(__fadd_rn(__fmul_rn(re[8], re[8]), __fmul_rn(im[8], im[8])));
         __syncwarp();
         for (int m = lane; m < t.mel; m += 32) {
             const int lo = band[m], hi = band[t.mel + m];
@@ -140,7 +172,7 @@ __global__ void __launch_bounds__(256) k_log_mel(const float* __restrict__ pcm, 
 }
 
 size_t log_mel_smem(const MelTables& t) {
-    return size_t(3 * kFft + t.nw) * 4 + size_t(kFft + 3 * t.mel) * 4 + size_t(8) * kLogMelWarpFloats * 4;
+    return size_t(3 * kFft + t.nw) * 4 + size_t(3 * t.mel) * 4 + size_t(8) * kLogMelWarpFloats * 4;
 }
 
 cudaError_t launch_log_mel(const float* pcm, const AudioChunk* chunks, int nchunks, int frames_total,
@@ -155,7 +187,7 @@ cudaError_t launch_log_mel(const float* pcm, const AudioChunk* chunks, int nchun
 
 cudaError_t configure_audio_kernels() {
     // The largest table set the launcher accepts: 128 filters of at most 257 weights each.
-    const size_t most = size_t(3 * kFft + kMel * kBins) * 4 + size_t(kFft + 3 * kMel) * 4 + size_t(8) * kLogMelWarpFloats * 4;
+    const size_t most = size_t(3 * kFft + kMel * kBins) * 4 + size_t(3 * kMel) * 4 + size_t(8) * kLogMelWarpFloats * 4;
     return cudaFuncSetAttribute(k_log_mel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(std::min<size_t>(most, 227 * 1024)));
 }
 
