@@ -191,7 +191,6 @@ void free_audio_workspace(AudioWorkspace& ws) {
     for (void* p : ws.allocations) cudaFree(p);
     for (void* p : {(void*)ws.h_chunks, (void*)ws.h_cs, (void*)ws.h_pcm})
         if (p) cudaFreeHost(p);
-    if (ws.pcm_copied) cudaEventDestroy(ws.pcm_copied);
     ws = AudioWorkspace();
 }
 
@@ -237,7 +236,6 @@ cudaError_t ensure_audio_workspace(const AudioConfig& c, Device& d, int trows, i
     if (err == cudaSuccess) err = cudaMallocHost(reinterpret_cast<void**>(&ws.h_chunks), size_t(C) * sizeof(AudioChunk));
     if (err == cudaSuccess) err = cudaMallocHost(reinterpret_cast<void**>(&ws.h_cs), r * sizeof(int));
     if (err == cudaSuccess && P > 1) err = cudaMallocHost(reinterpret_cast<void**>(&ws.h_pcm), P * sizeof(float));
-    if (err == cudaSuccess) err = cudaEventCreateWithFlags(&ws.pcm_copied, cudaEventDisableTiming);
     if (err != cudaSuccess) {
         free_audio_workspace(ws);
         return err;
@@ -538,6 +536,7 @@ int run_audio(ge_model* m, Device& d, const AudioArgs& a) {
     }
     const int nch = int(chunks.size());
     const int trows = std::max(kRowTile, round_up(tokens, kRowTile));
+    if ((e = staging_wait(d, kStageAudio)) != cudaSuccess) return gpu_fail(e, "staging");
     if ((e = ensure_audio_workspace(c, d, trows, frames, t0, nch, a.d_pcm ? 0 : size_t(pcm))) != cudaSuccess)
         return gpu_fail(e, "workspace");
     AudioWorkspace& ws = d.aud.ws;
@@ -547,9 +546,8 @@ int run_audio(ge_model* m, Device& d, const AudioArgs& a) {
     for (int r = tokens; r < trows; r++) ws.h_cs[r] = r;
     cudaStream_t st = a.stream ? a.stream : d.stream;
     if (!a.d_pcm) {
-        // The clips are gathered into pinned memory on several host threads (the previous upload
-        // out of it has finished first), then copied to the device in one transfer.
-        if ((e = cudaEventSynchronize(ws.pcm_copied)) != cudaSuccess) return gpu_fail(e, "audio staging");
+        // The clips are gathered into pinned memory on several host threads, then copied to the
+        // device in one transfer.
         std::vector<int64_t> start(size_t(a.n) + 1, 0);
         for (int i = 0; i < a.n; i++) start[size_t(i) + 1] = start[size_t(i)] + a.clips[i]->count;
         const int64_t per = std::max<int64_t>(int64_t(1) << 18, (pcm + 7) / 8);
@@ -567,11 +565,11 @@ int run_audio(ge_model* m, Device& d, const AudioArgs& a) {
         gather(0);
         for (auto& x : th) x.join();
         e = cudaMemcpyAsync(ws.pcm, ws.h_pcm, size_t(pcm) * 4, cudaMemcpyHostToDevice, st);
-        if (e == cudaSuccess) e = cudaEventRecord(ws.pcm_copied, st);
     }
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(ws.chunks, ws.h_chunks, size_t(nch) * sizeof(AudioChunk), cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess) e = cudaMemcpyAsync(ws.chunk_start, ws.h_cs, size_t(trows) * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = staging_done(d, kStageAudio, st);
     if (e != cudaSuccess) return gpu_fail(e, "audio upload");
     m->h2d_bytes += int64_t((a.d_pcm ? 0 : pcm * 4) + int64_t(nch) * int64_t(sizeof(AudioChunk)) + int64_t(trows) * 4);
     const float* src = a.d_pcm ? a.d_pcm : ws.pcm;

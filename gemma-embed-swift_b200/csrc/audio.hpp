@@ -60,8 +60,7 @@ struct AudioWorkspace {
     DevActivation a_a1, a_a2, a_h, a_hk, a_hv, a_attn, a_act, a_h2;
     AudioChunk* h_chunks = nullptr;
     int* h_cs = nullptr;
-    float* h_pcm = nullptr;                // pinned staging of the clips' samples
-    cudaEvent_t pcm_copied = nullptr;      // the last upload out of h_pcm has completed
+    float* h_pcm = nullptr;  // pinned staging of the clips' samples
     std::vector<void*> allocations;
 };
 

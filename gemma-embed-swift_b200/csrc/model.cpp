@@ -320,6 +320,13 @@ static int load_device(ge_model* m, Device& d, const std::vector<HostWeight>& hw
     return GE_OK;
 }
 
+cudaError_t staging_wait(Device& d, int kind) {
+    if (!d.staging[kind]) return cudaEventCreateWithFlags(&d.staging[kind], cudaEventDisableTiming);
+    return cudaEventSynchronize(d.staging[kind]);
+}
+
+cudaError_t staging_done(Device& d, int kind, cudaStream_t stream) { return cudaEventRecord(d.staging[kind], stream); }
+
 static void free_device(Device& d) {
     if (d.stream) {
         cudaSetDevice(d.ordinal);
@@ -332,6 +339,10 @@ static void free_device(Device& d) {
     if (d.mm_vectors) cudaFree(d.mm_vectors);
     d.mm_vectors = nullptr;
     d.mm_vectors_cap = 0;
+    for (cudaEvent_t& ev : d.staging) {
+        if (ev) cudaEventDestroy(ev);
+        ev = nullptr;
+    }
     for (void* p : d.allocations) cudaFree(p);
     d.allocations.clear();
     if (d.stream) cudaStreamDestroy(d.stream);
@@ -622,6 +633,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     }
     const int nwork512 = any512 ? build_work(a.seqs, nseq, kSimtQueriesPerItem, nullptr) : 0;
     const int work_words = words[0] + words[1] + 3 * nwork512;
+    if ((e = staging_wait(d, kStageText)) != cudaSuccess) return gpu_fail(e, "staging");
     if ((e = ensure_workspace(c, d, rows, nseq, work_words)) != cudaSuccess) return gpu_fail(e, "workspace");
     Workspace& ws = d.ws;
     int64_t launches = 0;
@@ -663,6 +675,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     } else {
         e = launch_positions(ws.seqs, nseq, ws.positions, st);
     }
+    if (e == cudaSuccess) e = staging_done(d, kStageText, st);
     if (e != cudaSuccess) return gpu_fail(e, "positions");
 
     cudaStream_t ks = st;  // the stream kernels are launched on (the capture stream while capturing)

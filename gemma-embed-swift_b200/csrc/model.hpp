@@ -112,7 +112,18 @@ struct Device {
     // Mixed inputs with both images and clips: their rows gathered in sequence order.
     float* mm_vectors = nullptr;
     size_t mm_vectors_cap = 0;  // floats
+    // Per path (text, image, audio): recorded after the copies out of that path's pinned staging
+    // buffers (see staging_wait).
+    cudaEvent_t staging[3] = {nullptr, nullptr, nullptr};
 };
+
+// Each call rewrites its path's pinned staging buffers, while the copies the previous call
+// enqueued from them may still be pending: the device-resident entry points return without
+// waiting for their stream.  A call therefore waits for the event recorded after the previous
+// call's copies (staging_done) before it writes or regrows those buffers (staging_wait).
+enum StagingKind : int { kStageText = 0, kStageImage = 1, kStageAudio = 2 };
+cudaError_t staging_wait(Device& d, int kind);
+cudaError_t staging_done(Device& d, int kind, cudaStream_t stream);
 
 }  // namespace ge
 

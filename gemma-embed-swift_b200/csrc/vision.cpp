@@ -358,6 +358,7 @@ int run_vision(ge_model* m, Device& d, const VisionArgs& a) {
     int ctas = 0;
     const int words = build_attention_work(seq_pairs.data(), n, c.heads, 1, 0, d.num_sms, nullptr, &ctas);
     const int items = words ? (words - ctas - 1) / 4 : 0;
+    if ((e = staging_wait(d, kStageImage)) != cudaSuccess) return gpu_fail(e, "staging");
     if ((e = ensure_vision_workspace(c, d, rows, trows, n, a.d_rgb ? 0 : rgb, words)) != cudaSuccess)
         return gpu_fail(e, "workspace");
     VisionWorkspace& ws = d.vis.ws;
@@ -380,7 +381,8 @@ int run_vision(ge_model* m, Device& d, const VisionArgs& a) {
     if ((!a.d_rgb && (e = cudaMemcpyAsync(ws.rgb, ws.h_rgb, rgb, cudaMemcpyHostToDevice, st)) != cudaSuccess) ||
         (e = cudaMemcpyAsync(ws.imgs, ws.h_imgs, size_t(n) * sizeof(VisionImage), cudaMemcpyHostToDevice, st)) != cudaSuccess ||
         (e = cudaMemcpyAsync(ws.xy, ws.h_xy, size_t(patches) * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
-        (e = cudaMemcpyAsync(ws.work, ws.h_work, size_t(words) * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess)
+        (e = cudaMemcpyAsync(ws.work, ws.h_work, size_t(words) * 4, cudaMemcpyHostToDevice, st)) != cudaSuccess ||
+        (e = staging_done(d, kStageImage, st)) != cudaSuccess)
         return gpu_fail(e, "image upload");
     m->h2d_bytes += int64_t((a.d_rgb ? 0 : rgb) + size_t(n) * sizeof(VisionImage) + size_t(patches) * 4 + size_t(words) * 4);
     // Padding rows of the GEMM operands are zero (VisionTower.upload, VisionTower.swift:145-146).

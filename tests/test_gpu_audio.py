@@ -287,3 +287,28 @@ def test_audio_chunk_edges_match_oracle(ge, audio_model):
         assert rows.shape == want.shape
         worst = min(cosine(a, b) for a, b in zip(rows, want))
         assert worst > COSINE_MIN, (len(c), worst)
+
+
+def test_device_forwards_back_to_back(ge, audio_model):
+    """Two device-resident audio forwards with different clips, enqueued on one stream without a
+    synchronisation between them, each give the pooled rows of embed_audios on its own clips: the
+    second call's staging of its chunk table waits for the first call's copies."""
+    import torch
+    model = audio_model[0]
+    a, b = clips(), [long_clip(), clips()[2]]
+    want_a = model.embed_audios(a, ge.AudioEmbedOptions(normalise=False))
+    want_b = model.embed_audios(b, ge.AudioEmbedOptions(normalise=False))
+    od = model.info.output_dimensions
+    pa, pb = torch.from_numpy(np.concatenate(a)).cuda(), torch.from_numpy(np.concatenate(b)).cuda()
+    oa = torch.zeros((len(a), od), dtype=torch.float32, device="cuda")
+    ob = torch.zeros((len(b), od), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    for _ in range(3):
+        model.audio_forward_device(pa.data_ptr(), [len(c) for c in a], oa.data_ptr(), stream=stream.cuda_stream)
+        model.audio_forward_device(pb.data_ptr(), [len(c) for c in b], ob.data_ptr(), stream=stream.cuda_stream)
+    torch.cuda.synchronize()
+    for e, row in zip(want_a, oa.cpu().numpy()):
+        assert np.array_equal(e.vector, row)
+    for e, row in zip(want_b, ob.cpu().numpy()):
+        assert np.array_equal(e.vector, row)
