@@ -22,7 +22,7 @@ import numpy as np
 from . import _lib
 
 __all__ = ["EmbeddingModel", "EmbedOptions", "LoadOptions", "ImageEmbedOptions", "MultimodalEmbedOptions", "AudioEmbedOptions",
-           "audio_tokens", "Embedding",
+           "audio_tokens", "audio_to_mono16k", "Embedding",
            "EmbeddingProgress", "ModelInfo", "GemmaEmbedError", "TaskPrefix", "Tokenizer", "ALLOWED_DIMENSIONS"]
 
 ALLOWED_DIMENSIONS = (768, 512, 256, 128)
@@ -278,6 +278,19 @@ AUDIO_SAMPLE_RATE = 16000
 def audio_tokens(samples: int) -> int:
     """AudioFrontEnd.tokenCount(samples:) (Audio/AudioPreprocessor.swift:86-95)."""
     return int(_lib.lib().ge_audio_tokens(int(samples)))
+
+
+def audio_to_mono16k(samples, sample_rate: int = AUDIO_SAMPLE_RATE, channels: int = 1) -> np.ndarray:
+    """MiniaudioConverter.toMono16k (Audio/MiniaudioConverter.swift:23-37): interleaved float
+    samples at any rate and channel count as the 16 kHz mono samples the audio encoder reads."""
+    c, keep = _audios([(samples, sample_rate, channels)])
+    n = ctypes.c_int64(0)
+    L = _lib.lib()
+    if L.ge_audio_convert(c, None, 0, ctypes.byref(n)) != 0:
+        raise GemmaEmbedError(16, "audioDecoding: " + (L.ge_last_error(None) or b"").decode())
+    out = np.zeros(max(n.value, 1), np.float32)
+    _check(L.ge_audio_convert(c, _ptr(out, ctypes.c_float), n.value, ctypes.byref(n)), None)
+    return out[:n.value]
 
 
 def _audios(clips):
@@ -625,8 +638,9 @@ class EmbeddingModel:
     def embed_audios(self, clips, options: Optional[AudioEmbedOptions] = None,
                      progress: Optional[Callable[[EmbeddingProgress], Optional[bool]]] = None) -> list:
         """embed(audios:options:progress:) (AudioEmbedding.swift:17-33) over PCM clips: 16 kHz mono
-        float32 arrays (or (samples, rate, channels) tuples, which must also be 16 kHz mono); a
-        single 1-D array embeds one clip and returns one Embedding."""
+        float32 arrays, or (interleaved samples, rate, channels) tuples at any rate and channel
+        count (converted as audio_to_mono16k does); a single 1-D array embeds one clip and returns
+        one Embedding."""
         options = options or AudioEmbedOptions()
         single = isinstance(clips, np.ndarray) and clips.ndim == 1
         items = [clips] if single else list(clips)

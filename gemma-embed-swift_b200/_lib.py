@@ -132,6 +132,7 @@ SIGNATURES = {
                          ctypes.c_int),
     "ge_audio_opts_default": ([P(GeAudioOpts)], None),
     "ge_audio_tokens": ([ctypes.c_int64], ctypes.c_int64),
+    "ge_audio_convert": ([P(GeAudio), f32p, ctypes.c_int64, i64p], ctypes.c_int),
     "ge_embed_audios": ([ctypes.c_void_p, P(GeAudio), ctypes.c_int32, P(GeAudioOpts), f32p, i32p, PROGRESS_FN,
                          ctypes.c_void_p], ctypes.c_int),
     "ge_audio_vectors": ([ctypes.c_void_p, P(GeAudio), ctypes.c_int32, f32p, ctypes.c_int64, i32p], ctypes.c_int),

@@ -11,6 +11,7 @@
 #include <numeric>
 #include <thread>
 
+#include "audio_convert.hpp"
 #include "gemma_embed.h"
 #include "model.hpp"
 #include "multimodal.hpp"
@@ -313,20 +314,50 @@ int audios_on_device(ge_model* m, ge::Device& d, const ge::PreparedAudio* const*
     return ge::run_forward(m, d, a);
 }
 
-// AudioEmbedding.prepare's checks (AudioEmbedding.swift:78-101) on PCM inputs: 16 kHz mono, at
-// least one frame, and at most max_rows rows with the 4 frame rows.
+// AudioDecoder.decode's checks on `.samples` inputs (Audio/AudioDecoder.swift:33-38, 48-51).
+std::string check_audio_input(const ge_audio& c) {
+    if (c.channels <= 0) return "channel count must be positive";
+    if (c.sample_rate <= 0) return "sample rate must be positive";
+    if (c.count < 0 || (c.count > 0 && !c.samples)) return "the samples are missing";
+    if (c.count == 0) return "audio has no samples";
+    return std::string();
+}
+
+// AudioEmbedding.prepare (AudioEmbedding.swift:78-101) on PCM inputs: decoded samples at any rate
+// and channel count go to 16 kHz mono (MiniaudioConverter) on host threads; then at least one
+// frame, and at most max_rows rows with the 4 frame rows.
 int prepare_audios(ge_model* m, const ge_audio* clips, int32_t count, int max_rows, std::vector<ge::PreparedAudio>& out) {
     out.assign(size_t(count), ge::PreparedAudio());
     for (int32_t i = 0; i < count; i++) {
-        const ge_audio& c = clips[i];
+        const std::string why = check_audio_input(clips[i]);
+        if (!why.empty())
+            return ge::set_error(m, GE_ERR_AUDIO_DECODING, "cannot decode audio: audio " + std::to_string(i) + ": " + why);
+    }
+    {
+        std::atomic<int32_t> next{0};
+        auto work = [&]() {
+            for (int32_t i = next++; i < count; i = next++) {
+                const ge_audio& c = clips[i];
+                ge::PreparedAudio& p = out[size_t(i)];
+                if (c.sample_rate == 16000 && c.channels == 1) {
+                    p.samples = c.samples;
+                    p.count = c.count;
+                } else {
+                    ge::audio_to_mono_16k(c.samples, c.count, c.channels, c.sample_rate, p.converted);
+                    p.samples = p.converted.data();
+                    p.count = int64_t(p.converted.size());
+                }
+            }
+        };
+        const int nt = int(std::min<int64_t>({int64_t(std::max(1u, std::thread::hardware_concurrency())), int64_t(count), 16}));
+        std::vector<std::thread> th;
+        for (int t = 1; t < nt; t++) th.emplace_back(work);
+        work();
+        for (auto& t : th) t.join();
+    }
+    for (int32_t i = 0; i < count; i++) {
+        const ge::PreparedAudio& c = out[size_t(i)];
         const std::string name = "audio " + std::to_string(i);
-        if (!c.samples && c.count > 0)
-            return ge::set_error(m, GE_ERR_AUDIO_DECODING, "cannot decode audio: " + name + " has no samples");
-        if (c.sample_rate != 16000 || c.channels != 1)
-            return ge::set_error(m, GE_ERR_AUDIO_DECODING, "cannot decode audio: " + name + " is " +
-                                                               std::to_string(c.channels) + " channel(s) at " +
-                                                               std::to_string(c.sample_rate) +
-                                                               " Hz; pass 16 kHz mono samples");
         if (c.count < ge::kAudioMinimumSamples)
             return ge::set_error(m, GE_ERR_AUDIO_DECODING, "cannot decode audio: " + name + ": the clip has " +
                                                                std::to_string(c.count) +
@@ -336,9 +367,6 @@ int prepare_audios(ge_model* m, const ge_audio* clips, int32_t count, int max_ro
         if (c.count % ge::kAudioChunkSamples == 1)
             return ge::set_error(m, GE_ERR_AUDIO_DECODING, "cannot decode audio: " + name + ": its last 30-second chunk "
                                                                "has 1 sample; at least 2 are needed for one frame");
-        ge::PreparedAudio& p = out[size_t(i)];
-        p.samples = c.samples;
-        p.count = c.count;
         const int64_t rows = ge::audio_token_count(c.count) + 4;
         if (rows > max_rows) {
             char buf[256];
@@ -980,6 +1008,29 @@ void ge_audio_opts_default(ge_audio_opts* o) {
     o->normalise = 1;
     o->max_tokens = 0;
     o->batch_size = 0;
+}
+
+int ge_audio_convert(const ge_audio* clip, float* out, int64_t cap, int64_t* count) {
+    if (!clip || !count || cap < 0 || (cap > 0 && !out)) {
+        t_last_error = "invalid options: NULL clip, count or output";
+        return GE_ERR_INVALID_OPTIONS;
+    }
+    const std::string why = check_audio_input(*clip);
+    if (!why.empty()) {
+        t_last_error = "cannot decode audio: " + why;
+        return GE_ERR_AUDIO_DECODING;
+    }
+    std::vector<float> v;
+    const float* src = clip->samples;
+    int64_t n = clip->count;
+    if (clip->sample_rate != 16000 || clip->channels != 1) {
+        ge::audio_to_mono_16k(clip->samples, clip->count, clip->channels, clip->sample_rate, v);
+        src = v.data();
+        n = int64_t(v.size());
+    }
+    *count = n;
+    if (cap > 0 && n > 0) memcpy(out, src, size_t(std::min(cap, n)) * sizeof(float));
+    return GE_OK;
 }
 
 int64_t ge_audio_tokens(int64_t samples) {

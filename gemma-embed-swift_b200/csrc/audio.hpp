@@ -84,6 +84,7 @@ struct AudioDev {
 struct PreparedAudio {
     const float* samples = nullptr;
     int64_t count = 0;
+    std::vector<float> converted;  // the 16 kHz mono samples when the input needed converting
     int64_t device_offset = 0;  // with a device PCM buffer: where this clip's samples start
     int frames() const;
     int tokens() const;

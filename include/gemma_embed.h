@@ -327,9 +327,12 @@ GE_API int ge_image_vectors(ge_model* model, const ge_image* images, int32_t cou
 
 /* ---- Audio (AudioEmbedding.swift, Metal/AudioTower.swift) -------------------------------- */
 
-/* AudioInput.samples (Audio/AudioInput.swift:12): `count` PCM samples in -1 .. 1 at
- * `sample_rate` Hz, `channels` interleaved.  The library takes 16 kHz mono; decoding files and
- * downmixing or resampling to 16 kHz mono are the caller's (GE_ERR_AUDIO_DECODING otherwise). */
+/* AudioInput.samples (Audio/AudioInput.swift:12): `count` frames of `channels` interleaved PCM
+ * samples (count * channels floats) in -1 .. 1 at `sample_rate` Hz.  Clips that are not 16 kHz
+ * mono are converted as llama.cpp's miniaudio decoder converts them (channels averaged in order,
+ * linear resampler with a 4th-order low-pass; MiniaudioConverter, Audio/MiniaudioConverter.swift);
+ * decoding files is the caller's.  A non-positive rate or channel count, or no samples, is
+ * GE_ERR_AUDIO_DECODING. */
 typedef struct ge_audio {
     const float* samples;
     int64_t count;
@@ -346,6 +349,11 @@ typedef struct ge_audio_opts {
 } ge_audio_opts;
 
 GE_API void ge_audio_opts_default(ge_audio_opts* opts);
+
+/* MiniaudioConverter.toMono16k (Audio/MiniaudioConverter.swift:23-37): the 16 kHz mono samples the
+ * audio encoder reads for `clip`; writes min(cap, n) of them to `out` and n to `*count`.  Host code
+ * only: needs no model and no GPU. */
+GE_API int ge_audio_convert(const ge_audio* clip, float* out, int64_t cap, int64_t* count);
 
 /* AudioFrontEnd.tokenCount(samples:) (Audio/AudioPreprocessor.swift:86-95): the rows a clip of
  * `samples` 16 kHz samples gives the text tower, before the 4 frame rows; 0 below 2 samples. */
@@ -368,7 +376,7 @@ GE_API int ge_audio_vectors(ge_model* model, const ge_audio* clips, int32_t coun
                             int32_t* rows_per_clip);
 
 /* The audio forward (audio and text towers) over device-resident samples on the caller's
- * stream, without synchronising: `d_pcm` holds the clips' 16 kHz samples back to back
+ * stream, without synchronising: `d_pcm` holds the clips' 16 kHz mono samples back to back
  * (clips[i].count each; clips[i].samples is ignored); d_pooled receives [count]
  * [output_dimensions] pooled, unnormalised fp32 rows.  NULL stream: the legacy default stream. */
 GE_API int ge_audio_forward_device(ge_model* model, int32_t device_ordinal, const float* d_pcm, const ge_audio* clips,

@@ -104,6 +104,10 @@ def lib():
         L.or_audio_tables.argtypes = [ctypes.c_int32, f32p, f32p, f32p, f32p, i32p, i32p, i32p]
         L.or_audio_log_mel.argtypes = [f32p, ctypes.c_int64, ctypes.c_int32, f32p]
         L.or_audio_log_mel.restype = ctypes.c_int32
+        L.or_audio_frames_after_resampling.argtypes = [ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint64]
+        L.or_audio_frames_after_resampling.restype = ctypes.c_uint64
+        L.or_audio_to_mono16k.argtypes = [f32p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, f32p]
+        L.or_audio_to_mono16k.restype = ctypes.c_int64
         _lib = L
     return _lib
 
@@ -334,6 +338,21 @@ def log_mel(samples, mel_bins: int = 128) -> np.ndarray:
     f32 = ctypes.POINTER(ctypes.c_float)
     lib().or_audio_log_mel(s.ctypes.data_as(f32), len(s), mel_bins, out.ctypes.data_as(f32))
     return out
+
+
+def frames_after_resampling(rate_in: int, frames: int, rate_out: int = 16000) -> int:
+    return int(lib().or_audio_frames_after_resampling(rate_out, rate_in, frames))
+
+
+def to_mono16k(samples, rate: int, channels: int = 1) -> np.ndarray:
+    """MiniaudioConverter.toMono16k: interleaved float samples at `rate` Hz to 16 kHz mono."""
+    s = np.ascontiguousarray(samples, dtype=np.float32).reshape(-1)
+    frames = s.size // channels
+    n = frames_after_resampling(rate, frames) if rate != 16000 else frames
+    out = np.zeros(max(n, 1), np.float32)
+    f32 = ctypes.POINTER(ctypes.c_float)
+    got = lib().or_audio_to_mono16k(s.ctypes.data_as(f32), frames, channels, rate, out.ctypes.data_as(f32))
+    return out[:got]
 
 
 def audio_sinusoid(position: int, width: int) -> np.ndarray:

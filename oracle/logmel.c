@@ -2,7 +2,9 @@
  * logmel.c -- CPU restatement of the reference's audio front end (AudioFrontEnd,
  * Sources/GemmaEmbed/Audio/AudioPreprocessor.swift:24-251).
  *
- * TEST INFRASTRUCTURE ONLY (see oracle.h): the checker for the CUDA front end.
+ * TEST INFRASTRUCTURE ONLY (see oracle.h): the checker for the CUDA front end.  It also restates
+ * the conversion of decoded PCM to 16 kHz mono (MiniaudioConverter, Audio/MiniaudioConverter.swift:
+ * miniaudio 0.11.25's channel average, linear resampler and 4th-order Butterworth low-pass).
  * This file is compiled with -ffp-contract=off: the reference's butterflies and
  * four-bin mel sums are separate fp32 multiplies and adds in a fixed order, and a
  * fused multiply-add would change their rounding.
@@ -145,4 +147,98 @@ int32_t or_audio_log_mel(const float* samples, int64_t n, int32_t mel_bins, floa
     free(lo);
     free(hi);
     return frames;
+}
+
+/* ---- MiniaudioConverter (Audio/MiniaudioConverter.swift:18-213) */
+
+/* ma_calculate_frame_count_after_resampling (MiniaudioConverter.swift:55-66). */
+uint64_t or_audio_frames_after_resampling(uint32_t rate_out, uint32_t rate_in, uint64_t n) {
+    if (rate_in == 0 || rate_out == 0 || n == 0) return 0;
+    if (rate_in == rate_out) return n;
+    uint64_t out = n * rate_out / rate_in;
+    const uint64_t frac = out * (rate_in / rate_out) / rate_out;
+    if (out * (rate_in % rate_out) + frac <= n) out++;
+    return out;
+}
+
+typedef struct { float b0, b1, b2, a1, a2, r1, r2; } biquad_t;
+
+static double mini_cos(double x) { return sin(3.14159265358979323846 * 0.5 - x); }
+
+/* Biquad.init (MiniaudioConverter.swift:175-192). */
+static void biquad_init(biquad_t* q, uint32_t rate, double cutoff, double qv) {
+    const double w = 2 * 3.14159265358979323846 * cutoff / (double)rate;
+    const double s = sin(w), c = mini_cos(w), a = s / (2 * qv), a0 = 1 + a;
+    q->b0 = (float)(((1 - c) / 2) / a0);
+    q->b1 = (float)((1 - c) / a0);
+    q->b2 = (float)(((1 - c) / 2) / a0);
+    q->a1 = (float)((-2 * c) / a0);
+    q->a2 = (float)((1 - a) / a0);
+    q->r1 = q->r2 = 0.0f;
+}
+
+/* Biquad.process (MiniaudioConverter.swift:198-203): the fused multiply-adds of llama.cpp's build. */
+static float biquad_run(biquad_t* q, float x) {
+    const float y = fmaf(q->b0, x, q->r1);
+    q->r1 = fmaf(q->b1, x, -(q->a1 * y)) + q->r2;
+    q->r2 = fmaf(q->b2, x, -(q->a2 * y));
+    return y;
+}
+
+/* MiniaudioConverter.toMono16k (MiniaudioConverter.swift:23-37): writes
+ * or_audio_frames_after_resampling(16000, rate, frames) samples (frames when rate is 16000). */
+int64_t or_audio_to_mono16k(const float* samples, int64_t frames, int32_t channels, int32_t rate, float* out) {
+    if (channels <= 0 || rate <= 0 || frames <= 0) return 0;
+    float* mono = (float*)malloc(sizeof(float) * (size_t)frames);
+    for (int64_t f = 0; f < frames; f++) {
+        float t = 0.0f;
+        for (int32_t c = 0; c < channels; c++) t += samples[f * channels + c];
+        mono[f] = channels == 1 ? samples[f] : t / (float)channels;
+    }
+    if (rate == 16000) {
+        memcpy(out, mono, sizeof(float) * (size_t)frames);
+        free(mono);
+        return frames;
+    }
+    uint32_t a = (uint32_t)rate, b = 16000;
+    while (b) {
+        const uint32_t t = a % b;
+        a = b;
+        b = t;
+    }
+    const uint32_t rin = (uint32_t)rate / a, rout = 16000 / a;
+    const uint32_t adv_i = rin / rout, adv_f = rin % rout;
+    const int down = rin > rout;
+    const uint32_t lpf_rate = rin > rout ? rin : rout;
+    const double cutoff = (double)(rin < rout ? rin : rout) * 0.5 * 1.0;
+    biquad_t st[2];
+    for (int k = 0; k < 2; k++) biquad_init(&st[k], lpf_rate, cutoff, 1 / (2 * mini_cos((double)(1 + 2 * k) * (3.14159265358979323846 / 8))));
+    const int64_t len = (int64_t)or_audio_frames_after_resampling(16000, (uint32_t)rate, (uint64_t)frames);
+    uint32_t ti = 1, tf = 0;
+    float x0 = 0.0f, x1 = 0.0f;
+    int64_t next = 0, n = 0;
+    while (n < len) {
+        while (ti > 0 && next < frames) {
+            x0 = x1;
+            x1 = mono[next++];
+            if (down) x1 = biquad_run(&st[1], biquad_run(&st[0], x1));
+            ti--;
+        }
+        if (ti > 0) break;
+        const float fa = (float)tf / (float)rout;
+        const float r0 = x1 - x0;
+        const float r1 = r0 * fa;
+        float y = x0 + r1;
+        if (!down) y = biquad_run(&st[1], biquad_run(&st[0], y));
+        out[n++] = y;
+        ti += adv_i;
+        tf += adv_f;
+        if (tf >= rout) {
+            tf -= rout;
+            ti++;
+        }
+    }
+    for (; n < len; n++) out[n] = 0.0f;
+    free(mono);
+    return len;
 }

@@ -130,6 +130,10 @@ void or_audio_tables(int32_t mel_bins, float* hann, float* sin_t, float* cos_t, 
                      int32_t* band_hi, int32_t* bitrev);
 /* AudioFrontEnd.logMel on one chunk of n <= 480000 samples: writes frame_count(n) rows of mel_bins. */
 int32_t or_audio_log_mel(const float* samples, int64_t n, int32_t mel_bins, float* out);
+/* MiniaudioConverter (Audio/MiniaudioConverter.swift): the resampled length, and `frames` frames of
+ * `channels` interleaved samples at `rate` Hz to 16 kHz mono (returns the samples written). */
+uint64_t or_audio_frames_after_resampling(uint32_t rate_out, uint32_t rate_in, uint64_t frames_in);
+int64_t or_audio_to_mono16k(const float* samples, int64_t frames, int32_t channels, int32_t rate, float* out);
 
 /* Static pieces, exposed for unit tests. */
 void or_matmul(const float* x, int64_t m, int64_t k, const float* w, int64_t n, float* y);

@@ -183,7 +183,7 @@ def test_audio_options_and_errors(ge, synth, audio_model):
         model.embed_audios([c], ge.AudioEmbedOptions(max_tokens=28))
     assert e.value.case == "invalidOptions"
     assert model.embed_audios([c], ge.AudioEmbedOptions(max_tokens=29))[0].token_count == 29
-    for bad_clip in (np.zeros(1, np.float32), np.zeros(0, np.float32), (c, 44100, 1), (np.repeat(c, 2), 16000, 2)):
+    for bad_clip in (np.zeros(1, np.float32), np.zeros(0, np.float32), (c, 0, 1), (c, 16000, 0)):
         with pytest.raises(ge.GemmaEmbedError) as e:
             model.embed_audios([bad_clip])
         assert e.value.case == "audioDecoding"
@@ -312,3 +312,19 @@ def test_device_forwards_back_to_back(ge, audio_model):
         assert np.array_equal(e.vector, row)
     for e, row in zip(want_b, ob.cpu().numpy()):
         assert np.array_equal(e.vector, row)
+
+
+def test_other_rates_and_channels_are_converted(ge, audio_model):
+    """Clips at other rates and channel counts embed as their 16 kHz mono conversion
+    (MiniaudioConverter, restated in the oracle) does, bit for bit."""
+    model = audio_model[0]
+    rng = np.random.default_rng(8)
+    inputs = [(rng.uniform(-0.5, 0.5, 2 * 22050).astype(np.float32), 44100, 2),
+              (rng.uniform(-0.5, 0.5, 12000).astype(np.float32), 8000, 1),
+              (rng.uniform(-0.5, 0.5, 4 * 24000).astype(np.float32), 48000, 4)]
+    got = model.embed_audios(inputs, ge.AudioEmbedOptions(normalise=False))
+    converted = [B.to_mono16k(x, rate, ch) for x, rate, ch in inputs]
+    want = model.embed_audios(converted, ge.AudioEmbedOptions(normalise=False))
+    for g, w, c in zip(got, want, converted):
+        assert g.token_count == w.token_count == B.audio_token_count(len(c)) + 4
+        assert g.vector.tobytes() == w.vector.tobytes()
