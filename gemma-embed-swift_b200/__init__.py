@@ -14,6 +14,7 @@ the task prefix of `EmbedOptions.task`) or pre-tokenised lists of token ids.
 from __future__ import annotations
 
 import ctypes
+import os
 from dataclasses import dataclass, field
 from typing import Callable, Optional, Sequence
 
@@ -22,7 +23,7 @@ import numpy as np
 from . import _lib
 
 __all__ = ["EmbeddingModel", "EmbedOptions", "LoadOptions", "ImageEmbedOptions", "MultimodalEmbedOptions", "AudioEmbedOptions",
-           "audio_tokens", "audio_to_mono16k", "Embedding",
+           "AudioInput", "audio_tokens", "audio_to_mono16k", "decode_wav", "Embedding",
            "EmbeddingProgress", "ModelInfo", "GemmaEmbedError", "TaskPrefix", "Tokenizer", "ALLOWED_DIMENSIONS"]
 
 ALLOWED_DIMENSIONS = (768, 512, 256, 128)
@@ -280,29 +281,98 @@ def audio_tokens(samples: int) -> int:
     return int(_lib.lib().ge_audio_tokens(int(samples)))
 
 
+class AudioInput:
+    """A sound to embed (AudioInput, Audio/AudioInput.swift:6-14): WAV bytes (`data`), a WAV file
+    (`url`) or PCM samples (`samples`).  The library decodes WAV itself as dr_wav does; other
+    containers, which the reference hands to AVFoundation, must be decoded to samples first."""
+
+    def __init__(self, kind: str, value, sample_rate: int = AUDIO_SAMPLE_RATE, channels: int = 1):
+        self.kind, self.value, self.sample_rate, self.channels = kind, value, sample_rate, channels
+
+    @classmethod
+    def data(cls, data: bytes) -> "AudioInput":
+        return cls("data", bytes(data))
+
+    @classmethod
+    def url(cls, path) -> "AudioInput":
+        return cls("url", os.fspath(path))
+
+    @classmethod
+    def samples(cls, samples, sample_rate: int, channels: int = 1) -> "AudioInput":
+        return cls("samples", samples, sample_rate, channels)
+
+
+def decode_wav(data: bytes):
+    """WAVDecoder.decode (Audio/WAVDecoder.swift:29-84): the interleaved float32 samples of a
+    RIFF/WAVE file (frames x channels, flattened), its sample rate and its channel count."""
+    L = _lib.lib()
+    buf = (ctypes.c_uint8 * max(len(data), 1)).from_buffer_copy(bytes(data) or b"\0")
+    frames, rate, ch = ctypes.c_int64(0), ctypes.c_int32(0), ctypes.c_int32(0)
+    refs = (ctypes.byref(frames), ctypes.byref(rate), ctypes.byref(ch))
+    rc = L.ge_audio_decode_wav(buf, len(data), None, 0, *refs)
+    if rc != 0:
+        raise GemmaEmbedError(rc, (L.ge_last_error(None) or b"").decode())
+    out = np.zeros(max(frames.value * ch.value, 1), np.float32)
+    _check(L.ge_audio_decode_wav(buf, len(data), _ptr(out, ctypes.c_float), out.size, *refs), None)
+    return out[:frames.value * ch.value], rate.value, ch.value
+
+
 def audio_to_mono16k(samples, sample_rate: int = AUDIO_SAMPLE_RATE, channels: int = 1) -> np.ndarray:
-    """MiniaudioConverter.toMono16k (Audio/MiniaudioConverter.swift:23-37): interleaved float
-    samples at any rate and channel count as the 16 kHz mono samples the audio encoder reads."""
-    c, keep = _audios([(samples, sample_rate, channels)])
+    """AudioDecoder.decode (Audio/AudioDecoder.swift:17-41) without the embedding: interleaved
+    float samples at any rate and channel count (or an AudioInput) as the 16 kHz mono samples the
+    audio encoder reads, converted as MiniaudioConverter.toMono16k
+    (Audio/MiniaudioConverter.swift:23-37) converts them."""
+    clip = samples if isinstance(samples, AudioInput) else (samples, sample_rate, channels)
+    c, keep = _audios([clip])
     n = ctypes.c_int64(0)
     L = _lib.lib()
     if L.ge_audio_convert(c, None, 0, ctypes.byref(n)) != 0:
-        raise GemmaEmbedError(16, "audioDecoding: " + (L.ge_last_error(None) or b"").decode())
+        raise GemmaEmbedError(16, (L.ge_last_error(None) or b"").decode())
     out = np.zeros(max(n.value, 1), np.float32)
     _check(L.ge_audio_convert(c, _ptr(out, ctypes.c_float), n.value, ctypes.byref(n)), None)
     return out[:n.value]
 
 
+def _read_audio_file(path: str):
+    """AudioDecoder.decode's `.url` case (Audio/AudioDecoder.swift:19-26): a WAV file's samples,
+    with the path in front of the reason when it cannot be read or decoded."""
+    try:
+        with open(path, "rb") as f:
+            data = f.read()
+    except OSError:
+        raise GemmaEmbedError(16, f"cannot decode audio: {path} is not readable") from None
+    if not (len(data) >= 12 and data[:4] == b"RIFF" and data[8:12] == b"WAVE"):
+        raise GemmaEmbedError(16, f"cannot decode audio: {path}: not a WAV file; other containers (MP3, M4A, "
+                                  "AIFF, CAF, FLAC) must be decoded to samples by the caller")
+    try:
+        return decode_wav(data)
+    except GemmaEmbedError as e:
+        raise GemmaEmbedError(e.code, e.message.replace("cannot decode audio: ", f"cannot decode audio: {path}: ", 1)) from None
+
+
 def _audios(clips):
-    """ge_audio views of 16 kHz mono float32 sample arrays (kept alive by the returned list).  A
-    clip may also be given as (samples, sample_rate, channels)."""
+    """ge_audio views of the clips (kept alive by the returned list): 16 kHz mono float32 sample
+    arrays, (samples, sample_rate, channels) tuples or AudioInput values."""
     c = (_lib.GeAudio * max(len(clips), 1))()
     keep = []
     for i, clip in enumerate(clips):
         rate, channels = AUDIO_SAMPLE_RATE, 1
-        if isinstance(clip, tuple):
+        if isinstance(clip, AudioInput):
+            if clip.kind == "data":
+                b = (ctypes.c_uint8 * max(len(clip.value), 1)).from_buffer_copy(clip.value or b"\0")
+                keep.append(b)
+                c[i].wav = ctypes.cast(b, ctypes.POINTER(ctypes.c_uint8))
+                c[i].wav_bytes = len(clip.value)
+                continue
+            if clip.kind == "url":
+                clip, rate, channels = _read_audio_file(clip.value)
+            else:
+                clip, rate, channels = clip.value, clip.sample_rate, clip.channels
+        elif isinstance(clip, tuple):
             clip, rate, channels = clip
         a = np.ascontiguousarray(np.asarray(clip, dtype=np.float32).reshape(-1))
+        if channels > 0 and a.size % int(channels):
+            raise GemmaEmbedError(16, f"cannot decode audio: {a.size} samples do not split over {int(channels)} channels")
         keep.append(a)
         c[i].samples = a.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
         c[i].count = a.size // max(int(channels), 1) if channels > 0 else a.size
@@ -591,8 +661,8 @@ class EmbeddingModel:
                          progress: Optional[Callable[[EmbeddingProgress], Optional[bool]]] = None) -> list:
         """embed(_ inputs: [MultimodalInput], options:progress:) (MultimodalEmbedding.swift:100-206).
         Each input is a list of parts in reading order: str (text), a height x width x 3 uint8
-        array (an image), or a 1-D float32 array of 16 kHz mono samples or a (samples, rate,
-        channels) tuple (a clip)."""
+        array (an image), or a 1-D float32 array of 16 kHz mono samples, a (samples, rate,
+        channels) tuple or an AudioInput (a clip)."""
         options = options or MultimodalEmbedOptions()
         if options.batch_size is not None and options.batch_size < 1:
             raise GemmaEmbedError(9, "invalid options: batchSize must be at least 1")
@@ -605,7 +675,7 @@ class EmbeddingModel:
                     data = part.encode() if isinstance(part, str) else bytes(part)
                     keep.append(data)
                     cp[k].kind, cp[k].text, cp[k].text_len = 0, data, len(data)
-                elif isinstance(part, tuple) or np.asarray(part).ndim == 1:
+                elif isinstance(part, (tuple, AudioInput)) or np.asarray(part).ndim == 1:
                     c, arrs = _audios([part])
                     arrays.append(arrs)
                     cp[k].kind = 2
@@ -637,12 +707,12 @@ class EmbeddingModel:
 
     def embed_audios(self, clips, options: Optional[AudioEmbedOptions] = None,
                      progress: Optional[Callable[[EmbeddingProgress], Optional[bool]]] = None) -> list:
-        """embed(audios:options:progress:) (AudioEmbedding.swift:17-33) over PCM clips: 16 kHz mono
-        float32 arrays, or (interleaved samples, rate, channels) tuples at any rate and channel
-        count (converted as audio_to_mono16k does); a single 1-D array embeds one clip and returns
-        one Embedding."""
+        """embed(audios:options:progress:) (AudioEmbedding.swift:17-33) over clips: 16 kHz mono
+        float32 arrays, (interleaved samples, rate, channels) tuples at any rate and channel count
+        (converted as audio_to_mono16k does) or AudioInput values (WAV bytes or files); a single
+        1-D array or AudioInput embeds one clip and returns one Embedding."""
         options = options or AudioEmbedOptions()
-        single = isinstance(clips, np.ndarray) and clips.ndim == 1
+        single = (isinstance(clips, np.ndarray) and clips.ndim == 1) or isinstance(clips, AudioInput)
         items = [clips] if single else list(clips)
         c, keep = _audios(items)
         n = len(items)

@@ -27,7 +27,7 @@ class GeLoadOpts(ctypes.Structure):
 
 class GeAudio(ctypes.Structure):
     _fields_ = [("samples", ctypes.POINTER(ctypes.c_float)), ("count", ctypes.c_int64), ("sample_rate", ctypes.c_int32),
-                ("channels", ctypes.c_int32)]
+                ("channels", ctypes.c_int32), ("wav", ctypes.POINTER(ctypes.c_uint8)), ("wav_bytes", ctypes.c_int64)]
 
 
 class GeAudioOpts(ctypes.Structure):
@@ -133,6 +133,8 @@ SIGNATURES = {
     "ge_audio_opts_default": ([P(GeAudioOpts)], None),
     "ge_audio_tokens": ([ctypes.c_int64], ctypes.c_int64),
     "ge_audio_convert": ([P(GeAudio), f32p, ctypes.c_int64, i64p], ctypes.c_int),
+    "ge_audio_decode_wav": ([ctypes.POINTER(ctypes.c_uint8), ctypes.c_int64, f32p, ctypes.c_int64, i64p,
+                             ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)], ctypes.c_int),
     "ge_embed_audios": ([ctypes.c_void_p, P(GeAudio), ctypes.c_int32, P(GeAudioOpts), f32p, i32p, PROGRESS_FN,
                          ctypes.c_void_p], ctypes.c_int),
     "ge_audio_vectors": ([ctypes.c_void_p, P(GeAudio), ctypes.c_int32, f32p, ctypes.c_int64, i32p], ctypes.c_int),

@@ -15,6 +15,7 @@
 #include "gemma_embed.h"
 #include "model.hpp"
 #include "multimodal.hpp"
+#include "wav.hpp"
 
 namespace ge {
 int load_model(ge_model* m, const char* path, const ge_load_opts* opts);
@@ -314,8 +315,16 @@ int audios_on_device(ge_model* m, ge::Device& d, const ge::PreparedAudio* const*
     return ge::run_forward(m, d, a);
 }
 
-// AudioDecoder.decode's checks on `.samples` inputs (Audio/AudioDecoder.swift:33-38, 48-51).
+// AudioDecoder.decode's checks on its inputs (Audio/AudioDecoder.swift:28-38, 48-51): WAV bytes
+// must be a RIFF/WAVE file (the library decodes no other container); samples need a positive
+// channel count and rate and at least one sample.
 std::string check_audio_input(const ge_audio& c) {
+    if (c.wav) {
+        if (!ge::is_wav(c.wav, c.wav_bytes))
+            return "the bytes are not a WAV file; other containers (MP3, M4A, AIFF, CAF, FLAC) must be decoded to "
+                   "samples by the caller";
+        return std::string();
+    }
     if (c.channels <= 0) return "channel count must be positive";
     if (c.sample_rate <= 0) return "sample rate must be positive";
     if (c.count < 0 || (c.count > 0 && !c.samples)) return "the samples are missing";
@@ -323,9 +332,41 @@ std::string check_audio_input(const ge_audio& c) {
     return std::string();
 }
 
-// AudioEmbedding.prepare (AudioEmbedding.swift:78-101) on PCM inputs: decoded samples at any rate
-// and channel count go to 16 kHz mono (MiniaudioConverter) on host threads; then at least one
-// frame, and at most max_rows rows with the 4 frame rows.
+// The 16 kHz mono samples of one clip (AudioDecoder.decode, Audio/AudioDecoder.swift:17-41): WAV
+// bytes are decoded first; 16 kHz mono samples are used in place, anything else is converted
+// (MiniaudioConverter).  An empty string, or the reason the clip cannot be decoded.
+std::string decode_clip(const ge_audio& c, ge::PreparedAudio& p) {
+    const float* samples = c.samples;
+    int64_t frames = c.count;
+    int channels = c.channels, rate = c.sample_rate;
+    ge::DecodedWav w;
+    if (c.wav) {
+        std::string why;
+        if (!ge::decode_wav(c.wav, c.wav_bytes, w, why)) return why;
+        channels = w.channels;
+        rate = w.sample_rate;
+        frames = int64_t(w.samples.size()) / channels;
+        samples = w.samples.data();
+        if (frames == 0) return "audio has no samples";
+    }
+    if (rate == 16000 && channels == 1) {
+        if (c.wav) {
+            p.converted = std::move(w.samples);
+            samples = p.converted.data();
+        }
+        p.samples = samples;
+        p.count = frames;
+    } else {
+        ge::audio_to_mono_16k(samples, frames, channels, rate, p.converted);
+        p.samples = p.converted.data();
+        p.count = int64_t(p.converted.size());
+    }
+    return std::string();
+}
+
+// AudioEmbedding.prepare (AudioEmbedding.swift:78-101): every clip decoded (WAV bytes) and
+// converted to 16 kHz mono (MiniaudioConverter) on host threads; then at least one frame, and at
+// most max_rows rows with the 4 frame rows.  The first failing clip, in order, names the error.
 int prepare_audios(ge_model* m, const ge_audio* clips, int32_t count, int max_rows, std::vector<ge::PreparedAudio>& out) {
     out.assign(size_t(count), ge::PreparedAudio());
     for (int32_t i = 0; i < count; i++) {
@@ -334,26 +375,20 @@ int prepare_audios(ge_model* m, const ge_audio* clips, int32_t count, int max_ro
             return ge::set_error(m, GE_ERR_AUDIO_DECODING, "cannot decode audio: audio " + std::to_string(i) + ": " + why);
     }
     {
+        std::vector<std::string> errors(static_cast<size_t>(count));
         std::atomic<int32_t> next{0};
         auto work = [&]() {
-            for (int32_t i = next++; i < count; i = next++) {
-                const ge_audio& c = clips[i];
-                ge::PreparedAudio& p = out[size_t(i)];
-                if (c.sample_rate == 16000 && c.channels == 1) {
-                    p.samples = c.samples;
-                    p.count = c.count;
-                } else {
-                    ge::audio_to_mono_16k(c.samples, c.count, c.channels, c.sample_rate, p.converted);
-                    p.samples = p.converted.data();
-                    p.count = int64_t(p.converted.size());
-                }
-            }
+            for (int32_t i = next++; i < count; i = next++) errors[size_t(i)] = decode_clip(clips[i], out[size_t(i)]);
         };
         const int nt = int(std::min<int64_t>({int64_t(std::max(1u, std::thread::hardware_concurrency())), int64_t(count), 16}));
         std::vector<std::thread> th;
         for (int t = 1; t < nt; t++) th.emplace_back(work);
         work();
         for (auto& t : th) t.join();
+        for (int32_t i = 0; i < count; i++)
+            if (!errors[size_t(i)].empty())
+                return ge::set_error(m, GE_ERR_AUDIO_DECODING,
+                                     "cannot decode audio: audio " + std::to_string(i) + ": " + errors[size_t(i)]);
     }
     for (int32_t i = 0; i < count; i++) {
         const ge::PreparedAudio& c = out[size_t(i)];
@@ -1020,16 +1055,34 @@ int ge_audio_convert(const ge_audio* clip, float* out, int64_t cap, int64_t* cou
         t_last_error = "cannot decode audio: " + why;
         return GE_ERR_AUDIO_DECODING;
     }
-    std::vector<float> v;
-    const float* src = clip->samples;
-    int64_t n = clip->count;
-    if (clip->sample_rate != 16000 || clip->channels != 1) {
-        ge::audio_to_mono_16k(clip->samples, clip->count, clip->channels, clip->sample_rate, v);
-        src = v.data();
-        n = int64_t(v.size());
+    ge::PreparedAudio p;
+    const std::string reason = decode_clip(*clip, p);
+    if (!reason.empty()) {
+        t_last_error = "cannot decode audio: " + reason;
+        return GE_ERR_AUDIO_DECODING;
     }
-    *count = n;
-    if (cap > 0 && n > 0) memcpy(out, src, size_t(std::min(cap, n)) * sizeof(float));
+    *count = p.count;
+    if (cap > 0 && p.count > 0) memcpy(out, p.samples, size_t(std::min(cap, p.count)) * sizeof(float));
+    return GE_OK;
+}
+
+int ge_audio_decode_wav(const uint8_t* bytes, int64_t length, float* out, int64_t cap, int64_t* frames,
+                        int32_t* sample_rate, int32_t* channels) {
+    if (!bytes || length < 0 || !frames || !sample_rate || !channels || cap < 0 || (cap > 0 && !out)) {
+        t_last_error = "invalid options: NULL bytes or outputs";
+        return GE_ERR_INVALID_OPTIONS;
+    }
+    ge::DecodedWav w;
+    std::string why;
+    if (!ge::decode_wav(bytes, length, w, why)) {
+        t_last_error = "cannot decode audio: " + why;
+        return GE_ERR_AUDIO_DECODING;
+    }
+    const int64_t n = int64_t(w.samples.size());
+    *frames = n / w.channels;
+    *sample_rate = w.sample_rate;
+    *channels = w.channels;
+    if (cap > 0 && n > 0) memcpy(out, w.samples.data(), size_t(std::min(cap, n)) * sizeof(float));
     return GE_OK;
 }
 
@@ -1184,10 +1237,10 @@ int ge_audio_forward_device(ge_model* m, int32_t device_ordinal, const float* d_
     std::vector<const ge::PreparedAudio*> ptrs;
     int64_t off = 0;
     for (int32_t i = 0; i < count; i++) {
-        if (clips[i].sample_rate != 16000 || clips[i].channels != 1 || clips[i].count < ge::kAudioMinimumSamples ||
+        if (clips[i].wav || clips[i].sample_rate != 16000 || clips[i].channels != 1 || clips[i].count < ge::kAudioMinimumSamples ||
             clips[i].count % ge::kAudioChunkSamples == 1)
             return ge::set_error(m, GE_ERR_AUDIO_DECODING, "cannot decode audio: clip " + std::to_string(i) +
-                                                               " is not 16 kHz mono with at least 2 samples in every "
+                                                               " is not 16 kHz mono samples with at least 2 in every "
                                                                "30-second chunk");
         cl[size_t(i)].count = clips[i].count;
         cl[size_t(i)].device_offset = off;

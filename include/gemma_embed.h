@@ -327,18 +327,37 @@ GE_API int ge_image_vectors(ge_model* model, const ge_image* images, int32_t cou
 
 /* ---- Audio (AudioEmbedding.swift, Metal/AudioTower.swift) -------------------------------- */
 
-/* AudioInput.samples (Audio/AudioInput.swift:12): `count` frames of `channels` interleaved PCM
- * samples (count * channels floats) in -1 .. 1 at `sample_rate` Hz.  Clips that are not 16 kHz
- * mono are converted as llama.cpp's miniaudio decoder converts them (channels averaged in order,
- * linear resampler with a 4th-order low-pass; MiniaudioConverter, Audio/MiniaudioConverter.swift);
- * decoding files is the caller's.  A non-positive rate or channel count, or no samples, is
- * GE_ERR_AUDIO_DECODING. */
+/* A sound to embed (AudioInput, Audio/AudioInput.swift:6-14), in one of two forms.
+ *
+ * AudioInput.samples: `count` frames of `channels` interleaved PCM samples (count * channels
+ * floats) in -1 .. 1 at `sample_rate` Hz, with `wav` NULL.
+ *
+ * AudioInput.data with WAV bytes: `wav` points at `wav_bytes` bytes of a RIFF/WAVE file, decoded
+ * as miniaudio's dr_wav decodes it (PCM 8, 16, 24, 32 and 33-64 bit, IEEE float 32 and 64,
+ * WAVE_FORMAT_EXTENSIBLE; WAVDecoder, Audio/WAVDecoder.swift); `samples`, `count`, `sample_rate`
+ * and `channels` are ignored.  Other containers (MP3, M4A, AIFF, CAF, FLAC, which the reference
+ * hands to AVFoundation) are the caller's to decode to samples.
+ *
+ * Clips that are not 16 kHz mono are converted as llama.cpp's miniaudio decoder converts them
+ * (channels averaged in order, linear resampler with a 4th-order low-pass; MiniaudioConverter,
+ * Audio/MiniaudioConverter.swift).  A non-positive rate or channel count, no samples, bytes that
+ * are not a WAV file or a WAV file dr_wav refuses is GE_ERR_AUDIO_DECODING. */
 typedef struct ge_audio {
     const float* samples;
     int64_t count;
     int32_t sample_rate;
     int32_t channels;
+    const uint8_t* wav;
+    int64_t wav_bytes;
 } ge_audio;
+
+/* WAVDecoder.decode (Audio/WAVDecoder.swift:29-84): the interleaved float samples of a RIFF/WAVE
+ * file, before any downmix or resampling.  Writes min(cap, frames * channels) floats to `out` and
+ * the frame count, rate and channel count to the (non-NULL) outputs.  A malformed file is
+ * GE_ERR_AUDIO_DECODING with the reason ("WAV: no data chunk", ...) in ge_last_error(NULL).  Host
+ * code only: needs no model and no GPU. */
+GE_API int ge_audio_decode_wav(const uint8_t* bytes, int64_t length, float* out, int64_t cap, int64_t* frames,
+                               int32_t* sample_rate, int32_t* channels);
 
 /* AudioEmbedOptions (EmbedOptions.swift:91-114). */
 typedef struct ge_audio_opts {
@@ -350,9 +369,10 @@ typedef struct ge_audio_opts {
 
 GE_API void ge_audio_opts_default(ge_audio_opts* opts);
 
-/* MiniaudioConverter.toMono16k (Audio/MiniaudioConverter.swift:23-37): the 16 kHz mono samples the
- * audio encoder reads for `clip`; writes min(cap, n) of them to `out` and n to `*count`.  Host code
- * only: needs no model and no GPU. */
+/* AudioDecoder.decode (Audio/AudioDecoder.swift:17-41): the 16 kHz mono samples the audio encoder
+ * reads for `clip` (WAV bytes decoded first, then MiniaudioConverter.toMono16k,
+ * Audio/MiniaudioConverter.swift:23-37); writes min(cap, n) of them to `out` and n to `*count`.
+ * Host code only: needs no model and no GPU. */
 GE_API int ge_audio_convert(const ge_audio* clip, float* out, int64_t cap, int64_t* count);
 
 /* AudioFrontEnd.tokenCount(samples:) (Audio/AudioPreprocessor.swift:86-95): the rows a clip of
@@ -377,7 +397,7 @@ GE_API int ge_audio_vectors(ge_model* model, const ge_audio* clips, int32_t coun
 
 /* The audio forward (audio and text towers) over device-resident samples on the caller's
  * stream, without synchronising: `d_pcm` holds the clips' 16 kHz mono samples back to back
- * (clips[i].count each; clips[i].samples is ignored); d_pooled receives [count]
+ * (clips[i].count each; clips[i].samples is ignored, clips[i].wav must be NULL); d_pooled receives [count]
  * [output_dimensions] pooled, unnormalised fp32 rows.  NULL stream: the legacy default stream. */
 GE_API int ge_audio_forward_device(ge_model* model, int32_t device_ordinal, const float* d_pcm, const ge_audio* clips,
                                    int32_t count, float* d_pooled, void* stream);
@@ -398,7 +418,7 @@ typedef struct ge_part {
     const char* text;  /* GE_PART_TEXT: text_len bytes of UTF-8 */
     int64_t text_len;
     ge_image image;    /* GE_PART_IMAGE: decoded pixels */
-    ge_audio audio;    /* GE_PART_AUDIO: 16 kHz mono samples */
+    ge_audio audio;    /* GE_PART_AUDIO: samples at any rate or WAV bytes */
 } ge_part;
 
 /* MultimodalInput (MultimodalEmbedding.swift:5-24): text, images and clips in reading order. */

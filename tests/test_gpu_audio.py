@@ -328,3 +328,47 @@ def test_other_rates_and_channels_are_converted(ge, audio_model):
     for g, w, c in zip(got, want, converted):
         assert g.token_count == w.token_count == B.audio_token_count(len(c)) + 4
         assert g.vector.tobytes() == w.vector.tobytes()
+
+
+def _wav(pcm16: np.ndarray, rate: int, channels: int) -> bytes:
+    """A plain 16-bit PCM RIFF/WAVE file around interleaved int16 samples."""
+    import struct
+    payload = np.asarray(pcm16, "<i2").tobytes()
+    fmt = struct.pack("<HHIIHH", 1, channels, rate, rate * 2 * channels, 2 * channels, 16)
+    body = b"fmt " + struct.pack("<I", 16) + fmt + b"data" + struct.pack("<I", len(payload)) + payload
+    return b"RIFF" + struct.pack("<I", 4 + len(body)) + b"WAVE" + body
+
+
+def test_wav_inputs_embed_as_their_decoded_samples(ge, audio_model, tmp_path):
+    """AudioInput.data and .url (Audio/AudioInput.swift:9-11): WAV bytes and files embed exactly
+    as their samples, decoded as dr_wav decodes them (oracle/wav.py), do; a batch mixing the
+    forms is bit-identical to each form alone, and a malformed file names its clip."""
+    from oracle import wav as W
+    model = audio_model[0]
+    rng = np.random.default_rng(12)
+    wavs = [_wav(rng.integers(-20000, 20000, 2 * 22050, dtype=np.int16), 22050, 2),
+            _wav(rng.integers(-20000, 20000, 40000, dtype=np.int16), 16000, 1),
+            _wav(rng.integers(-20000, 20000, 3 * 16000, dtype=np.int16), 48000, 1)]
+    path = tmp_path / "clip.wav"
+    path.write_bytes(wavs[0])
+    opts = ge.AudioEmbedOptions(normalise=False)
+    got = model.embed_audios([ge.AudioInput.data(w) for w in wavs], opts)
+    decoded = [W.decode(w) for w in wavs]
+    want = model.embed_audios([(x, rate, ch) for x, rate, ch in decoded], opts)
+    for g, w, (x, rate, ch) in zip(got, want, decoded):
+        assert g.token_count == w.token_count == B.audio_token_count(len(B.to_mono16k(x, rate, ch))) + 4
+        assert g.vector.tobytes() == w.vector.tobytes()
+    from_url = model.embed_audios(ge.AudioInput.url(path), opts)
+    assert from_url.vector.tobytes() == got[0].vector.tobytes()
+    mixed = model.embed_audios([decoded[1][0], ge.AudioInput.data(wavs[0]), ge.AudioInput.url(path)], opts)
+    assert mixed[0].vector.tobytes() == got[1].vector.tobytes()
+    assert mixed[1].vector.tobytes() == got[0].vector.tobytes() == mixed[2].vector.tobytes()
+    only = model.embed_multimodal([[ge.AudioInput.data(wavs[2])]], ge.MultimodalEmbedOptions(task="", normalise=False))[0]
+    assert only.vector.tobytes() == got[2].vector.tobytes()
+    bad = wavs[1][:36] + b"junk" + wavs[1][40:]
+    with pytest.raises(ge.GemmaEmbedError) as e:
+        model.embed_audios([ge.AudioInput.data(wavs[0]), ge.AudioInput.data(bad)], opts)
+    assert e.value.message == "cannot decode audio: audio 1: WAV: no data chunk"
+    with pytest.raises(ge.GemmaEmbedError) as e:
+        model.embed_audios([ge.AudioInput.data(b"ID3 an mp3 file, say")], opts)
+    assert e.value.case == "audioDecoding" and "not a WAV file" in e.value.message
