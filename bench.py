@@ -52,6 +52,8 @@ def args_():
     p.add_argument("--profile-reps", type=int, default=5)
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="bound of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--fused-qkv", choices=["on", "off"], default="off",
+                   help="q/k/v norms and RoPE in the q/k/v projection's epilogue (GE_LOAD_FUSED_QKV)")
     return p.parse_args()
 
 
@@ -216,7 +218,8 @@ def main():
         path = synth.model_path(a.arch, seed=0)
     # One packed batch per step: the budget covers the whole config-2 batch (BASELINE: "packed by
     # token count, about 16k tokens per batch"; the reference default of 8192 would cut it in three).
-    model = ge.EmbeddingModel.load(path, ge.LoadOptions(devices=(local,), batch_token_budget=BATCH_BUDGET))
+    model = ge.EmbeddingModel.load(path, ge.LoadOptions(devices=(local,), batch_token_budget=BATCH_BUDGET,
+                                                        fused_qkv=a.fused_qkv == "on"))
     seqs = synth.config_sequences(a.config, seed=rank)
     tokens, positions, ranges = ge.pack(seqs)
     ntok, nseq = len(tokens), len(ranges)
@@ -333,7 +336,7 @@ def main():
                 "dtype": "f16", "data": "synthetic",
                 "config": {"workload": f"config {a.config}", "arch": a.arch, "tokens_per_rank": ntok,
                            "texts_per_rank": nseq, "global_batch_tokens": tok_sum // a.steps,
-                           "parallelism": f"dp{world}",
+                           "parallelism": f"dp{world}", "fused_qkv": a.fused_qkv == "on",
                            "l2": "working set larger than L2 (fp16 weights 203 MB + ~0.5 GB of activations per step)"},
                 "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "api": "ge_embed_tokens (EmbeddingModel.embed), 256-d normalised output"},

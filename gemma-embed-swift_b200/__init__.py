@@ -39,6 +39,7 @@ LOAD_NO_GRAPHS = 1
 LOAD_Q8_ONLY = 2
 LOAD_NO_PDL = 4
 LOAD_FUSED_RESIDUAL = 8
+LOAD_FUSED_QKV = 16
 
 
 class GemmaEmbedError(RuntimeError):
@@ -190,6 +191,7 @@ class LoadOptions:
     q8_only: bool = False
     programmatic_launch: bool = True  # overlap each kernel's set-up with its predecessor's tail
     fused_residual: bool = False  # run each residual step inside the projection before it
+    fused_qkv: bool = False  # run the q/k/v norms and RoPE inside the q/k/v projection (head dim 256)
     image_encoder: Optional[str] = None  # LoadOptions.imageEncoder: the mmproj GGUF
     image_patch_budget: int = 4096       # ImageEmbedOptions.patchBudget: patches per image batch
     audio_encoder: Optional[str] = None  # LoadOptions.audioEncoder: the mmproj GGUF with a gemma4a tower
@@ -456,7 +458,8 @@ class EmbeddingModel:
         o.batch_token_budget = int(options.batch_token_budget)
         o.flags = ((0 if options.use_graphs else LOAD_NO_GRAPHS) | (LOAD_Q8_ONLY if options.q8_only else 0)
                    | (0 if options.programmatic_launch else LOAD_NO_PDL)
-                   | (LOAD_FUSED_RESIDUAL if options.fused_residual else 0))
+                   | (LOAD_FUSED_RESIDUAL if options.fused_residual else 0)
+                   | (LOAD_FUSED_QKV if options.fused_qkv else 0))
         o.image_encoder_path = str(options.image_encoder).encode() if options.image_encoder else None
         o.image_patch_budget = int(options.image_patch_budget)
         o.audio_encoder_path = str(options.audio_encoder).encode() if options.audio_encoder else None

@@ -630,13 +630,15 @@ static cudaError_t launch_simt(const AttnLaunch& a, cudaStream_t stream) {
 // Q as [rows][heads][hd] with boxes of 64 dims x G heads x T tokens (one work item's tile,
 // row t * G + g); K and V as [rows][kv_heads * hd] with boxes of 64 dims x 64 keys.
 bool encode_attention_maps(AttnMaps& m, const __half* q, const __half* k, const __half* v, int rows, int heads, int kvh,
-                           int hd) {
+                           int hd, int row_stride) {
     const int group = heads / kvh;
     if (hd != kTcHd || heads % kvh || group > kTcQ) return false;
+    const uint64_t qs = row_stride ? uint64_t(row_stride) : uint64_t(heads) * hd;
+    const uint64_t kvs = row_stride ? uint64_t(row_stride) : uint64_t(kvh) * hd;
     return encode_fp16_map_3d(&m.q, q, uint64_t(hd), uint64_t(heads), uint64_t(rows), 64, uint32_t(group),
-                              uint32_t(attention_tokens_per_item(group))) &&
-           encode_fp16_map(&m.k, k, uint64_t(kvh) * hd, rows, 64, kTcKeys) &&
-           encode_fp16_map(&m.v, v, uint64_t(kvh) * hd, rows, 64, kTcKeys);
+                              uint32_t(attention_tokens_per_item(group)), qs) &&
+           encode_fp16_map(&m.k, k, uint64_t(kvh) * hd, rows, 64, kTcKeys, kvs) &&
+           encode_fp16_map(&m.v, v, uint64_t(kvh) * hd, rows, 64, kTcKeys, kvs);
 }
 
 cudaError_t launch_attention(const AttnLaunch& a, cudaStream_t stream) {

@@ -70,6 +70,12 @@ struct GemmParams {
     int store_h, store_y;
     // clamp epilogues (aux holds the optional bias)
     float lo1, hi1, lo2, hi2;
+    // EPI_QKV (eps above)
+    const int32_t* pos;
+    const float* rope;
+    const float* qw;
+    const float* kw;
+    int ntok, heads, kvh;
 };
 
 // EPI_RESIDUAL output maps: the next norm's fp16 (boxes of 32 rows x 64) and fp32 (32 x 32)
@@ -534,7 +540,73 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
             const long row = y + lane;
             const uint32_t taddr = tmem + (uint32_t(warp * 32) << 16) + uint32_t(acc * BN);
             uint32_t packed[32];
-            if (EPI == EPI_F32 || EPI == EPI_CLAMP_F32) {
+            if constexpr (EPI == EPI_QKV) {
+                // One tile is one head slot of 256 columns.  Pass 1: the sum of squares of the
+                // fp16-rounded projection; pass 2: columns j and j + 128 (NeoX rotation partners)
+                // together, 64 of each per step, normalised, weighted, rotated and stored.
+                static_assert(BN == 256, "EPI_QKV tiles are one 256-wide head slot");
+                const int slot = n0 / BN;
+                const bool live = row < p.ntok;
+                const float* w = slot < p.heads ? p.qw : (slot < p.heads + p.kvh ? p.kw : nullptr);
+                float ss = 0.f;
+#pragma unroll 1
+                for (int c = 0; c < 2; c++) {
+                    uint32_t r[128];
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        tmem_ld32(taddr + uint32_t(c * 128 + q * 32), *reinterpret_cast<uint32_t(*)[32]>(&r[32 * q]));
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int i = 0; i < 128; i++) {
+                        const float v = round_f16(r[i]);
+                        ss += v * v;
+                    }
+                }
+                const float inv = 1.0f / sqrtf(ss / 256.0f + p.eps);
+                // This row's position's (cos, sin) pairs; read row-major, each thread's own
+                // 1 KB row (a pair-major table, coalesced across the warp, measured slower).
+                const float* cs = (w && live) ? p.rope + long(p.pos[row]) * 256 : nullptr;
+#pragma unroll 1
+                for (int c = 0; c < 2; c++) {
+                    uint32_t r[128];
+#pragma unroll
+                    for (int q = 0; q < 2; q++) {
+                        tmem_ld32(taddr + uint32_t(c * 64 + q * 32), *reinterpret_cast<uint32_t(*)[32]>(&r[32 * q]));
+                        tmem_ld32(taddr + uint32_t(128 + c * 64 + q * 32), *reinterpret_cast<uint32_t(*)[32]>(&r[64 + 32 * q]));
+                    }
+                    tmem_wait_ld();
+                    if (c == 1) release(acc);
+                    uint32_t pb[32];
+#pragma unroll
+                    for (int i = 0; i < 64; i += 2) {
+                        const int j = c * 64 + i;  // pair index (column of the first half)
+                        float a0 = round_f16(r[i]) * inv, a1 = round_f16(r[i + 1]) * inv;
+                        float b0 = round_f16(r[64 + i]) * inv, b1 = round_f16(r[64 + i + 1]) * inv;
+                        if (w) {
+                            const float2 wa = *reinterpret_cast<const float2*>(w + j);
+                            const float2 wb = *reinterpret_cast<const float2*>(w + 128 + j);
+                            a0 = a0 * wa.x;
+                            a1 = a1 * wa.y;
+                            b0 = b0 * wb.x;
+                            b1 = b1 * wb.y;
+                        }
+                        if (cs) {
+                            const float4 f = *reinterpret_cast<const float4*>(cs + 2 * j);  // cos j, sin j, cos j+1, sin j+1
+                            const float x0 = a0 * f.x - b0 * f.y, y0 = a0 * f.y + b0 * f.x;
+                            const float x1 = a1 * f.z - b1 * f.w, y1 = a1 * f.w + b1 * f.z;
+                            a0 = x0;
+                            b0 = y0;
+                            a1 = x1;
+                            b1 = y1;
+                        }
+                        if (!live) a0 = a1 = b0 = b1 = 0.f;
+                        packed[i / 2] = pack_half2(a0, a1);
+                        pb[i / 2] = pack_half2(b0, b1);
+                    }
+                    emit(packed, n0 + c * 64, y, &mapC);
+                    emit(pb, n0 + 128 + c * 64, y, &mapC);
+                }
+            } else if (EPI == EPI_F32 || EPI == EPI_CLAMP_F32) {
                 uint32_t r[32];
 #pragma unroll 1
                 for (int c = 0; c < BN / 32; c++) {
@@ -707,11 +779,12 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 static bool encode_2d(CUtensorMap* map, CUtensorMapDataType type, int elem_bytes, void* ptr, uint64_t inner,
-                      uint64_t outer, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+                      uint64_t outer, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz,
+                      uint64_t row_stride = 0) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {inner, outer};
-    cuuint64_t strides[1] = {inner * uint64_t(elem_bytes)};
+    cuuint64_t strides[1] = {(row_stride ? row_stride : inner) * uint64_t(elem_bytes)};
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
     return fn(map, type, 2, ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
@@ -736,17 +809,17 @@ bool encode_weight_maps(DevWeight& w, int bn) {
 }
 
 bool encode_fp16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint32_t box_inner,
-                     uint32_t box_outer) {
+                     uint32_t box_outer, uint64_t row_stride) {
     return encode_2d(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), inner, outer, box_inner, box_outer,
-                     CU_TENSOR_MAP_SWIZZLE_128B);
+                     CU_TENSOR_MAP_SWIZZLE_128B, row_stride);
 }
 
 bool encode_fp16_map_3d(CUtensorMap* map, const void* ptr, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0,
-                        uint32_t b1, uint32_t b2) {
+                        uint32_t b1, uint32_t b2, uint64_t stride2) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[3] = {d0, d1, d2};
-    cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
+    cuuint64_t strides[2] = {d0 * 2, (stride2 ? stride2 : d0 * d1) * 2};
     cuuint32_t box[3] = {b0, b1, b2};
     cuuint32_t estr[3] = {1, 1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
@@ -771,7 +844,8 @@ static cudaError_t configure_epi() {
     if (e == cudaSuccess) e = configure_t<EPI, true, false>();
     if constexpr (EPI != EPI_RESIDUAL) {
         if (e == cudaSuccess) e = configure_t<EPI, false, true>();
-        if (!epi_is_geglu(EPI) && e == cudaSuccess) e = configure_t<EPI, false, false, 128>();
+        if constexpr (!epi_is_geglu(EPI) && EPI != EPI_QKV)
+            if (e == cudaSuccess) e = configure_t<EPI, false, false, 128>();
     }
     return e;
 }
@@ -789,6 +863,7 @@ cudaError_t configure_gemm_kernels() {
     if (e == cudaSuccess) e = configure_epi<EPI_CLAMP_F16>();
     if (e == cudaSuccess) e = configure_epi<EPI_CLAMP_SILU>();
     if (e == cudaSuccess) e = configure_epi<EPI_GLU>();
+    if (e == cudaSuccess) e = configure_epi<EPI_QKV>();
     return e;
 }
 
@@ -845,6 +920,19 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
     p.hi1 = g.clamp_hi;
     p.lo2 = g.act_lo;
     p.hi2 = g.act_hi;
+    if (EPI == EPI_QKV) {
+        if (!g.positions || !g.rope || !g.q_norm || !g.k_norm || g.heads <= 0 || g.kv_heads <= 0 ||
+            g.w->N != (g.heads + 2 * g.kv_heads) * BN || g.ntok > g.m_rows)
+            return cudaErrorInvalidValue;
+        p.pos = g.positions;
+        p.rope = g.rope;
+        p.qw = g.q_norm;
+        p.kw = g.k_norm;
+        p.ntok = g.ntok;
+        p.heads = g.heads;
+        p.kvh = g.kv_heads;
+        p.eps = g.eps;
+    }
     // Weight boxes: kBN rows (map_f16, map_q8) or kBN / 2 rows (CTA pairs, 128-wide tiles).
     const CUtensorMap& mb = Q8 ? g.w->map_q8 : ((PAIR || BN != kBN) ? g.w->map_f16_half : g.w->map_f16);
     CUtensorMap mc;
@@ -906,7 +994,7 @@ static cudaError_t launch_epi(const GemmLaunch& g, cudaStream_t stream, bool q8,
         return launch_t<EPI, false, false>(g, stream);
     } else {
         if (pair) return launch_t<EPI, false, true>(g, stream);
-        if constexpr (!epi_is_geglu(EPI))
+        if constexpr (!epi_is_geglu(EPI) && EPI != EPI_QKV)
             if (narrow) return launch_t<EPI, false, false, 128>(g, stream);
         return launch_t<EPI, false, false>(g, stream);
     }
@@ -935,6 +1023,9 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream) {
     case EPI_CLAMP_F16: return launch_epi<EPI_CLAMP_F16>(g, stream, q8, pair, narrow);
     case EPI_CLAMP_SILU: return launch_epi<EPI_CLAMP_SILU>(g, stream, q8, pair, narrow);
     case EPI_GLU: return launch_epi<EPI_GLU>(g, stream, q8, pair, narrow);
+    case EPI_QKV:
+        if (narrow || g.mode == GEMM_NARROW) return cudaErrorInvalidValue;
+        return launch_epi<EPI_QKV>(g, stream, q8, pair, false);
     case EPI_RESIDUAL:
         if (g.mode == GEMM_PAIR || g.mode == GEMM_NARROW) return cudaErrorInvalidValue;
         return launch_epi<EPI_RESIDUAL>(g, stream, q8, false, false);

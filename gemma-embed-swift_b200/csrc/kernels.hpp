@@ -71,6 +71,12 @@ enum GemmEpilogue : int {
     // Gate/up interleaved as EPI_GEGLU: out = clamp(up) * sigmoid(clamp(gate)) (fp16), the
     // convolution module's GLU over a clipped pointwise linear.
     EPI_GLU = 9,
+    // The fused q/k/v projection of a head-dim-256 layer with the per-head norms and RoPE of
+    // k_qkv_norm_rope in its epilogue: each 256-column tile is one head slot (queries, then keys,
+    // then values); t = fp16(acc), then t * rsqrt(mean(t^2) + eps) * (q_norm or k_norm; values
+    // unweighted), then NeoX RoPE on query and key slots, stored as fp16 in place of the
+    // projection.  Rows at or past ntok are stored as zeros.
+    EPI_QKV = 10,
 };
 __host__ __device__ constexpr bool epi_is_geglu(int epi) {
     return epi == EPI_GEGLU || epi == EPI_GEGLU_QUICK || epi == EPI_GLU;
@@ -135,6 +141,13 @@ struct GemmLaunch {
     float clamp_lo = -3.402823466e38f, clamp_hi = 3.402823466e38f;
     float act_lo = -3.402823466e38f, act_hi = 3.402823466e38f;
     const float* bias = nullptr;
+    // EPI_QKV: token positions, the RoPE table ([position][128 pairs][cos, sin]), the query and
+    // key norm weights (256 each), the live rows and the head counts (eps above).
+    const int32_t* positions = nullptr;
+    const float* rope = nullptr;
+    const float* q_norm = nullptr;
+    const float* k_norm = nullptr;
+    int ntok = 0, heads = 0, kv_heads = 0;
 };
 cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream);
 // Kernel attributes (dynamic shared-memory limits) for the current device; call once per
@@ -316,14 +329,18 @@ cudaError_t configure_attention64();  // part of configure_attention_kernels
 struct AttnMaps {
     CUtensorMap q, k, v;
 };
+// row_stride: elements between consecutive tokens' rows (0: q, k and v are dense buffers of
+// heads * hd and kvh * hd columns; else they are column ranges of one fused projection row).
 bool encode_attention_maps(AttnMaps& m, const __half* q, const __half* k, const __half* v, int rows, int heads, int kvh,
-                           int hd);
-// A 2-D fp16 tensor map with 128-byte swizzle over a row-major [outer][inner] matrix.
+                           int hd, int row_stride = 0);
+// A 2-D fp16 tensor map with 128-byte swizzle over a row-major [outer][inner] matrix whose rows
+// are row_stride elements apart (0: inner).
 bool encode_fp16_map(CUtensorMap* map, const void* ptr, uint64_t inner, uint64_t outer, uint32_t box_inner,
-                     uint32_t box_outer);
-// The same over a dense [d2][d1][d0] array with boxes b0 x b1 x b2.
+                     uint32_t box_outer, uint64_t row_stride = 0);
+// The same over a [d2][d1][d0] array with boxes b0 x b1 x b2; d2 steps are stride2 elements
+// apart (0: d0 * d1).
 bool encode_fp16_map_3d(CUtensorMap* map, const void* ptr, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0,
-                        uint32_t b1, uint32_t b2);
+                        uint32_t b1, uint32_t b2, uint64_t stride2 = 0);
 
 struct AttnLaunch {
     const __half* q;  // [rows][heads * hd]

@@ -64,6 +64,8 @@ struct Workspace {
     DevActivation a_h, a_x16, a_act, a_g;
     std::vector<DevActivation> a_attn;  // one per distinct query width
     std::vector<std::pair<int, AttnMaps>> attn_maps;  // per KV head count, head-dim-256 layers
+    // The same over the fused projection rows of qkv16 (EPI_QKV layers read q, k and v in place).
+    std::vector<std::pair<int, AttnMaps>> attn_maps_fused;
     // Pinned host staging.
     int32_t *h_tokens = nullptr, *h_positions = nullptr;
     uint32_t *h_seqs = nullptr, *h_work = nullptr, *h_chunk_base = nullptr;

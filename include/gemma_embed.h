@@ -79,6 +79,8 @@ typedef struct ge_load_opts {
                                      dependent launch); results are bit-identical either way */
 #define GE_LOAD_FUSED_RESIDUAL 8u /* fuse each residual step into the projection before it (row clusters of
                                      hidden/256 CTAs exchanging row sums through distributed shared memory) */
+#define GE_LOAD_FUSED_QKV 16u     /* run the per-head q/k/v norms and RoPE of head-dim-256 layers in the q/k/v
+                                     projection's epilogue; attention reads q, k and v from its rows in place */
 
 /* EmbedOptions (EmbedOptions.swift:34-56) minus the task prefix, which ge_embed_texts takes
  * as a string (ge_task_prefix). */

@@ -150,14 +150,18 @@ def test_launch_options_do_not_change_results(ge, synth, cuda_device, arch, use_
             assert on.embed_tokens(seqs).tobytes() == off.embed_tokens(seqs).tobytes()
 
 
+@pytest.mark.parametrize("fused", [dict(fused_residual=True), dict(fused_qkv=True),
+                                   dict(fused_residual=True, fused_qkv=True)], ids=["residual", "qkv", "both"])
 @pytest.mark.parametrize("arch", ["gemma-embedding", "gemma-embedding2"])
-def test_fused_residual_forward(ge, synth, oracle, cuda_device, arch):
-    """The residual steps fused into their projections (row clusters, GE_LOAD_FUSED_RESIDUAL):
-    oracle parity at the same cosine bar and bit-identical vectors across batch compositions
-    (small batches take the Q8 path, large ones fp16 weights)."""
+def test_fused_forward(ge, synth, oracle, cuda_device, arch, fused):
+    """The load options that change the kernel sequence: the residual steps fused into their
+    projections (row clusters, GE_LOAD_FUSED_RESIDUAL) and the q/k/v norms and RoPE fused into the
+    q/k/v projection's epilogue (GE_LOAD_FUSED_QKV): oracle parity at the same cosine bar and
+    bit-identical vectors across batch compositions (small batches take the Q8 path, large ones
+    fp16 weights)."""
     path = synth.model_path(arch, seed=1, layers=6, vocab=4096)
     ref = oracle.OracleModel(path)
-    with ge.EmbeddingModel.load(path, ge.LoadOptions(fused_residual=True)) as model:
+    with ge.EmbeddingModel.load(path, ge.LoadOptions(**fused)) as model:
         seqs = synth.random_sequences([1, 64, 300, 700], seed=71, vocab=4096)
         got = model.embed_tokens(seqs)
         for s, g in zip(seqs, got):
