@@ -203,6 +203,7 @@ cudaError_t launch_rmsnorm_rows(const float* x, int rows, int width, float pre, 
 // chunks of rows (partial[chunk_base[s] + k], max_chunks = most chunks of any sequence),
 // then the per-sequence total.  pool_chunks(len) is a sequence's chunk count.
 int pool_chunks(uint32_t len);
+constexpr int kPoolChunkRows = 64;  // rows per partial sum of the mean pool
 cudaError_t launch_mean_pool(const float* y, int width, const uint32_t* seqs, int nseq, int max_chunks,
                              const uint32_t* chunk_base, float* partial, float* pooled, cudaStream_t stream);
 // The same mean in one launch, one block per sequence (sequence ranges on the device only).

@@ -196,7 +196,7 @@ static cudaError_t ensure_workspace(const Config& c, Device& d, int rows, int se
     }
     chk(A(&ws.pooled, size_t(S) * d_));
     chk(A(&ws.chunk_base, size_t(S)));
-    chk(A(&ws.pool_partial, (r / 256 + size_t(S)) * d_));
+    chk(A(&ws.pool_partial, (r / kPoolChunkRows + size_t(S)) * d_));
     chk(H(&ws.h_chunk_base, size_t(S)));
     chk(A(&ws.mid, size_t(S) * std::max(c.dense_head, 1)));
     chk(A(&ws.out, size_t(S) * c.out_dim));
@@ -989,7 +989,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
                 CK(K("dense_head", 2.0 * nseq * D * c.dense_head, double(D) * c.dense_head * 4,
                      [&] { return launch_dense_f32(ws.pooled, nseq, d.dense2, c.dense_head, D, ws.mid, ks); }),
                    "dense head");
-                CK(K("dense_head", 2.0 * nseq * D * c.dense_head, double(D) * c.dense_head * 4,
+                CK(K("dense_head_out", 2.0 * nseq * D * c.dense_head, double(D) * c.dense_head * 4,
                      [&] { return launch_dense_f32(ws.mid, nseq, d.dense3, c.out_dim, c.dense_head, ws.out, ks); }),
                    "dense head");
             } else {

@@ -52,7 +52,7 @@ struct Workspace {
     int cap_rows = 0, cap_seqs = 0, cap_work = 0;
     int32_t *tokens = nullptr, *positions = nullptr;
     uint32_t *seqs = nullptr, *work = nullptr, *chunk_base = nullptr;
-    float* pool_partial = nullptr;  // [rows / 256 + seqs][hidden] partial sums of the mean pool
+    float* pool_partial = nullptr;  // [rows / kPoolChunkRows + seqs][hidden] partial sums of the mean pool
     float *x = nullptr, *y = nullptr, *ple = nullptr;
     __half* o16 = nullptr;  // fp16 output of the o (and, with per-layer inputs, down and per-layer) projections
     __half* d16 = nullptr;  // fp16 output of the down projection, beside o16 until the FFN residual
