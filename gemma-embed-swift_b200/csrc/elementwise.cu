@@ -75,10 +75,83 @@ __global__ void k_embed(const int32_t* __restrict__ tokens, int ntok, int rows, 
     for (int i = lane; i < width; i += 32) hr[i] = __float2half_rn(xr[i] * inv * w[i]);
 }
 
+// k_embed with each lane owning G groups of 8 consecutive elements (group g = lane + 32 k): one
+// 8-byte load of int8 values per group, the row kept in registers for the norm, 32-byte stores
+// of x and 16-byte stores of h.  The same per-element arithmetic as k_embed.
+template <int G>
+__global__ void k_embed_vec(const int32_t* __restrict__ tokens, int ntok, int rows, const int8_t* __restrict__ tq,
+                            const __half* __restrict__ ts, float scale, float* __restrict__ x, __half* __restrict__ x16,
+                            const float* __restrict__ w, float eps, __half* __restrict__ h,
+                            const float* __restrict__ vectors) {
+    constexpr int width = G * 256;
+    pdl_wait();
+    pdl_launch_if_one_wave();
+    const int row = blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    float v[G][8];
+    float ss = 0.f;
+    const long id = row < ntok ? long(tokens[row]) : 0;
+#pragma unroll
+    for (int k = 0; k < G; k++) {
+        const int e0 = 8 * (lane + 32 * k);
+        if (row >= ntok) {
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[k][j] = 0.f;
+        } else if (id < 0) {
+            const float4* vr = reinterpret_cast<const float4*>(vectors + (-id - 1) * width + e0);
+            const float4 a = vr[0], b = vr[1];
+            v[k][0] = a.x; v[k][1] = a.y; v[k][2] = a.z; v[k][3] = a.w;
+            v[k][4] = b.x; v[k][5] = b.y; v[k][6] = b.z; v[k][7] = b.w;
+        } else {
+            const uint2 raw = *reinterpret_cast<const uint2*>(tq + id * width + e0);
+            const float sc = __half2float(ts[id * (width / 32) + (e0 >> 5)]);
+            const int8_t* q = reinterpret_cast<const int8_t*>(&raw);
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[k][j] = (sc * float(q[j])) * scale;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) ss += v[k][j] * v[k][j];
+        float4* xr = reinterpret_cast<float4*>(x + long(row) * width + e0);
+        xr[0] = make_float4(v[k][0], v[k][1], v[k][2], v[k][3]);
+        xr[1] = make_float4(v[k][4], v[k][5], v[k][6], v[k][7]);
+        if (x16) {
+            uint4 o;
+            o.x = pack_half2(v[k][0], v[k][1]);
+            o.y = pack_half2(v[k][2], v[k][3]);
+            o.z = pack_half2(v[k][4], v[k][5]);
+            o.w = pack_half2(v[k][6], v[k][7]);
+            *reinterpret_cast<uint4*>(x16 + long(row) * width + e0) = o;
+        }
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / float(width) + eps);
+#pragma unroll
+    for (int k = 0; k < G; k++) {
+        const int e0 = 8 * (lane + 32 * k);
+        const float4 wa = *reinterpret_cast<const float4*>(w + e0), wb = *reinterpret_cast<const float4*>(w + e0 + 4);
+        const float ww[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) o[j] = row < ntok ? v[k][j] * inv * ww[j] : 0.f;
+        uint4 u;
+        u.x = pack_half2(o[0], o[1]);
+        u.y = pack_half2(o[2], o[3]);
+        u.z = pack_half2(o[4], o[5]);
+        u.w = pack_half2(o[6], o[7]);
+        *reinterpret_cast<uint4*>(h + long(row) * width + e0) = u;
+    }
+}
+
 cudaError_t launch_embed(const int32_t* tokens, int ntok, int rows, const int8_t* table_q, const __half* table_s,
                          int width, float scale, float* x, __half* x16, const float* norm_w, float eps, __half* h,
                          cudaStream_t stream, const float* vectors) {
     if (rows <= 0) return cudaSuccess;
+    if (width == 768) {
+        CK_LAUNCH(launch_kernel(k_embed_vec<3>, dim3((rows + kRowsPerBlock - 1) / kRowsPerBlock), dim3(256), 0, stream,
+                                1, tokens, ntok, rows, table_q, table_s, scale, x, x16, norm_w, eps, h, vectors));
+        return cudaGetLastError();
+    }
     CK_LAUNCH(launch_kernel(k_embed, dim3((rows + kRowsPerBlock - 1) / kRowsPerBlock), dim3(256), 0, stream, 1, tokens,
                             ntok, rows, table_q, table_s, width, scale, x, x16, norm_w, eps, h, vectors));
     return cudaGetLastError();
