@@ -544,15 +544,37 @@ __global__ void k_pool_final(const float* __restrict__ partial, int width, const
                              const uint32_t* __restrict__ chunk_base, float* __restrict__ pooled) {
     pdl_wait();
     pdl_launch_if_one_wave();
+    // Block (s, y) owns columns [256 y, 256 y + 256) of sequence s, four per thread; the chunks
+    // are added in order, eight loads in flight at a time.
     const int s = blockIdx.x;
+    const int c = blockIdx.y * 256 + threadIdx.x * 4;
+    if (c >= width) return;
     const uint32_t len = seqs[2 * s + 1];
     const uint32_t nchunks = (len + kPoolChunk - 1) / kPoolChunk;
-    const float* in = partial + long(chunk_base[s]) * width;
-    for (int c = threadIdx.x; c < width; c += blockDim.x) {
-        float acc = 0.f;
-        for (uint32_t k = 0; k < nchunks; k++) acc += in[long(k) * width + c];
-        pooled[long(s) * width + c] = acc / float(len);
+    const float* in = partial + long(chunk_base[s]) * width + c;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    uint32_t k = 0;
+    for (; k + 8 <= nchunks; k += 8) {
+        float4 t[8];
+#pragma unroll
+        for (int j = 0; j < 8; j++) t[j] = *reinterpret_cast<const float4*>(in + long(k + j) * width);
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            acc.x += t[j].x;
+            acc.y += t[j].y;
+            acc.z += t[j].z;
+            acc.w += t[j].w;
+        }
     }
+    for (; k < nchunks; k++) {
+        const float4 t = *reinterpret_cast<const float4*>(in + long(k) * width);
+        acc.x += t.x;
+        acc.y += t.y;
+        acc.z += t.z;
+        acc.w += t.w;
+    }
+    const float n = float(len);
+    *reinterpret_cast<float4*>(pooled + long(s) * width + c) = make_float4(acc.x / n, acc.y / n, acc.z / n, acc.w / n);
 }
 
 int pool_chunks(uint32_t len) { return int((len + kPoolChunk - 1) / kPoolChunk); }
@@ -600,8 +622,8 @@ cudaError_t launch_mean_pool(const float* y, int width, const uint32_t* seqs, in
     if (width % 128) return cudaErrorInvalidValue;
     CK_LAUNCH(launch_kernel(k_pool_partial, dim3(max_chunks, nseq), dim3(256), 8 * width * sizeof(float), stream, 1, y,
                             width, seqs, chunk_base, partial));
-    CK_LAUNCH(launch_kernel(k_pool_final, dim3(nseq), dim3(256), 0, stream, 1, partial, width, seqs, chunk_base,
-                            pooled));
+    CK_LAUNCH(launch_kernel(k_pool_final, dim3(nseq, (width + 255) / 256), dim3(64), 0, stream, 1, partial, width, seqs,
+                            chunk_base, pooled));
     return cudaGetLastError();
 }
 
