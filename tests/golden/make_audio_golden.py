@@ -15,7 +15,9 @@ import os
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GE_REFERENCE", "/root/reference")
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GE_REFERENCE")
+if not REF:
+    sys.exit("usage: python make_audio_golden.py <reference checkout> (or set GE_REFERENCE to its path)")
 SRC = os.path.join(REF, "Tests/GemmaEmbedTests/Fixtures/audio/embeddings.jsonl")
 
 clips = []

@@ -14,7 +14,9 @@ import os
 import re
 import sys
 
-REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GE_REFERENCE", "/root/reference")
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GE_REFERENCE")
+if not REF:
+    sys.exit("usage: python make_golden.py <reference checkout> (or set GE_REFERENCE to its path)")
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 

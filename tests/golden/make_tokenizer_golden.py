@@ -26,7 +26,9 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
-REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GE_REFERENCE", "/root/reference")
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GE_REFERENCE")
+if not REF:
+    sys.exit("usage: python make_tokenizer_golden.py <reference checkout> (or set GE_REFERENCE to its path)")
 
 synth = importlib.import_module("gemma-embed-swift_b200.synthetic")
 from oracle.hf_bpe import HfBpe  # noqa: E402

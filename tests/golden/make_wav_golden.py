@@ -26,7 +26,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 from oracle import binding as B  # noqa: E402
 
-REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GE_REFERENCE", "/root/reference")
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GE_REFERENCE")
+if not REF:
+    sys.exit("usage: python make_wav_golden.py <reference checkout> (or set GE_REFERENCE to its path)")
 FIX = os.path.join(REF, "Tests/GemmaEmbedTests/Fixtures/audio")
 
 
