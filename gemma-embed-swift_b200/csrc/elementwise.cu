@@ -580,13 +580,17 @@ __global__ void k_pool_final(const float* __restrict__ partial, int width, const
 int pool_chunks(uint32_t len) { return int((len + kPoolChunk - 1) / kPoolChunk); }
 
 // Single-launch mean pool for callers that only hold the sequence ranges on the device: one
-// block per sequence, warp w summing rows w, w + 8, ..., then the 8 warp sums in order.
-__global__ void k_mean_pool_seq(const float* __restrict__ y, int width, const uint32_t* __restrict__ seqs,
-                                float* __restrict__ pooled) {
+// block per sequence, warp w summing rows w, w + 8, ..., then the 8 warp sums in order.  The
+// ranges come straight from the caller's device memory, so only rows inside [0, ntok) are read:
+// a range is cut at ntok, and a range with no row left (length 0, or a start at or past ntok)
+// gives a zero vector.
+__global__ void k_mean_pool_seq(const float* __restrict__ y, int width, uint32_t ntok,
+                                const uint32_t* __restrict__ seqs, float* __restrict__ pooled) {
     pdl_wait();
     pdl_launch_if_one_wave();
     extern __shared__ float part[];  // [8][width]
-    const uint32_t start = seqs[2 * blockIdx.x], len = seqs[2 * blockIdx.x + 1];
+    const uint32_t start = seqs[2 * blockIdx.x];
+    const uint32_t len = start >= ntok ? 0u : min(seqs[2 * blockIdx.x + 1], ntok - start);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int c0 = lane * 4; c0 < width; c0 += 128) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -603,16 +607,16 @@ __global__ void k_mean_pool_seq(const float* __restrict__ y, int width, const ui
     for (int c = threadIdx.x; c < width; c += blockDim.x) {
         float acc = 0.f;
         for (int w = 0; w < 8; w++) acc += part[w * width + c];
-        pooled[long(blockIdx.x) * width + c] = acc / float(len);
+        pooled[long(blockIdx.x) * width + c] = len ? acc / float(len) : 0.f;
     }
 }
 
-cudaError_t launch_mean_pool_seq(const float* y, int width, const uint32_t* seqs, int nseq, float* pooled,
+cudaError_t launch_mean_pool_seq(const float* y, int width, int ntok, const uint32_t* seqs, int nseq, float* pooled,
                                  cudaStream_t stream) {
     if (nseq <= 0) return cudaSuccess;
-    if (width % 128) return cudaErrorInvalidValue;
+    if (width % 128 || ntok < 0) return cudaErrorInvalidValue;
     CK_LAUNCH(launch_kernel(k_mean_pool_seq, dim3(nseq), dim3(256), 8 * width * sizeof(float), stream, 1, y, width,
-                            seqs, pooled));
+                            uint32_t(ntok), seqs, pooled));
     return cudaGetLastError();
 }
 

@@ -206,8 +206,9 @@ int pool_chunks(uint32_t len);
 constexpr int kPoolChunkRows = 64;  // rows per partial sum of the mean pool
 cudaError_t launch_mean_pool(const float* y, int width, const uint32_t* seqs, int nseq, int max_chunks,
                              const uint32_t* chunk_base, float* partial, float* pooled, cudaStream_t stream);
-// The same mean in one launch, one block per sequence (sequence ranges on the device only).
-cudaError_t launch_mean_pool_seq(const float* y, int width, const uint32_t* seqs, int nseq, float* pooled,
+// The same mean in one launch, one block per sequence (sequence ranges on the device only);
+// rows at or past ntok are never read (a range is cut there, an empty one pools to zeros).
+cudaError_t launch_mean_pool_seq(const float* y, int width, int ntok, const uint32_t* seqs, int nseq, float* pooled,
                                  cudaStream_t stream);
 
 // out[s][n] = sum_k in[s][k] * w[n][k], fp32 weights [N][K].

@@ -50,6 +50,20 @@ cudaError_t noalloc_setup(int device) {
 }
 }  // namespace ge
 
+namespace {
+// Puts the calling thread's current device back on every return path: the caller's host
+// runtime manages devices itself and must not see this call change them.
+struct CurrentDeviceGuard {
+    int saved = -1;
+    CurrentDeviceGuard() {
+        if (cudaGetDevice(&saved) != cudaSuccess) saved = -1;
+    }
+    ~CurrentDeviceGuard() {
+        if (saved >= 0) cudaSetDevice(saved);
+    }
+};
+}  // namespace
+
 extern "C" int ge_pool_head_noalloc(ge_model* m, int32_t device_ordinal, const float* d_hidden, int32_t ntok,
                                     const uint32_t* d_seqs, int32_t nseq, float* d_out, void* stream) {
     if (!m) return GE_ERR_INVALID_OPTIONS;
@@ -63,10 +77,17 @@ extern "C" int ge_pool_head_noalloc(ge_model* m, int32_t device_ordinal, const f
         return ge::set_error(m, GE_ERR_INVALID_OPTIONS,
                              "invalid options: ge_pool_head_noalloc takes 1.." + std::to_string(kMaxSeqs) +
                                  " sequences per call, got " + std::to_string(nseq));
-    if (ntok < nseq || !d_hidden || !d_seqs || !d_out)
+    if (ntok < 1 || !d_hidden || !d_seqs || !d_out)
         return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: bad sizes or NULL device arrays");
     if (c.hidden > kMaxHidden || (c.has_dense && c.dense_head > kMaxMid))
         return ge::set_error(m, GE_ERR_INVALID_OPTIONS, "invalid options: the model's head is wider than the scratch");
+    // The pooling and head kernels work in 128-column groups; other widths are refused here
+    // rather than reported later as a failed launch.
+    if (c.hidden % 128 || (c.has_dense && c.dense_head % 128))
+        return ge::set_error(m, GE_ERR_INVALID_OPTIONS,
+                             "invalid options: ge_pool_head_noalloc needs hidden and dense-head widths that are "
+                             "multiples of 128");
+    CurrentDeviceGuard keep_current_device;
     cudaError_t e = cudaSetDevice(dev->ordinal);
     float* scratch = nullptr;
     if (e == cudaSuccess) e = scratch_address(dev->ordinal, &scratch);
@@ -76,8 +97,9 @@ extern "C" int ge_pool_head_noalloc(ge_model* m, int32_t device_ordinal, const f
     float* mid = scratch + size_t(kMaxSeqs) * kMaxHidden;
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : cudaStreamLegacy;
     // Each kernel writes every scratch element it later reads, so no call depends on what the
-    // previous call left in the array and nothing needs clearing.
-    e = ge::launch_mean_pool_seq(d_hidden, c.hidden, d_seqs, nseq, pooled, st);
+    // previous call left in the array and nothing needs clearing.  The pooling kernel reads only
+    // rows [0, ntok) of d_hidden whatever the ranges say.
+    e = ge::launch_mean_pool_seq(d_hidden, c.hidden, ntok, d_seqs, nseq, pooled, st);
     int launches = 1;
     if (e == cudaSuccess && c.has_dense) {
         e = ge::launch_dense_f32(pooled, nseq, dev->dense2, c.dense_head, c.hidden, mid, st);

@@ -463,12 +463,18 @@ GE_API int ge_embed_multimodal(ge_model* model, const ge_multimodal_input* input
  *   d_hidden: device [ntok][hidden_size] fp32, the final-normed hidden states (the values
  *             ge_forward_trace returns for layer -1); d_seqs: device (start, length) uint32 pairs
  *             that tile [0, ntok); d_out: device [nseq][output_dimensions] fp32.
- * Work is enqueued on `stream` (a cudaStream_t; NULL is the legacy default stream) without
- * synchronising.  nseq above GE_NOALLOC_MAX_SEQS returns GE_ERR_INVALID_OPTIONS.  ge_load
- * looks up the array's device address (cudaGetSymbolAddress) once on each of its devices; if
- * that lookup has not succeeded, the first call on the device repeats it, so make the first
- * call before any stream capture.  All calls share the one array and each overwrites what it
- * reads: calls whose work overlaps on the GPU (other streams, other host threads) race on it. */
+ * Only rows [0, ntok) of d_hidden are read: a range that runs past ntok is cut there, and a
+ * range with no row inside (length 0, or a start at or past ntok) gives the head's value for a
+ * zero pooled row.  The pool adds each sequence's rows in a different order than the forward's
+ * chunked pool, so the output matches the forward's vectors within 1e-4 relative, not bit for
+ * bit.  Work is enqueued on `stream` (a cudaStream_t; NULL is the legacy default stream) without
+ * synchronising; the calling thread's current device is left as it was.  nseq above
+ * GE_NOALLOC_MAX_SEQS, and hidden or dense-head widths that are not multiples of 128, return
+ * GE_ERR_INVALID_OPTIONS.  ge_load looks up the array's device address (cudaGetSymbolAddress)
+ * once on each of its devices; if that lookup has not succeeded, the first call on the device
+ * repeats it, so make the first call before any stream capture.  All calls share the one array
+ * and each overwrites what it reads: calls whose work overlaps on the GPU (other streams, other
+ * host threads) race on it. */
 #define GE_NOALLOC_MAX_SEQS 128
 GE_API int ge_pool_head_noalloc(ge_model* model, int32_t device_ordinal, const float* d_hidden, int32_t ntok,
                                 const uint32_t* d_seqs, int32_t nseq, float* d_out, void* stream);
