@@ -16,6 +16,13 @@ device->host pooled vectors inside the timed region).  `e2e_text` does the same 
 (EmbeddingModel.embed on texts -> ge_embed_texts, tokenisation with the document prefix
 inside the timed region) on seeded synthetic texts cut to the batch's lengths, and
 `tokenizer` compares the library's tokenizer with the oracle's restatement on one thread.
+`e2e_stream` runs K *distinct* seeded config-2 batches through the same API (every step a new
+length mix, so a new batch shape: what an embedding service sees), with the CUDA graphs captured
+per step beside it.  `workloads` holds device-resident lines for the metric's literal 64 x 512
+batch and for config 3 (16 x 2048 + 4 x 8192 tokens), each with its own roofline.  `strong`
+times one config-2 batch on all N GPUs through the library's own dispatcher (rank 0 loads the
+model on devices 0..N-1 and EmbeddingModel.embed shards the batch's sequences over them, packs
+each share, and gathers the vectors on the host) while the other ranks wait: strong scaling.
 `--impl reference` times the CPU oracle (the restated CPUReference.forward, the only
 runnable form of the reference's path here) on the host cores.
 
@@ -52,6 +59,8 @@ def args_():
     p.add_argument("--profile-reps", type=int, default=5)
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="bound of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--q8-sweep", choices=["on", "off"], default="on",
+                   help="time the Q8_0 (dequantise in shared memory) and fp16-weight GEMM paths by batch size")
     p.add_argument("--fused-qkv", choices=["on", "off"], default="off",
                    help="q/k/v norms and RoPE in the q/k/v projection's epilogue (GE_LOAD_FUSED_QKV)")
     return p.parse_args()
@@ -259,6 +268,18 @@ def main():
     ms_max, tok_sum = reduce_max_sum(dist, ms_total, ntok * a.steps)
     value = tok_sum / (ms_max / 1000.0)
 
+    # ---- per-kernel roofline (rank 0): the kernel class with the largest share of a forward,
+    # profiled right after the timed region, at the clocks it ran at
+    pk = peaks()
+    roofline = None
+    prof = []
+    if rank == 0:
+        prof = model.profile(tokens, ranges, reps=a.profile_reps)
+        roofline = top_roofline(prof, pk)
+        traffic = NCU_DRAM_BYTES_CONFIG2["bytes"].get(roofline["kernel"]) if a.config == 2 and a.arch == "gemma-embedding" else None
+        roofline["traffic"] = traffic
+        roofline["traffic_source"] = NCU_DRAM_BYTES_CONFIG2["source"] if traffic else None
+
     # ---- end to end through the public API with host buffers: EmbeddingModel.embed on the
     # batch's token ids (one packed batch), Matryoshka 256-d L2-normalised vectors back
     texts = [np.asarray(q, dtype=np.int32) for q in seqs]
@@ -300,34 +321,81 @@ def main():
                 "api": "ge_embed_texts (EmbeddingModel.embed on strings), document prefix, 256-d normalised output"}
     tok_stats = tokenizer_throughput(synth, tk, path) if rank == 0 else None
 
-    # ---- per-kernel roofline (rank 0): the kernel class with the largest share of a forward
-    pk = peaks()
-    roofline = None
-    prof = []
-    if rank == 0:
-        prof = model.profile(tokens, ranges, reps=a.profile_reps)
-        fwd_ms = sum(p["ms_per_launch"] * p["launches_per_forward"] for p in prof)
-        top = max(prof, key=lambda p: p["ms_per_launch"] * p["launches_per_forward"])
-        # The binding roofline is the one the kernel runs closer to: tensor FLOP/s or HBM bytes/s.
-        sec = top["ms_per_launch"] / 1000.0
-        tf = top["flops_per_launch"] / sec / 1e12
-        gbs = top["bytes_per_launch"] / sec / 1e9
-        tensor = tf / pk["bf16_tflops"] > gbs / pk["hbm_gbs"]
-        if tensor:
-            ach, peak, unit = tf, pk["bf16_tflops"], "TFLOP/s"
-        else:
-            ach, peak, unit = gbs, pk["hbm_gbs"], "GB/s"
-        traffic = NCU_DRAM_BYTES_CONFIG2.get(top["name"]) if a.config == 2 and a.arch == "gemma-embedding" else None
-        roofline = {"kernel": top["name"], "bound": "tensor" if tensor else "hbm", "achieved": ach, "peak": peak,
-                    "unit": unit, "frac": ach / peak, "traffic": traffic,
-                    "traffic_source": "profiles/layer_config2_ncu_full.md" if traffic else None,
-                    "peak_source": pk["source"],
-                    "share_of_forward": top["ms_per_launch"] * top["launches_per_forward"] / fwd_ms,
-                    "launches_per_forward": top["launches_per_forward"]}
+    # ---- a stream of distinct batches through the same API: new lengths (a new batch shape)
+    # every step, as an embedding service sees them; graph captures per step beside it
+    stream_batches = [[np.asarray(q, dtype=np.int32) for q in synth.config_sequences(2, seed=10_000 + 100 * rank + i)]
+                      for i in range(a.steps + 2)]
+    for b in stream_batches[:2]:
+        model.embed(b, opts)
+    barrier()
+    c0 = model.counters()
+    st_ms, st_tok = [], 0
+    t0 = time.perf_counter()
+    for b in stream_batches[2:]:
+        s0 = time.perf_counter()
+        model.embed(b, opts)
+        st_ms.append((time.perf_counter() - s0) * 1000.0)
+        st_tok += sum(len(q) for q in b)
+    t1 = time.perf_counter()
+    barrier()
+    c1 = model.counters()
+    es_ms, es_tok = reduce_max_sum(dist, (t1 - t0) * 1000.0, st_tok)
+    st_ms.sort()
+    e2e_stream = {"value": es_tok / (es_ms / 1000.0), "unit": "tokens/s", "steps": a.steps,
+                  "tokens_per_step": es_tok // a.steps,
+                  "graph_captures_per_step": (c1["graph_captures"] - c0["graph_captures"]) / a.steps,
+                  "latency_ms_p50": pct(st_ms, 50), "latency_ms_p99": pct(st_ms, 99),
+                  "api": "ge_embed_tokens (EmbeddingModel.embed), a distinct seeded config-2 batch every step, "
+                         "256-d normalised output"}
+
+    # ---- the metric's literal 64 x 512 batch and config 3, device-resident, each with its roofline
+    workloads = {}
+    if a.config == 2:
+        for name, cfg in (("64x512", 4), ("config 3", 3)):
+            wseqs = synth.config_sequences(cfg, seed=rank)
+            wt, _, wr = ge.pack(wseqs)
+            w_tokens = torch.from_numpy(wt).cuda()
+            w_out = torch.empty((len(wr), od), dtype=torch.float32, device="cuda")
+            wsteps = max(3, min(a.steps, 10))
+            for _ in range(3):
+                model.forward_device(w_tokens, wr, w_out, stream=stream, device=local)
+            barrier()
+            torch.cuda.synchronize()
+            wev = [torch.cuda.Event(enable_timing=True) for _ in range(wsteps + 1)]
+            wev[0].record(stream)
+            for i in range(wsteps):
+                model.forward_device(w_tokens, wr, w_out, stream=stream, device=local)
+                wev[i + 1].record(stream)
+            torch.cuda.synchronize()
+            w_step = sorted(wev[i].elapsed_time(wev[i + 1]) for i in range(wsteps))
+            w_ms, w_tok = reduce_max_sum(dist, wev[0].elapsed_time(wev[-1]), len(wt) * wsteps)
+            entry = {"value": w_tok / (w_ms / 1000.0), "unit": "tokens/s", "ms_per_step": w_ms / wsteps,
+                     "steps": wsteps, "tokens_per_rank": int(len(wt)), "texts_per_rank": len(wr),
+                     "latency_ms_p50": pct(w_step, 50), "latency_ms_p99": pct(w_step, 99)}
+            if rank == 0:
+                wprof = model.profile(wt, wr, reps=max(1, a.profile_reps // 2))
+                entry["roofline"] = top_roofline(wprof, peaks())
+            workloads[name] = entry
+            del w_tokens, w_out
+
+    # ---- strong scaling through the library's dispatcher: rank 0 alone embeds one config-2
+    # batch on devices 0..N-1 (sequences sharded longest first onto the least-loaded device,
+    # each share packed and run on its own host thread and stream, vectors gathered on the host)
+    strong = None
+    if world > 1:
+        barrier()
+        if rank == 0:
+            strong = strong_scaling(ge, path, [np.asarray(q, dtype=np.int32) for q in synth.config_sequences(2, seed=0)],
+                                    opts, world, a.steps)
+        barrier()
+    else:
+        strong = {"value": e2e, "unit": "tokens/s", "devices": 1, "note": "one GPU: the e2e measurement"}
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         cpu = cpu_baseline(path, seqs, a.cpu_seconds)
+    q8 = q8_gemm_sweep(ge, synth, path) if rank == 0 and world == 1 and a.config == 2 and a.q8_sweep == "on" else None
+    gemm_paths = gemm_schedule_sweep() if rank == 0 and world == 1 and a.config == 2 and a.q8_sweep == "on" else None
 
     if rank == 0:
         line = {"metric": "embedded tokens/sec (config 2: 64 texts x 32..512 tokens)", "value": value,
@@ -340,7 +408,9 @@ def main():
                            "l2": "working set larger than L2 (fp16 weights 203 MB + ~0.5 GB of activations per step)"},
                 "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                         "api": "ge_embed_tokens (EmbeddingModel.embed), 256-d normalised output"},
-                "e2e_text": e2e_text, "tokenizer": tok_stats,
+                "e2e_text": e2e_text, "e2e_stream": e2e_stream, "strong": strong, "workloads": workloads,
+                "q8_gemm": q8, "gemm_schedules": gemm_paths,
+                "tokenizer": tok_stats,
                 "gpu_launches": int(launches), "clocks": clock_info, "roofline": roofline, "cpu_baseline": cpu,
                 "latency_ms_p50": pct(step_ms, 50), "latency_ms_p99": pct(step_ms, 99),
                 "kernels": [{k: (round(v, 5) if isinstance(v, float) else v) for k, v in p.items()} for p in prof]}
@@ -351,16 +421,131 @@ def main():
     return 0
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of each kernel class, from the
-# one-layer `ncu --set full` capture at config 2 summarised in profiles/layer_config2_ncu_full.md
-# (cold caches: reads include operands a normal run finds in L2).
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of each kernel class, from one
+# `ncu --set full` capture of one config-2 layer (cold caches: reads include operands a normal
+# run finds in L2).  The capture belongs to the kernels of the commit named in "source"; a
+# kernel changed since then needs a new capture.
 NCU_DRAM_BYTES_CONFIG2 = {
-    "gemm_qkv": 35.83e6, "qkv_norm_rope": 57.39e6, "attention_sliding": 53.24e6, "gemm_o": 31.75e6,
-    "residual_attn": 101.38e6, "gemm_gate_up": 39.70e6, "gemm_down": 49.08e6, "residual_ffn": 157.23e6,
+    "source": "ncu --set full, one layer of the config-2 forward, kernels of commit adaa5da",
+    "bytes": {"gemm_qkv": 35.83e6, "qkv_norm_rope": 57.39e6, "attention_sliding": 53.24e6, "gemm_o": 31.75e6,
+              "residual_attn": 101.38e6, "gemm_gate_up": 39.70e6, "gemm_down": 49.08e6, "residual_ffn": 157.23e6},
 }
 
 
 BATCH_BUDGET = 65536
+
+
+def top_roofline(prof, pk):
+    """The kernel class with the largest share of a forward (ge_profile: CUDA events on its
+    stream), against the peak it runs closer to: tensor FLOP/s or HBM bytes/s."""
+    fwd_ms = sum(p["ms_per_launch"] * p["launches_per_forward"] for p in prof)
+    top = max(prof, key=lambda p: p["ms_per_launch"] * p["launches_per_forward"])
+    sec = top["ms_per_launch"] / 1000.0
+    tf = top["flops_per_launch"] / sec / 1e12
+    gbs = top["bytes_per_launch"] / sec / 1e9
+    tensor = tf / pk["bf16_tflops"] > gbs / pk["hbm_gbs"]
+    ach, peak, unit = (tf, pk["bf16_tflops"], "TFLOP/s") if tensor else (gbs, pk["hbm_gbs"], "GB/s")
+    return {"kernel": top["name"], "bound": "tensor" if tensor else "hbm", "achieved": ach, "peak": peak,
+            "unit": unit, "frac": ach / peak, "traffic": None, "peak_source": pk["source"],
+            "share_of_forward": top["ms_per_launch"] * top["launches_per_forward"] / fwd_ms,
+            "launches_per_forward": top["launches_per_forward"], "forward_ms_sum_of_kernels": fwd_ms}
+
+
+# Projection shapes of the measured model (N, K): the weight bytes each GEMM launch streams.
+GEMM_SHAPES = {"gemm_qkv": (1280, 768), "gemm_o": (768, 768), "gemm_gate_up": (2304, 768), "gemm_down": (768, 1152)}
+
+
+def q8_gemm_sweep(ge, synth, path, rows_list=(128, 256, 512, 1024, 2048, 4096), reps=5):
+    """The two weight paths of the projection GEMMs by batch size: Q8_0 planes dequantised to
+    fp16 in shared memory (int8 values + fp16 scales, 34/32 bytes per weight) against the
+    fp16-resident copy (2 bytes per weight).  Per size, the four projection classes' mean time
+    per launch (ge_profile, CUDA events), the Q8 path's weight bytes per second against HBM, and
+    which path is faster.  The library reads the fp16 weights unless the model was loaded with
+    only the Q8_0 planes (LoadOptions.q8_only)."""
+    models = {"q8": ge.EmbeddingModel.load(path, ge.LoadOptions(q8_only=True, batch_token_budget=BATCH_BUDGET)),
+              "fp16": ge.EmbeddingModel.load(path, ge.LoadOptions(batch_token_budget=BATCH_BUDGET))}
+    pk = peaks()
+    out = []
+    try:
+        for rows in rows_list:
+            lens = [rows // 4] * 4  # four texts filling `rows` GEMM rows exactly
+            toks, _, ranges = ge.pack(synth.random_sequences(lens, seed=rows))
+            entry = {"rows": rows}
+            for name, m in models.items():
+                prof = {p["name"]: p for p in m.profile(toks, ranges, reps=reps)}
+                us = {k: prof[k]["ms_per_launch"] * 1000.0 for k in GEMM_SHAPES}
+                entry[name + "_us"] = {k: round(v, 2) for k, v in us.items()}
+                entry[name + "_layer_us"] = round(sum(us.values()), 2)
+                if name == "q8":
+                    wbytes = sum(n * k * 34 / 32 for n, k in GEMM_SHAPES.values())
+                    entry["q8_weight_gbs"] = wbytes / (sum(us.values()) * 1e-6) / 1e9
+                    entry["q8_weight_frac_of_hbm"] = entry["q8_weight_gbs"] / pk["hbm_gbs"]
+                    tflops = sum(2.0 * rows * n * k for n, k in GEMM_SHAPES.values()) / (sum(us.values()) * 1e-6) / 1e12
+                    entry["q8_tflops"] = tflops
+            entry["faster"] = "q8" if entry["q8_layer_us"] <= entry["fp16_layer_us"] else "fp16"
+            out.append(entry)
+    finally:
+        for m in models.values():
+            m.close()
+    return {"sizes": out, "library_default": "fp16 weights at every size (Q8 only with LoadOptions.q8_only)",
+            "crossover_rows": max([e["rows"] for e in out if e["faster"] == "q8"], default=None)}
+
+
+def gemm_schedule_sweep(rows_list=(1024, 2432, 19584), reps=20):
+    """Each projection GEMM of the measured model, per launch (ge_test_gemm_time: CUDA events
+    over back-to-back launches on seeded operands), under its four schedules: whole 128 x 256
+    tiles on persistent single CTAs (the library's default), the same with tiles split into
+    narrower pieces where that would shorten the schedule, CTA pairs (256 x 256 tiles), and Q8_0
+    weights dequantised in shared memory.  Rows: config 1 (1,024), a config-2 batch on 8 GPUs
+    (about 2,400 per GPU) and config 2 on one (19,516, padded to 19,584)."""
+    import ctypes
+    lib = importlib.import_module(PKG + "._lib").lib()
+    epi = {"gemm_qkv": 1, "gemm_o": 1, "gemm_gate_up": 2, "gemm_down": 1}
+    paths = {"whole_tiles": 0, "split_tiles": 4, "cta_pairs": 2, "q8_smem": 1}
+    pk = peaks()
+    out = []
+    for rows in rows_list:
+        for name, (n, k) in GEMM_SHAPES.items():
+            entry = {"gemm": name, "rows": rows, "n": n, "k": k, "tiles": (rows // 128) * (n // 256)}
+            for pname, path in paths.items():
+                us = ctypes.c_double(0.0)
+                rc = lib.ge_test_gemm_time(rows, k, n, epi[name], path, reps, ctypes.byref(us))
+                entry[pname + "_us"] = round(us.value, 2) if rc == 0 else None
+            best = min((v for key, v in entry.items() if key.endswith("_us") and v), default=None)
+            if best:
+                entry["best_frac_of_bf16_burst"] = 2.0 * rows * n * k / (best * 1e-6) / 1e12 / pk["bf16_tflops"]
+            out.append(entry)
+    return out
+
+
+def strong_scaling(ge, path, texts, opts, n_devices, steps):
+    """One config-2 batch embedded on devices 0..n-1 by one process through EmbeddingModel.embed
+    (ge_embed_tokens): the library shards the sequences, runs each device's share on its own
+    host thread and stream and gathers the vectors.  The call is synchronous, so each step is
+    timed on the host around it (host-to-device ids and device-to-host vectors included)."""
+    model = ge.EmbeddingModel.load(path, ge.LoadOptions(devices=tuple(range(n_devices)),
+                                                        batch_token_budget=BATCH_BUDGET))
+    try:
+        for _ in range(3):
+            model.embed(texts, opts)
+        c0 = model.counters()
+        ms = []
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            s0 = time.perf_counter()
+            model.embed(texts, opts)
+            ms.append((time.perf_counter() - s0) * 1000.0)
+        dt = time.perf_counter() - t0
+        c1 = model.counters()
+    finally:
+        model.close()
+    ntok = sum(len(t) for t in texts)
+    ms.sort()
+    return {"value": ntok * steps / dt, "unit": "tokens/s", "devices": n_devices, "steps": steps,
+            "tokens_per_step": ntok, "latency_ms_p50": pct(ms, 50), "latency_ms_p99": pct(ms, 99),
+            "h2d_bytes_per_step": (c1["host_to_device_bytes"] - c0["host_to_device_bytes"]) // steps,
+            "d2h_bytes_per_step": (c1["device_to_host_bytes"] - c0["device_to_host_bytes"]) // steps,
+            "api": "ge_embed_tokens on a model loaded on every device (in-library dispatcher), 256-d normalised output"}
 
 
 def text_batch(synth, tk, lengths, seed):

@@ -444,6 +444,14 @@ class EmbeddingModel:
             audio_feed_forward_size=info.audio_feed_forward_size, audio_mel_bins=info.audio_mel_bins,
             audio_projection_dim=info.audio_projection_dim)
 
+    def counters(self) -> dict:
+        """The library's running counts for this model (ge_info_get): kernel launches, bytes
+        copied host to device and back by the forwards, and CUDA graphs captured."""
+        info = _lib.GeInfo()
+        _check(_lib.lib().ge_info_get(self._h, ctypes.byref(info)), self._h)
+        return {"kernel_launches": int(info.kernel_launches), "host_to_device_bytes": int(info.host_to_device_bytes),
+                "device_to_host_bytes": int(info.device_to_host_bytes), "graph_captures": int(info.graph_captures)}
+
     @classmethod
     def load(cls, path: str, options: Optional[LoadOptions] = None) -> "EmbeddingModel":
         """EmbeddingModel.load(from:options:) (EmbeddingModel.swift:40-122)."""

@@ -72,7 +72,7 @@ class GeInfo(ctypes.Structure):
         (n, ctypes.c_int32) for n in ("image_layer_count", "image_hidden_size", "image_patch_size",
                                       "image_projection_dim", "audio_layer_count", "audio_hidden_size",
                                       "audio_head_count", "audio_feed_forward_size", "audio_mel_bins",
-                                      "audio_projection_dim")]
+                                      "audio_projection_dim")] + [("graph_captures", ctypes.c_int64)]
 
 
 class GeKernelTime(ctypes.Structure):
@@ -148,6 +148,8 @@ SIGNATURES = {
 
 # Kernel-level entry points of include/gemma_embed_testing.h.
 TEST_SIGNATURES = {
+    "ge_test_gemm_time": ([ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                           ctypes.c_int32, P(ctypes.c_double)], ctypes.c_int),
     "ge_test_gemm": ([u16p, ctypes.c_int32, ctypes.c_int32, P(ctypes.c_uint8), ctypes.c_int32, ctypes.c_int32,
                       ctypes.c_int32, f32p, f32p], ctypes.c_int),
     "ge_test_gemm_residual": ([u16p, ctypes.c_int32, ctypes.c_int32, P(ctypes.c_uint8), ctypes.c_int32, ctypes.c_int32,

@@ -533,6 +533,7 @@ int ge_info_get(const ge_model* m, ge_info* info) {
     info->kernel_launches = m->launches.load();
     info->host_to_device_bytes = m->h2d_bytes.load();
     info->device_to_host_bytes = m->d2h_bytes.load();
+    info->graph_captures = m->graph_captures.load();
     if (m->has_vision) {
         info->image_layer_count = m->vcfg.layers;
         info->image_hidden_size = m->vcfg.hidden;

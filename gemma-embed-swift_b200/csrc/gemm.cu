@@ -13,6 +13,18 @@
 //   warps 0-3   epilogue: tensor memory -> registers -> global, with fused activations
 // Two accumulators of BN columns let the epilogue of one tile overlap the next tile's MMAs.
 // Every wait is bounded: on timeout the kernel records GE_ERR_TIMEOUT and returns.
+//
+// Split tiles (fp16 weights on single CTAs, GEMM_SPLIT): tiles can run as S pieces of BN/S columns each (a
+// GeGLU piece: BN/2S gate rows and the BN/2S up rows they pair with) on S times as many CTAs.
+// When the tiles do not divide evenly over the CTAs, the last, partial round runs as S = 2
+// pieces per tile, so the kernel ends half a tile after the full rounds instead of a whole
+// tile; when all tiles fit in one round with SMs to spare (small batches), every tile is split
+// (S up to 8 for fp32 stores, 4 for fp16, 2 for GeGLU) to put more SMs on the batch.  A piece
+// multiplies the same A rows by the same B rows over the same K steps as the whole tile; only
+// the MMA's N differs, so every output element gets the same bits either way.  Measured on a
+// B200, neither split is faster than whole tiles on the forward's shapes: in the last round the
+// few busy CTAs already run faster than in a full one, and a small batch's time is the 12-step
+// K loop's latency, which pieces do not shorten.  So the split runs only on request.
 #include <cudaTypedefs.h>
 
 #include <map>
@@ -70,6 +82,9 @@ struct GemmParams {
     int store_h, store_y;
     // clamp epilogues (aux holds the optional bias)
     float lo1, hi1, lo2, hi2;
+    // Split tiles: tiles from split_from on run as `split` pieces of BN / split columns
+    // (split_from == the tile count: no split)
+    int split_from, split;
     // EPI_QKV (eps above)
     const int32_t* pos;
     const float* rope;
@@ -114,8 +129,8 @@ __device__ __forceinline__ void dequant16(uint4 raw, __half2 s2, uint32_t (&o)[8
 template <int BN, int EPI, bool Q8, bool PAIR>
 __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>::kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-           const __grid_constant__ CUtensorMap mapS, const __grid_constant__ CUtensorMap mapC,
-           const __grid_constant__ EpiMaps emaps, GemmParams p) {
+           const __grid_constant__ CUtensorMap mapS, const __grid_constant__ CUtensorMap mapP,
+           const __grid_constant__ CUtensorMap mapC, const __grid_constant__ EpiMaps emaps, GemmParams p) {
     constexpr bool RES = EPI == EPI_RESIDUAL;
     static_assert(!(PAIR && Q8), "the pair kernel reads fp16 weights");
     static_assert(!(PAIR && RES), "row clusters and CTA pairs are exclusive");
@@ -152,6 +167,21 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
             n0 = (t % n_tiles) * BN;
         }
     };
+    // Work items: tiles [0, split_from) whole, then `split` pieces (sub 0 .. split - 1) of each
+    // later tile.  Every role walks the same items in the same order.
+    constexpr bool kSplit = !PAIR && !RES && !Q8 && EPI != EPI_QKV;
+    const int split = kSplit ? p.split : 1;
+    const int split_from = split > 1 ? min(p.split_from, tiles) : tiles;
+    const int items = split_from + split * (tiles - split_from);
+    auto item_origin = [&](int w, int& m0, int& n0, int& sub) {
+        if (w < split_from) {
+            tile_origin(w, m0, n0);
+            sub = -1;
+        } else {
+            tile_origin(split_from + (w - split_from) / split, m0, n0);
+            sub = (w - split_from) % split;
+        }
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < L::kStages; s++) {
@@ -179,6 +209,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
         tma_prefetch(&mapA);
         tma_prefetch(&mapB);
         if (Q8) tma_prefetch(&mapS);
+        if (kSplit && split_from < tiles) tma_prefetch(&mapP);
         tma_prefetch(&mapC);
         if (RES) {
             tma_prefetch(&emaps.h);
@@ -209,9 +240,9 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
             uint32_t ph = 0;
             long issued = 0;
             bool ok = true;
-            for (int t = first; t < tiles && ok; t += step) {
-                int m0, n0;
-                tile_origin(t, m0, n0);
+            for (int w = first; w < items && ok; w += step) {
+                int m0, n0, sub;
+                item_origin(w, m0, n0, sub);
                 for (int kb = 0; kb < kb_count; kb++) {
                     if (!mbar_wait(&empty[s], ph ^ 1, p.err)) {
                         ok = false;
@@ -225,15 +256,22 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
                         tma_load_2d_pair(st, &mapA, bar, kb * BK, m0);
                         tma_load_2d_pair(st + L::kA, &mapB, bar, kb * BK, n0 + int(crank) * (BN / 2));
                     } else {
-                        mbar_expect_tx(&full_tma[s], L::kA + (Q8 ? L::kB8 + L::kSc : L::kB));
+                        mbar_expect_tx(&full_tma[s], L::kA + (Q8 ? L::kB8 + L::kSc : sub < 0 ? L::kB : L::kB / split));
                         tma_load_2d(st, &mapA, &full_tma[s], kb * BK, m0);
                     }
                     if (PAIR) {
                     } else if (Q8) {
                         tma_load_2d(st + L::kA + L::kB, &mapB, &full_tma[s], kb * BK, n0);
                         tma_load_2d(st + L::kA + L::kB + L::kB8, &mapS, &full_tma[s], n0, kb * 2);
-                    } else {
+                    } else if (sub < 0) {
                         tma_load_2d(st + L::kA, &mapB, &full_tma[s], kb * BK, n0);
+                    } else if (epi_is_geglu(EPI)) {
+                        // BN/2S gate rows, then the BN/2S up rows they pair with (BN/2 further on)
+                        const int hp = BN / (2 * split);
+                        tma_load_2d(st + L::kA, &mapP, &full_tma[s], kb * BK, n0 + sub * hp);
+                        tma_load_2d(st + L::kA + hp * BK * 2, &mapP, &full_tma[s], kb * BK, n0 + BN / 2 + sub * hp);
+                    } else {
+                        tma_load_2d(st + L::kA, &mapP, &full_tma[s], kb * BK, n0 + sub * (BN / split));
                     }
                     issued++;
                     if (++s == L::kStages) {
@@ -254,11 +292,13 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
     } else if (warp == 5) {
         // ---------------------------------------------------------- MMA issuer
         if (lane == 0 && leader) {  // a pair's MMAs are issued by its leader alone
-            const uint32_t idesc = idesc_f16(PAIR ? 2 * BM : BM, BN);
+            const uint32_t idesc_tile = idesc_f16(PAIR ? 2 * BM : BM, BN);
+            const uint32_t idesc_piece = idesc_f16(BM, BN / (kSplit ? split : 1));
             int s = 0, acc = 0;
             uint32_t ph = 0, acc_ph = 0;
             bool ok = true;
-            for (int t = first; t < tiles && ok; t += step) {
+            for (int w = first; w < items && ok; w += step) {
+                const uint32_t idesc = w < split_from ? idesc_tile : idesc_piece;
                 if (!mbar_wait(&tempty[acc], acc_ph ^ 1, p.err)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + uint32_t(acc * BN);
@@ -531,11 +571,16 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
             for (int b = 0; b < NB; b++)
                 if ((xin_pending >> b) & 1u) drain_wait(&xin_bar[epi * 4 + b], (xin_ph >> b) & 1u);
         } else
-        for (int t = first; t < tiles; t += step) {
+        for (int w = first; w < items; w += step) {
             if (!mbar_wait(&tfull[acc], acc_ph, p.err)) break;
             tc_fence_after();
-            int m0, n0;
-            tile_origin(t, m0, n0);
+            int m0, n0, sub;
+            item_origin(w, m0, n0, sub);
+            // A piece holds BN/S accumulator columns: output columns n0 + sub * BN/S onward, or
+            // for GeGLU BN/2S gate columns then BN/2S up columns (output n0/2 + sub * BN/2S on).
+            const int width = sub < 0 ? BN : BN / split;
+            const int nc = sub < 0 ? n0 : n0 + sub * width;
+            const int ng = sub < 0 ? n0 / 2 : n0 / 2 + sub * (width / 2);
             const int y = m0 + warp * 32;
             const long row = y + lane;
             const uint32_t taddr = tmem + (uint32_t(warp * 32) << 16) + uint32_t(acc * BN);
@@ -609,12 +654,12 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
             } else if (EPI == EPI_F32 || EPI == EPI_CLAMP_F32) {
                 uint32_t r[32];
 #pragma unroll 1
-                for (int c = 0; c < BN / 32; c++) {
+                for (int c = 0; c < width / 32; c++) {
                     tmem_ld32(taddr + uint32_t(c * 32), r);
                     tmem_wait_ld();
-                    if (c == BN / 32 - 1) release(acc);
+                    if (c == width / 32 - 1) release(acc);
                     if (EPI == EPI_CLAMP_F32) {
-                        const float* b = p.aux ? p.aux + n0 + c * 32 : nullptr;
+                        const float* b = p.aux ? p.aux + nc + c * 32 : nullptr;
 #pragma unroll
                         for (int i = 0; i < 32; i++) {
                             float v = fminf(fmaxf(__uint_as_float(r[i]), p.lo1), p.hi1);
@@ -622,20 +667,20 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
                             r[i] = __float_as_uint(v);
                         }
                     }
-                    emit(r, n0 + c * 32, y, &mapC);
+                    emit(r, nc + c * 32, y, &mapC);
                 }
             } else if (epi_is_geglu(EPI)) {
                 // Columns [0, BN/2) of the tile are gate rows, [BN/2, BN) the matching up rows.
                 // Per 64 output columns: 64 gate and 64 up values in flight, one wait.
 #pragma unroll 1
-                for (int c = 0; c < BN / 128; c++) {
+                for (int c = 0; c < width / 128; c++) {
                     uint32_t g[64], u[64];
                     tmem_ld32(taddr + uint32_t(c * 64), *reinterpret_cast<uint32_t(*)[32]>(&g[0]));
                     tmem_ld32(taddr + uint32_t(c * 64 + 32), *reinterpret_cast<uint32_t(*)[32]>(&g[32]));
-                    tmem_ld32(taddr + uint32_t(BN / 2 + c * 64), *reinterpret_cast<uint32_t(*)[32]>(&u[0]));
-                    tmem_ld32(taddr + uint32_t(BN / 2 + c * 64 + 32), *reinterpret_cast<uint32_t(*)[32]>(&u[32]));
+                    tmem_ld32(taddr + uint32_t(width / 2 + c * 64), *reinterpret_cast<uint32_t(*)[32]>(&u[0]));
+                    tmem_ld32(taddr + uint32_t(width / 2 + c * 64 + 32), *reinterpret_cast<uint32_t(*)[32]>(&u[32]));
                     tmem_wait_ld();
-                    if (c == BN / 128 - 1) release(acc);
+                    if (c == width / 128 - 1) release(acc);
 #pragma unroll
                     for (int i = 0; i < 32; i++) {
                         const float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
@@ -655,24 +700,27 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
                         }
                         packed[i] = pack_half2(a0 * u0, a1 * u1);
                     }
-                    emit(packed, n0 / 2 + c * 64, y, &mapC);
+                    emit(packed, ng + c * 64, y, &mapC);
                 }
             } else if (EPI == EPI_F16 || EPI == EPI_GELU_MUL || EPI == EPI_CLAMP_F16 || EPI == EPI_CLAMP_SILU) {
-                // 128 columns in flight per wait, stored as two 64-column boxes.
+                // 128 columns in flight per wait (64 for a 64-wide piece), stored as 64-column boxes.
+                const int chunk = width < 128 ? 64 : 128;
 #pragma unroll 1
-                for (int c = 0; c < BN / 128; c++) {
+                for (int c = 0; c < width / chunk; c++) {
                     uint32_t r[128];
 #pragma unroll
                     for (int q = 0; q < 4; q++)
-                        tmem_ld32(taddr + uint32_t(c * 128 + q * 32), *reinterpret_cast<uint32_t(*)[32]>(&r[32 * q]));
+                        if (q < chunk / 32)
+                            tmem_ld32(taddr + uint32_t(c * 128 + q * 32), *reinterpret_cast<uint32_t(*)[32]>(&r[32 * q]));
                     tmem_wait_ld();
-                    if (c == BN / 128 - 1) release(acc);
+                    if (c == width / chunk - 1) release(acc);
 #pragma unroll
                     for (int half = 0; half < 2; half++) {
+                        if (half >= chunk / 64) break;
                         const uint32_t* rv = r + 64 * half;
                         if (EPI == EPI_GELU_MUL) {
                             const float4* ax =
-                                reinterpret_cast<const float4*>(p.aux + row * p.ldaux + n0 + c * 128 + half * 64);
+                                reinterpret_cast<const float4*>(p.aux + row * p.ldaux + nc + c * 128 + half * 64);
 #pragma unroll
                             for (int i = 0; i < 16; i++) {
                                 const float4 a = ax[i];
@@ -682,7 +730,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
                                                                gelu_fast(__uint_as_float(rv[4 * i + 3])) * a.w);
                             }
                         } else if (EPI == EPI_CLAMP_F16 || EPI == EPI_CLAMP_SILU) {
-                            const float* b = p.aux ? p.aux + n0 + c * 128 + half * 64 : nullptr;
+                            const float* b = p.aux ? p.aux + nc + c * 128 + half * 64 : nullptr;
 #pragma unroll
                             for (int i = 0; i < 32; i++) {
                                 float v0 = fminf(fmaxf(__uint_as_float(rv[2 * i]), p.lo1), p.hi1);
@@ -702,7 +750,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
                             for (int i = 0; i < 32; i++)
                                 packed[i] = pack_half2(__uint_as_float(rv[2 * i]), __uint_as_float(rv[2 * i + 1]));
                         }
-                        emit(packed, n0 + c * 128 + half * 64, y, &mapC);
+                        emit(packed, nc + c * 128 + half * 64, y, &mapC);
                     }
                 }
             }
@@ -804,6 +852,10 @@ bool encode_weight_maps(DevWeight& w, int bn) {
         ok = encode_2d(&w.map_f16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.f16, w.K, w.N, BK,
                        uint32_t(w.N < bn ? w.N : bn), CU_TENSOR_MAP_SWIZZLE_128B) &&
              encode_2d(&w.map_f16_half, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.f16, w.K, w.N, BK, bn / 2,
+                       CU_TENSOR_MAP_SWIZZLE_128B) &&
+             encode_2d(&w.map_f16_quarter, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.f16, w.K, w.N, BK, bn / 4,
+                       CU_TENSOR_MAP_SWIZZLE_128B) &&
+             encode_2d(&w.map_f16_eighth, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.f16, w.K, w.N, BK, bn / 8,
                        CU_TENSOR_MAP_SWIZZLE_128B);
     return ok;
 }
@@ -933,8 +985,12 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
         p.kvh = g.kv_heads;
         p.eps = g.eps;
     }
-    // Weight boxes: kBN rows (map_f16, map_q8) or kBN / 2 rows (CTA pairs, 128-wide tiles).
+    // Weight boxes: kBN rows (map_f16, map_q8) or kBN / 2 rows (CTA pairs, 128-wide tiles);
+    // the pieces of split tail tiles use kBN / 2 rows, or kBN / 4 for the GeGLU gate and up halves.
     const CUtensorMap& mb = Q8 ? g.w->map_q8 : ((PAIR || BN != kBN) ? g.w->map_f16_half : g.w->map_f16);
+    p.split_from = 1 << 30;
+    p.split = 1;
+    const CUtensorMap* mp = &g.w->map_f16_half;
     CUtensorMap mc;
     EpiMaps em;
     if (RES) {
@@ -962,7 +1018,7 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
         const int cap = max_clusters(reinterpret_cast<const void*>(kern), csize, L::kThreads, L::kBytes, g.num_sms);
         const int clusters = row_blocks < cap ? row_blocks : cap;
         return launch_kernel(kern, dim3(csize * clusters), dim3(L::kThreads), L::kBytes, stream, csize, g.a->map, mb,
-                             g.w->map_scales, mc, em, p);
+                             g.w->map_scales, *mp, mc, em, p);
     }
     // Output map: boxes of 32 rows x 128 bytes (32 fp32 or 64 fp16 columns), 128-byte swizzle.
     const bool f32 = EPI == EPI_F32 || EPI == EPI_CLAMP_F32;
@@ -975,16 +1031,45 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
     em.y = mc;
     if (!PAIR) {
         const int tiles = (g.m_rows / BM) * (g.w->N / BN);
-        const int grid = tiles < g.num_sms ? tiles : g.num_sms;
+        int grid = tiles < g.num_sms ? tiles : g.num_sms;
+        // Split tiles (fp16 weights on 256-wide single-CTA tiles only).  With F full rounds of
+        // `grid` tiles and R < grid tiles left, the R tiles run as 2R half-width pieces when those
+        // fit in one round (2R <= grid), so the last round takes half a tile's time.  When every
+        // tile fits in one round, each tile runs as S pieces, S the largest power of two with
+        // S * tiles <= SMs, up to the narrowest piece the epilogue stores (32 fp32 columns, 64
+        // fp16 columns, 64 GeGLU output columns).
+        p.split_from = tiles;
+        if (!Q8 && BN == kBN && EPI != EPI_QKV && g.mode == GEMM_SPLIT) {
+            const bool f32 = EPI == EPI_F32 || EPI == EPI_CLAMP_F32;
+            const int max_split = epi_is_geglu(EPI) ? 2 : f32 ? 8 : 4;
+            if (tiles > grid) {
+                const int full = tiles / grid * grid, rest = tiles - full;
+                if (rest > 0 && 2 * rest <= grid) {
+                    p.split_from = full;
+                    p.split = 2;
+                }
+            } else {
+                int sp = 1;
+                while (sp < max_split && tiles * sp * 2 <= g.num_sms) sp *= 2;
+                if (sp > 1) {
+                    p.split_from = 0;
+                    p.split = sp;
+                    grid = tiles * sp;
+                }
+            }
+            // the B box of one piece: BN / S rows, or BN / 2S for the GeGLU gate and up halves
+            const int box = epi_is_geglu(EPI) ? BN / (2 * p.split) : BN / p.split;
+            mp = box == BN / 2 ? &g.w->map_f16_half : box == BN / 4 ? &g.w->map_f16_quarter : &g.w->map_f16_eighth;
+        }
         return launch_kernel(kern, dim3(grid), dim3(L::kThreads), L::kBytes, stream, 1, g.a->map, mb, g.w->map_scales,
-                             mc, em, p);
+                             *mp, mc, em, p);
     }
     // CTA pairs: clusters of 2, each pair looping over 256-row tiles.
     const int tiles = ((g.m_rows + 2 * BM - 1) / (2 * BM)) * (g.w->N / BN);
     const int cap = max_clusters(reinterpret_cast<const void*>(kern), 2, L::kThreads, L::kBytes, g.num_sms);
     const int pairs = tiles < cap ? tiles : cap;
     return launch_kernel(kern, dim3(2 * pairs), dim3(L::kThreads), L::kBytes, stream, 2, g.a->map, mb, g.w->map_scales,
-                         mc, em, p);
+                         *mp, mc, em, p);
 }
 
 template <int EPI>

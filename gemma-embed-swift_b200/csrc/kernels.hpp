@@ -95,7 +95,10 @@ struct DevWeight {
     int8_t* q8 = nullptr;
     __half* scales_t = nullptr;
     __half* f16 = nullptr;
-    CUtensorMap map_q8, map_scales, map_f16, map_f16_half;  // map_f16_half: boxes of BN/2 rows (CTA pairs)
+    // map_f16_half, _quarter, _eighth: boxes of BN/2, BN/4, BN/8 rows (CTA pairs and 128-wide
+    // tiles take BN/2; the pieces of split tiles take BN/S, the gate and up halves of a GeGLU
+    // piece BN/2S).
+    CUtensorMap map_q8, map_scales, map_f16, map_f16_half, map_f16_quarter, map_f16_eighth;
 };
 
 // A row-major fp16 activation matrix that feeds GEMMs as the A operand.
@@ -112,7 +115,11 @@ bool encode_activation_map(DevActivation& a);
 // 128 x 128 tiles, or CTA pairs (tcgen05.mma.cta_group::2, 256 x 256 tiles).  AUTO is single
 // CTAs with 128 x 256 tiles, the fastest of the three on the forward's shapes.  The Q8 path
 // always runs single CTAs with 128 x 256 tiles.
-enum GemmMode : int { GEMM_AUTO = 0, GEMM_SINGLE = 1, GEMM_PAIR = 2, GEMM_NARROW = 3 };
+// GEMM_SPLIT runs single-CTA 128 x 256 tiles as narrower pieces where that would shorten the
+// persistent schedule on paper (the last partial round, or every tile of a batch that leaves SMs
+// idle; see k_gemm).  Bit-identical to whole tiles, measured no faster on any forward shape
+// (bench.py's gemm_schedules), so only on request.
+enum GemmMode : int { GEMM_AUTO = 0, GEMM_SINGLE = 1, GEMM_PAIR = 2, GEMM_NARROW = 3, GEMM_SPLIT = 4 };
 
 struct GemmLaunch {
     const DevActivation* a;

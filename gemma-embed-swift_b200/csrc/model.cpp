@@ -34,7 +34,7 @@ int set_error(ge_model* m, int code, const std::string& msg) {
 
 namespace {
 
-constexpr int kQ8GemmMaxRows = 256;  // batches at or below this many rows read Q8 weights directly
+constexpr int kPresizeMaxRows = 262144;  // rows of the workspace reserved at load, at most
 
 
 bool read_config(const GgufFile& f, Config& c, LoadError& e) {
@@ -532,6 +532,16 @@ int load_model(ge_model* m, const char* path, const ge_load_opts* opts) {
     for (auto& dv : m->devs) {
         rc = load_device(m, dv, hw, norms, ropes, dense2, dense3, output, embw, c.has_ple ? &plpw : nullptr);
         if (rc) return rc;
+        // The workspace is sized at load for a whole batch of the token budget (or one longest
+        // sequence), so a stream of batches within the budget never stops to reallocate it,
+        // which would also drop every captured graph.  Larger packed batches still grow it.
+        const int rows = round_up(std::min(std::max(m->budget, c.max_tokens), kPresizeMaxRows), kRowTile);
+        const int seqs = 1024;
+        cudaError_t e = cudaSetDevice(dv.ordinal);
+        if (e == cudaSuccess) e = ensure_workspace(c, dv, rows, seqs, 16 * rows + 8 * seqs + 1024);
+        if (e != cudaSuccess)
+            return set_error(m, e == cudaErrorMemoryAllocation ? GE_ERR_OUT_OF_MEMORY : GE_ERR_GPU_FAILURE,
+                             std::string("GPU execution failed: workspace: ") + cudaGetErrorString(e));
     }
     return GE_OK;
 }
@@ -568,9 +578,23 @@ void store_graph(Device& d, const GraphKey& k, cudaGraphExec_t exec, int64_t lau
     d.graphs.push_back(g);
 }
 
+constexpr size_t kMaxSeenKeys = 64;
+
+bool seen_before(Device& d, const GraphKey& k) {
+    for (auto it = d.seen_keys.begin(); it != d.seen_keys.end(); ++it)
+        if (*it == k) {
+            d.seen_keys.erase(it);
+            return true;
+        }
+    if (d.seen_keys.size() >= kMaxSeenKeys) d.seen_keys.erase(d.seen_keys.begin());
+    d.seen_keys.push_back(k);
+    return false;
+}
+
 void clear_graphs(Device& d) {
     for (auto& g : d.graphs) cudaGraphExecDestroy(g.exec);
     d.graphs.clear();
+    d.seen_keys.clear();
 }
 
 // ------------------------------------------------------------------ forward
@@ -687,7 +711,10 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     cudaStream_t ks = st;  // the stream kernels are launched on (the capture stream while capturing)
     // ---- layers (MetalForward.encode, MetalForward.swift:364-423)
     const int D = c.hidden;
-    const bool q8 = rows <= kQ8GemmMaxRows || (m->flags & GE_LOAD_Q8_ONLY);
+    // Every GEMM reads the fp16-resident weights unless the model keeps only the Q8_0 planes: the
+    // in-shared-memory dequantisation was measured slower at every batch size from 128 rows up
+    // (bench.py's q8_gemm sweep), where it also streams fewer weight bytes.
+    const bool q8 = (m->flags & GE_LOAD_Q8_ONLY) != 0;
     auto gemm = [&](const DevActivation& A, const DevWeight& W, void* out, int ldo, int epi, const float* aux = nullptr,
                     int ldaux = 0) {
         GemmLaunch g;
@@ -1001,8 +1028,10 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         return GE_OK;
     };
     // Captured CUDA graphs replay the whole launch sequence of a batch shape with one call
-    // (kernel arguments, tensor maps included, are fixed per workspace and shape).
-    const bool use_graph = !(m->flags & GE_LOAD_NO_GRAPHS) && !a.profile && a.trace_layer < -1;
+    // (kernel arguments, tensor maps included, are fixed per workspace and shape).  A shape is
+    // captured the second time it runs: the first run launches directly, so a stream of
+    // distinct batches (every new length mix is a new shape) costs no capture it never replays.
+    bool use_graph = !(m->flags & GE_LOAD_NO_GRAPHS) && !a.profile && a.trace_layer < -1;
     GraphKey gk;
     gk.rows = rows;
     gk.ntok = ntok;
@@ -1013,6 +1042,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     gk.tokens = reinterpret_cast<uintptr_t>(tokens);
     gk.vectors = reinterpret_cast<uintptr_t>(a.vectors);
     GraphEntry* ge_ = use_graph ? find_graph(d, gk) : nullptr;
+    if (use_graph && !ge_ && !seen_before(d, gk)) use_graph = false;
     if (ge_) {
         if ((e = cudaGraphLaunch(ge_->exec, st)) != cudaSuccess) return gpu_fail(e, "graph launch");
         launches += ge_->launches;
@@ -1034,6 +1064,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         cudaGraphDestroy(graph);
         if (e != cudaSuccess) return gpu_fail(e, "graph instantiation");
         store_graph(d, gk, exec, launches - before);
+        m->graph_captures++;
         if ((e = cudaGraphLaunch(exec, st)) != cudaSuccess) return gpu_fail(e, "graph launch");
     } else {
         const int rc = launch_all();

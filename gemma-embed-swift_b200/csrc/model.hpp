@@ -108,6 +108,10 @@ struct Device {
     Workspace ws;
     std::vector<GraphEntry> graphs;  // at most kMaxGraphs, least recently used evicted
     uint64_t graph_clock = 0;
+    // Batch shapes seen once and not captured (at most kMaxSeenKeys, oldest dropped): a shape
+    // is captured the second time it runs, so a stream of distinct batches never pays for a
+    // capture it does not replay.
+    std::vector<GraphKey> seen_keys;
     std::vector<void*> allocations;
     VisionDev vis;  // the image encoder's weights and workspace, when one is loaded
     AudioDev aud;   // the audio encoder's weights and workspace, when one is loaded
@@ -144,6 +148,7 @@ struct ge_model {
     int64_t file_size = 0;
     std::atomic<int64_t> launches{0};  // kernel launches issued by this model so far
     std::atomic<int64_t> h2d_bytes{0}, d2h_bytes{0};  // host <-> device copies of the forwards so far
+    std::atomic<int64_t> graph_captures{0};           // CUDA graphs captured and instantiated so far
     std::unique_ptr<ge_tokenizer> tokenizer;  // null when the file carries no tokenizer
     // The image encoder (LoadOptions.imageEncoder): its file, configuration and the tokens that
     // frame an image's rows in the text sequence (SpanMarkers.image, Model/InputRow.swift:43-45).
@@ -237,6 +242,8 @@ GraphEntry* find_graph(Device& d, const GraphKey& k);
 // longest first onto the least-loaded device (cost n + n^2 / 2048), each in original order.
 std::vector<std::vector<int>> shard_sequences(const ge_seq* seqs, int nseq, int ndev);
 void store_graph(Device& d, const GraphKey& k, cudaGraphExec_t exec, int64_t launches);
+// True when `k` ran before without a capture; otherwise remembers it and returns false.
+bool seen_before(Device& d, const GraphKey& k);
 void clear_graphs(Device& d);
 int set_error(ge_model* m, int code, const std::string& msg);
 }  // namespace ge

@@ -2,6 +2,7 @@
 #include <string.h>
 
 #include <string>
+#include <cmath>
 #include <vector>
 
 #include "gemma_embed_testing.h"
@@ -155,7 +156,8 @@ int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int3
     g.aux = static_cast<const float*>(daux.p);
     g.ldaux = n;
     g.use_q8 = use_q8 == 1;
-    g.mode = use_q8 == 2 ? ge::GEMM_PAIR : use_q8 == 3 ? ge::GEMM_NARROW : ge::GEMM_SINGLE;
+    g.mode = use_q8 == 2 ? ge::GEMM_PAIR : use_q8 == 3 ? ge::GEMM_NARROW : use_q8 == 4 ? ge::GEMM_SPLIT
+                                                                                    : ge::GEMM_SINGLE;
     g.err = static_cast<int*>(derr.p);
     g.num_sms = sms;
     TRY(ge::launch_gemm(g, nullptr));
@@ -170,6 +172,78 @@ int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int3
         TRY(cudaMemcpy(h.data(), dout.p, h.size() * 2, cudaMemcpyDeviceToHost));
         for (size_t i = 0; i < h.size(); i++) out[i] = h2f(h[i]);
     }
+    return GE_OK;
+}
+
+int ge_test_gemm_time(int32_t m, int32_t k, int32_t n, int32_t epilogue, int32_t path, int32_t reps, double* us) {
+    if (m <= 0 || m % ge::kRowTile || k <= 0 || n <= 0 || k % 64 || n % 256 || epilogue < 0 || epilogue > 2 ||
+        path < 0 || path > 4 || reps <= 0 || !us)
+        return fail(GE_ERR_INVALID_OPTIONS,
+                    "invalid options: m % 128 == 0, k % 64 == 0, n % 256 == 0, epilogue 0..2, path 0..4");
+    int dev = 0, sms = 0;
+    TRY(cudaGetDevice(&dev));
+    TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    // Seeded operands of the model's scale: activations uniform in [-1, 1], Q8_0 weights with
+    // scales near 1/sqrt(k) (values matter only through the power they draw).
+    uint64_t state = 0x9E3779B97F4A7C15ull ^ (uint64_t(m) << 32) ^ uint64_t(n * 131 + k);
+    auto next = [&]() {
+        state += 0x9E3779B97F4A7C15ull;
+        uint64_t z = state;
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        return z ^ (z >> 31);
+    };
+    std::vector<uint16_t> a(size_t(m) * k);
+    for (auto& v : a) v = f2h(float(int(next() % 2001) - 1000) / 1000.0f);
+    std::vector<uint8_t> w(size_t(n) * (k / 32) * 34);
+    const uint16_t scale = f2h(1.0f / (127.0f * std::sqrt(float(k))));
+    for (size_t b = 0; b < size_t(n) * (k / 32); b++) {
+        memcpy(&w[b * 34], &scale, 2);
+        for (int j = 0; j < 32; j++) w[b * 34 + 2 + j] = uint8_t(int(next() % 255) - 127);
+    }
+    DevBuf da, dq, ds, dh, dout, derr;
+    ge::DevWeight W;
+    ge::DevActivation A;
+    int rc = upload_weight(w.data(), n, k, dq, ds, dh, W);
+    if (rc != GE_OK) return rc;
+    if ((rc = upload_activation(a.data(), m, k, m, da, A)) != GE_OK) return rc;
+    const int out_cols = ge::epi_is_geglu(epilogue) ? n / 2 : n;
+    TRY(dout.alloc(size_t(m) * out_cols * (epilogue == 0 ? 4 : 2)));
+    TRY(derr.alloc(sizeof(int)));
+    TRY(cudaMemset(derr.p, 0, sizeof(int)));
+    TRY(ge::configure_gemm_kernels());
+    ge::GemmLaunch g;
+    g.a = &A;
+    g.w = &W;
+    g.m_rows = m;
+    g.out = dout.p;
+    g.ldo = out_cols;
+    g.epilogue = epilogue;
+    g.use_q8 = path == 1;
+    g.mode = path == 2 ? ge::GEMM_PAIR : path == 3 ? ge::GEMM_NARROW : path == 4 ? ge::GEMM_SPLIT
+                                                                            : ge::GEMM_SINGLE;
+    g.err = static_cast<int*>(derr.p);
+    g.num_sms = sms;
+    cudaStream_t st = nullptr;
+    TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    cudaError_t e = cudaEventCreate(&e0);
+    if (e == cudaSuccess) e = cudaEventCreate(&e1);
+    for (int i = 0; i < 3 && e == cudaSuccess; i++) e = ge::launch_gemm(g, st);
+    if (e == cudaSuccess) e = cudaEventRecord(e0, st);
+    for (int i = 0; i < reps && e == cudaSuccess; i++) e = ge::launch_gemm(g, st);
+    if (e == cudaSuccess) e = cudaEventRecord(e1, st);
+    if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+    float ms = 0.f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    cudaStreamDestroy(st);
+    TRY(e);
+    int herr = 0;
+    TRY(cudaMemcpy(&herr, derr.p, sizeof(int), cudaMemcpyDeviceToHost));
+    if (herr) return fail(herr, "GPU execution failed: a device-side wait timed out");
+    *us = double(ms) * 1000.0 / reps;
     return GE_OK;
 }
 

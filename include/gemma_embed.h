@@ -126,6 +126,7 @@ typedef struct ge_info {
     int32_t audio_feed_forward_size;
     int32_t audio_mel_bins;
     int32_t audio_projection_dim;
+    int64_t graph_captures; /* CUDA graphs captured so far: a batch shape is captured the second time it runs */
 } ge_info;
 
 /* One kernel class of a profiling forward (ge_profile). */

@@ -129,28 +129,39 @@ def test_full_model_long_sequence_properties(full, synth):
 
 
 def test_graph_replay_matches_direct_launches(ge, synth, cuda_device):
-    """A captured CUDA graph, replayed for new ids of the same batch shape, gives the bits of
-    direct kernel launches."""
+    """A batch shape runs by direct launches the first time, is captured as a CUDA graph the
+    second time and replayed after that, for new ids of the same shape, with the bits of direct
+    kernel launches throughout; a stream of distinct shapes captures nothing."""
     path = synth.model_path("gemma-embedding", seed=1, layers=6, vocab=4096)
     with ge.EmbeddingModel.load(path) as graphed, \
             ge.EmbeddingModel.load(path, ge.LoadOptions(use_graphs=False)) as direct:
         lens = [37, 300, 5, 129]
         first = synth.random_sequences(lens, seed=41, vocab=4096)
         second = synth.random_sequences(lens, seed=42, vocab=4096)
-        for seqs in (first, second, first):
+        captures = []
+        for seqs in (first, second, first, second):
             assert graphed.embed_tokens(seqs).tobytes() == direct.embed_tokens(seqs).tobytes()
+            captures.append(graphed.counters()["graph_captures"])
+        assert captures == [captures[0], captures[0] + 1, captures[0] + 1, captures[0] + 1]
+        assert direct.counters()["graph_captures"] == 0
+        before = graphed.counters()["graph_captures"]
+        for i in range(5):  # five batch shapes, each seen once
+            graphed.embed_tokens(synth.random_sequences([50 + 20 * i, 7, 200], seed=60 + i, vocab=4096))
+        assert graphed.counters()["graph_captures"] == before
 
 
 @pytest.mark.parametrize("arch", ["gemma-embedding", "gemma-embedding2"])
 @pytest.mark.parametrize("use_graphs", [True, False])
-@pytest.mark.parametrize("option", ["programmatic_launch"])
+@pytest.mark.parametrize("option", [dict(programmatic_launch=False), dict(q8_only=True)], ids=["no_pdl", "q8_only"])
 def test_launch_options_do_not_change_results(ge, synth, cuda_device, arch, use_graphs, option):
     """Programmatic dependent launch (each kernel waits in-kernel for its predecessor) gives the
-    bits of plain serialised launches, graphed or direct."""
+    bits of plain serialised launches, graphed or direct; and GEMMs that dequantise the Q8_0
+    planes in shared memory (GE_LOAD_Q8_ONLY) give the bits of the fp16-resident weights."""
     path = synth.model_path(arch, seed=1, layers=6, vocab=4096)
     with ge.EmbeddingModel.load(path, ge.LoadOptions(use_graphs=use_graphs)) as on, \
-            ge.EmbeddingModel.load(path, ge.LoadOptions(use_graphs=use_graphs, **{option: False})) as off:
-        for seed, lens in ((51, [37, 300, 5, 129]), (52, [700, 1, 64]), (51, [37, 300, 5, 129])):
+            ge.EmbeddingModel.load(path, ge.LoadOptions(use_graphs=use_graphs, **option)) as off:
+        for seed, lens in ((51, [37, 300, 5, 129]), (52, [700, 1, 64]), (53, [100, 60, 1]), (51, [37, 300, 5, 129]),
+                           (53, [100, 60, 1])):
             seqs = synth.random_sequences(lens, seed=seed, vocab=4096)
             assert on.embed_tokens(seqs).tobytes() == off.embed_tokens(seqs).tobytes()
 
@@ -162,8 +173,7 @@ def test_fused_forward(ge, synth, oracle, cuda_device, arch, fused):
     """The load options that change the kernel sequence: the residual steps fused into their
     projections (row clusters, GE_LOAD_FUSED_RESIDUAL) and the q/k/v norms and RoPE fused into the
     q/k/v projection's epilogue (GE_LOAD_FUSED_QKV): oracle parity at the same cosine bar and
-    bit-identical vectors across batch compositions (small batches take the Q8 path, large ones
-    fp16 weights)."""
+    bit-identical vectors across batch compositions."""
     path = synth.model_path(arch, seed=1, layers=6, vocab=4096)
     ref = oracle.OracleModel(path)
     with ge.EmbeddingModel.load(path, ge.LoadOptions(**fused)) as model:

@@ -108,6 +108,39 @@ def test_gemm_epilogues(ge, synth, oracle, cuda_device, use_q8):
     assert max_rel(got, want) < TOL_F16
 
 
+# (k, n, m) on 148 SMs: 150 tiles of 128 x 256 (two past the full round) and 153 GeGLU tiles
+# (five past it) run their last round as half-width pieces; 3, 18 and 40 tiles (one round with
+# SMs to spare) run every tile as 2, 4 or 8 pieces.
+SPLIT_CASES = [(768, 768, 128 * 50), (1152, 768, 128 * 50), (768, 1280, 128 * 30), (768, 2304, 128 * 17),
+               (768, 768, 128), (768, 2304, 256), (1152, 768, 1024), (768, 1280, 1024)]
+
+
+@pytest.mark.parametrize("k,n,m", SPLIT_CASES)
+def test_gemm_split_tiles_match_whole_tiles(ge, synth, cuda_device, k, n, m):
+    """Path 4 runs tiles as narrower pieces where that would shorten the persistent schedule (a
+    GeGLU piece: part of the gate rows and the up rows they pair with); path 0 keeps every tile
+    whole.  The pieces multiply the same rows over the same K steps, so every epilogue gives
+    identical bits, and the results match float64."""
+    a, wq, wd = make_case(synth, m, k, n, seed=k * 7 + n + m)
+    a64 = a.astype(np.float64)
+    for epi in (0, 1):
+        split = gemm(ge, a, wq, n, epi, use_q8=4)
+        whole = gemm(ge, a, wq, n, epi, use_q8=0)
+        assert split.tobytes() == whole.tobytes(), epi
+    assert max_rel(split, a64 @ wd.T) < TOL_F16
+    assert max_rel(gemm(ge, a, wq, n, 0, use_q8=4), a64 @ wd.T) < TOL_F32
+    if n % 256 == 0 and n >= 1024:
+        aux = np.random.default_rng(n).normal(size=(m, n)).astype(np.float32)
+        assert gemm(ge, a, wq, n, 3, 4, aux=aux).tobytes() == gemm(ge, a, wq, n, 3, 0, aux=aux).tobytes()
+    if n == 2304:  # gate/up interleaved in blocks of 128 rows, as the loader lays them out
+        split = gemm(ge, a, wq, n, 2, use_q8=4)
+        assert split.tobytes() == gemm(ge, a, wq, n, 2, use_q8=0).tobytes()
+        g = np.concatenate([a64 @ wd[j * 256:j * 256 + 128].T for j in range(n // 256)], axis=1)
+        u = np.concatenate([a64 @ wd[j * 256 + 128:(j + 1) * 256].T for j in range(n // 256)], axis=1)
+        want = 0.5 * g * (1 + np.tanh(0.7978845608028654 * (g + 0.044715 * g ** 3))) * u  # GELU (tanh form)
+        assert max_rel(split, want) < TOL_F16
+
+
 def test_gemm_rows_are_independent_of_the_batch(ge, synth, cuda_device):
     """A row's result does not depend on the other rows of the batch or the tile it lands in
     (KernelTests.swift:323-339, MetalForwardTests.swift:75-97)."""
