@@ -59,6 +59,9 @@ def args_():
     p.add_argument("--profile-reps", type=int, default=5)
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="bound of the CPU-baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--legs", choices=["all", "core"], default="all",
+                   help="core: only the device-resident steps, the end-to-end steps and the kernel profile "
+                        "(for profiler captures)")
     p.add_argument("--q8-sweep", choices=["on", "off"], default="on",
                    help="time the Q8_0 (dequantise in shared memory) and fp16-weight GEMM paths by batch size")
     p.add_argument("--fused-qkv", choices=["on", "off"], default="off",
@@ -219,6 +222,10 @@ def main():
         if dist is not None:
             dist.barrier()
 
+    # A host-side (gloo) group for waits while rank 0 drives every GPU: an NCCL barrier would
+    # leave a kernel spinning on each waiting rank's GPU beside rank 0's work there.
+    host_group = dist.new_group(backend="gloo") if dist is not None else None
+
     # Rank 0 writes the synthetic GGUF first; the others then read the cached file.
     if rank == 0:
         path = synth.model_path(a.arch, seed=0)
@@ -280,6 +287,7 @@ def main():
         roofline["traffic"] = traffic
         roofline["traffic_source"] = NCU_DRAM_BYTES_CONFIG2["source"] if traffic else None
 
+    full = a.legs == "all"
     # ---- end to end through the public API with host buffers: EmbeddingModel.embed on the
     # batch's token ids (one packed batch), Matryoshka 256-d L2-normalised vectors back
     texts = [np.asarray(q, dtype=np.int32) for q in seqs]
@@ -302,100 +310,110 @@ def main():
     h2d = (info1.host_to_device_bytes - info0.host_to_device_bytes) // a.steps
     d2h = (info1.device_to_host_bytes - info0.device_to_host_bytes) // a.steps
 
-    # ---- end to end from strings: the same lengths as seeded synthetic prose, tokenised inside
-    # the timed region (EmbeddingModel.embed on texts with the default document prefix)
-    tk = model.tokenizer
-    strings = text_batch(synth, tk, [len(q) for q in seqs], seed=1000 + rank)
-    sopts = ge.EmbedOptions(max_tokens=opts.max_tokens, dimensions=256)
-    for _ in range(2):
-        model.embed(strings, sopts)
-    barrier()
-    t0 = time.perf_counter()
-    for _ in range(a.steps):
-        sout = model.embed(strings, sopts)
-    t1 = time.perf_counter()
-    barrier()
-    text_tokens = sum(e.token_count for e in sout)
-    et_ms, et_tok = reduce_max_sum(dist, (t1 - t0) * 1000.0, text_tokens * a.steps)
-    e2e_text = {"value": et_tok / (et_ms / 1000.0), "unit": "tokens/s", "tokens_per_step": et_tok // a.steps,
-                "api": "ge_embed_texts (EmbeddingModel.embed on strings), document prefix, 256-d normalised output"}
-    tok_stats = tokenizer_throughput(synth, tk, path) if rank == 0 else None
+    e2e_text, tok_stats, e2e_stream, workloads, strong = None, None, None, {}, None
+    if full:
+        # ---- end to end from strings: the same lengths as seeded synthetic prose, tokenised inside
+        # the timed region (EmbeddingModel.embed on texts with the default document prefix)
+        tk = model.tokenizer
+        strings = text_batch(synth, tk, [len(q) for q in seqs], seed=1000 + rank)
+        sopts = ge.EmbedOptions(max_tokens=opts.max_tokens, dimensions=256)
+        for _ in range(2):
+            model.embed(strings, sopts)
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(a.steps):
+            sout = model.embed(strings, sopts)
+        t1 = time.perf_counter()
+        barrier()
+        text_tokens = sum(e.token_count for e in sout)
+        et_ms, et_tok = reduce_max_sum(dist, (t1 - t0) * 1000.0, text_tokens * a.steps)
+        e2e_text = {"value": et_tok / (et_ms / 1000.0), "unit": "tokens/s", "tokens_per_step": et_tok // a.steps,
+                    "api": "ge_embed_texts (EmbeddingModel.embed on strings), document prefix, 256-d normalised output"}
+        tok_stats = tokenizer_throughput(synth, tk, path) if rank == 0 else None
 
-    # ---- a stream of distinct batches through the same API: new lengths (a new batch shape)
-    # every step, as an embedding service sees them; graph captures per step beside it
-    stream_batches = [[np.asarray(q, dtype=np.int32) for q in synth.config_sequences(2, seed=10_000 + 100 * rank + i)]
-                      for i in range(a.steps + 2)]
-    for b in stream_batches[:2]:
-        model.embed(b, opts)
-    barrier()
-    c0 = model.counters()
-    st_ms, st_tok = [], 0
-    t0 = time.perf_counter()
-    for b in stream_batches[2:]:
-        s0 = time.perf_counter()
-        model.embed(b, opts)
-        st_ms.append((time.perf_counter() - s0) * 1000.0)
-        st_tok += sum(len(q) for q in b)
-    t1 = time.perf_counter()
-    barrier()
-    c1 = model.counters()
-    es_ms, es_tok = reduce_max_sum(dist, (t1 - t0) * 1000.0, st_tok)
-    st_ms.sort()
-    e2e_stream = {"value": es_tok / (es_ms / 1000.0), "unit": "tokens/s", "steps": a.steps,
-                  "tokens_per_step": es_tok // a.steps,
-                  "graph_captures_per_step": (c1["graph_captures"] - c0["graph_captures"]) / a.steps,
-                  "latency_ms_p50": pct(st_ms, 50), "latency_ms_p99": pct(st_ms, 99),
-                  "api": "ge_embed_tokens (EmbeddingModel.embed), a distinct seeded config-2 batch every step, "
-                         "256-d normalised output"}
+    if full:
+        # ---- a stream of distinct batches through the same API: new lengths (a new batch shape)
+        # every step, as an embedding service sees them; graph captures per step beside it
+        stream_batches = [[np.asarray(q, dtype=np.int32) for q in synth.config_sequences(2, seed=10_000 + 100 * rank + i)]
+                          for i in range(a.steps + 2)]
+        for b in stream_batches[:2]:
+            model.embed(b, opts)
+        barrier()
+        c0 = model.counters()
+        st_ms, st_tok = [], 0
+        t0 = time.perf_counter()
+        for b in stream_batches[2:]:
+            s0 = time.perf_counter()
+            model.embed(b, opts)
+            st_ms.append((time.perf_counter() - s0) * 1000.0)
+            st_tok += sum(len(q) for q in b)
+        t1 = time.perf_counter()
+        barrier()
+        c1 = model.counters()
+        es_ms, es_tok = reduce_max_sum(dist, (t1 - t0) * 1000.0, st_tok)
+        st_ms.sort()
+        e2e_stream = {"value": es_tok / (es_ms / 1000.0), "unit": "tokens/s", "steps": a.steps,
+                      "tokens_per_step": es_tok // a.steps,
+                      "graph_captures_per_step": (c1["graph_captures"] - c0["graph_captures"]) / a.steps,
+                      "latency_ms_p50": pct(st_ms, 50), "latency_ms_p99": pct(st_ms, 99),
+                      "api": "ge_embed_tokens (EmbeddingModel.embed), a distinct seeded config-2 batch every step, "
+                             "256-d normalised output"}
 
-    # ---- the metric's literal 64 x 512 batch and config 3, device-resident, each with its roofline
-    workloads = {}
-    if a.config == 2:
-        for name, cfg in (("64x512", 4), ("config 3", 3)):
-            wseqs = synth.config_sequences(cfg, seed=rank)
-            wt, _, wr = ge.pack(wseqs)
-            w_tokens = torch.from_numpy(wt).cuda()
-            w_out = torch.empty((len(wr), od), dtype=torch.float32, device="cuda")
-            wsteps = max(3, min(a.steps, 10))
-            for _ in range(3):
-                model.forward_device(w_tokens, wr, w_out, stream=stream, device=local)
+    if full:
+        # ---- the metric's literal 64 x 512 batch and config 3, device-resident, each with its roofline
+        workloads = {}
+        if a.config == 2:
+            for name, cfg in (("64x512", 4), ("config 3", 3)):
+                wseqs = synth.config_sequences(cfg, seed=rank)
+                wt, _, wr = ge.pack(wseqs)
+                w_tokens = torch.from_numpy(wt).cuda()
+                w_out = torch.empty((len(wr), od), dtype=torch.float32, device="cuda")
+                wsteps = max(3, min(a.steps, 10))
+                for _ in range(3):
+                    model.forward_device(w_tokens, wr, w_out, stream=stream, device=local)
+                barrier()
+                torch.cuda.synchronize()
+                wev = [torch.cuda.Event(enable_timing=True) for _ in range(wsteps + 1)]
+                wev[0].record(stream)
+                for i in range(wsteps):
+                    model.forward_device(w_tokens, wr, w_out, stream=stream, device=local)
+                    wev[i + 1].record(stream)
+                torch.cuda.synchronize()
+                w_step = sorted(wev[i].elapsed_time(wev[i + 1]) for i in range(wsteps))
+                w_ms, w_tok = reduce_max_sum(dist, wev[0].elapsed_time(wev[-1]), len(wt) * wsteps)
+                entry = {"value": w_tok / (w_ms / 1000.0), "unit": "tokens/s", "ms_per_step": w_ms / wsteps,
+                         "steps": wsteps, "tokens_per_rank": int(len(wt)), "texts_per_rank": len(wr),
+                         "latency_ms_p50": pct(w_step, 50), "latency_ms_p99": pct(w_step, 99)}
+                if rank == 0:
+                    wprof = model.profile(wt, wr, reps=max(1, a.profile_reps // 2))
+                    entry["roofline"] = top_roofline(wprof, peaks())
+                workloads[name] = entry
+                del w_tokens, w_out
+            if a.arch == "gemma-embedding" and rank == 0:
+                workloads["gemma-embedding2 config 2"] = eg2_workload(ge, synth, seqs, a.profile_reps)
+
+    if full:
+        # ---- strong scaling through the library's dispatcher: rank 0 alone embeds one config-2
+        # batch on devices 0..N-1 (sequences sharded longest first onto the least-loaded device,
+        # each share packed and run on its own host thread and stream, vectors gathered on the host)
+        strong = None
+        if world > 1:
             barrier()
             torch.cuda.synchronize()
-            wev = [torch.cuda.Event(enable_timing=True) for _ in range(wsteps + 1)]
-            wev[0].record(stream)
-            for i in range(wsteps):
-                model.forward_device(w_tokens, wr, w_out, stream=stream, device=local)
-                wev[i + 1].record(stream)
-            torch.cuda.synchronize()
-            w_step = sorted(wev[i].elapsed_time(wev[i + 1]) for i in range(wsteps))
-            w_ms, w_tok = reduce_max_sum(dist, wev[0].elapsed_time(wev[-1]), len(wt) * wsteps)
-            entry = {"value": w_tok / (w_ms / 1000.0), "unit": "tokens/s", "ms_per_step": w_ms / wsteps,
-                     "steps": wsteps, "tokens_per_rank": int(len(wt)), "texts_per_rank": len(wr),
-                     "latency_ms_p50": pct(w_step, 50), "latency_ms_p99": pct(w_step, 99)}
+            # The other ranks wait on the host, with nothing of theirs running on any GPU.
             if rank == 0:
-                wprof = model.profile(wt, wr, reps=max(1, a.profile_reps // 2))
-                entry["roofline"] = top_roofline(wprof, peaks())
-            workloads[name] = entry
-            del w_tokens, w_out
-
-    # ---- strong scaling through the library's dispatcher: rank 0 alone embeds one config-2
-    # batch on devices 0..N-1 (sequences sharded longest first onto the least-loaded device,
-    # each share packed and run on its own host thread and stream, vectors gathered on the host)
-    strong = None
-    if world > 1:
-        barrier()
-        if rank == 0:
-            strong = strong_scaling(ge, path, [np.asarray(q, dtype=np.int32) for q in synth.config_sequences(2, seed=0)],
-                                    opts, world, a.steps)
-        barrier()
-    else:
-        strong = {"value": e2e, "unit": "tokens/s", "devices": 1, "note": "one GPU: the e2e measurement"}
+                strong = strong_scaling(ge, path, [np.asarray(q, dtype=np.int32) for q in synth.config_sequences(2, seed=0)],
+                                        opts, world, a.steps)
+            dist.barrier(group=host_group)
+        else:
+            strong = {"value": e2e, "unit": "tokens/s", "devices": 1, "note": "one GPU: the e2e measurement"}
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         cpu = cpu_baseline(path, seqs, a.cpu_seconds)
-    q8 = q8_gemm_sweep(ge, synth, path) if rank == 0 and world == 1 and a.config == 2 and a.q8_sweep == "on" else None
-    gemm_paths = gemm_schedule_sweep() if rank == 0 and world == 1 and a.config == 2 and a.q8_sweep == "on" else None
+    sweeps = full and rank == 0 and world == 1 and a.config == 2 and a.q8_sweep == "on"
+    q8 = q8_gemm_sweep(ge, synth, path) if sweeps else None
+    gemm_paths = gemm_schedule_sweep() if sweeps else None
 
     if rank == 0:
         line = {"metric": "embedded tokens/sec (config 2: 64 texts x 32..512 tokens)", "value": value,
@@ -515,6 +533,30 @@ def gemm_schedule_sweep(rows_list=(1024, 2432, 19584), reps=20):
             if best:
                 entry["best_frac_of_bf16_burst"] = 2.0 * rows * n * k / (best * 1e-6) / 1e12 / pk["bf16_tflops"]
             out.append(entry)
+    return out
+
+
+def eg2_workload(ge, synth, seqs, reps):
+    """The reference's own architecture (EmbeddingGemma 2: hidden 512, per-layer inputs, global
+    layers with head dim 512 on the CUDA-core attention kernel, output projection) on the
+    config-2 batch: one forward's kernel profile (ge_profile), rank 0 only."""
+    path2 = synth.model_path("gemma-embedding2", seed=0)
+    toks, _, ranges = ge.pack(seqs)
+    with ge.EmbeddingModel.load(path2, ge.LoadOptions(batch_token_budget=BATCH_BUDGET)) as m2:
+        for _ in range(3):
+            m2.forward_packed(toks, None, ranges)
+        prof = m2.profile(toks, ranges, reps=max(1, reps))
+    fwd_ms = sum(p["ms_per_launch"] * p["launches_per_forward"] for p in prof)
+    roof = top_roofline(prof, peaks())
+    out = {"tokens": int(len(toks)), "forward_ms_sum_of_kernels": fwd_ms, "tokens_per_s_from_kernels": len(toks) / (fwd_ms / 1000.0),
+           "roofline": roof,
+           "kernels": [{k: (round(v, 5) if isinstance(v, float) else v) for k, v in p.items()} for p in prof]}
+    for p in prof:
+        if p["name"] == "attention_global":  # head dim 512 (CUDA cores)
+            sec = p["ms_per_launch"] / 1000.0
+            out["attention_hd512"] = {"us_per_launch": p["ms_per_launch"] * 1000.0,
+                                      "tflops": p["flops_per_launch"] / sec / 1e12,
+                                      "launches_per_forward": p["launches_per_forward"]}
     return out
 
 

@@ -269,12 +269,124 @@ __global__ void k_qkv_norm_rope(const __half* __restrict__ qkv, int ntok, int ro
     }
 }
 
+// Head dim 256: a half-warp per token (lane l of the half holds elements 8l .. 8l + 7 of each
+// 128-element half of every head slot: 16-byte loads and stores), two tokens per warp, every
+// slot of both tokens loaded before the first is normalised; the norm weights are read as
+// float4.  Same steps as k_qkv_norm_rope (sum of squares, weighted norm, NeoX rotation of the
+// pairs (j, j + 128), v unweighted), with the sum of squares reduced over 16 lanes.
+template <int S>
+__global__ void __launch_bounds__(256, 3) k_qkv_norm_rope_hw(const __half* __restrict__ qkv, int ntok, int rows, int heads, int kvh,
+                                   const float* __restrict__ qw, const float* __restrict__ kw,
+                                   const int32_t* __restrict__ pos, const float* __restrict__ rope, float eps,
+                                   __half* __restrict__ q, __half* __restrict__ k, __half* __restrict__ v) {
+    pdl_wait();
+    pdl_launch_if_one_wave();
+    constexpr int HD = 256, HALF = 128;
+    const int lane = threadIdx.x & 31;
+    const int row = (blockIdx.x * kRowsPerBlock + (threadIdx.x >> 5)) * 2 + (lane >> 4);
+    if (row >= rows) return;  // the two halves of a warp reduce apart, so each may leave alone
+    const unsigned mask = lane < 16 ? 0x0000ffffu : 0xffff0000u;
+    const int c = (lane & 15) * 8;
+    const bool live = row < ntok;
+    const __half* src = qkv + long(row) * S * HD;
+    uint4 ra[S], rb[S];
+#pragma unroll
+    for (int s = 0; s < S; s++) {
+        ra[s] = live ? *reinterpret_cast<const uint4*>(src + s * HD + c) : make_uint4(0u, 0u, 0u, 0u);
+        rb[s] = live ? *reinterpret_cast<const uint4*>(src + s * HD + HALF + c) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    float cs_c[8], cs_s[8];
+    if (live) {
+        const float4* cs = reinterpret_cast<const float4*>(rope + long(pos[row]) * HD + 2 * c);  // [pair][cos, sin]
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float4 f = cs[i];
+            cs_c[2 * i] = f.x;
+            cs_s[2 * i] = f.y;
+            cs_c[2 * i + 1] = f.z;
+            cs_s[2 * i + 1] = f.w;
+        }
+    }
+#pragma unroll
+    for (int slot = 0; slot < S; slot++) {
+        __half* dst;
+        const float* w = nullptr;
+        if (slot < heads) {
+            dst = q + long(row) * heads * HD + slot * HD;
+            w = qw;
+        } else if (slot < heads + kvh) {
+            dst = k + long(row) * kvh * HD + (slot - heads) * HD;
+            w = kw;
+        } else {
+            dst = v + long(row) * kvh * HD + (slot - heads - kvh) * HD;
+        }
+        float a[8], b[8];
+        const __half2* ha = reinterpret_cast<const __half2*>(&ra[slot]);
+        const __half2* hb = reinterpret_cast<const __half2*>(&rb[slot]);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float2 fa = __half22float2(ha[i]), fb = __half22float2(hb[i]);
+            a[2 * i] = fa.x;
+            a[2 * i + 1] = fa.y;
+            b[2 * i] = fb.x;
+            b[2 * i + 1] = fb.y;
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) ss += a[i] * a[i] + b[i] * b[i];
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(mask, ss, o);
+        const float inv = 1.0f / sqrtf(ss / float(HD) + eps);
+        if (w) {
+            const float4 wa0 = *reinterpret_cast<const float4*>(w + c), wa1 = *reinterpret_cast<const float4*>(w + c + 4);
+            const float4 wb0 = *reinterpret_cast<const float4*>(w + HALF + c);
+            const float4 wb1 = *reinterpret_cast<const float4*>(w + HALF + c + 4);
+            const float wa[8] = {wa0.x, wa0.y, wa0.z, wa0.w, wa1.x, wa1.y, wa1.z, wa1.w};
+            const float wb[8] = {wb0.x, wb0.y, wb0.z, wb0.w, wb1.x, wb1.y, wb1.z, wb1.w};
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                a[i] = a[i] * inv * wa[i];
+                b[i] = b[i] * inv * wb[i];
+            }
+            if (live) {  // NeoX rotation of the pairs (c + i, HALF + c + i)
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const float a0 = a[i], b0 = b[i];
+                    a[i] = a0 * cs_c[i] - b0 * cs_s[i];
+                    b[i] = a0 * cs_s[i] + b0 * cs_c[i];
+                }
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                a[i] = a[i] * inv;
+                b[i] = b[i] * inv;
+            }
+        }
+        uint4 oa, ob;
+        __half2* pa = reinterpret_cast<__half2*>(&oa);
+        __half2* pb = reinterpret_cast<__half2*>(&ob);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            pa[i] = __floats2half2_rn(a[2 * i], a[2 * i + 1]);
+            pb[i] = __floats2half2_rn(b[2 * i], b[2 * i + 1]);
+        }
+        *reinterpret_cast<uint4*>(dst + c) = oa;
+        *reinterpret_cast<uint4*>(dst + HALF + c) = ob;
+    }
+}
+
 template <int HD, int S>
 static cudaError_t launch_qkv_t(const __half* qkv, int ntok, int rows, int heads, int kv_heads, const float* q_w,
                                 const float* k_w, const int32_t* positions, const float* rope, float eps, __half* q,
                                 __half* k, __half* v, cudaStream_t stream) {
-    // Two tokens per warp once the grid is many waves deep; one keeps small batches spread
-    // over every SM.
+    if (HD == 256) {
+        const int blocks = (rows + kRowsPerBlock * 2 - 1) / (kRowsPerBlock * 2);
+        return launch_kernel(k_qkv_norm_rope_hw<S>, dim3(blocks), dim3(256), 0, stream, 1, qkv, ntok, rows, heads,
+                             kv_heads, q_w, k_w, positions, rope, eps, q, k, v);
+    }
+    // Head dim 512: two tokens per warp once the grid is many waves deep; one keeps small
+    // batches spread over every SM.
     if (rows >= 8192) {
         const int blocks = (rows + kRowsPerBlock * 2 - 1) / (kRowsPerBlock * 2);
         return launch_kernel(k_qkv_norm_rope<HD, S, 2>, dim3(blocks), dim3(256), 0, stream, 1, qkv, ntok, rows, heads,
@@ -742,6 +854,100 @@ __global__ void k_dense_f32(const float* __restrict__ in, int nrows, const float
             if (lane == 0 && j < ns) out[long(s0 + j) * N + n] = v;
         }
     }
+}
+
+// The dense head of the forward: out[s][n] = sum_k in[s][k] * w[n][k] in fp32, as 64-row x
+// 64-column tiles over fixed 256-wide K chunks.  Pass 1: one block per (column tile, K chunk,
+// row tile); each thread keeps a 4 x 4 block of outputs in registers and adds its chunk's
+// products in increasing k, with the chunk's inputs and weights staged 32 k at a time in shared
+// memory (k-major, so each thread reads its 4 rows and 4 columns as two float4).  Pass 2 adds
+// the chunk partials in chunk order.  Every output's summation order depends only on K, not on
+// the number of rows, so a sequence's vector does not depend on its batch.
+constexpr int kHeadTile = 64, kHeadChunk = 256, kHeadStep = 32;
+
+__global__ void __launch_bounds__(256) k_dense_head_part(const float* __restrict__ in, int nrows,
+                                                         const float* __restrict__ w, int N, int K,
+                                                         float* __restrict__ part) {
+    pdl_wait();
+    pdl_launch_if_one_wave();
+    __shared__ float4 xs[kHeadStep][kHeadTile / 4 + 1];  // [k][row / 4], padded
+    __shared__ float4 ws[kHeadStep][kHeadTile / 4 + 1];  // [k][column / 4]
+    const int n0 = blockIdx.x * kHeadTile, k0 = blockIdx.y * kHeadChunk, r0 = blockIdx.z * kHeadTile;
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    float acc[4][4] = {};
+    // Staging: thread t loads row (or column) t % 64 of the tile at k offsets (t / 64) * 8 .. + 7
+    // (one whole 32-byte sector per thread), so a warp's shared-memory writes fall on 32
+    // consecutive words.
+    const int lr = tid & 63, lk = (tid >> 6) * 8;
+    const bool row_live = r0 + lr < nrows;
+    const float* xin = in + long(r0 + lr) * K + k0 + lk;
+    const float* win = w + long(n0 + lr) * K + k0 + lk;
+    for (int kk = 0; kk < kHeadChunk; kk += kHeadStep) {
+        float4 xa = make_float4(0.f, 0.f, 0.f, 0.f), xb = xa;
+        if (row_live) {
+            xa = *reinterpret_cast<const float4*>(xin + kk);
+            xb = *reinterpret_cast<const float4*>(xin + kk + 4);
+        }
+        const float4 wa = *reinterpret_cast<const float4*>(win + kk);
+        const float4 wb = *reinterpret_cast<const float4*>(win + kk + 4);
+        __syncthreads();
+        const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+        const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            reinterpret_cast<float*>(&xs[lk + j][lr >> 2])[lr & 3] = xv[j];
+            reinterpret_cast<float*>(&ws[lk + j][lr >> 2])[lr & 3] = wv[j];
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < kHeadStep; k++) {
+            const float4 a = xs[k][ty];
+            const float4 b = ws[k][tx];
+            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+    }
+    float* dst = part + (long(blockIdx.y) * nrows) * N;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int r = r0 + ty * 4 + i;
+        if (r < nrows)
+            *reinterpret_cast<float4*>(dst + long(r) * N + n0 + tx * 4) = make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+    }
+}
+
+__global__ void k_dense_head_sum(const float* __restrict__ part, int chunks, long count, float* __restrict__ out) {
+    pdl_wait();
+    pdl_launch_if_one_wave();
+    const long i = (long(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+    if (i >= count) return;
+    float4 s = *reinterpret_cast<const float4*>(part + i);
+    for (int c = 1; c < chunks; c++) {
+        const float4 t = *reinterpret_cast<const float4*>(part + long(c) * count + i);
+        s.x += t.x;
+        s.y += t.y;
+        s.z += t.z;
+        s.w += t.w;
+    }
+    *reinterpret_cast<float4*>(out + i) = s;
+}
+
+int dense_head_chunks(int K) { return K / kHeadChunk; }
+
+cudaError_t launch_dense_head(const float* in, int nrows, const float* w, int N, int K, float* part, float* out,
+                              cudaStream_t stream) {
+    if (nrows <= 0) return cudaSuccess;
+    if (N % kHeadTile || K % kHeadChunk) return cudaErrorInvalidValue;
+    const int chunks = K / kHeadChunk;
+    const dim3 grid(N / kHeadTile, chunks, (nrows + kHeadTile - 1) / kHeadTile);
+    CK_LAUNCH(launch_kernel(k_dense_head_part, grid, dim3(256), 0, stream, 1, in, nrows, w, N, K, part));
+    const long count = long(nrows) * N;
+    CK_LAUNCH(launch_kernel(k_dense_head_sum, dim3(unsigned((count / 4 + 255) / 256)), dim3(256), 0, stream, 1, part,
+                            chunks, count, out));
+    return cudaGetLastError();
 }
 
 cudaError_t launch_dense_f32(const float* in, int nrows, const float* w, int N, int K, float* out,

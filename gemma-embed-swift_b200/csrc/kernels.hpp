@@ -219,6 +219,12 @@ cudaError_t launch_mean_pool_seq(const float* y, int width, int ntok, const uint
                                  cudaStream_t stream);
 
 // out[s][n] = sum_k in[s][k] * w[n][k], fp32 weights [N][K].
+// The forward's dense head / output projection: 64 x 64 tiles over fixed 256-wide K chunks,
+// then the chunk partials added in order (`part` holds K / 256 x nrows x N floats); N a
+// multiple of 64 and K of 256.  launch_dense_f32 below needs no scratch.
+cudaError_t launch_dense_head(const float* in, int nrows, const float* w, int N, int K, float* part, float* out,
+                              cudaStream_t stream);
+int dense_head_chunks(int K);
 cudaError_t launch_dense_f32(const float* in, int nrows, const float* w, int N, int K, float* out,
                              cudaStream_t stream);
 
