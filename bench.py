@@ -538,8 +538,8 @@ def gemm_schedule_sweep(rows_list=(1024, 2432, 19584), reps=20):
 
 def eg2_workload(ge, synth, seqs, reps):
     """The reference's own architecture (EmbeddingGemma 2: hidden 512, per-layer inputs, global
-    layers with head dim 512 on the CUDA-core attention kernel, output projection) on the
-    config-2 batch: one forward's kernel profile (ge_profile), rank 0 only."""
+    layers with head dim 512, output projection) on the config-2 batch: one forward's kernel
+    profile (ge_profile), rank 0 only."""
     path2 = synth.model_path("gemma-embedding2", seed=0)
     toks, _, ranges = ge.pack(seqs)
     with ge.EmbeddingModel.load(path2, ge.LoadOptions(batch_token_budget=BATCH_BUDGET)) as m2:
@@ -552,7 +552,7 @@ def eg2_workload(ge, synth, seqs, reps):
            "roofline": roof,
            "kernels": [{k: (round(v, 5) if isinstance(v, float) else v) for k, v in p.items()} for p in prof]}
     for p in prof:
-        if p["name"] == "attention_global":  # head dim 512 (CUDA cores)
+        if p["name"] == "attention_global":  # head dim 512
             sec = p["ms_per_launch"] / 1000.0
             out["attention_hd512"] = {"us_per_launch": p["ms_per_launch"] * 1000.0,
                                       "tflops": p["flops_per_launch"] / sec / 1e12,

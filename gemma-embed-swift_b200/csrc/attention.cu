@@ -19,114 +19,19 @@
 namespace ge {
 
 // ---------------------------------------------------------------------------------------
-// CUDA-core kernel: one CTA of 8 warps per (work item of 32 queries, head); each warp owns
-// 4 queries, lane j scores key j of the 32-key block, and lane l accumulates output
-// dimensions l, l + 32, ... with an online softmax in fp32.
-constexpr int kSimtQueries = 32;
-constexpr int kSimtKeys = 32;
-
-template <int HD>
-__global__ void __launch_bounds__(256) k_attention_simt(const __half* __restrict__ Q, const __half* __restrict__ K,
-                                                        const __half* __restrict__ V, __half* __restrict__ O,
-                                                        const uint32_t* __restrict__ work, int heads, int kvh,
-                                                        int hw, float scale) {
-    pdl_wait();
-    pdl_launch_if_one_wave();
-    constexpr int PER = HD / 32;
-    extern __shared__ float sm[];
-    float* qs = sm;                          // [32][HD]
-    float* ks = qs + kSimtQueries * HD;      // [32][HD + 1]
-    float* vs = ks + kSimtKeys * (HD + 1);   // [32][HD]
-
-    const uint32_t seq_start = work[3 * blockIdx.x], len = work[3 * blockIdx.x + 1], q0 = work[3 * blockIdx.x + 2];
-    const int h = blockIdx.y;
-    const int kh = h / (heads / kvh);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long qstride = long(heads) * HD, kvstride = long(kvh) * HD;
-
-    for (int idx = threadIdx.x; idx < kSimtQueries * HD; idx += blockDim.x) {
-        const int r = idx / HD, c = idx % HD;
-        const uint32_t qi = q0 + r;
-        qs[idx] = qi < len ? __half2float(Q[(seq_start + qi) * qstride + h * HD + c]) : 0.f;
-    }
-
-    int k_start = 0, k_end = int(len);
-    if (hw > 0) {
-        k_start = max(int(q0) - hw, 0);
-        k_end = min(int(q0) + kSimtQueries - 1 + hw + 1, int(len));
-    }
-    k_start = k_start / kSimtKeys * kSimtKeys;
-
-    float m[4], l[4], acc[4][PER];
-#pragma unroll
-    for (int r = 0; r < 4; r++) {
-        m[r] = -INFINITY;
-        l[r] = 0.f;
-#pragma unroll
-        for (int i = 0; i < PER; i++) acc[r][i] = 0.f;
-    }
-
-    for (int kb = k_start; kb < k_end; kb += kSimtKeys) {
-        __syncthreads();
-        for (int idx = threadIdx.x; idx < kSimtKeys * HD; idx += blockDim.x) {
-            const int r = idx / HD, c = idx % HD;
-            const int kj = kb + r;
-            const bool in = kj < int(len);
-            ks[r * (HD + 1) + c] = in ? __half2float(K[(seq_start + kj) * kvstride + kh * HD + c]) : 0.f;
-            vs[r * HD + c] = in ? __half2float(V[(seq_start + kj) * kvstride + kh * HD + c]) : 0.f;
-        }
-        __syncthreads();
-        const int kj = kb + lane;
-#pragma unroll
-        for (int r = 0; r < 4; r++) {
-            const int qr = warp * 4 + r;
-            const int qi = int(q0) + qr;
-            const float* qrow = qs + qr * HD;
-            const float* krow = ks + lane * (HD + 1);
-            float s = 0.f;
-#pragma unroll 8
-            for (int d = 0; d < HD; d++) s += qrow[d] * krow[d];
-            bool valid = kj < int(len);
-            if (hw > 0) valid = valid && abs(qi - kj) <= hw;
-            s = valid ? s * scale : -INFINITY;
-            const float mb = warp_max(s);
-            const float m_new = fmaxf(m[r], mb);
-            float p = 0.f, alpha = 1.f;
-            if (m_new != -INFINITY) {
-                p = valid ? expf(s - m_new) : 0.f;
-                alpha = m[r] == -INFINITY ? 0.f : expf(m[r] - m_new);
-            }
-            l[r] = l[r] * alpha + warp_sum(p);
-            m[r] = m_new;
-#pragma unroll
-            for (int i = 0; i < PER; i++) acc[r][i] *= alpha;
-            for (int j = 0; j < kSimtKeys; j++) {
-                const float pj = __shfl_sync(0xffffffffu, p, j);
-                if (pj == 0.f) continue;
-                const float* vrow = vs + j * HD;
-#pragma unroll
-                for (int i = 0; i < PER; i++) acc[r][i] += pj * vrow[lane + 32 * i];
-            }
-        }
-    }
-
-#pragma unroll
-    for (int r = 0; r < 4; r++) {
-        const uint32_t qi = q0 + warp * 4 + r;
-        if (qi >= len) continue;
-        const float inv = l[r] > 0.f ? 1.0f / l[r] : 0.f;
-        __half* orow = O + (seq_start + qi) * qstride + h * HD;
-#pragma unroll
-        for (int i = 0; i < PER; i++) orow[lane + 32 * i] = __float2half_rn(acc[r][i] * inv);
-    }
-}
-
-// ---------------------------------------------------------------------------------------
-// Tensor-core kernel (head dim 256), persistent: CTA c walks its own range of work items,
-// assigned on the host longest-processing-time first by key blocks.  An item is T = 128 / G tokens of one sequence
-// with the G query heads that share one KV head (G = H / KV): row t * G + g of its Q tile is
-// token t0 + t, head kh * G + g (one 3-D TMA box per 64 dims), so each K and V tile serves
-// all G heads and a short sequence fills its tile with heads instead of padding.
+// Tensor-core kernel (head dim 256 or 512), persistent: CTA c walks its own range of work
+// items, assigned on the host longest-processing-time first by key blocks.  An item is T tokens
+// of one sequence with the G query heads that share one KV head (G = H / KV): row t * G + g of
+// its Q tile is token t0 + t, head kh * G + g (one 3-D TMA box per 64 dims), so each K and V
+// tile serves all G heads and a short sequence fills its tile with heads instead of padding.
+// Head dim 256: T = 128 / G, and O is the whole head (256 fp32 columns of tensor memory).
+// Head dim 512: O would need all 512 columns, so an item computes one half of the head's output
+// dims (the item's `half`, two items per token block) with S over all 512 dims; T = 64 / G, so
+// the Q tile (64 rows x 512 dims) fits the 64 KB that 128 x 256 takes.  Its eight 64-dim chunks
+// lie 8 KB apart, and the 128-row MMA reads rows 64..127 of chunk c from chunk c + 1 (the last
+// from the K ring): those S rows are masked and never stored.  A key block's K arrives as two
+// 256-dim halves through the 2-slot K ring, so the next block's first half loads while the
+// second half's MMAs run.
 //   warp 0      TMA producer: per item the Q tile, once the previous item's last S has read
 //               the buffer, then K and V tiles of 64 keys into 2-slot rings that run on from
 //               item to item
@@ -144,7 +49,7 @@ __global__ void __launch_bounds__(256) k_attention_simt(const __half* __restrict
 // Tensor memory: O in columns [0, 256), the S buffers in [256, 320) and [320, 384).
 constexpr int kTcQ = 128;
 constexpr int kTcKeys = 64;
-constexpr int kTcHd = 256;
+constexpr int kTcHd = 256;  // output dims per item (the head dim, or half of a 512-dim head) and K-ring slot width
 constexpr float kRescale = 8.0f;  // log2 units: a stale maximum may leave P up to 2^8
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kQBytes = kTcQ * kTcHd * 2;     // 64 KB: 4 chunks of [128 rows][64 dims]
@@ -186,9 +91,14 @@ __device__ __forceinline__ void item_keys(const uint4& w, const TcAttnParams& p,
     nblk = (ke - k_start + kTcKeys - 1) / kTcKeys;
 }
 
+template <int HD>
 __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_constant__ CUtensorMap mapQ,
                                                           const __grid_constant__ CUtensorMap mapK,
                                                           const __grid_constant__ CUtensorMap mapV, TcAttnParams p) {
+    static_assert(HD == 256 || HD == 512, "head dim 256 or 512");
+    constexpr int kChunks = HD / 64;              // 64-dim chunks of Q and K
+    constexpr int kHalves = HD / kTcHd;           // K-ring slots per key block
+    constexpr int kQChunk = kQBytes / kChunks;    // bytes between Q chunks: 128 or 64 rows x 128 bytes
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
@@ -206,7 +116,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int live_rows = p.group * p.tokens;
-    const uint32_t q_bytes = uint32_t(4 * 128 * live_rows);  // 4 boxes of live_rows x 128 bytes
+    const uint32_t q_bytes = uint32_t(kChunks * 128 * live_rows);  // kChunks boxes of live_rows x 128 bytes
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
@@ -242,30 +152,34 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
         // ---------------------------------------------------------- TMA producer
         if (lane == 0) {
             bool ok = true;
-            int gb = 0, issued_q = 0, issued_k = 0, issued_v = 0;
+            int gb = 0, gk = 0, issued_q = 0, issued_k = 0, issued_v = 0;
             for (int it = int(p.offset[blockIdx.x]), li = 0; it < int(p.offset[blockIdx.x + 1]) && ok; it++, li++) {
                 const uint4 w = p.work[it];
                 int k_start, nblk;
                 item_keys(w, p, k_start, nblk);
-                const int kh = int(w.w);
+                const int kh = int(w.w & 0xffffu), hv = int(w.w >> 16);  // KV head, output half
                 if (!mbar_wait(q_empty, uint32_t(li & 1) ^ 1u, p.err)) break;
                 mbar_expect_tx(q_full, q_bytes);
-                for (int c = 0; c < 4; c++)
-                    tma_load_3d(smem + c * (kQBytes / 4), &mapQ, q_full, c * 64, kh * p.group, int(w.x + w.z));
+                for (int c = 0; c < kChunks; c++)
+                    tma_load_3d(smem + c * kQChunk, &mapQ, q_full, c * 64, kh * p.group, int(w.x + w.z));
                 issued_q++;
                 for (int j = 0; j < nblk; j++, gb++) {
                     const int b = gb & 1;
                     const uint32_t ph = uint32_t((gb >> 1) & 1);
                     const int row = int(w.x) + k_start + j * kTcKeys;
-                    if (!mbar_wait(&k_empty[b], ph ^ 1, p.err)) {
-                        ok = false;
-                        break;
+                    for (int hk = 0; hk < kHalves && ok; hk++, gk++) {
+                        const int bk = gk & 1;
+                        if (!mbar_wait(&k_empty[bk], uint32_t((gk >> 1) & 1) ^ 1u, p.err)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_expect_tx(&k_full[bk], kKVBytes);
+                        for (int c = 0; c < 4; c++)
+                            tma_load_2d(smem + kOffK + bk * kKVBytes + c * (kKVBytes / 4), &mapK, &k_full[bk],
+                                        kh * HD + hk * kTcHd + c * 64, row);
+                        issued_k++;
                     }
-                    mbar_expect_tx(&k_full[b], kKVBytes);
-                    for (int c = 0; c < 4; c++)
-                        tma_load_2d(smem + kOffK + b * kKVBytes + c * (kKVBytes / 4), &mapK, &k_full[b],
-                                    kh * kTcHd + c * 64, row);
-                    issued_k++;
+                    if (!ok) break;
                     if (!mbar_wait(&v_empty[b], ph ^ 1, p.err)) {
                         ok = false;
                         break;
@@ -273,7 +187,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                     mbar_expect_tx(&v_full[b], kKVBytes);
                     for (int c = 0; c < 4; c++)
                         tma_load_2d(smem + kOffV + b * kKVBytes + c * (kKVBytes / 4), &mapV, &v_full[b],
-                                    kh * kTcHd + c * 64, row);
+                                    kh * HD + hv * kTcHd + c * 64, row);
                     issued_v++;
                 }
             }
@@ -315,7 +229,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                 umma_commit(&pv_done[b]);
                 return true;
             };
-            int gb = 0;
+            int gb = 0, gk = 0;
             for (int it = int(p.offset[blockIdx.x]), li = 0; it < int(p.offset[blockIdx.x + 1]) && ok; it++, li++) {
                 const uint4 w = p.work[it];
                 int k_start, nblk;
@@ -324,21 +238,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                 tc_fence_after();
                 for (int j = 0; j < nblk; j++, gb++) {
                     const int b = gb & 1;
-                    const uint32_t ph = uint32_t((gb >> 1) & 1);
-                    if (!mbar_wait(&k_full[b], ph, p.err)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t ka = smem_u32(smem + kOffK + b * kKVBytes);
+                    // S_j = Q K_j^T over every dim, one K-ring slot (256 dims) at a time
+                    for (int hk = 0; hk < kHalves && ok; hk++, gk++) {
+                        const int bk = gk & 1;
+                        if (!mbar_wait(&k_full[bk], uint32_t((gk >> 1) & 1), p.err)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t ka = smem_u32(smem + kOffK + bk * kKVBytes);
 #pragma unroll
-                    for (int kk = 0; kk < kTcHd / 16; kk++) {
-                        const int c = kk >> 2, wq = kk & 3;  // 64-dim chunk, 16-dim step inside it
-                        const uint64_t ad = sw128_desc(q_addr + c * (kQBytes / 4) + wq * 32, 16, 1024);
-                        const uint64_t bd = sw128_desc(ka + c * (kKVBytes / 4) + wq * 32, 16, 1024);
-                        umma_f16(tmem + kTmemS + b * kTcKeys, ad, bd, id_s, kk != 0);
+                        for (int kk = 0; kk < kTcHd / 16; kk++) {
+                            const int c = kk >> 2, wq = kk & 3;  // 64-dim chunk of the slot, 16-dim step inside it
+                            const uint64_t ad = sw128_desc(q_addr + (hk * 4 + c) * kQChunk + wq * 32, 16, 1024);
+                            const uint64_t bd = sw128_desc(ka + c * (kKVBytes / 4) + wq * 32, 16, 1024);
+                            umma_f16(tmem + kTmemS + b * kTcKeys, ad, bd, id_s, (hk | kk) != 0);
+                        }
+                        umma_commit(&k_empty[bk]);
                     }
-                    umma_commit(&k_empty[b]);
+                    if (!ok) break;
                     umma_commit(&s_full[b]);
                     if (j == nblk - 1) umma_commit(q_empty);  // every S of the item has read Q
                     if (j > 0 && !issue_pv(gb - 1, j == 1, li)) {
@@ -374,9 +292,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
             item_keys(w, p, k_start, nblk);
             const int len = int(w.y);
             const int qi = int(w.z) + rt;  // this row's token within its sequence
-            // Keys this row sees: [row_lo, row_hi) of its sequence.
+            // Keys this row sees: [row_lo, row_hi) of its sequence; none for the rows of the
+            // tile past the item's G x T (their scores come from whatever shared memory holds).
             const int row_lo = p.hw > 0 ? max(qi - p.hw, 0) : 0;
-            const int row_hi = p.hw > 0 ? min(qi + p.hw + 1, len) : len;
+            const int row_hi = r >= live_rows ? row_lo : p.hw > 0 ? min(qi + p.hw + 1, len) : len;
             float m_used = -INFINITY, l = 0.f;  // running maximum (log2 units) and this half's sum
             for (int j = 0; j < nblk; j++, gb++) {
                 const int b = gb & 1;
@@ -514,8 +433,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                             const int qr = int(w.z) + rrt;
                             const uint4 val = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((ch ^ (rr & 7)) * 16));
                             if (rr < live_rows && qr < len) {
-                                __half* dst = p.out + ((long(w.x) + qr) * p.heads + int(w.w) * p.group + rrg) * long(kTcHd) +
-                                              half * (kTcHd / 2) + rd * 64 + ch * 8;
+                                __half* dst = p.out +
+                                              ((long(w.x) + qr) * p.heads + int(w.w & 0xffffu) * p.group + rrg) * long(HD) +
+                                              int(w.w >> 16) * kTcHd + half * (kTcHd / 2) + rd * 64 + ch * 8;
                                 *reinterpret_cast<uint4*>(dst) = val;
                             }
                         }
@@ -534,11 +454,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
     }
 }
 
-static_assert(kSimtQueries == kSimtQueriesPerItem, "work list and kernel agree");
-
 int build_attention_work(const uint32_t* sl, int nseq, int kvh, int group, int hw, int max_ctas, uint32_t* out,
-                         int* ctas) {
-    const int T = attention_tokens_per_item(group);
+                         int* ctas, int hd) {
+    const int T = attention_tokens_per_item(group, hd);
+    const int halves = hd == 512 ? 2 : 1;  // a 512-dim head's output dims in two items
     struct Item {
         uint32_t start, len, t0, kh;
         int cost;
@@ -546,7 +465,7 @@ int build_attention_work(const uint32_t* sl, int nseq, int kvh, int group, int h
     std::vector<Item> items;
     for (int s = 0; s < nseq; s++)
         for (uint32_t t0 = 0; t0 < sl[2 * s + 1]; t0 += uint32_t(T))
-            for (int kh = 0; kh < kvh; kh++) {
+            for (int kh = 0; kh < kvh * halves; kh++) {
                 const int len = int(sl[2 * s + 1]);
                 int ks = 0, ke = len;
                 if (hw > 0) {
@@ -555,7 +474,9 @@ int build_attention_work(const uint32_t* sl, int nseq, int kvh, int group, int h
                 }
                 ks = ks / kTcKeys * kTcKeys;
                 // An item costs its key blocks plus about two blocks of set-up and epilogue.
-                items.push_back({sl[2 * s], sl[2 * s + 1], t0, uint32_t(kh), (ke - ks + kTcKeys - 1) / kTcKeys + 2});
+                // KV head in the low 16 bits, output half of a 512-dim head in the high 16
+                const uint32_t tag = uint32_t(kh / halves) | (uint32_t(kh % halves) << 16);
+                items.push_back({sl[2 * s], sl[2 * s + 1], t0, tag, (ke - ks + kTcKeys - 1) / kTcKeys + 2});
             }
     const int n = int(items.size());
     const int grid = std::max(1, std::min(n, max_ctas));
@@ -595,48 +516,37 @@ int build_attention_work(const uint32_t* sl, int nseq, int kvh, int group, int h
     return words;
 }
 
-template <int HD>
-static int simt_smem() {
-    return (kSimtQueries * HD + kSimtKeys * (HD + 1) + kSimtKeys * HD) * 4;
-}
-
 // Sets the shared-memory limits of the attention kernels on the current device; runs at
 // load, before any stream capture.
 cudaError_t configure_attention_kernels() {
-    cudaError_t e = cudaFuncSetAttribute(k_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+    cudaError_t e = cudaFuncSetAttribute(k_attention_tc<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(k_attention_simt<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, simt_smem<512>());
+        e = cudaFuncSetAttribute(k_attention_tc<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
     if (e == cudaSuccess) e = configure_attention64();
     return e;
 }
 
+template <int HD>
 static cudaError_t launch_tc(const AttnLaunch& a, cudaStream_t stream) {
     const int group = a.heads / a.kv_heads;
-    if (group > kTcQ) return cudaErrorInvalidValue;
+    if (attention_tokens_per_item(group, HD) < 1) return cudaErrorInvalidValue;
     TcAttnParams p{reinterpret_cast<const uint4*>(a.work), a.work + 4 * size_t(a.sched_items), a.out, a.heads, group,
-                   attention_tokens_per_item(group), a.half_window, a.err};
-    return launch_kernel(k_attention_tc, dim3(a.work_items), dim3(kTcThreads), kTcSmem, stream, 1, a.maps->q,
+                   attention_tokens_per_item(group, HD), a.half_window, a.err};
+    return launch_kernel(k_attention_tc<HD>, dim3(a.work_items), dim3(kTcThreads), kTcSmem, stream, 1, a.maps->q,
                          a.maps->k, a.maps->v, p);
-}
-
-template <int HD>
-static cudaError_t launch_simt(const AttnLaunch& a, cudaStream_t stream) {
-    const int smem = simt_smem<HD>();
-    dim3 grid(a.work_items, a.heads);
-    return launch_kernel(k_attention_simt<HD>, grid, dim3(256), smem, stream, 1, a.q, a.k, a.v, a.out, a.work, a.heads,
-                         a.kv_heads, a.half_window, 1.0f);
 }
 
 // Q as [rows][heads][hd] with boxes of 64 dims x G heads x T tokens (one work item's tile,
 // row t * G + g); K and V as [rows][kv_heads * hd] with boxes of 64 dims x 64 keys.
 bool encode_attention_maps(AttnMaps& m, const __half* q, const __half* k, const __half* v, int rows, int heads, int kvh,
                            int hd, int row_stride) {
+    if ((hd != 256 && hd != 512) || heads % kvh) return false;
     const int group = heads / kvh;
-    if (hd != kTcHd || heads % kvh || group > kTcQ) return false;
+    if (attention_tokens_per_item(group, hd) < 1) return false;
     const uint64_t qs = row_stride ? uint64_t(row_stride) : uint64_t(heads) * hd;
     const uint64_t kvs = row_stride ? uint64_t(row_stride) : uint64_t(kvh) * hd;
     return encode_fp16_map_3d(&m.q, q, uint64_t(hd), uint64_t(heads), uint64_t(rows), 64, uint32_t(group),
-                              uint32_t(attention_tokens_per_item(group)), qs) &&
+                              uint32_t(attention_tokens_per_item(group, hd)), qs) &&
            encode_fp16_map(&m.k, k, uint64_t(kvh) * hd, rows, 64, kTcKeys, kvs) &&
            encode_fp16_map(&m.v, v, uint64_t(kvh) * hd, rows, 64, kTcKeys, kvs);
 }
@@ -644,8 +554,9 @@ bool encode_attention_maps(AttnMaps& m, const __half* q, const __half* k, const 
 cudaError_t launch_attention(const AttnLaunch& a, cudaStream_t stream) {
     if (a.work_items <= 0) return cudaSuccess;
     if (a.heads % a.kv_heads) return cudaErrorInvalidValue;
-    if (a.hd == kTcHd) return a.maps ? launch_tc(a, stream) : cudaErrorInvalidValue;
-    if (a.hd == 512) return launch_simt<512>(a, stream);
+    if (!a.maps) return cudaErrorInvalidValue;
+    if (a.hd == 256) return launch_tc<256>(a, stream);
+    if (a.hd == 512) return launch_tc<512>(a, stream);
     return cudaErrorInvalidValue;
 }
 

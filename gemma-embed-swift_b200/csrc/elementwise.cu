@@ -882,14 +882,15 @@ __global__ void __launch_bounds__(256) k_dense_head_part(const float* __restrict
     const bool row_live = r0 + lr < nrows;
     const float* xin = in + long(r0 + lr) * K + k0 + lk;
     const float* win = w + long(n0 + lr) * K + k0 + lk;
+    // The next step's inputs and weights are loaded into registers while this step computes.
+    float4 xa = make_float4(0.f, 0.f, 0.f, 0.f), xb = xa;
+    if (row_live) {
+        xa = *reinterpret_cast<const float4*>(xin);
+        xb = *reinterpret_cast<const float4*>(xin + 4);
+    }
+    float4 wa = *reinterpret_cast<const float4*>(win);
+    float4 wb = *reinterpret_cast<const float4*>(win + 4);
     for (int kk = 0; kk < kHeadChunk; kk += kHeadStep) {
-        float4 xa = make_float4(0.f, 0.f, 0.f, 0.f), xb = xa;
-        if (row_live) {
-            xa = *reinterpret_cast<const float4*>(xin + kk);
-            xb = *reinterpret_cast<const float4*>(xin + kk + 4);
-        }
-        const float4 wa = *reinterpret_cast<const float4*>(win + kk);
-        const float4 wb = *reinterpret_cast<const float4*>(win + kk + 4);
         __syncthreads();
         const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
         const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
@@ -899,6 +900,14 @@ __global__ void __launch_bounds__(256) k_dense_head_part(const float* __restrict
             reinterpret_cast<float*>(&ws[lk + j][lr >> 2])[lr & 3] = wv[j];
         }
         __syncthreads();
+        if (kk + kHeadStep < kHeadChunk) {
+            if (row_live) {
+                xa = *reinterpret_cast<const float4*>(xin + kk + kHeadStep);
+                xb = *reinterpret_cast<const float4*>(xin + kk + kHeadStep + 4);
+            }
+            wa = *reinterpret_cast<const float4*>(win + kk + kHeadStep);
+            wb = *reinterpret_cast<const float4*>(win + kk + kHeadStep + 4);
+        }
 #pragma unroll 8
         for (int k = 0; k < kHeadStep; k++) {
             const float4 a = xs[k][ty];

@@ -362,30 +362,28 @@ struct AttnLaunch {
     const __half* k;  // [rows][kv_heads * hd]
     const __half* v;
     __half* out;      // [rows][heads * hd]
-    // head dim 256: the schedule build_attention_work writes (items grouped by CTA, then the
-    // CTAs' item offsets); head dim 512: (seq_start, seq_len, first query) triples per 32 queries
+    // the schedule build_attention_work writes (items grouped by CTA, then the CTAs' item offsets)
     const uint32_t* work;
-    int work_items;   // head dim 256: the schedule's CTA count; head dim 512: triples
-    int sched_items = 0;  // head dim 256: items in the schedule
-    int heads, kv_heads, hd;
+    int work_items;       // the schedule's CTA count
+    int sched_items = 0;  // items in the schedule
+    int heads, kv_heads, hd;  // hd 256 or 512
     int half_window;  // 0: global attention
     int* err;
     int num_sms = 148;
-    const AttnMaps* maps = nullptr;  // required for head dim 256 (tensor-core kernel)
+    const AttnMaps* maps = nullptr;  // encode_attention_maps over q, k and v
 };
 cudaError_t launch_attention(const AttnLaunch& a, cudaStream_t stream);
-// Tokens of one tensor-core work item: its 128-row Q tile holds `group` heads per token.
-inline int attention_tokens_per_item(int group) { return 128 / group; }
-// Queries per work item of the CUDA-core kernel (head dim 512).
-constexpr int kSimtQueriesPerItem = 32;
+// Tokens of one tensor-core work item: its Q tile holds `group` heads per token in 128 rows
+// (head dim 256) or 64 rows (head dim 512, whose 8 chunks of 64 dims fill the same 64 KB).
+inline int attention_tokens_per_item(int group, int hd = 256) { return (hd == 512 ? 64 : 128) / group; }
 // The tensor-core kernel's schedule for packed sequences (start, length pairs): one item per
-// block of attention_tokens_per_item(group) tokens and KV head (group = heads / kv_heads),
-// spread over min(items, max_ctas) CTAs by longest-processing-time-first on the item's key
-// blocks under `half_window` (0: global).  Layout: the items as (seq_start, seq_len, first
-// token, KV head), grouped by CTA, then CTA c's item range [off[c], off[c + 1]) as ctas + 1
-// offsets.  Returns the words written (or needed, when `out` is null); `ctas` receives the CTA
-// count.
+// block of attention_tokens_per_item(group, hd) tokens and KV head (group = heads / kv_heads;
+// head dim 512: two items, one per half of the output dims), spread over min(items, max_ctas)
+// CTAs by longest-processing-time-first on the item's key blocks under `half_window` (0:
+// global).  Layout: the items as (seq_start, seq_len, first token, KV head | half << 16),
+// grouped by CTA, then CTA c's item range [off[c], off[c + 1]) as ctas + 1 offsets.  Returns
+// the words written (or needed, when `out` is null); `ctas` receives the CTA count.
 int build_attention_work(const uint32_t* seq_start_len, int nseq, int kv_heads, int group, int half_window,
-                         int max_ctas, uint32_t* out, int* ctas);
+                         int max_ctas, uint32_t* out, int* ctas, int hd = 256);
 
 }  // namespace ge

@@ -131,7 +131,7 @@ bool read_config(const GgufFile& f, Config& c, LoadError& e) {
 
 static void free_workspace(Workspace& ws) {
     for (void* p : {(void*)ws.tokens, (void*)ws.positions, (void*)ws.seqs, (void*)ws.work, (void*)ws.x, (void*)ws.qkv16,
-                    (void*)ws.o16, (void*)ws.d16, (void*)ws.y, (void*)ws.ple, (void*)ws.pooled, (void*)ws.chunk_base, (void*)ws.pool_partial, (void*)ws.mid, (void*)ws.out,
+                    (void*)ws.o16, (void*)ws.d16, (void*)ws.y, (void*)ws.ple, (void*)ws.pooled, (void*)ws.chunk_base, (void*)ws.pool_partial, (void*)ws.mid, (void*)ws.head_part, (void*)ws.out,
                     (void*)ws.h, (void*)ws.x16, (void*)ws.q, (void*)ws.k, (void*)ws.v, (void*)ws.attn, (void*)ws.act,
                     (void*)ws.g})
         if (p) cudaFree(p);
@@ -199,6 +199,10 @@ static cudaError_t ensure_workspace(const Config& c, Device& d, int rows, int se
     chk(A(&ws.pool_partial, (r / kPoolChunkRows + size_t(S)) * d_));
     chk(H(&ws.h_chunk_base, size_t(S)));
     chk(A(&ws.mid, size_t(S) * std::max(c.dense_head, 1)));
+    const size_t head_floats = std::max({size_t(dense_head_chunks(c.hidden)) * std::max(c.dense_head, 1),
+                                         size_t(dense_head_chunks(std::max(c.dense_head, 1))) * c.out_dim,
+                                         size_t(dense_head_chunks(c.hidden)) * c.out_dim, size_t(1)});
+    chk(A(&ws.head_part, size_t(S) * head_floats));
     chk(A(&ws.out, size_t(S) * c.out_dim));
     chk(H(&ws.h_tokens, r));
     chk(H(&ws.h_positions, r));
@@ -224,18 +228,20 @@ static cudaError_t ensure_workspace(const Config& c, Device& d, int rows, int se
     ws.attn_maps.clear();
     ws.attn_maps_fused.clear();
     for (auto& l : c.layer) {
-        if (l.hd != 256) continue;
+        const int key = attn_map_key(l.kv, l.hd);
         bool have = false;
-        for (auto& x : ws.attn_maps) have = have || x.first == l.kv;
+        for (auto& x : ws.attn_maps) have = have || x.first == key;
         if (!have) {
             AttnMaps am, fm;
-            const int stride = (c.heads + 2 * l.kv) * l.hd;
-            const __half* q = ws.qkv16;
-            ok = ok && encode_attention_maps(am, ws.q, ws.k, ws.v, R, c.heads, l.kv, l.hd) &&
-                 encode_attention_maps(fm, q, q + c.heads * l.hd, q + (c.heads + l.kv) * l.hd, R, c.heads, l.kv, l.hd,
-                                       stride);
-            ws.attn_maps.push_back({l.kv, am});
-            ws.attn_maps_fused.push_back({l.kv, fm});
+            ok = ok && encode_attention_maps(am, ws.q, ws.k, ws.v, R, c.heads, l.kv, l.hd);
+            ws.attn_maps.push_back({key, am});
+            if (l.hd == 256) {  // q, k and v in place in the projection rows (GE_LOAD_FUSED_QKV)
+                const int stride = (c.heads + 2 * l.kv) * l.hd;
+                const __half* q = ws.qkv16;
+                ok = ok && encode_attention_maps(fm, q, q + c.heads * l.hd, q + (c.heads + l.kv) * l.hd, R, c.heads, l.kv,
+                                                 l.hd, stride);
+                ws.attn_maps_fused.push_back({key, fm});
+            }
         }
     }
     ws.a_attn.clear();
@@ -598,22 +604,6 @@ void clear_graphs(Device& d) {
 }
 
 // ------------------------------------------------------------------ forward
-// Work items, one per block of `qpi` queries of every sequence (AttentionWork.items,
-// MetalForward.swift:45-58).
-static int build_work(const ge_seq* seqs, int nseq, int qpi, uint32_t* out) {
-    int n = 0;
-    for (int s = 0; s < nseq; s++)
-        for (uint32_t q0 = 0; q0 < seqs[s].length; q0 += uint32_t(qpi)) {
-            if (out) {
-                out[3 * n] = seqs[s].start;
-                out[3 * n + 1] = seqs[s].length;
-                out[3 * n + 2] = q0;
-            }
-            n++;
-        }
-    return n;
-}
-
 int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     const Config& c = m->cfg;
     cudaError_t e = cudaSetDevice(d.ordinal);
@@ -636,33 +626,25 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     const int ntok = a.ntok, nseq = a.nseq;
     const int rows = std::max(kRowTile, round_up(ntok, kRowTile));
     // Attention work stored back to back, each part starting on 16 bytes: the tensor-core
-    // kernel's schedules for sliding and for global head-dim-256 layers (items of T tokens x
-    // the query heads of one KV head, spread over CTAs by key blocks), and the CUDA-core
-    // kernel's list for head-dim-512 layers (3 words per 32 queries).
+    // kernel's schedules (items of T tokens x the query heads of one KV head, spread over CTAs
+    // by key blocks) for each kind of layer the model has: schedule 2 * (hd == 512) + global,
+    // i.e. sliding and global head-dim-256 layers, then sliding and global head-dim-512 layers.
     static_assert(sizeof(ge_seq) == 8, "ge_seq is a (start, length) pair of uint32");
     const uint32_t* seq_pairs = reinterpret_cast<const uint32_t*>(a.seqs);
-    int kv256 = 0;
-    bool any512 = false, slide256 = false, global256 = false;
-    for (auto& l : c.layer) {
-        if (l.hd == 256) {
-            kv256 = l.kv;
-            (l.sliding ? slide256 : global256) = true;
-        }
-        any512 = any512 || l.hd == 512;
-    }
-    const int group = kv256 ? c.heads / kv256 : 1;
     const int hw_slide = c.sliding_window / 2;
-    int sched[4] = {0, 0, 0, 0};  // items and CTAs of the sliding, then the global schedule
-    int words[2] = {0, 0};
-    for (int k = 0; k < 2; k++) {
-        if (!(k == 0 ? slide256 : global256)) continue;
-        words[k] = build_attention_work(seq_pairs, nseq, kv256, group, k == 0 ? hw_slide : 0, d.num_sms, nullptr,
-                                        &sched[2 * k + 1]);
+    int kind_kv[4] = {0, 0, 0, 0};  // KV heads of the layers of each schedule (0: no such layer)
+    for (auto& l : c.layer) kind_kv[2 * (l.hd == 512) + (l.sliding ? 0 : 1)] = l.kv;
+    int sched[8] = {0, 0, 0, 0, 0, 0, 0, 0};  // (items, CTAs) of each schedule
+    int words[4] = {0, 0, 0, 0}, work_at[4] = {0, 0, 0, 0};
+    int work_words = 0;
+    for (int k = 0; k < 4; k++) {
+        work_at[k] = work_words;
+        if (!kind_kv[k]) continue;
+        words[k] = build_attention_work(seq_pairs, nseq, kind_kv[k], c.heads / kind_kv[k], (k & 1) ? 0 : hw_slide,
+                                        d.num_sms, nullptr, &sched[2 * k + 1], k >= 2 ? 512 : 256);
         sched[2 * k] = words[k] ? (words[k] - sched[2 * k + 1] - 1) / 4 : 0;
-        words[k] = (words[k] + 3) & ~3;
+        work_words += (words[k] + 3) & ~3;
     }
-    const int nwork512 = any512 ? build_work(a.seqs, nseq, kSimtQueriesPerItem, nullptr) : 0;
-    const int work_words = words[0] + words[1] + 3 * nwork512;
     if ((e = staging_wait(d, kStageText)) != cudaSuccess) return gpu_fail(e, "staging");
     if ((e = ensure_workspace(c, d, rows, nseq, work_words)) != cudaSuccess) return gpu_fail(e, "workspace");
     Workspace& ws = d.ws;
@@ -678,11 +660,10 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         chunk_total += uint32_t(ch);
         max_chunks = std::max(max_chunks, ch);
     }
-    for (int k = 0; k < 2; k++)
+    for (int k = 0; k < 4; k++)
         if (words[k])
-            build_attention_work(seq_pairs, nseq, kv256, group, k == 0 ? hw_slide : 0, d.num_sms,
-                                 ws.h_work + (k == 0 ? 0 : words[0]), nullptr);
-    if (any512) build_work(a.seqs, nseq, kSimtQueriesPerItem, ws.h_work + words[0] + words[1]);
+            build_attention_work(seq_pairs, nseq, kind_kv[k], c.heads / kind_kv[k], (k & 1) ? 0 : hw_slide, d.num_sms,
+                                 ws.h_work + work_at[k], nullptr, k >= 2 ? 512 : 256);
     const int32_t* tokens = ws.tokens;
     int64_t h2d = int64_t(nseq) * 8 + int64_t(work_words) * 4 + int64_t(nseq) * 4;  // seqs, work, chunk bases
     if (a.tokens_on_device) {
@@ -864,8 +845,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
             const LayerCfg& lc = c.layer[l];
             const LayerDev& L = d.layers[l];
             const int qd = c.heads * lc.hd;
-            const bool tc = lc.hd == 256;
-            const bool in_place = tc && fused_qkv;
+            const bool in_place = lc.hd == 256 && fused_qkv;
             if (in_place) {
                 CK(K("gemm_qkv_norm_rope", gemm_flops(L.qkv), gemm_bytes(L.qkv, 2), [&] { return gemm_qkv(L, lc); }),
                    "qkv projection with norms and rope");
@@ -886,10 +866,10 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
             al.k = in_place ? ws.qkv16 + c.heads * lc.hd : ws.k;
             al.v = in_place ? ws.qkv16 + (c.heads + lc.kv) * lc.hd : ws.v;
             al.out = ws.attn;
-            const int k = lc.sliding ? 0 : 1;
-            al.work = tc ? ws.work + (k == 0 ? 0 : words[0]) : ws.work + words[0] + words[1];
-            al.work_items = tc ? sched[2 * k + 1] : nwork512;
-            al.sched_items = tc ? sched[2 * k] : 0;
+            const int k = 2 * (lc.hd == 512) + (lc.sliding ? 0 : 1);
+            al.work = ws.work + work_at[k];
+            al.work_items = sched[2 * k + 1];
+            al.sched_items = sched[2 * k];
             al.num_sms = d.num_sms;
             al.heads = c.heads;
             al.kv_heads = lc.kv;
@@ -897,7 +877,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
             al.half_window = lc.sliding ? c.sliding_window / 2 : 0;
             al.err = d.err;
             for (auto& x : (in_place ? ws.attn_maps_fused : ws.attn_maps))
-                if (tc && x.first == lc.kv) al.maps = &x.second;
+                if (x.first == attn_map_key(lc.kv, lc.hd)) al.maps = &x.second;
             CK(K(lc.sliding ? "attention_sliding" : "attention_global",
                  4.0 * c.heads * lc.hd * (lc.sliding ? vk_sliding : vk_global),
                  double(ntok) * (2.0 * qd + 2.0 * lc.kv * lc.hd) * 2, [&] { return launch_attention(al, ks); }),
@@ -1012,16 +992,24 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
                                              ws.pooled, ks);
                  }, 2),
                "mean pool");
+            // 64 x 64 tiles over 256-wide K chunks, two launches each (launch_dense_head), where
+            // the widths allow; otherwise the scratch-free kernels
+            auto head = [&](const float* in, const float* w, int N, int Kd, float* out) {
+                if (N % 64 == 0 && Kd % 256 == 0) return launch_dense_head(in, nseq, w, N, Kd, ws.head_part, out, ks);
+                return launch_dense_f32(in, nseq, w, N, Kd, out, ks);
+            };
+            auto head_launches = [&](int N, int Kd) { return (N % 64 == 0 && Kd % 256 == 0) ? 2 : 1; };
             if (c.has_dense) {
                 CK(K("dense_head", 2.0 * nseq * D * c.dense_head, double(D) * c.dense_head * 4,
-                     [&] { return launch_dense_f32(ws.pooled, nseq, d.dense2, c.dense_head, D, ws.mid, ks); }),
+                     [&] { return head(ws.pooled, d.dense2, c.dense_head, D, ws.mid); }, head_launches(c.dense_head, D)),
                    "dense head");
                 CK(K("dense_head_out", 2.0 * nseq * D * c.dense_head, double(D) * c.dense_head * 4,
-                     [&] { return launch_dense_f32(ws.mid, nseq, d.dense3, c.out_dim, c.dense_head, ws.out, ks); }),
+                     [&] { return head(ws.mid, d.dense3, c.out_dim, c.dense_head, ws.out); },
+                     head_launches(c.out_dim, c.dense_head)),
                    "dense head");
             } else {
                 CK(K("output_projection", 2.0 * nseq * D * c.out_dim, double(D) * c.out_dim * 4,
-                     [&] { return launch_dense_f32(ws.pooled, nseq, d.output, c.out_dim, D, ws.out, ks); }),
+                     [&] { return head(ws.pooled, d.output, c.out_dim, D, ws.out); }, head_launches(c.out_dim, D)),
                    "output projection");
             }
         }
@@ -1036,9 +1024,8 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     gk.rows = rows;
     gk.ntok = ntok;
     gk.nseq = nseq;
-    gk.nwork512 = nwork512;
     gk.pool_chunks = max_chunks;
-    for (int k = 0; k < 4; k++) gk.sched[k] = sched[k];
+    for (int k = 0; k < 8; k++) gk.sched[k] = sched[k];
     gk.tokens = reinterpret_cast<uintptr_t>(tokens);
     gk.vectors = reinterpret_cast<uintptr_t>(a.vectors);
     GraphEntry* ge_ = use_graph ? find_graph(d, gk) : nullptr;

@@ -57,13 +57,14 @@ struct Workspace {
     __half* o16 = nullptr;  // fp16 output of the o (and, with per-layer inputs, down and per-layer) projections
     __half* d16 = nullptr;  // fp16 output of the down projection, beside o16 until the FFN residual
     float *pooled = nullptr, *mid = nullptr, *out = nullptr;
+    float* head_part = nullptr;  // the dense head's per-K-chunk partial sums [chunks][seqs][N]
     __half *qkv16 = nullptr;  // fused q|k|v projection output
     __half *h = nullptr, *x16 = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *act = nullptr,
            *g = nullptr;
     // GEMM A-operand views (buffer, column count) with their TMA descriptors.
     DevActivation a_h, a_x16, a_act, a_g;
     std::vector<DevActivation> a_attn;  // one per distinct query width
-    std::vector<std::pair<int, AttnMaps>> attn_maps;  // per KV head count, head-dim-256 layers
+    std::vector<std::pair<int, AttnMaps>> attn_maps;  // per attn_map_key(KV heads, head dim)
     // The same over the fused projection rows of qkv16 (EPI_QKV layers read q, k and v in place).
     std::vector<std::pair<int, AttnMaps>> attn_maps_fused;
     // Pinned host staging.
@@ -75,17 +76,22 @@ struct Workspace {
 
 // A captured forward for one batch shape on one workspace.
 struct GraphKey {
-    int rows = 0, ntok = 0, nseq = 0, nwork512 = 0, pool_chunks = 0;
-    int sched[4] = {0, 0, 0, 0};  // attention schedules: (items, CTAs) for sliding and global layers
+    int rows = 0, ntok = 0, nseq = 0, pool_chunks = 0;
+    // attention schedules: (items, CTAs) for sliding and global layers of head dim 256, then 512
+    int sched[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     uintptr_t tokens = 0;         // the token buffer the embedding kernel reads
     uintptr_t vectors = 0;        // and the vector rows it copies (image or audio rows), if any
     bool operator==(const GraphKey& o) const {
-        return rows == o.rows && ntok == o.ntok && nseq == o.nseq && nwork512 == o.nwork512 &&
-               pool_chunks == o.pool_chunks && tokens == o.tokens && vectors == o.vectors && sched[0] == o.sched[0] &&
-               sched[1] == o.sched[1] &&
-               sched[2] == o.sched[2] && sched[3] == o.sched[3];
+        if (rows != o.rows || ntok != o.ntok || nseq != o.nseq || pool_chunks != o.pool_chunks || tokens != o.tokens ||
+            vectors != o.vectors)
+            return false;
+        for (int k = 0; k < 8; k++)
+            if (sched[k] != o.sched[k]) return false;
+        return true;
     }
 };
+// The attention tensor maps of a workspace are kept per (KV heads, head dim).
+inline int attn_map_key(int kv_heads, int hd) { return kv_heads * 1024 + hd; }
 struct GraphEntry {
     GraphKey key;
     cudaGraphExec_t exec = nullptr;

@@ -329,23 +329,18 @@ int ge_test_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
     TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     std::vector<uint32_t> work;
     int items = 0, ctas = 0;
-    if (hd == 256 || hd == 64) {
+    {
         std::vector<uint32_t> pairs;
         for (int s = 0; s < nseq; s++) {
             pairs.push_back(seqs[s].start);
             pairs.push_back(seqs[s].length);
         }
-        const int words = ge::build_attention_work(pairs.data(), nseq, kvh, heads / kvh, half_window, sms, nullptr, &ctas);
+        const int shd = hd == 512 ? 512 : 256;  // head dim 64 (vision) schedules like 256 with group 1
+        const int words =
+            ge::build_attention_work(pairs.data(), nseq, kvh, heads / kvh, half_window, sms, nullptr, &ctas, shd);
         work.resize(size_t(words));
-        ge::build_attention_work(pairs.data(), nseq, kvh, heads / kvh, half_window, sms, work.data(), nullptr);
+        ge::build_attention_work(pairs.data(), nseq, kvh, heads / kvh, half_window, sms, work.data(), nullptr, shd);
         items = (words - ctas - 1) / 4;
-    } else {
-        for (int s = 0; s < nseq; s++)
-            for (uint32_t q0 = 0; q0 < seqs[s].length; q0 += uint32_t(ge::kSimtQueriesPerItem), items++) {
-                work.push_back(seqs[s].start);
-                work.push_back(seqs[s].length);
-                work.push_back(q0);
-            }
     }
     DevBuf dq, dk, dv, dout, dwork, derr;
     const size_t qn = size_t(rows) * heads * hd, kn = size_t(rows) * kvh * hd;
@@ -371,7 +366,7 @@ int ge_test_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
     al.v = static_cast<const __half*>(dv.p);
     al.out = static_cast<__half*>(dout.p);
     al.work = static_cast<const uint32_t*>(dwork.p);
-    al.work_items = hd == 256 ? ctas : items;
+    al.work_items = ctas;
     al.sched_items = items;
     al.heads = heads;
     al.kv_heads = kvh;
@@ -400,11 +395,9 @@ int ge_test_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
         return GE_OK;
     }
     ge::AttnMaps maps;
-    if (hd == 256) {
-        if (!ge::encode_attention_maps(maps, al.q, al.k, al.v, rows, heads, kvh, hd))
-            return fail(GE_ERR_GPU_FAILURE, "tensor map encoding failed");
-        al.maps = &maps;
-    }
+    if (!ge::encode_attention_maps(maps, al.q, al.k, al.v, rows, heads, kvh, hd))
+        return fail(GE_ERR_GPU_FAILURE, "tensor map encoding failed");
+    al.maps = &maps;
     TRY(ge::launch_attention(al, nullptr));
     TRY(cudaDeviceSynchronize());
     int herr = 0;

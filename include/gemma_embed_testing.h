@@ -46,8 +46,9 @@ GE_API int ge_test_gemm_residual(const uint16_t* a, int32_t m, int32_t k, const 
 
 /* Kernels.attention (Metal/MetalForward.swift:669-694): q [ntok][heads][hd], k and v
  * [ntok][kv_heads][hd] as fp16 bit patterns, sequences tiling [0, ntok); out receives fp16
- * bit patterns [ntok][heads][hd].  half_window 0 is global attention. */
-/* Head dim 64 (heads == kv_heads, no window) runs the vision tower's tensor-core kernel. */
+ * bit patterns [ntok][heads][hd].  half_window 0 is global attention.  Head dim 256 and 512
+ * run the text model's tensor-core kernel (512: one item per half of the output dims); head dim
+ * 64 (heads == kv_heads, no window) the vision tower's. */
 GE_API int ge_test_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, int32_t ntok, const ge_seq* seqs,
                              int32_t nseq, int32_t heads, int32_t kv_heads, int32_t hd, int32_t half_window,
                              uint16_t* out);

@@ -167,7 +167,8 @@ def attention(ge, q, k, v, lens, heads, kvh, hd, hw):
     return out.astype(np.float32)
 
 
-CONFIGS = [(3, 1, 256, 512), (3, 1, 256, 0), (4, 2, 256, 512), (4, 1, 512, 0), (4, 1, 512, 512)]
+CONFIGS = [(3, 1, 256, 512), (3, 1, 256, 0), (4, 2, 256, 512), (4, 1, 512, 0), (4, 1, 512, 512),
+           (3, 1, 512, 0), (4, 2, 512, 512)]  # head dim 512: 64-row items, 63 live rows for 3 heads
 # The last case packs more work items than the GPU has SMs, so the tensor-core kernel's
 # persistent CTAs each take several items of different lengths.
 LENGTHS = [[1, 7, 64], [1024, 5], [2048], [2048, 3, 1024, 7],
