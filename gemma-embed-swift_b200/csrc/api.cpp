@@ -85,6 +85,16 @@ int check_batch(ge_model* m, const int32_t* tokens, const int32_t* positions, in
     return GE_OK;
 }
 
+// Runs fn(dv) for each device share dv on the model's device workers (on the calling thread
+// when the model has one device).
+void run_per_device(ge_model* m, int n, const std::function<void(int)>& fn) {
+    if (n <= 1 || !m->workers) {
+        for (int i = 0; i < n; i++) fn(i);
+        return;
+    }
+    m->workers->run(n, fn);
+}
+
 int forward_packed_locked(ge_model* m, const int32_t* tokens, const int32_t* positions, int32_t ntok, const ge_seq* seqs,
                           int32_t nseq, float* out) {
     const int ndev = int(m->devs.size());
@@ -104,11 +114,9 @@ int forward_packed_locked(ge_model* m, const int32_t* tokens, const int32_t* pos
     auto parts = ge::shard_sequences(seqs, nseq, ndev);
     std::vector<int> rc(ndev, GE_OK);
     std::vector<std::string> msgs(ndev);
-    std::vector<std::thread> th;
-    for (int dv = 0; dv < ndev; dv++) {
-        if (parts[dv].empty()) continue;
-        th.emplace_back([&, dv]() {
-            const auto& idx = parts[dv];
+    run_per_device(m, ndev, [&](int dv) {
+            const auto& idx = parts[size_t(dv)];
+            if (idx.empty()) return;
             std::vector<int32_t> tk, ps;
             std::vector<ge_seq> sq;
             for (int i : idx) {
@@ -129,8 +137,6 @@ int forward_packed_locked(ge_model* m, const int32_t* tokens, const int32_t* pos
             if (rc[dv] == GE_OK)
                 for (size_t j = 0; j < idx.size(); j++) memcpy(out + size_t(idx[j]) * od, o.data() + j * od, od * 4);
         });
-    }
-    for (auto& t : th) t.join();
     for (int dv = 0; dv < ndev; dv++)
         if (rc[dv] != GE_OK) return ge::set_error(m, rc[dv], msgs[dv]);
     return GE_OK;
@@ -840,13 +846,10 @@ int ge_embed_images(ge_model* m, const ge_image* images, int32_t count, const ge
                 for (size_t k = 0; k < idx.size(); k++)
                     memcpy(pooled.data() + size_t(idx[k]) * od, po.data() + k * od, size_t(od) * sizeof(float));
         };
-        if (parts.size() == 1) {
+        if (parts.size() == 1)
             run_part(0);
-        } else {
-            std::vector<std::thread> th;
-            for (size_t dv = 0; dv < parts.size(); dv++) th.emplace_back(run_part, dv);
-            for (auto& t : th) t.join();
-        }
+        else
+            run_per_device(m, int(parts.size()), [&](int dv) { run_part(size_t(dv)); });
         for (size_t dv = 0; dv < parts.size(); dv++)
             if (rcs[dv] != GE_OK) return ge::set_error(m, rcs[dv], msgs[dv]);
         for (int32_t i = b; i < e; i++) {
@@ -1156,13 +1159,10 @@ int ge_embed_audios(ge_model* m, const ge_audio* clips, int32_t count, const ge_
                 for (size_t k = 0; k < idx.size(); k++)
                     memcpy(pooled.data() + size_t(idx[k]) * od, po.data() + k * od, size_t(od) * sizeof(float));
         };
-        if (parts.size() == 1) {
+        if (parts.size() == 1)
             run_part(0);
-        } else {
-            std::vector<std::thread> th;
-            for (size_t dv = 0; dv < parts.size(); dv++) th.emplace_back(run_part, dv);
-            for (auto& t : th) t.join();
-        }
+        else
+            run_per_device(m, int(parts.size()), [&](int dv) { run_part(size_t(dv)); });
         for (size_t dv = 0; dv < parts.size(); dv++)
             if (rcs[dv] != GE_OK) return ge::set_error(m, rcs[dv], msgs[dv]);
         for (int32_t i = b; i < e; i++) {

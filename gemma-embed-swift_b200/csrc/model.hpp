@@ -5,9 +5,12 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <condition_variable>
+#include <functional>
 #include <memory>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "gemma_embed.h"
@@ -143,6 +146,30 @@ struct ge_tokenizer {
     ge::Tokenizer t;
 };
 
+namespace ge {
+// One host thread per device of a multi-device model, started at load and kept until the model
+// is freed, so a sharded call hands each device its share without creating threads.
+class DeviceWorkers {
+public:
+    ~DeviceWorkers() { stop(); }
+    void start(int n);
+    void stop();
+    // Runs fn(i) for i in [0, n) (n at most the workers started), worker i on device share i,
+    // and returns once every one has finished.  Not reentrant (the model's lock serialises calls).
+    void run(int n, const std::function<void(int)>& fn);
+
+private:
+    void loop(int i);
+    std::vector<std::thread> threads_;
+    std::mutex mu_;
+    std::condition_variable cv_, done_cv_;
+    const std::function<void(int)>* task_ = nullptr;
+    uint64_t generation_ = 0;
+    int active_ = 0, pending_ = 0;
+    bool stop_ = false;
+};
+}  // namespace ge
+
 struct ge_model {
     ge::Config cfg;
     ge::GgufFile file;
@@ -156,6 +183,7 @@ struct ge_model {
     std::atomic<int64_t> h2d_bytes{0}, d2h_bytes{0};  // host <-> device copies of the forwards so far
     std::atomic<int64_t> graph_captures{0};           // CUDA graphs captured and instantiated so far
     std::unique_ptr<ge_tokenizer> tokenizer;  // null when the file carries no tokenizer
+    std::unique_ptr<ge::DeviceWorkers> workers;  // with two or more devices: one host thread each
     // The image encoder (LoadOptions.imageEncoder): its file, configuration and the tokens that
     // frame an image's rows in the text sequence (SpanMarkers.image, Model/InputRow.swift:43-45).
     bool has_vision = false;

@@ -156,8 +156,11 @@ int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int3
     g.aux = static_cast<const float*>(daux.p);
     g.ldaux = n;
     g.use_q8 = use_q8 == 1;
-    g.mode = use_q8 == 2 ? ge::GEMM_PAIR : use_q8 == 3 ? ge::GEMM_NARROW : use_q8 == 4 ? ge::GEMM_SPLIT
-                                                                                    : ge::GEMM_SINGLE;
+    g.mode = use_q8 == 2   ? ge::GEMM_PAIR
+             : use_q8 == 3 ? ge::GEMM_NARROW
+             : use_q8 == 4 ? ge::GEMM_SPLIT
+             : use_q8 == 5 ? ge::GEMM_LSU_STORE
+                           : ge::GEMM_SINGLE;
     g.err = static_cast<int*>(derr.p);
     g.num_sms = sms;
     TRY(ge::launch_gemm(g, nullptr));
@@ -177,9 +180,9 @@ int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int3
 
 int ge_test_gemm_time(int32_t m, int32_t k, int32_t n, int32_t epilogue, int32_t path, int32_t reps, double* us) {
     if (m <= 0 || m % ge::kRowTile || k <= 0 || n <= 0 || k % 64 || n % 256 || epilogue < 0 || epilogue > 2 ||
-        path < 0 || path > 4 || reps <= 0 || !us)
+        path < 0 || path > 5 || reps <= 0 || !us)
         return fail(GE_ERR_INVALID_OPTIONS,
-                    "invalid options: m % 128 == 0, k % 64 == 0, n % 256 == 0, epilogue 0..2, path 0..4");
+                    "invalid options: m % 128 == 0, k % 64 == 0, n % 256 == 0, epilogue 0..2, path 0..5");
     int dev = 0, sms = 0;
     TRY(cudaGetDevice(&dev));
     TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -220,22 +223,39 @@ int ge_test_gemm_time(int32_t m, int32_t k, int32_t n, int32_t epilogue, int32_t
     g.ldo = out_cols;
     g.epilogue = epilogue;
     g.use_q8 = path == 1;
-    g.mode = path == 2 ? ge::GEMM_PAIR : path == 3 ? ge::GEMM_NARROW : path == 4 ? ge::GEMM_SPLIT
-                                                                            : ge::GEMM_SINGLE;
+    g.mode = path == 2   ? ge::GEMM_PAIR
+             : path == 3 ? ge::GEMM_NARROW
+             : path == 4 ? ge::GEMM_SPLIT
+             : path == 5 ? ge::GEMM_LSU_STORE
+                         : ge::GEMM_SINGLE;
     g.err = static_cast<int*>(derr.p);
     g.num_sms = sms;
     cudaStream_t st = nullptr;
     TRY(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    // The launches are captured into a CUDA graph and the graph is timed: back-to-back host
+    // launches of a short kernel would time the host's launch rate instead of the kernel.
     cudaEvent_t e0 = nullptr, e1 = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
     cudaError_t e = cudaEventCreate(&e0);
     if (e == cudaSuccess) e = cudaEventCreate(&e1);
     for (int i = 0; i < 3 && e == cudaSuccess; i++) e = ge::launch_gemm(g, st);
+    if (e == cudaSuccess) e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+        for (int i = 0; i < reps && e == cudaSuccess; i++) e = ge::launch_gemm(g, st);
+        const cudaError_t ee = cudaStreamEndCapture(st, &graph);
+        if (e == cudaSuccess) e = ee;
+    }
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&exec, graph, 0);
+    if (e == cudaSuccess) e = cudaGraphLaunch(exec, st);
     if (e == cudaSuccess) e = cudaEventRecord(e0, st);
-    for (int i = 0; i < reps && e == cudaSuccess; i++) e = ge::launch_gemm(g, st);
+    if (e == cudaSuccess) e = cudaGraphLaunch(exec, st);
     if (e == cudaSuccess) e = cudaEventRecord(e1, st);
     if (e == cudaSuccess) e = cudaEventSynchronize(e1);
     float ms = 0.f;
     if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+    if (exec) cudaGraphExecDestroy(exec);
+    if (graph) cudaGraphDestroy(graph);
     if (e0) cudaEventDestroy(e0);
     if (e1) cudaEventDestroy(e1);
     cudaStreamDestroy(st);

@@ -24,13 +24,14 @@ extern "C" {
  * weights on single CTAs, 1 the in-shared-memory Q8 dequantisation, 2 fp16 weights on CTA
  * pairs (tcgen05.mma.cta_group::2), 3 fp16 weights on single CTAs with 128-wide tiles (not
  * for the GeGLU epilogue), 4 as 0 with tiles split into narrower pieces where that would
- * shorten the schedule (the last partial round, or every tile of a batch that leaves SMs idle).
+ * shorten the schedule (the last partial round, or every tile of a batch that leaves SMs idle),
+ * 5 as 0 with the epilogue's tiles written by ordinary stores instead of TMA bulk stores.
  * Results are returned as fp32 [m][n] (or [m][n/2]). */
 GE_API int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w_q8_0, int32_t n, int32_t epilogue,
                         int32_t path, const float* aux, float* out);
 
-/* Mean device time of one GEMM launch (CUDA events around `reps` back-to-back launches on a
- * stream of its own, after three untimed ones) for m x k seeded fp16 activations (m a multiple
+/* Mean device time of one GEMM launch (CUDA events around a CUDA graph of `reps` back-to-back
+ * launches on a stream of its own, after three untimed launches and one untimed graph run) for m x k seeded fp16 activations (m a multiple
  * of 128) and an n x k seeded Q8_0 weight: epilogue 0 fp32 store, 1 fp16 store, 2 GeGLU over
  * interleaved rows; path as ge_test_gemm.  Writes microseconds per launch to *us. */
 GE_API int ge_test_gemm_time(int32_t m, int32_t k, int32_t n, int32_t epilogue, int32_t path, int32_t reps, double* us);
