@@ -521,7 +521,7 @@ def gemm_schedule_sweep(rows_list=(1024, 2432, 19584), reps=20):
     import ctypes
     lib = importlib.import_module(PKG + "._lib").lib()
     epi = {"gemm_qkv": 1, "gemm_o": 1, "gemm_gate_up": 2, "gemm_down": 1}
-    paths = {"whole_tiles": 0, "split_tiles": 4, "cta_pairs": 2, "q8_smem": 1, "lsu_stores": 5}
+    paths = {"whole_tiles": 0, "split_tiles": 4, "cta_pairs": 2, "q8_smem": 1}
     pk = peaks()
     out = []
     for rows in rows_list:

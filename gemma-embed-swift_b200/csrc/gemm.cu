@@ -85,9 +85,6 @@ struct GemmParams {
     // Split tiles: tiles from split_from on run as `split` pieces of BN / split columns
     // (split_from == the tile count: no split)
     int split_from, split;
-    // Epilogue stores through the load/store units (each warp writes its staged rows as
-    // 128-byte lines) instead of TMA bulk stores (GEMM_LSU_STORE, single-CTA tiles)
-    int lsu_store;
     // EPI_QKV (eps above)
     const int32_t* pos;
     const float* rope;
@@ -353,26 +350,6 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
         uint8_t* stg = smem + L::kStgOff + epi * L::kStgBufs * 4096;
         int sbuf = 0;
         auto emit = [&](const uint32_t (&v)[32], int x, int y, const CUtensorMap* map) {
-            if (!RES && !PAIR && p.lsu_store) {
-                // The warp's 32 rows x 128 bytes go through its first staging buffer (swizzled
-                // like the TMA path) and out as four 128-byte lines per store instruction.
-                constexpr int kEB = (EPI == EPI_F32 || EPI == EPI_CLAMP_F32) ? 4 : 2;
-                __syncwarp();
-                uint8_t* row = stg + lane * 128;
-#pragma unroll
-                for (int j = 0; j < 8; j++)
-                    *reinterpret_cast<uint4*>(row + ((j ^ (lane & 7)) * 16)) =
-                        make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-                __syncwarp();
-                uint8_t* out = static_cast<uint8_t*>(p.out);
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const int rr = i * 4 + (lane >> 3), ch = lane & 7;
-                    const uint4 val = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((ch ^ (rr & 7)) * 16));
-                    *reinterpret_cast<uint4*>(out + (long(y + rr) * p.ldo + x) * kEB + ch * 16) = val;
-                }
-                return;
-            }
             if (lane == 0) bulk_wait_read<L::kStgBufs - 1>();
             __syncwarp();
             uint8_t* buf = stg + sbuf * 4096 + lane * 128;
@@ -1013,7 +990,6 @@ static cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
     const CUtensorMap& mb = Q8 ? g.w->map_q8 : ((PAIR || BN != kBN) ? g.w->map_f16_half : g.w->map_f16);
     p.split_from = 1 << 30;
     p.split = 1;
-    p.lsu_store = g.mode == GEMM_LSU_STORE ? 1 : 0;
     const CUtensorMap* mp = &g.w->map_f16_half;
     CUtensorMap mc;
     EpiMaps em;

@@ -119,9 +119,7 @@ bool encode_activation_map(DevActivation& a);
 // persistent schedule on paper (the last partial round, or every tile of a batch that leaves SMs
 // idle; see k_gemm).  Bit-identical to whole tiles, measured no faster on any forward shape
 // (bench.py's gemm_schedules), so only on request.
-// GEMM_LSU_STORE writes the epilogue's staged tiles with ordinary 16-byte stores instead of TMA
-// bulk stores (single-CTA 256-wide tiles; results identical).
-enum GemmMode : int { GEMM_AUTO = 0, GEMM_SINGLE = 1, GEMM_PAIR = 2, GEMM_NARROW = 3, GEMM_SPLIT = 4, GEMM_LSU_STORE = 5 };
+enum GemmMode : int { GEMM_AUTO = 0, GEMM_SINGLE = 1, GEMM_PAIR = 2, GEMM_NARROW = 3, GEMM_SPLIT = 4 };
 
 struct GemmLaunch {
     const DevActivation* a;

@@ -159,7 +159,6 @@ int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int3
     g.mode = use_q8 == 2   ? ge::GEMM_PAIR
              : use_q8 == 3 ? ge::GEMM_NARROW
              : use_q8 == 4 ? ge::GEMM_SPLIT
-             : use_q8 == 5 ? ge::GEMM_LSU_STORE
                            : ge::GEMM_SINGLE;
     g.err = static_cast<int*>(derr.p);
     g.num_sms = sms;
@@ -180,9 +179,9 @@ int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w, int3
 
 int ge_test_gemm_time(int32_t m, int32_t k, int32_t n, int32_t epilogue, int32_t path, int32_t reps, double* us) {
     if (m <= 0 || m % ge::kRowTile || k <= 0 || n <= 0 || k % 64 || n % 256 || epilogue < 0 || epilogue > 2 ||
-        path < 0 || path > 5 || reps <= 0 || !us)
+        path < 0 || path > 4 || reps <= 0 || !us)
         return fail(GE_ERR_INVALID_OPTIONS,
-                    "invalid options: m % 128 == 0, k % 64 == 0, n % 256 == 0, epilogue 0..2, path 0..5");
+                    "invalid options: m % 128 == 0, k % 64 == 0, n % 256 == 0, epilogue 0..2, path 0..4");
     int dev = 0, sms = 0;
     TRY(cudaGetDevice(&dev));
     TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -226,7 +225,6 @@ int ge_test_gemm_time(int32_t m, int32_t k, int32_t n, int32_t epilogue, int32_t
     g.mode = path == 2   ? ge::GEMM_PAIR
              : path == 3 ? ge::GEMM_NARROW
              : path == 4 ? ge::GEMM_SPLIT
-             : path == 5 ? ge::GEMM_LSU_STORE
                          : ge::GEMM_SINGLE;
     g.err = static_cast<int*>(derr.p);
     g.num_sms = sms;

@@ -24,8 +24,7 @@ extern "C" {
  * weights on single CTAs, 1 the in-shared-memory Q8 dequantisation, 2 fp16 weights on CTA
  * pairs (tcgen05.mma.cta_group::2), 3 fp16 weights on single CTAs with 128-wide tiles (not
  * for the GeGLU epilogue), 4 as 0 with tiles split into narrower pieces where that would
- * shorten the schedule (the last partial round, or every tile of a batch that leaves SMs idle),
- * 5 as 0 with the epilogue's tiles written by ordinary stores instead of TMA bulk stores.
+ * shorten the schedule (the last partial round, or every tile of a batch that leaves SMs idle).
  * Results are returned as fp32 [m][n] (or [m][n/2]). */
 GE_API int ge_test_gemm(const uint16_t* a, int32_t m, int32_t k, const uint8_t* w_q8_0, int32_t n, int32_t epilogue,
                         int32_t path, const float* aux, float* out);

@@ -73,8 +73,6 @@ def test_gemm_shapes_fp32(ge, synth, cuda_device, m, k, n):
     assert gotp.tobytes() == got16.tobytes()
     # 128-wide tiles: the same per-element accumulation order, identical bits.
     assert gotn.tobytes() == got16.tobytes()
-    # the epilogue's stores through the load/store units instead of TMA: the same values
-    assert gemm(ge, a, wq, n, 0, use_q8=5).tobytes() == got16.tobytes()
 
 
 @pytest.mark.parametrize("use_q8", [False, True, 2])
@@ -129,7 +127,6 @@ def test_gemm_split_tiles_match_whole_tiles(ge, synth, cuda_device, k, n, m):
         split = gemm(ge, a, wq, n, epi, use_q8=4)
         whole = gemm(ge, a, wq, n, epi, use_q8=0)
         assert split.tobytes() == whole.tobytes(), epi
-        assert gemm(ge, a, wq, n, epi, use_q8=5).tobytes() == whole.tobytes(), epi
     assert max_rel(split, a64 @ wd.T) < TOL_F16
     assert max_rel(gemm(ge, a, wq, n, 0, use_q8=4), a64 @ wd.T) < TOL_F32
     if n % 256 == 0 and n >= 1024:
@@ -138,7 +135,6 @@ def test_gemm_split_tiles_match_whole_tiles(ge, synth, cuda_device, k, n, m):
     if n == 2304:  # gate/up interleaved in blocks of 128 rows, as the loader lays them out
         split = gemm(ge, a, wq, n, 2, use_q8=4)
         assert split.tobytes() == gemm(ge, a, wq, n, 2, use_q8=0).tobytes()
-        assert gemm(ge, a, wq, n, 2, use_q8=5).tobytes() == split.tobytes()
         g = np.concatenate([a64 @ wd[j * 256:j * 256 + 128].T for j in range(n // 256)], axis=1)
         u = np.concatenate([a64 @ wd[j * 256 + 128:(j + 1) * 256].T for j in range(n // 256)], axis=1)
         want = 0.5 * g * (1 + np.tanh(0.7978845608028654 * (g + 0.044715 * g ** 3))) * u  # GELU (tanh form)
