@@ -61,7 +61,10 @@ constexpr int kOffP = kOffV + 2 * kKVBytes;
 constexpr int kOffRed = kOffP + 2 * kPBytes;    // [2 halves][128 rows] floats: row maxima, then sums
 constexpr int kOffBar = kOffRed + 2 * kTcQ * 4;
 constexpr int kTcSmem = kOffBar + 256 + 1024;
-constexpr int kTcThreads = 320;
+constexpr int kTcThreads = 384;
+constexpr int kSWarpB = 10;  // the second S issuer
+constexpr int kPVWarp = 11;  // the PV issuer
+constexpr uint32_t kPollNs = 64;  // producer and issuer poll interval
 constexpr uint32_t kTmemO = 0, kTmemS = 256;
 
 struct TcAttnParams {
@@ -112,7 +115,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
     uint64_t* p_full = bars + 12;
     uint64_t* pv_done = bars + 14;
     uint64_t* o_empty = bars + 16;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 17);
+    uint64_t* s_free = bars + 17;  // S buffer read into registers by every softmax thread
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int live_rows = p.group * p.tokens;
@@ -120,7 +124,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        mbar_init(q_empty, 1);
+        mbar_init(q_empty, 2);  // both S issuers sign off each Q tile
         for (int i = 0; i < 2; i++) {
             mbar_init(&k_full[i], 1);
             mbar_init(&k_empty[i], 1);
@@ -131,6 +135,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
             mbar_init(&pv_done[i], 1);
         }
         mbar_init(o_empty, 256);
+        for (int i = 0; i < 2; i++) mbar_init(&s_free[i], 256);
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
@@ -142,6 +147,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
         tmem_alloc(tmem_slot, 512);
         tmem_relinquish();
     }
+    // Rows [live_rows, rows per chunk) of the Q chunks are never loaded: zeroed once, their
+    // scores stay finite, so the softmax can treat them as unmasked rows (never stored).
+    {
+        constexpr int kChunkRows = kQChunk / 128;
+        const int dead = kChunkRows - live_rows;
+        for (int i = threadIdx.x; i < kChunks * dead * 8; i += kTcThreads) {
+            const int c = i / (dead * 8), rr = live_rows + (i / 8) % dead, q = i % 8;
+            *reinterpret_cast<uint4*>(smem + c * kQChunk + rr * 128 + q * 16) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        fence_proxy_async_smem();
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -150,45 +166,88 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
 
     if (warp == 0) {
         // ---------------------------------------------------------- TMA producer
+        // Two cursors walk the CTA's items: Q and K tiles (each item's Q, then its K tiles), and
+        // V tiles.  Each load is issued as soon as its ring slot is free, so a K tile never
+        // waits behind a V tile whose slot is still being read, or the other way round.
         if (lane == 0) {
+            const int it_end = int(p.offset[blockIdx.x + 1]);
+            int issued_q = 0, issued_k = 0, issued_v = 0;
+            // K cursor: item kit (local index kli), block kj of nk, half kh; global half gk.
+            int kit = int(p.offset[blockIdx.x]), kli = 0, kj = 0, kh = 0, gk = 0, nk = 0, ks = 0;
+            bool q_done = false;
+            // V cursor: item vit, block vj of nv; global block gv.
+            int vit = int(p.offset[blockIdx.x]), vj = 0, gv = 0, nv = 0, vs = 0;
+            if (vit < it_end) item_keys(p.work[vit], p, vs, nv);
+            uint64_t idle_since = globaltimer();
             bool ok = true;
-            int gb = 0, gk = 0, issued_q = 0, issued_k = 0, issued_v = 0;
-            for (int it = int(p.offset[blockIdx.x]), li = 0; it < int(p.offset[blockIdx.x + 1]) && ok; it++, li++) {
-                const uint4 w = p.work[it];
-                int k_start, nblk;
-                item_keys(w, p, k_start, nblk);
-                const int kh = int(w.w & 0xffffu), hv = int(w.w >> 16);  // KV head, output half
-                if (!mbar_wait(q_empty, uint32_t(li & 1) ^ 1u, p.err)) break;
-                mbar_expect_tx(q_full, q_bytes);
-                for (int c = 0; c < kChunks; c++)
-                    tma_load_3d(smem + c * kQChunk, &mapQ, q_full, c * 64, kh * p.group, int(w.x + w.z));
-                issued_q++;
-                for (int j = 0; j < nblk; j++, gb++) {
-                    const int b = gb & 1;
-                    const uint32_t ph = uint32_t((gb >> 1) & 1);
-                    const int row = int(w.x) + k_start + j * kTcKeys;
-                    for (int hk = 0; hk < kHalves && ok; hk++, gk++) {
-                        const int bk = gk & 1;
-                        if (!mbar_wait(&k_empty[bk], uint32_t((gk >> 1) & 1) ^ 1u, p.err)) {
-                            ok = false;
-                            break;
+            while (ok && (kit < it_end || vit < it_end)) {
+                bool moved = false;
+                if (kit < it_end) {
+                    const uint4 w = p.work[kit];
+                    const int kvh = int(w.w & 0xffffu);
+                    if (!q_done) {
+                        if (mbar_poll(q_empty, uint32_t(kli & 1) ^ 1u)) {
+                            mbar_expect_tx(q_full, q_bytes);
+                            for (int c = 0; c < kChunks; c++)
+                                tma_load_3d(smem + c * kQChunk, &mapQ, q_full, c * 64, kvh * p.group, int(w.x + w.z));
+                            issued_q++;
+                            q_done = true;
+                            item_keys(w, p, ks, nk);
+                            moved = true;
                         }
-                        mbar_expect_tx(&k_full[bk], kKVBytes);
+                    } else {
+                        const int bk = gk & 1;
+                        if (mbar_poll(&k_empty[bk], uint32_t((gk >> 1) & 1) ^ 1u)) {
+                            mbar_expect_tx(&k_full[bk], kKVBytes);
+                            const int row = int(w.x) + ks + kj * kTcKeys;
+                            for (int c = 0; c < 4; c++)
+                                tma_load_2d(smem + kOffK + bk * kKVBytes + c * (kKVBytes / 4), &mapK, &k_full[bk],
+                                            kvh * HD + kh * kTcHd + c * 64, row);
+                            issued_k++;
+                            gk++;
+                            moved = true;
+                            if (++kh == kHalves) {
+                                kh = 0;
+                                if (++kj == nk) {
+                                    kj = 0;
+                                    kit++;
+                                    kli++;
+                                    q_done = false;
+                                }
+                            }
+                        }
+                    }
+                }
+                if (vit < it_end) {
+                    const int b = gv & 1;
+                    if (mbar_poll(&v_empty[b], uint32_t((gv >> 1) & 1) ^ 1u)) {
+                        const uint4 w = p.work[vit];
+                        const int kvh = int(w.w & 0xffffu), hv = int(w.w >> 16);  // KV head, output half
+                        mbar_expect_tx(&v_full[b], kKVBytes);
+                        const int row = int(w.x) + vs + vj * kTcKeys;
                         for (int c = 0; c < 4; c++)
-                            tma_load_2d(smem + kOffK + bk * kKVBytes + c * (kKVBytes / 4), &mapK, &k_full[bk],
-                                        kh * HD + hk * kTcHd + c * 64, row);
-                        issued_k++;
+                            tma_load_2d(smem + kOffV + b * kKVBytes + c * (kKVBytes / 4), &mapV, &v_full[b],
+                                        kvh * HD + hv * kTcHd + c * 64, row);
+                        issued_v++;
+                        gv++;
+                        moved = true;
+                        if (++vj == nv) {
+                            vj = 0;
+                            if (++vit < it_end) item_keys(p.work[vit], p, vs, nv);
+                        }
                     }
-                    if (!ok) break;
-                    if (!mbar_wait(&v_empty[b], ph ^ 1, p.err)) {
+                }
+                if (moved) {
+                    idle_since = globaltimer();
+                } else {
+                    // Nothing to issue yet: back off, and give up like a bounded wait would.
+                    __nanosleep(kPollNs);
+                    if (*reinterpret_cast<volatile int*>(p.err) != 0) {
                         ok = false;
-                        break;
+                    } else if (globaltimer() - idle_since > kWaitLimitNs) {
+                        atomicCAS(p.err, 0, kErrTimeout);
+                        ok = false;
                     }
-                    mbar_expect_tx(&v_full[b], kKVBytes);
-                    for (int c = 0; c < 4; c++)
-                        tma_load_2d(smem + kOffV + b * kKVBytes + c * (kKVBytes / 4), &mapV, &v_full[b],
-                                    kh * HD + hv * kTcHd + c * 64, row);
-                    issued_v++;
                 }
             }
             pdl_launch();  // this CTA's loads are all issued: the next kernel may be scheduled
@@ -201,47 +260,41 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                 if (cv > 0) drain(&v_full[b], uint32_t((cv - 1) & 1));
             }
         }
-    } else if (warp == 1) {
-        // ---------------------------------------------------------- MMA issuer
+    } else if (warp == 1 || warp == kSWarpB) {
+        // ---------------------------------------------------------- S issuers
+        // A tcgen05.mma takes its issuing thread about as long to issue as a 128 x 64 x 16
+        // product takes the tensor core to run, so one thread cannot keep up with the S products
+        // of 64-key blocks.  Head dim 256: warp 1 issues S for the even global blocks and warp
+        // kSWarpB for the odd ones, each through its own K-ring slot (block g into S buffer
+        // g & 1, the same chain of MMAs one issuer would run).  Head dim 512 takes both K-ring
+        // slots per block, so warp 1 issues every block and warp kSWarpB only signs off Q tiles.
         if (lane == 0) {
-            const uint32_t id_s = idesc_f16(kTcQ, kTcKeys);            // K-major Q and K
-            const uint32_t id_o = idesc_f16(kTcQ, kTcHd, 0, 1);        // K-major P, MN-major V
+            const int par = warp == 1 ? 0 : 1;
+            const uint32_t id_s = idesc_f16(kTcQ, kTcKeys);  // K-major Q and K
             const uint32_t q_addr = smem_u32(smem);
             bool ok = true;
-            // PV of global block g; the first block of item li overwrites O once the previous
-            // item's O has been read out.
-            auto issue_pv = [&](int g, bool first, int li) -> bool {
-                const int b = g & 1;
-                const uint32_t ph = uint32_t((g >> 1) & 1);
-                if (first && li > 0 && !mbar_wait(o_empty, uint32_t((li - 1) & 1), p.err)) return false;
-                if (!mbar_wait(&p_full[b], ph, p.err) || !mbar_wait(&v_full[b], ph, p.err)) return false;
-                tc_fence_after();
-                const uint32_t pa = smem_u32(smem + kOffP + b * kPBytes);
-                const uint32_t va = smem_u32(smem + kOffV + b * kKVBytes);
-#pragma unroll
-                for (int kk = 0; kk < kTcKeys / 16; kk++) {
-                    const uint64_t ad = sw128_desc(pa + kk * 32, 16, 1024);
-                    // V chunk of 64 dims = one [64 keys][128 B] box; 16 keys advance 2048 B.
-                    const uint64_t bd = sw128_desc(va + kk * 2048, kKVBytes / 4, 1024);
-                    umma_f16(tmem + kTmemO, ad, bd, id_o, !(first && kk == 0));
-                }
-                umma_commit(&v_empty[b]);
-                umma_commit(&pv_done[b]);
-                return true;
-            };
-            int gb = 0, gk = 0;
+            int gb = 0;
             for (int it = int(p.offset[blockIdx.x]), li = 0; it < int(p.offset[blockIdx.x + 1]) && ok; it++, li++) {
                 const uint4 w = p.work[it];
                 int k_start, nblk;
                 item_keys(w, p, k_start, nblk);
-                if (!mbar_wait(q_full, uint32_t(li & 1), p.err)) break;
-                tc_fence_after();
+                // Every issuer waits for every Q tile, so neither runs a phase ahead of the other.
+                if (!mbar_wait_sleep(q_full, uint32_t(li & 1), p.err, kPollNs)) break;
+                bool used_q = false;
                 for (int j = 0; j < nblk; j++, gb++) {
+                    if (kHalves == 1 ? (gb & 1) != par : par != 0) continue;
                     const int b = gb & 1;
-                    // S_j = Q K_j^T over every dim, one K-ring slot (256 dims) at a time
-                    for (int hk = 0; hk < kHalves && ok; hk++, gk++) {
-                        const int bk = gk & 1;
-                        if (!mbar_wait(&k_full[bk], uint32_t((gk >> 1) & 1), p.err)) {
+                    // S buffer b is free once every softmax thread holds block gb - 2's scores.
+                    if (gb >= 2 && !mbar_wait_sleep(&s_free[b], uint32_t(((gb - 2) >> 1) & 1), p.err, kPollNs)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    used_q = true;
+                    // S_gb = Q K_gb^T over every dim, one K-ring slot (256 dims) at a time
+                    for (int hk = 0; hk < kHalves && ok; hk++) {
+                        const int gk = gb * kHalves + hk, bk = gk & 1;
+                        if (!mbar_wait_sleep(&k_full[bk], uint32_t((gk >> 1) & 1), p.err, kPollNs)) {
                             ok = false;
                             break;
                         }
@@ -258,13 +311,51 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                     }
                     if (!ok) break;
                     umma_commit(&s_full[b]);
-                    if (j == nblk - 1) umma_commit(q_empty);  // every S of the item has read Q
-                    if (j > 0 && !issue_pv(gb - 1, j == 1, li)) {
+                }
+                if (!ok) break;
+                // Both issuers sign off each item's Q: after their S products have read it, or
+                // at once when this issuer ran no block of the item.
+                if (used_q)
+                    umma_commit(q_empty);
+                else
+                    mbar_arrive(q_empty);
+            }
+        }
+    } else if (warp == kPVWarp) {
+        // ---------------------------------------------------------- PV issuer
+        if (lane == 0) {
+            const uint32_t id_o = idesc_f16(kTcQ, kTcHd, 0, 1);  // K-major P, MN-major V
+            bool ok = true;
+            int gb = 0;
+            for (int it = int(p.offset[blockIdx.x]), li = 0; it < int(p.offset[blockIdx.x + 1]) && ok; it++, li++) {
+                const uint4 w = p.work[it];
+                int k_start, nblk;
+                item_keys(w, p, k_start, nblk);
+                for (int j = 0; j < nblk; j++, gb++) {
+                    const int b = gb & 1;
+                    const uint32_t ph = uint32_t((gb >> 1) & 1);
+                    // An item's first PV overwrites O once the previous item's O has been read out.
+                    if (j == 0 && li > 0 && !mbar_wait_sleep(o_empty, uint32_t((li - 1) & 1), p.err, kPollNs)) {
                         ok = false;
                         break;
                     }
+                    if (!mbar_wait_sleep(&p_full[b], ph, p.err, kPollNs) || !mbar_wait_sleep(&v_full[b], ph, p.err, kPollNs)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t pa = smem_u32(smem + kOffP + b * kPBytes);
+                    const uint32_t va = smem_u32(smem + kOffV + b * kKVBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kTcKeys / 16; kk++) {
+                        const uint64_t ad = sw128_desc(pa + kk * 32, 16, 1024);
+                        // V chunk of 64 dims = one [64 keys][128 B] box; 16 keys advance 2048 B.
+                        const uint64_t bd = sw128_desc(va + kk * 2048, kKVBytes / 4, 1024);
+                        umma_f16(tmem + kTmemO, ad, bd, id_o, !(j == 0 && kk == 0));
+                    }
+                    umma_commit(&v_empty[b]);
+                    umma_commit(&pv_done[b]);
                 }
-                if (ok && !issue_pv(gb - 1, nblk == 1, li)) ok = false;
             }
         }
     } else {
@@ -292,10 +383,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
             item_keys(w, p, k_start, nblk);
             const int len = int(w.y);
             const int qi = int(w.z) + rt;  // this row's token within its sequence
-            // Keys this row sees: [row_lo, row_hi) of its sequence; none for the rows of the
-            // tile past the item's G x T (their scores come from whatever shared memory holds).
-            const int row_lo = p.hw > 0 ? max(qi - p.hw, 0) : 0;
-            const int row_hi = r >= live_rows ? row_lo : p.hw > 0 ? min(qi + p.hw + 1, len) : len;
+            // Keys this row sees: [row_lo, row_hi) of its sequence.  Rows past the item's G x T
+            // see every key (their Q rows are zero and they are never stored): no per-key mask,
+            // which would hold up their warps on every block.
+            const bool dead = r >= live_rows;
+            const int row_lo = dead ? 0 : p.hw > 0 ? max(qi - p.hw, 0) : 0;
+            const int row_hi = dead ? (1 << 30) : p.hw > 0 ? min(qi + p.hw + 1, len) : len;
             float m_used = -INFINITY, l = 0.f;  // running maximum (log2 units) and this half's sum
             for (int j = 0; j < nblk; j++, gb++) {
                 const int b = gb & 1;
@@ -308,6 +401,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                     tc_fence_after();
                     tmem_ld32(lane_base + kTmemS + b * kTcKeys + half * 32, sr);
                     tmem_wait_ld();
+                    tc_fence_before();
+                    mbar_arrive(&s_free[b]);  // the S buffer may take block gb + 2
                     // Scores in log2 units: p = 2^(s log2e - m), one FFMA and one ex2 per key.
                     if (kb >= row_lo && kb + 32 <= row_hi) {  // every key of this half is visible
 #pragma unroll
@@ -360,26 +455,27 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                     }
                 }
                 if (m_used == -INFINITY) m_used = mb;  // first block with a visible key (O and l are still 0)
-                // P goes to buffer b once the PV two blocks back, which read that buffer, has completed.
+                float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
+                const float mu = m_used == -INFINITY ? 0.f : m_used;
+                uint32_t pk[16];  // this half's 32 probabilities as fp16 pairs
+#pragma unroll
+                for (int e = 0; e < 16; e++) {
+                    const float p0 = ex2_approx(__uint_as_float(sr[2 * e]) - mu);  // 2^-inf = 0
+                    const float p1 = ex2_approx(__uint_as_float(sr[2 * e + 1]) - mu);
+                    ps[(2 * e) & 7] += p0;
+                    ps[(2 * e + 1) & 7] += p1;
+                    pk[e] = pack_half2(p0, p1);
+                }
+                // P goes to buffer b once the PV two blocks back, which read that buffer, has
+                // completed (waited for after the exponentials, which do not need the buffer).
                 if (gb >= 2) wait_all(&pv_done[b], uint32_t(((gb - 2) >> 1) & 1));
                 if (!ok) continue;
                 uint8_t* prow = smem + kOffP + b * kPBytes + r * 128;
-                float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
-                const float mu = m_used == -INFINITY ? 0.f : m_used;
 #pragma unroll
                 for (int c = 0; c < 4; c++) {  // 4 chunks of 8 keys = 16 bytes each
-                    uint32_t wv[4];
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const float p0 = ex2_approx(__uint_as_float(sr[c * 8 + 2 * e]) - mu);  // 2^-inf = 0
-                        const float p1 = ex2_approx(__uint_as_float(sr[c * 8 + 2 * e + 1]) - mu);
-                        ps[2 * e] += p0;
-                        ps[2 * e + 1] += p1;
-                        __half2 hp = __floats2half2_rn(p0, p1);
-                        wv[e] = *reinterpret_cast<uint32_t*>(&hp);
-                    }
                     const int chunk = half * 4 + c;
-                    *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) * 16)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+                    *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) * 16)) =
+                        make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
                 }
                 l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
                 fence_proxy_async_smem();

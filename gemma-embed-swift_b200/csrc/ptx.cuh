@@ -51,6 +51,18 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
+// Non-blocking check that the phase of parity `parity` has completed.
+__device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
 // Waits for the phase of parity `parity` to complete.  Gives up after kWaitLimitNs, or as
 // soon as another thread has recorded an error, and returns false in both cases.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
@@ -59,6 +71,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     for (uint32_t spin = 1;; spin++) {
         if (mbar_test(bar, parity)) return true;
         if ((spin & 63) == 0) {  // the error word and the clock are checked every 64 tries
+            if (*reinterpret_cast<volatile int*>(err) != 0) return false;
+            if (globaltimer() - t0 > kWaitLimitNs) {
+                atomicCAS(err, 0, kErrTimeout);
+                return false;
+            }
+        }
+    }
+}
+
+// mbar_wait for threads that share their scheduler with busy warps (TMA producers, MMA
+// issuers): between polls the thread sleeps `ns` nanoseconds instead of spinning, so its polls
+// do not take issue slots from the warps that produce what it waits for.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int* err, uint32_t ns) {
+    if (mbar_test(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t spin = 1;; spin++) {
+        __nanosleep(ns);
+        if (mbar_test(bar, parity)) return true;
+        if ((spin & 15) == 0) {
             if (*reinterpret_cast<volatile int*>(err) != 0) return false;
             if (globaltimer() - t0 > kWaitLimitNs) {
                 atomicCAS(err, 0, kErrTimeout);
