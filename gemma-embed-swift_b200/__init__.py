@@ -40,6 +40,7 @@ LOAD_Q8_ONLY = 2
 LOAD_NO_PDL = 4
 LOAD_FUSED_RESIDUAL = 8
 LOAD_FUSED_QKV = 16
+LOAD_SINGLE_CTA_GEMM = 32
 
 
 class GemmaEmbedError(RuntimeError):
@@ -192,6 +193,7 @@ class LoadOptions:
     programmatic_launch: bool = True  # overlap each kernel's set-up with its predecessor's tail
     fused_residual: bool = False  # run each residual step inside the projection before it
     fused_qkv: bool = False  # run the q/k/v norms and RoPE inside the q/k/v projection (head dim 256)
+    cta_pair_gemm: bool = True  # large batches' projections on CTA pairs (256 x 256 tiles); bit-identical
     image_encoder: Optional[str] = None  # LoadOptions.imageEncoder: the mmproj GGUF
     image_patch_budget: int = 4096       # ImageEmbedOptions.patchBudget: patches per image batch
     audio_encoder: Optional[str] = None  # LoadOptions.audioEncoder: the mmproj GGUF with a gemma4a tower
@@ -467,7 +469,8 @@ class EmbeddingModel:
         o.flags = ((0 if options.use_graphs else LOAD_NO_GRAPHS) | (LOAD_Q8_ONLY if options.q8_only else 0)
                    | (0 if options.programmatic_launch else LOAD_NO_PDL)
                    | (LOAD_FUSED_RESIDUAL if options.fused_residual else 0)
-                   | (LOAD_FUSED_QKV if options.fused_qkv else 0))
+                   | (LOAD_FUSED_QKV if options.fused_qkv else 0)
+                   | (0 if options.cta_pair_gemm else LOAD_SINGLE_CTA_GEMM))
         o.image_encoder_path = str(options.image_encoder).encode() if options.image_encoder else None
         o.image_patch_budget = int(options.image_patch_budget)
         o.audio_encoder_path = str(options.audio_encoder).encode() if options.audio_encoder else None

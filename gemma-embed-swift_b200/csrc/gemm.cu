@@ -44,11 +44,14 @@ constexpr int kBN = 256;
 // holds 128 rows of A and BN/2 rows of B per stage, so shared-memory traffic per MMA halves.
 // RES (EPI_RESIDUAL): clusters of N / BN CTAs share row blocks; the epilogue also stages
 // residual-stream tiles (kXin) and receives the cluster's per-row sums of squares (kXch).
+// PAIR stages hold 128 K (two 64-wide swizzled chunks per operand): a stage's wait and commits
+// then cover eight MMAs, and three 64 KB stages keep about two stages of loads in flight.
 template <int BN, bool Q8, bool PAIR = false, bool RES = false>
 struct GemmLayout {
-    static constexpr int kStages = RES ? (Q8 ? 2 : 3) : Q8 ? 3 : ((PAIR || BN < 256) ? 6 : 4);
-    static constexpr int kA = BM * BK * 2;
-    static constexpr int kB = (PAIR ? BN / 2 : BN) * BK * 2;
+    static constexpr int kBK = PAIR ? 2 * BK : BK;  // K per stage
+    static constexpr int kStages = RES ? (Q8 ? 2 : 3) : Q8 ? 3 : PAIR ? 3 : (BN < 256 ? 6 : 4);
+    static constexpr int kA = BM * kBK * 2;
+    static constexpr int kB = (PAIR ? BN / 2 : BN) * kBK * 2;
     static constexpr int kB8 = Q8 ? BN * BK : 0;
     static constexpr int kSc = Q8 ? 2 * BN * 2 : 0;
     static constexpr int kStage = (kA + kB + kB8 + kSc + 1023) / 1024 * 1024;
@@ -148,7 +151,7 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tiles = p.N / BN;
-    const int kb_count = p.K / BK;
+    const int kb_count = p.K / L::kBK;
     // Tiles in a fixed order: n fastest, so the CTAs working at one time share A rows in L2.
     // A pair's tile covers 256 rows: the pair leader (rank 0) the first 128, rank 1 the rest.
     // A row cluster (RES) walks row blocks; its CTA of rank r always takes columns r * BN.
@@ -253,8 +256,11 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
                         // Both CTAs' loads complete on the leader's barrier, which expects them all.
                         const uint32_t bar = mapa_shared(&full_tma[s], 0);
                         if (crank == 0) mbar_expect_tx(&full_tma[s], 2 * (L::kA + L::kB));
-                        tma_load_2d_pair(st, &mapA, bar, kb * BK, m0);
-                        tma_load_2d_pair(st + L::kA, &mapB, bar, kb * BK, n0 + int(crank) * (BN / 2));
+                        for (int c = 0; c < L::kBK / BK; c++) {  // 64-wide K chunks
+                            tma_load_2d_pair(st + c * (L::kA / (L::kBK / BK)), &mapA, bar, kb * L::kBK + c * BK, m0);
+                            tma_load_2d_pair(st + L::kA + c * (L::kB / (L::kBK / BK)), &mapB, bar, kb * L::kBK + c * BK,
+                                             n0 + int(crank) * (BN / 2));
+                        }
                     } else {
                         mbar_expect_tx(&full_tma[s], L::kA + (Q8 ? L::kB8 + L::kSc : sub < 0 ? L::kB : L::kB / split));
                         tma_load_2d(st, &mapA, &full_tma[s], kb * BK, m0);
@@ -312,9 +318,14 @@ __global__ void __launch_bounds__(GemmLayout<BN, Q8, PAIR, EPI == EPI_RESIDUAL>:
                     const uint64_t ad = sw128_desc(smem_u32(st), 16, 1024);
                     const uint64_t bd = sw128_desc(smem_u32(st + L::kA), 16, 1024);
                     if (PAIR) {
+                        // 16-wide K steps: chunk kk / 4 of each operand, 32 bytes apart inside it
 #pragma unroll
-                        for (int kk = 0; kk < BK / 16; kk++)
-                            umma_f16_pair(d, ad + uint64_t(kk * 2), bd + uint64_t(kk * 2), idesc, (kb | kk) != 0);
+                        for (int kk = 0; kk < L::kBK / 16; kk++) {
+                            const uint64_t ca = uint64_t(((kk >> 2) * (L::kA / (L::kBK / BK))) >> 4);
+                            const uint64_t cb = uint64_t(((kk >> 2) * (L::kB / (L::kBK / BK))) >> 4);
+                            umma_f16_pair(d, ad + ca + uint64_t((kk & 3) * 2), bd + cb + uint64_t((kk & 3) * 2), idesc,
+                                          (kb | kk) != 0);
+                        }
                         umma_commit_pair(mapa_shared(&empty[s], 0));
                         umma_commit_pair(mapa_shared(&empty[s], 1));
                     } else {
@@ -1090,7 +1101,16 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream) {
     // The Q8 path needs the Q8 planes; weights without them always take the fp16 path.
     if (!g.w->f16 && !g.w->q8) return cudaErrorInvalidValue;
     const bool q8 = g.w->q8 && (g.use_q8 || !g.w->f16);
-    const bool pair = !q8 && g.mode == GEMM_PAIR;
+    // CTA pairs run 128-deep K stages.  Under AUTO they take large batches: a pair streams half
+    // the operand bytes per MMA of a single CTA and issues one instruction per 256 x 256 x 16
+    // product, but below two rounds of pair tiles single CTAs spread the work over more SMs.
+    const int pair_tiles = ((g.m_rows + 2 * BM - 1) / (2 * BM)) * (g.w->N / kBN);
+    // The last pair tile's second CTA may lie wholly past m_rows (loads there read zeros and its
+    // stores are clipped), so epilogues that read per-row inputs (GELU_MUL's aux, QKV's
+    // positions) and the residual clusters stay on single CTAs.
+    const bool pair_ok = !q8 && g.w->K % (2 * BK) == 0 && g.w->N % kBN == 0 && g.epilogue != EPI_RESIDUAL &&
+                         g.epilogue != EPI_QKV && g.epilogue != EPI_GELU_MUL;
+    const bool pair = pair_ok && (g.mode == GEMM_PAIR || (g.mode == GEMM_AUTO && pair_tiles >= g.num_sms));
     // 128-wide tiles read each A tile twice as often; measured slower on every forward shape,
     // so they run only when asked for (or when N is a multiple of 128 but not of 256).
     const bool narrow = !q8 && !pair && !epi_is_geglu(g.epilogue) &&

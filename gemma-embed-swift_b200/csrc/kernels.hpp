@@ -112,9 +112,10 @@ bool encode_weight_maps(DevWeight& w, int bn);
 bool encode_activation_map(DevActivation& a);
 
 // Which fp16-path kernel a GEMM uses: single CTAs with 128 x 256 tiles, single CTAs with
-// 128 x 128 tiles, or CTA pairs (tcgen05.mma.cta_group::2, 256 x 256 tiles).  AUTO is single
-// CTAs with 128 x 256 tiles, the fastest of the three on the forward's shapes.  The Q8 path
-// always runs single CTAs with 128 x 256 tiles.
+// 128 x 128 tiles, or CTA pairs (tcgen05.mma.cta_group::2, 256 x 256 tiles, 128-deep K stages).
+// AUTO takes CTA pairs when their tiles fill at least two rounds of the SMs' pairs (and K is a
+// multiple of 128), else single CTAs with 128 x 256 tiles: the fastest on each forward shape.
+// The Q8 path always runs single CTAs with 128 x 256 tiles.
 // GEMM_SPLIT runs single-CTA 128 x 256 tiles as narrower pieces where that would shorten the
 // persistent schedule on paper (the last partial round, or every tile of a batch that leaves SMs
 // idle; see k_gemm).  Bit-identical to whole tiles, measured no faster on any forward shape

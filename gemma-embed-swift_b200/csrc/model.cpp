@@ -757,6 +757,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         g.aux = aux;
         g.ldaux = ldaux;
         g.use_q8 = q8;
+        if (m->flags & GE_LOAD_SINGLE_CTA_GEMM) g.mode = GEMM_SINGLE;
         g.err = d.err;
         g.num_sms = d.num_sms;
         return launch_gemm(g, ks);
@@ -783,6 +784,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         g.ldo = L.qkv.N;
         g.epilogue = EPI_QKV;
         g.use_q8 = q8;
+        if (m->flags & GE_LOAD_SINGLE_CTA_GEMM) g.mode = GEMM_SINGLE;
         g.err = d.err;
         g.num_sms = d.num_sms;
         g.positions = ws.positions;
@@ -805,6 +807,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         g.ldo = W.N;
         g.epilogue = EPI_RESIDUAL;
         g.use_q8 = q8;
+        if (m->flags & GE_LOAD_SINGLE_CTA_GEMM) g.mode = GEMM_SINGLE;
         g.err = d.err;
         g.num_sms = d.num_sms;
         g.x = ws.x;

@@ -81,6 +81,8 @@ typedef struct ge_load_opts {
                                      hidden/256 CTAs exchanging row sums through distributed shared memory) */
 #define GE_LOAD_FUSED_QKV 16u     /* run the per-head q/k/v norms and RoPE of head-dim-256 layers in the q/k/v
                                      projection's epilogue; attention reads q, k and v from its rows in place */
+#define GE_LOAD_SINGLE_CTA_GEMM 32u /* run every projection on single CTAs (128 x 256 tiles), never on CTA
+                                       pairs; results are bit-identical either way */
 
 /* EmbedOptions (EmbedOptions.swift:34-56) minus the task prefix, which ge_embed_texts takes
  * as a string (ge_task_prefix). */
