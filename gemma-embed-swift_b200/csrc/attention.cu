@@ -32,21 +32,27 @@ namespace ge {
 // from the K ring): those S rows are masked and never stored.  A key block's K arrives as two
 // 256-dim halves through the 2-slot K ring, so the next block's first half loads while the
 // second half's MMAs run.
-//   warp 0      TMA producer: per item the Q tile, once the previous item's last S has read
-//               the buffer, then K and V tiles of 64 keys into 2-slot rings that run on from
-//               item to item
-//   warp 1      tcgen05.mma issuer and tensor-memory owner: S_j = Q K_j^T (128 x 64, fp32 in
-//               TMEM, two buffers) and O += P_j V_j (128 x 256, fp32 in TMEM); an item's
-//               first PV waits until the previous item's O has been read out, so the next
-//               item's Q load and first S overlap the previous item's epilogue
+//   warp 0      TMA producer: per item the Q tile, once both S issuers have read the previous
+//               one, then K and V tiles of 64 keys into 2-slot rings that run on from item to
+//               item, K and V on independent cursors (each load as soon as its slot is free)
+//   warps 1, 10 S issuers (warp 1 also owns tensor memory): S_j = Q K_j^T (128 x 64, fp32 in
+//               TMEM, two buffers); head dim 256: warp 1 the even global key blocks and warp 10
+//               the odd ones, each through its own K-ring slot (one thread issues a tcgen05.mma
+//               about every 90 cycles, as long as a 128 x 64 x 16 product runs); head dim 512:
+//               warp 1 alone.  A buffer takes block j + 2 once every softmax thread holds block
+//               j's scores.
+//   warp 11     PV issuer: O += P_j V_j (128 x 256, fp32 in TMEM, P read from TMEM); an
+//               item's first PV waits until the previous item's O has been read out, so the next
+//               item's Q load and first S products overlap the previous item's epilogue
 //   warps 2-9   softmax, two threads per row (one per 32-key half of a block; warps w and
 //               w + 4 share a tensor-memory lane quarter): mask S_j, exchange the row's block
 //               maximum through shared memory, keep running maximum and partial sums, write
-//               their half of P_j (fp16, 128-byte swizzled) to shared memory, and rescale
-//               their half of O in tensor memory only when the row maximum grows by more than
-//               kRescale; until then every term of the row uses the same stale maximum, so the
-//               result is exact.  Then O / l for their half of the row.
-// Tensor memory: O in columns [0, 256), the S buffers in [256, 320) and [320, 384).
+//               their half of P_j (fp16 pairs) to tensor memory, and rescale their half of O in
+//               tensor memory only when the row maximum grows by more than kRescale; until then
+//               every term of the row uses the same stale maximum, so the result is exact.
+//               Then O / l for their half of the row, staged through shared memory.
+// Tensor memory: O in columns [0, 256), the S buffers in [256, 320) and [320, 384), the P
+// buffers in [384, 416) and [416, 448).
 constexpr int kTcQ = 128;
 constexpr int kTcKeys = 64;
 constexpr int kTcHd = 256;  // output dims per item (the head dim, or half of a 512-dim head) and K-ring slot width
@@ -65,7 +71,7 @@ constexpr int kTcThreads = 384;
 constexpr int kSWarpB = 10;  // the second S issuer
 constexpr int kPVWarp = 11;  // the PV issuer
 constexpr uint32_t kPollNs = 64;  // producer and issuer poll interval
-constexpr uint32_t kTmemO = 0, kTmemS = 256;
+constexpr uint32_t kTmemO = 0, kTmemS = 256, kTmemP = 384;
 
 struct TcAttnParams {
     const uint4* work;       // (sequence start, sequence length, first token, KV head), grouped by CTA
@@ -344,14 +350,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t pa = smem_u32(smem + kOffP + b * kPBytes);
                     const uint32_t va = smem_u32(smem + kOffV + b * kKVBytes);
 #pragma unroll
                     for (int kk = 0; kk < kTcKeys / 16; kk++) {
-                        const uint64_t ad = sw128_desc(pa + kk * 32, 16, 1024);
+                        // P_b's keys 16 kk .. 16 kk + 15 from tensor memory
+                        const uint32_t pa = tmem + kTmemP + uint32_t(b * (kTcKeys / 2) + kk * 8);
                         // V chunk of 64 dims = one [64 keys][128 B] box; 16 keys advance 2048 B.
                         const uint64_t bd = sw128_desc(va + kk * 2048, kKVBytes / 4, 1024);
-                        umma_f16(tmem + kTmemO, ad, bd, id_o, !(j == 0 && kk == 0));
+                        umma_f16_ta(tmem + kTmemO, pa, bd, id_o, !(j == 0 && kk == 0));
                     }
                     umma_commit(&v_empty[b]);
                     umma_commit(&pv_done[b]);
@@ -470,15 +476,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                 // completed (waited for after the exponentials, which do not need the buffer).
                 if (gb >= 2) wait_all(&pv_done[b], uint32_t(((gb - 2) >> 1) & 1));
                 if (!ok) continue;
-                uint8_t* prow = smem + kOffP + b * kPBytes + r * 128;
-#pragma unroll
-                for (int c = 0; c < 4; c++) {  // 4 chunks of 8 keys = 16 bytes each
-                    const int chunk = half * 4 + c;
-                    *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) * 16)) =
-                        make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-                }
+                // This half's 16 columns of P buffer b in tensor memory (the PV product's A).
+                tmem_st16(lane_base + kTmemP + uint32_t(b * (kTcKeys / 2) + half * 16), pk);
                 l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-                fence_proxy_async_smem();
+                tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(&p_full[b]);
             }
