@@ -555,11 +555,37 @@ int build_attention_work(const uint32_t* sl, int nseq, int kvh, int group, int h
                          int* ctas, int hd) {
     const int T = attention_tokens_per_item(group, hd);
     const int halves = hd == 512 ? 2 : 1;  // a 512-dim head's output dims in two items
+    // The item count alone answers the size query the forward makes before filling.
+    long count_items = 0;
+    for (int s = 0; s < nseq; s++) count_items += (long(sl[2 * s + 1]) + T - 1) / T * (kvh * halves);
+    const int n = int(count_items);
+    const int grid = std::max(1, std::min(n, max_ctas));
+    if (ctas) *ctas = n ? grid : 0;
+    if (n == 0) return 0;
+    const int words = 4 * n + grid + 1;
+    if (!out) return words;
+    // Built on every forward from the host, so the buffers are kept per thread.
     struct Item {
         uint32_t start, len, t0, kh;
         int cost;
     };
-    std::vector<Item> items;
+    struct Buffers {
+        std::vector<Item> items;
+        std::vector<int> order, owner, count, first;
+        std::vector<long> load;       // per CTA, the sum of its items' costs
+        std::vector<uint64_t> mask;   // per load value, the CTAs at that load
+    };
+    thread_local Buffers tls;
+    Buffers& B = tls;  // one thread-local lookup
+    auto& items = B.items;
+    auto& order = B.order;
+    auto& owner = B.owner;
+    auto& count = B.count;
+    auto& first = B.first;
+    auto& load = B.load;
+    auto& mask = B.mask;
+    items.clear();
+    int max_cost = 0;
     for (int s = 0; s < nseq; s++)
         for (uint32_t t0 = 0; t0 < sl[2 * s + 1]; t0 += uint32_t(T))
             for (int kh = 0; kh < kvh * halves; kh++) {
@@ -573,38 +599,53 @@ int build_attention_work(const uint32_t* sl, int nseq, int kvh, int group, int h
                 // An item costs its key blocks plus about two blocks of set-up and epilogue.
                 // KV head in the low 16 bits, output half of a 512-dim head in the high 16
                 const uint32_t tag = uint32_t(kh / halves) | (uint32_t(kh % halves) << 16);
-                items.push_back({sl[2 * s], sl[2 * s + 1], t0, tag, (ke - ks + kTcKeys - 1) / kTcKeys + 2});
+                const int cost = (ke - ks + kTcKeys - 1) / kTcKeys + 2;
+                max_cost = std::max(max_cost, cost);
+                items.push_back({sl[2 * s], sl[2 * s + 1], t0, tag, cost});
             }
-    const int n = int(items.size());
-    const int grid = std::max(1, std::min(n, max_ctas));
-    if (ctas) *ctas = n ? grid : 0;
-    if (n == 0) return 0;
-    const int words = 4 * n + grid + 1;
-    if (!out) return words;
-    std::stable_sort(items.begin(), items.end(), [](const Item& a, const Item& b) { return a.cost > b.cost; });
-    // Each item goes to the least-loaded CTA so far (lowest index on ties): deterministic.
-    std::vector<std::pair<long, int>> heap;
-    for (int c = 0; c < grid; c++) heap.push_back({0, c});
-    auto cmp = [](const std::pair<long, int>& a, const std::pair<long, int>& b) {
-        return a.first != b.first ? a.first > b.first : a.second > b.second;
-    };
-    std::make_heap(heap.begin(), heap.end(), cmp);
-    std::vector<int> owner(static_cast<size_t>(n)), count(static_cast<size_t>(grid), 0);
+    // Longest first, items of equal cost in the order they were made (a stable counting sort).
+    first.assign(size_t(max_cost) + 2, 0);
+    for (const Item& it : items) first[size_t(max_cost - it.cost) + 1]++;
+    for (size_t c = 1; c < first.size(); c++) first[c] += first[c - 1];
+    order.resize(size_t(n));
+    for (int i = 0; i < n; i++) order[size_t(first[size_t(max_cost - items[size_t(i)].cost)]++)] = i;
+    // Each item goes to the least-loaded CTA so far (lowest index on ties): deterministic.  The
+    // loads are small integers that only grow, so the CTAs sit in buckets by load, a bitmask of
+    // CTA indices each: the next CTA is the lowest bit of the lowest non-empty bucket.  No load
+    // exceeds the total cost / grid + the largest cost (a CTA is chosen only while it is the
+    // least loaded).
+    long total = 0;
+    for (const Item& it : items) total += it.cost;
+    const int mw = (grid + 63) / 64;  // mask words per bucket
+    const long nbuckets = total / grid + max_cost + 2;
+    mask.assign(size_t(nbuckets) * size_t(mw), 0ull);
+    for (int c = 0; c < grid; c++) mask[size_t(c >> 6)] |= 1ull << (c & 63);
+    load.assign(size_t(grid), 0);
+    owner.resize(size_t(n));
+    count.assign(size_t(grid), 0);
+    long lo = 0;  // the lowest bucket that may hold a CTA
     for (int i = 0; i < n; i++) {
-        std::pop_heap(heap.begin(), heap.end(), cmp);
-        auto& top = heap.back();
-        owner[size_t(i)] = top.second;
-        count[size_t(top.second)]++;
-        top.first += items[size_t(i)].cost;
-        std::push_heap(heap.begin(), heap.end(), cmp);
+        int c = -1;
+        while (c < 0) {
+            const uint64_t* m = &mask[size_t(lo) * size_t(mw)];
+            for (int q = 0; q < mw && c < 0; q++)
+                if (m[q]) c = q * 64 + __builtin_ctzll(m[q]);
+            if (c < 0) lo++;
+        }
+        const int cost = items[size_t(order[size_t(i)])].cost;
+        mask[size_t(lo) * size_t(mw) + size_t(c >> 6)] &= ~(1ull << (c & 63));
+        load[size_t(c)] += cost;
+        mask[size_t(load[size_t(c)]) * size_t(mw) + size_t(c >> 6)] |= 1ull << (c & 63);
+        owner[size_t(i)] = c;
+        count[size_t(c)]++;
     }
     uint32_t* off = out + 4 * size_t(n);
     off[0] = 0;
     for (int c = 0; c < grid; c++) off[c + 1] = off[c] + uint32_t(count[size_t(c)]);
-    std::vector<uint32_t> next(off, off + grid);
+    for (int c = 0; c < grid; c++) count[size_t(c)] = int(off[c]);  // next free slot of each CTA
     for (int i = 0; i < n; i++) {
-        const Item& it = items[size_t(i)];
-        uint32_t* w = out + 4 * size_t(next[size_t(owner[size_t(i)])]++);
+        const Item& it = items[size_t(order[size_t(i)])];
+        uint32_t* w = out + 4 * size_t(count[size_t(owner[size_t(i)])]++);
         w[0] = it.start;
         w[1] = it.len;
         w[2] = it.t0;
