@@ -4,17 +4,20 @@
 // Model/CPUReference.swift:117-174, scale 1).
 //
 // Persistent: one CTA per SM walks its list of work items, each item 128 query rows of one
-// head.  Roles (320 threads):
+// head.  Roles (352 threads):
 //   warp 0      TMA producer: the item's Q tile, then K and V tiles of 128 keys through
 //               3-stage rings that run on across items.
-//   warp 1      tcgen05.mma issuer: S_j = Q K_j^T (M 128, N 128, K 64) into one of two
-//               tensor-memory buffers, then O += P_{j-1} V_{j-1} (M 128, N 64, K 128) with P
-//               from shared memory.
+//   warp 1      S issuer: S_j = Q K_j^T (M 128, N 128, K 64) into one of two tensor-memory
+//               buffers; a buffer takes block j + 2 once every softmax thread has loaded block j.
+//   warp 10     PV issuer: O += P_j V_j (M 128, N 64, K 128) with P read from tensor memory.
+//               (One thread issues a tcgen05.mma about every 90 cycles whatever its N, so the
+//               eight PV products of a block, 32 tensor cycles each, get a thread of their own.)
 //   warps 2-9   softmax, two threads per query row (64 keys each): running maximum with a
 //               lazy rescale of O (only when the maximum grows by more than kRescaleRaw),
-//               P = 2^(s log2e - m log2e) in fp16 into a 128-byte-swizzled buffer, and at the end
-//               of an item O / l stored as fp16.
-// Tensor memory: S buffers in columns [0, 128) and [128, 256), O in [256, 320).
+//               P = 2^(s log2e - m log2e) in fp16 into tensor memory, and at the end of an item
+//               O / l stored as fp16.
+// Tensor memory: S buffers in columns [0, 128) and [128, 256), O in [256, 320), P buffers in
+// [320, 384) and [384, 448).
 // Every wait is bounded (mbar_wait); after an error the kernel drains its loads and returns.
 #include "kernels.hpp"
 #include "ptx.cuh"
@@ -30,13 +33,12 @@ constexpr float kRescaleRaw = 8.0f / kLog2e;
 constexpr int kTileBytes = kKeys * kHd * 2;       // 16 KB: [128 rows][64 dims] = [128][128 B]
 constexpr int kOffK = kTileBytes;                 // Q at 0
 constexpr int kOffV = kOffK + kStages * kTileBytes;
-constexpr int kOffP = kOffV + kStages * kTileBytes;
-constexpr int kPBytes = kQ * kKeys * 2;           // 32 KB: two [128 rows][64 keys] chunks
-constexpr int kOffRed = kOffP + 2 * kPBytes;      // [2 halves][128 rows] floats
+constexpr int kOffRed = kOffV + kStages * kTileBytes;  // [2 halves][128 rows] floats
 constexpr int kOffBar = kOffRed + 2 * kQ * 4;
 constexpr int kSmem = kOffBar + 256 + 1024;
-constexpr int kThreads = 320;
-constexpr uint32_t kTmemS = 0, kTmemO = 256;
+constexpr int kThreads = 352;
+constexpr int kPVWarp = 10;
+constexpr uint32_t kTmemS = 0, kTmemO = 256, kTmemP = 320;
 
 struct Params {
     const uint4* work;       // (sequence start, sequence length, first query, head), grouped by CTA
@@ -68,7 +70,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention64(const __grid_consta
     uint64_t* p_full = bars + 16;  // [2]
     uint64_t* pv_done = bars + 18; // [2]
     uint64_t* o_empty = bars + 20;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
+    uint64_t* s_free = bars + 21;  // [2] S buffer loaded by every softmax thread
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 23);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int it0 = int(p.offset[blockIdx.x]), it1 = int(p.offset[blockIdx.x + 1]);
@@ -88,6 +91,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention64(const __grid_consta
             mbar_init(&pv_done[i], 1);
         }
         mbar_init(o_empty, 256);
+        for (int i = 0; i < 2; i++) mbar_init(&s_free[i], 256);
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
@@ -149,32 +153,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention64(const __grid_consta
             }
         }
     } else if (warp == 1) {
-        // ---------------------------------------------------------- MMA issuer
+        // ---------------------------------------------------------- S issuer
         if (lane == 0) {
-            const uint32_t id_s = idesc_f16(kQ, kKeys);          // K-major Q and K
-            const uint32_t id_o = idesc_f16(kQ, kHd, 0, 1);      // K-major P, MN-major V
+            const uint32_t id_s = idesc_f16(kQ, kKeys);  // K-major Q and K
             const uint32_t q_addr = smem_u32(smem);
             bool ok = true;
-            auto issue_pv = [&](int g, bool first, int li) -> bool {
-                const int b = g & 1;
-                const uint32_t ph = uint32_t((g >> 1) & 1);
-                const int s = g % kStages;
-                const uint32_t kph = uint32_t((g / kStages) & 1);
-                if (first && li > 0 && !mbar_wait(o_empty, uint32_t((li - 1) & 1), p.err)) return false;
-                if (!mbar_wait(&p_full[b], ph, p.err) || !mbar_wait(&v_full[s], kph, p.err)) return false;
-                tc_fence_after();
-                const uint32_t pa = smem_u32(smem + kOffP + b * kPBytes);
-                const uint32_t va = smem_u32(smem + kOffV + s * kTileBytes);
-#pragma unroll
-                for (int kk = 0; kk < kKeys / 16; kk++) {
-                    const uint64_t ad = sw128_desc(pa + (kk >> 2) * (kPBytes / 2) + (kk & 3) * 32, 16, 1024);
-                    const uint64_t bd = sw128_desc(va + kk * 2048, kTileBytes, 1024);  // 16 keys = 2048 B
-                    umma_f16(tmem + kTmemO, ad, bd, id_o, !(first && kk == 0));
-                }
-                umma_commit(&v_empty[s]);
-                umma_commit(&pv_done[b]);
-                return true;
-            };
             int gb = 0;
             for (int it = it0, li = 0; it < it1 && ok; it++, li++) {
                 const uint4 w = p.work[it];
@@ -184,7 +167,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention64(const __grid_consta
                 for (int j = 0; j < nblk; j++, gb++) {
                     const int b = gb & 1;
                     const int s = gb % kStages;
-                    if (!mbar_wait(&k_full[s], uint32_t((gb / kStages) & 1), p.err)) {
+                    // S buffer b is free once every softmax thread holds block gb - 2's scores.
+                    if ((gb >= 2 && !mbar_wait(&s_free[b], uint32_t(((gb - 2) >> 1) & 1), p.err)) ||
+                        !mbar_wait(&k_full[s], uint32_t((gb / kStages) & 1), p.err)) {
                         ok = false;
                         break;
                     }
@@ -199,12 +184,39 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention64(const __grid_consta
                     umma_commit(&k_empty[s]);
                     umma_commit(&s_full[b]);
                     if (j == nblk - 1) umma_commit(q_empty);  // every S of the item has read Q
-                    if (j > 0 && !issue_pv(gb - 1, j == 1, li)) {
+                }
+            }
+        }
+    } else if (warp == kPVWarp) {
+        // ---------------------------------------------------------- PV issuer
+        if (lane == 0) {
+            const uint32_t id_o = idesc_f16(kQ, kHd, 0, 1);  // P from tensor memory, MN-major V
+            bool ok = true;
+            int gb = 0;
+            for (int it = it0, li = 0; it < it1 && ok; it++, li++) {
+                const uint4 w = p.work[it];
+                const int nblk = (int(w.y) + kKeys - 1) / kKeys;
+                for (int j = 0; j < nblk; j++, gb++) {
+                    const int b = gb & 1;
+                    const int s = gb % kStages;
+                    // An item's first PV overwrites O once the previous item's O has been read.
+                    if ((j == 0 && li > 0 && !mbar_wait(o_empty, uint32_t((li - 1) & 1), p.err)) ||
+                        !mbar_wait(&p_full[b], uint32_t((gb >> 1) & 1), p.err) ||
+                        !mbar_wait(&v_full[s], uint32_t((gb / kStages) & 1), p.err)) {
                         ok = false;
                         break;
                     }
+                    tc_fence_after();
+                    const uint32_t va = smem_u32(smem + kOffV + s * kTileBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kKeys / 16; kk++) {
+                        const uint64_t bd = sw128_desc(va + kk * 2048, kTileBytes, 1024);  // 16 keys = 2048 B
+                        umma_f16_ta(tmem + kTmemO, tmem + kTmemP + uint32_t(b * (kKeys / 2) + kk * 8), bd, id_o,
+                                    !(j == 0 && kk == 0));
+                    }
+                    umma_commit(&v_empty[s]);
+                    umma_commit(&pv_done[b]);
                 }
-                if (ok && !issue_pv(gb - 1, nblk == 1, li)) ok = false;
             }
         }
     } else {
@@ -241,6 +253,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention64(const __grid_consta
                     tmem_ld32(lane_base + kTmemS + b * kKeys + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
                     tmem_ld32(lane_base + kTmemS + b * kKeys + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
                     tmem_wait_ld();
+                    tc_fence_before();
+                    mbar_arrive(&s_free[b]);  // the S buffer may take block gb + 2
                     if (kb + 64 > len) {
 #pragma unroll
                         for (int i = 0; i < 64; i++)
@@ -282,24 +296,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_attention64(const __grid_consta
                 // P goes to buffer b once the PV two blocks back, which read that buffer, is done.
                 if (gb >= 2) wait_all(&pv_done[b], uint32_t(((gb - 2) >> 1) & 1));
                 if (!ok) continue;
-                uint8_t* prow = smem + kOffP + b * kPBytes + half * (kPBytes / 2) + r * 128;
                 float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
                 const float nmu = m_used == -INFINITY ? 0.f : -m_used * kLog2e;
+                uint32_t pk[32];  // this half's 64 probabilities as fp16 pairs
 #pragma unroll
-                for (int c = 0; c < 8; c++) {  // 8 chunks of 8 keys = 16 bytes each
-                    uint32_t wv[4];
+                for (int c = 0; c < 8; c++) {  // 8 groups of 8 keys
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
                         const float p0 = ex2_approx(fmaf(__uint_as_float(sr[c * 8 + 2 * e]), kLog2e, nmu));
                         const float p1 = ex2_approx(fmaf(__uint_as_float(sr[c * 8 + 2 * e + 1]), kLog2e, nmu));
                         ps[2 * e] += p0;
                         ps[2 * e + 1] += p1;
-                        wv[e] = pack_half2(p0, p1);
+                        pk[c * 4 + e] = pack_half2(p0, p1);
                     }
-                    *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) * 16)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
                 }
+                // This half's 32 columns of P buffer b in tensor memory (the PV product's A).
+                tmem_st32(lane_base + kTmemP + uint32_t(b * (kKeys / 2) + half * 32), pk);
                 l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-                fence_proxy_async_smem();
+                tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(&p_full[b]);
             }
