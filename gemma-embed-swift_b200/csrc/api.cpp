@@ -95,10 +95,13 @@ void run_per_device(ge_model* m, int n, const std::function<void(int)>& fn) {
     m->workers->run(n, fn);
 }
 
+// The packed forward over every device of the model.  With fin_dims > 0 each device also runs
+// EmbeddingModel.finish (the first fin_dims values, L2-normalised when fin_norm) and `out`
+// receives [nseq][fin_dims] finished rows; otherwise [nseq][out_dim] pooled rows.
 int forward_packed_locked(ge_model* m, const int32_t* tokens, const int32_t* positions, int32_t ntok, const ge_seq* seqs,
-                          int32_t nseq, float* out) {
+                          int32_t nseq, float* out, int fin_dims = 0, bool fin_norm = false) {
     const int ndev = int(m->devs.size());
-    const int od = m->cfg.out_dim;
+    const int od = fin_dims > 0 ? fin_dims : m->cfg.out_dim;  // width of an output row
     if (ndev == 1 || nseq <= 1) {
         ge::ForwardArgs a;
         a.tokens = tokens;
@@ -107,6 +110,8 @@ int forward_packed_locked(ge_model* m, const int32_t* tokens, const int32_t* pos
         a.seqs = seqs;
         a.nseq = nseq;
         a.out = out;
+        a.finish_dims = fin_dims;
+        a.finish_normalise = fin_norm;
         return ge::run_forward(m, m->devs[0], a);
     }
     // Multi-GPU: each device packs its own share of the sequences, runs it on its own host
@@ -132,6 +137,8 @@ int forward_packed_locked(ge_model* m, const int32_t* tokens, const int32_t* pos
             a.seqs = sq.data();
             a.nseq = int(sq.size());
             a.out = o.data();
+            a.finish_dims = fin_dims;
+            a.finish_normalise = fin_norm;
             a.error = &msgs[dv];  // each device thread reports into its own string
             rc[dv] = ge::run_forward(m, m->devs[dv], a);
             if (rc[dv] == GE_OK)
@@ -176,7 +183,6 @@ void truncate_keeping_eos(ge_model* m, const ge_embed_opts& o, std::vector<int32
 // the prepared lengths, one packed forward each, then finish into the caller's rows.
 int embed_prepared(ge_model* m, const std::vector<std::vector<int32_t>>& prepared, const ge_embed_opts& o, float* out,
                    ge_progress_fn progress, void* user) {
-    const ge::Config& c = m->cfg;
     const int32_t count = int32_t(prepared.size());
     std::vector<int64_t> costs(static_cast<size_t>(count));
     for (int32_t i = 0; i < count; i++) costs[size_t(i)] = int64_t(prepared[size_t(i)].size());
@@ -186,7 +192,6 @@ int embed_prepared(ge_model* m, const std::vector<std::vector<int32_t>>& prepare
     ge_batches(costs.data(), count, 1, o.batch_size, &budget, ranges.data(), &nr);
     int32_t done_texts = 0;
     int64_t done_tokens = 0;
-    std::vector<float> pooled;
     std::vector<int32_t> toks;
     std::vector<ge_seq> seqs;
     for (int32_t r = 0; r < nr; r++) {
@@ -197,13 +202,18 @@ int embed_prepared(ge_model* m, const std::vector<std::vector<int32_t>>& prepare
             seqs.push_back({uint32_t(toks.size()), uint32_t(prepared[size_t(i)].size())});
             toks.insert(toks.end(), prepared[size_t(i)].begin(), prepared[size_t(i)].end());
         }
-        pooled.resize(size_t(e - b) * size_t(c.out_dim));
-        int rc = ge_forward_packed(m, toks.data(), nullptr, int32_t(toks.size()), seqs.data(), int32_t(seqs.size()),
-                                   pooled.data());
+        // finish (EmbeddingModel.swift:260-267) runs on the device, after the head: only the
+        // rows' first o.dimensions values come back, finished, straight into the caller's rows.
+        int rc;
+        {
+            std::lock_guard<std::mutex> g(m->mu);
+            rc = check_batch(m, toks.data(), nullptr, int32_t(toks.size()), seqs.data(), int32_t(seqs.size()));
+            if (rc == GE_OK)
+                rc = forward_packed_locked(m, toks.data(), nullptr, int32_t(toks.size()), seqs.data(),
+                                           int32_t(seqs.size()), out + size_t(b) * size_t(o.dimensions), o.dimensions,
+                                           o.normalise != 0);
+        }
         if (rc) return rc;
-        for (int32_t i = b; i < e; i++)
-            ge_finish(pooled.data() + size_t(i - b) * size_t(c.out_dim), c.out_dim, o.dimensions, o.normalise,
-                      out + size_t(i) * size_t(o.dimensions));
         done_texts += e - b;
         done_tokens += int64_t(toks.size());
         if (progress && progress(done_texts, count, done_tokens, user) != 0 && r + 1 < nr)

@@ -743,6 +743,36 @@ cudaError_t launch_mean_pool(const float* y, int width, const uint32_t* seqs, in
     return cudaGetLastError();
 }
 
+// EmbeddingModel.finish (EmbeddingModel.swift:260-267) on the device: the first `dims` values of
+// each pooled row, divided by their L2 norm when `normalise` (and the norm is positive).  One
+// thread per row adds the squares in order with separately rounded products and sums, the same
+// operations as the host's ge_finish, so the rows match it bit for bit.
+__global__ void k_finish_rows(const float* __restrict__ in, int nseq, int width, int dims, int normalise,
+                              float* __restrict__ out) {
+    pdl_wait();
+    const int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= nseq) return;
+    const float* v = in + long(s) * width;
+    float* o = out + long(s) * dims;
+    const int k = min(dims, width);
+    float norm = 0.f;
+    if (normalise) {
+        float acc = 0.f;
+        for (int i = 0; i < k; i++) acc = __fadd_rn(acc, __fmul_rn(v[i], v[i]));
+        norm = sqrtf(acc);
+    }
+    for (int i = 0; i < k; i++) o[i] = norm > 0.f ? __fdiv_rn(v[i], norm) : v[i];
+}
+
+cudaError_t launch_finish_rows(const float* in, int nseq, int width, int dims, int normalise, float* out,
+                               cudaStream_t stream) {
+    if (nseq <= 0) return cudaSuccess;
+    if (dims <= 0 || dims > width) return cudaErrorInvalidValue;
+    CK_LAUNCH(launch_kernel(k_finish_rows, dim3((nseq + 63) / 64), dim3(64), 0, stream, 1, in, nseq, width, dims,
+                            normalise, out));
+    return cudaGetLastError();
+}
+
 // positions[start + i] = i for every sequence (PackedBatch.append, MetalForward.swift:17-21).
 __global__ void k_positions(const uint32_t* __restrict__ seqs, int32_t* __restrict__ positions) {
     pdl_wait();

@@ -230,6 +230,10 @@ cudaError_t launch_dense_f32(const float* in, int nrows, const float* w, int N, 
                              cudaStream_t stream);
 
 // positions[start + i] = i over the sequences (start, length) pairs.
+// The first `dims` of each of nseq rows of `width` values, L2-normalised when `normalise`
+// (EmbeddingModel.finish), into out [nseq][dims]; bit-identical to the host's ge_finish.
+cudaError_t launch_finish_rows(const float* in, int nseq, int width, int dims, int normalise, float* out,
+                               cudaStream_t stream);
 cudaError_t launch_positions(const uint32_t* seqs, int nseq, int32_t* positions, cudaStream_t stream);
 
 // ------------------------------------------------------------------ vision tower

@@ -131,7 +131,7 @@ bool read_config(const GgufFile& f, Config& c, LoadError& e) {
 
 static void free_workspace(Workspace& ws) {
     for (void* p : {(void*)ws.tokens, (void*)ws.positions, (void*)ws.seqs, (void*)ws.work, (void*)ws.x, (void*)ws.qkv16,
-                    (void*)ws.o16, (void*)ws.d16, (void*)ws.y, (void*)ws.ple, (void*)ws.pooled, (void*)ws.chunk_base, (void*)ws.pool_partial, (void*)ws.mid, (void*)ws.head_part, (void*)ws.out,
+                    (void*)ws.o16, (void*)ws.d16, (void*)ws.y, (void*)ws.ple, (void*)ws.pooled, (void*)ws.fin, (void*)ws.chunk_base, (void*)ws.pool_partial, (void*)ws.mid, (void*)ws.head_part, (void*)ws.out,
                     (void*)ws.h, (void*)ws.x16, (void*)ws.q, (void*)ws.k, (void*)ws.v, (void*)ws.attn, (void*)ws.act,
                     (void*)ws.g})
         if (p) cudaFree(p);
@@ -195,6 +195,7 @@ static cudaError_t ensure_workspace(const Config& c, Device& d, int rows, int se
         chk(A(&ws.g, r * size_t(c.per_layer)));
     }
     chk(A(&ws.pooled, size_t(S) * d_));
+    chk(A(&ws.fin, size_t(S) * size_t(c.out_dim)));
     chk(A(&ws.chunk_base, size_t(S)));
     chk(A(&ws.pool_partial, (r / kPoolChunkRows + size_t(S)) * d_));
     chk(H(&ws.h_chunk_base, size_t(S)));
@@ -1079,6 +1080,13 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
                      [&] { return head(ws.pooled, d.output, c.out_dim, D, ws.out); }, head_launches(c.out_dim, D)),
                    "output projection");
             }
+            if (a.finish_dims > 0)
+                CK(K("finish", 0, double(nseq) * (c.out_dim + a.finish_dims) * 4,
+                     [&] {
+                         return launch_finish_rows(ws.out, nseq, c.out_dim, a.finish_dims, a.finish_normalise ? 1 : 0,
+                                                   ws.fin, ks);
+                     }),
+                   "finish");
         }
         return GE_OK;
     };
@@ -1095,6 +1103,7 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     for (int k = 0; k < 8; k++) gk.sched[k] = sched[k];
     gk.tokens = reinterpret_cast<uintptr_t>(tokens);
     gk.vectors = reinterpret_cast<uintptr_t>(a.vectors);
+    gk.finish = a.trace_layer < -1 && a.finish_dims > 0 ? 2 * a.finish_dims + (a.finish_normalise ? 1 : 0) : 0;
     GraphEntry* ge_ = use_graph ? find_graph(d, gk) : nullptr;
     if (use_graph && !ge_ && !seen_before(d, gk)) use_graph = false;
     if (ge_) {
@@ -1124,8 +1133,9 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
         const int rc = launch_all();
         if (rc != GE_OK) return rc;
     }
-    const float* result = a.trace_layer >= 0 ? ws.x : a.trace_layer == -1 ? ws.y : ws.out;
-    const int width = a.trace_layer >= -1 ? D : c.out_dim;
+    const bool finished = a.trace_layer < -1 && a.finish_dims > 0;
+    const float* result = a.trace_layer >= 0 ? ws.x : a.trace_layer == -1 ? ws.y : finished ? ws.fin : ws.out;
+    const int width = a.trace_layer >= -1 ? D : finished ? a.finish_dims : c.out_dim;
     const size_t out_elems = a.trace_layer >= -1 ? size_t(ntok) * D : size_t(nseq) * width;
     float* host_out = a.trace_layer >= -1 ? a.trace_out : a.out;
     m->launches += launches;

@@ -60,6 +60,7 @@ struct Workspace {
     __half* o16 = nullptr;  // fp16 output of the o (and, with per-layer inputs, down and per-layer) projections
     __half* d16 = nullptr;  // fp16 output of the down projection, beside o16 until the FFN residual
     float *pooled = nullptr, *mid = nullptr, *out = nullptr;
+    float* fin = nullptr;  // finished rows [seqs][dims] (ForwardArgs::finish_dims)
     float* head_part = nullptr;  // the dense head's per-K-chunk partial sums [chunks][seqs][N]
     __half *qkv16 = nullptr;  // fused q|k|v projection output
     __half *h = nullptr, *x16 = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr, *act = nullptr,
@@ -84,9 +85,10 @@ struct GraphKey {
     int sched[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     uintptr_t tokens = 0;         // the token buffer the embedding kernel reads
     uintptr_t vectors = 0;        // and the vector rows it copies (image or audio rows), if any
+    int finish = 0;               // 2 * finish_dims + normalise, 0 without the device finish
     bool operator==(const GraphKey& o) const {
         if (rows != o.rows || ntok != o.ntok || nseq != o.nseq || pool_chunks != o.pool_chunks || tokens != o.tokens ||
-            vectors != o.vectors)
+            vectors != o.vectors || finish != o.finish)
             return false;
         for (int k = 0; k < 8; k++)
             if (sched[k] != o.sched[k]) return false;
@@ -235,6 +237,10 @@ struct ForwardArgs {
     float* out = nullptr;
     bool out_on_device = false;
     cudaStream_t stream = nullptr;  // stream for device-resident calls; nullptr uses the device's own
+    // > 0: EmbeddingModel.finish on the device (the first finish_dims of each pooled row,
+    // L2-normalised when finish_normalise); out then receives [nseq][finish_dims]
+    int finish_dims = 0;
+    bool finish_normalise = false;
     int trace_layer = -2;           // >= -1: copy that layer's hidden state into trace_out instead
     float* trace_out = nullptr;
     std::string* error = nullptr;   // where failures are reported; nullptr: the model's last_error

@@ -41,6 +41,21 @@ def test_tiny_forward_matches_oracle(tiny, synth):
         assert c >= COSINE_MIN, (arch, len(s), c)
 
 
+@pytest.mark.parametrize("dims,normalise", [(768, True), (256, True), (128, False)])
+def test_device_finish_equals_host_finish(tiny, ge, synth, dims, normalise):
+    """EmbeddingModel.embed finishes on the device (Matryoshka prefix, then L2) and copies back
+    only the finished rows; they equal the host's ge_finish of the raw pooled rows bit for bit,
+    in one batch and in several (batch_size 2)."""
+    arch, model, ref = tiny
+    seqs = synth.random_sequences([1, 7, 64, 300, 700], seed=7, vocab=4096)
+    raw = model.embed_tokens(seqs)
+    want = np.stack([model.finish(v, dims, normalise) for v in raw])
+    for batch_size in (None, 2):
+        opts = ge.EmbedOptions(dimensions=dims, normalise=normalise, batch_size=batch_size)
+        got = np.stack([e.vector for e in model.embed(seqs, opts)])
+        assert got.tobytes() == want.tobytes(), (arch, dims, normalise, batch_size)
+
+
 def test_tiny_per_layer_hidden_states(tiny, synth):
     arch, model, ref = tiny
     toks = synth.random_sequences([600], seed=9, vocab=4096)[0]
