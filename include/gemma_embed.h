@@ -194,8 +194,8 @@ GE_API int ge_profile(ge_model* model, const int32_t* tokens, int32_t ntok, cons
 
 /* EmbeddingModel.embed over pre-tokenised texts (EmbeddingModel.swift:145-175 without the
  * tokenizer): truncation to max_tokens keeping EOS (189-196), batching by count or token
- * budget (200-215), one forward per batch, then the Matryoshka prefix and L2 (260-267).
- * `out` receives count * dimensions floats; `token_counts` and `truncated` (count entries
+ * budget (200-215), one forward per batch, then the Matryoshka prefix and L2 (260-267) on the
+ * device, with the arithmetic of ge_finish (the same bits).  `out` receives count * dimensions floats; `token_counts` and `truncated` (count entries
  * each, may be NULL) receive Embedding.tokenCount and Embedding.truncated. */
 GE_API int ge_embed_tokens(ge_model* model, const int32_t* const* texts, const int32_t* lengths, int32_t count,
                            const ge_embed_opts* opts, float* out, int32_t* token_counts, int32_t* truncated,
