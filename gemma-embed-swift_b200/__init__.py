@@ -637,12 +637,19 @@ class EmbeddingModel:
                                     ctypes.byref(o), _ptr(out, ctypes.c_float), _ptr(counts, ctypes.c_int32),
                                     _ptr(trunc, ctypes.c_int32), cb, None), self._h)
         else:
-            ptrs = (_lib.i32p * n)(*[_ptr(s, ctypes.c_int32) for s in data])
-            lens = np.array([len(s) for s in data], dtype=np.int32)
-            _check(L.ge_embed_tokens(self._h, ptrs, _ptr(lens, ctypes.c_int32), n, ctypes.byref(o),
+            # The texts' ids in one buffer and the per-text pointers computed from their offsets:
+            # one ctypes conversion per call instead of one per text (about 2.5 us each).
+            lens = np.fromiter((len(s) for s in data), dtype=np.int32, count=n)
+            flat = np.concatenate(data) if n > 1 else data[0]
+            starts = np.zeros(n, dtype=np.int64)
+            np.cumsum(lens[:-1], out=starts[1:])
+            addrs = (flat.ctypes.data + 4 * starts).astype(np.uintp)
+            _check(L.ge_embed_tokens(self._h, addrs.ctypes.data_as(ctypes.POINTER(_lib.i32p)),
+                                     _ptr(lens, ctypes.c_int32), n, ctypes.byref(o),
                                      _ptr(out, ctypes.c_float), _ptr(counts, ctypes.c_int32),
                                      _ptr(trunc, ctypes.c_int32), cb, None), self._h)
-        res = [Embedding(out[i].copy(), int(counts[i]), bool(trunc[i])) for i in range(n)]
+        # Each vector is its own row of `out` (rows are disjoint views, not copies).
+        res = [Embedding(v, c, bool(t)) for v, c, t in zip(out, counts.tolist(), trunc.tolist())]
         return res[0] if single else res
 
     def embed_images(self, images, options: Optional[ImageEmbedOptions] = None,

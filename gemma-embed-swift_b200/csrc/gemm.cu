@@ -1106,10 +1106,11 @@ cudaError_t launch_gemm(const GemmLaunch& g, cudaStream_t stream) {
     // product, but below two rounds of pair tiles single CTAs spread the work over more SMs.
     const int pair_tiles = ((g.m_rows + 2 * BM - 1) / (2 * BM)) * (g.w->N / kBN);
     // The last pair tile's second CTA may lie wholly past m_rows (loads there read zeros and its
-    // stores are clipped), so epilogues that read per-row inputs (GELU_MUL's aux, QKV's
-    // positions) and the residual clusters stay on single CTAs.
+    // stores are clipped), so an epilogue that reads per-row inputs for every row (GELU_MUL's
+    // aux) and the residual clusters stay on single CTAs.  QKV reads positions only for rows
+    // below ntok <= m_rows.
     const bool pair_ok = !q8 && g.w->K % (2 * BK) == 0 && g.w->N % kBN == 0 && g.epilogue != EPI_RESIDUAL &&
-                         g.epilogue != EPI_QKV && g.epilogue != EPI_GELU_MUL;
+                         g.epilogue != EPI_GELU_MUL;
     const bool pair = pair_ok && (g.mode == GEMM_PAIR || (g.mode == GEMM_AUTO && pair_tiles >= g.num_sms));
     // 128-wide tiles read each A tile twice as often; measured slower on every forward shape,
     // so they run only when asked for (or when N is a multiple of 128 but not of 256).

@@ -181,16 +181,19 @@ def test_launch_options_do_not_change_results(ge, synth, cuda_device, arch, use_
             assert on.embed_tokens(seqs).tobytes() == off.embed_tokens(seqs).tobytes()
 
 
+@pytest.mark.parametrize("fused", [{}, dict(fused_qkv=True)], ids=["plain", "fused_qkv"])
 @pytest.mark.parametrize("arch", ["gemma-embedding", "gemma-embedding2"])
-def test_cta_pair_gemms_match_single_ctas(ge, synth, cuda_device, arch):
+def test_cta_pair_gemms_match_single_ctas(ge, synth, cuda_device, arch, fused):
     """Batches whose 256 x 256 tiles fill two rounds of SM pairs run their projections on CTA
     pairs with 128-deep K stages; GE_LOAD_SINGLE_CTA_GEMM keeps 128 x 256 tiles on single CTAs.
     Both accumulate every output over the same 16-deep K steps, so the vectors agree bit for
     bit, at a size that takes the pair kernel for every projection (13,312 rows) and at one that
-    takes it for some projections only."""
+    takes it for some projections only; also with the q/k/v norms and RoPE in the projection's
+    epilogue (GE_LOAD_FUSED_QKV), whose per-row position reads stop at the batch's tokens."""
     path = synth.model_path(arch, seed=1, layers=6, vocab=4096)
-    with ge.EmbeddingModel.load(path, ge.LoadOptions(batch_token_budget=16384)) as pairs, \
-            ge.EmbeddingModel.load(path, ge.LoadOptions(batch_token_budget=16384, cta_pair_gemm=False)) as single:
+    with ge.EmbeddingModel.load(path, ge.LoadOptions(batch_token_budget=16384, **fused)) as pairs, \
+            ge.EmbeddingModel.load(path, ge.LoadOptions(batch_token_budget=16384, cta_pair_gemm=False,
+                                                        **fused)) as single:
         for seed, lens in ((71, [512] * 26), (72, [400, 33, 1000, 2000, 7, 511, 1500])):
             seqs = synth.random_sequences(lens, seed=seed, vocab=4096)
             assert pairs.embed_tokens(seqs).tobytes() == single.embed_tokens(seqs).tobytes()
