@@ -23,6 +23,9 @@ batch and for config 3 (16 x 2048 + 4 x 8192 tokens), each with its own roofline
 times one config-2 batch on all N GPUs through the library's own dispatcher (rank 0 loads the
 model on devices 0..N-1 and EmbeddingModel.embed shards the batch's sequences over them, packs
 each share, and gathers the vectors on the host) while the other ranks wait: strong scaling.
+`roofline` is the forward's largest kernel class against its peak; `step_roofline` is the whole
+timed region's algorithmic FLOPs (every GEMM and attention FLOP of the forward) against the
+sustained tensor peak.
 `--impl reference` times the CPU oracle (the restated CPUReference.forward, the only
 runnable form of the reference's path here) on the host cores.
 
@@ -286,6 +289,7 @@ def main():
         traffic = NCU_DRAM_BYTES_CONFIG2["bytes"].get(roofline["kernel"]) if a.config == 2 and a.arch == "gemma-embedding" else None
         roofline["traffic"] = traffic
         roofline["traffic_source"] = NCU_DRAM_BYTES_CONFIG2["source"] if traffic else None
+    step_roof = step_roofline(prof, pk, a.steps, world, ms_max) if rank == 0 else None
 
     full = a.legs == "all"
     # ---- end to end through the public API with host buffers: EmbeddingModel.embed on the
@@ -429,8 +433,8 @@ def main():
                 "e2e_text": e2e_text, "e2e_stream": e2e_stream, "strong": strong, "workloads": workloads,
                 "q8_gemm": q8, "gemm_schedules": gemm_paths,
                 "tokenizer": tok_stats,
-                "gpu_launches": int(launches), "clocks": clock_info, "roofline": roofline, "cpu_baseline": cpu,
-                "latency_ms_p50": pct(step_ms, 50), "latency_ms_p99": pct(step_ms, 99),
+                "gpu_launches": int(launches), "clocks": clock_info, "roofline": roofline, "step_roofline": step_roof,
+                "cpu_baseline": cpu, "latency_ms_p50": pct(step_ms, 50), "latency_ms_p99": pct(step_ms, 99),
                 "kernels": [{k: (round(v, 5) if isinstance(v, float) else v) for k, v in p.items()} for p in prof]}
         print(json.dumps(line), flush=True)
     model.close()
@@ -453,6 +457,19 @@ NCU_DRAM_BYTES_CONFIG2 = {
 
 
 BATCH_BUDGET = 65536
+
+
+def step_roofline(prof, pk, steps, world, ms):
+    """The whole timed region against the tensor peak: algorithmic FLOPs of rank 0's forward (every
+    GEMM's 2.N.K per row and the attention's 4.H.hd per visible query-key pair, as ge_profile
+    counts them) times the forwards of all ranks, over the max-over-ranks time, against the
+    per-GPU peak times the ranks.  A step runs seconds of back-to-back GEMMs under the power cap,
+    so the sustained peak applies."""
+    flops = sum(p["flops_per_launch"] * p["launches_per_forward"] for p in prof)
+    ach = flops * steps * world / (ms / 1000.0) / 1e12
+    peak = pk["bf16_tflops_sustained"] * world
+    return {"flop_per_forward": flops, "achieved": ach, "unit": "TFLOP/s", "peak": peak,
+            "peak_kind": "sustained bf16", "frac": ach / peak, "peak_source": pk["source"]}
 
 
 def top_roofline(prof, pk):
