@@ -912,32 +912,34 @@ __global__ void __launch_bounds__(256) k_dense_head_part(const float* __restrict
     const bool row_live = r0 + lr < nrows;
     const float* xin = in + long(r0 + lr) * K + k0 + lk;
     const float* win = w + long(n0 + lr) * K + k0 + lk;
-    // The next step's inputs and weights are loaded into registers while this step computes.
-    float4 xa = make_float4(0.f, 0.f, 0.f, 0.f), xb = xa;
-    if (row_live) {
-        xa = *reinterpret_cast<const float4*>(xin);
-        xb = *reinterpret_cast<const float4*>(xin + 4);
-    }
-    float4 wa = *reinterpret_cast<const float4*>(win);
-    float4 wb = *reinterpret_cast<const float4*>(win + 4);
-    for (int kk = 0; kk < kHeadChunk; kk += kHeadStep) {
+    // Loads run kPre steps ahead of the products (a ring of register sets, one per step in
+    // flight), so each thread has up to 3 x 64 bytes outstanding while it computes.
+    constexpr int kSteps = kHeadChunk / kHeadStep, kPre = 3;
+    float4 ring[kPre][4];
+    auto load = [&](float4 (&r)[4], int kk) {
+        r[0] = r[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row_live) {
+            r[0] = *reinterpret_cast<const float4*>(xin + kk);
+            r[1] = *reinterpret_cast<const float4*>(xin + kk + 4);
+        }
+        r[2] = *reinterpret_cast<const float4*>(win + kk);
+        r[3] = *reinterpret_cast<const float4*>(win + kk + 4);
+    };
+#pragma unroll
+    for (int i = 0; i < kPre; i++) load(ring[i], i * kHeadStep);
+#pragma unroll
+    for (int st = 0; st < kSteps; st++) {
+        float4(&r)[4] = ring[st % kPre];
         __syncthreads();
-        const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-        const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+        const float xv[8] = {r[0].x, r[0].y, r[0].z, r[0].w, r[1].x, r[1].y, r[1].z, r[1].w};
+        const float wv[8] = {r[2].x, r[2].y, r[2].z, r[2].w, r[3].x, r[3].y, r[3].z, r[3].w};
 #pragma unroll
         for (int j = 0; j < 8; j++) {
             reinterpret_cast<float*>(&xs[lk + j][lr >> 2])[lr & 3] = xv[j];
             reinterpret_cast<float*>(&ws[lk + j][lr >> 2])[lr & 3] = wv[j];
         }
         __syncthreads();
-        if (kk + kHeadStep < kHeadChunk) {
-            if (row_live) {
-                xa = *reinterpret_cast<const float4*>(xin + kk + kHeadStep);
-                xb = *reinterpret_cast<const float4*>(xin + kk + kHeadStep + 4);
-            }
-            wa = *reinterpret_cast<const float4*>(win + kk + kHeadStep);
-            wb = *reinterpret_cast<const float4*>(win + kk + kHeadStep + 4);
-        }
+        if (st + kPre < kSteps) load(r, (st + kPre) * kHeadStep);
 #pragma unroll 8
         for (int k = 0; k < kHeadStep; k++) {
             const float4 a = xs[k][ty];
