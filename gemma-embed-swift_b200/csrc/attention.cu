@@ -35,22 +35,25 @@ namespace ge {
 //   warp 0      TMA producer: per item the Q tile, once both S issuers have read the previous
 //               one, then K and V tiles of 64 keys into 2-slot rings that run on from item to
 //               item, K and V on independent cursors (each load as soon as its slot is free)
-//   warps 1, 10 S issuers (warp 1 also owns tensor memory): S_j = Q K_j^T (128 x 64, fp32 in
-//               TMEM, two buffers); head dim 256: warp 1 the even global key blocks and warp 10
+//   warps 1, 2  S issuers (warp 1 also owns tensor memory): S_j = Q K_j^T (128 x 64, fp32 in
+//               TMEM, two buffers); head dim 256: warp 1 the even global key blocks and warp 2
 //               the odd ones, each through its own K-ring slot (one thread issues a tcgen05.mma
 //               about every 90 cycles, as long as a 128 x 64 x 16 product runs); head dim 512:
 //               warp 1 alone.  A buffer takes block j + 2 once every softmax thread holds block
 //               j's scores.
-//   warp 11     PV issuer: O += P_j V_j (128 x 256, fp32 in TMEM, P read from TMEM); an
-//               item's first PV waits until the previous item's O has been read out, so the next
-//               item's Q load and first S products overlap the previous item's epilogue
-//   warps 2-9   softmax, two threads per row (one per 32-key half of a block; warps w and
+//   warp 3      PV issuer: O += P_j V_j (128 x 256, fp32 in TMEM, P read from TMEM); an
+//               item's first PV waits until the epilogue warps have read the previous item's O
+//   warps 4-11  softmax, two threads per row (one per 32-key half of a block; warps w and
 //               w + 4 share a tensor-memory lane quarter): mask S_j, exchange the row's block
 //               maximum through shared memory, keep running maximum and partial sums, write
 //               their half of P_j (fp16 pairs) to tensor memory, and rescale their half of O in
 //               tensor memory only when the row maximum grows by more than kRescale; until then
 //               every term of the row uses the same stale maximum, so the result is exact.
-//               Then O / l for their half of the row, staged through shared memory.
+//               At an item's end each thread leaves its half sum in shared memory and goes on
+//               with the next item's first block.
+//   warps 12-15 O epilogue, one warp per lane quarter: once an item's last PV has completed,
+//               O / l of the live rows, staged through shared memory into coalesced stores, so
+//               the next item's softmax overlaps the previous item's epilogue.
 // Tensor memory: O in columns [0, 256), the S buffers in [256, 320) and [320, 384), the P
 // buffers in [384, 416) and [416, 448).
 constexpr int kTcQ = 128;
@@ -60,16 +63,23 @@ constexpr float kRescale = 8.0f;  // log2 units: a stale maximum may leave P up 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kQBytes = kTcQ * kTcHd * 2;     // 64 KB: 4 chunks of [128 rows][64 dims]
 constexpr int kKVBytes = kTcKeys * kTcHd * 2; // 32 KB per stage: 4 chunks of [64 keys][64 dims]
-constexpr int kPBytes = kTcQ * kTcKeys * 2;   // 16 KB per buffer: [128 rows][64 keys]
+constexpr int kPBytes = kTcQ * kTcKeys * 2;   // 16 KB: [128 rows][64 keys] fp16, two of them (see kOffStg)
 constexpr int kOffK = kQBytes;
 constexpr int kOffV = kOffK + 2 * kKVBytes;
 constexpr int kOffP = kOffV + 2 * kKVBytes;
-constexpr int kOffRed = kOffP + 2 * kPBytes;    // [2 halves][128 rows] floats: row maxima, then sums
+constexpr int kOffRed = kOffP + 2 * kPBytes;    // [2 halves][128 rows] floats: row maxima
 constexpr int kOffBar = kOffRed + 2 * kTcQ * 4;
+// The P region is free since P moved to tensor memory: the epilogue warps' staging tiles
+// ([4 warps][32 rows][128 B]) and the row sums the softmax hands them ([2 item parities][2
+// halves][128 rows] floats).
+constexpr int kOffStg = kOffP;
+constexpr int kOffL = kOffP + 4 * 32 * 128;
 constexpr int kTcSmem = kOffBar + 256 + 1024;
-constexpr int kTcThreads = 384;
-constexpr int kSWarpB = 10;  // the second S issuer
-constexpr int kPVWarp = 11;  // the PV issuer
+constexpr int kTcThreads = 512;
+constexpr int kSWarpB = 2;     // the second S issuer
+constexpr int kPVWarp = 3;     // the PV issuer
+constexpr int kSoftWarp0 = 4;  // softmax warps 4-11
+constexpr int kEpiWarp0 = 12;  // O epilogue warps 12-15
 constexpr uint32_t kPollNs = 64;  // producer and issuer poll interval
 constexpr uint32_t kTmemO = 0, kTmemS = 256, kTmemP = 384;
 
@@ -122,7 +132,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
     uint64_t* pv_done = bars + 14;
     uint64_t* o_empty = bars + 16;
     uint64_t* s_free = bars + 17;  // S buffer read into registers by every softmax thread
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+    uint64_t* o_full = bars + 19;  // an item's last PV has completed
+    uint64_t* l_full = bars + 20;  // an item's row sums are in shared memory (by item parity)
+    uint64_t* l_empty = bars + 22; // and have been read by the epilogue warps
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int live_rows = p.group * p.tokens;
@@ -140,8 +153,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
             mbar_init(&p_full[i], 256);
             mbar_init(&pv_done[i], 1);
         }
-        mbar_init(o_empty, 256);
-        for (int i = 0; i < 2; i++) mbar_init(&s_free[i], 256);
+        mbar_init(o_empty, 128);
+        mbar_init(o_full, 1);
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&s_free[i], 256);
+            mbar_init(&l_full[i], 256);
+            mbar_init(&l_empty[i], 128);
+        }
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
@@ -361,13 +379,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                     }
                     umma_commit(&v_empty[b]);
                     umma_commit(&pv_done[b]);
+                    if (j == nblk - 1) umma_commit(o_full);  // O of the item is complete
                 }
             }
         }
-    } else {
+    } else if (warp < kEpiWarp0) {
         // ---------------------------------------------------------- softmax (two threads per row)
-        const int quad = warp & 3;         // tensor-memory lane quarter of this warp
-        const int half = (warp - 2) >> 2;  // which 32 keys of each block, and which 128 O columns
+        const int quad = warp & 3;                  // tensor-memory lane quarter of this warp
+        const int half = (warp - kSoftWarp0) >> 2;  // which 32 keys of each block
         const int r = quad * 32 + lane;
         const int rt = r / p.group;  // token of this row within a tile (rows are token * G + head)
         const uint32_t lane_base = tmem + (uint32_t(quad * 32) << 16);
@@ -382,8 +401,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
             const bool w = ok && mbar_wait(bar, parity, p.err);
             ok = __all_sync(0xffffffffu, w);
         };
+        float* lbuf = reinterpret_cast<float*>(smem + kOffL);
         int gb = 0;
-        for (int it = int(p.offset[blockIdx.x]); it < int(p.offset[blockIdx.x + 1]); it++) {
+        for (int it = int(p.offset[blockIdx.x]), li = 0; it < int(p.offset[blockIdx.x + 1]); it++, li++) {
             const uint4 w = p.work[it];
             int k_start, nblk;
             item_keys(w, p, k_start, nblk);
@@ -483,62 +503,87 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                 tc_fence_before();
                 mbar_arrive(&p_full[b]);
             }
-            // ---- epilogue: O / l of the live rows; each half stores its 128 columns, then O is
-            // handed back for the next item's first PV
-            red[half * kTcQ + r] = l;
-            pair_sync();
-            const float lt = l + red[(1 - half) * kTcQ + r];
-            pair_sync();  // the slots are free for the next item's first block
-            if (ok) {
-                wait_all(&pv_done[(gb - 1) & 1], uint32_t(((gb - 1) >> 1) & 1));
-                if (ok) {
-                    tc_fence_after();
-                    const float inv = lt > 0.f ? 1.0f / lt : 0.f;
-                    // O leaves through this half's P buffer (free: the item's last PV has run, and
-                    // the next item writes P only after both halves pass its first pair_sync):
-                    // each thread writes its row's 64 columns, then each warp stores 4 rows of
-                    // 128 bytes per instruction.
-                    uint8_t* stg = smem + kOffP + half * kPBytes;
+            // ---- the row's half sum goes to the epilogue warps, which read O once the item's last
+            // PV has completed; this warp goes on with the next item's first block.
+            if (ok && li >= 2) wait_all(&l_empty[li & 1], uint32_t(((li - 2) >> 1) & 1));
+            lbuf[(li & 1) * 2 * kTcQ + half * kTcQ + r] = l;
+            mbar_arrive(&l_full[li & 1]);
+        }
+    } else {
+        // ---------------------------------------------------------- O epilogue (one warp per lane quarter)
+        // Per item: both halves' row sums, then O / l of the live rows once the item's last PV
+        // has completed, 64 columns at a time: each thread writes its row's 128 bytes to the
+        // warp's staging tile, then the warp stores 4 rows of 128 bytes per instruction.  O is
+        // handed back for the next item's first PV after its last columns are in registers.
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
+        const uint32_t lane_base = tmem + (uint32_t(quad * 32) << 16);
+        const float* lbuf = reinterpret_cast<const float*>(smem + kOffL);
+        uint8_t* stg = smem + kOffStg + quad * 32 * 128;
+        bool ok = true;
+        auto wait_all = [&](uint64_t* bar, uint32_t parity) {
+            const bool w = ok && mbar_wait(bar, parity, p.err);
+            ok = __all_sync(0xffffffffu, w);
+        };
+        for (int it = int(p.offset[blockIdx.x]), li = 0; it < int(p.offset[blockIdx.x + 1]); it++, li++) {
+            const uint4 w = p.work[it];
+            const int len = int(w.y);
+            wait_all(&l_full[li & 1], uint32_t((li >> 1) & 1));
+            // Half 0's sum plus half 1's (the order the two halves added them in before).
+            const float lt = ok ? lbuf[(li & 1) * 2 * kTcQ + r] + lbuf[(li & 1) * 2 * kTcQ + kTcQ + r] : 0.f;
+            mbar_arrive(&l_empty[li & 1]);
+            wait_all(o_full, uint32_t(li & 1));
+            if (!ok) {
+                mbar_arrive(o_empty);
+                continue;
+            }
+            tc_fence_after();
+            const float inv = lt > 0.f ? 1.0f / lt : 0.f;
+            // Where each of this lane's eight store slots goes (row i * 4 + lane / 8 of the
+            // warp's 32, 16 bytes at column 8 * (lane % 8) of each 64-column round), or null
+            // for a row past the item's tokens.
+            __half* dst[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int rr = quad * 32 + i * 4 + (lane >> 3);
+                const int rrt = rr / p.group, rrg = rr - rrt * p.group;
+                const int qr = int(w.z) + rrt;
+                dst[i] = (rr < live_rows && qr < len)
+                             ? p.out + ((long(w.x) + qr) * p.heads + int(w.w & 0xffffu) * p.group + rrg) * long(HD) +
+                                   int(w.w >> 16) * kTcHd + (lane & 7) * 8
+                             : nullptr;
+            }
 #pragma unroll 1
-                    for (int rd = 0; rd < 2; rd++) {
-                        uint32_t o[64];
-                        const uint32_t col = kTmemO + uint32_t(half * (kTcHd / 2) + rd * 64);
-                        tmem_ld32(lane_base + col, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
-                        tmem_ld32(lane_base + col + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
-                        tmem_wait_ld();
-                        if (rd == 1) {  // O is read: the next item's first PV may overwrite it
-                            tc_fence_before();
-                            mbar_arrive(o_empty);
-                        }
-                        uint8_t* srow = stg + r * 128;
-#pragma unroll
-                        for (int j = 0; j < 8; j++) {
-                            uint32_t pk[4];
-#pragma unroll
-                            for (int e = 0; e < 4; e++) {
-                                __half2 hv = __floats2half2_rn(__uint_as_float(o[8 * j + 2 * e]) * inv,
-                                                               __uint_as_float(o[8 * j + 2 * e + 1]) * inv);
-                                pk[e] = *reinterpret_cast<uint32_t*>(&hv);
-                            }
-                            *reinterpret_cast<uint4*>(srow + ((j ^ (r & 7)) * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                        }
-                        __syncwarp();
-#pragma unroll
-                        for (int i = 0; i < 8; i++) {
-                            const int rr = quad * 32 + i * 4 + (lane >> 3), ch = lane & 7;
-                            const int rrt = rr / p.group, rrg = rr - rrt * p.group;
-                            const int qr = int(w.z) + rrt;
-                            const uint4 val = *reinterpret_cast<const uint4*>(stg + rr * 128 + ((ch ^ (rr & 7)) * 16));
-                            if (rr < live_rows && qr < len) {
-                                __half* dst = p.out +
-                                              ((long(w.x) + qr) * p.heads + int(w.w & 0xffffu) * p.group + rrg) * long(HD) +
-                                              int(w.w >> 16) * kTcHd + half * (kTcHd / 2) + rd * 64 + ch * 8;
-                                *reinterpret_cast<uint4*>(dst) = val;
-                            }
-                        }
-                        __syncwarp();
-                    }
+            for (int rd = 0; rd < kTcHd / 64; rd++) {
+                uint32_t o[64];
+                const uint32_t col = kTmemO + uint32_t(rd * 64);
+                tmem_ld32(lane_base + col, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+                tmem_ld32(lane_base + col + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+                tmem_wait_ld();
+                if (rd == kTcHd / 64 - 1) {  // O is read: the next item's first PV may overwrite it
+                    tc_fence_before();
+                    mbar_arrive(o_empty);
                 }
+                uint8_t* srow = stg + lane * 128;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    uint32_t pk[4];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        __half2 hv = __floats2half2_rn(__uint_as_float(o[8 * j + 2 * e]) * inv,
+                                                       __uint_as_float(o[8 * j + 2 * e + 1]) * inv);
+                        pk[e] = *reinterpret_cast<uint32_t*>(&hv);
+                    }
+                    *reinterpret_cast<uint4*>(srow + ((j ^ (lane & 7)) * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                }
+                __syncwarp();
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const int lr = i * 4 + (lane >> 3), ch = lane & 7;
+                    const uint4 val = *reinterpret_cast<const uint4*>(stg + lr * 128 + ((ch ^ (lr & 7)) * 16));
+                    if (dst[i]) *reinterpret_cast<uint4*>(dst[i] + rd * 64) = val;
+                }
+                __syncwarp();
             }
         }
     }
