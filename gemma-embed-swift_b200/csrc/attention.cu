@@ -42,7 +42,8 @@ namespace ge {
 //               warp 1 alone.  A buffer takes block j + 2 once every softmax thread holds block
 //               j's scores.
 //   warp 3      PV issuer: O += P_j V_j (128 x 256, fp32 in TMEM, P read from TMEM); an
-//               item's first PV waits until the epilogue warps have read the previous item's O
+//               item's first PV runs as two 128-column halves, each once the epilogue warps
+//               have read that half of the previous item's O
 //   warps 4-11  softmax, two threads per row (one per 32-key half of a block; warps w and
 //               w + 4 share a tensor-memory lane quarter): mask S_j, exchange the row's block
 //               maximum through shared memory, keep running maximum and partial sums, write
@@ -130,12 +131,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
     uint64_t* s_full = bars + 10;
     uint64_t* p_full = bars + 12;
     uint64_t* pv_done = bars + 14;
-    uint64_t* o_empty = bars + 16;
+    uint64_t* o_empty = bars + 16;  // columns [0, 128) of O read out (and bars + 25: [128, 256))
     uint64_t* s_free = bars + 17;  // S buffer read into registers by every softmax thread
     uint64_t* o_full = bars + 19;  // an item's last PV has completed
     uint64_t* l_full = bars + 20;  // an item's row sums are in shared memory (by item parity)
     uint64_t* l_empty = bars + 22; // and have been read by the epilogue warps
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+    uint64_t* o_empty_hi = bars + 25;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int live_rows = p.group * p.tokens;
@@ -154,6 +156,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
             mbar_init(&pv_done[i], 1);
         }
         mbar_init(o_empty, 128);
+        mbar_init(o_empty_hi, 128);
         mbar_init(o_full, 1);
         for (int i = 0; i < 2; i++) {
             mbar_init(&s_free[i], 256);
@@ -348,7 +351,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
     } else if (warp == kPVWarp) {
         // ---------------------------------------------------------- PV issuer
         if (lane == 0) {
-            const uint32_t id_o = idesc_f16(kTcQ, kTcHd, 0, 1);  // K-major P, MN-major V
+            const uint32_t id_o = idesc_f16(kTcQ, kTcHd, 0, 1);          // K-major P, MN-major V
+            const uint32_t id_oh = idesc_f16(kTcQ, kTcHd / 2, 0, 1);     // one 128-column half of O
             bool ok = true;
             int gb = 0;
             for (int it = int(p.offset[blockIdx.x]), li = 0; it < int(p.offset[blockIdx.x + 1]) && ok; it++, li++) {
@@ -358,24 +362,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                 for (int j = 0; j < nblk; j++, gb++) {
                     const int b = gb & 1;
                     const uint32_t ph = uint32_t((gb >> 1) & 1);
-                    // An item's first PV overwrites O once the previous item's O has been read out.
-                    if (j == 0 && li > 0 && !mbar_wait_sleep(o_empty, uint32_t((li - 1) & 1), p.err, kPollNs)) {
-                        ok = false;
-                        break;
-                    }
                     if (!mbar_wait_sleep(&p_full[b], ph, p.err, kPollNs) || !mbar_wait_sleep(&v_full[b], ph, p.err, kPollNs)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint32_t va = smem_u32(smem + kOffV + b * kKVBytes);
+                    if (j == 0 && li > 0) {
+                        // An item's first PV overwrites O in two 128-column halves, each once the
+                        // epilogue warps have read that half of the previous item's O.
+                        for (int hh = 0; hh < 2 && ok; hh++) {
+                            if (!mbar_wait_sleep(hh ? o_empty_hi : o_empty, uint32_t((li - 1) & 1), p.err, kPollNs)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
 #pragma unroll
-                    for (int kk = 0; kk < kTcKeys / 16; kk++) {
-                        // P_b's keys 16 kk .. 16 kk + 15 from tensor memory
-                        const uint32_t pa = tmem + kTmemP + uint32_t(b * (kTcKeys / 2) + kk * 8);
-                        // V chunk of 64 dims = one [64 keys][128 B] box; 16 keys advance 2048 B.
-                        const uint64_t bd = sw128_desc(va + kk * 2048, kKVBytes / 4, 1024);
-                        umma_f16_ta(tmem + kTmemO, pa, bd, id_o, !(j == 0 && kk == 0));
+                            for (int kk = 0; kk < kTcKeys / 16; kk++) {
+                                const uint32_t pa = tmem + kTmemP + uint32_t(b * (kTcKeys / 2) + kk * 8);
+                                // dims 128 hh .. 128 hh + 127: two 64-dim chunks of V on
+                                const uint64_t bd = sw128_desc(va + hh * 2 * (kKVBytes / 4) + kk * 2048, kKVBytes / 4, 1024);
+                                umma_f16_ta(tmem + kTmemO + uint32_t(hh * (kTcHd / 2)), pa, bd, id_oh, kk != 0);
+                            }
+                        }
+                        if (!ok) break;
+                    } else {
+#pragma unroll
+                        for (int kk = 0; kk < kTcKeys / 16; kk++) {
+                            // P_b's keys 16 kk .. 16 kk + 15 from tensor memory
+                            const uint32_t pa = tmem + kTmemP + uint32_t(b * (kTcKeys / 2) + kk * 8);
+                            // V chunk of 64 dims = one [64 keys][128 B] box; 16 keys advance 2048 B.
+                            const uint64_t bd = sw128_desc(va + kk * 2048, kKVBytes / 4, 1024);
+                            umma_f16_ta(tmem + kTmemO, pa, bd, id_o, !(j == 0 && kk == 0));
+                        }
                     }
                     umma_commit(&v_empty[b]);
                     umma_commit(&pv_done[b]);
@@ -535,24 +554,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
             wait_all(o_full, uint32_t(li & 1));
             if (!ok) {
                 mbar_arrive(o_empty);
+                mbar_arrive(o_empty_hi);
                 continue;
             }
             tc_fence_after();
             const float inv = lt > 0.f ? 1.0f / lt : 0.f;
-            // Where each of this lane's eight store slots goes (row i * 4 + lane / 8 of the
-            // warp's 32, 16 bytes at column 8 * (lane % 8) of each 64-column round), or null
-            // for a row past the item's tokens.
-            __half* dst[8];
+            // The output row (token x heads + head) of each of this lane's eight store slots (row
+            // i * 4 + lane / 8 of the warp's 32), or -1 for a row past the item's tokens; the
+            // lane stores 16 bytes at column 8 * (lane % 8) of each 64-column round.
+            int orow[8];
 #pragma unroll
             for (int i = 0; i < 8; i++) {
                 const int rr = quad * 32 + i * 4 + (lane >> 3);
                 const int rrt = rr / p.group, rrg = rr - rrt * p.group;
                 const int qr = int(w.z) + rrt;
-                dst[i] = (rr < live_rows && qr < len)
-                             ? p.out + ((long(w.x) + qr) * p.heads + int(w.w & 0xffffu) * p.group + rrg) * long(HD) +
-                                   int(w.w >> 16) * kTcHd + (lane & 7) * 8
-                             : nullptr;
+                orow[i] = (rr < live_rows && qr < len) ? (int(w.x) + qr) * p.heads + int(w.w & 0xffffu) * p.group + rrg : -1;
             }
+            __half* const ocol = p.out + int(w.w >> 16) * kTcHd + (lane & 7) * 8;
 #pragma unroll 1
             for (int rd = 0; rd < kTcHd / 64; rd++) {
                 uint32_t o[64];
@@ -560,9 +578,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                 tmem_ld32(lane_base + col, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
                 tmem_ld32(lane_base + col + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
                 tmem_wait_ld();
-                if (rd == kTcHd / 64 - 1) {  // O is read: the next item's first PV may overwrite it
+                if (rd % 2 == 1) {  // a half of O is read: the next item's first PV may overwrite it
                     tc_fence_before();
-                    mbar_arrive(o_empty);
+                    mbar_arrive(rd == 1 ? o_empty : o_empty_hi);
                 }
                 uint8_t* srow = stg + lane * 128;
 #pragma unroll
@@ -581,7 +599,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                 for (int i = 0; i < 8; i++) {
                     const int lr = i * 4 + (lane >> 3), ch = lane & 7;
                     const uint4 val = *reinterpret_cast<const uint4*>(stg + lr * 128 + ((ch ^ (lr & 7)) * 16));
-                    if (dst[i]) *reinterpret_cast<uint4*>(dst[i] + rd * 64) = val;
+                    if (orow[i] >= 0) *reinterpret_cast<uint4*>(ocol + long(orow[i]) * HD + rd * 64) = val;
                 }
                 __syncwarp();
             }
