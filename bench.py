@@ -449,10 +449,10 @@ def main():
 # kernel changed since then needs a new capture.
 NCU_DRAM_BYTES_CONFIG2 = {
     "source": "ncu --set full on layer 6 of a config-2 forward: the GEMMs at commit 8909a33 (CTA pairs), the "
-              "q/k/v norm, attention and residual kernels at commit 97dff94",
+              "q/k/v norm, attention and residual kernels at commit dc778e8",
     "bytes": {"gemm_qkv": 36.83e6, "gemm_o": 33.54e6, "gemm_gate_up": 40.26e6, "gemm_down": 50.74e6,
-              "qkv_norm_rope": 58.28e6, "attention_sliding": 52.44e6, "residual_attn": 99.77e6,
-              "residual_ffn": 156.61e6},
+              "qkv_norm_rope": 58.00e6, "attention_sliding": 52.73e6, "residual_attn": 100.92e6,
+              "residual_ffn": 156.96e6},
 }
 
 
