@@ -448,16 +448,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                     tmem_wait_ld();
                     tc_fence_before();
                     mbar_arrive(&s_free[b]);  // the S buffer may take block gb + 2
-                    // Scores in log2 units: p = 2^(s log2e - m), one FFMA and one ex2 per key.
-                    if (kb >= row_lo && kb + 32 <= row_hi) {  // every key of this half is visible
-#pragma unroll
-                        for (int i = 0; i < 32; i++) sr[i] = __float_as_uint(__uint_as_float(sr[i]) * kLog2e);
-                    } else {
+                    // Raw scores, masked keys at -inf; the maximum is taken on them and scaled once
+                    // (x -> x log2e rounds monotonically), and p = 2^(s log2e - m) is one FFMA and
+                    // one ex2 per key.
+                    if (!(kb >= row_lo && kb + 32 <= row_hi)) {  // some key of this half is masked
 #pragma unroll
                         for (int i = 0; i < 32; i++) {
                             const int kj = kb + i;
-                            const float t = (kj >= row_lo && kj < row_hi) ? __uint_as_float(sr[i]) * kLog2e : -INFINITY;
-                            sr[i] = __float_as_uint(t);
+                            if (!(kj >= row_lo && kj < row_hi)) sr[i] = __float_as_uint(-INFINITY);
                         }
                     }
                     // Eight independent partial maxima instead of one 32-long dependency chain.
@@ -467,6 +465,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
 #pragma unroll
                     for (int i = 8; i < 32; i++) mp[i & 7] = fmaxf(mp[i & 7], __uint_as_float(sr[i]));
                     mh = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])), fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7])));
+                    mh *= kLog2e;
                 }
                 // Row maximum of the block from both halves (the slot is rewritten only after the
                 // next pair_sync, by which time the partner has read it).
@@ -505,8 +504,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
                 uint32_t pk[16];  // this half's 32 probabilities as fp16 pairs
 #pragma unroll
                 for (int e = 0; e < 16; e++) {
-                    const float p0 = ex2_approx(__uint_as_float(sr[2 * e]) - mu);  // 2^-inf = 0
-                    const float p1 = ex2_approx(__uint_as_float(sr[2 * e + 1]) - mu);
+                    const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * e]), kLog2e, -mu));  // 2^-inf = 0
+                    const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * e + 1]), kLog2e, -mu));
                     ps[(2 * e) & 7] += p0;
                     ps[(2 * e + 1) & 7] += p1;
                     pk[e] = pack_half2(p0, p1);
