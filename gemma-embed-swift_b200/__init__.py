@@ -413,6 +413,20 @@ def _ptr(a: np.ndarray, t):
     return a.ctypes.data_as(ctypes.POINTER(t))
 
 
+def _id_arrays(data) -> tuple:
+    """Token-id arrays for ge_embed_tokens: the texts' ids in one int32 buffer, their lengths,
+    and each text's address in that buffer (uintp), computed from the offsets with one ctypes
+    conversion per call instead of one per text (about 2.5 us each).  The addresses are valid
+    while the returned buffer is alive."""
+    n = len(data)
+    lens = np.fromiter((len(s) for s in data), dtype=np.int32, count=n)
+    flat = np.concatenate(data) if n > 1 else data[0]
+    starts = np.zeros(n, dtype=np.int64)
+    np.cumsum(lens[:-1], out=starts[1:])
+    addrs = (flat.ctypes.data + 4 * starts).astype(np.uintp)
+    return flat, lens, addrs
+
+
 def pack(sequences) -> tuple:
     """PackedBatch.append over `sequences` (MetalForward.swift:17-21): ids, positions, ranges."""
     seqs = [_i32(s) for s in sequences]
@@ -637,13 +651,7 @@ class EmbeddingModel:
                                     ctypes.byref(o), _ptr(out, ctypes.c_float), _ptr(counts, ctypes.c_int32),
                                     _ptr(trunc, ctypes.c_int32), cb, None), self._h)
         else:
-            # The texts' ids in one buffer and the per-text pointers computed from their offsets:
-            # one ctypes conversion per call instead of one per text (about 2.5 us each).
-            lens = np.fromiter((len(s) for s in data), dtype=np.int32, count=n)
-            flat = np.concatenate(data) if n > 1 else data[0]
-            starts = np.zeros(n, dtype=np.int64)
-            np.cumsum(lens[:-1], out=starts[1:])
-            addrs = (flat.ctypes.data + 4 * starts).astype(np.uintp)
+            flat, lens, addrs = _id_arrays(data)  # `flat` stays alive through the call
             _check(L.ge_embed_tokens(self._h, addrs.ctypes.data_as(ctypes.POINTER(_lib.i32p)),
                                      _ptr(lens, ctypes.c_int32), n, ctypes.byref(o),
                                      _ptr(out, ctypes.c_float), _ptr(counts, ctypes.c_int32),

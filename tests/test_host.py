@@ -121,3 +121,16 @@ def test_pack(ge):
     assert tokens.tolist() == [5, 6, 7, 1, 9, 9]
     assert positions.tolist() == [0, 1, 2, 0, 0, 1]
     assert [(r[0], r[1]) for r in ranges] == [(0, 3), (3, 1), (4, 2)]
+
+
+def test_id_arrays_address_every_text(ge):
+    """EmbeddingModel.embed passes pre-tokenised texts as one buffer with per-text addresses: each
+    address reads back exactly its text's ids, for one text and for many of mixed lengths."""
+    rng = np.random.default_rng(7)
+    for lens in ([5], [1, 300, 17, 2, 64], [3] * 40):
+        data = [rng.integers(0, 262144, size=n).astype(np.int32) for n in lens]
+        flat, lengths, addrs = ge._id_arrays(data)
+        assert lengths.tolist() == lens and addrs.dtype == np.uintp
+        for d, a, n in zip(data, addrs.tolist(), lens):
+            got = np.ctypeslib.as_array(ctypes.cast(a, ctypes.POINTER(ctypes.c_int32)), shape=(n,))
+            assert np.array_equal(got, d)
