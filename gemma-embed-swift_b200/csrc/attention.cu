@@ -560,7 +560,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_attention_tc(const __grid_con
             const float inv = lt > 0.f ? 1.0f / lt : 0.f;
             // The output row (token x heads + head) of each of this lane's eight store slots (row
             // i * 4 + lane / 8 of the warp's 32), or -1 for a row past the item's tokens; the
-            // lane stores 16 bytes at column 8 * (lane % 8) of each 64-column round.
+            // lane stores 16 bytes at column 8 * (lane % 8) of each 64-column round.  The row
+            // index fits 32 bits: the output holds tokens x heads x head-dim fp16 values, and
+            // a batch's int32 token count times the heads stays far below 2^31 for any
+            // workspace that fits a device.
             int orow[8];
 #pragma unroll
             for (int i = 0; i < 8; i++) {
