@@ -771,10 +771,10 @@ int run_forward(ge_model* m, Device& d, const ForwardArgs& a) {
     const bool fused = (m->flags & GE_LOAD_FUSED_RESIDUAL) != 0;
     // The q/k/v projection of a head-dim-256 layer with its per-head norms and RoPE in the GEMM
     // epilogue (EPI_QKV), attention reading q, k and v in place from the projection rows.
-    // On request (GE_LOAD_FUSED_QKV).  Measured on B200 at 19.5k tokens: 61 us per layer against
-    // 38 + 25 us for the projection and k_qkv_norm_rope, and whole forwards within 1 % of each
-    // other: the epilogue (one thread per token, two passes over the 256 columns, each thread
-    // reading its own position's RoPE row) outlasts the K = 768 main loop it overlaps.
+    // On request (GE_LOAD_FUSED_QKV).  Measured on B200 at 19.5k tokens: 61 us per layer on single
+    // CTAs against 38 + 25 us for the projection and k_qkv_norm_rope, and 71 us on CTA pairs
+    // against 35 + 22 us: the epilogue (one thread per token, two passes over the 256 columns,
+    // each thread reading its own position's RoPE row) outlasts the K = 768 main loop it overlaps.
     const bool fused_qkv = (m->flags & GE_LOAD_FUSED_QKV) != 0;
     auto gemm_qkv = [&](const LayerDev& L, const LayerCfg& lc) {
         GemmLaunch g;
